@@ -1,0 +1,365 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference.
+
+Runs ONLY in the build container, where the reference checkout is mounted
+read-only (default ``/root/reference``; override with ``SRSWA_REFERENCE``).  It
+imports the reference's own code -- the HF PyTorch SR-SWA path, its Triton
+kernels under the Triton CPU interpreter, and the SGLang serving ops from the
+reference's wheel -- runs them on small seeded inputs and writes
+``tests/golden/<case>.npz`` (inputs + outputs + version metadata).  The GPU box
+never runs this script; tests there read the committed ``.npz`` files.
+
+Usage:  python tests/golden/make_golden.py
+"""
+
+from __future__ import annotations
+
+import importlib
+import importlib.util
+import json
+import math
+import os
+import shutil
+import sys
+import tempfile
+import types
+import zipfile
+
+os.environ["TRITON_INTERPRET"] = "1"
+os.environ.setdefault("CODE_STAMP_LOG", "0")
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+REF = os.environ.get("SRSWA_REFERENCE", "/root/reference")
+OUT = os.path.dirname(os.path.abspath(__file__))
+WHEEL = "wheel/sglang-0.5.20.dev10+g8d62f5fb9c-py3-none-any.whl"
+
+
+def _shim_transformers():
+    """Four attributes the reference expects from transformers 4.52 (its pin);
+    the container has transformers 5.x where they moved or were removed."""
+    import transformers.pytorch_utils as pu
+    import transformers.utils as tu
+    import transformers.utils.import_utils as iu
+    iu.is_torch_fx_available = lambda: False
+    pu.is_torch_greater_or_equal_than_1_13 = True
+    pu.ALL_LAYERNORM_LAYERS = []
+    tu.is_flash_attn_greater_or_equal_2_10 = lambda *a, **k: False
+
+
+def import_reference():
+    """Copy hf-model-code to a temp package (it uses relative imports) and
+    import the modules the SR-SWA path lives in."""
+    _shim_transformers()
+    tmp = tempfile.mkdtemp(prefix="uocr_ref_")
+    pkg = os.path.join(tmp, "uocr_ref")
+    shutil.copytree(os.path.join(REF, "hf-model-code"), pkg,
+                    ignore=shutil.ignore_patterns("tokenizer*", "*.json", "*.md"))
+    open(os.path.join(pkg, "__init__.py"), "w").close()
+    sys.path.insert(0, tmp)
+    mods = {}
+    for name in ("modeling_deepseekv2", "dash_attention", "sparse_gather_triton",
+                 "sparse_gather_e2e_triton"):
+        mods[name] = importlib.import_module(f"uocr_ref.{name}")
+    return mods
+
+
+def import_sglang_ops():
+    """Load the SGLang DASH ops from the reference wheel with stub parent
+    packages (the rest of SGLang is not needed for these files)."""
+    tmp = tempfile.mkdtemp(prefix="uocr_sgl_")
+    sub = "sglang/srt/layers/attention/unlimited_dash_ops/"
+    with zipfile.ZipFile(os.path.join(REF, WHEEL)) as z:
+        for n in z.namelist():
+            if n.startswith(sub) and n.endswith(".py"):
+                z.extract(n, tmp)
+    for pk in ("sglang", "sglang.srt", "sglang.srt.layers", "sglang.srt.layers.attention",
+               "sglang.srt.layers.attention.unlimited_dash_ops"):
+        m = types.ModuleType(pk)
+        m.__path__ = [os.path.join(tmp, *pk.split("."))]
+        sys.modules[pk] = m
+    out = {}
+    for name in ("common", "dash_router", "dash_stage0", "attend_triton"):
+        full = f"sglang.srt.layers.attention.unlimited_dash_ops.{name}"
+        spec = importlib.util.spec_from_file_location(full, os.path.join(tmp, sub, name + ".py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[full] = mod
+        spec.loader.exec_module(mod)
+        out[name] = mod
+    # CPU interpreter: no PDL, no graph capture
+    out["common"]._PDL_SUPPORTED = False
+    out["attend_triton"]._arch_supports_pdl = lambda: False
+    torch.cuda.is_current_stream_capturing = lambda: False
+    return out
+
+
+def bf16r(t):
+    return t.to(torch.bfloat16).to(torch.float32)
+
+
+def save(name, **arrs):
+    meta = dict(torch=torch.__version__, numpy=np.__version__,
+                transformers=__import__("transformers").__version__,
+                triton=__import__("triton").__version__, triton_interpret=True,
+                reference=REF, shim="transformers 4-symbol shim (see import_reference)")
+    arrs = {k: (v.detach().cpu().numpy() if torch.is_tensor(v) else np.asarray(v))
+            for k, v in arrs.items()}
+    np.savez_compressed(os.path.join(OUT, name + ".npz"), meta=json.dumps(meta), **arrs)
+    print("wrote", name, {k: v.shape for k, v in arrs.items()})
+
+
+def router_ns(block_size, local_blocks, head_cls, stage0="head_cls", q_chunk=2048):
+    return types.SimpleNamespace(block_size=block_size, local_blocks=local_blocks,
+                                 local_window=local_blocks * block_size,
+                                 head_cls=head_cls, stage0=stage0, q_chunk=q_chunk)
+
+
+def case_route(m):
+    """_block_scores_infer (head_cls + indexer) and _infer_route_select."""
+    md = m["modeling_deepseekv2"]
+    g = torch.Generator().manual_seed(11)
+    B, S, d, BS, L = 2, 700, 128, 64, 2
+    nblk = (S + BS - 1) // BS
+    idx_q = bf16r(torch.randn(B, S, d, generator=g))
+    idx_k = bf16r(torch.randn(B, S, d, generator=g))
+    hc0 = torch.zeros(d)
+    hc1 = torch.randn(d, generator=g) * 0.3
+    q_pos = torch.arange(S)[None].expand(B, S).contiguous()
+    p = dict(idx_scale=128.0 / math.sqrt(d), floor=1e-4, sigma=1.0, K=4, topm=6)
+    outs = {}
+    for tag, hc in (("hc0", hc0), ("hc1", hc1)):
+        sc = md._block_scores_infer(router_ns(BS, L, hc), idx_q, idx_k, q_pos, nblk)
+        topi, bias, valid = md._infer_route_select(sc, None, p)
+        outs[f"scores_{tag}"] = sc
+        outs[f"topi_{tag}"] = topi
+        outs[f"bias_{tag}"] = bias
+        outs[f"valid_{tag}"] = valid
+    # page-aware candidate mask (with rows whose mask empties -> fallback)
+    cand = torch.rand(B, S, nblk, generator=g) < 0.3
+    cand[:, 500:560] = False
+    sc = outs["scores_hc0"]
+    topi, bias, valid = md._infer_route_select(sc, cand, p)
+    outs.update(cand=cand, topi_cand=topi, bias_cand=bias, valid_cand=valid)
+    # sigma != 1, different K/M
+    p2 = dict(idx_scale=3.0, floor=1e-2, sigma=0.7, K=8, topm=16)
+    topi, bias, valid = md._infer_route_select(sc, None, p2)
+    outs.update(topi_p2=topi, bias_p2=bias, valid_p2=valid)
+    # indexer stage0 (token block-max)
+    sci = md._block_scores_infer(router_ns(BS, L, hc0, stage0="indexer"), idx_q, idx_k, q_pos, nblk)
+    outs["scores_indexer"] = sci
+    save("route", idx_q=idx_q, idx_k=idx_k, hc1=hc1, q_pos=q_pos,
+         params=np.array([BS, L, p["K"], p["topm"]]),
+         fparams=np.array([p["idx_scale"], p["floor"], p["sigma"]]),
+         fparams2=np.array([p2["idx_scale"], p2["floor"], p2["sigma"], p2["K"], p2["topm"]]),
+         **outs)
+
+
+def case_entmax(m):
+    da = m["dash_attention"]
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(64, 16, generator=g) * 8.0
+    x[5:9, 10:] = -1.0e4
+    x[20] = -1.0e4
+    x[30, :3] = 3.0
+    y = da.entmax15(x, dim=-1)
+    save("entmax", x=x, y=y)
+
+
+def case_decode_attend(m):
+    """_decode_attend, with selections from the reference router."""
+    md = m["modeling_deepseekv2"]
+    g = torch.Generator().manual_seed(13)
+    B, H, D, S, BS, L, d = 2, 2, 64, 1100, 64, 3, 128
+    nblk = (S + BS - 1) // BS
+    q = bf16r(torch.randn(B, H, 2, D, generator=g))
+    k = bf16r(torch.randn(B, H, S, D, generator=g))
+    v = bf16r(torch.randn(B, H, S, D, generator=g))
+    idx_q = bf16r(torch.randn(B, 2, d, generator=g))
+    idx_k = bf16r(torch.randn(B, S, d, generator=g))
+    q_pos = torch.tensor([[S - 2, S - 1], [700, 1003]])
+    sc = md._block_scores_infer(router_ns(BS, L, torch.zeros(d)), idx_q, idx_k, q_pos, nblk)
+    p = dict(idx_scale=128.0 / math.sqrt(d), floor=1e-4, sigma=1.0, K=5, topm=8)
+    topi, bias, valid = md._infer_route_select(sc, None, p)
+    scale = 1.0 / math.sqrt(D)
+    out = md._decode_attend(q, k, v, topi, bias, valid, q_pos, BS, L * BS, scale)
+    save("decode_attend", q=q, k=k, v=v, idx_q=idx_q, idx_k=idx_k, q_pos=q_pos,
+         scores=sc, topi=topi, bias=bias, valid=valid, out=out,
+         params=np.array([BS, L, p["K"], p["topm"]]), scale=np.array(scale))
+
+
+def case_forward_dense(m):
+    """DashAttention._forward_dense fwd + autograd grads (the DASH merge
+    semantics, incl. selected blocks overlapping the window)."""
+    da = m["dash_attention"]
+    md = m["modeling_deepseekv2"]
+    g = torch.Generator().manual_seed(14)
+    B, H, S, D, BS, L, K = 2, 2, 256, 32, 32, 2, 4
+    nblk = (S + BS - 1) // BS
+    q = bf16r(torch.randn(B, H, S, D, generator=g))
+    k = bf16r(torch.randn(B, H, S, D, generator=g))
+    v = bf16r(torch.randn(B, H, S, D, generator=g))
+    # selection: random distinct blocks <= qblk (some overlap the window, some
+    # are purely remote); invalid slots marked by valid=False
+    topi = torch.zeros(B, S, K, dtype=torch.long)
+    valid = torch.zeros(B, S, K, dtype=torch.bool)
+    for b in range(B):
+        for t in range(S):
+            qb = t // BS
+            perm = torch.randperm(qb + 1, generator=g)[:K]
+            n = perm.numel()
+            topi[b, t, :n] = perm
+            valid[b, t, :n] = True
+            if n < K:
+                # invalid slots point at blocks not selected by a valid slot
+                rest = [c for c in range(nblk) if c not in perm.tolist()][:K - n]
+                topi[b, t, n:] = torch.tensor(rest)
+    bias = (torch.randn(B, S, K, generator=g) * 0.5).requires_grad_(True)
+    qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
+    self_ = types.SimpleNamespace(block_size=BS, q_chunk=128, local_window=L * BS,
+                                  _scale=1.0 / math.sqrt(D))
+    o = da.DashAttention._forward_dense(self_, qg, kg, vg, topi, bias, valid, S, nblk, None)
+    do = torch.randn(o.shape, generator=g)
+    (o * do).sum().backward()
+    save("forward_dense", q=q, k=k, v=v, topi=topi, valid=valid, bias=bias.detach(),
+         o=o.detach(), do=do, dq=qg.grad, dk=kg.grad, dv=vg.grad, dbias=bias.grad,
+         params=np.array([BS, L]), scale=np.array(1.0 / math.sqrt(D)))
+    del md
+
+
+def case_gather_triton(m):
+    """triton_gather_attention (K1-K3) under the Triton CPU interpreter:
+    packing (seg), two index heads, duplicate ids and -1 padding."""
+    sg = m["sparse_gather_triton"]
+    g = torch.Generator().manual_seed(15)
+    B, HQ, Hkv, T, D, BS, S, LW = 2, 4, 2, 160, 32, 16, 4, 40
+    q = torch.randn(B, HQ, T, D, generator=g)
+    k = torch.randn(B, Hkv, T, D, generator=g)
+    v = torch.randn(B, Hkv, T, D, generator=g)
+    nb = (T + BS - 1) // BS
+    pos = torch.arange(T)[None].repeat(B, 1)
+    pos[1, 70:] = torch.arange(T - 70)         # packed: 2nd sample starts at 70
+    # The reference K1 has no NaN-safe running max (sparse_gather_triton.py:90-94):
+    # a leading selected block with no kept key gives NaN.  Its callers only
+    # select remote blocks, so slot 0 holds a block with >= 1 key in
+    # [seg, t - LW + 1) whenever one exists; later slots are random (window
+    # blocks, future blocks, -1) and slot 1 repeats slot 0 (dedup).
+    sel = torch.randint(-1, nb, (B, 2, T, S), generator=g)
+    for b in range(B):
+        for t in range(T):
+            seg = t - int(pos[b, t])
+            ls = max(t - LW + 1, seg)
+            rem = [c for c in range(nb) if max(c * BS, seg) < min((c + 1) * BS, ls)]
+            for hi in range(2):
+                if rem:
+                    sel[b, hi, t, 0] = rem[int(torch.randint(len(rem), (1,), generator=g))]
+                else:
+                    # no remote key at all: only -1 or future blocks (skipped)
+                    row = sel[b, hi, t]
+                    sel[b, hi, t] = torch.where((row >= 0) & (row * BS <= t), -1, row)
+    sel[:, :, :, 1] = sel[:, :, :, 0]          # duplicates
+    qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
+    o = sg.triton_gather_attention(qg, kg, vg, sel, pos, None, BS, 0.3, LW)
+    do = torch.randn(o.shape, generator=g)
+    (o * do).sum().backward()
+    save("gather_triton", q=q, k=k, v=v, sel=sel, pos=pos, o=o.detach(), do=do,
+         dq=qg.grad, dk=kg.grad, dv=vg.grad, params=np.array([BS, LW]), scale=np.array(0.3))
+
+
+def case_gather_e2e(m):
+    """triton_gather_attention_e2e (K5-K7) under the interpreter, with grads
+    to q/k/v and the per-slot bias."""
+    se = m["sparse_gather_e2e_triton"]
+    g = torch.Generator().manual_seed(16)
+    B, H, T, D, BS, S, LW = 2, 3, 150, 32, 16, 3, 48
+    q = torch.randn(B, H, T, D, generator=g)
+    k = torch.randn(B, H, T, D, generator=g)
+    v = torch.randn(B, H, T, D, generator=g)
+    nb = (T + BS - 1) // BS
+    sel = torch.full((B, 1, T, S), -1, dtype=torch.long)
+    for b in range(B):
+        for t in range(T):
+            cand = torch.randperm(t // BS + 1, generator=g)[:S]
+            sel[b, 0, t, :cand.numel()] = cand
+    sel[0, 0, 100, 2] = sel[0, 0, 100, 0]      # one duplicate
+    bias = (torch.randn(B, T, S, generator=g) * 0.5).requires_grad_(True)
+    pos = torch.arange(T)[None].repeat(B, 1)
+    qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
+    o = se.triton_gather_attention_e2e(qg, kg, vg, sel, bias, pos, None, BS, 0.25, LW)
+    do = torch.randn(o.shape, generator=g)
+    (o * do).sum().backward()
+    save("gather_e2e", q=q, k=k, v=v, sel=sel, bias=bias.detach(), o=o.detach(), do=do,
+         dq=qg.grad, dk=kg.grad, dv=vg.grad, dbias=bias.grad,
+         params=np.array([BS, LW]), scale=np.array(0.25))
+    del nb
+
+
+def case_block_max(m):
+    sg = m["sparse_gather_triton"]
+    g = torch.Generator().manual_seed(17)
+    B, C, Sk, D, BS, LW = 2, 90, 200, 64, 16, 40
+    q = torch.randn(B, C, D, generator=g)
+    k = torch.randn(B, Sk, D, generator=g)
+    pos = torch.arange(Sk - C, Sk)[None].repeat(B, 1)
+    seg = torch.zeros(B, C, dtype=torch.long)
+    seg[1, 40:] = 150
+    nblk = (Sk + BS - 1) // BS
+    out = sg.triton_block_max_score(q, k, pos, seg, BS, nblk, LW)
+    save("block_max", q=q, k=k, pos=pos, seg=seg, out=out, params=np.array([BS, LW, nblk]))
+
+
+def case_paged(sgl):
+    """SGLang KBarCache summaries, torch decode scores + route_and_select, and
+    the dash_sparse_attn_decode kernel (interpreter) on a shuffled page pool."""
+    at, st, dr = sgl["attend_triton"], sgl["dash_stage0"], sgl["dash_router"]
+    g = torch.Generator().manual_seed(18)
+    R, H, Hkv, D, d, BS, L, W = 3, 2, 2, 64, 64, 16, 2, 20
+    P = R * W + 3
+    seq = torch.tensor([300, 47, 161], dtype=torch.int32)
+    perm = torch.randperm(P, generator=g)[: R * W].view(R, W).to(torch.int32)
+    k_cache = bf16r(torch.randn(P, BS, Hkv, D, generator=g))
+    v_cache = bf16r(torch.randn(P, BS, Hkv, D, generator=g))
+    idx_cache = bf16r(torch.randn(P, BS, d, generator=g))
+    q = bf16r(torch.randn(R, H, D, generator=g))
+    idx_q = bf16r(torch.randn(R, d, generator=g))
+    hc = torch.randn(d, generator=g) * 0.2
+    cache = st.KBarCache(P, d, "cpu")
+    # summaries of every page in use
+    for r in range(R):
+        nb = (int(seq[r]) + BS - 1) // BS
+        pages = perm[r, :nb].long()
+        pos = torch.arange(nb)[:, None] * BS + torch.arange(BS)[None, :]
+        cache.put(pages, st._summary_keys(idx_cache[pages].float(), pos < int(seq[r]), hc,
+                                          1.0 / math.sqrt(d)))
+    kbar = cache.k_bar.clone()
+    sc = st.headcls_scores_decode(idx_q=idx_q, cache=cache, block_table=perm, seq_lens=seq,
+                                  max_block=W, block_size=BS, local_blocks=L, decode_query_len=1)
+    router = dr.DashRouterMath(index_dim=d, block_size=BS, local_blocks=L, topk_blocks=8,
+                               scaling_factor=5.0, sigma=1.0, prior_floor=1e-3,
+                               budget_remote=3, topm=4)
+    idx, bias = router.route_and_select(sc[0], W)
+    out = torch.zeros(R, H, D)
+    ti = idx.unsqueeze(0).expand(Hkv, -1, -1)
+    tb = bias.unsqueeze(0).expand(Hkv, -1, -1)
+    at.dash_sparse_attn_decode(q, k_cache, v_cache, ti, tb, perm, seq, Hkv, 0.2, out, 1,
+                               local_blocks=L, sparse_block_size=BS)
+    save("paged", q=q, k_cache=k_cache, v_cache=v_cache, idx_cache=idx_cache, idx_q=idx_q,
+         hc=hc, block_table=perm, seq_lens=seq, kbar=kbar, scores=sc[0], idx=idx, bias=bias,
+         out=out, params=np.array([BS, L, 3, 4]), fparams=np.array([5.0 / math.sqrt(d), 1e-3, 1.0, 0.2]))
+
+
+def main():
+    m = import_reference()
+    sgl = import_sglang_ops()
+    torch.manual_seed(0)
+    case_route(m)
+    case_entmax(m)
+    case_decode_attend(m)
+    case_forward_dense(m)
+    case_gather_triton(m)
+    case_gather_e2e(m)
+    case_block_max(m)
+    case_paged(sgl)
+
+
+if __name__ == "__main__":
+    main()

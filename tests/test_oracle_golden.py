@@ -1,0 +1,212 @@
+"""Pin the CPU oracle against golden vectors produced by the reference itself.
+
+The fixtures under tests/golden/ were written by tests/golden/make_golden.py,
+which runs the reference's PyTorch SR-SWA functions, its Triton kernels under
+the Triton CPU interpreter, and the SGLang serving ops from the reference wheel.
+These tests need no GPU and no reference checkout.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import golden
+from oracle import srswa_oracle as O
+
+
+def _sets_equal_except_ties(topi_a, topi_b, valid, scores, tol=1e-5):
+    """Selected index sets per row must match; a mismatch is allowed only when
+    the differing blocks' scores tie (within tol) with the row's boundary."""
+    bad = 0
+    for idx in np.ndindex(topi_a.shape[:-1]):
+        va = valid[idx]
+        a = set(topi_a[idx][va].tolist())
+        b = set(topi_b[idx][va].tolist())
+        if a != b:
+            s = scores[idx]
+            diff = [s[i] for i in (a ^ b)]
+            kth = min(s[i] for i in a | b)
+            if max(abs(x - kth) for x in diff) > tol * max(1.0, abs(kth)):
+                bad += 1
+    return bad
+
+
+def test_entmax_golden():
+    g = golden("entmax")
+    y = O.entmax15(g["x"])
+    np.testing.assert_allclose(y, g["y"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("tag", ["hc0", "hc1"])
+def test_route_headcls_golden(tag):
+    g = golden("route")
+    BS, L, K, M = (int(x) for x in g["params"])
+    idx_scale, floor, sigma = (float(x) for x in g["fparams"])
+    hc = np.zeros(128, np.float32) if tag == "hc0" else g["hc1"]
+    B, S, d = g["idx_k"].shape
+    nblk = (S + BS - 1) // BS
+    kb, cv = O.kbar_contiguous(g["idx_k"], hc, BS, nblk)
+    sc = O.block_scores_headcls(g["idx_q"], kb, cv, g["q_pos"], BS, L)
+    ref = g[f"scores_{tag}"]
+    np.testing.assert_allclose(sc, ref, rtol=2e-5, atol=2e-5)
+    topi, bias, valid = O.infer_route_select(ref, None, idx_scale, floor, sigma, K, M)
+    np.testing.assert_array_equal(valid, g[f"valid_{tag}"])
+    assert _sets_equal_except_ties(topi, g[f"topi_{tag}"], valid, ref) == 0
+    np.testing.assert_allclose(bias, g[f"bias_{tag}"], rtol=1e-5, atol=1e-5)
+
+
+def test_route_cand_and_params_golden():
+    g = golden("route")
+    BS, L, K, M = (int(x) for x in g["params"])
+    idx_scale, floor, sigma = (float(x) for x in g["fparams"])
+    sc = g["scores_hc0"]
+    topi, bias, valid = O.infer_route_select(sc, g["cand"], idx_scale, floor, sigma, K, M)
+    np.testing.assert_array_equal(valid, g["valid_cand"])
+    assert _sets_equal_except_ties(topi, g["topi_cand"], valid, sc) == 0
+    np.testing.assert_allclose(bias, g["bias_cand"], rtol=1e-5, atol=1e-5)
+    s2, f2, sg2, K2, M2 = g["fparams2"]
+    topi, bias, valid = O.infer_route_select(sc, None, s2, f2, sg2, int(K2), int(M2))
+    np.testing.assert_array_equal(valid, g["valid_p2"])
+    assert _sets_equal_except_ties(topi, g["topi_p2"], valid, sc) == 0
+    np.testing.assert_allclose(bias, g["bias_p2"], rtol=1e-5, atol=1e-5)
+
+
+def test_route_indexer_golden():
+    g = golden("route")
+    BS, L, _, _ = (int(x) for x in g["params"])
+    B, S, d = g["idx_k"].shape
+    nblk = (S + BS - 1) // BS
+    sc = O.block_scores_indexer(g["idx_q"], g["idx_k"], g["q_pos"], nblk, BS, L * BS)
+    np.testing.assert_allclose(sc, g["scores_indexer"], rtol=2e-5, atol=2e-4)
+
+
+def test_decode_attend_golden():
+    g = golden("decode_attend")
+    BS, L, K, M = (int(x) for x in g["params"])
+    out = O.decode_attend(g["q"], g["k"], g["v"], g["topi"], g["bias"], g["valid"],
+                          g["q_pos"], BS, L * BS, float(g["scale"]))
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=1e-5)
+
+
+def test_decode_step_golden():
+    """full HF decode step (k_bar + scores + select + attend) on the oracle."""
+    g = golden("decode_attend")
+    BS, L, K, M = (int(x) for x in g["params"])
+    d = g["idx_k"].shape[-1]
+    out, topi, bias, valid = O.decode_step_reference(
+        g["q"], g["k"], g["v"], g["idx_q"], g["idx_k"], np.zeros(d, np.float32), g["q_pos"],
+        BS, L, K, M, 128.0 / np.sqrt(d), 1e-4, 1.0, float(g["scale"]))
+    assert _sets_equal_except_ties(topi, g["topi"], valid, g["scores"]) == 0
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=1e-5)
+
+
+def _sel_from_topi(topi, valid):
+    return np.where(valid, topi, -1)[:, None]
+
+
+def test_forward_dense_golden():
+    g = golden("forward_dense")
+    BS, L = (int(x) for x in g["params"])
+    q, k, v = (np.swapaxes(g[n], 1, 2) for n in ("q", "k", "v"))  # -> [B,T,H,D]
+    sel = _sel_from_topi(g["topi"], g["valid"])
+    B, T = sel.shape[0], sel.shape[2]
+    seg = np.zeros((B, T), np.int64)
+    bias = np.where(g["valid"], g["bias"], 0).astype(np.float32)
+    o, lse = O.gather_attention_fwd(q, k, v, sel, seg, BS, float(g["scale"]), L * BS, bias)
+    np.testing.assert_allclose(np.swapaxes(o, 1, 2), g["o"], rtol=1e-4, atol=2e-5)
+    do = np.swapaxes(g["do"], 1, 2)
+    dq, dk, dv, db = O.gather_attention_bwd(q, k, v, do, sel, seg, BS, float(g["scale"]), L * BS, bias)
+    for name, mine in (("dq", dq), ("dk", dk), ("dv", dv)):
+        np.testing.assert_allclose(np.swapaxes(mine, 1, 2), g[name], rtol=1e-3, atol=1e-4)
+    np.testing.assert_allclose(np.where(g["valid"], db, 0), np.where(g["valid"], g["dbias"], 0),
+                               rtol=1e-3, atol=1e-4)
+
+
+def test_gather_triton_golden():
+    g = golden("gather_triton")
+    BS, LW = (int(x) for x in g["params"])
+    q, k, v = (np.swapaxes(g[n], 1, 2) for n in ("q", "k", "v"))
+    T = q.shape[1]
+    seg = (np.arange(T)[None, :] - g["pos"]).astype(np.int64)
+    sel = O.dedup_rows(g["sel"])
+    o, lse = O.gather_attention_fwd(q, k, v, sel, seg, BS, float(g["scale"]), LW)
+    np.testing.assert_allclose(np.swapaxes(o, 1, 2), g["o"], rtol=1e-4, atol=2e-5)
+    do = np.swapaxes(g["do"], 1, 2)
+    dq, dk, dv, _ = O.gather_attention_bwd(q, k, v, do, sel, seg, BS, float(g["scale"]), LW)
+    for name, mine in (("dq", dq), ("dk", dk), ("dv", dv)):
+        np.testing.assert_allclose(np.swapaxes(mine, 1, 2), g[name], rtol=1e-3, atol=1e-4)
+
+
+def test_gather_e2e_golden():
+    g = golden("gather_e2e")
+    BS, LW = (int(x) for x in g["params"])
+    q, k, v = (np.swapaxes(g[n], 1, 2) for n in ("q", "k", "v"))
+    B, T = q.shape[:2]
+    sel = O.dedup_rows(g["sel"])
+    seg = np.zeros((B, T), np.int64)
+    o, _ = O.gather_attention_fwd(q, k, v, sel, seg, BS, float(g["scale"]), LW, g["bias"])
+    np.testing.assert_allclose(np.swapaxes(o, 1, 2), g["o"], rtol=1e-4, atol=2e-5)
+    do = np.swapaxes(g["do"], 1, 2)
+    dq, dk, dv, db = O.gather_attention_bwd(q, k, v, do, sel, seg, BS, float(g["scale"]), LW, g["bias"])
+    for name, mine in (("dq", dq), ("dk", dk), ("dv", dv)):
+        np.testing.assert_allclose(np.swapaxes(mine, 1, 2), g[name], rtol=1e-3, atol=1e-4)
+    np.testing.assert_allclose(db, g["dbias"], rtol=1e-3, atol=1e-4)
+
+
+def test_block_max_golden():
+    g = golden("block_max")
+    BS, LW, nblk = (int(x) for x in g["params"])
+    out = O.block_max_score(g["q"], g["k"], g["pos"], g["seg"], BS, nblk, LW)
+    ref = g["out"]
+    assert np.array_equal(np.isneginf(out), np.isneginf(ref))
+    fin = np.isfinite(ref)
+    np.testing.assert_allclose(out[fin], ref[fin], rtol=1e-5, atol=1e-4)
+
+
+def test_paged_golden():
+    g = golden("paged")
+    BS, L, Kb, M = (int(x) for x in g["params"])
+    idx_scale, floor, sigma, sm_scale = (float(x) for x in g["fparams"])
+    R, W = g["block_table"].shape
+    d = g["idx_q"].shape[-1]
+    # k_bar of every page in use
+    for r in range(R):
+        n = int(g["seq_lens"][r])
+        nb = (n + BS - 1) // BS
+        pages = g["block_table"][r, :nb]
+        pos = np.arange(nb)[:, None] * BS + np.arange(BS)[None, :]
+        kb = O.kbar_summary(g["idx_cache"][pages], pos < n, g["hc"])
+        np.testing.assert_allclose(kb, g["kbar"][pages], rtol=1e-5, atol=1e-6)
+    # decode scores off the page cache
+    qpos = g["seq_lens"].astype(np.int64) - 1
+    kb_rows = g["kbar"][g["block_table"]]                      # [R,W,d]
+    cv = (np.arange(W)[None, :] * BS) < g["seq_lens"][:, None]
+    sc = O.block_scores_headcls(g["idx_q"][:, None], kb_rows, cv, qpos[:, None], BS, L)[:, 0]
+    np.testing.assert_allclose(sc, g["scores"], rtol=2e-5, atol=2e-5)
+    topi, bias, valid = O.infer_route_select(sc, None, idx_scale, floor, sigma, Kb, M)
+    ref_idx = g["idx"][:, :Kb]
+    mine = np.where(valid, topi, -1)
+    assert _sets_equal_except_ties(mine, ref_idx, valid, sc) == 0
+    np.testing.assert_allclose(bias, g["bias"][:, :Kb], rtol=1e-5, atol=1e-5)
+    out, _ = O.paged_decode(g["q"], g["k_cache"], g["v_cache"], g["idx"][None], g["bias"][None],
+                            g["block_table"], g["seq_lens"], sm_scale, 1, L, BS)
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=2e-5)
+
+
+def test_lse_merge_matches_single_pass():
+    rng = np.random.default_rng(0)
+    s = rng.standard_normal((3, 50)).astype(np.float32)
+    v = rng.standard_normal((50, 8)).astype(np.float32)
+    parts_o, parts_l = [], []
+    for lo, hi in ((0, 20), (20, 20), (20, 50)):
+        if hi == lo:
+            parts_o.append(np.zeros((3, 8), np.float32))
+            parts_l.append(np.full(3, -np.inf, np.float32))
+            continue
+        ss = s[:, lo:hi]
+        m = ss.max(-1, keepdims=True)
+        e = np.exp(ss - m)
+        parts_o.append((e @ v[lo:hi]) / e.sum(-1, keepdims=True))
+        parts_l.append((m + np.log(e.sum(-1, keepdims=True)))[:, 0])
+    o, lse = O.lse_merge(np.stack(parts_o), np.stack(parts_l))
+    e = np.exp(s - s.max(-1, keepdims=True))
+    np.testing.assert_allclose(o, (e @ v) / e.sum(-1, keepdims=True), rtol=1e-5, atol=1e-6)
