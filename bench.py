@@ -1,0 +1,505 @@
+#!/usr/bin/env python
+"""SR-SWA decode benchmark on 1..8 B200s.
+
+One step = one SR-SWA decode step of every request in the batch:
+  k_bar tail-page refresh (a1) -> fused scores + top-M entmax + top-K + bias
+  over the paged k_bar cache (a2+a4) -> block-sparse paged attend of the
+  selected blocks + the 512-token window (a9),
+for 256 concurrent requests with S_r ~ U[16384, 131072] (seeded), page = block
+= 64 tokens, 10 heads x 128, index dim 128, K = 8, M = 16, LW = 512.  Requests
+are sharded across ranks (greedy balance of sum S_r); no collective on the
+data path (strong scaling: the 256 requests are split).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl srswa|reference]
+
+`value` = algorithmic HBM bytes of all ranks' steps / (max-over-ranks device
+time per step), GB/s.  Algorithmic bytes per step: the unique attended keys'
+K and V rows (Hkv*D*2 B each), the k_bar rows of every remote candidate block
+(d*4 B), block-table entries, the refreshed tail pages, q and the outputs.
+The KV cache is resident (~100 GB at N=1); L2 is flushed between timed steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "unlimited-ocr_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
+BS, H, HKV, D, DI, L, K, M = 64, 10, 10, 128, 128, 8, 8, 16
+IDX_SCALE, FLOOR, SIGMA = 128.0 / math.sqrt(DI), 1e-4, 1.0
+SM_SCALE = 1.0 / math.sqrt(D)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="srswa", choices=["srswa", "reference"])
+    ap.add_argument("--requests", type=int, default=256)
+    ap.add_argument("--smin", type=int, default=16384)
+    ap.add_argument("--smax", type=int, default=131072)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+def workload(args):
+    """Seeded request lengths (drawn first from the seed-2 generator)."""
+    g = torch.Generator().manual_seed(2)
+    S = torch.randint(args.smin, args.smax + 1, (args.requests,), generator=g).tolist()
+    return S, g
+
+
+def shard(S, world):
+    """Greedy balance of sum S_r over ranks (the k_bar scan is O(S_r))."""
+    order = sorted(range(len(S)), key=lambda i: -S[i])
+    load = [0] * world
+    parts = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda j: load[j])
+        parts[r].append(i)
+        load[r] += S[i]
+    return [sorted(p) for p in parts]
+
+
+def step_bytes(S_local, topi):
+    """Algorithmic bytes of one decode step for these requests, counted from
+    the emitted selection topi [R, K] (int32, -1 unused)."""
+    attend = route = kbar = 0
+    for r, s in enumerate(S_local):
+        p = s - 1
+        lws = max(0, p - L * BS + 1)
+        remote = 0
+        seen = set()
+        for blk in topi[r].tolist():
+            if blk < 0 or blk in seen:
+                continue
+            seen.add(blk)
+            lo, hi = blk * BS, min((blk + 1) * BS, p + 1, lws)
+            remote += max(0, hi - lo)
+        n_keys = remote + (p + 1 - lws)
+        attend += n_keys * HKV * D * 2 * 2 + 2 * H * D * 2          # K+V rows, q, out
+        cand = max(0, p // BS - L + 1)
+        route += cand * (DI * 4 + 4) + DI * 4 + K * 8                # k_bar rows, table, idx_q, outputs
+        ntok = s - (math.ceil(s / BS) - 1) * BS
+        kbar += ntok * DI * 2 + DI * 4 + 8                          # tail page keys, summary
+    return attend, route, kbar
+
+
+# ---------------------------------------------------------------------------
+class Clocks:
+    """nvidia-smi sampler for the timed region (clocks + throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.idx), "-lms", "50"], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=10)
+        except Exception:
+            self.p.kill()
+            return None
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def peaks():
+    try:
+        p = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic_ratio():
+    """DRAM bytes per algorithmic byte of the attend kernel, from the committed
+    ncu summary (a capture of a smaller case of the same kernel)."""
+    path = os.path.join(ROOT, "profiles", "decode_attend_cfg3.txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_algorithmic_byte:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+def fill_from_pool(t, pool, gen):
+    """Fill a bf16 tensor with windows of a seeded N(0,1) pool at seeded random
+    offsets (generating ~100 GB of fresh normals would dominate the run)."""
+    flat = t.view(-1)
+    n = flat.numel()
+    chunk = pool.numel() // 2
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        off = int(torch.randint(0, pool.numel() - (e - s) + 1, (1,), generator=gen))
+        flat[s:e].copy_(pool[off:off + (e - s)])
+
+
+def build_rank(S_local, seed, dev):
+    from srswa import ops
+    gen = torch.Generator().manual_seed(seed)
+    nb = [math.ceil(s / BS) for s in S_local]
+    R = len(S_local)
+    W = max(nb)
+    P = sum(nb)
+    perm = torch.randperm(P, generator=gen)
+    bt = torch.zeros(R, W, dtype=torch.int32)
+    o = 0
+    for r, n in enumerate(nb):
+        bt[r, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    gdev = torch.Generator(device=dev).manual_seed(seed)
+    pool = torch.randn(1 << 27, device=dev, dtype=torch.bfloat16, generator=gdev)
+    k_cache = torch.empty(P, BS, HKV, D, device=dev, dtype=torch.bfloat16)
+    v_cache = torch.empty_like(k_cache)
+    idx_cache = torch.empty(P, BS, DI, device=dev, dtype=torch.bfloat16)
+    for t in (k_cache, v_cache, idx_cache):
+        fill_from_pool(t, pool, gen)
+    del pool
+    st = dict(
+        bt=bt.to(dev), sl=torch.tensor(S_local, dtype=torch.int32, device=dev),
+        k=k_cache, v=v_cache, idx=idx_cache,
+        kbar=torch.zeros(P, DI, device=dev, dtype=torch.float32),
+        hc=torch.zeros(DI, device=dev),
+        q=torch.randn(R, H, D, generator=gen).to(torch.bfloat16).to(dev),
+        iq=torch.randn(R, DI, generator=gen).to(torch.bfloat16).float().to(dev),
+        out=torch.empty(R, H, D, device=dev, dtype=torch.bfloat16),
+    )
+    ops.kbar_paged(st["idx"], st["hc"], st["bt"], st["sl"], st["kbar"], tail_pages=0)   # prefill summaries
+    torch.cuda.synchronize()
+    return st
+
+
+def run_step(st):
+    """One decode step through the library (device-resident inputs)."""
+    from srswa import ops
+    ops.kbar_paged(st["idx"], st["hc"], st["bt"], st["sl"], st["kbar"], tail_pages=1)
+    r = ops.route(st["iq"], st["kbar"], block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=IDX_SCALE,
+                  floor=FLOOR, sigma=SIGMA, seq_lens=st["sl"], block_table=st["bt"], want=("topi32", "bias"))
+    st["topi"], st["bias"] = r["topi32"], r["bias"]
+    run_attend(st)
+
+
+def run_attend(st):
+    from srswa import ops
+    ops.decode_attend(st["q"], st["k"], st["v"], st["topi"], st["bias"], block_size=BS, local_blocks=L,
+                      sm_scale=SM_SCALE, out=st["out"], block_table=st["bt"], seq_lens=st["sl"])
+
+
+def timed_graph(fn, steps, warmup, flush, use_graph=True):
+    """Per-step device times (ms) of fn, L2 flushed before each step."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(max(warmup, 1)):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = None
+    if use_graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize()
+    run = g.replay if g is not None else fn
+    for _ in range(max(warmup, 1)):
+        run()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        flush.zero_()
+        a.record()
+        run()
+        b.record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev], g
+
+
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(S, budget_s=20.0, max_req=4):
+    """The reference's CPU decode step (oracle port of _block_scores_infer ->
+    _infer_route_select -> _decode_attend, dense over the whole cache) on a
+    bounded sample of the workload's requests.  Returns (GB/s, cores, sample,
+    seconds per request list)."""
+    from oracle import srswa_oracle as O
+    rng = np.random.default_rng(2)
+    done, t_all, bytes_all, lens = 0, 0.0, 0, []
+    for s in S[:max_req]:
+        k = rng.standard_normal((HKV, s, D), dtype=np.float32)
+        v = rng.standard_normal((HKV, s, D), dtype=np.float32)
+        ik = rng.standard_normal((1, s, DI), dtype=np.float32)
+        q = rng.standard_normal((H, D), dtype=np.float32)
+        iq = rng.standard_normal((1, 1, DI), dtype=np.float32)
+        p = s - 1
+        t0 = time.perf_counter()
+        nblk = math.ceil(s / BS)
+        kb, cv = O.kbar_contiguous(ik, np.zeros(DI, np.float32), BS, nblk)
+        sc = O.block_scores_headcls(iq, kb, cv, np.array([[p]]), BS, L)
+        topi, bias, valid = O.infer_route_select(sc, None, IDX_SCALE, FLOOR, SIGMA, K, M)
+        O.decode_attend_one(q, k, v, topi[0, 0], bias[0, 0], valid[0, 0], p, BS, L * BS, SM_SCALE)
+        t_all += time.perf_counter() - t0
+        sel = np.where(valid[0, 0], topi[0, 0], -1)[None].astype(np.int32)
+        a, r_, kk = step_bytes([s], torch.from_numpy(sel))
+        bytes_all += a + r_ + kk
+        lens.append(s)
+        done += 1
+        if t_all > budget_s:
+            break
+    cores = os.cpu_count()
+    return bytes_all / t_all / 1e9, cores, lens, t_all
+
+
+# ---------------------------------------------------------------------------
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    S, _ = workload(args)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        # the reference's own CPU implementation (oracle port), one request per step
+        from oracle import srswa_oracle as O  # noqa: F401
+        order = S[: max(1, args.steps + args.warmup)]
+        per, byts = [], []
+        for i in range(args.warmup + args.steps):
+            gbs, cores, lens, t = cpu_decode_sample([order[i % len(order)]], budget_s=1e9, max_req=1)
+            if i >= args.warmup:
+                per.append(t)
+                byts.append(gbs * t * 1e9)
+        val = sum(byts) / sum(per) / 1e9
+        line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(per) / len(per),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded N(0,1))",
+                "config": {"workload": "cfg3 decode step per request (CPU: HF _block_scores_infer -> "
+                                       "_infer_route_select -> _decode_attend, dense over the cache)",
+                           "requests_per_step": 1, "parallelism": "host cores"},
+                "cpu_baseline": {"value": val, "unit": "GB/s", "cores": cores, "kind": "port",
+                                 "sample": f"{args.steps} request decode steps, S from the cfg3 draw"},
+                "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch.distributed as dist
+    from srswa import ops  # noqa: F401  (fails loudly without libsrswa.so)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    parts = shard(S, world)
+    mine = parts[rank]
+    S_local = [S[i] for i in mine]
+    st = build_rank(S_local, 1000 + rank, dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    # warm-up and selection for byte accounting
+    run_step(st)
+    torch.cuda.synchronize()
+    a_b, r_b, k_b = step_bytes(S_local, st["topi"].cpu())
+    bytes_rank = a_b + r_b + k_b
+
+    clocks = Clocks(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                    os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+    # soak so the clock sampler sees the loaded state, then the timed steps
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t_soak = time.time()
+    while time.time() - t_soak < 1.5:
+        run_step(st)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    times, graph = timed_graph(lambda: run_step(st), args.steps, args.warmup, flush, not args.no_graph)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    step_ms = sum(times) / len(times)
+
+    # dominant kernel alone (attend), same stream discipline
+    att_times, g2 = timed_graph(lambda: run_attend(st), args.steps, args.warmup, flush, not args.no_graph)
+    att_ms = sum(att_times) / len(att_times)
+    rt_times, g3 = timed_graph(lambda: ops.route(st["iq"], st["kbar"], block_size=BS, local_blocks=L, topk=K,
+                                                  topm=M, idx_scale=IDX_SCALE, floor=FLOOR, sigma=SIGMA,
+                                                  seq_lens=st["sl"], block_table=st["bt"],
+                                                  want=("topi32", "bias")),
+                               args.steps, args.warmup, flush, not args.no_graph)
+    rt_ms = sum(rt_times) / len(rt_times)
+
+    # e2e: host buffers through the public API, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_measure(st, S_local, args, dev)
+
+    # reduce across ranks: max time, sum bytes
+    vec = torch.tensor([step_ms, att_ms, rt_ms, e2e["ms"] if e2e else 0.0], device=dev, dtype=torch.float64)
+    tot = torch.tensor([bytes_rank, a_b, e2e["h2d"] if e2e else 0, e2e["d2h"] if e2e else 0],
+                       device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    step_ms, att_ms, rt_ms, e2e_ms = vec.tolist()
+    bytes_all, att_bytes_all, h2d_all, d2h_all = tot.tolist()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, cores, lens, t = cpu_decode_sample(S)
+        cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"{len(lens)} of {len(S)} requests (S={lens}): full HF CPU decode step "
+                         f"(k_bar of every block, scores, top-M entmax, dense attend), {t:.1f} s"}
+
+    peak, src = peaks()
+    att_gbs = (a_b / (att_ms * 1e-3)) / 1e9     # this rank's attend kernel
+    ratio = ncu_traffic_ratio()
+    if graph is not None:
+        del graph, g2, g3
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": bytes_all / (step_ms * 1e-3) / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "us_per_step": step_ms * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded request lengths U[16384,131072]; K/V/index keys N(0,1) bf16 "
+                    "(windows of a seeded randn pool); q, idx_q seeded randn",
+            "config": {"workload": "cfg3 paged SR-SWA decode: 256 requests, S~U[16384,131072], page=block 64, "
+                                   "H=Hkv=10, D=128, index d=128, K=8, M=16, LW=512; per step k_bar tail "
+                                   "refresh + fused route + sparse attend (CUDA graph)",
+                       "global_batch": len(S), "seq_len": "U[16384,131072]", "parallelism": f"requests/dp{world}",
+                       "l2": "flushed (256 MiB write) before every timed step",
+                       "bytes_per_step": bytes_all},
+            "breakdown_us": {"attend": att_ms * 1e3, "route": rt_ms * 1e3},
+            "roofline": {"bound": "hbm", "kernel": "attend_rows_kernel<128,bf16>",
+                         "achieved": att_gbs, "peak": peak, "unit": "GB/s", "frac": att_gbs / peak,
+                         "peak_source": src,
+                         "traffic": (ratio * a_b) if ratio else None,
+                         "algorithmic_bytes_per_launch": a_b},
+            "cpu_baseline": cpu,
+            "e2e": None if e2e is None else {
+                "value": bytes_all / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def e2e_measure(st, S_local, args, dev):
+    """Per step: H2D of this step's q, idx_q, the new token's K/V/index-key
+    rows and its cache slot (pinned host buffers), append to the paged caches,
+    then k_bar refresh, route_decode and dash_sparse_attn_decode through the
+    public paged API, D2H of the output."""
+    from srswa import paged
+    R = len(S_local)
+    g = torch.Generator().manual_seed(77)
+    hq = torch.randn(R, H, D, generator=g).to(torch.bfloat16).pin_memory()
+    hiq = torch.randn(R, DI, generator=g).to(torch.bfloat16).float().pin_memory()
+    hk = torch.randn(R, HKV, D, generator=g).to(torch.bfloat16).pin_memory()
+    hv = torch.randn(R, HKV, D, generator=g).to(torch.bfloat16).pin_memory()
+    hik = torch.randn(R, DI, generator=g).to(torch.bfloat16).pin_memory()
+    bt = st["bt"].cpu()
+    page = torch.tensor([int(bt[r, (s - 1) // BS]) for r, s in enumerate(S_local)], dtype=torch.int64)
+    slot = torch.tensor([(s - 1) % BS for s in S_local], dtype=torch.int64)
+    hslot = torch.stack([page, slot]).pin_memory()
+    hout = torch.empty(R, H, D, dtype=torch.bfloat16).pin_memory()
+    q, iq = torch.empty_like(hq, device=dev), torch.empty_like(hiq, device=dev)
+    nk, nv, nik = (torch.empty_like(x, device=dev) for x in (hk, hv, hik))
+    sl_ = torch.empty_like(hslot, device=dev)
+    out = torch.empty(R, H, D, dtype=torch.bfloat16, device=dev)
+    idx_buf = torch.empty(R, M, dtype=torch.int32, device=dev)
+    bias_buf = torch.empty(R, M, dtype=torch.float32, device=dev)
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hiq, hk, hv, hik, hslot))
+    d2h = hout.numel() * hout.element_size()
+
+    def step():
+        for d_, h_ in ((q, hq), (iq, hiq), (nk, hk), (nv, hv), (nik, hik), (sl_, hslot)):
+            d_.copy_(h_, non_blocking=True)
+        st["k"][sl_[0], sl_[1]] = nk
+        st["v"][sl_[0], sl_[1]] = nv
+        st["idx"][sl_[0], sl_[1]] = nik
+        paged.kbar_refresh_tail(kv_cache=st["idx"], k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"],
+                                head_cls=st["hc"], block_size=BS, tail_pages=1)
+        w = paged.route_decode(idx_q=iq, k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"],
+                               image_allow=None, out_idx=idx_buf, out_bias=bias_buf, max_block=st["bt"].shape[1],
+                               block_size=BS, local_blocks=L, decode_query_len=1, idx_scale=IDX_SCALE,
+                               prior_floor=FLOOR, sigma=SIGMA, topm=M, budget=K)
+        ti = idx_buf[:, :w].unsqueeze(0).expand(HKV, -1, -1)
+        tb = bias_buf[:, :w].unsqueeze(0).expand(HKV, -1, -1)
+        paged.dash_sparse_attn_decode(q, st["k"], st["v"], ti, tb, st["bt"], st["sl"], HKV, SM_SCALE, out, 1,
+                                      local_blocks=L, sparse_block_size=BS)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    return {"ms": e0.elapsed_time(e1) / args.steps, "h2d": h2d, "d2h": d2h}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

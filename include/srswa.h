@@ -1,0 +1,245 @@
+/*
+ * srswa.h -- C ABI of the B200 (sm_100a) SR-SWA hot-path library (libsrswa.so).
+ *
+ * SR-SWA = Sparse-Reference Sliding-Window Attention of Unlimited-OCR 2: every
+ * query attends a token-level local window plus K remote key blocks chosen by
+ * a single-head router.  This library implements the router (block summaries,
+ * scores, top-M 1.5-entmax, top-K, centred log-prior bias), the fused
+ * gather-attention forward/backward, and the paged decode attend with its
+ * split-KV log-sum-exp merge.
+ *
+ * Conventions (all entry points):
+ *   - pointers are device pointers; shapes/strides are int64 element counts;
+ *     the innermost (feature) dimension of every tensor is contiguous;
+ *   - work is enqueued on `stream`; nothing blocks the host; nothing allocates:
+ *     any scratch memory is passed in by the caller (size from the matching
+ *     *_workspace_size query);
+ *   - return 0 on success, a negative SRSWA_E* code for invalid or unsupported
+ *     arguments (nothing was launched), or a positive cudaError_t value.
+ *
+ * Reference citations are paths inside the reference project; "whl:" paths are
+ * files inside its wheel sglang-0.5.20.dev10+g8d62f5fb9c-py3-none-any.whl.
+ */
+#ifndef SRSWA_H
+#define SRSWA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define SRSWA_API __attribute__((visibility("default")))
+#else
+#define SRSWA_API
+#endif
+
+typedef struct CUstream_st* srswa_stream_t; /* == cudaStream_t */
+
+/* element types */
+enum { SRSWA_F32 = 0, SRSWA_BF16 = 1, SRSWA_F16 = 2 };
+
+/* negative status codes */
+enum {
+  SRSWA_OK = 0,
+  SRSWA_EINVAL = -1,       /* bad pointer / negative size / inconsistent shape */
+  SRSWA_EUNSUPPORTED = -2, /* valid but unsupported (head dim, block size, ...) */
+  SRSWA_EALIGN = -3,       /* pointer or stride not 16-byte aligned where needed */
+  SRSWA_EWORKSPACE = -4,   /* caller workspace too small */
+  SRSWA_ETOOLARGE = -5     /* size above a compiled-in maximum */
+};
+
+/* Library version (major*10000 + minor*100 + patch) and status text. */
+SRSWA_API int srswa_version(void);
+SRSWA_API const char* srswa_status_string(int status);
+
+/* ------------------------------------------------------------------ a1 --
+ * head_cls block summaries k_bar of index keys, contiguous sequences.
+ * idx_k [B,S,d] (strides sb, st; d contiguous) -> kbar [B,nblk,d] fp32
+ * contiguous, nblk = ceil(S/block_size); chunk_valid [B,nblk] (optional,
+ * 1 = block holds >= 1 token).
+ * Replaces the head_cls branch of modeling_deepseekv2._block_scores_infer
+ * (hf-model-code/modeling_deepseekv2.py:391-408) and Stage 0 of
+ * DashAttention._block_scores_headcls (hf-model-code/dash_attention.py:1079-1119). */
+SRSWA_API int srswa_kbar_contig(const void* idx_k, int dtype, int64_t sb, int64_t st, int64_t B,
+                      int64_t S, int64_t d, int64_t block_size, const float* head_cls,
+                      float* kbar, uint8_t* chunk_valid, srswa_stream_t stream);
+
+/* head_cls summaries of pages of a paged index-key cache.
+ * idx_cache [P, block_size, d] (strides s_page, s_tok); block_table [R, W]
+ * int32 (row stride s_bt); seq_lens [R] int32.  Refreshes, for each request,
+ * the summaries of its last `tail_pages` pages in use (all pages in use when
+ * tail_pages <= 0) into kbar_cache [P, d] fp32 (row stride s_kbar).
+ * Replaces KBarCache.put/refresh_tail + K11 _kbar_page_kernel
+ * (whl:sglang/srt/layers/attention/unlimited_dash_ops/dash_stage0.py:106-150,
+ *  route_triton.py:36-72, 681-726). */
+SRSWA_API int srswa_kbar_paged(const void* idx_cache, int dtype, int64_t s_page, int64_t s_tok,
+                     int64_t d, int64_t block_size, const int32_t* block_table, int64_t s_bt,
+                     int64_t W, const int32_t* seq_lens, int64_t R, int64_t tail_pages,
+                     const float* head_cls, float* kbar_cache, int64_t s_kbar,
+                     srswa_stream_t stream);
+
+/* --------------------------------------------------------------- a2+a4 --
+ * Router parameters (the per-layer _infer_params dict of
+ * configure_dash_inference, hf-model-code/modeling_deepseekv2.py:296-335). */
+typedef struct {
+  int64_t block_size;   /* BS */
+  int64_t local_blocks; /* L: remote candidates are blocks c <= q_pos/BS - L */
+  int64_t topk;         /* K: slots returned (the reference clamps to <= M) */
+  int64_t topm;         /* M: entmax window (<= 0: whole row) */
+  float idx_scale;      /* entmax input scale (dash_scaling_factor / sqrt(d)) */
+  float prior_floor;    /* log-prior floor */
+  float sigma;          /* bias divisor */
+} srswa_route_params;
+
+/* Fused router over a set of query rows.
+ * Scores: z[n,c] = clamp(idx_q[n] . kbar_c / sqrt(d), +-1e4) for remote blocks
+ * c <= q_pos[n]/BS - L that hold a token, SCORE_NEG (-1e9) elsewhere.  kbar_c
+ * comes either from a contiguous kbar [B, nblk, d] (block_table == NULL; row n
+ * belongs to batch n / rows_per_seq) or from a paged kbar cache [P, d] through
+ * block_table [R, W] (row n belongs to request n / rows_per_seq).
+ * q_pos [N] int64, or NULL to use seq_lens[r] - rows_per_seq + n % rows_per_seq.
+ * seq_lens (NULL allowed when q_pos is given and blocks are contiguous) bounds
+ * blocks holding tokens.  cand [N, nblk] uint8 (row stride s_cand, 0 = shared
+ * row; NULL = all remote blocks) is the page-aware candidate domain.
+ * Selection: _infer_route_select semantics (hf-model-code/modeling_deepseekv2.py:339-362):
+ * top-M by x = cand ? z*idx_scale : -1e4, exact 1.5-entmax over those M,
+ * first K slots, bias = (log max(p, floor) - mean_valid)/sigma.
+ * Outputs (each optional, [N, K] row-major): topi64 (raw indices, score-desc),
+ * topi32 (-1 on invalid slots: the serving layout), bias (0 on invalid),
+ * valid (uint8); scores [N, nblk] fp32 (the _block_scores_infer output).
+ * Replaces _block_scores_infer + _infer_route_select (modeling_deepseekv2.py:339-430)
+ * and route_decode_triton / route_prefill_triton
+ * (whl:.../unlimited_dash_ops/route_triton.py:624-680, 729-847). */
+SRSWA_API int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
+                const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk,
+                const int32_t* block_table, int64_t s_bt, const int32_t* seq_lens,
+                int64_t rows_per_seq, const int64_t* q_pos, const uint8_t* cand,
+                int64_t s_cand, srswa_route_params params, int64_t* topi64, int32_t* topi32,
+                float* bias, uint8_t* valid, float* scores, srswa_stream_t stream);
+
+/* Selection only, from given block scores [N, nblk] (row stride s_sc):
+ * _infer_route_select (hf-model-code/modeling_deepseekv2.py:339-362) and
+ * DashRouterMath.route_and_select (whl:.../unlimited_dash_ops/dash_router.py:131-174). */
+SRSWA_API int srswa_route_select(const float* scores, int64_t s_sc, int64_t N, int64_t nblk,
+                       const uint8_t* cand, int64_t s_cand, srswa_route_params params,
+                       int64_t* topi64, int32_t* topi32, float* bias, uint8_t* valid,
+                       srswa_stream_t stream);
+
+/* ------------------------------------------------------------------ a3 --
+ * Token block-max scores.  q [B,C,D] (strides), k [B,Sk,D], pos/seg [B,C]
+ * int64 (seg may be NULL = 0) -> out [B,C,nblk] fp32 contiguous:
+ * max over keys j of the block with seg <= j < pos - LW + 1, j < Sk, of q.k.
+ * mode 0: triton_block_max_score (hf-model-code/sparse_gather_triton.py:445-524):
+ *         unscaled, ls clamped at 0, -inf where empty.
+ * mode 1: stage0 "indexer" _block_scores_infer
+ *         (hf-model-code/modeling_deepseekv2.py:418-430): clamp(+-1e4),
+ *         SCORE_NEG where empty. */
+SRSWA_API int srswa_block_max_score(const void* q, int q_dtype, int64_t sqb, int64_t sqc, const void* k,
+                          int k_dtype, int64_t skb, int64_t sks, const int64_t* pos,
+                          const int64_t* seg, int64_t B, int64_t C, int64_t Sk, int64_t D,
+                          int64_t block_size, int64_t nblk, int64_t local_window, int mode,
+                          float* out, srswa_stream_t stream);
+
+/* ------------------------------------------------------------------ a5 --
+ * Selection packing: sel [B,HI,T,S] (int32 or int64, is64) -> out int32 with
+ * ids < 0 or >= nblk and repeated ids inside a row set to -1 (the first slot
+ * of an id survives).  Replaces the dedup of triton_gather_attention /
+ * triton_gather_attention_e2e (hf-model-code/sparse_gather_triton.py:418-428,
+ * sparse_gather_e2e_triton.py:383-394). */
+SRSWA_API int srswa_pack_selection(const void* sel, int is64, int64_t rows, int64_t S, int64_t nblk,
+                         int32_t* out, srswa_stream_t stream);
+
+/* --------------------------------------------------------------- a6/a7 --
+ * Fused gather-attention over (selected blocks' keys < local start) U window.
+ * q [B,T,HQ,D], k/v [B,T,Hkv,D] (strides sb, st, sh; D contiguous), sel
+ * [B,HI,T,S] int32 packed (srswa_pack_selection), bias [B,T,S] fp32 per-slot
+ * remote bias or NULL, seg [B,T] int32 segment starts or NULL.
+ * Outputs o [B,T,HQ,D] (o_dtype, strides), lse [B,T,HQ] fp32 natural log.
+ * Replaces K1 _gather_attn_fwd_kernel / K5 _e2e_attn_fwd_kernel
+ * (hf-model-code/sparse_gather_triton.py:35-122, 308-321;
+ *  sparse_gather_e2e_triton.py:36-121, 303-322). */
+typedef struct {
+  int64_t B, T, HQ, Hkv, HI, D, S;
+  int64_t block_size, local_window;
+  float scale;
+  int dtype; /* q/k/v element type */
+  int64_t sqb, sqt, sqh;
+  int64_t skb, skt, skh;
+  int64_t svb, svt, svh;
+} srswa_gather_desc;
+
+SRSWA_API size_t srswa_gather_fwd_workspace_size(const srswa_gather_desc* g);
+SRSWA_API int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v,
+                     const int32_t* sel, const float* bias, const int32_t* seg, void* o,
+                     int o_dtype, int64_t sob, int64_t sot, int64_t soh, float* lse,
+                     void* workspace, size_t workspace_bytes, srswa_stream_t stream);
+
+/* Backward.  do [B,T,HQ,D] (strides as o), o and lse from the forward.
+ * Outputs dq/dk/dv (dtype of q, same strides as q/k/v), d_bias [B,T,S] fp32
+ * (required iff bias != NULL; 0 on -1/deduped slots).  Deterministic, no
+ * atomics.  Replaces K2/K3 (hf-model-code/sparse_gather_triton.py:125-279,
+ * 324-353) and K6/K7 (sparse_gather_e2e_triton.py:124-275, 324-352). */
+SRSWA_API size_t srswa_gather_bwd_workspace_size(const srswa_gather_desc* g);
+SRSWA_API int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v,
+                     const void* o, int64_t sob, int64_t sot, int64_t soh, const void* dout,
+                     const float* lse, const int32_t* sel, const float* bias,
+                     const int32_t* seg, void* dq, void* dk, void* dv, float* d_bias,
+                     void* workspace, size_t workspace_bytes, srswa_stream_t stream);
+
+/* ------------------------------------------------------------------ a9 --
+ * Block-sparse decode attend over a paged (or contiguous) KV cache.
+ * q [N,H,D] (row stride s_qn, head stride s_qh).  k/v caches: element of
+ * (page, pos-in-page, kv head, d) at page*s_page + pos*s_pos + h*s_head + d.
+ * block_table [R,W] int32 maps (request, block) -> page; NULL means one
+ * contiguous cache per request: block blk of request r starts at element
+ * r*s_req + blk*s_page.
+ * Row n belongs to request n / rows_per_req and sits at position
+ * q_pos[n] (int64, optional) or seq_lens[r] - rows_per_req + n % rows_per_req.
+ * topk_idx [.., N, K] (int32 or int64; head stride s_ti_h may be 0; -1 or
+ * valid==0 = unused slot; repeated ids count once), bias same layout (NULL =
+ * no bias), valid uint8 same layout as topk_idx (NULL = all slots with id >= 0).
+ * Remote keys of a selected block: pos <= p and pos < max(0, p-LW+1) (biased);
+ * local keys: max(0, p-LW+1) <= pos <= p (unbiased), LW = L*BS.
+ * out [N,H,D] (out_dtype, strides), lse_out [N,H] fp32 natural log (optional).
+ * nsplit: CTAs per (row, head) merged on-chip through a thread-block cluster
+ * (0 = choose).  Replaces dash_sparse_attn_decode + K9/K10
+ * (whl:.../unlimited_dash_ops/attend_triton.py:307-518, 600-715; common.py:43-89)
+ * and _decode_attend (hf-model-code/modeling_deepseekv2.py:455-481). */
+typedef struct {
+  int64_t N, H, Hkv, D, K;
+  int64_t block_size, local_blocks;
+  float sm_scale;
+  int q_dtype, kv_dtype, out_dtype;
+  int64_t s_qn, s_qh;
+  int64_t s_page, s_pos, s_head;
+  int64_t s_on, s_oh;
+  int64_t R, W, s_req, rows_per_req;
+  int idx_is64;
+  int64_t s_ti_h, s_ti_n; /* topk_idx / bias / valid strides (head, row) */
+  int64_t s_b_h, s_b_n;
+  int nsplit;
+} srswa_decode_desc;
+
+SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache,
+                        const void* v_cache, const int32_t* block_table,
+                        const int32_t* seq_lens, const int64_t* q_pos, const void* topk_idx,
+                        const float* bias, const uint8_t* valid, void* out, float* lse_out,
+                        srswa_stream_t stream);
+
+/* Log-sum-exp merge of C split-KV partials: o_parts [C,N,H,D] fp32, lse_parts
+ * [C,N,H] fp32 natural log (-inf = empty part) -> out [N,H,D] (out_dtype,
+ * contiguous) and lse_out [N,H] (optional).  Replaces
+ * _merge_topk_attn_out_kernel (whl:.../unlimited_dash_ops/common.py:43-89);
+ * also the cross-GPU combine of the split-KV decode. */
+SRSWA_API int srswa_lse_merge(const float* o_parts, const float* lse_parts, int64_t C, int64_t N,
+                    int64_t H, int64_t D, void* out, int out_dtype, float* lse_out,
+                    srswa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SRSWA_H */

@@ -488,6 +488,31 @@ def lse_merge(o_parts, lse_parts):
     return o.astype(F32), lse.astype(F32)
 
 
+def decode_attend_one(q, k_all, v_all, topi, bias, valid, p, block_size, local_window, scale):
+    """``_decode_attend`` for one request and one query row, vectorised over
+    heads (the CPU-baseline unit; same math as ``decode_attend``).
+    q [H,D], k_all/v_all [Hkv,S,D], topi/bias/valid [K] -> [H,D]."""
+    H, D = q.shape
+    Hkv, S, _ = k_all.shape
+    nblk = (S + block_size - 1) // block_size
+    blk = np.full(nblk, MASK_NEG, F32)
+    for s in range(topi.shape[0]):
+        blk[int(topi[s])] = bias[s] if valid[s] else MASK_NEG
+    kpos = np.arange(S)
+    base = blk[kpos // block_size]
+    causal = kpos <= p
+    local = causal & (kpos > p - local_window)
+    keep = causal & (local | (base > MASK_NEG * F32(0.5)))
+    madd = np.where(keep, np.where(local, F32(0.0), base), -np.inf).astype(F32)
+    G = H // Hkv
+    qg = q.reshape(Hkv, G, D).astype(F32)
+    s_ = np.matmul(qg, np.swapaxes(k_all, 1, 2).astype(F32)) * F32(scale) + madd   # [Hkv,G,S]
+    s_ = s_ - s_.max(-1, keepdims=True)
+    e = np.exp(s_).astype(F32)
+    e /= e.sum(-1, keepdims=True, dtype=F32)
+    return np.matmul(e, v_all.astype(F32)).reshape(H, -1)
+
+
 # ---------------------------------------------------------------------------
 # composite: one decode step of the HF inference path (CPU baseline unit)
 # ---------------------------------------------------------------------------

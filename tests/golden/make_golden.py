@@ -193,7 +193,7 @@ def case_forward_dense(m):
     da = m["dash_attention"]
     md = m["modeling_deepseekv2"]
     g = torch.Generator().manual_seed(14)
-    B, H, S, D, BS, L, K = 2, 2, 256, 32, 32, 2, 4
+    B, H, S, D, BS, L, K = 2, 2, 256, 64, 32, 2, 4
     nblk = (S + BS - 1) // BS
     q = bf16r(torch.randn(B, H, S, D, generator=g))
     k = bf16r(torch.randn(B, H, S, D, generator=g))
@@ -231,13 +231,14 @@ def case_gather_triton(m):
     packing (seg), two index heads, duplicate ids and -1 padding."""
     sg = m["sparse_gather_triton"]
     g = torch.Generator().manual_seed(15)
-    B, HQ, Hkv, T, D, BS, S, LW = 2, 4, 2, 160, 32, 16, 4, 40
-    q = torch.randn(B, HQ, T, D, generator=g)
-    k = torch.randn(B, Hkv, T, D, generator=g)
-    v = torch.randn(B, Hkv, T, D, generator=g)
+    B, HQ, Hkv, T, D, BS, S, LW = 2, 4, 2, 224, 64, 32, 4, 72
+    # bf16-representable fp32 inputs: the GPU runs bf16 on exactly these values
+    q = bf16r(torch.randn(B, HQ, T, D, generator=g))
+    k = bf16r(torch.randn(B, Hkv, T, D, generator=g))
+    v = bf16r(torch.randn(B, Hkv, T, D, generator=g))
     nb = (T + BS - 1) // BS
     pos = torch.arange(T)[None].repeat(B, 1)
-    pos[1, 70:] = torch.arange(T - 70)         # packed: 2nd sample starts at 70
+    pos[1, 90:] = torch.arange(T - 90)         # packed: 2nd sample starts at 90
     # The reference K1 has no NaN-safe running max (sparse_gather_triton.py:90-94):
     # a leading selected block with no kept key gives NaN.  Its callers only
     # select remote blocks, so slot 0 holds a block with >= 1 key in
@@ -270,17 +271,17 @@ def case_gather_e2e(m):
     to q/k/v and the per-slot bias."""
     se = m["sparse_gather_e2e_triton"]
     g = torch.Generator().manual_seed(16)
-    B, H, T, D, BS, S, LW = 2, 3, 150, 32, 16, 3, 48
-    q = torch.randn(B, H, T, D, generator=g)
-    k = torch.randn(B, H, T, D, generator=g)
-    v = torch.randn(B, H, T, D, generator=g)
+    B, H, T, D, BS, S, LW = 2, 2, 200, 64, 32, 3, 64
+    q = bf16r(torch.randn(B, H, T, D, generator=g))
+    k = bf16r(torch.randn(B, H, T, D, generator=g))
+    v = bf16r(torch.randn(B, H, T, D, generator=g))
     nb = (T + BS - 1) // BS
     sel = torch.full((B, 1, T, S), -1, dtype=torch.long)
     for b in range(B):
         for t in range(T):
             cand = torch.randperm(t // BS + 1, generator=g)[:S]
             sel[b, 0, t, :cand.numel()] = cand
-    sel[0, 0, 100, 2] = sel[0, 0, 100, 0]      # one duplicate
+    sel[0, 0, 150, 2] = sel[0, 0, 150, 0]      # one duplicate
     bias = (torch.randn(B, T, S, generator=g) * 0.5).requires_grad_(True)
     pos = torch.arange(T)[None].repeat(B, 1)
     qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
@@ -297,8 +298,8 @@ def case_block_max(m):
     sg = m["sparse_gather_triton"]
     g = torch.Generator().manual_seed(17)
     B, C, Sk, D, BS, LW = 2, 90, 200, 64, 16, 40
-    q = torch.randn(B, C, D, generator=g)
-    k = torch.randn(B, Sk, D, generator=g)
+    q = bf16r(torch.randn(B, C, D, generator=g))
+    k = bf16r(torch.randn(B, Sk, D, generator=g))
     pos = torch.arange(Sk - C, Sk)[None].repeat(B, 1)
     seg = torch.zeros(B, C, dtype=torch.long)
     seg[1, 40:] = 150
@@ -312,9 +313,9 @@ def case_paged(sgl):
     the dash_sparse_attn_decode kernel (interpreter) on a shuffled page pool."""
     at, st, dr = sgl["attend_triton"], sgl["dash_stage0"], sgl["dash_router"]
     g = torch.Generator().manual_seed(18)
-    R, H, Hkv, D, d, BS, L, W = 3, 2, 2, 64, 64, 16, 2, 20
+    R, H, Hkv, D, d, BS, L, W = 3, 2, 2, 64, 64, 32, 2, 12
     P = R * W + 3
-    seq = torch.tensor([300, 47, 161], dtype=torch.int32)
+    seq = torch.tensor([350, 47, 161], dtype=torch.int32)
     perm = torch.randperm(P, generator=g)[: R * W].view(R, W).to(torch.int32)
     k_cache = bf16r(torch.randn(P, BS, Hkv, D, generator=g))
     v_cache = bf16r(torch.randn(P, BS, Hkv, D, generator=g))

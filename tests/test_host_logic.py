@@ -1,0 +1,66 @@
+"""Host-side contract of the Python boundary (no GPU needed): the same
+None-return cases as the reference wrappers, effective K/M, loud failure on
+CPU tensors (no CPU fallback)."""
+
+import pytest
+import torch
+
+from srswa import _lib as L
+from srswa import ops
+from srswa.sparse_gather import SPARSE_BLOCK_SIZE_SENTINEL, triton_gather_attention
+from srswa.sparse_gather_e2e import SPARSE_E2E_SENTINEL, triton_gather_attention_e2e
+
+
+def _qkv(B=1, H=2, T=64, D=64):
+    q = torch.zeros(B, H, T, D, dtype=torch.bfloat16)
+    return q, q.clone(), q.clone()
+
+
+def test_sentinels():
+    assert SPARSE_BLOCK_SIZE_SENTINEL == 128 and SPARSE_E2E_SENTINEL == 1
+
+
+def test_gather_returns_none_like_reference():
+    q, k, v = _qkv()
+    sel = torch.zeros(1, 1, 64, 2, dtype=torch.int32)
+    pos = torch.arange(64)[None]
+    # sparse_gather_triton.py:400-412
+    assert triton_gather_attention(q, k, v, sel, pos, torch.zeros(1), 32, 0.1) is None
+    assert triton_gather_attention(q, k, v, torch.zeros(1, 3, 64, 2, dtype=torch.int32), pos, None, 32, 0.1) is None
+    assert triton_gather_attention(q, k[:, :, :32], v[:, :, :32], sel, pos, None, 32, 0.1) is None
+    assert triton_gather_attention(q, k, v, sel, None, None, 32, 0.1) is None
+    assert triton_gather_attention(q, k, v, sel, pos[0], None, 32, 0.1) is None
+
+
+def test_gather_e2e_returns_none_like_reference():
+    q, k, v = _qkv()
+    sel = torch.zeros(1, 1, 64, 2, dtype=torch.int32)
+    b = torch.zeros(1, 64, 2)
+    pos = torch.arange(64)[None]
+    # sparse_gather_e2e_triton.py:370-381
+    assert triton_gather_attention_e2e(q, k, v, sel, b, pos, torch.zeros(1), 32, 0.1) is None
+    assert triton_gather_attention_e2e(q, k, v, torch.zeros(1, 2, 64, 2), b, pos, None, 32, 0.1) is None
+    assert triton_gather_attention_e2e(q, k[:, :, :32], v[:, :, :32], sel, b, pos, None, 32, 0.1) is None
+    packed = pos.clone()
+    packed[0, 40:] = torch.arange(24)
+    assert triton_gather_attention_e2e(q, k, v, sel, b, packed, None, 32, 0.1) is None
+
+
+def test_unsupported_head_dim_raises():
+    q, k, v = _qkv(D=96)
+    sel = torch.zeros(1, 1, 64, 2, dtype=torch.int32)
+    with pytest.raises(NotImplementedError):
+        triton_gather_attention(q, k, v, sel, torch.arange(64)[None], None, 32, 0.1)
+
+
+def test_cpu_tensors_fail_loudly():
+    x = torch.zeros(4, 128)
+    with pytest.raises(L.SrswaError):
+        ops.route_select(x, None, topk=2, topm=4, idx_scale=1.0, floor=1e-4, sigma=1.0)
+
+
+@pytest.mark.parametrize("topk,topm,nblk,K,M", [(8, 16, 100, 8, 16), (8, 16, 5, 5, 5), (12, 4, 50, 4, 4),
+                                                 (0, 16, 50, 1, 16), (3, 0, 20, 3, 20)])
+def test_effective_km(topk, topm, nblk, K, M):
+    # _infer_route_select: M = max(1, min(topm, nblk)) if topm > 0 else nblk; K = max(1, min(K, M))
+    assert ops.effective_km(topk, topm, nblk) == (K, M)

@@ -1,0 +1,389 @@
+// Row-streaming sparse attend: one query row x one head per CTA (or per
+// cluster of CTAs), keys = selected remote blocks U local window.
+//
+// Used by
+//   * the paged decode attend, semantics of dash_sparse_attn_decode / K9+K10
+//     (whl:sglang/srt/layers/attention/unlimited_dash_ops/attend_triton.py:307-518,
+//     600-715; common.py:43-89) and _decode_attend
+//     (hf-model-code/modeling_deepseekv2.py:455-481);
+//   * the query-major gather-attention forward, semantics of K1/K5
+//     (hf-model-code/sparse_gather_triton.py:35-122; sparse_gather_e2e_triton.py:36-121).
+//
+// For a query at position p with segment start sg (0 when unpacked):
+//   ls = max(p - LW + 1, sg)
+//   remote keys: keys j of selected blocks with sg <= j < ls and j <= p,
+//                logit scale*q.k + bias(slot)
+//   local keys:  ls <= j <= p, logit scale*q.k
+// One softmax over the (disjoint) union; empty rows give o = 0, lse = -inf.
+// Unused slots (id < 0, >= W, or valid == 0) are skipped wherever they sit; a
+// repeated block id counts once.
+//
+// Design (memory-bound per row):
+//   * grid.x = rows * nsplit, grid.y = heads; the nsplit CTAs of one
+//     (row, head) form a thread-block cluster and merge (m, l, o) through
+//     distributed shared memory: no global scratch, no second launch;
+//   * each warp streams chunks of KPC keys: lanes form groups of LPK = D/8,
+//     each lane loads 16 B (8 elements) of a key row, so a warp instruction
+//     covers 32/LPK whole rows (fully coalesced 128-bit loads);
+//   * q.k partials are combined by a transposed butterfly (7-8 shuffles per 8
+//     keys); online softmax in the log2 domain; P.V accumulates 8 features per
+//     lane in fp32.
+
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "attend.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace srswa {
+
+struct SlotInfo {
+  int64_t page_off;  // element offset of the block (without pos / head)
+  int64_t key0;      // absolute position of the block's first key
+  float bias2;       // bias * log2(e) (0 for local)
+  int remote;        // 1 remote, 0 local
+};
+
+__device__ __forceinline__ void attend_row_position(const AttendArgs& a, int64_t row, int64_t& seq,
+                                                    int64_t& t, int64_t& p, int64_t& sg) {
+  seq = row / a.rps;
+  t = row % a.rps;
+  if (a.pos_mode == 0) p = a.q_pos[row];
+  else if (a.pos_mode == 1) p = static_cast<int64_t>(a.seq_lens[seq]) - a.rps + t;
+  else p = t;
+  sg = a.seg ? static_cast<int64_t>(a.seg[row]) : 0;
+}
+
+__device__ __forceinline__ int64_t block_offset(const AttendArgs& a, int64_t seq, int64_t blk) {
+  if (a.block_table) return static_cast<int64_t>(a.block_table[seq * a.s_bt + blk]) * a.s_page;
+  return seq * a.s_seq + blk * a.s_blk;
+}
+
+template <int D, int KVT>
+__global__ void __launch_bounds__(kAttendThreads) attend_rows_kernel(const AttendArgs a) {
+  constexpr int LPK = D / 8;     // lanes per key row
+  constexpr int KPI = 32 / LPK;  // key rows per warp load instruction
+  constexpr int KPC = KPI * 8;   // keys per chunk (8 loads per lane)
+
+  __shared__ SlotInfo slots[kAttendMaxSlots];
+  __shared__ int n_slots;
+  __shared__ float w_m[kAttendWarps], w_l[kAttendWarps];
+  __shared__ __align__(16) float w_o[kAttendWarps][D];
+  __shared__ float c_m, c_l;
+  __shared__ __align__(16) float c_o[D];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nsplit = a.nsplit;
+  const int64_t row = blockIdx.x / nsplit;
+  const int split = blockIdx.x % nsplit;
+  const int h = blockIdx.y;
+  const int hk = static_cast<int>(h / (a.H / a.Hkv));
+  const int hi = static_cast<int>((static_cast<int64_t>(hk) * a.HI) / a.Hkv);
+  int64_t seq, t, p, sg;
+  attend_row_position(a, row, seq, t, p, sg);
+  const int64_t BS = a.BS;
+  int64_t ls = p - a.LW + 1;
+  if (ls < sg) ls = sg;
+  if (ls < 0) ls = 0;
+
+  // ---- slot list: remote selections (deduped, useful only), then window ----
+  if (tid == 0) {
+    int n = 0;
+    if (p >= 0 && p >= sg) {
+      const int64_t ibase = seq * a.s_sel_seq + t * a.s_sel_t + hi * a.s_sel_h;
+      const int64_t bbase = seq * a.s_b_seq + t * a.s_b_t + hi * a.s_b_h;
+      for (int64_t s = 0; s < a.K && n < kAttendMaxSlots; ++s) {
+        const int64_t blk = load_index(a.sel, ibase + s, a.idx_is64);
+        if (blk < 0 || blk >= a.W) continue;
+        if (a.valid && !a.valid[ibase + s]) continue;
+        // a remote key must satisfy sg <= j < ls and j <= p
+        const int64_t lo = blk * BS > sg ? blk * BS : sg;
+        const int64_t hi_ = (blk + 1) * BS < ls ? (blk + 1) * BS : ls;
+        if (lo >= hi_ || lo > p) continue;
+        bool dup = false;
+        for (int j = 0; j < n; ++j) dup |= (slots[j].key0 == blk * BS);
+        if (dup) continue;
+        slots[n].page_off = block_offset(a, seq, blk);
+        slots[n].key0 = blk * BS;
+        slots[n].bias2 = a.bias ? a.bias[bbase + s] * kLog2e : 0.f;
+        slots[n].remote = 1;
+        ++n;
+      }
+      if (!a.skip_local) {
+        for (int64_t blk = ls / BS; blk <= p / BS && n < kAttendMaxSlots; ++blk) {
+          if (blk >= a.W) break;
+          slots[n].page_off = block_offset(a, seq, blk);
+          slots[n].key0 = blk * BS;
+          slots[n].bias2 = 0.f;
+          slots[n].remote = 0;
+          ++n;
+        }
+      }
+    }
+    n_slots = n;
+  }
+  __syncthreads();
+
+  // ---- this lane's slice of q (pre-scaled into the log2 domain) ----
+  const int g = lane / LPK, u = lane % LPK;
+  float qv[8];
+  load8(a.q, seq * a.s_q_seq + t * a.s_q_t + static_cast<int64_t>(h) * a.s_qh + u * 8, a.q_dtype, qv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) qv[e] *= a.q_scale_log2;
+
+  const int cpb = static_cast<int>(BS / KPC);  // chunks per block
+  const int nch = n_slots * cpb;
+  const int c_begin = static_cast<int>((static_cast<int64_t>(nch) * split) / nsplit);
+  const int c_end = static_cast<int>((static_cast<int64_t>(nch) * (split + 1)) / nsplit);
+
+  float m = -INFINITY, lsum = 0.f;
+  float o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = 0.f;
+  // after transpose_reduce8 each key's score sits in LPK/8 lanes; count it once
+  const int count_lane = (u & (LPK / 8 - 1)) == 0;
+  const int my_idx = 4 * ((u & (LPK / 2)) != 0) + 2 * ((u & (LPK / 4)) != 0) + ((u & (LPK / 8)) != 0);
+
+  for (int ch = c_begin + warp; ch < c_end; ch += kAttendWarps) {
+    const SlotInfo si = slots[ch / cpb];
+    const int sub = ch % cpb;
+    const int64_t k0 = si.key0 + static_cast<int64_t>(sub) * KPC;
+    int64_t lo, hi_;  // valid absolute key range [lo, hi_)
+    if (si.remote) {
+      lo = k0 > sg ? k0 : sg;
+      hi_ = min(min(k0 + KPC, p + 1), ls);
+    } else {
+      lo = k0 > ls ? k0 : ls;
+      hi_ = min(k0 + KPC, p + 1);
+    }
+    if (lo >= hi_) continue;  // warp-uniform
+
+    const int64_t base = si.page_off + static_cast<int64_t>(hk) * a.s_head +
+                         static_cast<int64_t>(sub) * KPC * a.s_pos + u * 8;
+    uint4 kr[8], vr[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int j = i * KPI + g;
+      const int64_t pos = k0 + j;
+      if (pos >= lo && pos < hi_) {
+        const int64_t off = base + j * a.s_pos;
+        kr[i] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(a.k) + off));
+        vr[i] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(a.v) + off));
+      } else {
+        kr[i] = make_uint4(0, 0, 0, 0);
+        vr[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    float part[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float f[8];
+      unpack8<KVT>(kr[i], f);
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaf(qv[e], f[e], acc);
+      part[i] = acc;
+    }
+    const float dot = transpose_reduce8<LPK>(part, u);
+    const int64_t my_pos = k0 + my_idx * KPI + g;
+    const float s2 = (my_pos >= lo && my_pos < hi_) ? dot + si.bias2 : -INFINITY;
+    const float cmax = warp_max(s2);
+    const float m_new = fmaxf(m, cmax);
+    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+    const float alpha = exp2f(m - m_use);
+    const float pr = exp2f(s2 - m_use);
+    lsum = lsum * alpha + (count_lane ? pr : 0.f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] *= alpha;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float pi = __shfl_sync(0xffffffffu, pr, g * LPK + transpose_owner<LPK>(i));
+      float f[8];
+      unpack8<KVT>(vr[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = fmaf(pi, f[e], o[e]);
+    }
+    m = m_new;
+  }
+
+  // ---- warp combine: sum l over lanes, o over key groups ----
+  lsum = warp_sum(lsum);
+#pragma unroll
+  for (int msk = LPK; msk < 32; msk <<= 1) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] += __shfl_xor_sync(0xffffffffu, o[e], msk);
+  }
+  if (lane == 0) { w_m[warp] = m; w_l[warp] = lsum; }
+  if (lane < LPK) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w_o[warp][u * 8 + e] = o[e];
+  }
+  __syncthreads();
+
+  // ---- CTA combine ----
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kAttendWarps; ++w) M = fmaxf(M, w_m[w]);
+  const float Mu = (M == -INFINITY) ? 0.f : M;
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < kAttendWarps; ++w) L += w_l[w] * exp2f(w_m[w] - Mu);
+  for (int d = tid; d < D; d += kAttendThreads) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttendWarps; ++w) acc += w_o[w][d] * exp2f(w_m[w] - Mu);
+    c_o[d] = acc;
+  }
+  if (tid == 0) { c_m = M; c_l = L; }
+
+  const int64_t obase = seq * a.s_o_seq + t * a.s_o_t + static_cast<int64_t>(h) * a.s_oh;
+  const int64_t lbase = seq * a.s_l_seq + t * a.s_l_t + h;
+  if (nsplit == 1) {
+    __syncthreads();
+    const float inv = c_l > 0.f ? 1.f / c_l : 0.f;
+    for (int d = tid; d < D; d += kAttendThreads) store_elem(a.out, obase + d, a.out_dtype, c_o[d] * inv);
+    if (tid == 0 && a.lse_out) a.lse_out[lbase] = c_l > 0.f ? (c_m + log2f(c_l)) * kLn2 : -INFINITY;
+    return;
+  }
+
+  // ---- cluster combine through distributed shared memory ----
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  if (cluster.block_rank() == 0) {
+    float Mg = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) Mg = fmaxf(Mg, *cluster.map_shared_rank(&c_m, s));
+    const float Mgu = (Mg == -INFINITY) ? 0.f : Mg;
+    float Lg = 0.f;
+    for (int s = 0; s < nsplit; ++s)
+      Lg += *cluster.map_shared_rank(&c_l, s) * exp2f(*cluster.map_shared_rank(&c_m, s) - Mgu);
+    const float inv = Lg > 0.f ? 1.f / Lg : 0.f;
+    for (int d = tid; d < D; d += kAttendThreads) {
+      float acc = 0.f;
+      for (int s = 0; s < nsplit; ++s)
+        acc += cluster.map_shared_rank(c_o, s)[d] * exp2f(*cluster.map_shared_rank(&c_m, s) - Mgu);
+      store_elem(a.out, obase + d, a.out_dtype, acc * inv);
+    }
+    if (tid == 0 && a.lse_out) a.lse_out[lbase] = Lg > 0.f ? (Mg + log2f(Lg)) * kLn2 : -INFINITY;
+  }
+  cluster.sync();
+}
+
+template <int D, int KVT>
+static int launch_attend(const AttendArgs& a, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.N * a.nsplit), static_cast<unsigned>(a.H), 1);
+  cfg.blockDim = dim3(kAttendThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.nsplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attend_rows_kernel<D, KVT>, a);
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
+  if (a.N == 0) return 0;
+  if (!(D == 64 || D == 128)) return SRSWA_EUNSUPPORTED;
+  if (!(kv_dtype == SRSWA_BF16 || kv_dtype == SRSWA_F16)) return SRSWA_EUNSUPPORTED;
+  const int kpc = (32 / (static_cast<int>(D) / 8)) * 8;
+  if (a.BS % kpc != 0) return SRSWA_EUNSUPPORTED;
+  if (a.K + a.LW / a.BS + 2 > kAttendMaxSlots) return SRSWA_ETOOLARGE;
+  if (a.H >= 65536) return SRSWA_ETOOLARGE;
+  int nsplit = a.nsplit;
+  if (nsplit <= 0) {
+    // enough CTAs for ~4 per SM on 148 SMs; at most 8 (portable cluster size)
+    const int64_t want = (148 * 4 + a.N * a.H - 1) / (a.N * a.H);
+    nsplit = 1;
+    while (nsplit * 2 <= want && nsplit < 8) nsplit *= 2;
+  }
+  if (nsplit < 1 || nsplit > 8) return SRSWA_EUNSUPPORTED;
+  if (a.N * nsplit >= (1ll << 31)) return SRSWA_ETOOLARGE;
+  a.nsplit = nsplit;
+  if (D == 128) {
+    if (kv_dtype == SRSWA_BF16) return launch_attend<128, SRSWA_BF16>(a, st);
+    return launch_attend<128, SRSWA_F16>(a, st);
+  }
+  if (kv_dtype == SRSWA_BF16) return launch_attend<64, SRSWA_BF16>(a, st);
+  return launch_attend<64, SRSWA_F16>(a, st);
+}
+
+__global__ void lse_merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ lse_parts,
+                                 int64_t C, int64_t NH, int64_t D, void* out, int out_dtype,
+                                 float* lse_out) {
+  const int64_t nh = blockIdx.x;
+  float M = -INFINITY;
+  for (int64_t c = 0; c < C; ++c) M = fmaxf(M, lse_parts[c * NH + nh]);
+  const float Mu = (M == -INFINITY) ? 0.f : M;
+  float den = 0.f;
+  for (int64_t c = 0; c < C; ++c) {
+    const float l = lse_parts[c * NH + nh];
+    den += (l == -INFINITY) ? 0.f : expf(l - Mu);
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int64_t c = 0; c < C; ++c) {
+      const float l = lse_parts[c * NH + nh];
+      if (l != -INFINITY) acc += expf(l - Mu) * o_parts[(c * NH + nh) * D + d];
+    }
+    store_elem(out, nh * D + d, out_dtype, acc * inv);
+  }
+  if (threadIdx.x == 0 && lse_out) lse_out[nh] = den > 0.f ? Mu + logf(den) : -INFINITY;
+}
+
+}  // namespace srswa
+
+using namespace srswa;
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache,
+                                   const void* v_cache, const int32_t* block_table,
+                                   const int32_t* seq_lens, const int64_t* q_pos,
+                                   const void* topk_idx, const float* bias, const uint8_t* valid,
+                                   void* out, float* lse_out, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(dd && q && k_cache && v_cache && out, SRSWA_EINVAL);
+  const srswa_decode_desc& d = *dd;
+  SRSWA_CHECK_ARG(d.N >= 0 && d.H > 0 && d.Hkv > 0 && d.H % d.Hkv == 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(d.K >= 0 && (d.K == 0 || topk_idx), SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(q_pos || seq_lens, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(d.rows_per_req > 0 && d.block_size > 0 && d.local_blocks >= 0 && d.W > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(aligned16(q) && aligned16(k_cache) && aligned16(v_cache), SRSWA_EALIGN);
+  SRSWA_CHECK_ARG(((d.s_page | d.s_pos | d.s_head) & 7) == 0, SRSWA_EALIGN);
+  SRSWA_CHECK_ARG(((d.s_qn | d.s_qh) & (d.q_dtype == SRSWA_F32 ? 3 : 7)) == 0, SRSWA_EALIGN);
+  AttendArgs a = {};
+  a.q = q; a.k = k_cache; a.v = v_cache; a.q_dtype = d.q_dtype; a.out_dtype = d.out_dtype;
+  a.N = d.N; a.rps = d.rows_per_req; a.H = d.H; a.Hkv = d.Hkv;
+  a.seq_lens = seq_lens; a.q_pos = q_pos; a.seg = nullptr;
+  a.pos_mode = q_pos ? 0 : 1;
+  a.block_table = block_table; a.s_bt = d.W; a.W = d.W;
+  a.s_page = d.s_page; a.s_seq = d.s_req; a.s_blk = d.s_page;
+  a.s_pos = d.s_pos; a.s_head = d.s_head;
+  a.sel = topk_idx; a.idx_is64 = d.idx_is64; a.K = d.K; a.valid = valid;
+  a.s_sel_seq = d.rows_per_req * d.s_ti_n; a.s_sel_t = d.s_ti_n; a.s_sel_h = d.s_ti_h; a.HI = d.Hkv;
+  a.bias = bias; a.s_b_seq = d.rows_per_req * d.s_b_n; a.s_b_t = d.s_b_n; a.s_b_h = d.s_b_h;
+  a.BS = d.block_size; a.LW = d.local_blocks * d.block_size;
+  a.q_scale_log2 = d.sm_scale * kLog2e;
+  a.s_q_seq = d.rows_per_req * d.s_qn; a.s_q_t = d.s_qn; a.s_qh = d.s_qh;
+  a.out = out; a.s_o_seq = d.rows_per_req * d.s_on; a.s_o_t = d.s_on; a.s_oh = d.s_oh;
+  a.lse_out = lse_out; a.s_l_seq = d.rows_per_req * d.H; a.s_l_t = d.H;
+  a.nsplit = d.nsplit; a.skip_local = 0;
+  return attend_rows_launch(a, d.D, d.kv_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int srswa_lse_merge(const float* o_parts, const float* lse_parts, int64_t C, int64_t N,
+                               int64_t H, int64_t D, void* out, int out_dtype, float* lse_out,
+                               srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(o_parts && lse_parts && out && C > 0 && N >= 0 && H > 0 && D > 0, SRSWA_EINVAL);
+  if (N == 0) return 0;
+  SRSWA_CHECK_ARG(N * H < (1ll << 31), SRSWA_ETOOLARGE);
+  lse_merge_kernel<<<static_cast<unsigned>(N * H), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      o_parts, lse_parts, C, N * H, D, out, out_dtype, lse_out);
+  return srswa_last_launch_status();
+}

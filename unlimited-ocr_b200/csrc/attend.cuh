@@ -1,0 +1,66 @@
+// Internal interface of the row-streaming sparse attend (attend.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace srswa {
+
+constexpr int kAttendWarps = 4;
+constexpr int kAttendThreads = kAttendWarps * 32;
+constexpr int kAttendMaxSlots = 64;  // remote slots + window blocks per row
+
+// Row n is (seq = n / rps, t = n % rps).  Its query position p is q_pos[n]
+// (pos_mode 0), seq_lens[seq] - rps + t (pos_mode 1) or t (pos_mode 2).
+// A key block blk of sequence seq starts at element
+//   block_table[seq * s_bt + blk] * s_page      (paged), or
+//   seq * s_seq + blk * s_blk                   (contiguous),
+// and key position i inside it / kv head h add i * s_pos + h * s_head.
+struct AttendArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  int q_dtype, out_dtype;
+  int64_t N, rps, H, Hkv;
+  const int32_t* seq_lens;
+  const int64_t* q_pos;
+  const int32_t* seg;  // per row segment start (NULL = 0)
+  int pos_mode;
+  const int32_t* block_table;
+  int64_t s_bt, W;
+  int64_t s_page, s_seq, s_blk, s_pos, s_head;
+  const void* sel;  // selection ids, offset seq*s_sel_seq + t*s_sel_t + hi*s_sel_h + slot
+  int idx_is64;
+  int64_t K, s_sel_seq, s_sel_t, s_sel_h, HI;
+  const uint8_t* valid;  // same offsets as sel (NULL = every id >= 0 is used)
+  const float* bias;     // offset seq*s_b_seq + t*s_b_t + hi*s_b_h + slot (NULL = 0)
+  int64_t s_b_seq, s_b_t, s_b_h;
+  int64_t BS, LW;
+  float q_scale_log2;
+  int64_t s_q_seq, s_q_t, s_qh;
+  void* out;
+  int64_t s_o_seq, s_o_t, s_oh;
+  float* lse_out;  // natural log, offset seq*s_l_seq + t*s_l_t + h
+  int64_t s_l_seq, s_l_t;
+  int nsplit;      // CTAs per (row, head); 0 = choose
+  int skip_local;  // 1: attend remote selections only
+};
+
+template <int KVT>
+__device__ __forceinline__ void unpack8(const uint4& r, float* f) {
+  if (KVT == SRSWA_BF16) {
+    f[0] = bf16_lo(r.x); f[1] = bf16_hi(r.x); f[2] = bf16_lo(r.y); f[3] = bf16_hi(r.y);
+    f[4] = bf16_lo(r.z); f[5] = bf16_hi(r.z); f[6] = bf16_lo(r.w); f[7] = bf16_hi(r.w);
+  } else {
+    const __half2* hh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = __half22float2(hh[e]);
+      f[2 * e] = t.x;
+      f[2 * e + 1] = t.y;
+    }
+  }
+}
+
+int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st);
+
+}  // namespace srswa

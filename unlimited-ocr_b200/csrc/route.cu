@@ -1,0 +1,644 @@
+// SR-SWA router kernels: block summaries (a1), fused remote scores + top-M
+// 1.5-entmax + top-K + centred log-prior bias (a2 + a4), token block-max
+// scores (a3) and selection packing (a5).
+//
+// All arithmetic that decides the selection is IEEE fp32 (this file must not
+// be built with fast-math: divisions and square roots of the entmax threshold
+// have to round like the reference's CPU path).
+
+#include "common.cuh"
+
+namespace srswa {
+
+// ============================================================================
+// a1: head_cls block summaries
+// (hf-model-code/modeling_deepseekv2.py:391-408; dash_attention.py:1079-1119;
+//  whl:.../unlimited_dash_ops/dash_stage0.py:25-41, route_triton.py:36-72)
+// One warp per block; lane l owns features [4l, 4l+4) (d <= 128).
+// ============================================================================
+constexpr int kMaxBlockSize = 256;
+
+struct KbarArgs {
+  const void* keys;
+  int dtype;
+  int64_t d, bs;
+  const float* hc;
+  float* out;
+  uint8_t* chunk_valid;
+  // contiguous
+  int64_t sb, st, S, nblk, B;
+  // paged
+  const int32_t* block_table;
+  const int32_t* seq_lens;
+  int64_t s_page, s_bt, W, R, tail, s_kbar;
+  int paged;
+};
+
+__device__ __forceinline__ void load4(const void* p, int64_t i, int dtype, float* o) {
+  if (dtype == SRSWA_F32) {
+    float4 f = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i));
+    o[0] = f.x; o[1] = f.y; o[2] = f.z; o[3] = f.w;
+  } else if (dtype == SRSWA_BF16) {
+    uint2 u = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned short*>(p) + i));
+    o[0] = bf16_lo(u.x); o[1] = bf16_hi(u.x); o[2] = bf16_lo(u.y); o[3] = bf16_hi(u.y);
+  } else {
+    uint2 u = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p) + i));
+    float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+  }
+}
+
+__global__ void __launch_bounds__(256) kbar_kernel(const KbarArgs a) {
+  __shared__ float aw_s[8][kMaxBlockSize];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  int64_t base, ntok, out_row;
+  if (!a.paged) {
+    if (item >= a.B * a.nblk) return;
+    const int64_t b = item / a.nblk, c = item % a.nblk;
+    base = b * a.sb + c * a.bs * a.st;
+    ntok = min(a.bs, a.S - c * a.bs);
+    out_row = item * a.d;
+    if (a.chunk_valid && lane == 0) a.chunk_valid[item] = ntok > 0;
+  } else {
+    const int64_t per = a.tail > 0 ? a.tail : a.W;
+    if (item >= a.R * per) return;
+    const int64_t r = item / per, j = item % per;
+    const int64_t sl = a.seq_lens[r];
+    const int64_t nb = (sl + a.bs - 1) / a.bs;
+    const int64_t blk = a.tail > 0 ? nb - 1 - j : j;
+    if (blk < 0 || blk >= nb || blk >= a.W) return;
+    ntok = min(a.bs, sl - blk * a.bs);
+    if (ntok <= 0) return;  // not a page in use: never clobber another request
+    const int64_t page = a.block_table[r * a.s_bt + blk];
+    base = page * a.s_page;
+    out_row = page * a.s_kbar;
+  }
+  const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
+  const bool act = 4 * lane < a.d;
+  float hc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (act) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) hc[e] = a.hc[4 * lane + e];
+  }
+  // pass 1: aw_i = clamp(k_i . hc / sqrt(d)) for valid tokens
+  for (int64_t i0 = 0; i0 < ntok; i0 += 8) {
+    float part[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float kv[4] = {0.f, 0.f, 0.f, 0.f};
+      if (act && i0 + j < ntok) load4(a.keys, base + (i0 + j) * a.st + 4 * lane, a.dtype, kv);
+      part[j] = kv[0] * hc[0] + kv[1] * hc[1] + kv[2] * hc[2] + kv[3] * hc[3];
+    }
+    const float s = transpose_reduce8<32>(part, lane);
+    const int my = 4 * ((lane & 16) != 0) + 2 * ((lane & 8) != 0) + ((lane & 4) != 0);
+    if ((lane & 3) == 0 && i0 + my < ntok)
+      aw_s[warp][i0 + my] = fminf(fmaxf(s * inv_sqrt_d, -kActClamp), kActClamp);
+  }
+  __syncwarp();
+  // masked softmax over valid tokens (row max over valid tokens only)
+  float mx = -INFINITY;
+  for (int64_t i = lane; i < ntok; i += 32) mx = fmaxf(mx, aw_s[warp][i]);
+  mx = warp_max(mx);
+  if (ntok <= 0) mx = 0.f;
+  float den = 0.f;
+  for (int64_t i = lane; i < ntok; i += 32) {
+    const float e = expf(aw_s[warp][i] - mx);
+    aw_s[warp][i] = e;
+    den += e;
+  }
+  den = warp_sum(den);
+  __syncwarp();
+  const float dn = fmaxf(den, 1e-6f);
+  // pass 2: k_bar = sum_i w_i k_i
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (act) {
+    for (int64_t i = 0; i < ntok; ++i) {
+      const float w = aw_s[warp][i] / dn;
+      float kv[4];
+      load4(a.keys, base + i * a.st + 4 * lane, a.dtype, kv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = fmaf(w, kv[e], acc[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float v = acc[e];
+      a.out[out_row + 4 * lane + e] = isfinite(v) ? v : 0.f;
+    }
+  }
+}
+
+// ============================================================================
+// a2 + a4: fused scores + selection
+// ============================================================================
+constexpr int kRouteThreads = 256;
+constexpr int kMaxTopM = 32;
+
+struct RouteArgs {
+  // score source: 0 = dots against k_bar, 1 = given scores
+  int from_scores;
+  const void* q;
+  int q_dtype;
+  int64_t s_q, d;
+  const float* kbar;
+  int64_t s_kbar_b, s_kbar_c;
+  const int32_t* block_table;
+  int64_t s_bt;
+  const int32_t* seq_lens;
+  int64_t rows_per_seq;
+  const int64_t* q_pos;
+  const float* scores_in;
+  int64_t s_sc;
+  const uint8_t* cand;
+  int64_t s_cand;
+  int64_t N, nblk;
+  int64_t BS, L, K, M;
+  float idx_scale, floor_, inv_sigma;
+  int64_t* topi64;
+  int32_t* topi32;
+  float* bias;
+  uint8_t* valid;
+  float* scores_out;
+  int rows_per_cta;
+};
+
+struct Best {
+  float v;
+  int i;
+};
+__device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
+  return v1 > v2 || (v1 == v2 && i1 < i2);
+}
+
+// dot products of one query row against k_bar rows [c_lo, c_hi), written to xs[c]
+// as clamped fp32 scores.  ws warps of the row cooperate (wr = rank among them).
+template <int LPB>
+__device__ void route_dots(const RouteArgs& a, int64_t n, int64_t seq, int64_t c_hi, float* zs,
+                           int wr, int ws, int lane) {
+  constexpr int RPI = 32 / LPB;  // k_bar rows per warp instruction
+  constexpr int BPG = RPI * 8;   // blocks per group (8 loads per lane)
+  const int g = lane / LPB, u = lane % LPB;
+  float qv[4];
+  load4(a.q, n * a.s_q + 4 * u, a.q_dtype, qv);
+  const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
+  const int64_t ngroups = (c_hi + BPG - 1) / BPG;
+  for (int64_t gi = wr; gi < ngroups; gi += ws) {
+    const int64_t c0 = gi * BPG;
+    float part[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t c = c0 + i * RPI + g;
+      float kv[4] = {0.f, 0.f, 0.f, 0.f};
+      if (c < c_hi) {
+        int64_t off;
+        if (a.block_table) off = static_cast<int64_t>(a.block_table[seq * a.s_bt + c]) * a.s_kbar_c;
+        else off = seq * a.s_kbar_b + c * a.s_kbar_c;
+        const float4 f = __ldg(reinterpret_cast<const float4*>(a.kbar + off + 4 * u));
+        kv[0] = f.x; kv[1] = f.y; kv[2] = f.z; kv[3] = f.w;
+      }
+      part[i] = qv[0] * kv[0] + qv[1] * kv[1] + qv[2] * kv[2] + qv[3] * kv[3];
+    }
+    const float s = transpose_reduce8<LPB>(part, u);
+    const int my = 4 * ((u & (LPB / 2)) != 0) + 2 * ((u & (LPB / 4)) != 0) + ((u & (LPB / 8)) != 0);
+    const int64_t c = c0 + my * RPI + g;
+    if ((u & (LPB / 8 - 1)) == 0 && c < c_hi) {
+      float z = s * inv_sqrt_d;
+      z = fminf(fmaxf(z, -kActClamp), kActClamp);  // NaN propagates (fmin/fmax drop it) -> handled below
+      if (s != s) z = s;
+      zs[c] = z;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int rpc = a.rows_per_cta;
+  const int64_t nblk = a.nblk;
+  float* xs_all = reinterpret_cast<float*>(smem_raw);
+  uint8_t* fl_all = reinterpret_cast<uint8_t*>(xs_all + rpc * nblk);
+  __shared__ int any_cand[8];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int wpr = 8 / rpc;  // warps per row
+  const int rr = warp / wpr, wr = warp % wpr;
+  const int64_t n = static_cast<int64_t>(blockIdx.x) * rpc + rr;
+  const bool row_ok = n < a.N;
+  float* xs = xs_all + rr * nblk;
+  uint8_t* fl = fl_all + rr * nblk;
+
+  int64_t seq = 0, p = 0, c_hi = 0;
+  if (row_ok) {
+    seq = n / a.rows_per_seq;
+    if (!a.from_scores) {
+      p = a.q_pos ? a.q_pos[n] : static_cast<int64_t>(a.seq_lens[seq]) - a.rows_per_seq + n % a.rows_per_seq;
+      // remote blocks: c <= p/BS - L, holding a token (c*BS < seq_len)
+      c_hi = p >= 0 ? p / a.BS - a.L + 1 : 0;
+      if (c_hi < 0) c_hi = 0;
+      if (c_hi > nblk) c_hi = nblk;
+      if (a.seq_lens) {
+        const int64_t nb = (static_cast<int64_t>(a.seq_lens[seq]) + a.BS - 1) / a.BS;
+        if (c_hi > nb) c_hi = nb;
+      }
+    }
+  }
+  if (warp < 8 && wr == 0 && lane == 0) any_cand[rr] = 0;
+
+  // ---- phase 1: scores (z), SCORE_NEG outside [0, c_hi) ----
+  if (row_ok) {
+    if (a.from_scores) {
+      for (int64_t c = wr * 32 + lane; c < nblk; c += wpr * 32) xs[c] = a.scores_in[n * a.s_sc + c];
+    } else {
+      for (int64_t c = c_hi + wr * 32 + lane; c < nblk; c += wpr * 32) xs[c] = kScoreNeg;
+      if (a.d == 128) route_dots<32>(a, n, seq, c_hi, xs, wr, wpr, lane);
+      else route_dots<16>(a, n, seq, c_hi, xs, wr, wpr, lane);
+    }
+  }
+  __syncthreads();
+  // ---- phase 2: candidacy flags, x = cand ? z*idx_scale : -1e4 ----
+  if (row_ok) {
+    int found = 0;
+    for (int64_t c = wr * 32 + lane; c < nblk; c += wpr * 32) {
+      const float z = xs[c];
+      if (a.scores_out) a.scores_out[n * nblk + c] = z;
+      const bool remote = z > kScoreNeg * 0.5f;  // NaN -> not remote
+      const bool cm = remote && (a.cand == nullptr || a.cand[n * a.s_cand + c] != 0);
+      fl[c] = static_cast<uint8_t>((remote ? 2 : 0) | (cm ? 1 : 0));
+      found |= cm;
+    }
+    found = __any_sync(0xffffffffu, found);
+    if (lane == 0 && found) atomicOr(&any_cand[rr], 1);
+  }
+  __syncthreads();
+  if (row_ok) {
+    const bool fallback = any_cand[rr] == 0;
+    for (int64_t c = wr * 32 + lane; c < nblk; c += wpr * 32) {
+      uint8_t f = fl[c];
+      if (fallback) f = (f & 2) ? 3 : 0;  // rows with an empty domain use all remote blocks
+      fl[c] = f;
+      float x = (f & 1) ? xs[c] * a.idx_scale : kEntmaxNeg;
+      if (!isfinite(x)) x = kEntmaxNeg;
+      xs[c] = x;
+    }
+  }
+  __syncthreads();
+  if (!row_ok || wr != 0) return;
+
+  // ---- phase 3: top-M by repeated warp arg-max (ties: lower index first) ----
+  const int M = static_cast<int>(a.M);
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int64_t c = lane; c < nblk; c += 32)
+    if (better(xs[c], static_cast<int>(c), bv, bi)) { bv = xs[c]; bi = static_cast<int>(c); }
+  float sel_v = 0.f;
+  int sel_i = -1;
+  for (int j = 0; j < M; ++j) {
+    float wv = bv;
+    int wi = bi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
+      if (better(ov, oi, wv, wi)) { wv = ov; wi = oi; }
+    }
+    if (lane == j) { sel_v = wv; sel_i = wi; }
+    if (wi != 0x7fffffff && (wi & 31) == lane) {
+      xs[wi] = -INFINITY;  // removed
+      bv = -INFINITY;
+      bi = 0x7fffffff;
+      for (int64_t c = lane; c < nblk; c += 32)
+        if (better(xs[c], static_cast<int>(c), bv, bi)) { bv = xs[c]; bi = static_cast<int>(c); }
+    }
+    __syncwarp();
+  }
+
+  // ---- phase 4: exact 1.5-entmax over the M sorted values
+  // (hf-model-code/dash_attention.py:772-800): X = (x - max)/2; prefix sums in
+  // float64 rounded to fp32 per prefix (torch CPU cumsum of fp32); tau_rho =
+  // mean - sqrt(max(0, (1 - rho(meansq - mean^2))/rho)); support = #(tau <= X)
+  const float xmax = __shfl_sync(0xffffffffu, sel_v, 0);
+  const float X = (sel_v - xmax) / 2.0f;
+  double acc1 = 0.0, acc2 = 0.0;
+  float my_cs = 0.f, my_cs2 = 0.f;
+  for (int j = 0; j < M; ++j) {
+    const float xj = __shfl_sync(0xffffffffu, X, j);
+    acc1 += static_cast<double>(xj);
+    acc2 += static_cast<double>(xj * xj);
+    if (lane == j) { my_cs = static_cast<float>(acc1); my_cs2 = static_cast<float>(acc2); }
+  }
+  const float rho = static_cast<float>(lane + 1);
+  const float mean = my_cs / rho;
+  const float mean_sq = my_cs2 / rho;
+  const float ss = rho * (mean_sq - mean * mean);
+  const float delta = (1.0f - ss) / rho;
+  const float tau = mean - sqrtf(fmaxf(delta, 0.0f));
+  const unsigned sup_mask = __ballot_sync(0xffffffffu, lane < M && tau <= X);
+  int support = __popc(sup_mask);
+  if (support < 1) support = 1;
+  const float tau_star = __shfl_sync(0xffffffffu, tau, support - 1);
+  const float pm = fmaxf(X - tau_star, 0.0f);
+  const float prior = pm * pm;
+
+  // ---- phase 5: first K slots, centred log-prior bias ----
+  const int K = static_cast<int>(a.K);
+  const bool is_cand = lane < M && sel_i >= 0 && (fl[sel_i] & 1);
+  const bool vld = lane < K && is_cand;
+  const float logp = logf(fmaxf(prior, a.floor_));
+  float sum = 0.f;
+  int cnt = 0;
+  for (int j = 0; j < K; ++j) {
+    const float lj = __shfl_sync(0xffffffffu, logp, j);
+    const int vj = __shfl_sync(0xffffffffu, static_cast<int>(vld), j);
+    if (vj) { sum += lj; ++cnt; }
+  }
+  const float mu = sum / static_cast<float>(cnt > 0 ? cnt : 1);
+  const float bias = vld ? (logp - mu) * a.inv_sigma : 0.f;
+  if (lane < K) {
+    const int64_t o = n * K + lane;
+    if (a.topi64) a.topi64[o] = sel_i;
+    if (a.topi32) a.topi32[o] = vld ? sel_i : -1;
+    if (a.bias) a.bias[o] = bias;
+    if (a.valid) a.valid[o] = vld ? 1 : 0;
+  }
+}
+
+// ============================================================================
+// a3: token block-max scores, 64 queries x 1 key block per CTA, fp32 FMA
+// ============================================================================
+constexpr int kBmQ = 64;
+
+struct BlockMaxArgs {
+  const void* q;
+  int q_dtype;
+  int64_t sqb, sqc;
+  const void* k;
+  int k_dtype;
+  int64_t skb, sks;
+  const int64_t* pos;
+  const int64_t* seg;
+  int64_t B, C, Sk, D, BS, nblk, LW;
+  int mode;
+  float* out;
+};
+
+__global__ void __launch_bounds__(256) block_max_kernel(const BlockMaxArgs a) {
+  extern __shared__ __align__(16) float bm_smem[];
+  const int64_t D = a.D;
+  const int64_t DP = D + 1;  // padded rows: conflict-free column reads
+  float* qs = bm_smem;                  // [64][DP]
+  float* ks = bm_smem + kBmQ * DP;      // [BS][DP]
+  __shared__ int64_t lo_s[kBmQ], hi_s[kBmQ];
+  const int64_t b = blockIdx.z, blk = blockIdx.y, q0 = static_cast<int64_t>(blockIdx.x) * kBmQ;
+  const int tid = threadIdx.x;
+  const int64_t j0 = blk * a.BS;
+  const float fill = a.mode == 0 ? -INFINITY : kScoreNeg;
+  // per-query valid key range [lo, hi) inside this block
+  if (tid < kBmQ) {
+    const int64_t c = q0 + tid;
+    int64_t lo = j0, hi = j0;
+    if (c < a.C) {
+      const int64_t pc = a.pos[b * a.C + c];
+      int64_t ls = pc - a.LW + 1;
+      if (a.mode == 0 && ls < 0) ls = 0;
+      const int64_t sg = a.seg ? a.seg[b * a.C + c] : 0;
+      lo = max(j0, sg);
+      hi = min(min(j0 + a.BS, a.Sk), ls);
+    }
+    lo_s[tid] = lo;
+    hi_s[tid] = hi;
+  }
+  __syncthreads();
+  int any = 0;
+  for (int i = 0; i < kBmQ; ++i) any |= lo_s[i] < hi_s[i];
+  if (!any) {
+    if (tid < kBmQ && q0 + tid < a.C) a.out[(b * a.C + q0 + tid) * a.nblk + blk] = fill;
+    return;
+  }
+  for (int64_t e = tid; e < kBmQ * D; e += 256) {
+    const int64_t r = e / D, dd = e % D;
+    const int64_t c = q0 + r;
+    qs[r * DP + dd] = c < a.C ? load_elem(a.q, b * a.sqb + c * a.sqc + dd, a.q_dtype) : 0.f;
+  }
+  for (int64_t e = tid; e < a.BS * D; e += 256) {
+    const int64_t r = e / D, dd = e % D;
+    const int64_t j = j0 + r;
+    ks[r * DP + dd] = j < a.Sk ? load_elem(a.k, b * a.skb + j * a.sks + dd, a.k_dtype) : 0.f;
+  }
+  __syncthreads();
+  // thread -> (query ty*4..+4, keys tx + 16*m)
+  const int tx = tid & 15, ty = tid >> 4;
+  float best[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  for (int64_t kk0 = 0; kk0 < a.BS; kk0 += 64) {
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int64_t dd = 0; dd < D; ++dd) {
+      float qa[4], kb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qa[i] = qs[(ty * 4 + i) * DP + dd];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t kr = kk0 + tx + 16 * j;
+        kb[j] = kr < a.BS ? ks[kr * DP + dd] : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(qa[i], kb[j], acc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = ty * 4 + i;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t jj = j0 + kk0 + tx + 16 * j;
+        if (kk0 + tx + 16 * j < a.BS && jj >= lo_s[r] && jj < hi_s[r]) best[i] = fmaxf(best[i], acc[i][j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) best[i] = fmaxf(best[i], __shfl_xor_sync(0xffffffffu, best[i], o));
+  }
+  if (tx == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = ty * 4 + i;
+      const int64_t c = q0 + r;
+      if (c >= a.C) continue;
+      float v;
+      if (lo_s[r] >= hi_s[r]) v = fill;
+      else v = a.mode == 1 ? fminf(fmaxf(best[i], -kActClamp), kActClamp) : best[i];
+      a.out[(b * a.C + c) * a.nblk + blk] = v;
+    }
+  }
+}
+
+// ============================================================================
+// a5: selection packing (dedup; invalid ids -> -1)
+// ============================================================================
+__global__ void pack_selection_kernel(const void* sel, int is64, int64_t rows, int64_t S, int64_t nblk,
+                                      int32_t* out) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  for (int64_t s = 0; s < S; ++s) {
+    const int64_t v = load_index(sel, r * S + s, is64);
+    bool keep = v >= 0 && v < nblk;
+    for (int64_t t = 0; t < s && keep; ++t) keep = load_index(sel, r * S + t, is64) != v;
+    out[r * S + s] = keep ? static_cast<int32_t>(v) : -1;
+  }
+}
+
+static int route_launch(RouteArgs a, cudaStream_t st) {
+  if (a.N == 0) return 0;
+  int rpc = 1;
+  while (rpc < 8 && a.nblk * rpc * 2 <= 2048) rpc *= 2;
+  a.rows_per_cta = rpc;
+  const size_t smem = static_cast<size_t>(rpc) * a.nblk * (sizeof(float) + 1);
+  if (smem > 227 * 1024) return SRSWA_ETOOLARGE;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  const int64_t grid = (a.N + rpc - 1) / rpc;
+  if (grid >= (1ll << 31)) return SRSWA_ETOOLARGE;
+  route_kernel<<<static_cast<unsigned>(grid), kRouteThreads, smem, st>>>(a);
+  return srswa_last_launch_status();
+}
+
+static int fill_route_params(RouteArgs& a, const srswa_route_params& p, int64_t nblk) {
+  if (p.block_size <= 0 || p.local_blocks < 0 || p.sigma == 0.f) return SRSWA_EINVAL;
+  int64_t M = p.topm > 0 ? (p.topm < nblk ? p.topm : nblk) : nblk;
+  if (M < 1) M = 1;
+  if (M > kMaxTopM) return SRSWA_EUNSUPPORTED;
+  int64_t K = p.topk < M ? p.topk : M;
+  if (K < 1) K = 1;
+  a.BS = p.block_size;
+  a.L = p.local_blocks;
+  a.M = M;
+  a.K = K;
+  a.idx_scale = p.idx_scale;
+  a.floor_ = p.prior_floor;
+  a.inv_sigma = static_cast<float>(1.0 / static_cast<double>(p.sigma));
+  return 0;
+}
+
+}  // namespace srswa
+
+using namespace srswa;
+
+extern "C" int srswa_kbar_contig(const void* idx_k, int dtype, int64_t sb, int64_t st, int64_t B,
+                                 int64_t S, int64_t d, int64_t block_size, const float* head_cls,
+                                 float* kbar, uint8_t* chunk_valid, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(idx_k && head_cls && kbar && B >= 0 && S >= 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(d > 0 && d <= 128 && d % 4 == 0, SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG(block_size > 0 && block_size <= kMaxBlockSize, SRSWA_EUNSUPPORTED);
+  const int64_t align = dtype == SRSWA_F32 ? 4 : 4;
+  SRSWA_CHECK_ARG((sb % align) == 0 && (st % align) == 0, SRSWA_EALIGN);
+  const int64_t nblk = (S + block_size - 1) / block_size;
+  if (B * nblk == 0) return 0;
+  KbarArgs a = {};
+  a.keys = idx_k; a.dtype = dtype; a.d = d; a.bs = block_size; a.hc = head_cls; a.out = kbar;
+  a.chunk_valid = chunk_valid; a.sb = sb; a.st = st; a.S = S; a.nblk = nblk; a.B = B; a.paged = 0;
+  const int64_t items = B * nblk;
+  kbar_kernel<<<static_cast<unsigned>((items + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_kbar_paged(const void* idx_cache, int dtype, int64_t s_page, int64_t s_tok,
+                                int64_t d, int64_t block_size, const int32_t* block_table, int64_t s_bt,
+                                int64_t W, const int32_t* seq_lens, int64_t R, int64_t tail_pages,
+                                const float* head_cls, float* kbar_cache, int64_t s_kbar,
+                                srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(idx_cache && block_table && seq_lens && head_cls && kbar_cache, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(R >= 0 && W > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(d > 0 && d <= 128 && d % 4 == 0, SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG(block_size > 0 && block_size <= kMaxBlockSize, SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG((s_page % 4) == 0 && (s_tok % 4) == 0 && (s_kbar % 4) == 0, SRSWA_EALIGN);
+  const int64_t per = tail_pages > 0 ? tail_pages : W;
+  if (R * per == 0) return 0;
+  KbarArgs a = {};
+  a.keys = idx_cache; a.dtype = dtype; a.d = d; a.bs = block_size; a.hc = head_cls; a.out = kbar_cache;
+  a.st = s_tok; a.block_table = block_table; a.seq_lens = seq_lens; a.s_page = s_page; a.s_bt = s_bt;
+  a.W = W; a.R = R; a.tail = tail_pages; a.s_kbar = s_kbar; a.paged = 1;
+  const int64_t items = R * per;
+  kbar_kernel<<<static_cast<unsigned>((items + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
+                           const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk,
+                           const int32_t* block_table, int64_t s_bt, const int32_t* seq_lens,
+                           int64_t rows_per_seq, const int64_t* q_pos, const uint8_t* cand,
+                           int64_t s_cand, srswa_route_params params, int64_t* topi64,
+                           int32_t* topi32, float* bias, uint8_t* valid, float* scores,
+                           srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(idx_q && kbar && N >= 0 && nblk > 0 && rows_per_seq > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(q_pos || seq_lens, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(d == 128 || d == 64, SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG((reinterpret_cast<uintptr_t>(kbar) & 15) == 0 && (s_kbar_b % 4) == 0 &&
+                      (s_kbar_c % 4) == 0 && (s_q % 4) == 0,
+                  SRSWA_EALIGN);
+  RouteArgs a = {};
+  int rc = fill_route_params(a, params, nblk);
+  if (rc) return rc;
+  a.from_scores = 0; a.q = idx_q; a.q_dtype = q_dtype; a.s_q = s_q; a.d = d; a.kbar = kbar;
+  a.s_kbar_b = s_kbar_b; a.s_kbar_c = s_kbar_c; a.block_table = block_table; a.s_bt = s_bt;
+  a.seq_lens = seq_lens; a.rows_per_seq = rows_per_seq; a.q_pos = q_pos; a.cand = cand;
+  a.s_cand = s_cand; a.N = N; a.nblk = nblk; a.topi64 = topi64; a.topi32 = topi32; a.bias = bias;
+  a.valid = valid; a.scores_out = scores;
+  return route_launch(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int srswa_route_select(const float* scores, int64_t s_sc, int64_t N, int64_t nblk,
+                                  const uint8_t* cand, int64_t s_cand, srswa_route_params params,
+                                  int64_t* topi64, int32_t* topi32, float* bias, uint8_t* valid,
+                                  srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(scores && N >= 0 && nblk > 0, SRSWA_EINVAL);
+  RouteArgs a = {};
+  int rc = fill_route_params(a, params, nblk);
+  if (rc) return rc;
+  a.from_scores = 1; a.scores_in = scores; a.s_sc = s_sc; a.cand = cand; a.s_cand = s_cand;
+  a.N = N; a.nblk = nblk; a.rows_per_seq = 1; a.topi64 = topi64; a.topi32 = topi32; a.bias = bias;
+  a.valid = valid;
+  return route_launch(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int srswa_block_max_score(const void* q, int q_dtype, int64_t sqb, int64_t sqc, const void* k,
+                                     int k_dtype, int64_t skb, int64_t sks, const int64_t* pos,
+                                     const int64_t* seg, int64_t B, int64_t C, int64_t Sk, int64_t D,
+                                     int64_t block_size, int64_t nblk, int64_t local_window, int mode,
+                                     float* out, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(q && k && pos && out && B >= 0 && C >= 0 && Sk >= 0 && nblk >= 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(mode == 0 || mode == 1, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(D > 0 && D <= 256, SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG(block_size > 0 && block_size <= 128, SRSWA_EUNSUPPORTED);
+  if (B * C * nblk == 0) return 0;
+  SRSWA_CHECK_ARG(nblk < 65536 && B < 65536, SRSWA_ETOOLARGE);
+  BlockMaxArgs a = {};
+  a.q = q; a.q_dtype = q_dtype; a.sqb = sqb; a.sqc = sqc; a.k = k; a.k_dtype = k_dtype; a.skb = skb;
+  a.sks = sks; a.pos = pos; a.seg = seg; a.B = B; a.C = C; a.Sk = Sk; a.D = D; a.BS = block_size;
+  a.nblk = nblk; a.LW = local_window > 0 ? local_window : block_size; a.mode = mode; a.out = out;
+  const size_t smem = static_cast<size_t>(kBmQ + block_size) * (D + 1) * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(block_max_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  dim3 grid(static_cast<unsigned>((C + kBmQ - 1) / kBmQ), static_cast<unsigned>(nblk), static_cast<unsigned>(B));
+  block_max_kernel<<<grid, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_pack_selection(const void* sel, int is64, int64_t rows, int64_t S, int64_t nblk,
+                                    int32_t* out, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(sel && out && rows >= 0 && S >= 0, SRSWA_EINVAL);
+  if (rows * S == 0) return 0;
+  pack_selection_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0,
+                          reinterpret_cast<cudaStream_t>(stream)>>>(sel, is64, rows, S, nblk, out);
+  return srswa_last_launch_status();
+}

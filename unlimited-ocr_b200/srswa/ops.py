@@ -1,0 +1,307 @@
+"""Thin torch-facing wrappers over the C ABI (one function per entry point).
+
+Every function takes CUDA tensors, allocates its outputs (and any workspace)
+through torch's caching allocator, launches on the current stream and returns.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+
+from . import _lib as L
+
+
+def _cand_args(cand, N, nblk):
+    if cand is None:
+        return None, 0
+    c = cand
+    if c.dtype != torch.uint8:
+        c = c.to(torch.uint8)
+    if c.dim() == 1:
+        return c.contiguous(), 0
+    c = c.reshape(-1, nblk)
+    if c.shape[0] == 1:
+        return c.contiguous(), 0
+    c = c.contiguous()
+    assert c.shape[0] == N
+    return c, nblk
+
+
+def _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma):
+    return L.RouteParams(int(block_size), int(local_blocks), int(topk), int(topm),
+                         float(idx_scale), float(floor), float(sigma))
+
+
+def effective_km(topk, topm, nblk):
+    M = max(1, min(int(topm), nblk)) if int(topm) > 0 else nblk
+    K = max(1, min(int(topk), M))
+    return K, M
+
+
+def kbar_contig(idx_k: torch.Tensor, head_cls: torch.Tensor, block_size: int):
+    """[B,S,d] index keys -> (kbar [B,nblk,d] fp32, chunk_valid [B,nblk] bool)."""
+    B, S, d = idx_k.shape
+    if idx_k.stride(-1) != 1:
+        idx_k = idx_k.contiguous()
+    nblk = (S + block_size - 1) // block_size
+    out = torch.empty(B, nblk, d, device=idx_k.device, dtype=torch.float32)
+    cv = torch.empty(B, nblk, device=idx_k.device, dtype=torch.uint8)
+    hc = head_cls.to(device=idx_k.device, dtype=torch.float32).contiguous()
+    rc = L.lib().srswa_kbar_contig(idx_k.data_ptr(), L.dtype_code(idx_k), idx_k.stride(0), idx_k.stride(1),
+                                   B, S, d, block_size, hc.data_ptr(), out.data_ptr(), cv.data_ptr(),
+                                   L.stream_of(idx_k))
+    L.check(rc, "srswa_kbar_contig")
+    return out, cv.bool()
+
+
+def kbar_paged(idx_cache, head_cls, block_table, seq_lens, kbar_cache, tail_pages=0):
+    """Refresh k_bar of the last `tail_pages` pages per request (all when <= 0)."""
+    P, BS, d = idx_cache.shape
+    assert idx_cache.stride(-1) == 1 and kbar_cache.stride(-1) == 1
+    bt = block_table.to(torch.int32).contiguous()
+    sl = seq_lens.to(torch.int32).contiguous()
+    hc = head_cls.to(device=idx_cache.device, dtype=torch.float32).contiguous()
+    rc = L.lib().srswa_kbar_paged(idx_cache.data_ptr(), L.dtype_code(idx_cache), idx_cache.stride(0),
+                                  idx_cache.stride(1), d, BS, bt.data_ptr(), bt.stride(0), bt.shape[1],
+                                  sl.data_ptr(), sl.shape[0], int(tail_pages), hc.data_ptr(),
+                                  kbar_cache.data_ptr(), kbar_cache.stride(0), L.stream_of(idx_cache))
+    L.check(rc, "srswa_kbar_paged")
+
+
+def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor, sigma,
+          q_pos=None, seq_lens=None, rows_per_seq=1, block_table=None, cand=None,
+          want=("topi64", "bias", "valid"), nblk=None):
+    """Fused scores + selection for query rows idx_q [N, d].
+
+    kbar: contiguous [B, nblk, d] (block_table None) or paged cache [P, d].
+    Returns a dict with the requested outputs among topi64, topi32, bias,
+    valid, scores."""
+    N, d = idx_q.shape
+    if idx_q.stride(-1) != 1:
+        idx_q = idx_q.contiguous()
+    dev = idx_q.device
+    if block_table is None:
+        B, nb, _ = kbar.shape
+        s_b, s_c = kbar.stride(0), kbar.stride(1)
+        bt = None
+        nblk = nb if nblk is None else nblk
+    else:
+        s_b, s_c = 0, kbar.stride(0)
+        bt = block_table.to(torch.int32).contiguous()
+        nblk = bt.shape[1] if nblk is None else nblk
+    K, M = effective_km(topk, topm, nblk)
+    out = {}
+    for name, dt, shape in (("topi64", torch.int64, (N, K)), ("topi32", torch.int32, (N, K)),
+                            ("bias", torch.float32, (N, K)), ("valid", torch.uint8, (N, K)),
+                            ("scores", torch.float32, (N, nblk))):
+        out[name] = torch.empty(shape, device=dev, dtype=dt) if name in want else None
+    qp = None if q_pos is None else q_pos.to(device=dev, dtype=torch.int64).contiguous().view(-1)
+    sl = None if seq_lens is None else seq_lens.to(device=dev, dtype=torch.int32).contiguous()
+    cnd, s_cand = _cand_args(cand, N, nblk)
+    p = _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma)
+    rc = L.lib().srswa_route(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
+                             kbar.data_ptr(), s_b, s_c, nblk, L.ptr(bt), 0 if bt is None else bt.stride(0),
+                             L.ptr(sl), int(rows_per_seq), L.ptr(qp), L.ptr(cnd), s_cand, p,
+                             L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
+                             L.ptr(out["valid"]), L.ptr(out["scores"]), L.stream_of(idx_q))
+    L.check(rc, "srswa_route")
+    if out["valid"] is not None:
+        out["valid"] = out["valid"].bool()
+    return {k: v for k, v in out.items() if v is not None}
+
+
+def route_select(scores, cand, *, topk, topm, idx_scale, floor, sigma, want=("topi64", "bias", "valid")):
+    """Selection from given scores [..., nblk] (fp32)."""
+    shape = scores.shape
+    nblk = shape[-1]
+    sc = scores.reshape(-1, nblk)
+    if sc.dtype != torch.float32 or sc.stride(-1) != 1:
+        sc = sc.float().contiguous()
+    N = sc.shape[0]
+    K, M = effective_km(topk, topm, nblk)
+    dev = sc.device
+    out = {}
+    for name, dt in (("topi64", torch.int64), ("topi32", torch.int32), ("bias", torch.float32),
+                     ("valid", torch.uint8)):
+        out[name] = torch.empty((N, K), device=dev, dtype=dt) if name in want else None
+    cnd, s_cand = _cand_args(cand, N, nblk)
+    p = _route_params(1, 0, topk, topm, idx_scale, floor, sigma)
+    rc = L.lib().srswa_route_select(sc.data_ptr(), sc.stride(0), N, nblk, L.ptr(cnd), s_cand, p,
+                                    L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
+                                    L.ptr(out["valid"]), L.stream_of(sc))
+    L.check(rc, "srswa_route_select")
+    res = {}
+    for k, v in out.items():
+        if v is None:
+            continue
+        v = v.view(*shape[:-1], K)
+        res[k] = v.bool() if k == "valid" else v
+    return res
+
+
+def block_max_score(q, k, pos, seg, block_size, num_key_blocks, local_window, mode):
+    B, Cq, D = q.shape
+    Sk = k.shape[1]
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if k.stride(-1) != 1:
+        k = k.contiguous()
+    out = torch.empty(B, Cq, num_key_blocks, device=q.device, dtype=torch.float32)
+    pos = pos.to(torch.int64).contiguous()
+    seg = None if seg is None else seg.to(torch.int64).contiguous()
+    rc = L.lib().srswa_block_max_score(q.data_ptr(), L.dtype_code(q), q.stride(0), q.stride(1),
+                                       k.data_ptr(), L.dtype_code(k), k.stride(0), k.stride(1),
+                                       pos.data_ptr(), L.ptr(seg), B, Cq, Sk, D, block_size,
+                                       num_key_blocks, int(local_window), int(mode), out.data_ptr(),
+                                       L.stream_of(q))
+    L.check(rc, "srswa_block_max_score")
+    return out
+
+
+def pack_selection(sel, nblk):
+    """int32 copy of sel with ids outside [0, nblk) and repeats inside a row -> -1."""
+    s = sel.contiguous()
+    is64 = 1 if s.dtype == torch.int64 else 0
+    if s.dtype not in (torch.int64, torch.int32):
+        s = s.to(torch.int64)
+        is64 = 1
+    out = torch.empty(s.shape, device=s.device, dtype=torch.int32)
+    S = s.shape[-1]
+    rows = s.numel() // max(S, 1)
+    rc = L.lib().srswa_pack_selection(s.data_ptr(), is64, rows, S, int(nblk), out.data_ptr(), L.stream_of(s))
+    L.check(rc, "srswa_pack_selection")
+    return out
+
+
+def _gather_desc(q, k, v, sel, block_size, scale, local_window):
+    B, T, HQ, D = q.shape
+    Hkv = k.shape[2]
+    HI, S = sel.shape[1], sel.shape[-1]
+    lw = block_size if local_window is None else max(1, int(local_window))
+    return L.GatherDesc(B, T, HQ, Hkv, HI, D, S, int(block_size), lw, float(scale), L.dtype_code(q),
+                        q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+                        v.stride(0), v.stride(1), v.stride(2))
+
+
+def gather_fwd(q, k, v, sel, bias, seg, block_size, scale, local_window):
+    """q/k/v [B,T,H,D] (D contiguous), sel [B,HI,T,S] int32 packed, bias [B,T,S]
+    fp32 or None, seg [B,T] int32 or None -> (o [B,T,HQ,D] q.dtype, lse [B,T,HQ])."""
+    B, T, HQ, D = q.shape
+    o = torch.empty(B, T, HQ, D, device=q.device, dtype=q.dtype)
+    lse = torch.empty(B, T, HQ, device=q.device, dtype=torch.float32)
+    g = _gather_desc(q, k, v, sel, block_size, scale, local_window)
+    lib = L.lib()
+    ws_n = lib.srswa_gather_fwd_workspace_size(C.byref(g))
+    ws = torch.empty(max(ws_n, 1), device=q.device, dtype=torch.uint8)
+    rc = lib.srswa_gather_fwd(C.byref(g), q.data_ptr(), k.data_ptr(), v.data_ptr(), sel.data_ptr(),
+                              L.ptr(bias), L.ptr(seg), o.data_ptr(), L.dtype_code(o), o.stride(0),
+                              o.stride(1), o.stride(2), lse.data_ptr(), ws.data_ptr(), ws_n, L.stream_of(q))
+    L.check(rc, "srswa_gather_fwd")
+    return o, lse
+
+
+def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_window):
+    g = _gather_desc(q, k, v, sel, block_size, scale, local_window)
+    lib = L.lib()
+    if do.stride() != o.stride():
+        do = do.contiguous()
+        o = o.contiguous()
+        assert do.stride() == o.stride()
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    assert dq.stride() == q.stride() and dk.stride() == k.stride() and dv.stride() == v.stride()
+    d_bias = None
+    if bias is not None:
+        d_bias = torch.empty(bias.shape, device=q.device, dtype=torch.float32)
+    ws_n = lib.srswa_gather_bwd_workspace_size(C.byref(g))
+    ws = torch.empty(max(ws_n, 1), device=q.device, dtype=torch.uint8)
+    rc = lib.srswa_gather_bwd(C.byref(g), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                              o.stride(0), o.stride(1), o.stride(2), do.data_ptr(), lse.data_ptr(),
+                              sel.data_ptr(), L.ptr(bias), L.ptr(seg), dq.data_ptr(), dk.data_ptr(),
+                              dv.data_ptr(), L.ptr(d_bias), ws.data_ptr(), ws_n, L.stream_of(q))
+    L.check(rc, "srswa_gather_bwd")
+    return dq, dk, dv, d_bias
+
+
+def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_blocks, sm_scale,
+                  out=None, block_table=None, seq_lens=None, q_pos=None, rows_per_req=1,
+                  valid=None, lse=False, nsplit=0, kv_layout=None):
+    """Sparse decode attend.  q [N,H,D]; paged k/v caches [P, BS, Hkv, D] (any
+    strides with D contiguous) indexed by block_table [R,W].  With
+    block_table None, kv_layout = (R, W, s_req, s_pos, s_head, Hkv) describes
+    one contiguous cache per request (block blk of request r at r*s_req +
+    blk*BS*s_pos).  topk_idx [Hkv or 1 (stride 0 ok), N, K] or [N, K]; bias
+    like topk_idx or None."""
+    N, H, D = q.shape
+    assert k_cache.stride() == v_cache.stride()
+    if block_table is not None:
+        P, BS, Hkv, _ = k_cache.shape
+        assert BS == block_size
+        s_page, s_pos, s_head = k_cache.stride(0), k_cache.stride(1), k_cache.stride(2)
+        s_req = 0
+    else:
+        _, _, s_req, s_pos, s_head, Hkv = kv_layout
+        s_page = block_size * s_pos
+    if topk_idx.dim() == 2:
+        topk_idx = topk_idx.unsqueeze(0)
+    ti = topk_idx
+    if ti.stride(-1) != 1:
+        ti = ti.contiguous()
+    s_ti_h = ti.stride(0) if ti.shape[0] > 1 else 0
+    b = None
+    s_b_h = s_b_n = 0
+    if bias is not None:
+        b = bias.unsqueeze(0) if bias.dim() == 2 else bias
+        if b.dtype != torch.float32 or b.stride(-1) != 1:
+            b = b.float().contiguous()
+        s_b_h = b.stride(0) if b.shape[0] > 1 else 0
+        s_b_n = b.stride(1)
+    vd = None
+    if valid is not None:
+        vd = (valid.unsqueeze(0) if valid.dim() == 2 else valid).to(torch.uint8)
+        vd = vd.expand(ti.shape).contiguous() if vd.shape != ti.shape else vd.contiguous()
+        if vd.stride() != ti.stride():
+            ti = ti.contiguous()
+            vd = vd.contiguous()
+            s_ti_h = ti.stride(0) if ti.shape[0] > 1 else 0
+    if out is None:
+        out = torch.empty(N, H, D, device=q.device, dtype=q.dtype)
+    lse_t = torch.empty(N, H, device=q.device, dtype=torch.float32) if lse else None
+    bt = None if block_table is None else block_table.to(torch.int32).contiguous()
+    sl = None if seq_lens is None else seq_lens.to(device=q.device, dtype=torch.int32).contiguous()
+    qp = None if q_pos is None else q_pos.to(device=q.device, dtype=torch.int64).contiguous().view(-1)
+    if bt is not None:
+        R, W = bt.shape
+    else:
+        R, W = kv_layout[0], kv_layout[1]
+    d = L.DecodeDesc(N, H, Hkv, D, ti.shape[-1], block_size, local_blocks, float(sm_scale),
+                     L.dtype_code(q), L.dtype_code(k_cache), L.dtype_code(out), q.stride(0), q.stride(1),
+                     s_page, s_pos, s_head, out.stride(0), out.stride(1),
+                     R, W, s_req, rows_per_req, 1 if ti.dtype == torch.int64 else 0,
+                     s_ti_h, ti.stride(1), s_b_h, s_b_n, int(nsplit))
+    if ti.dtype not in (torch.int32, torch.int64):
+        raise NotImplementedError("topk_idx must be int32 or int64")
+    rc = L.lib().srswa_decode_attend(C.byref(d), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                     L.ptr(bt), L.ptr(sl), L.ptr(qp), ti.data_ptr(), L.ptr(b), L.ptr(vd),
+                                     out.data_ptr(), L.ptr(lse_t), L.stream_of(q))
+    L.check(rc, "srswa_decode_attend")
+    return (out, lse_t) if lse else out
+
+
+def lse_merge(o_parts, lse_parts, out_dtype=torch.float32):
+    Cn, N, H, D = o_parts.shape
+    o_parts = o_parts.float().contiguous()
+    lse_parts = lse_parts.float().contiguous()
+    out = torch.empty(N, H, D, device=o_parts.device, dtype=out_dtype)
+    lse = torch.empty(N, H, device=o_parts.device, dtype=torch.float32)
+    rc = L.lib().srswa_lse_merge(o_parts.data_ptr(), lse_parts.data_ptr(), Cn, N, H, D, out.data_ptr(),
+                                 L.dtype_code(out), lse.data_ptr(), L.stream_of(o_parts))
+    L.check(rc, "srswa_lse_merge")
+    return out, lse
+
+
+INV_SQRT = lambda d: 1.0 / math.sqrt(d)  # noqa: E731
