@@ -189,6 +189,24 @@ SRSWA_API int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const 
                      const int32_t* seg, void* dq, void* dk, void* dv, float* d_bias,
                      void* workspace, size_t workspace_bytes, srswa_stream_t stream);
 
+/* Backward that allocates nothing and takes no workspace.  No counterpart in
+ * the reference (whose Triton path always allocates through torch).  For
+ * callers that cannot allocate device memory at all (a runtime that reserves
+ * all device memory up front, a plugin/FFI host that passes only input and
+ * output buffers): the scratch is a 32 MiB array inside this library
+ * (srswa_gather_bwd_noalloc_max_scratch()), present on every device that loads
+ * it until exit.  Shapes needing more scratch than that return
+ * SRSWA_ETOOLARGE.  The first call on a device looks up the array's device
+ * address (make it outside stream capture).  Calls share the array: calls
+ * whose GPU work overlaps race and must be serialised by the caller.
+ * Results equal srswa_gather_bwd's. */
+SRSWA_API size_t srswa_gather_bwd_noalloc_max_scratch(void);
+SRSWA_API int srswa_gather_bwd_noalloc(const srswa_gather_desc* g, const void* q, const void* k,
+                                       const void* v, const void* o, int64_t sob, int64_t sot, int64_t soh,
+                                       const void* dout, const float* lse, const int32_t* sel,
+                                       const float* bias, const int32_t* seg, void* dq, void* dk, void* dv,
+                                       float* d_bias, srswa_stream_t stream);
+
 /* ------------------------------------------------------------------ a9 --
  * Block-sparse decode attend over a paged (or contiguous) KV cache.
  * q [N,H,D] (row stride s_qn, head stride s_qh).  k/v caches: element of

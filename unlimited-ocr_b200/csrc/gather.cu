@@ -471,3 +471,67 @@ extern "C" int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const
   else bwd_dkdv_kernel<64><<<gk, 256, 0, st>>>(a);
   return srswa_last_launch_status();
 }
+
+// ---------------------------------------------------------------------------
+// Backward without any allocation by anyone: the scratch the backward needs
+// (delta, per-head d_bias partials, selection bitmap) lives in a file-scope
+// device array instead of a caller workspace.  For callers that cannot call
+// cudaMalloc or an allocator at all: code embedded in a runtime that reserves
+// all device memory up front and forbids allocation afterwards, plugin or FFI
+// hosts that hand a kernel only its input/output buffers, and host code with
+// no device allocator of its own.
+//
+// The array is kNoAllocScratchBytes (32 MiB) on every device that loads this
+// library, held until process exit.  Problems whose backward scratch exceeds
+// it are rejected with SRSWA_ETOOLARGE.  In host code the array's name is a
+// host-side stand-in, so its device address is looked up once per device
+// (cudaGetSymbolAddress, with that device current) on the first call made on
+// that device; make that first call outside any stream capture.  All calls
+// share the one array, so calls whose GPU work overlaps (different streams,
+// or graph replays running concurrently) race on it and must be serialised by
+// the caller.  The existing backward path clears the parts that must start at
+// zero (the bitmap) on every call; the rest is fully overwritten.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace srswa {
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(32) << 20;
+static __device__ __align__(256) unsigned char g_bwd_scratch[kNoAllocScratchBytes];
+constexpr int kMaxDevices = 64;
+static void* g_bwd_scratch_dev[kMaxDevices] = {};
+static std::mutex g_bwd_scratch_mu;
+
+static int bwd_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices) return SRSWA_EUNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_bwd_scratch_mu);
+  if (g_bwd_scratch_dev[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_bwd_scratch);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    g_bwd_scratch_dev[dev] = p;
+  }
+  *out = g_bwd_scratch_dev[dev];
+  return 0;
+}
+}  // namespace srswa
+
+extern "C" size_t srswa_gather_bwd_noalloc_max_scratch(void) { return srswa::kNoAllocScratchBytes; }
+
+extern "C" int srswa_gather_bwd_noalloc(const srswa_gather_desc* g, const void* q, const void* k,
+                                        const void* v, const void* o, int64_t sob, int64_t sot, int64_t soh,
+                                        const void* dout, const float* lse, const int32_t* sel,
+                                        const float* bias, const int32_t* seg, void* dq, void* dk, void* dv,
+                                        float* d_bias, srswa_stream_t stream) {
+  int rc = check_gather_desc(g);
+  if (rc) return rc;
+  const size_t need = bwd_layout(g, bias != nullptr).total;
+  if (need > srswa::kNoAllocScratchBytes) return SRSWA_ETOOLARGE;
+  void* scratch = nullptr;
+  rc = srswa::bwd_scratch_address(&scratch);
+  if (rc) return rc;
+  return srswa_gather_bwd(g, q, k, v, o, sob, sot, soh, dout, lse, sel, bias, seg, dq, dk, dv, d_bias,
+                          scratch, srswa::kNoAllocScratchBytes, stream);
+}

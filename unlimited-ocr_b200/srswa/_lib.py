@@ -64,6 +64,9 @@ _SIGS = {
     "srswa_gather_bwd_workspace_size": (C.c_size_t, [C.POINTER(GatherDesc)]),
     "srswa_gather_bwd": (C.c_int, [C.POINTER(GatherDesc), vp, vp, vp, vp, i64, i64, i64, vp, vp, vp, vp,
                                    vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),
+    "srswa_gather_bwd_noalloc_max_scratch": (C.c_size_t, []),
+    "srswa_gather_bwd_noalloc": (C.c_int, [C.POINTER(GatherDesc), vp, vp, vp, vp, i64, i64, i64, vp, vp, vp,
+                                           vp, vp, vp, vp, vp, vp, vp]),
     "srswa_decode_attend": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                       vp]),
     "srswa_lse_merge": (C.c_int, [vp, vp, i64, i64, i64, i64, vp, C.c_int, vp, vp]),
