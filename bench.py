@@ -56,6 +56,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route"],
+                    help="decode = cfg3 (default, the headline); prefill = cfg2; train = cfg4 fwd+bwd; "
+                         "route = the cfg3 router alone (k_bar cache + block table, no KV; for profiling)")
+    ap.add_argument("--batch", type=int, default=0, help="prefill/train batch override (smaller cases)")
+    ap.add_argument("--seq", type=int, default=0, help="prefill/train sequence override")
     return ap.parse_args()
 
 
@@ -301,8 +306,155 @@ def cpu_decode_sample(S, budget_s=20.0, max_req=4):
 
 
 # ---------------------------------------------------------------------------
+def attend_flops(T, LW, sel, BS):
+    """Exact forward flops of the gather-attention: 4*D per (query, head,
+    attended key); attended keys = window + unique remote keys of the
+    selection (sel [B, T, K] int, -1 unused)."""
+    B = sel.shape[0]
+    t = torch.arange(T, device=sel.device)
+    ls = (t - LW + 1).clamp(min=0)
+    n = (t - ls + 1).to(torch.float64).sum() * B
+    s = sel.clone()
+    valid = s >= 0
+    lo = s * BS
+    hi = torch.minimum(torch.minimum((s + 1) * BS, (t + 1)[None, :, None]), ls[None, :, None])
+    cnt = (hi - lo).clamp(min=0) * valid
+    # repeated ids were removed by the router (distinct top-k)
+    n = n + cnt.to(torch.float64).sum()
+    return float(n) * 4 * D * H
+
+
+def main_dense(args):
+    """cfg2 prefill (route + gather fwd) or cfg4 training (route + gather fwd
+    + bwd), 1 GPU per rank, batch sharded across ranks (weak: per-rank work
+    fixed)."""
+    import torch.distributed as dist
+    from srswa import dash_infer, ops  # noqa: F401
+    from srswa.sparse_gather_e2e import triton_gather_attention_e2e
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    train = args.workload == "train"
+    B, T, Kk, LW, seed, sc = (8, 32768, 16, 1024, 3, 1.0) if train else (4, 16384, 8, 512, 1, 0.5)
+    if args.batch:
+        B = args.batch
+    if args.seq:
+        T = args.seq
+    Bl = max(1, B // world)
+    g = torch.Generator(device=dev).manual_seed(seed * 100 + rank)
+    mk = lambda *shape: (torch.randn(*shape, device=dev, generator=g) * sc).to(torch.bfloat16)  # noqa: E731
+    q, k, v = mk(Bl, H, T, D), mk(Bl, HKV, T, D), mk(Bl, HKV, T, D)
+    iq = mk(Bl, T, DI).float()
+    ik = mk(Bl, T, DI)
+    nblk = T // BS
+    router = type("R", (), dict(block_size=BS, local_blocks=LW // BS, local_window=LW,
+                                head_cls=torch.zeros(DI, device=dev), stage0="head_cls"))()
+    pos = torch.arange(T, device=dev)[None].expand(Bl, T).contiguous()
+    p = dict(idx_scale=IDX_SCALE, floor=FLOOR, sigma=SIGMA, K=Kk, topm=M)
+    do = torch.randn(Bl, H, T, D, device=dev, generator=g).to(torch.bfloat16) if train else None
+    state = {}
+
+    def step():
+        topi, bias, valid = dash_infer.route(router, iq, ik, pos, nblk, None, p)
+        sel = torch.where(valid, topi, torch.full_like(topi, -1))[:, None]
+        b = (bias * valid).float()
+        if train:
+            qq, kk, vv, bb = (x.detach().requires_grad_(True) for x in (q, k, v, b))
+            o = triton_gather_attention_e2e(qq, kk, vv, sel, bb, pos, None, BS, SM_SCALE, LW)
+            o.backward(do)
+        else:
+            o = triton_gather_attention_e2e(q, k, v, sel, b, pos, None, BS, SM_SCALE, LW)
+        state["sel"] = sel
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    fl = attend_flops(T, LW, state["sel"][:, 0], BS) * (3.5 if train else 1.0)  # fwd 4, bwd 10 per D
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a_, b_ in ev:
+        flush.zero_()
+        a_.record()
+        step()
+        b_.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = sum(a_.elapsed_time(b_) for a_, b_ in ev) / args.steps
+    vec = torch.tensor([ms], device=dev, dtype=torch.float64)
+    fl_t = torch.tensor([fl], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+        dist.all_reduce(fl_t, op=dist.ReduceOp.SUM)
+    ms, fl_all = vec.item(), fl_t.item()
+    try:
+        pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak = float(pk["bf16_tflops"]) * 1e12
+        src = "measured"
+    except Exception:
+        peak, src = 1.59e15, "fallback"
+    if rank == 0:
+        line = {"metric": METRIC, "value": fl_all / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic seeded N(0,1)",
+                "config": {"workload": ("cfg4 train: route + gather-attention e2e fwd+bwd" if train else
+                                        "cfg2 prefill: route + gather-attention fwd"),
+                           "global_batch": Bl * world, "seq_len": T, "K": Kk, "LW": LW,
+                           "parallelism": f"batch/dp{world}", "l2": "flushed before every timed step"},
+                "roofline": {"bound": "tensor", "achieved": fl_all / world / (ms * 1e-3) / 1e12,
+                             "peak": peak / 1e12, "unit": "TFLOP/s",
+                             "frac": fl_all / world / (ms * 1e-3) / peak, "peak_source": src, "traffic": None},
+                "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main_route(args):
+    """The cfg3 decode router alone (fused scores + selection over the paged
+    k_bar cache of 256 requests), for profiling at full size without the KV."""
+    from srswa import ops
+    dev = torch.device("cuda", 0)
+    S, _ = workload(args)
+    gen = torch.Generator().manual_seed(1000)
+    nb = [math.ceil(s / BS) for s in S]
+    R, W, P = len(S), max(nb), sum(nb)
+    perm = torch.randperm(P, generator=gen)
+    bt = torch.zeros(R, W, dtype=torch.int32)
+    o = 0
+    for r, n in enumerate(nb):
+        bt[r, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    bt, sl = bt.to(dev), torch.tensor(S, dtype=torch.int32, device=dev)
+    kbar = torch.randn(P, DI, generator=gen).to(dev) * 0.1
+    iq = torch.randn(R, DI, generator=gen).to(torch.bfloat16).float().to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    fn = lambda: ops.route(iq, kbar, block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=IDX_SCALE,  # noqa: E731
+                           floor=FLOOR, sigma=SIGMA, seq_lens=sl, block_table=bt, want=("topi32", "bias"))
+    times, g = timed_graph(fn, args.steps, args.warmup, flush, not args.no_graph)
+    ms = sum(times) / len(times)
+    byts = sum(max(0, (s - 1) // BS - L + 1) * (DI * 4 + 4) + DI * 4 + K * 8 for s in S)
+    print(json.dumps({"workload": "cfg3 router alone", "us": ms * 1e3, "bytes": byts,
+                      "GB/s": byts / (ms * 1e-3) / 1e9}), flush=True)
+    del g
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "route":
+        return main_route(args)
+    if args.workload != "decode" and args.impl != "reference":
+        return main_dense(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -110,15 +110,20 @@ typedef struct {
  * Outputs (each optional, [N, K] row-major): topi64 (raw indices, score-desc),
  * topi32 (-1 on invalid slots: the serving layout), bias (0 on invalid),
  * valid (uint8); scores [N, nblk] fp32 (the _block_scores_infer output).
+ * workspace: caller scratch of srswa_route_workspace_size(N, nblk, params,
+ * cand != NULL) bytes (0 for small rows; ~N*nblk/8 bytes for decode rows).
  * Replaces _block_scores_infer + _infer_route_select (modeling_deepseekv2.py:339-430)
  * and route_decode_triton / route_prefill_triton
  * (whl:.../unlimited_dash_ops/route_triton.py:624-680, 729-847). */
+SRSWA_API size_t srswa_route_workspace_size(int64_t N, int64_t nblk, int64_t d, srswa_route_params params,
+                                            int has_cand);
 SRSWA_API int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
                 const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk,
                 const int32_t* block_table, int64_t s_bt, const int32_t* seq_lens,
                 int64_t rows_per_seq, const int64_t* q_pos, const uint8_t* cand,
                 int64_t s_cand, srswa_route_params params, int64_t* topi64, int32_t* topi32,
-                float* bias, uint8_t* valid, float* scores, srswa_stream_t stream);
+                float* bias, uint8_t* valid, float* scores, void* workspace,
+                size_t workspace_bytes, srswa_stream_t stream);
 
 /* Selection only, from given block scores [N, nblk] (row stride s_sc):
  * _infer_route_select (hf-model-code/modeling_deepseekv2.py:339-362) and

@@ -189,3 +189,34 @@ def test_route_decode_long_vs_oracle(cuda, S_list):
         np.testing.assert_allclose(r["bias"].cpu().numpy()[i], bias[0], rtol=1e-5, atol=5e-4)
         t32 = r["topi32"].cpu().numpy()[i]
         assert np.array_equal(t32 >= 0, gv) and (t32[gv] <= qb - L).all()
+
+
+def test_route_decode_cand_mask_vs_oracle(cuda):
+    """Chunked decode router with a page-aware candidate mask; rows 1 and 3
+    have an empty mask and fall back to every remote block."""
+    rng = np.random.default_rng(4)
+    BS, L, K, M, d = 64, 8, 8, 16, 128
+    S_list = [40000, 52000, 33000, 60000, 45000]
+    R = len(S_list)
+    W = max((s + BS - 1) // BS for s in S_list)
+    P = R * W
+    perm = rng.permutation(P).astype(np.int32).reshape(R, W)
+    kbar = rng.standard_normal((P, d)).astype(np.float32) * 0.1
+    idx_q = O.bf16_round(rng.standard_normal((R, d)).astype(np.float32))
+    cand = rng.random((R, W)) < 0.2
+    cand[1] = False
+    cand[3] = False
+    sl = np.asarray(S_list, np.int32)
+    r = ops.route(T(idx_q, cuda), T(kbar, cuda), block_size=BS, local_blocks=L, topk=K, topm=M,
+                  idx_scale=11.3, floor=1e-4, sigma=1.0, seq_lens=T(sl, cuda), block_table=T(perm, cuda),
+                  cand=T(cand, cuda), want=("topi64", "bias", "valid", "scores"))
+    sc = r["scores"].cpu().numpy()
+    for i in range(R):
+        cv = np.arange(W) < (S_list[i] + BS - 1) // BS
+        ref_sc = O.block_scores_headcls(idx_q[i][None, None], kbar[perm[i]][None], cv[None],
+                                        np.array([[S_list[i] - 1]]), BS, L)[0, 0]
+        np.testing.assert_allclose(sc[i], ref_sc, rtol=2e-5, atol=2e-5)
+        topi, bias, valid = O.infer_route_select(ref_sc[None], cand[i][None], 11.3, 1e-4, 1.0, K, M)
+        assert np.array_equal(r["valid"].cpu().numpy()[i], valid[0])
+        assert ties_only(r["topi64"].cpu().numpy()[i][None], topi, valid, ref_sc[None]) == 0
+        np.testing.assert_allclose(r["bias"].cpu().numpy()[i], bias[0], rtol=1e-5, atol=5e-4)

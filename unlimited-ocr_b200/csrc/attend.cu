@@ -87,41 +87,75 @@ __global__ void __launch_bounds__(kAttendThreads) attend_rows_kernel(const Atten
   if (ls < sg) ls = sg;
   if (ls < 0) ls = 0;
 
-  // ---- slot list: remote selections (deduped, useful only), then window ----
-  if (tid == 0) {
+  // ---- slot list: remote selections (deduped, useful only), then window.
+  //      Built by warp 0 with one lane per slot: the index, block-table and
+  //      bias loads of all slots are issued together. ----
+  if (warp == 0) {
     int n = 0;
     if (p >= 0 && p >= sg) {
       const int64_t ibase = seq * a.s_sel_seq + t * a.s_sel_t + hi * a.s_sel_h;
       const int64_t bbase = seq * a.s_b_seq + t * a.s_b_t + hi * a.s_b_h;
-      for (int64_t s = 0; s < a.K && n < kAttendMaxSlots; ++s) {
-        const int64_t blk = load_index(a.sel, ibase + s, a.idx_is64);
-        if (blk < 0 || blk >= a.W) continue;
-        if (a.valid && !a.valid[ibase + s]) continue;
-        // a remote key must satisfy sg <= j < ls and j <= p
-        const int64_t lo = blk * BS > sg ? blk * BS : sg;
-        const int64_t hi_ = (blk + 1) * BS < ls ? (blk + 1) * BS : ls;
-        if (lo >= hi_ || lo > p) continue;
-        bool dup = false;
-        for (int j = 0; j < n; ++j) dup |= (slots[j].key0 == blk * BS);
-        if (dup) continue;
-        slots[n].page_off = block_offset(a, seq, blk);
-        slots[n].key0 = blk * BS;
-        slots[n].bias2 = a.bias ? a.bias[bbase + s] * kLog2e : 0.f;
-        slots[n].remote = 1;
-        ++n;
+      for (int64_t s0 = 0; s0 < a.K; s0 += 32) {
+        const int64_t s = s0 + lane;
+        int64_t blk = -1;
+        bool ok = false;
+        if (s < a.K) {
+          blk = load_index(a.sel, ibase + s, a.idx_is64);
+          ok = blk >= 0 && blk < a.W && (a.valid == nullptr || a.valid[ibase + s] != 0);
+          if (ok) {  // a remote key must satisfy sg <= j < ls and j <= p
+            const int64_t lo = blk * BS > sg ? blk * BS : sg;
+            const int64_t hi_ = (blk + 1) * BS < ls ? (blk + 1) * BS : ls;
+            ok = lo < hi_ && lo <= p;
+          }
+        }
+        // drop repeats of an earlier usable slot (this batch, then earlier batches)
+        for (int j = 0; j < 32; ++j) {
+          const int64_t ob = __shfl_sync(0xffffffffu, blk, j);
+          const bool ook = __shfl_sync(0xffffffffu, ok, j);
+          if (j < lane && ook && ob == blk) ok = false;
+        }
+        for (int j = 0; j < n; ++j)
+          if (ok && slots[j].key0 == blk * BS) ok = false;
+        int64_t off = 0;
+        float b2 = 0.f;
+        if (ok) {
+          off = block_offset(a, seq, blk);
+          b2 = a.bias ? a.bias[bbase + s] * kLog2e : 0.f;
+        }
+        const unsigned msk = __ballot_sync(0xffffffffu, ok);
+        if (ok) {
+          const int pos = n + __popc(msk & ((1u << lane) - 1u));
+          if (pos < kAttendMaxSlots) {
+            slots[pos].page_off = off;
+            slots[pos].key0 = blk * BS;
+            slots[pos].bias2 = b2;
+            slots[pos].remote = 1;
+          }
+        }
+        n += __popc(msk);
+        if (n > kAttendMaxSlots) n = kAttendMaxSlots;
+        __syncwarp();
       }
       if (!a.skip_local) {
-        for (int64_t blk = ls / BS; blk <= p / BS && n < kAttendMaxSlots; ++blk) {
-          if (blk >= a.W) break;
-          slots[n].page_off = block_offset(a, seq, blk);
-          slots[n].key0 = blk * BS;
-          slots[n].bias2 = 0.f;
-          slots[n].remote = 0;
-          ++n;
+        const int64_t b_lo = ls / BS, b_hi = min(p / BS, a.W - 1);
+        for (int64_t b0 = b_lo; b0 <= b_hi; b0 += 32) {
+          const int64_t blk = b0 + lane;
+          const bool ok = blk <= b_hi;
+          const int64_t off = ok ? block_offset(a, seq, blk) : 0;
+          const unsigned msk = __ballot_sync(0xffffffffu, ok);
+          const int pos = n + lane;
+          if (ok && pos < kAttendMaxSlots) {
+            slots[pos].page_off = off;
+            slots[pos].key0 = blk * BS;
+            slots[pos].bias2 = 0.f;
+            slots[pos].remote = 0;
+          }
+          n += __popc(msk);
+          if (n > kAttendMaxSlots) n = kAttendMaxSlots;
         }
       }
     }
-    n_slots = n;
+    if (lane == 0) n_slots = n;
   }
   __syncthreads();
 

@@ -49,18 +49,22 @@ __device__ __forceinline__ void load4(const void* p, int64_t i, int dtype, float
   }
 }
 
-__global__ void __launch_bounds__(256) kbar_kernel(const KbarArgs a) {
-  __shared__ float aw_s[8][kMaxBlockSize];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + warp;
-  int64_t base, ntok, out_row;
+// One CTA (128 threads) per block/page: the block's tokens are staged in
+// shared memory as fp32 [bs][d+1] with every 16-byte global load of the block
+// issued before any arithmetic (8 per thread for a 64 x 128 bf16 page), then
+// thread i scores token i, warp 0 forms the masked softmax weights, and
+// thread f accumulates feature f of k_bar.
+constexpr int kKbarThreads = 128;
+
+__device__ __forceinline__ void kbar_item(const KbarArgs& a, int64_t item, int64_t& base, int64_t& ntok,
+                                          int64_t& out_row) {
+  ntok = -1;
   if (!a.paged) {
     if (item >= a.B * a.nblk) return;
     const int64_t b = item / a.nblk, c = item % a.nblk;
     base = b * a.sb + c * a.bs * a.st;
     ntok = min(a.bs, a.S - c * a.bs);
     out_row = item * a.d;
-    if (a.chunk_valid && lane == 0) a.chunk_valid[item] = ntok > 0;
   } else {
     const int64_t per = a.tail > 0 ? a.tail : a.W;
     if (item >= a.R * per) return;
@@ -69,64 +73,98 @@ __global__ void __launch_bounds__(256) kbar_kernel(const KbarArgs a) {
     const int64_t nb = (sl + a.bs - 1) / a.bs;
     const int64_t blk = a.tail > 0 ? nb - 1 - j : j;
     if (blk < 0 || blk >= nb || blk >= a.W) return;
-    ntok = min(a.bs, sl - blk * a.bs);
-    if (ntok <= 0) return;  // not a page in use: never clobber another request
+    const int64_t nt = min(a.bs, sl - blk * a.bs);
+    if (nt <= 0) return;  // not a page in use: never clobber another request's summary
     const int64_t page = a.block_table[r * a.s_bt + blk];
     base = page * a.s_page;
     out_row = page * a.s_kbar;
+    ntok = nt;
   }
-  const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
-  const bool act = 4 * lane < a.d;
-  float hc[4] = {0.f, 0.f, 0.f, 0.f};
-  if (act) {
+}
+
+__global__ void __launch_bounds__(kKbarThreads) kbar_kernel(const KbarArgs a) {
+  extern __shared__ __align__(16) float kb_smem[];  // [bs][d+1] then w[bs]
+  const int tid = threadIdx.x;
+  const int64_t item = blockIdx.x;
+  int64_t base = 0, ntok = -1, out_row = 0;
+  kbar_item(a, item, base, ntok, out_row);
+  if (ntok < 0) return;  // CTA-uniform
+  if (!a.paged && a.chunk_valid && tid == 0) a.chunk_valid[item] = ntok > 0;
+  const int d = static_cast<int>(a.d);
+  const int dp = d + 1;
+  float* ks = kb_smem;
+  float* w = kb_smem + a.bs * dp;
+  // stage: 16-byte pieces (8 elements of a 16-bit type, 4 of fp32), all loads
+  // of an 8-piece batch issued before any shared-memory store
+  const int vec = a.dtype == SRSWA_F32 ? 4 : 8;
+  const int ppt = d / vec;  // pieces per token
+  const int pieces = static_cast<int>(ntok) * ppt;
+  float* hcs = w + a.bs;
+  for (int f = tid; f < d; f += kKbarThreads) hcs[f] = a.hc[f];
+  for (int i0 = tid; i0 < pieces; i0 += kKbarThreads * 8) {
+    float v[8][8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) hc[e] = a.hc[4 * lane + e];
-  }
-  // pass 1: aw_i = clamp(k_i . hc / sqrt(d)) for valid tokens
-  for (int64_t i0 = 0; i0 < ntok; i0 += 8) {
-    float part[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float kv[4] = {0.f, 0.f, 0.f, 0.f};
-      if (act && i0 + j < ntok) load4(a.keys, base + (i0 + j) * a.st + 4 * lane, a.dtype, kv);
-      part[j] = kv[0] * hc[0] + kv[1] * hc[1] + kv[2] * hc[2] + kv[3] * hc[3];
-    }
-    const float s = transpose_reduce8<32>(part, lane);
-    const int my = 4 * ((lane & 16) != 0) + 2 * ((lane & 8) != 0) + ((lane & 4) != 0);
-    if ((lane & 3) == 0 && i0 + my < ntok)
-      aw_s[warp][i0 + my] = fminf(fmaxf(s * inv_sqrt_d, -kActClamp), kActClamp);
-  }
-  __syncwarp();
-  // masked softmax over valid tokens (row max over valid tokens only)
-  float mx = -INFINITY;
-  for (int64_t i = lane; i < ntok; i += 32) mx = fmaxf(mx, aw_s[warp][i]);
-  mx = warp_max(mx);
-  if (ntok <= 0) mx = 0.f;
-  float den = 0.f;
-  for (int64_t i = lane; i < ntok; i += 32) {
-    const float e = expf(aw_s[warp][i] - mx);
-    aw_s[warp][i] = e;
-    den += e;
-  }
-  den = warp_sum(den);
-  __syncwarp();
-  const float dn = fmaxf(den, 1e-6f);
-  // pass 2: k_bar = sum_i w_i k_i
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  if (act) {
-    for (int64_t i = 0; i < ntok; ++i) {
-      const float w = aw_s[warp][i] / dn;
-      float kv[4];
-      load4(a.keys, base + i * a.st + 4 * lane, a.dtype, kv);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[e] = fmaf(w, kv[e], acc[e]);
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kKbarThreads;
+      if (i < pieces) {
+        const int t = i / ppt, f = (i % ppt) * vec;
+        if (vec == 8) load8(a.keys, base + static_cast<int64_t>(t) * a.st + f, a.dtype, v[u]);
+        else load4(a.keys, base + static_cast<int64_t>(t) * a.st + f, a.dtype, v[u]);
+      }
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float v = acc[e];
-      a.out[out_row + 4 * lane + e] = isfinite(v) ? v : 0.f;
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kKbarThreads;
+      if (i < pieces) {
+        const int t = i / ppt, f = (i % ppt) * vec;
+        for (int e = 0; e < vec; ++e) ks[t * dp + f + e] = v[u][e];
+      }
     }
   }
+  __syncthreads();
+  const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(d));
+  for (int t = tid; t < ntok; t += kKbarThreads) {
+    float acc = 0.f;
+    for (int f = 0; f < d; ++f) acc = fmaf(ks[t * dp + f], hcs[f], acc);
+    w[t] = fminf(fmaxf(acc * inv_sqrt_d, -kActClamp), kActClamp);
+  }
+  __syncthreads();
+  if (tid < 32) {
+    // masked softmax over the valid tokens (row max over valid tokens only)
+    float mx = -INFINITY;
+    for (int t = tid; t < ntok; t += 32) mx = fmaxf(mx, w[t]);
+    mx = warp_max(mx);
+    if (ntok <= 0) mx = 0.f;
+    float den = 0.f;
+    for (int t = tid; t < ntok; t += 32) {
+      const float e = expf(w[t] - mx);
+      w[t] = e;
+      den += e;
+    }
+    den = warp_sum(den);
+    const float dn = fmaxf(den, 1e-6f);
+    __syncwarp();
+    for (int t = tid; t < ntok; t += 32) w[t] = w[t] / dn;
+  }
+  __syncthreads();
+  for (int f = tid; f < d; f += kKbarThreads) {
+    float acc = 0.f;
+    for (int t = 0; t < ntok; ++t) acc = fmaf(w[t], ks[t * dp + f], acc);
+    a.out[out_row + f] = isfinite(acc) ? acc : 0.f;
+  }
+}
+
+static int kbar_launch(const KbarArgs& a, int64_t items, cudaStream_t st) {
+  const size_t smem = (static_cast<size_t>(a.bs) * (a.d + 1) + a.bs + a.d) * sizeof(float);
+  if (smem > 227 * 1024) return SRSWA_ETOOLARGE;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kbar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  if (items >= (1ll << 31)) return SRSWA_ETOOLARGE;
+  kbar_kernel<<<static_cast<unsigned>(items), kKbarThreads, smem, st>>>(a);
+  return srswa_last_launch_status();
 }
 
 // ============================================================================
@@ -210,6 +248,63 @@ __device__ void route_dots(const RouteArgs& a, int64_t n, int64_t seq, int64_t c
     }
   }
 }
+
+// Exact 1.5-entmax over the M sorted top values held one per lane (lane j <
+// M holds the j-th largest x, its block sel_i and whether it is a candidate),
+// then the first K slots and their centred log-prior bias, written for row n.
+// Called by one warp.
+__device__ __forceinline__ void route_epilogue(const RouteArgs& a, int64_t n, int lane, float sel_v, int sel_i,
+                                               bool sel_cand) {
+  const int M = static_cast<int>(a.M);
+  // ---- exact 1.5-entmax over the M sorted values
+  // (hf-model-code/dash_attention.py:772-800): X = (x - max)/2; prefix sums in
+  // float64 rounded to fp32 per prefix (torch CPU cumsum of fp32); tau_rho =
+  // mean - sqrt(max(0, (1 - rho(meansq - mean^2))/rho)); support = #(tau <= X)
+  const float xmax = __shfl_sync(0xffffffffu, sel_v, 0);
+  const float X = (sel_v - xmax) / 2.0f;
+  double acc1 = 0.0, acc2 = 0.0;
+  float my_cs = 0.f, my_cs2 = 0.f;
+  for (int j = 0; j < M; ++j) {
+    const float xj = __shfl_sync(0xffffffffu, X, j);
+    acc1 += static_cast<double>(xj);
+    acc2 += static_cast<double>(xj * xj);
+    if (lane == j) { my_cs = static_cast<float>(acc1); my_cs2 = static_cast<float>(acc2); }
+  }
+  const float rho = static_cast<float>(lane + 1);
+  const float mean = my_cs / rho;
+  const float mean_sq = my_cs2 / rho;
+  const float ss = rho * (mean_sq - mean * mean);
+  const float delta = (1.0f - ss) / rho;
+  const float tau = mean - sqrtf(fmaxf(delta, 0.0f));
+  const unsigned sup_mask = __ballot_sync(0xffffffffu, lane < M && tau <= X);
+  int support = __popc(sup_mask);
+  if (support < 1) support = 1;
+  const float tau_star = __shfl_sync(0xffffffffu, tau, support - 1);
+  const float pm = fmaxf(X - tau_star, 0.0f);
+  const float prior = pm * pm;
+
+  // ---- first K slots, centred log-prior bias ----
+  const int K = static_cast<int>(a.K);
+  const bool vld = lane < K && sel_cand;
+  const float logp = logf(fmaxf(prior, a.floor_));
+  float sum = 0.f;
+  int cnt = 0;
+  for (int j = 0; j < K; ++j) {
+    const float lj = __shfl_sync(0xffffffffu, logp, j);
+    const int vj = __shfl_sync(0xffffffffu, static_cast<int>(vld), j);
+    if (vj) { sum += lj; ++cnt; }
+  }
+  const float mu = sum / static_cast<float>(cnt > 0 ? cnt : 1);
+  const float bias = vld ? (logp - mu) * a.inv_sigma : 0.f;
+  if (lane < K) {
+    const int64_t o = n * K + lane;
+    if (a.topi64) a.topi64[o] = sel_i;
+    if (a.topi32) a.topi32[o] = vld ? sel_i : -1;
+    if (a.bias) a.bias[o] = bias;
+    if (a.valid) a.valid[o] = vld ? 1 : 0;
+  }
+}
+
 
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -312,54 +407,192 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
     __syncwarp();
   }
 
-  // ---- phase 4: exact 1.5-entmax over the M sorted values
-  // (hf-model-code/dash_attention.py:772-800): X = (x - max)/2; prefix sums in
-  // float64 rounded to fp32 per prefix (torch CPU cumsum of fp32); tau_rho =
-  // mean - sqrt(max(0, (1 - rho(meansq - mean^2))/rho)); support = #(tau <= X)
-  const float xmax = __shfl_sync(0xffffffffu, sel_v, 0);
-  const float X = (sel_v - xmax) / 2.0f;
-  double acc1 = 0.0, acc2 = 0.0;
-  float my_cs = 0.f, my_cs2 = 0.f;
-  for (int j = 0; j < M; ++j) {
-    const float xj = __shfl_sync(0xffffffffu, X, j);
-    acc1 += static_cast<double>(xj);
-    acc2 += static_cast<double>(xj * xj);
-    if (lane == j) { my_cs = static_cast<float>(acc1); my_cs2 = static_cast<float>(acc2); }
-  }
-  const float rho = static_cast<float>(lane + 1);
-  const float mean = my_cs / rho;
-  const float mean_sq = my_cs2 / rho;
-  const float ss = rho * (mean_sq - mean * mean);
-  const float delta = (1.0f - ss) / rho;
-  const float tau = mean - sqrtf(fmaxf(delta, 0.0f));
-  const unsigned sup_mask = __ballot_sync(0xffffffffu, lane < M && tau <= X);
-  int support = __popc(sup_mask);
-  if (support < 1) support = 1;
-  const float tau_star = __shfl_sync(0xffffffffu, tau, support - 1);
-  const float pm = fmaxf(X - tau_star, 0.0f);
-  const float prior = pm * pm;
+  const bool sel_cand = lane < M && sel_i >= 0 && (fl[sel_i] & 1);
+  route_epilogue(a, n, lane, sel_v, sel_i, sel_cand);
+}
 
-  // ---- phase 5: first K slots, centred log-prior bias ----
-  const int K = static_cast<int>(a.K);
-  const bool is_cand = lane < M && sel_i >= 0 && (fl[sel_i] & 1);
-  const bool vld = lane < K && is_cand;
-  const float logp = logf(fmaxf(prior, a.floor_));
-  float sum = 0.f;
-  int cnt = 0;
-  for (int j = 0; j < K; ++j) {
-    const float lj = __shfl_sync(0xffffffffu, logp, j);
-    const int vj = __shfl_sync(0xffffffffu, static_cast<int>(vld), j);
-    if (vj) { sum += lj; ++cnt; }
+// ============================================================================
+// a2 + a4 for wide rows (decode shapes: few rows, hundreds to thousands of
+// candidate blocks): two kernels.
+//
+// route_score_kernel  streaming scores: one CTA per (row, 128-block chunk),
+//   clamped scores z (SCORE_NEG outside the row's remote range, with no loads
+//   there) written to a [N, nblk] array.
+// select_wide_kernel  one CTA per row.  x = cand ? z * idx_scale : -1e4 is
+//   packed with its block index and candidacy into a 64-bit key (x descending,
+//   then block ascending); each of the 8 warps extracts the top-M keys of its
+//   slice by repeated warp arg-max, warp 0 merges the 8 lists and runs the
+//   entmax / top-K / bias epilogue.  A candidate mask with no candidate in the
+//   row falls back to all remote blocks (CTA-wide OR).
+// ============================================================================
+constexpr int kWideMaxBlocks = 24576;  // shared-memory key array bound (192 KiB)
+
+__device__ __forceinline__ uint32_t ordered_bits(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float from_ordered(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+__device__ __forceinline__ unsigned long long pack_key(float x, int64_t c, bool cand) {
+  const uint32_t lo = (static_cast<uint32_t>(0x7fffffff - static_cast<int32_t>(c)) << 1) | (cand ? 1u : 0u);
+  return (static_cast<unsigned long long>(ordered_bits(x)) << 32) | lo;
+}
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
   }
-  const float mu = sum / static_cast<float>(cnt > 0 ? cnt : 1);
-  const float bias = vld ? (logp - mu) * a.inv_sigma : 0.f;
-  if (lane < K) {
-    const int64_t o = n * K + lane;
-    if (a.topi64) a.topi64[o] = sel_i;
-    if (a.topi32) a.topi32[o] = vld ? sel_i : -1;
-    if (a.bias) a.bias[o] = bias;
-    if (a.valid) a.valid[o] = vld ? 1 : 0;
+  return v;
+}
+
+// Top-M keys of k[0..n) (shared memory, unique non-zero keys) by one warp;
+// written in descending order to out[0..M) (0 where fewer than M keys).
+// Extracted keys are zeroed in k.
+__device__ void warp_topm_smem(unsigned long long* k, int n, int M, unsigned long long* out, int lane) {
+  unsigned long long best = 0ull;
+  for (int i = lane; i < n; i += 32) best = k[i] > best ? k[i] : best;
+  for (int m = 0; m < M; ++m) {
+    const unsigned long long w = warp_max_u64(best);
+    if (lane == 0) out[m] = w;
+    if (w != 0ull && best == w) {  // unique keys: exactly one owner lane
+      best = 0ull;
+      for (int i = lane; i < n; i += 32) {
+        unsigned long long v = k[i];
+        if (v == w) { k[i] = 0ull; v = 0ull; }
+        best = v > best ? v : best;
+      }
+    }
+    __syncwarp();
   }
+}
+
+// One CTA per (row, 128-block chunk): the chunk's block-table slice (one
+// coalesced load), then its k_bar rows in a single round (16 independent
+// 16-byte loads per lane, 8 warps).  Register-capped for 3 CTAs per SM.
+constexpr int kChunkBlocks = 128;
+
+__global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const RouteArgs a, float* zout) {
+  __shared__ int32_t bts[kChunkBlocks];
+  const int64_t n = blockIdx.y;
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * kChunkBlocks;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t seq = n / a.rows_per_seq;
+  const int64_t p = a.q_pos ? a.q_pos[n]
+                            : static_cast<int64_t>(a.seq_lens[seq]) - a.rows_per_seq + n % a.rows_per_seq;
+  int64_t c_hi = p >= 0 ? p / a.BS - a.L + 1 : 0;
+  if (c_hi < 0) c_hi = 0;
+  if (c_hi > a.nblk) c_hi = a.nblk;
+  if (a.seq_lens) {
+    const int64_t nb = (static_cast<int64_t>(a.seq_lens[seq]) + a.BS - 1) / a.BS;
+    if (c_hi > nb) c_hi = nb;
+  }
+  const int64_t hi = min(lo + kChunkBlocks, a.nblk);
+  const int64_t dhi = max(lo, min(hi, c_hi));  // blocks [lo, dhi) are remote
+  float* zrow = zout + n * a.nblk;
+  for (int64_t c = dhi + tid; c < hi; c += kRouteThreads) zrow[c] = kScoreNeg;
+  if (dhi == lo) return;  // CTA-uniform: nothing remote in this chunk
+  if (a.block_table && tid < dhi - lo) bts[tid] = a.block_table[seq * a.s_bt + lo + tid];
+  __syncthreads();
+  const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
+  float qv[4];
+  load4(a.q, n * a.s_q + 4 * lane, a.q_dtype, qv);
+  const int64_t c0 = lo + warp * 16;
+  if (c0 >= dhi) return;  // warp-uniform
+  float4 f[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int64_t c = c0 + i;
+    f[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < dhi) {
+      const int64_t off = a.block_table ? static_cast<int64_t>(bts[c - lo]) * a.s_kbar_c
+                                        : seq * a.s_kbar_b + c * a.s_kbar_c;
+      f[i] = __ldg(reinterpret_cast<const float4*>(a.kbar + off + 4 * lane));
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float part[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = f[8 * h + i];
+      part[i] = qv[0] * v.x + qv[1] * v.y + qv[2] * v.z + qv[3] * v.w;
+    }
+    const float sdot = transpose_reduce8<32>(part, lane);
+    const int my = 4 * ((lane & 16) != 0) + 2 * ((lane & 8) != 0) + ((lane & 4) != 0);
+    const int64_t c = c0 + 8 * h + my;
+    if ((lane & 3) == 0 && c < dhi) {
+      float z = fminf(fmaxf(sdot * inv_sqrt_d, -kActClamp), kActClamp);
+      if (sdot != sdot) z = sdot;  // NaN stays NaN (then "not remote")
+      zrow[c] = z;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteArgs a, const float* zin,
+                                                                    int64_t s_z) {
+  extern __shared__ __align__(16) unsigned long long wk[];  // [nblk] keys
+  __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
+  const int64_t n = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t nblk = a.nblk;
+  const int M = static_cast<int>(a.M);
+  const float* z = zin + n * s_z;
+  int any = 1;
+  if (a.cand) {
+    int f = 0;
+    for (int64_t c = tid; c < nblk; c += kRouteThreads)
+      f |= (z[c] > kScoreNeg * 0.5f) && a.cand[n * a.s_cand + c] != 0;
+    any = __syncthreads_or(f);
+  }
+  for (int64_t c = tid; c < nblk; c += kRouteThreads) {
+    const float zc = z[c];
+    if (a.scores_out) a.scores_out[n * nblk + c] = zc;
+    const bool remote = zc > kScoreNeg * 0.5f;
+    const bool cm = remote && (a.cand == nullptr || !any || a.cand[n * a.s_cand + c] != 0);
+    float x = cm ? zc * a.idx_scale : kEntmaxNeg;
+    if (!isfinite(x)) x = kEntmaxNeg;
+    wk[c] = pack_key(x, c, cm);
+  }
+  __syncthreads();
+  const int64_t per = (nblk + 7) / 8;
+  const int64_t wlo = warp * per;
+  const int64_t rem = nblk - wlo;
+  const int64_t wn = rem < 0 ? 0 : (rem < per ? rem : per);
+  warp_topm_smem(wk + wlo, static_cast<int>(wn), M, lists[warp], lane);
+  __syncthreads();
+  if (warp != 0) return;
+  unsigned long long* flat = &lists[0][0];
+  // merge: the 8 lists (M keys each, kMaxTopM stride) -> top-M
+  unsigned long long best = 0ull;
+  for (int i = lane; i < 8 * kMaxTopM; i += 32)
+    if ((i % kMaxTopM) < M) best = flat[i] > best ? flat[i] : best;
+  unsigned long long mine = 0ull;
+  for (int m = 0; m < M; ++m) {
+    const unsigned long long w = warp_max_u64(best);
+    if (lane == m) mine = w;
+    if (w != 0ull && best == w) {
+      best = 0ull;
+      for (int i = lane; i < 8 * kMaxTopM; i += 32) {
+        if ((i % kMaxTopM) >= M) continue;
+        unsigned long long v = flat[i];
+        if (v == w) { flat[i] = 0ull; v = 0ull; }
+        best = v > best ? v : best;
+      }
+    }
+    __syncwarp();
+  }
+  float sel_v = 0.f;
+  int sel_i = -1;
+  bool sel_c = false;
+  if (lane < M) {
+    sel_v = from_ordered(static_cast<uint32_t>(mine >> 32));
+    const uint32_t lo32 = static_cast<uint32_t>(mine);
+    sel_i = 0x7fffffff - static_cast<int>(lo32 >> 1);
+    sel_c = (lo32 & 1u) != 0;
+  }
+  route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
 }
 
 // ============================================================================
@@ -492,8 +725,47 @@ __global__ void pack_selection_kernel(const void* sel, int is64, int64_t rows, i
   }
 }
 
-static int route_launch(RouteArgs a, cudaStream_t st) {
+static bool use_wide(const RouteArgs& a) { return a.nblk >= 512 && a.nblk <= kWideMaxBlocks; }
+
+static size_t chunk_workspace(int64_t N, int64_t nblk) {
+  return (static_cast<size_t>(N * nblk) * 4 + 255) & ~static_cast<size_t>(255);
+}
+
+static bool use_chunked(const RouteArgs& a) { return !a.from_scores && a.d == 128 && use_wide(a); }
+
+static int select_wide_launch(RouteArgs a, const float* z, int64_t s_z, cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(a.nblk) * 8;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(select_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  if (a.N >= (1ll << 31)) return SRSWA_ETOOLARGE;
+  select_wide_kernel<<<static_cast<unsigned>(a.N), kRouteThreads, smem, st>>>(a, z, s_z);
+  return srswa_last_launch_status();
+}
+
+static int route_chunk_launch(RouteArgs a, void* ws, size_t ws_bytes, cudaStream_t st) {
+  // scores go to the caller's scores output when requested, else to workspace
+  float* z = a.scores_out;
+  if (!z) {
+    if (!ws || ws_bytes < chunk_workspace(a.N, a.nblk)) return SRSWA_EWORKSPACE;
+    z = static_cast<float*>(ws);
+  }
+  const int64_t nch = (a.nblk + kChunkBlocks - 1) / kChunkBlocks;
+  if (a.N >= 65536) return SRSWA_ETOOLARGE;
+  route_score_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(a.N)), kRouteThreads, 0, st>>>(a, z);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return static_cast<int>(e);
+  a.scores_out = nullptr;  // already written
+  return select_wide_launch(a, z, a.nblk, st);
+}
+
+static int route_launch(RouteArgs a, cudaStream_t st, void* ws = nullptr, size_t ws_bytes = 0) {
   if (a.N == 0) return 0;
+  // decode-shaped rows with many candidate blocks -> chunked score + merge
+  if (use_chunked(a)) return route_chunk_launch(a, ws, ws_bytes, st);
+  if (a.from_scores && use_wide(a)) return select_wide_launch(a, a.scores_in, a.s_sc, st);
   int rpc = 1;
   while (rpc < 8 && a.nblk * rpc * 2 <= 2048) rpc *= 2;
   a.rows_per_cta = rpc;
@@ -535,18 +807,17 @@ extern "C" int srswa_kbar_contig(const void* idx_k, int dtype, int64_t sb, int64
                                  int64_t S, int64_t d, int64_t block_size, const float* head_cls,
                                  float* kbar, uint8_t* chunk_valid, srswa_stream_t stream) {
   SRSWA_CHECK_ARG(idx_k && head_cls && kbar && B >= 0 && S >= 0, SRSWA_EINVAL);
-  SRSWA_CHECK_ARG(d > 0 && d <= 128 && d % 4 == 0, SRSWA_EUNSUPPORTED);
+  const int64_t align = dtype == SRSWA_F32 ? 4 : 8;  // 16-byte vector loads
+  SRSWA_CHECK_ARG(d > 0 && d <= 128 && d % align == 0, SRSWA_EUNSUPPORTED);
   SRSWA_CHECK_ARG(block_size > 0 && block_size <= kMaxBlockSize, SRSWA_EUNSUPPORTED);
-  const int64_t align = dtype == SRSWA_F32 ? 4 : 4;
-  SRSWA_CHECK_ARG((sb % align) == 0 && (st % align) == 0, SRSWA_EALIGN);
+  SRSWA_CHECK_ARG((sb % align) == 0 && (st % align) == 0 && (reinterpret_cast<uintptr_t>(idx_k) & 15) == 0,
+                  SRSWA_EALIGN);
   const int64_t nblk = (S + block_size - 1) / block_size;
   if (B * nblk == 0) return 0;
   KbarArgs a = {};
   a.keys = idx_k; a.dtype = dtype; a.d = d; a.bs = block_size; a.hc = head_cls; a.out = kbar;
   a.chunk_valid = chunk_valid; a.sb = sb; a.st = st; a.S = S; a.nblk = nblk; a.B = B; a.paged = 0;
-  const int64_t items = B * nblk;
-  kbar_kernel<<<static_cast<unsigned>((items + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  return srswa_last_launch_status();
+  return kbar_launch(a, B * nblk, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int srswa_kbar_paged(const void* idx_cache, int dtype, int64_t s_page, int64_t s_tok,
@@ -556,18 +827,19 @@ extern "C" int srswa_kbar_paged(const void* idx_cache, int dtype, int64_t s_page
                                 srswa_stream_t stream) {
   SRSWA_CHECK_ARG(idx_cache && block_table && seq_lens && head_cls && kbar_cache, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(R >= 0 && W > 0, SRSWA_EINVAL);
-  SRSWA_CHECK_ARG(d > 0 && d <= 128 && d % 4 == 0, SRSWA_EUNSUPPORTED);
+  const int64_t align = dtype == SRSWA_F32 ? 4 : 8;  // 16-byte vector loads
+  SRSWA_CHECK_ARG(d > 0 && d <= 128 && d % align == 0, SRSWA_EUNSUPPORTED);
   SRSWA_CHECK_ARG(block_size > 0 && block_size <= kMaxBlockSize, SRSWA_EUNSUPPORTED);
-  SRSWA_CHECK_ARG((s_page % 4) == 0 && (s_tok % 4) == 0 && (s_kbar % 4) == 0, SRSWA_EALIGN);
+  SRSWA_CHECK_ARG((s_page % align) == 0 && (s_tok % align) == 0 &&
+                      (reinterpret_cast<uintptr_t>(idx_cache) & 15) == 0,
+                  SRSWA_EALIGN);
   const int64_t per = tail_pages > 0 ? tail_pages : W;
   if (R * per == 0) return 0;
   KbarArgs a = {};
   a.keys = idx_cache; a.dtype = dtype; a.d = d; a.bs = block_size; a.hc = head_cls; a.out = kbar_cache;
   a.st = s_tok; a.block_table = block_table; a.seq_lens = seq_lens; a.s_page = s_page; a.s_bt = s_bt;
   a.W = W; a.R = R; a.tail = tail_pages; a.s_kbar = s_kbar; a.paged = 1;
-  const int64_t items = R * per;
-  kbar_kernel<<<static_cast<unsigned>((items + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  return srswa_last_launch_status();
+  return kbar_launch(a, R * per, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
@@ -576,7 +848,7 @@ extern "C" int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t 
                            int64_t rows_per_seq, const int64_t* q_pos, const uint8_t* cand,
                            int64_t s_cand, srswa_route_params params, int64_t* topi64,
                            int32_t* topi32, float* bias, uint8_t* valid, float* scores,
-                           srswa_stream_t stream) {
+                           void* workspace, size_t workspace_bytes, srswa_stream_t stream) {
   SRSWA_CHECK_ARG(idx_q && kbar && N >= 0 && nblk > 0 && rows_per_seq > 0, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(q_pos || seq_lens, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(d == 128 || d == 64, SRSWA_EUNSUPPORTED);
@@ -591,7 +863,19 @@ extern "C" int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t 
   a.seq_lens = seq_lens; a.rows_per_seq = rows_per_seq; a.q_pos = q_pos; a.cand = cand;
   a.s_cand = s_cand; a.N = N; a.nblk = nblk; a.topi64 = topi64; a.topi32 = topi32; a.bias = bias;
   a.valid = valid; a.scores_out = scores;
-  return route_launch(a, reinterpret_cast<cudaStream_t>(stream));
+  return route_launch(a, reinterpret_cast<cudaStream_t>(stream), workspace, workspace_bytes);
+}
+
+extern "C" size_t srswa_route_workspace_size(int64_t N, int64_t nblk, int64_t d, srswa_route_params params,
+                                             int has_cand) {
+  RouteArgs a = {};
+  if (N < 0 || nblk <= 0 || fill_route_params(a, params, nblk)) return 0;
+  a.d = d;
+  a.nblk = nblk;
+  a.N = N;
+  (void)has_cand;
+  if (!use_chunked(a)) return 0;
+  return chunk_workspace(N, nblk);
 }
 
 extern "C" int srswa_route_select(const float* scores, int64_t s_sc, int64_t N, int64_t nblk,

@@ -52,8 +52,9 @@ _SIGS = {
     "srswa_kbar_contig": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp]),
     "srswa_kbar_paged": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, vp, i64, i64, vp, i64, i64, vp, vp,
                                    i64, vp]),
+    "srswa_route_workspace_size": (C.c_size_t, [i64, i64, i64, RouteParams, C.c_int]),
     "srswa_route": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp, i64, vp, vp, i64,
-                              RouteParams, vp, vp, vp, vp, vp, vp]),
+                              RouteParams, vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),
     "srswa_route_select": (C.c_int, [vp, i64, i64, i64, vp, i64, RouteParams, vp, vp, vp, vp, vp]),
     "srswa_block_max_score": (C.c_int, [vp, C.c_int, i64, i64, vp, C.c_int, i64, i64, vp, vp, i64, i64,
                                         i64, i64, i64, i64, i64, C.c_int, vp, vp]),

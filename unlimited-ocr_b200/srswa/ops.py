@@ -102,11 +102,14 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
     sl = None if seq_lens is None else seq_lens.to(device=dev, dtype=torch.int32).contiguous()
     cnd, s_cand = _cand_args(cand, N, nblk)
     p = _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma)
-    rc = L.lib().srswa_route(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
-                             kbar.data_ptr(), s_b, s_c, nblk, L.ptr(bt), 0 if bt is None else bt.stride(0),
-                             L.ptr(sl), int(rows_per_seq), L.ptr(qp), L.ptr(cnd), s_cand, p,
-                             L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
-                             L.ptr(out["valid"]), L.ptr(out["scores"]), L.stream_of(idx_q))
+    lib = L.lib()
+    ws_n = lib.srswa_route_workspace_size(N, nblk, d, p, 1 if cnd is not None else 0)
+    ws = torch.empty(ws_n, device=dev, dtype=torch.uint8) if ws_n else None
+    rc = lib.srswa_route(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
+                         kbar.data_ptr(), s_b, s_c, nblk, L.ptr(bt), 0 if bt is None else bt.stride(0),
+                         L.ptr(sl), int(rows_per_seq), L.ptr(qp), L.ptr(cnd), s_cand, p,
+                         L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
+                         L.ptr(out["valid"]), L.ptr(out["scores"]), L.ptr(ws), ws_n, L.stream_of(idx_q))
     L.check(rc, "srswa_route")
     if out["valid"] is not None:
         out["valid"] = out["valid"].bool()
