@@ -252,6 +252,11 @@ SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, co
                         const float* bias, const uint8_t* valid, void* out, float* lse_out,
                         srswa_stream_t stream);
 
+/* Reads and clears the library's device error word: non-zero when a kernel's
+ * bounded wait on a tensor-core completion barrier expired (the kernel then
+ * skipped its outputs and exited cleanly).  No reference counterpart. */
+SRSWA_API int srswa_device_status(int* out);
+
 /* Log-sum-exp merge of C split-KV partials: o_parts [C,N,H,D] fp32, lse_parts
  * [C,N,H] fp32 natural log (-inf = empty part) -> out [N,H,D] (out_dtype,
  * contiguous) and lse_out [N,H] (optional).  Replaces

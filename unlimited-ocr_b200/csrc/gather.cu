@@ -375,22 +375,37 @@ static int check_gather_desc(const srswa_gather_desc* g) {
 
 using namespace srswa;
 
+namespace srswa {
+struct TcLayout {
+  size_t part_o, part_lse, count, offs, cursor, tiles, ntiles, pairs, total;
+  int64_t max_tiles;
+};
+TcLayout tc_layout(const srswa_gather_desc* g);
+bool tc_eligible(const srswa_gather_desc* g);
+int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const int32_t* sel,
+                  const float* bias, const int32_t* seg, void* o, int64_t sob, int64_t sot, int64_t soh, float* lse,
+                  void* workspace, size_t workspace_bytes, cudaStream_t st);
+}  // namespace srswa
+
 extern "C" size_t srswa_gather_fwd_workspace_size(const srswa_gather_desc* g) {
-  (void)g;
-  return 0;
+  if (check_gather_desc(g) || !tc_eligible(g)) return 0;
+  return tc_layout(g).total;
 }
 
 extern "C" int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v,
                                 const int32_t* sel, const float* bias, const int32_t* seg, void* o,
                                 int o_dtype, int64_t sob, int64_t sot, int64_t soh, float* lse,
                                 void* workspace, size_t workspace_bytes, srswa_stream_t stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   int rc = check_gather_desc(g);
   if (rc) return rc;
   SRSWA_CHECK_ARG(q && k && v && o && (g->S == 0 || sel), SRSWA_EINVAL);
   SRSWA_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                     reinterpret_cast<uintptr_t>(v)) & 15) == 0, SRSWA_EALIGN);
+  if (g->B * g->T == 0) return 0;
+  // tensor-core path (bf16, D = 128, 64-token blocks); CUDA-core rows otherwise
+  if (tc_eligible(g) && o_dtype == SRSWA_BF16 && ((sob | sot | soh) & 7) == 0)
+    return tc_gather_fwd(g, q, k, v, sel, bias, seg, o, sob, sot, soh, lse, workspace, workspace_bytes,
+                         reinterpret_cast<cudaStream_t>(stream));
   const int64_t nblk = (g->T + g->block_size - 1) / g->block_size;
   AttendArgs a = {};
   a.q = q; a.k = k; a.v = v; a.q_dtype = g->dtype; a.out_dtype = o_dtype;

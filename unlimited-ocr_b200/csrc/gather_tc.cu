@@ -1,0 +1,693 @@
+// Gather-attention forward on the 5th-generation tensor cores (tcgen05 / TMEM).
+//
+// Same semantics as the query-major forward (K1/K5 of the reference:
+// hf-model-code/sparse_gather_triton.py:35-122, sparse_gather_e2e_triton.py:36-121),
+// split in two passes so that every MMA has M = 128 real rows:
+//
+//  1. remote pass (remote_fwd_kernel): the selection is inverted into per
+//     (batch, index head, block) lists of (query, slot) pairs; a work item is
+//     one block and up to 128 of its pairs for one query head.  The pairs' q
+//     rows are gathered into shared memory, S = Q_g K_blk^T (M=128, N=64,
+//     K=128) goes to TMEM, the per-row softmax (slot bias, keys below the
+//     query's window start) runs on the 128 rows, O = P V_blk (N=128) goes to
+//     TMEM and the normalised partial (o bf16, lse fp32 log2) is written to a
+//     [B, T, S, HQ, D] workspace.
+//  2. band pass (band_fwd_kernel): one CTA per (batch, head, 128-query tile)
+//     walks the ~LW/64 + 2 key blocks of the local window with an online
+//     softmax (lazy rescaling of O in TMEM when the running max grows by more
+//     than 2^8), then merges each row with its remote partials (log-sum-exp
+//     weights) and writes o and lse.
+//
+// Shared-memory operand layout: see tc.cuh (128-byte swizzle, K-major Q/K/P,
+// MN-major V).  Every mbarrier is waited on by thread 0 only, with a bounded
+// spin; the result is broadcast through __syncthreads so an expired wait takes
+// a CTA-uniform exit path that drains the tensor pipe and frees TMEM.
+
+#include "attend.cuh"
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace srswa {
+
+constexpr int kTcThreads = 128;
+constexpr int kTileM = 128;
+constexpr int kBlk = 64;        // key block (BS)
+constexpr int kD = 128;         // head dim
+constexpr uint32_t kTmemCols = 256;
+constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (factor 256)
+
+// smem layout of the band kernel (bytes, 1024-aligned pieces)
+constexpr uint32_t kQBytes = kTileM * 128 * 2;  // two 64-col halves of [128 x 128 B]
+constexpr uint32_t kKVHalf = kBlk * 128;        // [64 rows x 128 B]
+constexpr uint32_t kKVBytes = 2 * kKVHalf;      // one 64 x 128 operand
+constexpr uint32_t kPBytes = kTileM * 128;      // [128 x 64 keys] bf16
+constexpr uint32_t kBandSmem = kQBytes + 2 * 2 * kKVBytes + kPBytes + 1024;  // + alignment slack
+
+struct TcArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t sqb, sqt, sqh, skb, skt, skh, svb, svt, svh;
+  __nv_bfloat16* o;
+  int64_t sob, sot, soh;
+  float* lse;                 // [B, T, HQ] natural log
+  const int32_t* sel;         // [B, HI, T, S] packed
+  const float* bias;          // [B, T, S] or null
+  const int32_t* seg;         // [B, T] or null
+  __nv_bfloat16* part_o;      // [B, T, S, HQ, D]
+  float* part_lse;            // [B, T, S, HQ] log2 domain
+  const int32_t* pairs;       // packed t * S + s, grouped by (b, hi, block)
+  const int4* tiles;          // (b*HI + hi, block, first pair, count)
+  const int32_t* ntiles;      // device count of tiles
+  int64_t B, T, HQ, Hkv, HI, S, LW, nblk;
+  float scale_log2;
+};
+
+__device__ __forceinline__ int64_t seg_start(const TcArgs& a, int64_t b, int64_t t) {
+  return a.seg ? static_cast<int64_t>(a.seg[b * a.T + t]) : 0;
+}
+__device__ __forceinline__ int64_t win_start(const TcArgs& a, int64_t b, int64_t t) {
+  int64_t ls = t - a.LW + 1;
+  const int64_t sg = seg_start(a, b, t);
+  if (ls < sg) ls = sg;
+  return ls < 0 ? 0 : ls;
+}
+// remote key range of block blk for query t: [lo, hi) (empty if lo >= hi)
+__device__ __forceinline__ void remote_range(const TcArgs& a, int64_t b, int64_t t, int64_t blk, int64_t& lo,
+                                             int64_t& hi) {
+  const int64_t sg = seg_start(a, b, t);
+  const int64_t ls = win_start(a, b, t);
+  lo = blk * kBlk > sg ? blk * kBlk : sg;
+  hi = min(min((blk + 1) * kBlk, ls), t + 1);
+}
+
+// 16-byte chunk loads of a [rows x 128] bf16 operand into the two swizzled
+// halves at sbase; row r of the operand comes from src(r) (null -> zeros).
+template <int ROWS, typename RowPtr>
+__device__ __forceinline__ void load_operand(uint32_t sbase, uint32_t half_bytes, RowPtr src, int tid,
+                                             const void* any_valid) {
+#pragma unroll
+  for (int i = 0; i < ROWS * 16 / kTcThreads; ++i) {
+    const int id = tid + i * kTcThreads;
+    const int r = id >> 4, c = id & 15;
+    const __nv_bfloat16* g = src(r);
+    const uint32_t dst = sbase + (c >> 3) * half_bytes + sw128_off(r, c & 7);
+    cp_async16_zfill(dst, g ? static_cast<const void*>(g + c * 8) : any_valid, g != nullptr);
+  }
+}
+
+// 32 fp32 -> 32 bf16 stored as four 16-byte chunks of a swizzled P row
+__device__ __forceinline__ void store_p_row(uint32_t pbase, int r, int chunk0, const float* p) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(p[8 * c + 2 * e], p[8 * c + 2 * e + 1]);
+      w[e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    const uint32_t dst = pbase + sw128_off(r, chunk0 + c);
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                 : "memory");
+  }
+}
+
+// S = Q K^T : M=128, N=64, K=128 (8 k-steps of 16)
+__device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t q_s, uint32_t k_s) {
+  constexpr uint32_t id = idesc_bf16(128, 64, 0);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint32_t off = (ks & 3) * 32u;  // 16-element step inside the 128-byte row
+    const uint64_t ad = sw128_desc(q_s + (ks >> 2) * kQBytes / 2 + off, 16, 1024);
+    const uint64_t bd = sw128_desc(k_s + (ks >> 2) * kKVHalf + off, 16, 1024);
+    mma_bf16_ss(tmem_s, ad, bd, id, ks > 0 ? 1u : 0u);
+  }
+}
+// O (+)= P V : M=128, N=128, K=64 (4 k-steps of 16 keys); V MN-major (halves LBO apart)
+__device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t p_s, uint32_t v_s, bool accumulate) {
+  constexpr uint32_t id = idesc_bf16(128, 128, 1);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const uint64_t ad = sw128_desc(p_s + ks * 32u, 16, 1024);
+    const uint64_t bd = sw128_desc(v_s + ks * 2048u, kKVHalf, 1024);
+    mma_bf16_ss(tmem_o, ad, bd, id, (accumulate || ks > 0) ? 1u : 0u);
+  }
+}
+
+// ============================================================================
+// band pass
+// ============================================================================
+__global__ void __launch_bounds__(kTcThreads) band_fwd_kernel(const TcArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t bar_s, bar_o;
+  __shared__ uint32_t tmem_base;
+  __shared__ int ok_s;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int64_t G = a.HQ / a.Hkv;
+  const int64_t hk = h / G;
+  const int64_t t0 = tile * kTileM;
+
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t q_s = sbase;
+  const uint32_t kv_s = q_s + kQBytes;  // stage st: K at kv_s + st*2*kKVBytes, V after it
+  const uint32_t p_s = kv_s + 2 * 2 * kKVBytes;
+
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bar_s, 1);
+    mbar_init(&bar_o, 1);
+    fence_mbar_init();
+    ok_s = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t tm_s = tmem, tm_o = tmem + 128;
+
+  // this thread's row
+  const int64_t t = t0 + tid;
+  const bool row_ok = t < a.T;
+  const int64_t ls = row_ok ? win_start(a, b, t) : 0;
+
+  // key blocks of the tile's window
+  const int64_t tlast = min(a.T, t0 + kTileM) - 1;
+  int64_t key_lo = t0 - a.LW + 1;
+  if (key_lo < 0) key_lo = 0;
+  const int64_t blo = key_lo / kBlk, bhi = tlast / kBlk;
+
+  auto q_row = [&](int r) -> const __nv_bfloat16* {
+    const int64_t tt = t0 + r;
+    return tt < a.T ? a.q + b * a.sqb + tt * a.sqt + h * a.sqh : nullptr;
+  };
+  auto kv_rows = [&](int64_t blk, const __nv_bfloat16* base, int64_t sb, int64_t st, int64_t sh) {
+    return [=](int r) -> const __nv_bfloat16* {
+      const int64_t kk = blk * kBlk + r;
+      return kk < a.T ? base + b * sb + kk * st + hk * sh : nullptr;
+    };
+  };
+  load_operand<kTileM>(q_s, kQBytes / 2, q_row, tid, a.q);
+  load_operand<kBlk>(kv_s, kKVHalf, kv_rows(blo, a.k, a.skb, a.skt, a.skh), tid, a.k);
+  load_operand<kBlk>(kv_s + kKVBytes, kKVHalf, kv_rows(blo, a.v, a.svb, a.svt, a.svh), tid, a.v);
+  cp_async_commit();
+
+  float m_ref = -INFINITY, l = 0.f;
+  bool aborted = false;
+  for (int64_t j = blo; j <= bhi; ++j) {
+    const int jj = static_cast<int>(j - blo);
+    const int st = jj & 1;
+    // previous P.V complete: its P buffer and the other stage are free
+    if (tid == 0 && jj > 0) ok_s = mbar_wait(&bar_o, (jj - 1) & 1, 101) ? 1 : 0;
+    __syncthreads();
+    if (!ok_s) { aborted = true; break; }
+    if (j + 1 <= bhi) {
+      const uint32_t nx = kv_s + (st ^ 1) * 2 * kKVBytes;
+      load_operand<kBlk>(nx, kKVHalf, kv_rows(j + 1, a.k, a.skb, a.skt, a.skh), tid, a.k);
+      load_operand<kBlk>(nx + kKVBytes, kKVHalf, kv_rows(j + 1, a.v, a.svb, a.svt, a.svh), tid, a.v);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    fence_async_smem();
+    __syncthreads();
+    const uint32_t k_cur = kv_s + st * 2 * kKVBytes;
+    if (tid == 0) {
+      tc_fence_after();
+      issue_qk(tm_s, q_s, k_cur);
+      mma_commit(&bar_s);
+      ok_s = mbar_wait(&bar_s, jj & 1, 102) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!ok_s) { aborted = true; break; }
+    tc_fence_after();
+    // ---- softmax of this row over the block's 64 keys ----
+    float s[64];
+    {
+      float s0[32], s1[32];
+      tmem_ld32(tm_s + lane_off, s0);
+      tmem_ld32(tm_s + lane_off + 32, s1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) { s[i] = s0[i]; s[32 + i] = s1[i]; }
+    }
+    const int64_t k0 = j * kBlk;
+    float mloc = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const int64_t key = k0 + i;
+      const bool valid = row_ok && key >= ls && key <= t;
+      s[i] = valid ? s[i] * a.scale_log2 : -INFINITY;
+      mloc = fmaxf(mloc, s[i]);
+    }
+    const bool need = mloc > m_ref + kRescaleLog2;  // also true on the first valid block
+    const float alpha = need ? (m_ref == -INFINITY ? 0.f : exp2f(m_ref - mloc)) : 1.f;
+    if (need) {
+      l *= alpha;
+      m_ref = mloc;
+    }
+    if (__any_sync(0xffffffffu, need && jj > 0)) {  // rescale O rows of this warp in TMEM
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(tm_o + lane_off + 32 * c, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+        tmem_st32(tm_o + lane_off + 32 * c, ov);
+      }
+      tmem_wait_st();
+    }
+    float lsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float p = (s[i] == -INFINITY) ? 0.f : exp2f(s[i] - m_ref);
+      s[i] = p;
+      lsum += p;
+    }
+    l += lsum;
+    store_p_row(p_s, tid, 0, s);
+    store_p_row(p_s, tid, 4, s + 32);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      issue_pv(tm_o, p_s, k_cur + kKVBytes, jj > 0);
+      mma_commit(&bar_o);
+    }
+  }
+  const int nblocks = static_cast<int>(bhi - blo + 1);
+  // drain: the last P.V (or, after an abort, whatever was committed)
+  if (tid == 0) ok_s = mbar_wait(&bar_o, (nblocks - 1) & 1, 103) ? 1 : 0;
+  __syncthreads();
+  cp_async_wait<0>();
+  if (!aborted && ok_s) {
+    tc_fence_after();
+    // ---- epilogue: merge with remote partials, write o and lse ----
+    const int64_t hi = (hk * a.HI) / a.Hkv;
+    float M = (l > 0.f) ? m_ref + log2f(l) : -INFINITY;
+    float lse_s[64];
+    int64_t slot_base = 0;
+    int nslot = 0;
+    if (row_ok && a.part_o) {
+      const int32_t* srow = a.sel + ((b * a.HI + hi) * a.T + t) * a.S;
+      slot_base = ((b * a.T + t) * a.S) * a.HQ + h;
+      for (int64_t s2 = 0; s2 < a.S && s2 < 64; ++s2) {
+        lse_s[s2] = -INFINITY;
+        const int64_t blk = srow[s2];
+        if (blk < 0 || blk >= a.nblk) continue;
+        int64_t lo, hi2;
+        remote_range(a, b, t, blk, lo, hi2);
+        if (lo >= hi2) continue;
+        bool dup = false;
+        for (int64_t u = 0; u < s2; ++u) dup |= srow[u] == blk;
+        if (dup) continue;
+        lse_s[s2] = a.part_lse[slot_base + s2 * a.HQ];
+        M = fmaxf(M, lse_s[s2]);
+      }
+      nslot = static_cast<int>(a.S < 64 ? a.S : 64);
+    }
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    const float wb = (l > 0.f) ? exp2f(m_ref - Mu) : 0.f;
+    float den = l * wb;
+    for (int s2 = 0; s2 < nslot; ++s2)
+      if (lse_s[s2] != -INFINITY) den += exp2f(lse_s[s2] - Mu);
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float ov[32];
+      tmem_ld32(tm_o + lane_off + 32 * c, ov);
+      tmem_wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ov[i] *= wb;
+        for (int s2 = 0; s2 < nslot; ++s2) {
+          if (lse_s[s2] == -INFINITY) continue;
+          const float w = exp2f(lse_s[s2] - Mu);
+          const uint4* src = reinterpret_cast<const uint4*>(a.part_o + (slot_base + s2 * a.HQ) * kD + 32 * c);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const uint4 u = src[q4];
+            ov[8 * q4 + 0] = fmaf(w, bf16_lo(u.x), ov[8 * q4 + 0]);
+            ov[8 * q4 + 1] = fmaf(w, bf16_hi(u.x), ov[8 * q4 + 1]);
+            ov[8 * q4 + 2] = fmaf(w, bf16_lo(u.y), ov[8 * q4 + 2]);
+            ov[8 * q4 + 3] = fmaf(w, bf16_hi(u.y), ov[8 * q4 + 3]);
+            ov[8 * q4 + 4] = fmaf(w, bf16_lo(u.z), ov[8 * q4 + 4]);
+            ov[8 * q4 + 5] = fmaf(w, bf16_hi(u.z), ov[8 * q4 + 5]);
+            ov[8 * q4 + 6] = fmaf(w, bf16_lo(u.w), ov[8 * q4 + 6]);
+            ov[8 * q4 + 7] = fmaf(w, bf16_hi(u.w), ov[8 * q4 + 7]);
+          }
+        }
+        __nv_bfloat16* dst = a.o + b * a.sob + t * a.sot + h * a.soh + 32 * c;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float tmp[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
+          store8(dst, 8 * q4, SRSWA_BF16, tmp);
+        }
+      }
+    }
+    if (row_ok && a.lse) a.lse[(b * a.T + t) * a.HQ + h] = den > 0.f ? (Mu + log2f(den)) * kLn2 : -INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ============================================================================
+// remote pass: inverted selection lists
+// ============================================================================
+// count[b*HI+hi][blk] += 1 for every usable (t, slot) selection
+__global__ void pairs_count_kernel(const TcArgs a, int32_t* count) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, hi, t)
+  if (i >= a.B * a.HI * a.T) return;
+  const int64_t t = i % a.T, bh = i / a.T, b = bh / a.HI;
+  const int32_t* srow = a.sel + i * a.S;
+  for (int64_t s = 0; s < a.S; ++s) {
+    const int64_t blk = srow[s];
+    if (blk < 0 || blk >= a.nblk) continue;
+    int64_t lo, hi;
+    remote_range(a, b, t, blk, lo, hi);
+    if (lo >= hi) continue;
+    bool dup = false;
+    for (int64_t u = 0; u < s; ++u) dup |= srow[u] == blk;
+    if (dup) continue;
+    atomicAdd(count + bh * a.nblk + blk, 1);
+  }
+}
+
+// single-CTA exclusive scans: pair offsets and tile offsets per (b*HI+hi, blk);
+// writes the tile descriptors and the tile count
+__global__ void pairs_scan_kernel(const TcArgs a, const int32_t* count, int32_t* offs, int32_t* cursor,
+                                  int4* tiles, int32_t* ntiles) {
+  __shared__ int32_t sh_p[1024], sh_t[1024];
+  const int64_t n = a.B * a.HI * a.nblk;
+  int32_t base_p = 0, base_t = 0;
+  for (int64_t c0 = 0; c0 < n; c0 += 1024) {
+    const int64_t i = c0 + threadIdx.x;
+    const int32_t cnt = i < n ? count[i] : 0;
+    sh_p[threadIdx.x] = cnt;
+    sh_t[threadIdx.x] = (cnt + kTileM - 1) / kTileM;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {  // inclusive Hillis-Steele scan
+      const int32_t vp = threadIdx.x >= static_cast<unsigned>(o) ? sh_p[threadIdx.x - o] : 0;
+      const int32_t vt = threadIdx.x >= static_cast<unsigned>(o) ? sh_t[threadIdx.x - o] : 0;
+      __syncthreads();
+      sh_p[threadIdx.x] += vp;
+      sh_t[threadIdx.x] += vt;
+      __syncthreads();
+    }
+    if (i < n) {
+      const int32_t op = base_p + sh_p[threadIdx.x] - cnt;
+      const int32_t nt = (cnt + kTileM - 1) / kTileM;
+      const int32_t ot = base_t + sh_t[threadIdx.x] - nt;
+      offs[i] = op;
+      cursor[i] = op;
+      for (int32_t k = 0; k < nt; ++k) {
+        const int32_t first = op + k * kTileM;
+        tiles[ot + k] = make_int4(static_cast<int>(i / a.nblk), static_cast<int>(i % a.nblk), first,
+                                  min(kTileM, cnt - k * kTileM));
+      }
+    }
+    __syncthreads();
+    base_p += sh_p[1023];
+    base_t += sh_t[1023];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *ntiles = base_t;
+}
+
+__global__ void pairs_fill_kernel(const TcArgs a, int32_t* cursor, int32_t* pairs) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= a.B * a.HI * a.T) return;
+  const int64_t t = i % a.T, bh = i / a.T, b = bh / a.HI;
+  const int32_t* srow = a.sel + i * a.S;
+  for (int64_t s = 0; s < a.S; ++s) {
+    const int64_t blk = srow[s];
+    if (blk < 0 || blk >= a.nblk) continue;
+    int64_t lo, hi;
+    remote_range(a, b, t, blk, lo, hi);
+    if (lo >= hi) continue;
+    bool dup = false;
+    for (int64_t u = 0; u < s; ++u) dup |= srow[u] == blk;
+    if (dup) continue;
+    const int32_t pos = atomicAdd(cursor + bh * a.nblk + blk, 1);
+    pairs[pos] = static_cast<int32_t>(t * a.S + s);
+  }
+}
+
+// One work item = (tile, query head of the tile's index head).  Persistent:
+// grid-stride over items; the item count comes from device memory.
+__global__ void __launch_bounds__(kTcThreads) remote_fwd_kernel(const TcArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int ok_s;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t q_s = sbase;
+  const uint32_t k_s = q_s + kQBytes;
+  const uint32_t v_s = k_s + kKVBytes;
+  const uint32_t p_s = v_s + kKVBytes;
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    ok_s = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t tm_s = tmem, tm_o = tmem + 128;
+  const int64_t hpi = a.HQ / a.HI;  // query heads per index head
+  const int64_t nitems = static_cast<int64_t>(*a.ntiles) * hpi;
+  uint32_t phase = 0;
+  for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x) {
+    const int4 td = a.tiles[item / hpi];
+    const int64_t bh = td.x, blk = td.y, first = td.z, cnt = td.w;
+    const int64_t b = bh / a.HI, hi = bh % a.HI;
+    const int64_t h = hi * hpi + item % hpi;
+    const int64_t hk = h / (a.HQ / a.Hkv);
+    // this thread's pair
+    int64_t t = -1, slot = 0;
+    if (tid < cnt) {
+      const int32_t pk = a.pairs[first + tid];
+      t = pk / a.S;
+      slot = pk % a.S;
+    }
+    auto q_row = [&](int r) -> const __nv_bfloat16* {
+      if (r >= cnt) return nullptr;
+      const int32_t pk = a.pairs[first + r];
+      return a.q + b * a.sqb + static_cast<int64_t>(pk / a.S) * a.sqt + h * a.sqh;
+    };
+    auto k_row = [&](int r) -> const __nv_bfloat16* {
+      const int64_t kk = blk * kBlk + r;
+      return kk < a.T ? a.k + b * a.skb + kk * a.skt + hk * a.skh : nullptr;
+    };
+    auto v_row = [&](int r) -> const __nv_bfloat16* {
+      const int64_t kk = blk * kBlk + r;
+      return kk < a.T ? a.v + b * a.svb + kk * a.svt + hk * a.svh : nullptr;
+    };
+    load_operand<kTileM>(q_s, kQBytes / 2, q_row, tid, a.q);
+    load_operand<kBlk>(k_s, kKVHalf, k_row, tid, a.k);
+    load_operand<kBlk>(v_s, kKVHalf, v_row, tid, a.v);
+    cp_async_commit();
+    cp_async_wait<0>();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      issue_qk(tm_s, q_s, k_s);
+      mma_commit(&bar);
+      ok_s = mbar_wait(&bar, phase, 201) ? 1 : 0;
+    }
+    phase ^= 1;
+    __syncthreads();
+    if (!ok_s) break;
+    tc_fence_after();
+    float s[64];
+    {
+      float s0[32], s1[32];
+      tmem_ld32(tm_s + lane_off, s0);
+      tmem_ld32(tm_s + lane_off + 32, s1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) { s[i] = s0[i]; s[32 + i] = s1[i]; }
+    }
+    float m = -INFINITY;
+    int64_t lo = 0, hi2 = 0;
+    float bias2 = 0.f;
+    if (t >= 0) {
+      remote_range(a, b, t, blk, lo, hi2);
+      if (a.bias) bias2 = a.bias[(b * a.T + t) * a.S + slot] * kLog2e;
+    }
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const int64_t key = blk * kBlk + i;
+      const bool valid = t >= 0 && key >= lo && key < hi2;
+      s[i] = valid ? s[i] * a.scale_log2 + bias2 : -INFINITY;
+      m = fmaxf(m, s[i]);
+    }
+    float lsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float p = (s[i] == -INFINITY) ? 0.f : exp2f(s[i] - m);
+      s[i] = p;
+      lsum += p;
+    }
+    store_p_row(p_s, tid, 0, s);
+    store_p_row(p_s, tid, 4, s + 32);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      issue_pv(tm_o, p_s, v_s, false);
+      mma_commit(&bar);
+      ok_s = mbar_wait(&bar, phase, 202) ? 1 : 0;
+    }
+    phase ^= 1;
+    __syncthreads();
+    if (!ok_s) break;
+    tc_fence_after();
+    const int64_t prow = ((b * a.T + (t < 0 ? 0 : t)) * a.S + slot) * a.HQ + h;
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float ov[32];
+      tmem_ld32(tm_o + lane_off + 32 * c, ov);
+      tmem_wait_ld();
+      if (t >= 0) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float tmp[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
+          store8(a.part_o + prow * kD + 32 * c, 8 * q4, SRSWA_BF16, tmp);
+        }
+      }
+    }
+    if (t >= 0) a.part_lse[prow] = lsum > 0.f ? m + log2f(lsum) : -INFINITY;
+    tc_fence_before();
+    __syncthreads();  // smem and TMEM reuse by the next item
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+struct TcLayout {
+  size_t part_o, part_lse, count, offs, cursor, tiles, ntiles, pairs, total;
+  int64_t max_tiles;
+};
+
+static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+TcLayout tc_layout(const srswa_gather_desc* g) {
+  TcLayout L;
+  const int64_t nblk = (g->T + kBlk - 1) / kBlk;
+  const int64_t nbh = g->B * g->HI * nblk;
+  const int64_t npairs = g->B * g->HI * g->T * g->S;
+  L.max_tiles = npairs / kTileM + nbh + 1;
+  size_t off = 0;
+  L.part_o = off;
+  off += al256(static_cast<size_t>(g->B * g->T * g->S * g->HQ * kD) * 2);
+  L.part_lse = off;
+  off += al256(static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4);
+  L.count = off;
+  off += al256(static_cast<size_t>(nbh) * 4);
+  L.offs = off;
+  off += al256(static_cast<size_t>(nbh) * 4);
+  L.cursor = off;
+  off += al256(static_cast<size_t>(nbh) * 4);
+  L.tiles = off;
+  off += al256(static_cast<size_t>(L.max_tiles) * 16);
+  L.ntiles = off;
+  off += 256;
+  L.pairs = off;
+  off += al256(static_cast<size_t>(npairs) * 4);
+  L.total = off;
+  return L;
+}
+
+bool tc_eligible(const srswa_gather_desc* g) {
+  return g->D == kD && g->block_size == kBlk && g->dtype == SRSWA_BF16 && g->S <= 64 && g->T > 0 &&
+         ((g->sqb | g->sqt | g->sqh | g->skb | g->skt | g->skh | g->svb | g->svt | g->svh) & 7) == 0;
+}
+
+int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const int32_t* sel,
+                  const float* bias, const int32_t* seg, void* o, int64_t sob, int64_t sot, int64_t soh, float* lse,
+                  void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const TcLayout L = tc_layout(g);
+  if (!workspace || workspace_bytes < L.total) return SRSWA_EWORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  TcArgs a = {};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.sqb = g->sqb; a.sqt = g->sqt; a.sqh = g->sqh; a.skb = g->skb; a.skt = g->skt; a.skh = g->skh;
+  a.svb = g->svb; a.svt = g->svt; a.svh = g->svh;
+  a.o = static_cast<__nv_bfloat16*>(o); a.sob = sob; a.sot = sot; a.soh = soh; a.lse = lse;
+  a.sel = sel; a.bias = bias; a.seg = seg;
+  a.part_o = reinterpret_cast<__nv_bfloat16*>(ws + L.part_o);
+  a.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
+  a.pairs = reinterpret_cast<int32_t*>(ws + L.pairs);
+  a.tiles = reinterpret_cast<int4*>(ws + L.tiles);
+  a.ntiles = reinterpret_cast<int32_t*>(ws + L.ntiles);
+  a.B = g->B; a.T = g->T; a.HQ = g->HQ; a.Hkv = g->Hkv; a.HI = g->HI; a.S = g->S;
+  a.LW = g->local_window > 0 ? g->local_window : kBlk;
+  a.nblk = (g->T + kBlk - 1) / kBlk;
+  a.scale_log2 = g->scale * kLog2e;
+  int32_t* count = reinterpret_cast<int32_t*>(ws + L.count);
+  int32_t* offs = reinterpret_cast<int32_t*>(ws + L.offs);
+  int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
+
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(band_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBandSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(remote_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kQBytes + 2 * kKVBytes + kPBytes + 1024);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_done = true;
+  }
+  if (g->S > 0) {
+    const int64_t nbh = a.B * a.HI * a.nblk;
+    SRSWA_CUDA_TRY(cudaMemsetAsync(count, 0, static_cast<size_t>(nbh) * 4, st));
+    const int64_t rows = a.B * a.HI * a.T;
+    pairs_count_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, count);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    pairs_scan_kernel<<<1, 1024, 0, st>>>(a, count, offs, cursor, const_cast<int4*>(a.tiles),
+                                          const_cast<int32_t*>(a.ntiles));
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    pairs_fill_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, cursor,
+                                                                               const_cast<int32_t*>(a.pairs));
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    remote_fwd_kernel<<<148 * 2, kTcThreads, kQBytes + 2 * kKVBytes + kPBytes + 1024, st>>>(a);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+  } else {
+    a.part_o = nullptr;
+  }
+  dim3 grid(static_cast<unsigned>((g->T + kTileM - 1) / kTileM), static_cast<unsigned>(g->HQ),
+            static_cast<unsigned>(g->B));
+  band_fwd_kernel<<<grid, kTcThreads, kBandSmem, st>>>(a);
+  return srswa_last_launch_status();
+}
+
+}  // namespace srswa
+
+extern "C" int srswa_device_status(int* out) {
+  if (!out) return SRSWA_EINVAL;
+  return srswa::tc_read_clear_error(out);
+}

@@ -920,8 +920,9 @@ extern "C" int srswa_block_max_score(const void* q, int q_dtype, int64_t sqb, in
 
 extern "C" int srswa_pack_selection(const void* sel, int is64, int64_t rows, int64_t S, int64_t nblk,
                                     int32_t* out, srswa_stream_t stream) {
-  SRSWA_CHECK_ARG(sel && out && rows >= 0 && S >= 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(rows >= 0 && S >= 0, SRSWA_EINVAL);
   if (rows * S == 0) return 0;
+  SRSWA_CHECK_ARG(sel && out, SRSWA_EINVAL);
   pack_selection_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0,
                           reinterpret_cast<cudaStream_t>(stream)>>>(sel, is64, rows, S, nblk, out);
   return srswa_last_launch_status();

@@ -172,6 +172,8 @@ def pack_selection(sel, nblk):
         s = s.to(torch.int64)
         is64 = 1
     out = torch.empty(s.shape, device=s.device, dtype=torch.int32)
+    if s.numel() == 0:
+        return out
     S = s.shape[-1]
     rows = s.numel() // max(S, 1)
     rc = L.lib().srswa_pack_selection(s.data_ptr(), is64, rows, S, int(nblk), out.data_ptr(), L.stream_of(s))
