@@ -40,8 +40,11 @@ constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (factor 256)
 constexpr uint32_t kQBytes = kTileM * 128 * 2;  // two 64-col halves of [128 x 128 B]
 constexpr uint32_t kKVHalf = kBlk * 128;        // [64 rows x 128 B]
 constexpr uint32_t kKVBytes = 2 * kKVHalf;      // one 64 x 128 operand
-constexpr uint32_t kPBytes = kTileM * 128;      // [128 x 64 keys] bf16
-constexpr uint32_t kBandSmem = kQBytes + 2 * 2 * kKVBytes + kPBytes + 1024;  // + alignment slack
+constexpr uint32_t kPBytes = kTileM * 128;      // [128 x 64 keys] bf16 (fits a K operand's 16 KB)
+// P of a block is written over that block's K operand, dead once S is in TMEM
+constexpr uint32_t kBandSmem = kQBytes + 2 * 2 * kKVBytes + 1024;  // + alignment slack -> 2 CTAs/SM
+constexpr uint32_t kRemoteSmem = kQBytes + 2 * kKVBytes + 1024;     // -> 3 CTAs/SM
+constexpr uint32_t kRemoteTmemCols = 128;  // S (cols 0-63) is dead before O (cols 0-127) is written
 
 struct TcArgs {
   const __nv_bfloat16* q;
@@ -151,7 +154,6 @@ __global__ void __launch_bounds__(kTcThreads) band_fwd_kernel(const TcArgs a) {
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t q_s = sbase;
   const uint32_t kv_s = q_s + kQBytes;  // stage st: K at kv_s + st*2*kKVBytes, V after it
-  const uint32_t p_s = kv_s + 2 * 2 * kKVBytes;
 
   if (warp == 0) {
     tmem_alloc(&tmem_base, kTmemCols);
@@ -201,21 +203,13 @@ __global__ void __launch_bounds__(kTcThreads) band_fwd_kernel(const TcArgs a) {
   for (int64_t j = blo; j <= bhi; ++j) {
     const int jj = static_cast<int>(j - blo);
     const int st = jj & 1;
-    // previous P.V complete: its P buffer and the other stage are free
-    if (tid == 0 && jj > 0) ok_s = mbar_wait(&bar_o, (jj - 1) & 1, 101) ? 1 : 0;
-    __syncthreads();
-    if (!ok_s) { aborted = true; break; }
-    if (j + 1 <= bhi) {
-      const uint32_t nx = kv_s + (st ^ 1) * 2 * kKVBytes;
-      load_operand<kBlk>(nx, kKVHalf, kv_rows(j + 1, a.k, a.skb, a.skt, a.skh), tid, a.k);
-      load_operand<kBlk>(nx + kKVBytes, kKVHalf, kv_rows(j + 1, a.v, a.svb, a.svt, a.svh), tid, a.v);
-    }
-    cp_async_commit();
-    cp_async_wait<1>();
+    // block j's operands have landed (its group; the prefetch group may pend)
+    cp_async_wait<0>();
     fence_async_smem();
     __syncthreads();
     const uint32_t k_cur = kv_s + st * 2 * kKVBytes;
     if (tid == 0) {
+      // S_j queues behind P.V_{j-1}; its completion implies P.V_{j-1} done
       tc_fence_after();
       issue_qk(tm_s, q_s, k_cur);
       mma_commit(&bar_s);
@@ -223,6 +217,13 @@ __global__ void __launch_bounds__(kTcThreads) band_fwd_kernel(const TcArgs a) {
     }
     __syncthreads();
     if (!ok_s) { aborted = true; break; }
+    // the other stage (block j-1, its P.V done) is free: prefetch block j+1
+    if (j + 1 <= bhi) {
+      const uint32_t nx = kv_s + (st ^ 1) * 2 * kKVBytes;
+      load_operand<kBlk>(nx, kKVHalf, kv_rows(j + 1, a.k, a.skb, a.skt, a.skh), tid, a.k);
+      load_operand<kBlk>(nx + kKVBytes, kKVHalf, kv_rows(j + 1, a.v, a.svb, a.svt, a.svh), tid, a.v);
+    }
+    cp_async_commit();
     tc_fence_after();
     // ---- softmax of this row over the block's 64 keys ----
     float s[64];
@@ -269,14 +270,14 @@ __global__ void __launch_bounds__(kTcThreads) band_fwd_kernel(const TcArgs a) {
       lsum += p;
     }
     l += lsum;
-    store_p_row(p_s, tid, 0, s);
-    store_p_row(p_s, tid, 4, s + 32);
+    store_p_row(k_cur, tid, 0, s);  // P over the dead K operand of this stage
+    store_p_row(k_cur, tid, 4, s + 32);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      issue_pv(tm_o, p_s, k_cur + kKVBytes, jj > 0);
+      issue_pv(tm_o, k_cur, k_cur + kKVBytes, jj > 0);
       mma_commit(&bar_o);
     }
   }
@@ -453,9 +454,9 @@ __global__ void __launch_bounds__(kTcThreads) remote_fwd_kernel(const TcArgs a) 
   const uint32_t q_s = sbase;
   const uint32_t k_s = q_s + kQBytes;
   const uint32_t v_s = k_s + kKVBytes;
-  const uint32_t p_s = v_s + kKVBytes;
+  const uint32_t p_s = k_s;  // P over K (dead once S is in TMEM)
   if (warp == 0) {
-    tmem_alloc(&tmem_base, kTmemCols);
+    tmem_alloc(&tmem_base, kRemoteTmemCols);
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -468,7 +469,7 @@ __global__ void __launch_bounds__(kTcThreads) remote_fwd_kernel(const TcArgs a) 
   tc_fence_after();
   const uint32_t tmem = tmem_base;
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t tm_s = tmem, tm_o = tmem + 128;
+  const uint32_t tm_s = tmem, tm_o = tmem;  // O overwrites S after the softmax read it
   const int64_t hpi = a.HQ / a.HI;  // query heads per index head
   const int64_t nitems = static_cast<int64_t>(*a.ntiles) * hpi;
   uint32_t phase = 0;
@@ -583,7 +584,7 @@ __global__ void __launch_bounds__(kTcThreads) remote_fwd_kernel(const TcArgs a) 
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 0) tmem_dealloc(tmem, kRemoteTmemCols);
 }
 
 // ---------------------------------------------------------------------------
@@ -657,8 +658,7 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(band_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBandSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(remote_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kQBytes + 2 * kKVBytes + kPBytes + 1024);
+    e = cudaFuncSetAttribute(remote_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRemoteSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done = true;
   }
@@ -674,7 +674,7 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     pairs_fill_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, cursor,
                                                                                const_cast<int32_t*>(a.pairs));
     SRSWA_CUDA_TRY(cudaGetLastError());
-    remote_fwd_kernel<<<148 * 2, kTcThreads, kQBytes + 2 * kKVBytes + kPBytes + 1024, st>>>(a);
+    remote_fwd_kernel<<<148 * 3, kTcThreads, kRemoteSmem, st>>>(a);
     SRSWA_CUDA_TRY(cudaGetLastError());
   } else {
     a.part_o = nullptr;
