@@ -1,8 +1,9 @@
-"""GPU parity of the tensor-core (tcgen05/TMEM) gather-attention forward:
-band pass + block-major remote pass over inverted selection lists.  Taken for
-bf16, head dim 128, 64-token blocks; compared with the CPU oracle and, at
-larger sizes, with the CUDA-core row kernel (selected here by asking for fp32
-output, which the tensor-core path does not produce).
+"""GPU parity of the tensor-core (tcgen05/TMEM) gather-attention forward and
+backward: band pass + block-major remote pass over inverted selection lists.
+Taken for bf16, head dim 128, 64-token blocks; compared with the CPU oracle
+and, at larger sizes, with the CUDA-core kernels (selected here by asking for
+an fp32 forward output, or fp16 inputs for the backward, which the
+tensor-core path does not take).
 
 Bar (north star): bf16 outputs within 2e-2 abs / 1e-2 rel."""
 
@@ -112,3 +113,93 @@ def test_tc_forward_vs_row_kernel_large(cuda):
     assert device_status() == 0
     np.testing.assert_allclose(o_tc.float().cpu().numpy(), o_rows.cpu().numpy(), rtol=RTOL, atol=ATOL)
     np.testing.assert_allclose(lse_tc.cpu().numpy(), lse_rows.cpu().numpy(), rtol=1e-3, atol=1e-3)
+
+
+def _route_case(cuda, seed, B, T_, H, Hkv, K, LW, dtype=torch.bfloat16):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    D, BS = 128, 64
+    q = (torch.randn(B, T_, H, D, device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, T_, Hkv, D, device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, T_, Hkv, D, device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+    do = torch.randn(B, T_, H, D, device=cuda, generator=g).to(torch.bfloat16)
+    iq = (torch.randn(B, T_, 128, device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+    from srswa import dash_infer
+    router = type("R", (), dict(block_size=BS, local_blocks=LW // BS, local_window=LW,
+                                head_cls=torch.zeros(128, device=cuda), stage0="head_cls"))()
+    pos = torch.arange(T_, device=cuda)[None].repeat(B, 1)
+    nblk = (T_ + BS - 1) // BS
+    topi, bias, valid = dash_infer.route(router, iq.float(), iq, pos, nblk, None,
+                                         dict(idx_scale=11.3, floor=1e-4, sigma=1.0, K=K, topm=16))
+    sel = ops.pack_selection(torch.where(valid, topi, torch.full_like(topi, -1))[:, None], nblk)
+    b = (bias * valid).float().contiguous()
+    return q, k, v, do, sel, b
+
+
+@pytest.mark.parametrize("B,T_,H,Hkv,K,LW,packed,use_bias", [
+    (1, 256, 2, 2, 0, 128, False, False),      # band only
+    (2, 700, 4, 4, 6, 256, False, True),       # T not a multiple of 128, bias
+    (1, 1000, 4, 2, 8, 512, True, False),      # GQA + packed segments
+    (1, 1536, 10, 10, 8, 512, False, True),    # BASELINE head layout
+])
+def test_tc_backward_vs_oracle(cuda, B, T_, H, Hkv, K, LW, packed, use_bias):
+    rng = np.random.default_rng(100 + T_ + K)
+    Kk = max(K, 1)
+    q, k, v, sel, bias, nblk = _inputs(rng, B, T_, H, Hkv, Kk)
+    if K == 0:
+        sel = sel[..., :0]
+        bias = bias[..., :0]
+    do = O.bf16_round(rng.standard_normal((B, T_, H, 128)).astype(np.float32))
+    pos = np.tile(np.arange(T_), (B, 1))
+    if packed:
+        pos[0, 400:] = np.arange(T_ - 400)
+    seg = (np.arange(T_)[None] - pos).astype(np.int64)
+    scale = 1 / math.sqrt(128)
+    sel_p = ops.pack_selection(T(sel, cuda), nblk)
+    qd, kd, vd = (T(x, cuda, torch.bfloat16) for x in (q, k, v))
+    bd = T(bias, cuda) if use_bias else None
+    segd = T(seg, cuda).to(torch.int32) if packed else None
+    o, lse = ops.gather_fwd(qd, kd, vd, sel_p, bd, segd, 64, scale, LW)
+    dq, dk, dv, db = ops.gather_bwd(qd, kd, vd, o, lse, T(do, cuda, torch.bfloat16), sel_p, bd, segd, 64,
+                                    scale, LW)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    rq, rk, rv, rb = O.gather_attention_bwd(q, k, v, do, sel, seg, 64, scale, LW, bias if use_bias else None)
+    np.testing.assert_allclose(dq.float().cpu().numpy(), rq, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(dk.float().cpu().numpy(), rk, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(dv.float().cpu().numpy(), rv, rtol=RTOL, atol=ATOL)
+    if use_bias:
+        # d_bias sums dS over a block's 64 keys and all heads: absolute error
+        # grows with that count, hence the wider absolute bound
+        np.testing.assert_allclose(db.cpu().numpy(), rb, rtol=1e-2, atol=5e-2)
+
+
+def test_tc_backward_vs_cuda_core_large(cuda):
+    """Long-sequence shape: tensor-core backward (bf16) vs the CUDA-core
+    backward run on the same values in fp16 (exact for these magnitudes)."""
+    B, T_, H, Hkv, K, LW = 1, 8192, 10, 10, 8, 512
+    q, k, v, do, sel, b = _route_case(cuda, 5, B, T_, H, Hkv, K, LW)
+    scale = 1 / math.sqrt(128)
+    o, lse = ops.gather_fwd(q, k, v, sel, b, None, 64, scale, LW)
+    dq, dk, dv, db = ops.gather_bwd(q, k, v, o, lse, do, sel, b, None, 64, scale, LW)
+    h = [x.to(torch.float16) for x in (q, k, v, o, do)]
+    dq2, dk2, dv2, db2 = ops.gather_bwd(h[0], h[1], h[2], h[3], lse, h[4], sel, b, None, 64, scale, LW)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    for a, r in ((dq, dq2), (dk, dk2), (dv, dv2)):
+        np.testing.assert_allclose(a.float().cpu().numpy(), r.float().cpu().numpy(), rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(db.cpu().numpy(), db2.cpu().numpy(), rtol=1e-2, atol=5e-2)
+
+
+def test_tc_backward_deterministic(cuda):
+    """Two calls give bit-identical gradients (fixed-order pair lists and
+    partial sums; no floating-point atomics)."""
+    q, k, v, do, sel, b = _route_case(cuda, 7, 2, 3000, 4, 2, 8, 512)
+    scale = 1 / math.sqrt(128)
+    o, lse = ops.gather_fwd(q, k, v, sel, b, None, 64, scale, 512)
+    r1 = ops.gather_bwd(q, k, v, o, lse, do, sel, b, None, 64, scale, 512)
+    r2 = ops.gather_bwd(q, k, v, o, lse, do, sel, b, None, 64, scale, 512)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    for a, c in zip(r1, r2):
+        assert torch.isfinite(a).all()
+        assert torch.equal(a, c)

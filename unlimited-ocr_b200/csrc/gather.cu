@@ -385,6 +385,21 @@ bool tc_eligible(const srswa_gather_desc* g);
 int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const int32_t* sel,
                   const float* bias, const int32_t* seg, void* o, int64_t sob, int64_t sot, int64_t soh, float* lse,
                   void* workspace, size_t workspace_bytes, cudaStream_t st);
+size_t tc_bwd_workspace(const srswa_gather_desc* g, bool with_bias);
+int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const void* o,
+                  int64_t sob, int64_t sot, int64_t soh, const void* dout, const float* lse, const int32_t* sel,
+                  const float* bias, const int32_t* seg, void* dq, void* dk, void* dv, float* d_bias,
+                  void* workspace, size_t workspace_bytes, cudaStream_t st);
+
+// The tensor-core backward takes bf16 / head dim 128 / 64-token blocks with
+// 8-element-aligned strides (o and do included); other shapes use the
+// CUDA-core kernels below.
+static bool tc_bwd_path(const srswa_gather_desc* g, int64_t sob, int64_t sot, int64_t soh) {
+  return tc_eligible(g) && ((sob | sot | soh) & 7) == 0;
+}
+static size_t bwd_need(const srswa_gather_desc* g, int64_t sob, int64_t sot, int64_t soh, bool with_bias) {
+  return tc_bwd_path(g, sob, sot, soh) ? tc_bwd_workspace(g, with_bias) : bwd_layout(g, with_bias).total;
+}
 }  // namespace srswa
 
 extern "C" size_t srswa_gather_fwd_workspace_size(const srswa_gather_desc* g) {
@@ -400,7 +415,7 @@ extern "C" int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const
   if (rc) return rc;
   SRSWA_CHECK_ARG(q && k && v && o && (g->S == 0 || sel), SRSWA_EINVAL);
   SRSWA_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
-                    reinterpret_cast<uintptr_t>(v)) & 15) == 0, SRSWA_EALIGN);
+                    reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15) == 0, SRSWA_EALIGN);
   if (g->B * g->T == 0) return 0;
   // tensor-core path (bf16, D = 128, 64-token blocks); CUDA-core rows otherwise
   if (tc_eligible(g) && o_dtype == SRSWA_BF16 && ((sob | sot | soh) & 7) == 0)
@@ -429,7 +444,7 @@ extern "C" int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const
 
 extern "C" size_t srswa_gather_bwd_workspace_size(const srswa_gather_desc* g) {
   if (check_gather_desc(g)) return 0;
-  return bwd_layout(g, true).total;
+  return bwd_need(g, 8, 8, 8, true);
 }
 
 extern "C" int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v,
@@ -442,6 +457,17 @@ extern "C" int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const
   SRSWA_CHECK_ARG(q && k && v && o && dout && lse && dq && dk && dv && (g->S == 0 || sel), SRSWA_EINVAL);
   SRSWA_CHECK_ARG(!bias || d_bias, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(((sob | sot | soh) & 7) == 0, SRSWA_EALIGN);
+  SRSWA_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+                    reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(dq) |
+                    reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15) == 0,
+                  SRSWA_EALIGN);
+  if (tc_bwd_path(g, sob, sot, soh)) {
+    SRSWA_CHECK_ARG(g->B * g->T < (1ll << 31) && g->HQ < 65536 && g->B * g->HI * g->T * g->S < (1ll << 31),
+                    SRSWA_ETOOLARGE);
+    if (g->B * g->T == 0) return 0;
+    return tc_gather_bwd(g, q, k, v, o, sob, sot, soh, dout, lse, sel, bias, seg, dq, dk, dv, d_bias, workspace,
+                         workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+  }
   const BwdLayout L = bwd_layout(g, bias != nullptr);
   SRSWA_CHECK_ARG(workspace && workspace_bytes >= L.total, SRSWA_EWORKSPACE);
   if (g->B * g->T == 0) return 0;
@@ -489,7 +515,8 @@ extern "C" int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const
 
 // ---------------------------------------------------------------------------
 // Backward without any allocation by anyone: the scratch the backward needs
-// (delta, per-head d_bias partials, selection bitmap) lives in a file-scope
+// (delta, per-head d_bias partials, selection bitmap; on the tensor-core path
+// also the remote dQ / dK / dV partials and pair lists) lives in a file-scope
 // device array instead of a caller workspace.  For callers that cannot call
 // cudaMalloc or an allocator at all: code embedded in a runtime that reserves
 // all device memory up front and forbids allocation afterwards, plugin or FFI
@@ -504,8 +531,8 @@ extern "C" int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const
 // that device; make that first call outside any stream capture.  All calls
 // share the one array, so calls whose GPU work overlaps (different streams,
 // or graph replays running concurrently) race on it and must be serialised by
-// the caller.  The existing backward path clears the parts that must start at
-// zero (the bitmap) on every call; the rest is fully overwritten.
+// the caller.  The backward clears the parts that must start at zero (bitmaps,
+// d_bias partials) on every call; the rest is fully overwritten.
 // ---------------------------------------------------------------------------
 #include <mutex>
 
@@ -542,7 +569,7 @@ extern "C" int srswa_gather_bwd_noalloc(const srswa_gather_desc* g, const void* 
                                         float* d_bias, srswa_stream_t stream) {
   int rc = check_gather_desc(g);
   if (rc) return rc;
-  const size_t need = bwd_layout(g, bias != nullptr).total;
+  const size_t need = srswa::bwd_need(g, sob, sot, soh, bias != nullptr);
   if (need > srswa::kNoAllocScratchBytes) return SRSWA_ETOOLARGE;
   void* scratch = nullptr;
   rc = srswa::bwd_scratch_address(&scratch);

@@ -587,6 +587,670 @@ __global__ void __launch_bounds__(kTcThreads) remote_fwd_kernel(const TcArgs a) 
   if (warp == 0) tmem_dealloc(tmem, kRemoteTmemCols);
 }
 
+// ============================================================================
+// backward (deterministic: every gradient element has one writer; remote and
+// band contributions meet through fixed-order partial sums)
+// ============================================================================
+struct TcBwdArgs {
+  TcArgs f;
+  const __nv_bfloat16* dout;  // strides sob/sot/soh of TcArgs
+  const float* lse;           // [B, T, HQ] natural log
+  float* delta;               // [B, T, HQ]
+  __nv_bfloat16* dq;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  __nv_bfloat16* dq_part;     // [B, T, S, HQ, D] (scaled)
+  float* dbias_part;          // [B, T, S, HQ]
+  float* dkv_part;            // [B, HQ, nblk, 2, 64, 128] (dK scaled, dV)
+  const int32_t* count;       // [B*HI*nblk]
+  const int32_t* offs;        // [B*HI*nblk]
+  float* d_bias;              // [B, T, S]
+  float scale;
+};
+
+constexpr uint32_t kTile128 = 128 * 128 * 2;  // [128 rows x 128 bf16] = two 16 KB halves
+
+// D = A^T B with A, B both stored rows = K (MN-major): M = 128 (A's 128
+// features, halves a_lbo apart), N = 64 (B's 64 columns), K = 128 rows.
+__device__ __forceinline__ void issue_tn(uint32_t tmem_d, uint32_t a_s, uint32_t a_lbo, uint32_t b_s,
+                                         bool accumulate) {
+  constexpr uint32_t id = idesc_bf16(128, 64, 1, 1);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint64_t ad = sw128_desc(a_s + ks * 2048u, a_lbo, 1024);
+    const uint64_t bd = sw128_desc(b_s + ks * 2048u, 8192, 1024);
+    mma_bf16_ss(tmem_d, ad, bd, id, (accumulate || ks > 0) ? 1u : 0u);
+  }
+}
+// D = A B^T, A and B K-major [128 rows x 128]: M = N = K = 128
+__device__ __forceinline__ void issue_nt128(uint32_t tmem_d, uint32_t a_s, uint32_t b_s) {
+  constexpr uint32_t id = idesc_bf16(128, 128, 0);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint32_t off = (ks >> 2) * (kTile128 / 2) + (ks & 3) * 32u;
+    mma_bf16_ss(tmem_d, sw128_desc(a_s + off, 16, 1024), sw128_desc(b_s + off, 16, 1024), id, ks > 0 ? 1u : 0u);
+  }
+}
+// D (+)= A B, A K-major [128 x 128 (K)], B MN-major [128 (K) rows x 128 (N)]
+__device__ __forceinline__ void issue_nn128(uint32_t tmem_d, uint32_t a_s, uint32_t b_s, bool accumulate) {
+  constexpr uint32_t id = idesc_bf16(128, 128, 1);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint32_t aoff = (ks >> 2) * (kTile128 / 2) + (ks & 3) * 32u;
+    mma_bf16_ss(tmem_d, sw128_desc(a_s + aoff, 16, 1024), sw128_desc(b_s + ks * 2048u, kTile128 / 2, 1024), id,
+                (accumulate || ks > 0) ? 1u : 0u);
+  }
+}
+
+__device__ __forceinline__ void store_row128(uint32_t base, int r, const float* v) {
+  store_p_row(base, r, 0, v);
+  store_p_row(base, r, 4, v + 32);
+  store_p_row(base + kTile128 / 2, r, 0, v + 64);
+  store_p_row(base + kTile128 / 2, r, 4, v + 96);
+}
+
+__global__ void tc_delta_kernel(const TcBwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const TcArgs& f = a.f;
+  if (item >= f.B * f.T * f.HQ) return;
+  const int64_t h = item % f.HQ, bt = item / f.HQ, t = bt % f.T, b = bt / f.T;
+  const int64_t off = b * f.sob + t * f.sot + h * f.soh + lane * 4;
+  const uint2 uo = *reinterpret_cast<const uint2*>(f.o + off);
+  const uint2 ug = *reinterpret_cast<const uint2*>(a.dout + off);
+  float acc = bf16_lo(uo.x) * bf16_lo(ug.x) + bf16_hi(uo.x) * bf16_hi(ug.x) + bf16_lo(uo.y) * bf16_lo(ug.y) +
+              bf16_hi(uo.y) * bf16_hi(ug.y);
+  acc = warp_sum(acc);
+  if (lane == 0) a.delta[item] = acc;
+}
+
+// ---- backward pair lists, ordered by query inside each (b, hi, block) list,
+// so that the remote dK / dV accumulation order is fixed from call to call.
+// A query selects a block at most once (later duplicate slots are dropped),
+// so one bit per (list, query) is the whole list.
+__global__ void bwd_pairs_bitmap_kernel(const TcArgs a, uint32_t* bitmap, int64_t T32) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, hi, t)
+  if (i >= a.B * a.HI * a.T) return;
+  const int64_t t = i % a.T, bh = i / a.T, b = bh / a.HI;
+  const int32_t* srow = a.sel + i * a.S;
+  for (int64_t s = 0; s < a.S; ++s) {
+    const int64_t blk = srow[s];
+    if (blk < 0 || blk >= a.nblk) continue;
+    int64_t lo, hi;
+    remote_range(a, b, t, blk, lo, hi);
+    if (lo >= hi) continue;
+    atomicOr(bitmap + (bh * a.nblk + blk) * T32 + (t >> 5), 1u << (t & 31));
+  }
+}
+
+// one warp per list: its length
+__global__ void bwd_pairs_count_kernel(const TcArgs a, const uint32_t* bitmap, int64_t T32, int32_t* count) {
+  const int lane = threadIdx.x & 31;
+  const int64_t seg = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (seg >= a.B * a.HI * a.nblk) return;
+  const uint32_t* w = bitmap + seg * T32;
+  int n = 0;
+  for (int64_t i = lane; i < T32; i += 32) n += __popc(w[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+  if (lane == 0) count[seg] = n;
+}
+
+// one warp per list: emit (t * S + first slot holding the block) in t order
+__global__ void bwd_pairs_fill_kernel(const TcArgs a, const uint32_t* bitmap, int64_t T32, const int32_t* offs,
+                                      int32_t* pairs) {
+  const int lane = threadIdx.x & 31;
+  const int64_t seg = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (seg >= a.B * a.HI * a.nblk) return;
+  const int64_t blk = seg % a.nblk, bh = seg / a.nblk;
+  const uint32_t* w = bitmap + seg * T32;
+  int64_t pos = offs[seg];
+  for (int64_t w0 = 0; w0 < T32; w0 += 32) {
+    uint32_t word = (w0 + lane < T32) ? w[w0 + lane] : 0u;
+    const int n = __popc(word);
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int64_t p = pos + incl - n;
+    while (word) {
+      const int bit = __ffs(word) - 1;
+      word &= word - 1;
+      const int64_t t = (w0 + lane) * 32 + bit;
+      const int32_t* srow = a.sel + (bh * a.T + t) * a.S;
+      int64_t s = 0;
+      while (s < a.S && srow[s] != blk) ++s;
+      pairs[p++] = static_cast<int32_t>(t * a.S + s);
+    }
+    pos += __shfl_sync(0xffffffffu, incl, 31);
+  }
+}
+
+// ---- remote pairs: one item = (batch, index head, block, query head) ------
+constexpr uint32_t kRBSmem = 2 * kKVBytes + 2 * kTile128 + 2 * kPBytes + 1024;
+
+__global__ void __launch_bounds__(kTcThreads) bwd_remote_kernel(const TcBwdArgs a) {
+  const TcArgs& f = a.f;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int ok_s;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t k_s = sbase, v_s = k_s + kKVBytes;
+  const uint32_t q_s = v_s + kKVBytes, do_s = q_s + kTile128;
+  const uint32_t p_s = do_s + kTile128, ds_s = p_s + kPBytes;
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    ok_s = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t tm_s = tmem, tm_dp = tmem + 64, tm_dq = tmem, tm_dvt = tmem + 128, tm_dkt = tmem + 192;
+  const int64_t hpi = f.HQ / f.HI, G = f.HQ / f.Hkv;
+  const int64_t nitems = f.B * f.HI * f.nblk * hpi;
+  uint32_t phase = 0;
+  bool failed = false;
+  for (int64_t item = blockIdx.x; item < nitems && !failed; item += gridDim.x) {
+    const int64_t bhc = item / hpi;
+    const int64_t cnt = a.count[bhc];
+    if (cnt == 0) continue;
+    const int64_t first = a.offs[bhc];
+    const int64_t bh = bhc / f.nblk, blk = bhc % f.nblk, b = bh / f.HI, hi = bh % f.HI;
+    const int64_t h = hi * hpi + item % hpi, hk = h / G;
+    auto k_row = [&](int r) -> const __nv_bfloat16* {
+      const int64_t kk = blk * kBlk + r;
+      return kk < f.T ? f.k + b * f.skb + kk * f.skt + hk * f.skh : nullptr;
+    };
+    auto v_row = [&](int r) -> const __nv_bfloat16* {
+      const int64_t kk = blk * kBlk + r;
+      return kk < f.T ? f.v + b * f.svb + kk * f.svt + hk * f.svh : nullptr;
+    };
+    load_operand<kBlk>(k_s, kKVHalf, k_row, tid, f.k);
+    load_operand<kBlk>(v_s, kKVHalf, v_row, tid, f.v);
+    const int64_t ntile = (cnt + kTileM - 1) / kTileM;
+    for (int64_t tl = 0; tl < ntile; ++tl) {
+      const int64_t base = first + tl * kTileM, n_here = (cnt - tl * kTileM) < kTileM ? (cnt - tl * kTileM) : int64_t(kTileM);
+      int64_t t = -1, slot = 0;
+      if (tid < n_here) {
+        const int32_t pk = f.pairs[base + tid];
+        t = pk / f.S;
+        slot = pk % f.S;
+      }
+      auto q_row = [&](int r) -> const __nv_bfloat16* {
+        if (r >= n_here) return nullptr;
+        const int64_t tt = f.pairs[base + r] / f.S;
+        return f.q + b * f.sqb + tt * f.sqt + h * f.sqh;
+      };
+      auto g_row = [&](int r) -> const __nv_bfloat16* {
+        if (r >= n_here) return nullptr;
+        const int64_t tt = f.pairs[base + r] / f.S;
+        return a.dout + b * f.sob + tt * f.sot + h * f.soh;
+      };
+      load_operand<kTileM>(q_s, kTile128 / 2, q_row, tid, f.q);
+      load_operand<kTileM>(do_s, kTile128 / 2, g_row, tid, a.dout);
+      cp_async_commit();
+      cp_async_wait<0>();
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        issue_qk(tm_s, q_s, k_s);
+        issue_qk(tm_dp, do_s, v_s);
+        mma_commit(&bar);
+        ok_s = mbar_wait(&bar, phase, 301) ? 1 : 0;
+      }
+      phase ^= 1;
+      __syncthreads();
+      if (!ok_s) { failed = true; break; }
+      tc_fence_after();
+      float sv[64], dp[64];
+      {
+        float x0[32], x1[32];
+        tmem_ld32(tm_s + lane_off, x0);
+        tmem_ld32(tm_s + lane_off + 32, x1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
+        tmem_ld32(tm_dp + lane_off, x0);
+        tmem_ld32(tm_dp + lane_off + 32, x1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
+      }
+      float lse2 = 0.f, dlt = 0.f, bias2 = 0.f;
+      int64_t lo = 0, hi2 = 0;
+      if (t >= 0) {
+        lse2 = a.lse[(b * f.T + t) * f.HQ + h] * kLog2e;
+        dlt = a.delta[(b * f.T + t) * f.HQ + h];
+        if (f.bias) bias2 = f.bias[(b * f.T + t) * f.S + slot] * kLog2e;
+        remote_range(f, b, t, blk, lo, hi2);
+      }
+      float dsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const int64_t key = blk * kBlk + i;
+        const bool valid = t >= 0 && key >= lo && key < hi2 && lse2 != -INFINITY;
+        const float p = valid ? exp2f(sv[i] * f.scale_log2 + bias2 - lse2) : 0.f;
+        const float ds = p * (dp[i] - dlt);
+        sv[i] = p;
+        dp[i] = ds;
+        dsum += ds;
+      }
+      if (t >= 0 && a.dbias_part) a.dbias_part[((b * f.T + t) * f.S + slot) * f.HQ + h] = dsum;
+      store_p_row(p_s, tid, 0, sv);
+      store_p_row(p_s, tid, 4, sv + 32);
+      store_p_row(ds_s, tid, 0, dp);
+      store_p_row(ds_s, tid, 4, dp + 32);
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        issue_pv(tm_dq, ds_s, k_s, false);                 // dQ_g = dS K
+        issue_tn(tm_dvt, do_s, kTile128 / 2, p_s, tl > 0);  // dV^T += dO_g^T P
+        issue_tn(tm_dkt, q_s, kTile128 / 2, ds_s, tl > 0);  // dK^T += Q_g^T dS
+        mma_commit(&bar);
+        ok_s = mbar_wait(&bar, phase, 302) ? 1 : 0;
+      }
+      phase ^= 1;
+      __syncthreads();
+      if (!ok_s) { failed = true; break; }
+      tc_fence_after();
+      const int64_t prow = ((b * f.T + (t < 0 ? 0 : t)) * f.S + slot) * f.HQ + h;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(tm_dq + lane_off + 32 * c, ov);
+        tmem_wait_ld();
+        if (t >= 0) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            float tmp[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * a.scale;
+            store8(a.dq_part + prow * kD + 32 * c, 8 * q4, SRSWA_BF16, tmp);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncthreads();
+    }
+    if (failed) break;
+    // this block's remote dK / dV for query head h: thread = feature d
+    tc_fence_after();
+    float* dst = a.dkv_part + ((b * f.HQ + h) * f.nblk + blk) * (2 * 64 * 128);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float kv[32], vv[32];
+      tmem_ld32(tm_dkt + lane_off + 32 * half, kv);
+      tmem_ld32(tm_dvt + lane_off + 32 * half, vv);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        dst[(32 * half + i) * 128 + tid] = kv[i] * a.scale;
+        dst[8192 + (32 * half + i) * 128 + tid] = vv[i];
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ---- band dK / dV: one CTA per (batch, kv head, 128-key tile) -------------
+constexpr uint32_t kBDSmem = 6 * kTile128 + 1024;
+
+__global__ void __launch_bounds__(kTcThreads) bwd_band_dkdv_kernel(const TcBwdArgs a) {
+  const TcArgs& f = a.f;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int ok_s;
+  __shared__ float lse2_s[128], dl_s[128];
+  __shared__ int64_t ls_s[128];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t tile = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int64_t k0 = tile * 128, G = f.HQ / f.Hkv;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t kt_s = sbase, vt_s = kt_s + kTile128, qt_s = vt_s + kTile128, dot_s = qt_s + kTile128;
+  const uint32_t pt_s = dot_s + kTile128, dst_s = pt_s + kTile128;
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    ok_s = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t tm_st = tmem, tm_dpt = tmem + 128, tm_dk = tmem + 256, tm_dv = tmem + 384;
+  auto kt_row = [&](int r) -> const __nv_bfloat16* {
+    const int64_t kk = k0 + r;
+    return kk < f.T ? f.k + b * f.skb + kk * f.skt + hk * f.skh : nullptr;
+  };
+  auto vt_row = [&](int r) -> const __nv_bfloat16* {
+    const int64_t kk = k0 + r;
+    return kk < f.T ? f.v + b * f.svb + kk * f.svt + hk * f.svh : nullptr;
+  };
+  load_operand<kTileM>(kt_s, kTile128 / 2, kt_row, tid, f.k);
+  load_operand<kTileM>(vt_s, kTile128 / 2, vt_row, tid, f.v);
+  const int64_t key = k0 + tid;
+  const int64_t q_hi = min(f.T, k0 + 127 + f.LW);  // exclusive end of queries seeing this tile locally
+  const int64_t nqt = (q_hi - k0 + 127) / 128;
+  uint32_t phase = 0;
+  bool failed = false, any = false;
+  for (int64_t gq = 0; gq < G && !failed; ++gq) {
+    const int64_t h = hk * G + gq;
+    for (int64_t qt = 0; qt < nqt; ++qt) {
+      const int64_t q0 = k0 + qt * 128;
+      auto q_row = [&](int r) -> const __nv_bfloat16* {
+        const int64_t tt = q0 + r;
+        return tt < f.T ? f.q + b * f.sqb + tt * f.sqt + h * f.sqh : nullptr;
+      };
+      auto g_row = [&](int r) -> const __nv_bfloat16* {
+        const int64_t tt = q0 + r;
+        return tt < f.T ? a.dout + b * f.sob + tt * f.sot + h * f.soh : nullptr;
+      };
+      load_operand<kTileM>(qt_s, kTile128 / 2, q_row, tid, f.q);
+      load_operand<kTileM>(dot_s, kTile128 / 2, g_row, tid, a.dout);
+      cp_async_commit();
+      {
+        const int64_t tq = q0 + tid;
+        const bool ok = tq < f.T;
+        lse2_s[tid] = ok ? a.lse[(b * f.T + tq) * f.HQ + h] * kLog2e : INFINITY;
+        dl_s[tid] = ok ? a.delta[(b * f.T + tq) * f.HQ + h] : 0.f;
+        ls_s[tid] = ok ? win_start(f, b, tq) : (int64_t(1) << 62);
+      }
+      cp_async_wait<0>();
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        issue_nt128(tm_st, kt_s, qt_s);   // S^T = K Q^T
+        issue_nt128(tm_dpt, vt_s, dot_s); // dP^T = V dO^T
+        mma_commit(&bar);
+        ok_s = mbar_wait(&bar, phase, 311) ? 1 : 0;
+      }
+      phase ^= 1;
+      __syncthreads();
+      if (!ok_s) { failed = true; break; }
+      tc_fence_after();
+      // row = key; columns = the tile's 128 queries, 32 at a time
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float sv[32], dp[32];
+        tmem_ld32(tm_st + lane_off + 32 * c, sv);
+        tmem_ld32(tm_dpt + lane_off + 32 * c, dp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int qi = 32 * c + i;
+          const int64_t tq = q0 + qi;
+          const bool local = key < f.T && key <= tq && key >= ls_s[qi];
+          const float p = local ? exp2f(sv[i] * f.scale_log2 - lse2_s[qi]) : 0.f;
+          sv[i] = p;
+          dp[i] = p * (dp[i] - dl_s[qi]);
+        }
+        const uint32_t half = (c >> 1) * (kTile128 / 2);
+        store_p_row(pt_s + half, tid, (c & 1) * 4, sv);
+        store_p_row(dst_s + half, tid, (c & 1) * 4, dp);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        issue_nn128(tm_dv, pt_s, dot_s, any);   // dV += P^T dO
+        issue_nn128(tm_dk, dst_s, qt_s, any);   // dK += dS^T Q
+        mma_commit(&bar);
+        ok_s = mbar_wait(&bar, phase, 312) ? 1 : 0;
+      }
+      phase ^= 1;
+      any = true;
+      __syncthreads();
+      if (!ok_s) { failed = true; break; }
+    }
+  }
+  if (!failed) {
+    tc_fence_after();
+    const int64_t blk = key / kBlk, hi = (hk * f.HI) / f.Hkv;
+    const int64_t bhc = (b * f.HI + hi) * f.nblk + blk;
+    const bool has_remote = key < f.T && a.count && a.count[bhc] > 0;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float kv[32], vv[32];
+      if (any) {
+        tmem_ld32(tm_dk + lane_off + 32 * c, kv);
+        tmem_ld32(tm_dv + lane_off + 32 * c, vv);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) kv[i] = vv[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) kv[i] *= a.scale;
+      if (has_remote) {
+        for (int64_t gq = 0; gq < G; ++gq) {
+          const float* src = a.dkv_part + ((b * f.HQ + hk * G + gq) * f.nblk + blk) * (2 * 64 * 128) +
+                             (key % kBlk) * 128 + 32 * c;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            kv[i] += src[i];
+            vv[i] += src[8192 + i];
+          }
+        }
+      }
+      if (key < f.T) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          store8(a.dk + b * f.skb + key * f.skt + hk * f.skh + 32 * c, 8 * q4, SRSWA_BF16, kv + 8 * q4);
+          store8(a.dv + b * f.svb + key * f.svt + hk * f.svh + 32 * c, 8 * q4, SRSWA_BF16, vv + 8 * q4);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ---- band dQ (+ remote dQ partials): one CTA per (batch, head, 128 queries)
+constexpr uint32_t kBQSmem = 2 * kTile128 + 2 * 2 * kKVBytes + 1024;
+
+__global__ void __launch_bounds__(kTcThreads) bwd_band_dq_kernel(const TcBwdArgs a) {
+  const TcArgs& f = a.f;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t bar_s, bar_o;
+  __shared__ uint32_t tmem_base;
+  __shared__ int ok_s;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int64_t hk = h / (f.HQ / f.Hkv);
+  const int64_t t0 = tile * kTileM;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t q_s = sbase, do_s = q_s + kTile128, kv_s = do_s + kTile128;
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bar_s, 1);
+    mbar_init(&bar_o, 1);
+    fence_mbar_init();
+    ok_s = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t tm_s = tmem, tm_dp = tmem + 64, tm_dq = tmem + 128;
+  const int64_t t = t0 + tid;
+  const bool row_ok = t < f.T;
+  const int64_t ls = row_ok ? win_start(f, b, t) : 0;
+  const float lse2 = row_ok ? a.lse[(b * f.T + t) * f.HQ + h] * kLog2e : INFINITY;
+  const float dlt = row_ok ? a.delta[(b * f.T + t) * f.HQ + h] : 0.f;
+  const int64_t tlast = min(f.T, t0 + kTileM) - 1;
+  int64_t key_lo = t0 - f.LW + 1;
+  if (key_lo < 0) key_lo = 0;
+  const int64_t blo = key_lo / kBlk, bhi = tlast / kBlk;
+  auto q_row = [&](int r) -> const __nv_bfloat16* {
+    const int64_t tt = t0 + r;
+    return tt < f.T ? f.q + b * f.sqb + tt * f.sqt + h * f.sqh : nullptr;
+  };
+  auto g_row = [&](int r) -> const __nv_bfloat16* {
+    const int64_t tt = t0 + r;
+    return tt < f.T ? a.dout + b * f.sob + tt * f.sot + h * f.soh : nullptr;
+  };
+  auto kv_rows = [&](int64_t blk, const __nv_bfloat16* base, int64_t sb, int64_t st, int64_t sh) {
+    return [=](int r) -> const __nv_bfloat16* {
+      const int64_t kk = blk * kBlk + r;
+      return kk < f.T ? base + b * sb + kk * st + hk * sh : nullptr;
+    };
+  };
+  load_operand<kTileM>(q_s, kTile128 / 2, q_row, tid, f.q);
+  load_operand<kTileM>(do_s, kTile128 / 2, g_row, tid, a.dout);
+  load_operand<kBlk>(kv_s, kKVHalf, kv_rows(blo, f.k, f.skb, f.skt, f.skh), tid, f.k);
+  load_operand<kBlk>(kv_s + kKVBytes, kKVHalf, kv_rows(blo, f.v, f.svb, f.svt, f.svh), tid, f.v);
+  cp_async_commit();
+  bool aborted = false;
+  for (int64_t j = blo; j <= bhi; ++j) {
+    const int jj = static_cast<int>(j - blo);
+    const int st = jj & 1;
+    cp_async_wait<0>();
+    fence_async_smem();
+    __syncthreads();
+    const uint32_t k_cur = kv_s + st * 2 * kKVBytes, v_cur = k_cur + kKVBytes;
+    if (tid == 0) {
+      tc_fence_after();
+      issue_qk(tm_s, q_s, k_cur);
+      issue_qk(tm_dp, do_s, v_cur);
+      mma_commit(&bar_s);
+      ok_s = mbar_wait(&bar_s, jj & 1, 321) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!ok_s) { aborted = true; break; }
+    if (j + 1 <= bhi) {
+      const uint32_t nx = kv_s + (st ^ 1) * 2 * kKVBytes;
+      load_operand<kBlk>(nx, kKVHalf, kv_rows(j + 1, f.k, f.skb, f.skt, f.skh), tid, f.k);
+      load_operand<kBlk>(nx + kKVBytes, kKVHalf, kv_rows(j + 1, f.v, f.svb, f.svt, f.svh), tid, f.v);
+    }
+    cp_async_commit();
+    tc_fence_after();
+    float sv[64], dp[64];
+    {
+      float x0[32], x1[32];
+      tmem_ld32(tm_s + lane_off, x0);
+      tmem_ld32(tm_s + lane_off + 32, x1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
+      tmem_ld32(tm_dp + lane_off, x0);
+      tmem_ld32(tm_dp + lane_off + 32, x1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
+    }
+    const int64_t k0 = j * kBlk;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const int64_t kk = k0 + i;
+      const bool valid = row_ok && kk >= ls && kk <= t;
+      const float p = valid ? exp2f(sv[i] * f.scale_log2 - lse2) : 0.f;
+      dp[i] = p * (dp[i] - dlt);
+    }
+    store_p_row(v_cur, tid, 0, dp);  // dS over the dead V operand of this stage
+    store_p_row(v_cur, tid, 4, dp + 32);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      issue_pv(tm_dq, v_cur, k_cur, jj > 0);  // dQ += dS K (K MN-major)
+      mma_commit(&bar_o);
+    }
+  }
+  const int nblocks = static_cast<int>(bhi - blo + 1);
+  if (tid == 0) ok_s = mbar_wait(&bar_o, (nblocks - 1) & 1, 322) ? 1 : 0;
+  __syncthreads();
+  cp_async_wait<0>();
+  if (!aborted && ok_s) {
+    tc_fence_after();
+    const int64_t hi = (hk * f.HI) / f.Hkv;
+    int64_t slot_rows[64];
+    int nsl = 0;
+    if (row_ok && f.S > 0) {
+      const int32_t* srow = f.sel + ((b * f.HI + hi) * f.T + t) * f.S;
+      for (int64_t s2 = 0; s2 < f.S && s2 < 64; ++s2) {
+        const int64_t blk = srow[s2];
+        if (blk < 0 || blk >= f.nblk) continue;
+        int64_t lo, hi2;
+        remote_range(f, b, t, blk, lo, hi2);
+        if (lo >= hi2) continue;
+        bool dup = false;
+        for (int64_t u = 0; u < s2; ++u) dup |= srow[u] == blk;
+        if (dup) continue;
+        slot_rows[nsl++] = ((b * f.T + t) * f.S + s2) * f.HQ + h;
+      }
+    }
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float ov[32];
+      tmem_ld32(tm_dq + lane_off + 32 * c, ov);
+      tmem_wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ov[i] *= a.scale;
+        for (int u = 0; u < nsl; ++u) {
+          const uint4* src = reinterpret_cast<const uint4*>(a.dq_part + slot_rows[u] * kD + 32 * c);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const uint4 w = src[q4];
+            ov[8 * q4 + 0] += bf16_lo(w.x); ov[8 * q4 + 1] += bf16_hi(w.x);
+            ov[8 * q4 + 2] += bf16_lo(w.y); ov[8 * q4 + 3] += bf16_hi(w.y);
+            ov[8 * q4 + 4] += bf16_lo(w.z); ov[8 * q4 + 5] += bf16_hi(w.z);
+            ov[8 * q4 + 6] += bf16_lo(w.w); ov[8 * q4 + 7] += bf16_hi(w.w);
+          }
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+          store8(a.dq + b * f.sqb + t * f.sqt + h * f.sqh + 32 * c, 8 * q4, SRSWA_BF16, ov + 8 * q4);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// d_bias[b,t,s] = sum over query heads of the per-head partials (fixed order)
+__global__ void tc_dbias_reduce_kernel(const TcBwdArgs a) {
+  const TcArgs& f = a.f;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= f.B * f.T * f.S) return;
+  float acc = 0.f;
+  for (int64_t h = 0; h < f.HQ; ++h) acc += a.dbias_part[i * f.HQ + h];
+  a.d_bias[i] = acc;
+}
+
 // ---------------------------------------------------------------------------
 struct TcLayout {
   size_t part_o, part_lse, count, offs, cursor, tiles, ntiles, pairs, total;
@@ -685,6 +1349,133 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   return srswa_last_launch_status();
 }
 
+
+// ---------------------------------------------------------------------------
+struct TcBwdLayout {
+  size_t delta, dq_part, dbias_part, dkv_part, bitmap, count, offs, cursor, tiles, ntiles, pairs, total;
+  int64_t max_tiles, T32;
+};
+
+TcBwdLayout tc_bwd_layout(const srswa_gather_desc* g, bool with_bias) {
+  TcBwdLayout L;
+  const int64_t nblk = (g->T + kBlk - 1) / kBlk;
+  const int64_t nbh = g->B * g->HI * nblk;
+  const int64_t npairs = g->B * g->HI * g->T * g->S;
+  L.max_tiles = npairs / kTileM + nbh + 1;
+  L.T32 = (g->T + 31) / 32;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += al256(bytes);
+    return at;
+  };
+  L.delta = take(static_cast<size_t>(g->B * g->T * g->HQ) * 4);
+  const bool remote = g->S > 0;
+  L.dq_part = take(remote ? static_cast<size_t>(g->B * g->T * g->S * g->HQ * kD) * 2 : 0);
+  L.dbias_part = take(remote && with_bias ? static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4 : 0);
+  L.dkv_part = take(remote ? static_cast<size_t>(g->B * g->HQ * nblk) * 2 * kBlk * kD * 4 : 0);
+  L.bitmap = take(remote ? static_cast<size_t>(nbh * L.T32) * 4 : 0);
+  L.count = take(static_cast<size_t>(nbh) * 4);
+  L.offs = take(static_cast<size_t>(nbh) * 4);
+  L.cursor = take(static_cast<size_t>(nbh) * 4);
+  L.tiles = take(remote ? static_cast<size_t>(L.max_tiles) * 16 : 0);
+  L.ntiles = take(4);
+  L.pairs = take(static_cast<size_t>(npairs) * 4);
+  L.total = off;
+  return L;
+}
+
+size_t tc_bwd_workspace(const srswa_gather_desc* g, bool with_bias) { return tc_bwd_layout(g, with_bias).total; }
+
+int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const void* o,
+                  int64_t sob, int64_t sot, int64_t soh, const void* dout, const float* lse, const int32_t* sel,
+                  const float* bias, const int32_t* seg, void* dq, void* dk, void* dv, float* d_bias,
+                  void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const TcBwdLayout L = tc_bwd_layout(g, bias != nullptr);
+  if (!workspace || workspace_bytes < L.total) return SRSWA_EWORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  TcBwdArgs a = {};
+  TcArgs& f = a.f;
+  f.q = static_cast<const __nv_bfloat16*>(q);
+  f.k = static_cast<const __nv_bfloat16*>(k);
+  f.v = static_cast<const __nv_bfloat16*>(v);
+  f.sqb = g->sqb; f.sqt = g->sqt; f.sqh = g->sqh; f.skb = g->skb; f.skt = g->skt; f.skh = g->skh;
+  f.svb = g->svb; f.svt = g->svt; f.svh = g->svh;
+  f.o = const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(o));
+  f.sob = sob; f.sot = sot; f.soh = soh;
+  f.sel = sel; f.bias = bias; f.seg = seg;
+  f.pairs = reinterpret_cast<int32_t*>(ws + L.pairs);
+  f.tiles = reinterpret_cast<int4*>(ws + L.tiles);
+  f.ntiles = reinterpret_cast<int32_t*>(ws + L.ntiles);
+  f.B = g->B; f.T = g->T; f.HQ = g->HQ; f.Hkv = g->Hkv; f.HI = g->HI; f.S = g->S;
+  f.LW = g->local_window > 0 ? g->local_window : kBlk;
+  f.nblk = (g->T + kBlk - 1) / kBlk;
+  f.scale_log2 = g->scale * kLog2e;
+  a.dout = static_cast<const __nv_bfloat16*>(dout);
+  a.lse = lse;
+  a.delta = reinterpret_cast<float*>(ws + L.delta);
+  a.dq = static_cast<__nv_bfloat16*>(dq);
+  a.dk = static_cast<__nv_bfloat16*>(dk);
+  a.dv = static_cast<__nv_bfloat16*>(dv);
+  a.d_bias = d_bias;
+  a.scale = g->scale;
+  const bool remote = g->S > 0;
+  a.dq_part = remote ? reinterpret_cast<__nv_bfloat16*>(ws + L.dq_part) : nullptr;
+  a.dbias_part = remote && bias ? reinterpret_cast<float*>(ws + L.dbias_part) : nullptr;
+  a.dkv_part = remote ? reinterpret_cast<float*>(ws + L.dkv_part) : nullptr;
+  int32_t* count = reinterpret_cast<int32_t*>(ws + L.count);
+  int32_t* offs = reinterpret_cast<int32_t*>(ws + L.offs);
+  a.count = remote ? count : nullptr;
+  a.offs = offs;
+
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(bwd_remote_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRBSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(bwd_band_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBDSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(bwd_band_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBQSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_done = true;
+  }
+  const int64_t nrows_h = g->B * g->T * g->HQ;
+  tc_delta_kernel<<<static_cast<unsigned>((nrows_h + 7) / 8), 256, 0, st>>>(a);
+  SRSWA_CUDA_TRY(cudaGetLastError());
+  if (remote) {
+    const int64_t nbh = f.B * f.HI * f.nblk;
+    uint32_t* bitmap = reinterpret_cast<uint32_t*>(ws + L.bitmap);
+    SRSWA_CUDA_TRY(cudaMemsetAsync(bitmap, 0, static_cast<size_t>(nbh * L.T32) * 4, st));
+    const int64_t rows = f.B * f.HI * f.T;
+    bwd_pairs_bitmap_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(f, bitmap, L.T32);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    bwd_pairs_count_kernel<<<static_cast<unsigned>((nbh + 7) / 8), 256, 0, st>>>(f, bitmap, L.T32, count);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    pairs_scan_kernel<<<1, 1024, 0, st>>>(f, count, offs, reinterpret_cast<int32_t*>(ws + L.cursor),
+                                          const_cast<int4*>(f.tiles), const_cast<int32_t*>(f.ntiles));
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    bwd_pairs_fill_kernel<<<static_cast<unsigned>((nbh + 7) / 8), 256, 0, st>>>(f, bitmap, L.T32, offs,
+                                                                              const_cast<int32_t*>(f.pairs));
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    if (a.dbias_part)
+      SRSWA_CUDA_TRY(cudaMemsetAsync(a.dbias_part, 0, static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4, st));
+    bwd_remote_kernel<<<148, kTcThreads, kRBSmem, st>>>(a);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+  }
+  const unsigned ntile = static_cast<unsigned>((g->T + kTileM - 1) / kTileM);
+  bwd_band_dkdv_kernel<<<dim3(ntile, static_cast<unsigned>(g->Hkv), static_cast<unsigned>(g->B)), kTcThreads,
+                         kBDSmem, st>>>(a);
+  SRSWA_CUDA_TRY(cudaGetLastError());
+  bwd_band_dq_kernel<<<dim3(ntile, static_cast<unsigned>(g->HQ), static_cast<unsigned>(g->B)), kTcThreads,
+                       kBQSmem, st>>>(a);
+  SRSWA_CUDA_TRY(cudaGetLastError());
+  if (bias) {
+    if (remote) {
+      const int64_t n = g->B * g->T * g->S;
+      tc_dbias_reduce_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(a);
+    }
+  }
+  return srswa_last_launch_status();
+}
 }  // namespace srswa
 
 extern "C" int srswa_device_status(int* out) {

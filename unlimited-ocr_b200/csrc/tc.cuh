@@ -145,10 +145,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
 
 // Instruction descriptor of tcgen05.mma kind::f16 with bf16 A/B, fp32 D.
 //   bits 4-5 D format (1 = f32), 7-9 A format (1 = bf16), 10-12 B format,
-//   15 A major (0 = K), 16 B major (1 = MN), 17-22 N >> 3, 24-28 M >> 4
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(b_mn_major) << 16) |
-         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+//   15 A major (0 = K, 1 = MN), 16 B major (0 = K, 1 = MN), 17-22 N >> 3,
+//   24-28 M >> 4
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn_major, int a_mn_major = 0) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
+         (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // D[tmem] (+)= A[smem] x B[smem]; issued by one thread.
