@@ -56,9 +56,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx"],
                     help="decode = cfg3 (default, the headline); prefill = cfg2; train = cfg4 fwd+bwd; "
-                         "route = the cfg3 router alone (k_bar cache + block table, no KV; for profiling)")
+                         "route = the cfg3 router alone (k_bar cache + block table, no KV; for profiling); "
+                         "longctx = cfg5 attention share (12 layers, one 1M-token sequence, split-KV)")
+    ap.add_argument("--layers", type=int, default=12, help="longctx: decoder layers")
     ap.add_argument("--batch", type=int, default=0, help="prefill/train batch override (smaller cases)")
     ap.add_argument("--seq", type=int, default=0, help="prefill/train sequence override")
     return ap.parse_args()
@@ -449,10 +451,124 @@ def main_route(args):
     return 0
 
 
+def main_longctx(args):
+    """cfg5 attention share: one decode step of a 1M-token sequence through
+    the SR-SWA attention of 12 layers, split-KV over the ranks (rank g owns a
+    contiguous block range of every layer's K/V, index keys and k_bar; the
+    last rank also owns the window).  Per layer: shard router keys ->
+    all-gather -> merged selection -> owned-slot attention -> all-gather of
+    partials -> log-sum-exp merge; the owner of the newest page refreshes its
+    k_bar.  The non-attention layers of the model (MoE, norms, LM head) are
+    not part of this path."""
+    import torch.distributed as dist
+    from srswa import ops
+    from srswa.split_kv import SplitKVDecode
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    S0 = args.seq or 1_048_576
+    nblk_filled = S0 // BS
+    nblk_total = nblk_filled + 4                     # room for 256 decoded tokens
+    p = S0 - 1                                       # the step decodes the last position
+    nl = args.layers
+    gen = torch.Generator().manual_seed(4 * 100 + rank)
+    decs, layers = [], []
+    pool = torch.randn(64 << 20, generator=gen).to(torch.bfloat16).to(dev)
+    hc = torch.zeros(DI, device=dev)
+    for _ in range(nl):
+        dec = SplitKVDecode(nblk_total=nblk_total, nblk_filled=nblk_filled, block_size=BS, local_blocks=L, topk=K,
+                            topm=M, idx_scale=IDX_SCALE, floor=FLOOR, sigma=SIGMA, sm_scale=SM_SCALE, rank=rank,
+                            world=world)
+        lo, hi = dec.plan.lo, dec.plan.hi
+        nloc = hi - lo
+        kc = torch.empty(nloc, BS, HKV, D, device=dev, dtype=torch.bfloat16)
+        vc = torch.empty_like(kc)
+        ic = torch.empty(nloc, BS, DI, device=dev, dtype=torch.bfloat16)
+        for t in (kc, vc, ic):
+            fill_from_pool(t, pool, gen)
+        filled = max(0, min(nloc, nblk_filled - lo))   # pages holding tokens on this rank
+        kbar = torch.zeros(1, nloc, DI, device=dev)
+        if filled:
+            kbar[:, :filled] = ops.kbar_contig(ic[:filled].view(1, filled * BS, DI), hc, BS)[0]
+        table = torch.zeros(1, nblk_total, device=dev, dtype=torch.int32)
+        table[0, lo:hi] = torch.arange(nloc, device=dev, dtype=torch.int32)
+        layers.append(dict(kbar=kbar, k_cache=kc, v_cache=vc, block_table=table, idx=ic))
+        decs.append(dec)
+    del pool
+    qs = (torch.randn(nl, 1, H, D, generator=gen) * 0.5).to(torch.bfloat16).to(dev)
+    iqs = (torch.randn(nl, 1, DI, generator=gen) * 0.5).to(torch.bfloat16).to(dev)
+    q_pos = torch.tensor([p], device=dev, dtype=torch.int64)
+    tail = p // BS
+    own_tail = decs[0].plan.lo <= tail < decs[0].plan.hi
+    t_loc = tail - decs[0].plan.lo
+    outs = []
+
+    def step():
+        outs.clear()
+        for li in range(nl):
+            lay = layers[li]
+            if own_tail:   # k_bar of the page receiving the new token
+                lay["kbar"][:, t_loc:t_loc + 1] = ops.kbar_contig(lay["idx"][t_loc:t_loc + 1], hc, BS)[0]
+            outs.append(decs[li].step(qs[li], iqs[li], q_pos, lay, p_range=(p, p)))
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    times, g = timed_graph(step, args.steps, max(args.warmup, 3), flush, not args.no_graph)
+    clk = clocks.stop()
+    ms = sum(times) / len(times)
+    # algorithmic bytes of this rank: k_bar of its remote-candidate blocks,
+    # the K/V rows of the keys it attends (its selected blocks + the window
+    # on its owner), q and o; the selection is recomputed once, untimed, with
+    # the same collectives on every rank
+    plan0 = decs[0].plan
+    ncand = max(0, min(plan0.hi, p // BS - L + 1) - plan0.lo)
+    keys_att = 0
+    for li in range(nl):
+        be = decs[li].backend
+        kk = be.shard_keys(iqs[li], layers[li], decs[li].plan, q_pos, decs[li].rp)
+        sel = be.merge_keys(be.all_gather(kk, world), decs[li].plan, decs[li].rp)
+        keys_att += int((sel["topi32_own"] >= 0).sum()) * BS + (L * BS if own_tail else 0)
+    byts = nl * ncand * DI * 4 + keys_att * HKV * D * 2 * 2 + nl * H * D * 2 * 2
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    b = torch.tensor([float(byts)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(b, op=dist.ReduceOp.SUM)
+    ms, byts = t.item(), b.item()
+    hbm = peaks()[0]
+    if rank == 0:
+        line = {"metric": METRIC, "value": byts / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms, "us_per_step": ms * 1e3,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic seeded N(0,1) (pooled)",
+                "config": {"workload": "cfg5 attention share: 12-layer split-KV decode, one 1M-token sequence",
+                           "seq_len": S0, "layers": nl, "K": K, "LW": L * BS, "parallelism": f"split-kv{world}",
+                           "l2": "flushed before every timed step", "graph": not args.no_graph},
+                "roofline": {"bound": "latency", "achieved": byts / (ms * 1e-3) / 1e9, "peak": hbm * world,
+                             "unit": "GB/s", "frac": byts / (ms * 1e-3) / 1e9 / (hbm * world), "traffic": None},
+                "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if g is not None:
+        del g
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.workload == "route":
         return main_route(args)
+    if args.workload == "longctx":
+        return main_longctx(args)
     if args.workload != "decode" and args.impl != "reference":
         return main_dense(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))

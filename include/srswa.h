@@ -133,6 +133,52 @@ SRSWA_API int srswa_route_select(const float* scores, int64_t s_sc, int64_t N, i
                        int64_t* topi64, int32_t* topi32, float* bias, uint8_t* valid,
                        srswa_stream_t stream);
 
+/* ------------------------------------------------------------ split-KV --
+ * Router for rows whose blocks are spread over shards (the GPUs of a
+ * split-KV decode, where GPU g owns a contiguous block range), or too many for
+ * one CTA (a 1M-token row has 16384 blocks).
+ *
+ * Stage 1, per shard: srswa_route_shard_keys scores the blocks the shard owns,
+ * global ids [block_offset, block_offset + nblk_local), with the global
+ * candidacy rule (c <= q_pos/BS - L, block holds a token; nblk_total = blocks
+ * of the whole row) and writes each row's best M as packed keys, keys_out
+ * [N, M] uint64.  kbar is the shard's own: contiguous [B, nblk_local, d]
+ * (block_table NULL, local index) or a paged cache [P, d] through
+ * block_table [R, W] indexed by GLOBAL block id (only the owned range is
+ * read).  d = 128.  workspace: srswa_route_shard_workspace_size bytes.
+ *
+ * Keys travel between processes (an all-gather), so their format is part of
+ * this interface: bits 63..32 = order-preserving bits of the fp32 entmax input
+ * x (z * idx_scale, or -1e4 off-candidate), bits 31..1 = 0x7fffffff - global
+ * block id, bit 0 = candidate flag.  A larger key ranks first (x descending,
+ * then block id ascending, the reference's tie order); 0 = no key.
+ *
+ * Stage 2: srswa_route_merge_keys reads nlists key lists per row (list l of
+ * row n at keys[l * s_list + n * s_row], M keys each), keeps the global top-M
+ * and runs the selection epilogue of srswa_route (exact entmax over the M,
+ * first K slots, centred log-prior bias).  The lists must come from shards
+ * that together cover [0, nblk_total) once; the top-M of the whole row is then
+ * inside the union of the shards' top-Ms and the outputs equal srswa_route on
+ * the whole row.  topi32_own (optional, [N, K]) is topi32 with -1 for blocks
+ * outside [own_lo, own_hi): the slots the calling shard attends.
+ * No candidate mask in this form (the reference's empty-row fallback needs
+ * the whole row).
+ * Serves the per-GPU local top-M + global merge of the 1M-token split-KV
+ * decode, over _infer_route_select semantics
+ * (hf-model-code/modeling_deepseekv2.py:339-362) and
+ * DashRouterMath.route_and_select (whl:.../unlimited_dash_ops/dash_router.py:131-174). */
+SRSWA_API size_t srswa_route_shard_workspace_size(int64_t N, int64_t nblk_local, srswa_route_params params);
+SRSWA_API int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
+                           const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk_local,
+                           int64_t block_offset, int64_t nblk_total, const int32_t* block_table,
+                           int64_t s_bt, const int32_t* seq_lens, int64_t rows_per_seq,
+                           const int64_t* q_pos, srswa_route_params params, uint64_t* keys_out,
+                           void* workspace, size_t workspace_bytes, srswa_stream_t stream);
+SRSWA_API int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int64_t s_list, int64_t s_row,
+                           int64_t N, int64_t nblk_total, srswa_route_params params, int64_t* topi64,
+                           int32_t* topi32, float* bias, uint8_t* valid, int64_t own_lo,
+                           int64_t own_hi, int32_t* topi32_own, srswa_stream_t stream);
+
 /* ------------------------------------------------------------------ a3 --
  * Token block-max scores.  q [B,C,D] (strides), k [B,Sk,D], pos/seg [B,C]
  * int64 (seg may be NULL = 0) -> out [B,C,nblk] fp32 contiguous:
@@ -244,6 +290,8 @@ typedef struct {
   int64_t s_ti_h, s_ti_n; /* topk_idx / bias / valid strides (head, row) */
   int64_t s_b_h, s_b_n;
   int nsplit;
+  int skip_local; /* 1: attend the selected remote blocks only, not the window
+                     (split-KV shards that do not own the window) */
 } srswa_decode_desc;
 
 SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache,

@@ -388,6 +388,8 @@ extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, c
   SRSWA_CHECK_ARG(d.K >= 0 && (d.K == 0 || topk_idx), SRSWA_EINVAL);
   SRSWA_CHECK_ARG(q_pos || seq_lens, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(d.rows_per_req > 0 && d.block_size > 0 && d.local_blocks >= 0 && d.W > 0, SRSWA_EINVAL);
+  // every row's request must exist: rows n / rows_per_req < R
+  SRSWA_CHECK_ARG(d.R > 0 && (d.N + d.rows_per_req - 1) / d.rows_per_req <= d.R, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(aligned16(q) && aligned16(k_cache) && aligned16(v_cache), SRSWA_EALIGN);
   SRSWA_CHECK_ARG(((d.s_page | d.s_pos | d.s_head) & 7) == 0, SRSWA_EALIGN);
   SRSWA_CHECK_ARG(((d.s_qn | d.s_qh) & (d.q_dtype == SRSWA_F32 ? 3 : 7)) == 0, SRSWA_EALIGN);
@@ -407,7 +409,7 @@ extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, c
   a.s_q_seq = d.rows_per_req * d.s_qn; a.s_q_t = d.s_qn; a.s_qh = d.s_qh;
   a.out = out; a.s_o_seq = d.rows_per_req * d.s_on; a.s_o_t = d.s_on; a.s_oh = d.s_oh;
   a.lse_out = lse_out; a.s_l_seq = d.rows_per_req * d.H; a.s_l_t = d.H;
-  a.nsplit = d.nsplit; a.skip_local = 0;
+  a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0;
   return attend_rows_launch(a, d.D, d.kv_dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 

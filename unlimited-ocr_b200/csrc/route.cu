@@ -530,6 +530,36 @@ __global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const Rou
   }
 }
 
+// Top-M of the 8 per-warp lists (M keys each, kMaxTopM apart) by warp 0;
+// lane m returns the m-th key.  The lists are consumed.
+__device__ unsigned long long merge8_topm(unsigned long long* flat, int M, int lane) {
+  unsigned long long best = 0ull;
+  for (int i = lane; i < 8 * kMaxTopM; i += 32)
+    if ((i % kMaxTopM) < M) best = flat[i] > best ? flat[i] : best;
+  unsigned long long mine = 0ull;
+  for (int m = 0; m < M; ++m) {
+    const unsigned long long w = warp_max_u64(best);
+    if (lane == m) mine = w;
+    if (w != 0ull && best == w) {
+      best = 0ull;
+      for (int i = lane; i < 8 * kMaxTopM; i += 32) {
+        if ((i % kMaxTopM) >= M) continue;
+        unsigned long long v = flat[i];
+        if (v == w) { flat[i] = 0ull; v = 0ull; }
+        best = v > best ? v : best;
+      }
+    }
+    __syncwarp();
+  }
+  return mine;
+}
+__device__ __forceinline__ void unpack_key(unsigned long long k, float& x, int& blk, bool& cand) {
+  x = from_ordered(static_cast<uint32_t>(k >> 32));
+  const uint32_t lo32 = static_cast<uint32_t>(k);
+  blk = 0x7fffffff - static_cast<int>(lo32 >> 1);
+  cand = (lo32 & 1u) != 0;
+}
+
 __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteArgs a, const float* zin,
                                                                     int64_t s_z) {
   extern __shared__ __align__(16) unsigned long long wk[];  // [nblk] keys
@@ -563,36 +593,140 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
   warp_topm_smem(wk + wlo, static_cast<int>(wn), M, lists[warp], lane);
   __syncthreads();
   if (warp != 0) return;
-  unsigned long long* flat = &lists[0][0];
-  // merge: the 8 lists (M keys each, kMaxTopM stride) -> top-M
-  unsigned long long best = 0ull;
-  for (int i = lane; i < 8 * kMaxTopM; i += 32)
-    if ((i % kMaxTopM) < M) best = flat[i] > best ? flat[i] : best;
-  unsigned long long mine = 0ull;
-  for (int m = 0; m < M; ++m) {
-    const unsigned long long w = warp_max_u64(best);
-    if (lane == m) mine = w;
-    if (w != 0ull && best == w) {
-      best = 0ull;
-      for (int i = lane; i < 8 * kMaxTopM; i += 32) {
-        if ((i % kMaxTopM) >= M) continue;
-        unsigned long long v = flat[i];
-        if (v == w) { flat[i] = 0ull; v = 0ull; }
-        best = v > best ? v : best;
+  const unsigned long long mine = merge8_topm(&lists[0][0], M, lane);
+  float sel_v = 0.f;
+  int sel_i = -1;
+  bool sel_c = false;
+  if (lane < M) unpack_key(mine, sel_v, sel_i, sel_c);
+  route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+}
+
+// ============================================================================
+// Split-KV router: rows whose blocks are spread over shards (GPUs), or are too
+// many for one CTA (16384 blocks of a 1M-token row).  Packed keys are the
+// interface between the stages (and between processes):
+//   bits 63..32 ordered bits of x, bits 31..1 0x7fffffff - global block id,
+//   bit 0 candidate; larger = ranks first; 0 = no key.
+// route_chunk_keys_kernel  one CTA per (row, 128 owned blocks): scores like
+//   route_score_kernel (global candidacy: block id = block_offset + local),
+//   packs keys in shared memory, warp 0 keeps the chunk's top-M.
+// keys_merge_kernel  one CTA per row over nlists lists of M keys: per-warp
+//   top-M, 8-list merge; then either the merged M keys or the entmax / top-K
+//   / bias epilogue (plus the shard-owned copy of topi32).
+// The top-M of a union of disjoint sets is contained in the union of the
+// sets' top-Ms, so both stages are exact.
+// ============================================================================
+__global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const RouteArgs a, int64_t blk_off,
+                                                                         int64_t nblk_local,
+                                                                         unsigned long long* out) {
+  __shared__ int32_t bts[kChunkBlocks];
+  __shared__ float zs[kChunkBlocks];
+  __shared__ unsigned long long keys[kChunkBlocks];
+  const int64_t n = blockIdx.y;
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * kChunkBlocks;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t seq = n / a.rows_per_seq;
+  const int64_t p = a.q_pos ? a.q_pos[n]
+                            : static_cast<int64_t>(a.seq_lens[seq]) - a.rows_per_seq + n % a.rows_per_seq;
+  int64_t c_hi = p >= 0 ? p / a.BS - a.L + 1 : 0;  // global: remote blocks are [0, c_hi)
+  if (c_hi < 0) c_hi = 0;
+  if (c_hi > a.nblk) c_hi = a.nblk;
+  if (a.seq_lens) {
+    const int64_t nb = (static_cast<int64_t>(a.seq_lens[seq]) + a.BS - 1) / a.BS;
+    if (c_hi > nb) c_hi = nb;
+  }
+  const int64_t hi = min(lo + kChunkBlocks, nblk_local);
+  const int64_t dhi = max(lo, min(hi, c_hi - blk_off));  // local blocks [lo, dhi) are remote
+  for (int64_t c = lo + tid; c < lo + kChunkBlocks; c += kRouteThreads) zs[c - lo] = kScoreNeg;
+  if (a.block_table && tid < dhi - lo) bts[tid] = a.block_table[seq * a.s_bt + blk_off + lo + tid];
+  __syncthreads();
+  const int64_t c0 = lo + warp * 16;
+  if (c0 < dhi) {  // warp-uniform
+    const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
+    float qv[4];
+    load4(a.q, n * a.s_q + 4 * lane, a.q_dtype, qv);
+    float4 f[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int64_t c = c0 + i;
+      f[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < dhi) {
+        const int64_t off = a.block_table ? static_cast<int64_t>(bts[c - lo]) * a.s_kbar_c
+                                          : seq * a.s_kbar_b + c * a.s_kbar_c;
+        f[i] = __ldg(reinterpret_cast<const float4*>(a.kbar + off + 4 * lane));
       }
     }
-    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float part[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = f[8 * h + i];
+        part[i] = qv[0] * v.x + qv[1] * v.y + qv[2] * v.z + qv[3] * v.w;
+      }
+      const float sdot = transpose_reduce8<32>(part, lane);
+      const int my = 4 * ((lane & 16) != 0) + 2 * ((lane & 8) != 0) + ((lane & 4) != 0);
+      const int64_t c = c0 + 8 * h + my;
+      if ((lane & 3) == 0 && c < dhi) {
+        float z = fminf(fmaxf(sdot * inv_sqrt_d, -kActClamp), kActClamp);
+        if (sdot != sdot) z = sdot;
+        zs[c - lo] = z;
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < kChunkBlocks; i += kRouteThreads) {
+    const int64_t c = lo + i;
+    unsigned long long key = 0ull;
+    if (c < hi) {
+      const float zc = zs[i];
+      const bool cm = zc > kScoreNeg * 0.5f;  // no candidate mask in this form
+      float x = cm ? zc * a.idx_scale : kEntmaxNeg;
+      if (!isfinite(x)) x = kEntmaxNeg;
+      key = pack_key(x, blk_off + c, cm);
+    }
+    keys[i] = key;
+  }
+  __syncthreads();
+  if (warp == 0) warp_topm_smem(keys, kChunkBlocks, static_cast<int>(a.M), out + (n * gridDim.x + blockIdx.x) * a.M,
+                                lane);
+}
+
+constexpr int64_t kMergeMaxKeys = 24576;  // nlists * M per row (192 KiB of shared memory)
+
+__global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteArgs a, const unsigned long long* keys,
+                                                                   int64_t nlists, int64_t s_list, int64_t s_row,
+                                                                   unsigned long long* keys_out, int64_t own_lo,
+                                                                   int64_t own_hi, int32_t* topi32_own) {
+  extern __shared__ __align__(16) unsigned long long mk[];
+  __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
+  const int64_t n = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int M = static_cast<int>(a.M);
+  const int64_t total = nlists * M;
+  for (int64_t i = tid; i < total; i += kRouteThreads) mk[i] = keys[(i / M) * s_list + n * s_row + i % M];
+  __syncthreads();
+  const int64_t per = (total + 7) / 8;
+  const int64_t wlo = warp * per;
+  const int64_t rem = total - wlo;
+  const int64_t wn = rem < 0 ? 0 : (rem < per ? rem : per);
+  warp_topm_smem(mk + wlo, static_cast<int>(wn), M, lists[warp], lane);
+  __syncthreads();
+  if (warp != 0) return;
+  const unsigned long long mine = merge8_topm(&lists[0][0], M, lane);
+  if (keys_out) {
+    if (lane < M) keys_out[n * M + lane] = mine;
+    return;
   }
   float sel_v = 0.f;
   int sel_i = -1;
   bool sel_c = false;
-  if (lane < M) {
-    sel_v = from_ordered(static_cast<uint32_t>(mine >> 32));
-    const uint32_t lo32 = static_cast<uint32_t>(mine);
-    sel_i = 0x7fffffff - static_cast<int>(lo32 >> 1);
-    sel_c = (lo32 & 1u) != 0;
-  }
+  if (lane < M) unpack_key(mine, sel_v, sel_i, sel_c);
   route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+  if (topi32_own && lane < a.K) {
+    const bool own = sel_c && sel_i >= own_lo && sel_i < own_hi;
+    topi32_own[n * a.K + lane] = own ? sel_i : -1;
+  }
 }
 
 // ============================================================================
@@ -890,6 +1024,88 @@ extern "C" int srswa_route_select(const float* scores, int64_t s_sc, int64_t N, 
   a.N = N; a.nblk = nblk; a.rows_per_seq = 1; a.topi64 = topi64; a.topi32 = topi32; a.bias = bias;
   a.valid = valid;
   return route_launch(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------- split-KV --
+static int64_t shard_topm_bound(const srswa_route_params& p) {
+  const int64_t M = p.topm > 0 ? p.topm : kMaxTopM;
+  return M < kMaxTopM ? (M < 1 ? 1 : M) : kMaxTopM;
+}
+
+static int keys_merge_launch(const RouteArgs& a, const unsigned long long* keys, int64_t nlists, int64_t s_list,
+                             int64_t s_row, unsigned long long* keys_out, int64_t own_lo, int64_t own_hi,
+                             int32_t* topi32_own, cudaStream_t st) {
+  if (nlists * a.M > kMergeMaxKeys) return SRSWA_ETOOLARGE;
+  if (a.N >= (1ll << 31)) return SRSWA_ETOOLARGE;
+  const size_t smem = static_cast<size_t>(nlists * a.M) * 8;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(keys_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  keys_merge_kernel<<<static_cast<unsigned>(a.N), kRouteThreads, smem, st>>>(a, keys, nlists, s_list, s_row, keys_out,
+                                                                             own_lo, own_hi, topi32_own);
+  return srswa_last_launch_status();
+}
+
+extern "C" size_t srswa_route_shard_workspace_size(int64_t N, int64_t nblk_local, srswa_route_params params) {
+  if (N <= 0 || nblk_local <= 0) return 0;
+  const int64_t nch = (nblk_local + kChunkBlocks - 1) / kChunkBlocks;
+  if (nch == 1) return 0;
+  return (static_cast<size_t>(N * nch * shard_topm_bound(params)) * 8 + 255) & ~static_cast<size_t>(255);
+}
+
+extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
+                                      const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk_local,
+                                      int64_t block_offset, int64_t nblk_total, const int32_t* block_table,
+                                      int64_t s_bt, const int32_t* seq_lens, int64_t rows_per_seq,
+                                      const int64_t* q_pos, srswa_route_params params, uint64_t* keys_out,
+                                      void* workspace, size_t workspace_bytes, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(idx_q && kbar && keys_out && N >= 0 && rows_per_seq > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(nblk_local > 0 && block_offset >= 0 && block_offset + nblk_local <= nblk_total, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(q_pos || seq_lens, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(d == 128, SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG((reinterpret_cast<uintptr_t>(kbar) & 15) == 0 && (s_kbar_b % 4) == 0 && (s_kbar_c % 4) == 0 &&
+                      (s_q % 4) == 0,
+                  SRSWA_EALIGN);
+  RouteArgs a = {};
+  int rc = fill_route_params(a, params, nblk_total);
+  if (rc) return rc;
+  a.from_scores = 0; a.q = idx_q; a.q_dtype = q_dtype; a.s_q = s_q; a.d = d; a.kbar = kbar;
+  a.s_kbar_b = s_kbar_b; a.s_kbar_c = s_kbar_c; a.block_table = block_table; a.s_bt = s_bt;
+  a.seq_lens = seq_lens; a.rows_per_seq = rows_per_seq; a.q_pos = q_pos; a.N = N; a.nblk = nblk_total;
+  if (N == 0) return 0;
+  SRSWA_CHECK_ARG(N < 65536, SRSWA_ETOOLARGE);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t nch = (nblk_local + kChunkBlocks - 1) / kChunkBlocks;
+  unsigned long long* out = reinterpret_cast<unsigned long long*>(keys_out);
+  if (nch == 1) {
+    route_chunk_keys_kernel<<<dim3(1, static_cast<unsigned>(N)), kRouteThreads, 0, st>>>(a, block_offset, nblk_local,
+                                                                                      out);
+    return srswa_last_launch_status();
+  }
+  const size_t need = static_cast<size_t>(N * nch * a.M) * 8;
+  SRSWA_CHECK_ARG(workspace && workspace_bytes >= need, SRSWA_EWORKSPACE);
+  unsigned long long* ck = static_cast<unsigned long long*>(workspace);
+  route_chunk_keys_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(N)), kRouteThreads, 0, st>>>(
+      a, block_offset, nblk_local, ck);
+  SRSWA_CUDA_TRY(cudaGetLastError());
+  return keys_merge_launch(a, ck, nch, a.M, nch * a.M, out, 0, 0, nullptr, st);
+}
+
+extern "C" int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int64_t s_list, int64_t s_row, int64_t N,
+                                      int64_t nblk_total, srswa_route_params params, int64_t* topi64,
+                                      int32_t* topi32, float* bias, uint8_t* valid, int64_t own_lo, int64_t own_hi,
+                                      int32_t* topi32_own, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(keys && nlists > 0 && N >= 0 && nblk_total > 0, SRSWA_EINVAL);
+  RouteArgs a = {};
+  int rc = fill_route_params(a, params, nblk_total);
+  if (rc) return rc;
+  SRSWA_CHECK_ARG(s_list >= 0 && s_row >= a.M, SRSWA_EINVAL);
+  a.N = N; a.nblk = nblk_total; a.topi64 = topi64; a.topi32 = topi32; a.bias = bias; a.valid = valid;
+  if (N == 0) return 0;
+  return keys_merge_launch(a, reinterpret_cast<const unsigned long long*>(keys), nlists, s_list, s_row, nullptr,
+                           own_lo, own_hi, topi32_own, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int srswa_block_max_score(const void* q, int q_dtype, int64_t sqb, int64_t sqc, const void* k,

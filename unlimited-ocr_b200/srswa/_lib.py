@@ -43,7 +43,7 @@ class DecodeDesc(C.Structure):
                 ("s_qn", i64), ("s_qh", i64), ("s_page", i64), ("s_pos", i64), ("s_head", i64),
                 ("s_on", i64), ("s_oh", i64), ("R", i64), ("W", i64), ("s_req", i64),
                 ("rows_per_req", i64), ("idx_is64", C.c_int), ("s_ti_h", i64), ("s_ti_n", i64),
-                ("s_b_h", i64), ("s_b_n", i64), ("nsplit", C.c_int)]
+                ("s_b_h", i64), ("s_b_n", i64), ("nsplit", C.c_int), ("skip_local", C.c_int)]
 
 
 _SIGS = {
@@ -56,6 +56,11 @@ _SIGS = {
     "srswa_route": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp, i64, vp, vp, i64,
                               RouteParams, vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),
     "srswa_route_select": (C.c_int, [vp, i64, i64, i64, vp, i64, RouteParams, vp, vp, vp, vp, vp]),
+    "srswa_route_shard_workspace_size": (C.c_size_t, [i64, i64, RouteParams]),
+    "srswa_route_shard_keys": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, i64, i64, i64, i64, i64, vp, i64, vp,
+                                         i64, vp, RouteParams, vp, vp, C.c_size_t, vp]),
+    "srswa_route_merge_keys": (C.c_int, [vp, i64, i64, i64, i64, i64, RouteParams, vp, vp, vp, vp, i64, i64,
+                                         vp, vp]),
     "srswa_block_max_score": (C.c_int, [vp, C.c_int, i64, i64, vp, C.c_int, i64, i64, vp, vp, i64, i64,
                                         i64, i64, i64, i64, i64, C.c_int, vp, vp]),
     "srswa_pack_selection": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, vp]),

@@ -35,6 +35,20 @@ def _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma)
                          float(idx_scale), float(floor), float(sigma))
 
 
+def _check_rows(N, rows_per_seq, kbar, block_table, nblk):
+    """Every query row must map to an existing sequence of the k_bar source
+    (row n belongs to sequence n // rows_per_seq), and a block table must
+    cover the blocks scored; checked here because the C interface takes no
+    sequence count."""
+    nseq = -(-N // int(rows_per_seq))
+    if block_table is None:
+        if kbar.shape[0] < nseq:
+            raise ValueError(f"{N} rows at {rows_per_seq} per sequence need {nseq} k_bar sequences, "
+                             f"got {kbar.shape[0]}")
+    elif block_table.shape[0] < nseq or block_table.shape[1] < nblk:
+        raise ValueError(f"block_table {tuple(block_table.shape)} does not cover {nseq} sequences x {nblk} blocks")
+
+
 def effective_km(topk, topm, nblk):
     M = max(1, min(int(topm), nblk)) if int(topm) > 0 else nblk
     K = max(1, min(int(topk), M))
@@ -92,6 +106,7 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
         s_b, s_c = 0, kbar.stride(0)
         bt = block_table.to(torch.int32).contiguous()
         nblk = bt.shape[1] if nblk is None else nblk
+    _check_rows(N, rows_per_seq, kbar, bt, nblk)
     K, M = effective_km(topk, topm, nblk)
     out = {}
     for name, dt, shape in (("topi64", torch.int64, (N, K)), ("topi32", torch.int32, (N, K)),
@@ -111,6 +126,71 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
                          L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
                          L.ptr(out["valid"]), L.ptr(out["scores"]), L.ptr(ws), ws_n, L.stream_of(idx_q))
     L.check(rc, "srswa_route")
+    if out["valid"] is not None:
+        out["valid"] = out["valid"].bool()
+    return {k: v for k, v in out.items() if v is not None}
+
+
+def route_shard_keys(idx_q, kbar, *, block_offset, nblk_local, nblk_total, block_size, local_blocks, topk, topm,
+                     idx_scale, floor, sigma, q_pos=None, seq_lens=None, rows_per_seq=1, block_table=None,
+                     out=None):
+    """Split-KV router stage 1: packed top-M keys [N, M] (int64 storage of
+    the uint64 keys) of the blocks this shard owns, global ids
+    [block_offset, block_offset + nblk_local).  kbar: the shard's contiguous
+    [B, nblk_local, d], or a paged cache [P, d] with block_table [R, >=
+    nblk_total] indexed by global block id."""
+    N, d = idx_q.shape
+    if idx_q.stride(-1) != 1:
+        idx_q = idx_q.contiguous()
+    dev = idx_q.device
+    if block_table is None:
+        s_b, s_c, bt = kbar.stride(0), kbar.stride(1), None
+    else:
+        s_b, s_c = 0, kbar.stride(0)
+        bt = block_table if block_table.dtype == torch.int32 and block_table.is_contiguous() else \
+            block_table.to(torch.int32).contiguous()
+    _check_rows(N, rows_per_seq, kbar, bt, nblk_total)
+    if bt is None and kbar.shape[1] < nblk_local:
+        raise ValueError(f"k_bar holds {kbar.shape[1]} blocks, shard has {nblk_local}")
+    _, M = effective_km(topk, topm, nblk_total)
+    if out is None:
+        out = torch.empty(N, M, device=dev, dtype=torch.int64)
+    qp = None if q_pos is None else q_pos.to(device=dev, dtype=torch.int64).contiguous().view(-1)
+    sl = None if seq_lens is None else seq_lens.to(device=dev, dtype=torch.int32).contiguous()
+    p = _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma)
+    lib = L.lib()
+    ws_n = lib.srswa_route_shard_workspace_size(N, int(nblk_local), p)
+    ws = torch.empty(ws_n, device=dev, dtype=torch.uint8) if ws_n else None
+    rc = lib.srswa_route_shard_keys(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
+                                    kbar.data_ptr(), s_b, s_c, int(nblk_local), int(block_offset),
+                                    int(nblk_total), L.ptr(bt), 0 if bt is None else bt.stride(0), L.ptr(sl),
+                                    int(rows_per_seq), L.ptr(qp), p, out.data_ptr(), L.ptr(ws), ws_n,
+                                    L.stream_of(idx_q))
+    L.check(rc, "srswa_route_shard_keys")
+    return out
+
+
+def route_merge_keys(keys, *, nblk_total, topk, topm, idx_scale, floor, sigma, own=None,
+                     want=("topi64", "bias", "valid")):
+    """Split-KV router stage 2: keys [nlists, N, M] (the all-gathered stage-1
+    outputs) -> the selection of the whole row, as srswa_route.  own =
+    (lo, hi) adds "topi32_own": topi32 with -1 outside the owned range."""
+    nl, N, M = keys.shape
+    assert keys.stride(2) == 1
+    dev = keys.device
+    K, _ = effective_km(topk, topm, nblk_total)
+    out = {}
+    for name, dt in (("topi64", torch.int64), ("topi32", torch.int32), ("bias", torch.float32),
+                     ("valid", torch.uint8), ("topi32_own", torch.int32)):
+        req = name in want or (name == "topi32_own" and own is not None)
+        out[name] = torch.empty(N, K, device=dev, dtype=dt) if req else None
+    lo, hi = own if own is not None else (0, 0)
+    p = _route_params(1, 0, topk, topm, idx_scale, floor, sigma)
+    rc = L.lib().srswa_route_merge_keys(keys.data_ptr(), nl, keys.stride(0), keys.stride(1), N, int(nblk_total), p,
+                                        L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
+                                        L.ptr(out["valid"]), int(lo), int(hi), L.ptr(out["topi32_own"]),
+                                        L.stream_of(keys))
+    L.check(rc, "srswa_route_merge_keys")
     if out["valid"] is not None:
         out["valid"] = out["valid"].bool()
     return {k: v for k, v in out.items() if v is not None}
@@ -234,13 +314,14 @@ def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_win
 
 def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_blocks, sm_scale,
                   out=None, block_table=None, seq_lens=None, q_pos=None, rows_per_req=1,
-                  valid=None, lse=False, nsplit=0, kv_layout=None):
+                  valid=None, lse=False, nsplit=0, kv_layout=None, skip_local=False):
     """Sparse decode attend.  q [N,H,D]; paged k/v caches [P, BS, Hkv, D] (any
     strides with D contiguous) indexed by block_table [R,W].  With
     block_table None, kv_layout = (R, W, s_req, s_pos, s_head, Hkv) describes
     one contiguous cache per request (block blk of request r at r*s_req +
     blk*BS*s_pos).  topk_idx [Hkv or 1 (stride 0 ok), N, K] or [N, K]; bias
-    like topk_idx or None."""
+    like topk_idx or None.  skip_local: attend the selected remote blocks
+    only (a split-KV shard that does not own the window)."""
     N, H, D = q.shape
     assert k_cache.stride() == v_cache.stride()
     if block_table is not None:
@@ -287,7 +368,7 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
                      L.dtype_code(q), L.dtype_code(k_cache), L.dtype_code(out), q.stride(0), q.stride(1),
                      s_page, s_pos, s_head, out.stride(0), out.stride(1),
                      R, W, s_req, rows_per_req, 1 if ti.dtype == torch.int64 else 0,
-                     s_ti_h, ti.stride(1), s_b_h, s_b_n, int(nsplit))
+                     s_ti_h, ti.stride(1), s_b_h, s_b_n, int(nsplit), 1 if skip_local else 0)
     if ti.dtype not in (torch.int32, torch.int64):
         raise NotImplementedError("topk_idx must be int32 or int64")
     rc = L.lib().srswa_decode_attend(C.byref(d), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
@@ -297,12 +378,15 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
     return (out, lse_t) if lse else out
 
 
-def lse_merge(o_parts, lse_parts, out_dtype=torch.float32):
+def lse_merge(o_parts, lse_parts, out_dtype=torch.float32, out=None, lse=None):
     Cn, N, H, D = o_parts.shape
     o_parts = o_parts.float().contiguous()
     lse_parts = lse_parts.float().contiguous()
-    out = torch.empty(N, H, D, device=o_parts.device, dtype=out_dtype)
-    lse = torch.empty(N, H, device=o_parts.device, dtype=torch.float32)
+    if out is None:
+        out = torch.empty(N, H, D, device=o_parts.device, dtype=out_dtype)
+    assert out.is_contiguous()
+    if lse is None:
+        lse = torch.empty(N, H, device=o_parts.device, dtype=torch.float32)
     rc = L.lib().srswa_lse_merge(o_parts.data_ptr(), lse_parts.data_ptr(), Cn, N, H, D, out.data_ptr(),
                                  L.dtype_code(out), lse.data_ptr(), L.stream_of(o_parts))
     L.check(rc, "srswa_lse_merge")

@@ -1,0 +1,156 @@
+"""Split-KV decode of one long sequence over the ranks of a process group.
+
+The 1M-token decode (16384 blocks of 64 tokens per layer) keeps K/V, the
+index keys and the block summaries k_bar of a contiguous range of blocks on
+each GPU; the GPU owning the newest blocks also owns the local window.  One
+decode step of one layer is:
+
+1. every rank scores the blocks it owns and keeps its best M as packed keys
+   (``srswa_route_shard_keys``);
+2. all-gather of the ``[world, rows, M]`` keys (8 bytes each);
+3. every rank merges them into the same global selection
+   (``srswa_route_merge_keys``: exact top-M, entmax, top-K, bias; the top-M of
+   the whole row lies inside the union of the ranks' top-Ms) and keeps the
+   slots it owns;
+4. every rank attends its own selected blocks, the window owner also the
+   window (``srswa_decode_attend`` with ``skip_local`` elsewhere), giving a
+   partial output (fp32) and its log-sum-exp (``-inf`` when empty);
+5. all-gather of the partials and the log-sum-exp merge (``srswa_lse_merge``).
+
+Every rank issues the same two collectives in the same order on every step.
+The reference decodes one GPU at a time (``_dash_decode_forward``,
+hf-model-code/modeling_deepseekv2.py:483-530); the selection it must
+reproduce is ``_block_scores_infer`` + ``_infer_route_select`` (:339-430) and
+the attention ``_decode_attend`` (:455-481).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    """Contiguous block ranges per rank: ranks 0..world-2 own ``per`` blocks
+    of the first ``nblk_filled``; the last rank owns the rest, including the
+    blocks the sequence grows into, so the window (the newest blocks) stays on
+    one rank."""
+
+    nblk_total: int
+    world: int
+    rank: int
+    nblk_filled: int
+
+    @property
+    def per(self) -> int:
+        return max(1, math.ceil(self.nblk_filled / self.world))
+
+    def bounds(self, r: int) -> tuple[int, int]:
+        lo = min(r * self.per, self.nblk_total)
+        hi = self.nblk_total if r == self.world - 1 else min((r + 1) * self.per, self.nblk_total)
+        return lo, hi
+
+    @property
+    def lo(self) -> int:
+        return self.bounds(self.rank)[0]
+
+    @property
+    def hi(self) -> int:
+        return self.bounds(self.rank)[1]
+
+    def owner(self, blk: int) -> int:
+        for r in range(self.world):
+            lo, hi = self.bounds(r)
+            if lo <= blk < hi:
+                return r
+        raise ValueError(f"block {blk} outside [0, {self.nblk_total})")
+
+
+class CudaBackend:
+    """The library's kernels on the current CUDA device, NCCL collectives."""
+
+    def __init__(self, group=None):
+        from . import ops
+        self.ops = ops
+        self.group = group
+
+    def shard_keys(self, idx_q, layer, plan, q_pos, rp):
+        return self.ops.route_shard_keys(
+            idx_q, layer["kbar"], block_offset=plan.lo, nblk_local=plan.hi - plan.lo,
+            nblk_total=plan.nblk_total, q_pos=q_pos, rows_per_seq=idx_q.shape[0],
+            block_table=layer.get("kbar_table"), **rp)
+
+    def merge_keys(self, keys, plan, rp):
+        p = {k: v for k, v in rp.items() if k not in ("block_size", "local_blocks")}
+        return self.ops.route_merge_keys(keys, nblk_total=plan.nblk_total, own=(plan.lo, plan.hi),
+                                         want=("topi32", "bias"), **p)
+
+    def attend(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local):
+        out = torch.empty(q.shape, device=q.device, dtype=torch.float32)
+        return self.ops.decode_attend(q, layer["k_cache"], layer["v_cache"], topi, bias, block_size=block_size,
+                                      local_blocks=local_blocks, sm_scale=sm_scale, out=out,
+                                      block_table=layer["block_table"], q_pos=q_pos, rows_per_req=q.shape[0],
+                                      lse=True, skip_local=skip_local)
+
+    def lse_merge(self, o_parts, lse_parts, out_dtype):
+        return self.ops.lse_merge(o_parts, lse_parts, out_dtype=out_dtype)[0]
+
+    def all_gather(self, x, world):
+        if world == 1:
+            return x.unsqueeze(0)
+        import torch.distributed as dist
+        out = torch.empty((world,) + tuple(x.shape), device=x.device, dtype=x.dtype)
+        dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        return out
+
+
+class SplitKVDecode:
+    """Decode step of one layer for the rows of one sequence (all rows share
+    the sequence; ``q_pos`` holds their global positions)."""
+
+    def __init__(self, *, nblk_total, nblk_filled, block_size, local_blocks, topk, topm, idx_scale, floor,
+                 sigma, sm_scale, rank=0, world=1, backend=None):
+        self.plan = ShardPlan(nblk_total, world, rank, nblk_filled)
+        self.block_size = block_size
+        self.local_blocks = local_blocks
+        self.sm_scale = sm_scale
+        self.rp = dict(block_size=block_size, local_blocks=local_blocks, topk=topk, topm=topm,
+                       idx_scale=idx_scale, floor=floor, sigma=sigma)
+        self.backend = backend if backend is not None else CudaBackend()
+
+    def window_owner(self, p_max: int, p_min: int) -> int:
+        """Rank owning the window of rows at positions [p_min, p_max]; the
+        window must not straddle two ranks."""
+        lw = self.local_blocks * self.block_size
+        first = max(p_min - lw + 1, 0) // self.block_size
+        last = p_max // self.block_size
+        own = self.plan.owner(last)
+        if self.plan.owner(first) != own:
+            raise ValueError("the local window spans two shards: give the last shard at least "
+                             "local_blocks + 1 blocks before the current one")
+        return own
+
+    def step(self, q, idx_q, q_pos, layer, p_range=None, out_dtype=torch.bfloat16):
+        """q [N,H,D], idx_q [N,d], q_pos [N] int64 (device), layer: this
+        rank's {kbar, k_cache, v_cache, block_table (global block ids, [1, W]),
+        optional kbar_table}.  p_range = (min, max) of q_pos known on the host
+        (avoids a device read).  Returns o [N,H,D] (out_dtype)."""
+        be, plan, world = self.backend, self.plan, self.plan.world
+        if p_range is None:
+            qp = q_pos.cpu()
+            p_range = (int(qp.min()), int(qp.max()))
+        keys = be.shard_keys(idx_q, layer, plan, q_pos, self.rp)            # [N, M]
+        all_keys = be.all_gather(keys, world)                                # [world, N, M]
+        sel = be.merge_keys(all_keys, plan, self.rp)
+        owner = self.window_owner(p_range[1], p_range[0])
+        o_part, lse_part = be.attend(q, layer, sel["topi32_own"], sel["bias"], q_pos,
+                                     block_size=self.block_size, local_blocks=self.local_blocks,
+                                     sm_scale=self.sm_scale, skip_local=(plan.rank != owner))
+        if world == 1:
+            return o_part.to(out_dtype)
+        o_all = be.all_gather(o_part, world)                                 # [world, N, H, D]
+        lse_all = be.all_gather(lse_part, world)                             # [world, N, H]
+        return be.lse_merge(o_all, lse_all, out_dtype)
