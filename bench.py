@@ -506,14 +506,19 @@ def main_longctx(args):
     own_tail = decs[0].plan.lo <= tail < decs[0].plan.hi
     t_loc = tail - decs[0].plan.lo
     outs = []
+    side = torch.cuda.Stream()
 
     def step():
         outs.clear()
         for li in range(nl):
             lay = layers[li]
-            if own_tail:   # k_bar of the page receiving the new token
-                lay["kbar"][:, t_loc:t_loc + 1] = ops.kbar_contig(lay["idx"][t_loc:t_loc + 1], hc, BS)[0]
+            if own_tail:   # k_bar of the page receiving the new token (read by later steps' routing)
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    ops.kbar_contig(lay["idx"][t_loc:t_loc + 1], hc, BS, out=lay["kbar"][:, t_loc:t_loc + 1],
+                                    chunk_valid=False)
             outs.append(decs[li].step(qs[li], iqs[li], q_pos, lay, p_range=(p, p)))
+        torch.cuda.current_stream().wait_stream(side)
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     if world > 1:

@@ -92,7 +92,8 @@ class NumpyBackend:
         own = np.where((topi >= plan.lo) & (topi < plan.hi), topi, -1)
         return dict(topi32=topi, bias=bias, topi32_own=own)
 
-    def attend(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local):
+    def attend(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local,
+               out_dtype=None):
         lo_tok = layer["tok0"]
         k, v = layer["k"], layer["v"]          # this shard's tokens [HKV, ntok, D]
         N = len(q_pos)

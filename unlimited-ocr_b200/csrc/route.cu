@@ -438,13 +438,13 @@ __device__ __forceinline__ unsigned long long pack_key(float x, int64_t c, bool 
   const uint32_t lo = (static_cast<uint32_t>(0x7fffffff - static_cast<int32_t>(c)) << 1) | (cand ? 1u : 0u);
   return (static_cast<unsigned long long>(ordered_bits(x)) << 32) | lo;
 }
+// Warp-wide maximum of 64-bit keys: the high words by one warp reduction,
+// then the low words of the lanes holding that high word.
 __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
-    v = w > v ? w : v;
-  }
-  return v;
+  const uint32_t hi = static_cast<uint32_t>(v >> 32), lo = static_cast<uint32_t>(v);
+  const uint32_t mh = __reduce_max_sync(0xffffffffu, hi);
+  const uint32_t ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+  return (static_cast<unsigned long long>(mh) << 32) | ml;
 }
 
 // Top-M keys of k[0..n) (shared memory, unique non-zero keys) by one warp;
@@ -560,6 +560,30 @@ __device__ __forceinline__ void unpack_key(unsigned long long k, float& x, int& 
   cand = (lo32 & 1u) != 0;
 }
 
+// Top-M of `total` unique keys in shared memory (consumed) by the whole CTA:
+// one warp for short lists, else a per-warp top-M of each eighth and a merge
+// of the 8 lists.  Called by all threads; lane m of warp 0 gets key m.
+__device__ unsigned long long block_topm(unsigned long long* mk, int64_t total, int M,
+                                         unsigned long long (*lists)[kMaxTopM], int warp, int lane) {
+  unsigned long long mine = 0ull;
+  if (total <= 256) {  // CTA-uniform
+    if (warp == 0) {
+      warp_topm_smem(mk, static_cast<int>(total), M, lists[0], lane);
+      __syncwarp();
+      mine = lane < M ? lists[0][lane] : 0ull;
+    }
+    return mine;
+  }
+  const int64_t per = (total + 7) / 8;
+  const int64_t wlo = warp * per;
+  const int64_t rem = total - wlo;
+  const int64_t wn = rem < 0 ? 0 : (rem < per ? rem : per);
+  warp_topm_smem(mk + wlo, static_cast<int>(wn), M, lists[warp], lane);
+  __syncthreads();
+  if (warp == 0) mine = merge8_topm(&lists[0][0], M, lane);
+  return mine;
+}
+
 __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteArgs a, const float* zin,
                                                                     int64_t s_z) {
   extern __shared__ __align__(16) unsigned long long wk[];  // [nblk] keys
@@ -618,10 +642,15 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
 // ============================================================================
 __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const RouteArgs a, int64_t blk_off,
                                                                          int64_t nblk_local,
-                                                                         unsigned long long* out) {
+                                                                         unsigned long long* chunk_out,
+                                                                         unsigned int* counters,
+                                                                         unsigned long long* keys_out) {
+  extern __shared__ __align__(16) unsigned long long mk[];  // [nch * M] (last CTA of a row)
   __shared__ int32_t bts[kChunkBlocks];
   __shared__ float zs[kChunkBlocks];
   __shared__ unsigned long long keys[kChunkBlocks];
+  __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
+  __shared__ unsigned int ticket;
   const int64_t n = blockIdx.y;
   const int64_t lo = static_cast<int64_t>(blockIdx.x) * kChunkBlocks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -688,8 +717,24 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
     keys[i] = key;
   }
   __syncthreads();
-  if (warp == 0) warp_topm_smem(keys, kChunkBlocks, static_cast<int>(a.M), out + (n * gridDim.x + blockIdx.x) * a.M,
-                                lane);
+  const int M = static_cast<int>(a.M);
+  const int64_t nch = gridDim.x;
+  if (warp == 0) warp_topm_smem(keys, kChunkBlocks, M, chunk_out + (n * nch + blockIdx.x) * M, lane);
+  if (nch == 1) return;  // chunk_out is the row's output
+  // the last CTA of the row to finish merges the row's chunk lists
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) ticket = atomicAdd(counters + n, 1u);
+  __syncthreads();
+  if (ticket != static_cast<unsigned int>(nch - 1)) return;
+  __threadfence();
+  const int64_t total = nch * M;
+  const unsigned long long* src = chunk_out + n * total;
+  for (int64_t i = tid; i < total; i += kRouteThreads) mk[i] = __ldcg(src + i);
+  __syncthreads();
+  const unsigned long long mine = block_topm(mk, total, M, lists, warp, lane);
+  if (warp == 0 && lane < M) keys_out[n * M + lane] = mine;
+  if (tid == 0) counters[n] = 0u;
 }
 
 constexpr int64_t kMergeMaxKeys = 24576;  // nlists * M per row (192 KiB of shared memory)
@@ -704,16 +749,11 @@ __global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteAr
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int M = static_cast<int>(a.M);
   const int64_t total = nlists * M;
-  for (int64_t i = tid; i < total; i += kRouteThreads) mk[i] = keys[(i / M) * s_list + n * s_row + i % M];
+  for (int64_t l = warp; l < nlists; l += kRouteThreads / 32)
+    if (lane < M) mk[l * M + lane] = keys[l * s_list + n * s_row + lane];
   __syncthreads();
-  const int64_t per = (total + 7) / 8;
-  const int64_t wlo = warp * per;
-  const int64_t rem = total - wlo;
-  const int64_t wn = rem < 0 ? 0 : (rem < per ? rem : per);
-  warp_topm_smem(mk + wlo, static_cast<int>(wn), M, lists[warp], lane);
-  __syncthreads();
+  const unsigned long long mine = block_topm(mk, total, M, lists, warp, lane);
   if (warp != 0) return;
-  const unsigned long long mine = merge8_topm(&lists[0][0], M, lane);
   if (keys_out) {
     if (lane < M) keys_out[n * M + lane] = mine;
     return;
@@ -1052,7 +1092,8 @@ extern "C" size_t srswa_route_shard_workspace_size(int64_t N, int64_t nblk_local
   if (N <= 0 || nblk_local <= 0) return 0;
   const int64_t nch = (nblk_local + kChunkBlocks - 1) / kChunkBlocks;
   if (nch == 1) return 0;
-  return (static_cast<size_t>(N * nch * shard_topm_bound(params)) * 8 + 255) & ~static_cast<size_t>(255);
+  const size_t cnt_bytes = (static_cast<size_t>(N) * 4 + 255) & ~static_cast<size_t>(255);
+  return cnt_bytes + ((static_cast<size_t>(N * nch * shard_topm_bound(params)) * 8 + 255) & ~static_cast<size_t>(255));
 }
 
 extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
@@ -1081,16 +1122,25 @@ extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_
   unsigned long long* out = reinterpret_cast<unsigned long long*>(keys_out);
   if (nch == 1) {
     route_chunk_keys_kernel<<<dim3(1, static_cast<unsigned>(N)), kRouteThreads, 0, st>>>(a, block_offset, nblk_local,
-                                                                                      out);
+                                                                                      out, nullptr, nullptr);
     return srswa_last_launch_status();
   }
-  const size_t need = static_cast<size_t>(N * nch * a.M) * 8;
+  SRSWA_CHECK_ARG(nch * a.M <= kMergeMaxKeys, SRSWA_ETOOLARGE);
+  const size_t cnt_bytes = (static_cast<size_t>(N) * 4 + 255) & ~static_cast<size_t>(255);
+  const size_t need = cnt_bytes + static_cast<size_t>(N * nch * a.M) * 8;
   SRSWA_CHECK_ARG(workspace && workspace_bytes >= need, SRSWA_EWORKSPACE);
-  unsigned long long* ck = static_cast<unsigned long long*>(workspace);
-  route_chunk_keys_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(N)), kRouteThreads, 0, st>>>(
-      a, block_offset, nblk_local, ck);
-  SRSWA_CUDA_TRY(cudaGetLastError());
-  return keys_merge_launch(a, ck, nch, a.M, nch * a.M, out, 0, 0, nullptr, st);
+  unsigned int* counters = static_cast<unsigned int*>(workspace);
+  unsigned long long* ck = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + cnt_bytes);
+  SRSWA_CUDA_TRY(cudaMemsetAsync(counters, 0, static_cast<size_t>(N) * 4, st));
+  const size_t smem = static_cast<size_t>(nch * a.M) * 8;
+  if (smem > 40 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(route_chunk_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  route_chunk_keys_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(N)), kRouteThreads, smem, st>>>(
+      a, block_offset, nblk_local, ck, counters, out);
+  return srswa_last_launch_status();
 }
 
 extern "C" int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int64_t s_list, int64_t s_row, int64_t N,

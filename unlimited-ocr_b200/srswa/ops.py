@@ -55,20 +55,29 @@ def effective_km(topk, topm, nblk):
     return K, M
 
 
-def kbar_contig(idx_k: torch.Tensor, head_cls: torch.Tensor, block_size: int):
-    """[B,S,d] index keys -> (kbar [B,nblk,d] fp32, chunk_valid [B,nblk] bool)."""
+def kbar_contig(idx_k: torch.Tensor, head_cls: torch.Tensor, block_size: int, out=None, chunk_valid=True):
+    """[B,S,d] index keys -> (kbar [B,nblk,d] fp32, chunk_valid [B,nblk] bool).
+    out: a caller's [B, nblk, d] fp32 tensor with contiguous rows (written in
+    place, e.g. a slice of a larger k_bar); chunk_valid=False skips that output
+    (returned as None)."""
     B, S, d = idx_k.shape
     if idx_k.stride(-1) != 1:
         idx_k = idx_k.contiguous()
     nblk = (S + block_size - 1) // block_size
-    out = torch.empty(B, nblk, d, device=idx_k.device, dtype=torch.float32)
-    cv = torch.empty(B, nblk, device=idx_k.device, dtype=torch.uint8)
-    hc = head_cls.to(device=idx_k.device, dtype=torch.float32).contiguous()
+    if out is None:
+        out = torch.empty(B, nblk, d, device=idx_k.device, dtype=torch.float32)
+    elif (out.shape != (B, nblk, d) or out.dtype != torch.float32 or out.stride(2) != 1
+          or out.stride(1) != d or (B > 1 and out.stride(0) != nblk * d)):
+        raise ValueError("out must be a [B, nblk, d] fp32 tensor laid out contiguously")
+    cv = torch.empty(B, nblk, device=idx_k.device, dtype=torch.uint8) if chunk_valid else None
+    hc = head_cls if (head_cls.dtype == torch.float32 and head_cls.is_contiguous()
+                      and head_cls.device == idx_k.device) else \
+        head_cls.to(device=idx_k.device, dtype=torch.float32).contiguous()
     rc = L.lib().srswa_kbar_contig(idx_k.data_ptr(), L.dtype_code(idx_k), idx_k.stride(0), idx_k.stride(1),
-                                   B, S, d, block_size, hc.data_ptr(), out.data_ptr(), cv.data_ptr(),
+                                   B, S, d, block_size, hc.data_ptr(), out.data_ptr(), L.ptr(cv),
                                    L.stream_of(idx_k))
     L.check(rc, "srswa_kbar_contig")
-    return out, cv.bool()
+    return out, (cv.bool() if cv is not None else None)
 
 
 def kbar_paged(idx_cache, head_cls, block_table, seq_lens, kbar_cache, tail_pages=0):

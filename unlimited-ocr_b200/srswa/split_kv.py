@@ -88,8 +88,9 @@ class CudaBackend:
         return self.ops.route_merge_keys(keys, nblk_total=plan.nblk_total, own=(plan.lo, plan.hi),
                                          want=("topi32", "bias"), **p)
 
-    def attend(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local):
-        out = torch.empty(q.shape, device=q.device, dtype=torch.float32)
+    def attend(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local,
+               out_dtype=torch.float32):
+        out = torch.empty(q.shape, device=q.device, dtype=out_dtype)
         return self.ops.decode_attend(q, layer["k_cache"], layer["v_cache"], topi, bias, block_size=block_size,
                                       local_blocks=local_blocks, sm_scale=sm_scale, out=out,
                                       block_table=layer["block_table"], q_pos=q_pos, rows_per_req=q.shape[0],
@@ -146,11 +147,13 @@ class SplitKVDecode:
         all_keys = be.all_gather(keys, world)                                # [world, N, M]
         sel = be.merge_keys(all_keys, plan, self.rp)
         owner = self.window_owner(p_range[1], p_range[0])
+        # one rank: its output is final, written in out_dtype; else fp32 partials
         o_part, lse_part = be.attend(q, layer, sel["topi32_own"], sel["bias"], q_pos,
                                      block_size=self.block_size, local_blocks=self.local_blocks,
-                                     sm_scale=self.sm_scale, skip_local=(plan.rank != owner))
+                                     sm_scale=self.sm_scale, skip_local=(plan.rank != owner),
+                                     out_dtype=out_dtype if world == 1 else torch.float32)
         if world == 1:
-            return o_part.to(out_dtype)
+            return o_part
         o_all = be.all_gather(o_part, world)                                 # [world, N, H, D]
         lse_all = be.all_gather(lse_part, world)                             # [world, N, H]
         return be.lse_merge(o_all, lse_all, out_dtype)
