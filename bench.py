@@ -518,7 +518,8 @@ def main_longctx(args):
                     ops.kbar_contig(lay["idx"][t_loc:t_loc + 1], hc, BS, out=lay["kbar"][:, t_loc:t_loc + 1],
                                     chunk_valid=False)
             outs.append(decs[li].step(qs[li], iqs[li], q_pos, lay, p_range=(p, p)))
-        torch.cuda.current_stream().wait_stream(side)
+        if own_tail:   # join the side stream only where it was forked (graph capture)
+            torch.cuda.current_stream().wait_stream(side)
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     if world > 1:

@@ -305,14 +305,17 @@ SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, co
  * skipped its outputs and exited cleanly).  No reference counterpart. */
 SRSWA_API int srswa_device_status(int* out);
 
-/* Log-sum-exp merge of C split-KV partials: o_parts [C,N,H,D] fp32, lse_parts
- * [C,N,H] fp32 natural log (-inf = empty part) -> out [N,H,D] (out_dtype,
+/* Log-sum-exp merge of C split-KV partials: part c of o at o_parts + c *
+ * s_o_part ([N,H,D] fp32, contiguous inside the part), of the log-sum-exp at
+ * lse_parts + c * s_l_part ([N,H] fp32 natural log, -inf = empty part); the
+ * strides let the parts come straight out of one packed all-gather buffer
+ * (0 = tightly stacked: N*H*D and N*H).  -> out [N,H,D] (out_dtype,
  * contiguous) and lse_out [N,H] (optional).  Replaces
  * _merge_topk_attn_out_kernel (whl:.../unlimited_dash_ops/common.py:43-89);
  * also the cross-GPU combine of the split-KV decode. */
 SRSWA_API int srswa_lse_merge(const float* o_parts, const float* lse_parts, int64_t C, int64_t N,
-                    int64_t H, int64_t D, void* out, int out_dtype, float* lse_out,
-                    srswa_stream_t stream);
+                    int64_t H, int64_t D, int64_t s_o_part, int64_t s_l_part, void* out,
+                    int out_dtype, float* lse_out, srswa_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -127,6 +127,9 @@ class NumpyBackend:
                 lse[n, h] = mx + np.log(e.sum())
         return torch.from_numpy(o), torch.from_numpy(lse)
 
+    def exchange_partials(self, o_part, lse_part, world):
+        return self.all_gather(o_part, world), self.all_gather(lse_part, world)
+
     def lse_merge(self, o_all, lse_all, out_dtype):
         return torch.from_numpy(O.lse_merge(o_all.numpy(), lse_all.numpy())[0])
 

@@ -348,23 +348,23 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
 }
 
 __global__ void lse_merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ lse_parts,
-                                 int64_t C, int64_t NH, int64_t D, void* out, int out_dtype,
-                                 float* lse_out) {
+                                 int64_t C, int64_t NH, int64_t D, int64_t s_o, int64_t s_l, void* out,
+                                 int out_dtype, float* lse_out) {
   const int64_t nh = blockIdx.x;
   float M = -INFINITY;
-  for (int64_t c = 0; c < C; ++c) M = fmaxf(M, lse_parts[c * NH + nh]);
+  for (int64_t c = 0; c < C; ++c) M = fmaxf(M, lse_parts[c * s_l + nh]);
   const float Mu = (M == -INFINITY) ? 0.f : M;
   float den = 0.f;
   for (int64_t c = 0; c < C; ++c) {
-    const float l = lse_parts[c * NH + nh];
+    const float l = lse_parts[c * s_l + nh];
     den += (l == -INFINITY) ? 0.f : expf(l - Mu);
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.f;
     for (int64_t c = 0; c < C; ++c) {
-      const float l = lse_parts[c * NH + nh];
-      if (l != -INFINITY) acc += expf(l - Mu) * o_parts[(c * NH + nh) * D + d];
+      const float l = lse_parts[c * s_l + nh];
+      if (l != -INFINITY) acc += expf(l - Mu) * o_parts[c * s_o + nh * D + d];
     }
     store_elem(out, nh * D + d, out_dtype, acc * inv);
   }
@@ -414,12 +414,15 @@ extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, c
 }
 
 extern "C" int srswa_lse_merge(const float* o_parts, const float* lse_parts, int64_t C, int64_t N,
-                               int64_t H, int64_t D, void* out, int out_dtype, float* lse_out,
-                               srswa_stream_t stream) {
+                               int64_t H, int64_t D, int64_t s_o_part, int64_t s_l_part, void* out,
+                               int out_dtype, float* lse_out, srswa_stream_t stream) {
   SRSWA_CHECK_ARG(o_parts && lse_parts && out && C > 0 && N >= 0 && H > 0 && D > 0, SRSWA_EINVAL);
+  if (s_o_part == 0) s_o_part = N * H * D;
+  if (s_l_part == 0) s_l_part = N * H;
+  SRSWA_CHECK_ARG(s_o_part >= N * H * D && s_l_part >= N * H, SRSWA_EINVAL);
   if (N == 0) return 0;
   SRSWA_CHECK_ARG(N * H < (1ll << 31), SRSWA_ETOOLARGE);
   lse_merge_kernel<<<static_cast<unsigned>(N * H), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      o_parts, lse_parts, C, N * H, D, out, out_dtype, lse_out);
+      o_parts, lse_parts, C, N * H, D, s_o_part, s_l_part, out, out_dtype, lse_out);
   return srswa_last_launch_status();
 }

@@ -76,7 +76,7 @@ _SIGS = {
     "srswa_decode_attend": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                       vp]),
     "srswa_device_status": (C.c_int, [C.POINTER(C.c_int)]),
-    "srswa_lse_merge": (C.c_int, [vp, vp, i64, i64, i64, i64, vp, C.c_int, vp, vp]),
+    "srswa_lse_merge": (C.c_int, [vp, vp, i64, i64, i64, i64, i64, i64, vp, C.c_int, vp, vp]),
 }
 
 _lib = None

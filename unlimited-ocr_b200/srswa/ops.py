@@ -323,7 +323,7 @@ def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_win
 
 def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_blocks, sm_scale,
                   out=None, block_table=None, seq_lens=None, q_pos=None, rows_per_req=1,
-                  valid=None, lse=False, nsplit=0, kv_layout=None, skip_local=False):
+                  valid=None, lse=False, nsplit=0, kv_layout=None, skip_local=False, lse_out=None):
     """Sparse decode attend.  q [N,H,D]; paged k/v caches [P, BS, Hkv, D] (any
     strides with D contiguous) indexed by block_table [R,W].  With
     block_table None, kv_layout = (R, W, s_req, s_pos, s_head, Hkv) describes
@@ -365,7 +365,10 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
             s_ti_h = ti.stride(0) if ti.shape[0] > 1 else 0
     if out is None:
         out = torch.empty(N, H, D, device=q.device, dtype=q.dtype)
-    lse_t = torch.empty(N, H, device=q.device, dtype=torch.float32) if lse else None
+    lse_t = None
+    if lse:
+        lse_t = lse_out if lse_out is not None else torch.empty(N, H, device=q.device, dtype=torch.float32)
+        assert lse_t.shape == (N, H) and lse_t.is_contiguous() and lse_t.dtype == torch.float32
     bt = None if block_table is None else block_table.to(torch.int32).contiguous()
     sl = None if seq_lens is None else seq_lens.to(device=q.device, dtype=torch.int32).contiguous()
     qp = None if q_pos is None else q_pos.to(device=q.device, dtype=torch.int64).contiguous().view(-1)
@@ -388,16 +391,22 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
 
 
 def lse_merge(o_parts, lse_parts, out_dtype=torch.float32, out=None, lse=None):
+    """o_parts [C,N,H,D], lse_parts [C,N,H] fp32 (each part contiguous; the
+    parts may be strided, e.g. views into one packed all-gather buffer) ->
+    (out [N,H,D] out_dtype, lse [N,H])."""
     Cn, N, H, D = o_parts.shape
-    o_parts = o_parts.float().contiguous()
-    lse_parts = lse_parts.float().contiguous()
+    if o_parts.dtype != torch.float32 or o_parts[0].stride() != (H * D, D, 1):
+        o_parts = o_parts.float().contiguous()
+    if lse_parts.dtype != torch.float32 or lse_parts[0].stride() != (H, 1):
+        lse_parts = lse_parts.float().contiguous()
     if out is None:
         out = torch.empty(N, H, D, device=o_parts.device, dtype=out_dtype)
     assert out.is_contiguous()
     if lse is None:
         lse = torch.empty(N, H, device=o_parts.device, dtype=torch.float32)
-    rc = L.lib().srswa_lse_merge(o_parts.data_ptr(), lse_parts.data_ptr(), Cn, N, H, D, out.data_ptr(),
-                                 L.dtype_code(out), lse.data_ptr(), L.stream_of(o_parts))
+    rc = L.lib().srswa_lse_merge(o_parts.data_ptr(), lse_parts.data_ptr(), Cn, N, H, D, o_parts.stride(0),
+                                 lse_parts.stride(0), out.data_ptr(), L.dtype_code(out), lse.data_ptr(),
+                                 L.stream_of(o_parts))
     L.check(rc, "srswa_lse_merge")
     return out, lse
 

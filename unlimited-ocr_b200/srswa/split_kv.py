@@ -15,7 +15,8 @@ decode step of one layer is:
 4. every rank attends its own selected blocks, the window owner also the
    window (``srswa_decode_attend`` with ``skip_local`` elsewhere), giving a
    partial output (fp32) and its log-sum-exp (``-inf`` when empty);
-5. all-gather of the partials and the log-sum-exp merge (``srswa_lse_merge``).
+5. all-gather of the partials (o and its log-sum-exp packed in one buffer)
+   and the log-sum-exp merge (``srswa_lse_merge``).
 
 Every rank issues the same two collectives in the same order on every step.
 The reference decodes one GPU at a time (``_dash_decode_forward``,
@@ -90,11 +91,24 @@ class CudaBackend:
 
     def attend(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local,
                out_dtype=torch.float32):
-        out = torch.empty(q.shape, device=q.device, dtype=out_dtype)
+        N, H, D = q.shape
+        if out_dtype == torch.float32:
+            # partial o and its lse packed in one buffer: one all-gather moves both
+            buf = torch.empty(N * H * D + N * H, device=q.device, dtype=torch.float32)
+            out, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:].view(N, H)
+        else:
+            out, lse = torch.empty(q.shape, device=q.device, dtype=out_dtype), None
         return self.ops.decode_attend(q, layer["k_cache"], layer["v_cache"], topi, bias, block_size=block_size,
                                       local_blocks=local_blocks, sm_scale=sm_scale, out=out,
-                                      block_table=layer["block_table"], q_pos=q_pos, rows_per_req=q.shape[0],
-                                      lse=True, skip_local=skip_local)
+                                      block_table=layer["block_table"], q_pos=q_pos, rows_per_req=N,
+                                      lse=True, skip_local=skip_local, lse_out=lse)
+
+    def exchange_partials(self, o_part, lse_part, world):
+        """All-gather of the packed partials -> ([world,N,H,D], [world,N,H]) views."""
+        N, H, D = o_part.shape
+        buf = torch.as_strided(o_part, (N * H * D + N * H,), (1,))   # the packed buffer of attend()
+        g = self.all_gather(buf, world)
+        return g[:, :N * H * D].view(world, N, H, D), g[:, N * H * D:].view(world, N, H)
 
     def lse_merge(self, o_parts, lse_parts, out_dtype):
         return self.ops.lse_merge(o_parts, lse_parts, out_dtype=out_dtype)[0]
@@ -154,6 +168,5 @@ class SplitKVDecode:
                                      out_dtype=out_dtype if world == 1 else torch.float32)
         if world == 1:
             return o_part
-        o_all = be.all_gather(o_part, world)                                 # [world, N, H, D]
-        lse_all = be.all_gather(lse_part, world)                             # [world, N, H]
+        o_all, lse_all = be.exchange_partials(o_part, lse_part, world)      # [world,N,H,D], [world,N,H]
         return be.lse_merge(o_all, lse_all, out_dtype)
