@@ -15,6 +15,13 @@ constexpr int kAttendMaxSlots = 64;  // remote slots + window blocks per row
 //   block_table[seq * s_bt + blk] * s_page      (paged), or
 //   seq * s_seq + blk * s_blk                   (contiguous),
 // and key position i inside it / kv head h add i * s_pos + h * s_head.
+// Workspace layout of the tensor-core gather forward (byte offsets); one
+// definition shared by gather.cu (sizing) and gather_tc.cu (use).
+struct TcLayout {
+  size_t part_o, part_lse, count, offs, cursor, tiles, ntiles, pairs, lse, pair_q, pair_bias, total;
+  int64_t max_tiles;
+};
+
 struct AttendArgs {
   const void* q;
   const void* k;

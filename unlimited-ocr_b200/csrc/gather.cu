@@ -376,10 +376,6 @@ static int check_gather_desc(const srswa_gather_desc* g) {
 using namespace srswa;
 
 namespace srswa {
-struct TcLayout {
-  size_t part_o, part_lse, count, offs, cursor, tiles, ntiles, pairs, total;
-  int64_t max_tiles;
-};
 TcLayout tc_layout(const srswa_gather_desc* g);
 bool tc_eligible(const srswa_gather_desc* g);
 int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const int32_t* sel,

@@ -23,6 +23,8 @@
 // spin; the result is broadcast through __syncthreads so an expired wait takes
 // a CTA-uniform exit path that drains the tensor pipe and frees TMEM.
 
+#include <cuda.h>  // CUtensorMap (the encoder is looked up at run time; libcuda is not linked)
+
 #include "attend.cuh"
 #include "common.cuh"
 #include "tc.cuh"
@@ -62,6 +64,10 @@ struct TcArgs {
   const int32_t* pairs;       // packed t * S + s, grouped by (b, hi, block)
   const int4* tiles;          // (b*HI + hi, block, first pair, count)
   const int32_t* ntiles;      // device count of tiles
+  const int32_t* count;       // pairs per (b*HI + hi, block)
+  const int32_t* offs;        // first pair of each (b*HI + hi, block)
+  int64_t* pair_q;            // per pair: b * sqb + t * sqt (the query head's offset is added per item)
+  float* pair_bias;           // per pair: slot bias * log2 e (0 without bias)
   int64_t B, T, HQ, Hkv, HI, S, LW, nblk;
   float scale_log2;
 };
@@ -439,6 +445,10 @@ __global__ void pairs_fill_kernel(const TcArgs a, int32_t* cursor, int32_t* pair
     if (dup) continue;
     const int32_t pos = atomicAdd(cursor + bh * a.nblk + blk, 1);
     pairs[pos] = static_cast<int32_t>(t * a.S + s);
+    if (a.pair_q) {
+      a.pair_q[pos] = b * a.sqb + t * a.sqt;
+      a.pair_bias[pos] = a.bias ? a.bias[(b * a.T + t) * a.S + s] * kLog2e : 0.f;
+    }
   }
 }
 
@@ -585,6 +595,988 @@ __global__ void __launch_bounds__(kTcThreads) remote_fwd_kernel(const TcArgs a) 
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kRemoteTmemCols);
+}
+
+// ============================================================================
+// Warp-specialised forward: both passes on one engine.
+//
+// A CTA is persistent over work items (band: (b, h, 128-query tile); remote:
+// (pair tile, query head)) and runs two items at a time, one per slot.
+//   warps 0-3 / 4-7  softmax warpgroup of slot 0 / 1 (thread = query row): S
+//                    from TMEM, mask, online softmax with lazy O rescale, P
+//                    (bf16) over the dead K operand, and the item's epilogue
+//                    from O in TMEM;
+//   warp 8           producer: cp.async of the slot's Q tile and of each key
+//                    block's K and V into the slot's 2-stage ring; completion
+//                    arrives on mbarriers (cp.async.mbarrier.arrive.noinc);
+//   warp 9           MMA issuer (one thread) and TMEM owner: S = Q K^T and
+//                    O += P V of the two slots in ping-pong order, so one
+//                    slot's MMAs run while the other slot's softmax does.
+// Every wait is bounded and also gives up once another role has set the CTA's
+// abort flag, so a stuck role releases the others; the CTA then drains the
+// tensor pipe and frees TMEM.
+// ============================================================================
+constexpr int kWsThreads = 320;
+constexpr int kWsProducer = 8, kWsMma = 9;
+constexpr uint32_t kWsStage = 2 * kKVBytes;                              // K then V
+constexpr uint32_t kWsSmem = 2 * kQBytes + 2 * 2 * kWsStage + 1024;      // 193 KB -> 1 CTA/SM
+constexpr uint32_t kWsTmemCols = 512;                                   // per slot: S 0-63, O 128-255
+
+__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+  const uint32_t a = smem_u32(bar);
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 31) == 31 && *abort_flag) return false;
+  }
+  atomicExch(&g_tc_error, code);
+  *abort_flag = 1;
+  return false;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// arrive once every cp.async this thread issued so far has landed
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// 2^x on the MUFU unit (ex2.approx, flush-to-zero; 2^-inf = +0)
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Max of one row's raw scores of a 64-key block; keys outside [lo, hi)
+// (relative to the block) are set to -inf first unless `full` (warp-uniform)
+// says every key is valid.  Four independent max chains.
+__device__ __forceinline__ float block_row_max(float (&sv)[64], int lo, int hi, bool full) {
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  if (full) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) m[i & 3] = fmaxf(m[i & 3], sv[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      sv[i] = (i >= lo && i < hi) ? sv[i] : -INFINITY;
+      m[i & 3] = fmaxf(m[i & 3], sv[i]);
+    }
+  }
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+// In place p = 2^(s * c + off) (c > 0; masked keys hold -inf and give 0);
+// returns the row sum (four independent chains)
+__device__ __forceinline__ float block_row_exp(float (&sv)[64], float c, float off) {
+  float l[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    sv[i] = fast_exp2(fmaf(sv[i], c, off));
+    l[i & 3] += sv[i];
+  }
+  return (l[0] + l[1]) + (l[2] + l[3]);
+}
+__device__ __forceinline__ int clamp_key(int64_t v) { return static_cast<int>(v < 0 ? 0 : (v > kBlk ? kBlk : v)); }
+
+struct WsItem {
+  int64_t b, h, hk;
+  int64_t blo, bhi;     // key blocks, inclusive
+  int64_t t0;           // band: first query row
+  int64_t first, cnt;   // remote: pair range
+};
+
+template <bool kRemote>
+__device__ __forceinline__ int64_t ws_num_items(const TcArgs& a) {
+  if (kRemote) return static_cast<int64_t>(*a.ntiles) * (a.HQ / a.HI);
+  return a.B * a.HQ * ((a.T + kTileM - 1) / kTileM);
+}
+
+template <bool kRemote>
+__device__ __forceinline__ WsItem ws_item(const TcArgs& a, int64_t item) {
+  WsItem w;
+  if (kRemote) {
+    const int64_t hpi = a.HQ / a.HI;
+    const int4 td = a.tiles[item / hpi];
+    w.b = td.x / a.HI;
+    w.h = (td.x % a.HI) * hpi + item % hpi;
+    w.blo = w.bhi = td.y;
+    w.first = td.z;
+    w.cnt = td.w;
+    w.t0 = 0;
+  } else {
+    const int64_t nt = (a.T + kTileM - 1) / kTileM;
+    const int64_t tile = item % nt, bh = item / nt;
+    w.b = bh / a.HQ;
+    w.h = bh % a.HQ;
+    w.t0 = tile * kTileM;
+    const int64_t tlast = min(a.T, w.t0 + kTileM) - 1;
+    int64_t key_lo = w.t0 - a.LW + 1;
+    if (key_lo < 0) key_lo = 0;
+    w.blo = key_lo / kBlk;
+    w.bhi = tlast / kBlk;
+    w.first = 0;
+    w.cnt = 0;
+  }
+  w.hk = w.h / (a.HQ / a.Hkv);
+  return w;
+}
+
+// The step sequence of one slot: its items (blockIdx.x + (2m + slot) *
+// gridDim.x) and, inside each, the key blocks blo..bhi.  Every role walks the
+// same sequence.
+template <bool kRemote>
+struct WsCursor {
+  int64_t item, nitems, m, j, n;
+  WsItem w;
+  bool done;
+  __device__ __forceinline__ void start(const TcArgs& a, int slot, int64_t ni) {
+    nitems = ni;
+    item = blockIdx.x + static_cast<int64_t>(slot) * gridDim.x;
+    m = 0;
+    n = 0;
+    done = item >= nitems;
+    if (!done) {
+      w = ws_item<kRemote>(a, item);
+      j = w.blo;
+    }
+  }
+  __device__ __forceinline__ bool first() const { return j == w.blo; }
+  __device__ __forceinline__ bool last() const { return j == w.bhi; }
+  __device__ __forceinline__ void advance(const TcArgs& a) {
+    ++n;
+    if (j < w.bhi) {
+      ++j;
+      return;
+    }
+    ++m;
+    item += 2 * static_cast<int64_t>(gridDim.x);
+    done = item >= nitems;
+    if (!done) {
+      w = ws_item<kRemote>(a, item);
+      j = w.blo;
+    }
+  }
+};
+
+// [ROWS x 128] bf16 operand rows -> swizzled halves, issued by one warp
+template <int ROWS, typename RowPtr>
+__device__ __forceinline__ void warp_load_operand(uint32_t sbase, uint32_t half_bytes, RowPtr src, int lane,
+                                                  const void* any_valid) {
+#pragma unroll 4
+  for (int i = 0; i < ROWS * 16 / 32; ++i) {
+    const int id = lane + i * 32;
+    const int r = id >> 4, c = id & 15;
+    const __nv_bfloat16* g = src(r);
+    const uint32_t dst = sbase + (c >> 3) * half_bytes + sw128_off(r, c & 7);
+    cp_async16_zfill(dst, g ? static_cast<const void*>(g + c * 8) : any_valid, g != nullptr);
+  }
+}
+
+// Band epilogue of one row in the warp-specialised kernel: the window-only
+// result, o = O / l (bf16) and lse (ln); merge_partials_kernel folds the
+// remote partials in afterwards.  Called by whole warps (tcgen05.ld is
+// warp-collective).
+__device__ __forceinline__ void band_row_store(const TcArgs& a, int64_t b, int64_t h, int64_t t, bool row_ok,
+                                               float m_ref, float l, uint32_t tm_o_row) {
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float ov[32];
+    tmem_ld32(tm_o_row + 32 * c, ov);
+    tmem_wait_ld();
+    if (row_ok) {
+      __nv_bfloat16* dst = a.o + b * a.sob + t * a.sot + h * a.soh + 32 * c;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float tmp[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
+        store8(dst, 8 * q4, SRSWA_BF16, tmp);
+      }
+    }
+  }
+  if (row_ok && a.lse) a.lse[(b * a.T + t) * a.HQ + h] = l > 0.f ? (m_ref + log2f(l)) * kLn2 : -INFINITY;
+}
+
+// Row-wise log-sum-exp merge of the window result (o, lse, as written by the
+// band pass) with the row's remote partials; one warp per (b, t, h), lane =
+// 4 features.  part_lse is pre-filled with NaN, so a slot that produced no
+// partial (unused, repeated or empty) reads as NaN and needs no look at the
+// selection: every load of the row (window o and lse, the S slot lse values
+// and partial rows) is issued at once.  Partial rows of unused slots are
+// dropped by a select (their bytes are never multiplied in).  Rows without a
+// usable slot keep the window result.  Memory-bound.
+__global__ void __launch_bounds__(256) merge_partials_kernel(const TcArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= a.B * a.T * a.HQ) return;
+  const int64_t h = row % a.HQ, bt = row / a.HQ;
+  const int64_t t = bt % a.T, b = bt / a.T;
+  const int64_t slot_base = (bt * a.S) * a.HQ + h;
+  const int ns = static_cast<int>(a.S < 64 ? a.S : 64);
+  float* lse_p = a.lse + bt * a.HQ + h;
+  __nv_bfloat16* op = a.o + b * a.sob + t * a.sot + h * a.soh + lane * 4;
+  // lane s (and s + 32) owns slot s's lse
+  const float ls0 = lane < ns ? __ldcs(a.part_lse + slot_base + lane * a.HQ) : __int_as_float(0x7fffffff);
+  const float ls1 = lane + 32 < ns ? __ldcs(a.part_lse + slot_base + (lane + 32) * a.HQ) : __int_as_float(0x7fffffff);
+  const float lb = *lse_p * kLog2e;
+  const uint2 ob = *reinterpret_cast<const uint2*>(op);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float M = -INFINITY;
+  const float v0 = (ls0 == ls0) ? ls0 : -INFINITY, v1 = (ls1 == ls1) ? ls1 : -INFINITY;  // NaN -> no partial
+  M = warp_max(fmaxf(v0, v1));
+  if (M == -INFINITY) return;  // no remote slot: the window result stands (warp-uniform)
+  M = fmaxf(M, lb);
+  float den = (v0 == -INFINITY ? 0.f : exp2f(v0 - M)) + (v1 == -INFINITY ? 0.f : exp2f(v1 - M));
+  den = warp_sum(den);
+  const float wb = lb == -INFINITY ? 0.f : exp2f(lb - M);
+  den += wb;
+  acc[0] = wb * bf16_lo(ob.x);
+  acc[1] = wb * bf16_hi(ob.x);
+  acc[2] = wb * bf16_lo(ob.y);
+  acc[3] = wb * bf16_hi(ob.y);
+  for (int g0 = 0; g0 < ns; g0 += 8) {
+    uint2 u[8];
+    float w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int s2 = g0 + k;
+      const float l2 = __shfl_sync(0xffffffffu, s2 < 32 ? v0 : v1, s2 & 31);
+      w[k] = (s2 < ns && l2 != -INFINITY) ? exp2f(l2 - M) : 0.f;
+      u[k] = s2 < ns ? __ldcs(reinterpret_cast<const uint2*>(a.part_o + (slot_base + s2 * a.HQ) * kD + lane * 4))
+                     : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (w[k] != 0.f) {
+        acc[0] = fmaf(w[k], bf16_lo(u[k].x), acc[0]);
+        acc[1] = fmaf(w[k], bf16_hi(u[k].x), acc[1]);
+        acc[2] = fmaf(w[k], bf16_lo(u[k].y), acc[2]);
+        acc[3] = fmaf(w[k], bf16_hi(u[k].y), acc[3]);
+      }
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  __nv_bfloat162 r0 = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
+  __nv_bfloat162 r1 = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
+  uint2 w2;
+  w2.x = *reinterpret_cast<uint32_t*>(&r0);
+  w2.y = *reinterpret_cast<uint32_t*>(&r1);
+  *reinterpret_cast<uint2*>(op) = w2;
+  if (lane == 0) *lse_p = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
+}
+
+// Band epilogue of one row: merge the window softmax state (m_ref, l in
+// log2 units) with the row's remote partials, write o (bf16) and lse (ln).
+// Called by whole warps (tcgen05.ld is warp-collective).
+__device__ __forceinline__ void band_row_epilogue(const TcArgs& a, int64_t b, int64_t h, int64_t hk, int64_t t,
+                                                  bool row_ok, float m_ref, float l, uint32_t tm_o_row) {
+  const int64_t hi = (hk * a.HI) / a.Hkv;
+  float M = (l > 0.f) ? m_ref + log2f(l) : -INFINITY;
+  float lse_s[64];
+  int64_t slot_base = 0;
+  int nslot = 0;
+  if (row_ok && a.part_o) {
+    const int32_t* srow = a.sel + ((b * a.HI + hi) * a.T + t) * a.S;
+    slot_base = ((b * a.T + t) * a.S) * a.HQ + h;
+    for (int64_t s2 = 0; s2 < a.S && s2 < 64; ++s2) {
+      lse_s[s2] = -INFINITY;
+      const int64_t blk = srow[s2];
+      if (blk < 0 || blk >= a.nblk) continue;
+      int64_t lo, hi2;
+      remote_range(a, b, t, blk, lo, hi2);
+      if (lo >= hi2) continue;
+      bool dup = false;
+      for (int64_t u = 0; u < s2; ++u) dup |= srow[u] == blk;
+      if (dup) continue;
+      lse_s[s2] = a.part_lse[slot_base + s2 * a.HQ];
+      M = fmaxf(M, lse_s[s2]);
+    }
+    nslot = static_cast<int>(a.S < 64 ? a.S : 64);
+  }
+  const float Mu = (M == -INFINITY) ? 0.f : M;
+  const float wb = (l > 0.f) ? exp2f(m_ref - Mu) : 0.f;
+  float den = l * wb;
+  for (int s2 = 0; s2 < nslot; ++s2)
+    if (lse_s[s2] != -INFINITY) den += exp2f(lse_s[s2] - Mu);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float ov[32];
+    tmem_ld32(tm_o_row + 32 * c, ov);
+    tmem_wait_ld();
+    if (row_ok) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) ov[i] *= wb;
+      for (int s2 = 0; s2 < nslot; ++s2) {
+        if (lse_s[s2] == -INFINITY) continue;
+        const float w = exp2f(lse_s[s2] - Mu);
+        const uint4* src = reinterpret_cast<const uint4*>(a.part_o + (slot_base + s2 * a.HQ) * kD + 32 * c);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const uint4 u = src[q4];
+          ov[8 * q4 + 0] = fmaf(w, bf16_lo(u.x), ov[8 * q4 + 0]);
+          ov[8 * q4 + 1] = fmaf(w, bf16_hi(u.x), ov[8 * q4 + 1]);
+          ov[8 * q4 + 2] = fmaf(w, bf16_lo(u.y), ov[8 * q4 + 2]);
+          ov[8 * q4 + 3] = fmaf(w, bf16_hi(u.y), ov[8 * q4 + 3]);
+          ov[8 * q4 + 4] = fmaf(w, bf16_lo(u.z), ov[8 * q4 + 4]);
+          ov[8 * q4 + 5] = fmaf(w, bf16_hi(u.z), ov[8 * q4 + 5]);
+          ov[8 * q4 + 6] = fmaf(w, bf16_lo(u.w), ov[8 * q4 + 6]);
+          ov[8 * q4 + 7] = fmaf(w, bf16_hi(u.w), ov[8 * q4 + 7]);
+        }
+      }
+      __nv_bfloat16* dst = a.o + b * a.sob + t * a.sot + h * a.soh + 32 * c;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float tmp[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
+        store8(dst, 8 * q4, SRSWA_BF16, tmp);
+      }
+    }
+  }
+  if (row_ok && a.lse) a.lse[(b * a.T + t) * a.HQ + h] = den > 0.f ? (Mu + log2f(den)) * kLn2 : -INFINITY;
+}
+
+// tmq / tmk / tmv: 4-D tensor maps over q, k, v ([B,T,H,D] with their
+// strides; dims ordered D, T, H, B) with 128-byte swizzle: boxes of 64
+// features x 128 query rows (tmq) or x 64 key rows (tmk, tmv) land in shared
+// memory in the K-major layout the MMAs read.  The gathered q rows of the
+// remote pass are copied with cp.async through a per-tile row table.
+template <bool kRemote>
+__global__ void __launch_bounds__(kWsThreads, 1)
+    fwd_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                  const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t q_full[2], q_empty[2], kv_full[2][2], kv_empty[2][2], s_full[2], p_full[2], o_full[2];
+  __shared__ const __nv_bfloat16* qrows[2][kTileM];
+  // remote pass: each row's (query, slot, bias * log2 e), resolved by the
+  // producer per item (double-buffered by item parity) and published on info_full
+  __shared__ int32_t r_t[2][2][kTileM], r_slot[2][2][kTileM];
+  __shared__ float r_bias[2][2][kTileM];
+  __shared__ uint64_t info_full[2][2];
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  auto q_s = [&](int s) { return sbase + static_cast<uint32_t>(s) * kQBytes; };
+  auto kv_s = [&](int s, int st) { return sbase + 2 * kQBytes + static_cast<uint32_t>(s * 2 + st) * kWsStage; };
+  if (warp == kWsMma) {
+    tmem_alloc(&tmem_base, kWsTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], kRemote ? 32 : 1);
+      mbar_init(&q_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], kTileM);
+      mbar_init(&o_full[s], 1);
+      for (int st = 0; st < 2; ++st) {
+        mbar_init(&kv_full[s][st], 1);
+        mbar_init(&kv_empty[s][st], 1);
+      }
+    }
+    for (int s = 0; s < 2; ++s)
+      for (int pb = 0; pb < 2; ++pb) mbar_init(&info_full[s][pb], 32);
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  volatile int* abort_p = &abort_flag;
+  const int64_t nitems = ws_num_items<kRemote>(a);
+
+  if (warp == kWsProducer) {
+    // ---------------------------------------------------------------- producer
+    WsCursor<kRemote> c[2];
+    c[0].start(a, 0, nitems);
+    c[1].start(a, 1, nitems);
+    bool ok = true;
+    while (ok && !(c[0].done && c[1].done)) {
+      for (int s = 0; s < 2 && ok; ++s) {
+        WsCursor<kRemote>& cs = c[s];
+        if (cs.done) continue;
+        const WsItem& w = cs.w;
+        if (cs.first()) {
+          if (cs.m > 0 &&
+              !__all_sync(0xffffffffu, ws_wait(&q_empty[s], static_cast<uint32_t>((cs.m - 1) & 1), abort_p, 401))) {
+            ok = false;
+            break;
+          }
+          if (kRemote) {
+            // row table: lane L resolves rows L, L+32, L+64, L+96 of the pair tile
+            const int pb = static_cast<int>(cs.m & 1);
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+              const int r = lane + 32 * k4;
+              const __nv_bfloat16* p = nullptr;
+              int32_t tt = -1, sl = 0;
+              float bz = 0.f;
+              if (r < w.cnt) {
+                const int32_t pk = a.pairs[w.first + r];
+                tt = pk / static_cast<int32_t>(a.S);
+                sl = pk - tt * static_cast<int32_t>(a.S);
+                p = a.q + w.b * a.sqb + static_cast<int64_t>(tt) * a.sqt + w.h * a.sqh;
+                if (a.bias) bz = a.bias[(w.b * a.T + tt) * a.S + sl] * kLog2e;
+              }
+              qrows[s][r] = p;
+              r_t[s][pb][r] = tt;
+              r_slot[s][pb][r] = sl;
+              r_bias[s][pb][r] = bz;
+            }
+            mbar_arrive(&info_full[s][pb]);  // release: the row info above
+            __syncwarp();
+            const int c = lane & 15;
+            const uint32_t dst0 = q_s(s) + (c >> 3) * (kQBytes / 2);
+#pragma unroll 8
+            for (int i = 0; i < kTileM / 2; ++i) {
+              const int r = (lane >> 4) + 2 * i;
+              const __nv_bfloat16* g = qrows[s][r];
+              cp_async16_zfill(dst0 + sw128_off(r, c & 7), g ? static_cast<const void*>(g + c * 8) : a.q,
+                               g != nullptr);
+            }
+            cp_async_mbar_arrive(&q_full[s]);
+            __syncwarp();
+          } else if (lane == 0) {
+            mbar_arrive_expect_tx(&q_full[s], kQBytes);
+            tma_load_4d(q_s(s), &tmq, 0, static_cast<int>(w.t0), static_cast<int>(w.h), static_cast<int>(w.b),
+                        &q_full[s]);
+            tma_load_4d(q_s(s) + kQBytes / 2, &tmq, 64, static_cast<int>(w.t0), static_cast<int>(w.h),
+                        static_cast<int>(w.b), &q_full[s]);
+          }
+        }
+        const int st = static_cast<int>(cs.n & 1);
+        if (cs.n >= 2 && !__all_sync(0xffffffffu, ws_wait(&kv_empty[s][st],
+                                                          static_cast<uint32_t>(((cs.n >> 1) - 1) & 1), abort_p,
+                                                          402))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {  // K and V of the block: four 64 x 64 boxes (rows past T read as zeros)
+          const int row0 = static_cast<int>(cs.j * kBlk), hh = static_cast<int>(w.hk), bb = static_cast<int>(w.b);
+          const uint32_t dst = kv_s(s, st);
+          mbar_arrive_expect_tx(&kv_full[s][st], kWsStage);
+          tma_load_4d(dst, &tmk, 0, row0, hh, bb, &kv_full[s][st]);
+          tma_load_4d(dst + kKVHalf, &tmk, 64, row0, hh, bb, &kv_full[s][st]);
+          tma_load_4d(dst + kKVBytes, &tmv, 0, row0, hh, bb, &kv_full[s][st]);
+          tma_load_4d(dst + kKVBytes + kKVHalf, &tmv, 64, row0, hh, bb, &kv_full[s][st]);
+        }
+        __syncwarp();
+        cs.advance(a);
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp == kWsMma) {
+    // --------------------------------------------------------------------- MMA
+    if (lane == 0) {
+      WsCursor<kRemote> c[2];
+      c[0].start(a, 0, nitems);
+      c[1].start(a, 1, nitems);
+      bool pend[2] = {false, false}, pfirst[2] = {false, false}, plast[2] = {false, false};
+      int64_t pn[2] = {0, 0};
+      bool ok = true;
+      auto issue_s = [&](int s) -> bool {
+        WsCursor<kRemote>& cs = c[s];
+        const int st = static_cast<int>(cs.n & 1);
+        if (!ws_wait(&kv_full[s][st], static_cast<uint32_t>((cs.n >> 1) & 1), abort_p, 403)) return false;
+        if (cs.first() && !ws_wait(&q_full[s], static_cast<uint32_t>(cs.m & 1), abort_p, 404)) return false;
+        tc_fence_after();
+        issue_qk(tmem + s * 256, q_s(s), kv_s(s, st));
+        mma_commit(&s_full[s]);
+        if (cs.last()) mma_commit(&q_empty[s]);
+        pend[s] = true;
+        pfirst[s] = cs.first();
+        plast[s] = cs.last();
+        pn[s] = cs.n;
+        cs.advance(a);
+        return true;
+      };
+      auto issue_pv_step = [&](int s) -> bool {
+        if (!ws_wait(&p_full[s], static_cast<uint32_t>(pn[s] & 1), abort_p, 405)) return false;
+        const int st = static_cast<int>(pn[s] & 1);
+        tc_fence_after();
+        issue_pv(tmem + s * 256 + 128, kv_s(s, st), kv_s(s, st) + kKVBytes, !pfirst[s]);
+        mma_commit(&kv_empty[s][st]);
+        if (plast[s]) mma_commit(&o_full[s]);
+        pend[s] = false;
+        return true;
+      };
+      for (int s = 0; s < 2 && ok; ++s)
+        if (!c[s].done) ok = issue_s(s);
+      while (ok && (pend[0] || pend[1])) {
+        for (int s = 0; s < 2 && ok; ++s) {
+          if (pend[s]) ok = issue_pv_step(s);
+          if (ok && !c[s].done) ok = issue_s(s);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------------- softmax
+    const int s = warp >> 2;
+    const int r = tid & (kTileM - 1);
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tm_s = tmem + s * 256 + lane_off, tm_o = tmem + s * 256 + 128 + lane_off;
+    WsCursor<kRemote> cs;
+    cs.start(a, s, nitems);
+    float m_ref = -INFINITY, l = 0.f, bias2 = 0.f;
+    int64_t t = -1, slot = 0, ls = 0, rlo = 0, rhi = 0;
+    bool row_ok = false;
+    while (!cs.done) {
+      const WsItem& w = cs.w;
+      const bool first = cs.first(), last = cs.last();
+      if (first) {
+        m_ref = -INFINITY;
+        l = 0.f;
+        bias2 = 0.f;
+        if (kRemote) {
+          const int pb = static_cast<int>(cs.m & 1);
+          if (!__all_sync(0xffffffffu, ws_wait(&info_full[s][pb], static_cast<uint32_t>((cs.m >> 1) & 1), abort_p,
+                                               409)))
+            break;
+          t = r_t[s][pb][r];
+          slot = r_slot[s][pb][r];
+          bias2 = r_bias[s][pb][r];
+          row_ok = t >= 0;
+          if (row_ok) remote_range(a, w.b, t, w.blo, rlo, rhi);
+        } else {
+          t = w.t0 + r;
+          row_ok = t < a.T;
+          ls = row_ok ? win_start(a, w.b, t) : 0;
+        }
+      }
+      // warp-uniform outcome: the TMEM accesses below are warp-collective
+      if (!__all_sync(0xffffffffu, ws_wait(&s_full[s], static_cast<uint32_t>(cs.n & 1), abort_p, 406))) break;
+      tc_fence_after();
+      float sv[64];
+      {
+        float s0[32], s1[32];
+        tmem_ld32(tm_s, s0);
+        tmem_ld32(tm_s + 32, s1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { sv[i] = s0[i]; sv[32 + i] = s1[i]; }
+      }
+      const int64_t k0 = cs.j * kBlk;
+      int klo = 0, khi = 0;  // this row's valid keys of the block, relative
+      if (row_ok) {
+        klo = clamp_key((kRemote ? rlo : ls) - k0);
+        khi = clamp_key((kRemote ? rhi : t + 1) - k0);
+      }
+      const bool full = __all_sync(0xffffffffu, klo == 0 && khi == kBlk);
+      const float mraw = block_row_max(sv, klo, khi, full);
+      const float mloc = mraw == -INFINITY ? -INFINITY : fmaf(mraw, a.scale_log2, bias2);
+      const bool need = mloc > m_ref + kRescaleLog2;
+      const float alpha = need ? (m_ref == -INFINITY ? 0.f : exp2f(m_ref - mloc)) : 1.f;
+      if (need) {
+        l *= alpha;
+        m_ref = mloc;
+      }
+      if (!kRemote && __any_sync(0xffffffffu, need && !first)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tm_o + 32 * c, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(tm_o + 32 * c, ov);
+        }
+        tmem_wait_st();
+      }
+      l += block_row_exp(sv, a.scale_log2, bias2 - (m_ref == -INFINITY ? 0.f : m_ref));
+      const uint32_t p_s = kv_s(s, static_cast<int>(cs.n & 1));  // P over this stage's dead K
+      store_p_row(p_s, r, 0, sv);
+      store_p_row(p_s, r, 4, sv + 32);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[s]);
+      if (last) {
+        if (!__all_sync(0xffffffffu, ws_wait(&o_full[s], static_cast<uint32_t>(cs.m & 1), abort_p, 407))) break;
+        tc_fence_after();
+        if (kRemote) {
+          const int64_t prow = ((w.b * a.T + (row_ok ? t : 0)) * a.S + slot) * a.HQ + w.h;
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float ov[32];
+            tmem_ld32(tm_o + 32 * c, ov);
+            tmem_wait_ld();
+            if (row_ok) {
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                float tmp[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
+                store8(a.part_o + prow * kD + 32 * c, 8 * q4, SRSWA_BF16, tmp);
+              }
+            }
+          }
+          if (row_ok) a.part_lse[prow] = l > 0.f ? m_ref + log2f(l) : -INFINITY;
+        } else {
+          band_row_store(a, w.b, w.h, t, row_ok, m_ref, l, tm_o);
+        }
+        tc_fence_before();
+      }
+      cs.advance(a);
+    }
+  }
+  // ------------------------------------------------------------------- exit
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWsMma) {
+    if (*abort_p) {  // MMAs may still be in flight: wait for all of them
+      if (lane == 0) {
+        mma_commit(&drain_bar);
+        mbar_wait(&drain_bar, 0, 408);
+      }
+      __syncwarp();
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, kWsTmemCols);
+  }
+}
+
+// ============================================================================
+// Warp-specialised remote pass.  A work item is one selected block of one
+// query head with all of its (query, slot) pairs: K and V are loaded once
+// (TMA) and the pairs go through in tiles of 128 rows whose q rows are
+// gathered with cp.async into a double-buffered Q tile per slot; P overwrites
+// the dead Q tile.  The producer resolves each tile's rows (query, slot,
+// bias) into shared memory for the softmax warps.  Roles and bounded waits as
+// in fwd_ws_kernel; each tile writes its normalised partial (o bf16, lse
+// log2) at the end of its step.
+// ============================================================================
+struct RwCursor {
+  int64_t item, nitems, m, j, n, ntile, pbase, cnt, b, h, hk, blk;
+  bool done;
+  __device__ __forceinline__ void seek(const TcArgs& a) {  // first item with pairs at or after `item`
+    const int64_t hpi = a.HQ / a.HI;
+    while (item < nitems) {
+      const int64_t bhc = item / hpi;
+      const int32_t c = a.count[bhc];
+      if (c > 0) {
+        cnt = c;
+        pbase = a.offs[bhc];
+        ntile = (c + kTileM - 1) / kTileM;
+        const int64_t bh = bhc / a.nblk;
+        blk = bhc % a.nblk;
+        b = bh / a.HI;
+        h = (bh % a.HI) * hpi + item % hpi;
+        hk = h / (a.HQ / a.Hkv);
+        j = 0;
+        done = false;
+        return;
+      }
+      item += 2 * static_cast<int64_t>(gridDim.x);
+    }
+    done = true;
+  }
+  __device__ __forceinline__ void start(const TcArgs& a, int slot) {
+    nitems = a.B * a.HI * a.nblk * (a.HQ / a.HI);
+    item = blockIdx.x + static_cast<int64_t>(slot) * gridDim.x;
+    m = 0;
+    n = 0;
+    seek(a);
+  }
+  __device__ __forceinline__ bool first() const { return j == 0; }
+  __device__ __forceinline__ bool last() const { return j == ntile - 1; }
+  __device__ __forceinline__ int64_t tile_first() const { return pbase + j * kTileM; }
+  __device__ __forceinline__ int64_t tile_rows() const {
+    const int64_t r = cnt - j * kTileM;
+    return r < kTileM ? r : kTileM;
+  }
+  __device__ __forceinline__ void advance(const TcArgs& a) {
+    ++n;
+    if (j + 1 < ntile) {
+      ++j;
+      return;
+    }
+    ++m;
+    item += 2 * static_cast<int64_t>(gridDim.x);
+    seek(a);
+  }
+};
+
+constexpr int kRwThreads = 352;  // + a second producer warp (warp 10): one producer per slot
+__global__ void __launch_bounds__(kRwThreads, 1)
+    remote_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t kv_full[2], kv_empty[2], q_full[2][2], q_empty[2][2], info_full[2][2], info_empty[2][2];
+  __shared__ uint64_t s_full[2], p_full[2], o_full[2], drain_bar;
+  __shared__ const __nv_bfloat16* qrows[2][kTileM];
+  __shared__ int32_t r_t[2][2][kTileM], r_slot[2][2][kTileM];
+  __shared__ float r_bias[2][2][kTileM];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  auto q_buf = [&](int s, int qb) { return sbase + static_cast<uint32_t>(s * 2 + qb) * kQBytes; };
+  auto kv_buf = [&](int s) { return sbase + 4 * kQBytes + static_cast<uint32_t>(s) * kWsStage; };
+  if (warp == kWsMma) {
+    tmem_alloc(&tmem_base, kWsTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], kTileM);
+      mbar_init(&o_full[s], 1);
+      for (int qb = 0; qb < 2; ++qb) {
+        mbar_init(&q_full[s][qb], 32);
+        mbar_init(&q_empty[s][qb], kTileM);
+        mbar_init(&info_full[s][qb], 32);
+        mbar_init(&info_empty[s][qb], kTileM);
+      }
+    }
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  volatile int* abort_p = &abort_flag;
+
+  if (warp == kWsProducer || warp == kWsProducer + 2) {
+    // ------------------------------------------------- producer of one slot
+    const int s = warp == kWsProducer ? 0 : 1;
+    RwCursor cs;
+    cs.start(a, s);
+    // this tile's rows (lane L: rows L, L+32, L+64, L+96), fetched one tile ahead
+    int64_t pq[4];
+    float pbz[4];
+    int32_t ppk[4];
+    auto fetch = [&]() {
+      const int64_t fp = cs.tile_first(), nh = cs.tile_rows();
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const int r = lane + 32 * k4;
+        ppk[k4] = -1;
+        if (r < nh) {
+          pq[k4] = a.pair_q[fp + r];
+          pbz[k4] = a.pair_bias[fp + r];
+          ppk[k4] = a.pairs[fp + r];
+        }
+      }
+    };
+    if (!cs.done) fetch();
+    bool ok = true;
+    while (ok && !cs.done) {
+      if (cs.first()) {
+        if (cs.m > 0 &&
+            !__all_sync(0xffffffffu, ws_wait(&kv_empty[s], static_cast<uint32_t>((cs.m - 1) & 1), abort_p, 421))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const int row0 = static_cast<int>(cs.blk * kBlk), hh = static_cast<int>(cs.hk), bb = static_cast<int>(cs.b);
+          const uint32_t dst = kv_buf(s);
+          mbar_arrive_expect_tx(&kv_full[s], kWsStage);
+          tma_load_4d(dst, &tmk, 0, row0, hh, bb, &kv_full[s]);
+          tma_load_4d(dst + kKVHalf, &tmk, 64, row0, hh, bb, &kv_full[s]);
+          tma_load_4d(dst + kKVBytes, &tmv, 0, row0, hh, bb, &kv_full[s]);
+          tma_load_4d(dst + kKVBytes + kKVHalf, &tmv, 64, row0, hh, bb, &kv_full[s]);
+        }
+        __syncwarp();
+      }
+      const int qb = static_cast<int>(cs.n & 1);
+      if (cs.n >= 2) {
+        const uint32_t par = static_cast<uint32_t>(((cs.n >> 1) - 1) & 1);
+        if (!__all_sync(0xffffffffu, ws_wait(&q_empty[s][qb], par, abort_p, 422) &&
+                                         ws_wait(&info_empty[s][qb], par, abort_p, 423))) {
+          ok = false;
+          break;
+        }
+      }
+      const int64_t hq = cs.h * a.sqh;
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const int r = lane + 32 * k4;
+        const int32_t pk = ppk[k4];
+        const int32_t tt = pk >= 0 ? pk / static_cast<int32_t>(a.S) : -1;
+        qrows[s][r] = pk >= 0 ? a.q + pq[k4] + hq : nullptr;
+        r_t[s][qb][r] = tt;
+        r_slot[s][qb][r] = pk >= 0 ? pk - tt * static_cast<int32_t>(a.S) : 0;
+        r_bias[s][qb][r] = pk >= 0 ? pbz[k4] : 0.f;
+      }
+      mbar_arrive(&info_full[s][qb]);  // release: the row info above
+      __syncwarp();
+      const int cc = lane & 15;
+      const uint32_t dst0 = q_buf(s, qb) + (cc >> 3) * (kQBytes / 2);
+#pragma unroll 8
+      for (int i = 0; i < kTileM / 2; ++i) {
+        const int r = (lane >> 4) + 2 * i;
+        const __nv_bfloat16* g = qrows[s][r];
+        cp_async16_zfill(dst0 + sw128_off(r, cc & 7), g ? static_cast<const void*>(g + cc * 8) : a.q, g != nullptr);
+      }
+      cp_async_mbar_arrive(&q_full[s][qb]);
+      __syncwarp();  // qrows is rewritten by the next tile
+      cs.advance(a);
+      if (!cs.done) fetch();  // next tile's rows in flight while this one's copies land
+    }
+    cp_async_wait_all();
+  } else if (warp == kWsMma) {
+    // --------------------------------------------------------------------- MMA
+    if (lane == 0) {
+      RwCursor c[2];
+      c[0].start(a, 0);
+      c[1].start(a, 1);
+      bool pend[2] = {false, false}, plast[2] = {false, false};
+      int64_t pn[2] = {0, 0};
+      bool ok = true;
+      auto issue_s = [&](int s) -> bool {
+        RwCursor& cs = c[s];
+        const int qb = static_cast<int>(cs.n & 1);
+        if (cs.first() && !ws_wait(&kv_full[s], static_cast<uint32_t>(cs.m & 1), abort_p, 424)) return false;
+        if (!ws_wait(&q_full[s][qb], static_cast<uint32_t>((cs.n >> 1) & 1), abort_p, 425)) return false;
+        tc_fence_after();
+        issue_qk(tmem + s * 256, q_buf(s, qb), kv_buf(s));
+        mma_commit(&s_full[s]);
+        pend[s] = true;
+        plast[s] = cs.last();
+        pn[s] = cs.n;
+        cs.advance(a);
+        return true;
+      };
+      auto issue_pv_step = [&](int s) -> bool {
+        if (!ws_wait(&p_full[s], static_cast<uint32_t>(pn[s] & 1), abort_p, 426)) return false;
+        const int qb = static_cast<int>(pn[s] & 1);
+        tc_fence_after();
+        issue_pv(tmem + s * 256 + 128, q_buf(s, qb), kv_buf(s) + kKVBytes, false);  // P over the dead Q tile
+        mma_commit(&o_full[s]);
+        if (plast[s]) mma_commit(&kv_empty[s]);
+        pend[s] = false;
+        return true;
+      };
+      for (int s = 0; s < 2 && ok; ++s)
+        if (!c[s].done) ok = issue_s(s);
+      while (ok && (pend[0] || pend[1])) {
+        for (int s = 0; s < 2 && ok; ++s) {
+          if (pend[s]) ok = issue_pv_step(s);
+          if (ok && !c[s].done) ok = issue_s(s);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------------- softmax
+    const int s = warp >> 2;
+    const int r = tid & (kTileM - 1);
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tm_s = tmem + s * 256 + lane_off, tm_o = tmem + s * 256 + 128 + lane_off;
+    RwCursor cs;
+    cs.start(a, s);
+    while (!cs.done) {
+      const int qb = static_cast<int>(cs.n & 1);
+      if (!__all_sync(0xffffffffu,
+                      ws_wait(&info_full[s][qb], static_cast<uint32_t>((cs.n >> 1) & 1), abort_p, 427)))
+        break;
+      const int64_t t = r_t[s][qb][r];
+      const int64_t slot = r_slot[s][qb][r];
+      const float bias2 = r_bias[s][qb][r];
+      mbar_arrive(&info_empty[s][qb]);
+      const bool row_ok = t >= 0;
+      int64_t rlo = 0, rhi = 0;
+      if (row_ok) remote_range(a, cs.b, t, cs.blk, rlo, rhi);
+      if (!__all_sync(0xffffffffu, ws_wait(&s_full[s], static_cast<uint32_t>(cs.n & 1), abort_p, 428))) break;
+      tc_fence_after();
+      float sv[64];
+      {
+        float s0[32], s1[32];
+        tmem_ld32(tm_s, s0);
+        tmem_ld32(tm_s + 32, s1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { sv[i] = s0[i]; sv[32 + i] = s1[i]; }
+      }
+      const int64_t k0 = cs.blk * kBlk;
+      const int klo = row_ok ? clamp_key(rlo - k0) : 0, khi = row_ok ? clamp_key(rhi - k0) : 0;
+      const bool full = __all_sync(0xffffffffu, klo == 0 && khi == kBlk);
+      const float mraw = block_row_max(sv, klo, khi, full);
+      const float mx = mraw == -INFINITY ? -INFINITY : fmaf(mraw, a.scale_log2, bias2);
+      const float l = block_row_exp(sv, a.scale_log2, bias2 - (mx == -INFINITY ? 0.f : mx));
+      const uint32_t p_s = q_buf(s, qb);  // Q of this tile is dead once S is in TMEM
+      store_p_row(p_s, r, 0, sv);
+      store_p_row(p_s, r, 4, sv + 32);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[s]);
+      if (!__all_sync(0xffffffffu, ws_wait(&o_full[s], static_cast<uint32_t>(cs.n & 1), abort_p, 429))) break;
+      tc_fence_after();
+      const int64_t prow = row_ok ? ((cs.b * a.T + t) * a.S + slot) * a.HQ + cs.h : -1;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      // stage the normalised rows (bf16) in the dead Q tile, 16-byte chunks
+      // rotated by the row so the row-per-thread writes spread over the banks
+      const uint32_t stg = q_buf(s, qb);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(tm_o + 32 * c, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 hv = __floats2bfloat162_rn(ov[8 * q4 + 2 * e] * inv, ov[8 * q4 + 2 * e + 1] * inv);
+            w4[e] = *reinterpret_cast<uint32_t*>(&hv);
+          }
+          const int k = 4 * c + q4;
+          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(stg + r * 256 + ((k ^ (r & 15)) << 4)),
+                       "r"(w4[0]), "r"(w4[1]), "r"(w4[2]), "r"(w4[3])
+                       : "memory");
+        }
+      }
+      __syncwarp();
+      // this warp's 32 rows leave as whole 256-byte rows, two rows per instruction
+      const int wrow0 = 32 * (warp & 3);
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int rl = 2 * i + (lane >> 4), rr = wrow0 + rl, k = lane & 15;
+        const int64_t pr = __shfl_sync(0xffffffffu, prow, rl);
+        uint4 val;
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                     : "r"(stg + rr * 256 + ((k ^ (rr & 15)) << 4))
+                     : "memory");
+        if (pr >= 0) *reinterpret_cast<uint4*>(a.part_o + pr * kD + k * 8) = val;
+      }
+      if (row_ok) a.part_lse[prow] = l > 0.f ? mx + log2f(l) : -INFINITY;
+      tc_fence_before();            // O read before the next step's P.V overwrites it
+      mbar_arrive(&q_empty[s][qb]);  // the Q tile (staging) may be refilled
+      cs.advance(a);
+    }
+  }
+  // ------------------------------------------------------------------- exit
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWsMma) {
+    if (*abort_p) {
+      if (lane == 0) {
+        mma_commit(&drain_bar);
+        mbar_wait(&drain_bar, 0, 430);
+      }
+      __syncwarp();
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, kWsTmemCols);
+  }
 }
 
 // ============================================================================
@@ -1252,10 +2244,6 @@ __global__ void tc_dbias_reduce_kernel(const TcBwdArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-struct TcLayout {
-  size_t part_o, part_lse, count, offs, cursor, tiles, ntiles, pairs, total;
-  int64_t max_tiles;
-};
 
 static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
@@ -1282,12 +2270,56 @@ TcLayout tc_layout(const srswa_gather_desc* g) {
   off += 256;
   L.pairs = off;
   off += al256(static_cast<size_t>(npairs) * 4);
+  L.lse = off;  // the window lse when the caller asks for none (the merge reads it)
+  off += al256(static_cast<size_t>(g->B * g->T * g->HQ) * 4);
+  L.pair_q = off;
+  off += al256(static_cast<size_t>(npairs) * 8);
+  L.pair_bias = off;
+  off += al256(static_cast<size_t>(npairs) * 4);
   L.total = off;
   return L;
 }
 
+// cuTensorMapEncodeTiled, looked up through the runtime (no libcuda link)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn tmap_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+// Tensor map of a [B, T, H, 128] bf16 tensor with element strides (sb, st, sh):
+// dims (D, T, H, B), box of 64 features x box_rows rows, 128-byte swizzle,
+// out-of-range rows read as zeros.  False when the driver refuses it.
+static bool make_tmap(CUtensorMap* m, const void* base, int64_t B, int64_t T, int64_t H, int64_t sb, int64_t st,
+                      int64_t sh, uint32_t box_rows) {
+  EncodeTiledFn enc = tmap_encoder();
+  if (!enc) return false;
+  auto stride_of = [](int64_t extent, int64_t s_el) -> cuuint64_t {
+    // the coordinate of a size-1 dimension is always 0: any legal stride will do
+    return extent == 1 ? static_cast<cuuint64_t>(256) : static_cast<cuuint64_t>(s_el) * 2;
+  };
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {stride_of(T, st), stride_of(H, sh), stride_of(B, sb)};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool tc_eligible(const srswa_gather_desc* g) {
-  return g->D == kD && g->block_size == kBlk && g->dtype == SRSWA_BF16 && g->S <= 64 && g->T > 0 &&
+  return g->D == kD && g->block_size == kBlk && g->dtype == SRSWA_BF16 && g->S <= 64 && g->T > 0 && g->scale > 0.f &&
          ((g->sqb | g->sqt | g->sqh | g->skb | g->skt | g->skh | g->svb | g->svt | g->svh) & 7) == 0;
 }
 
@@ -1303,11 +2335,14 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   a.v = static_cast<const __nv_bfloat16*>(v);
   a.sqb = g->sqb; a.sqt = g->sqt; a.sqh = g->sqh; a.skb = g->skb; a.skt = g->skt; a.skh = g->skh;
   a.svb = g->svb; a.svt = g->svt; a.svh = g->svh;
-  a.o = static_cast<__nv_bfloat16*>(o); a.sob = sob; a.sot = sot; a.soh = soh; a.lse = lse;
+  a.o = static_cast<__nv_bfloat16*>(o); a.sob = sob; a.sot = sot; a.soh = soh;
+  a.lse = lse ? lse : reinterpret_cast<float*>(ws + L.lse);
   a.sel = sel; a.bias = bias; a.seg = seg;
   a.part_o = reinterpret_cast<__nv_bfloat16*>(ws + L.part_o);
   a.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
   a.pairs = reinterpret_cast<int32_t*>(ws + L.pairs);
+  a.pair_q = reinterpret_cast<int64_t*>(ws + L.pair_q);
+  a.pair_bias = reinterpret_cast<float*>(ws + L.pair_bias);
   a.tiles = reinterpret_cast<int4*>(ws + L.tiles);
   a.ntiles = reinterpret_cast<int32_t*>(ws + L.ntiles);
   a.B = g->B; a.T = g->T; a.HQ = g->HQ; a.Hkv = g->Hkv; a.HI = g->HI; a.S = g->S;
@@ -1317,15 +2352,31 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   int32_t* count = reinterpret_cast<int32_t*>(ws + L.count);
   int32_t* offs = reinterpret_cast<int32_t*>(ws + L.offs);
   int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
+  a.count = count;
+  a.offs = offs;
 
   static bool attr_done = false;
+  static int num_sms = 148;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(band_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBandSmem);
+    cudaError_t e = cudaFuncSetAttribute(remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(fwd_ws_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(band_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBandSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     e = cudaFuncSetAttribute(remote_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRemoteSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     attr_done = true;
   }
+  // warp-specialised TMA path when the driver encodes the tensor maps; the
+  // cp.async tensor-core kernels otherwise
+  alignas(64) CUtensorMap tmq, tmk, tmv;
+  const bool use_ws =
+      make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
+      make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
+      make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk);
   if (g->S > 0) {
     const int64_t nbh = a.B * a.HI * a.nblk;
     SRSWA_CUDA_TRY(cudaMemsetAsync(count, 0, static_cast<size_t>(nbh) * 4, st));
@@ -1338,14 +2389,32 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     pairs_fill_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, cursor,
                                                                                const_cast<int32_t*>(a.pairs));
     SRSWA_CUDA_TRY(cudaGetLastError());
-    remote_fwd_kernel<<<148 * 3, kTcThreads, kRemoteSmem, st>>>(a);
+    if (use_ws) {
+      // slots without a partial read as NaN in the merge
+      SRSWA_CUDA_TRY(cudaMemsetAsync(a.part_lse, 0xff, static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4, st));
+      remote_ws_kernel<<<num_sms, kRwThreads, kWsSmem, st>>>(a, tmk, tmv);
+    }
+    else {
+      remote_fwd_kernel<<<148 * 3, kTcThreads, kRemoteSmem, st>>>(a);
+    }
     SRSWA_CUDA_TRY(cudaGetLastError());
   } else {
     a.part_o = nullptr;
   }
-  dim3 grid(static_cast<unsigned>((g->T + kTileM - 1) / kTileM), static_cast<unsigned>(g->HQ),
-            static_cast<unsigned>(g->B));
-  band_fwd_kernel<<<grid, kTcThreads, kBandSmem, st>>>(a);
+  if (use_ws) {
+    const int64_t band_items = g->B * g->HQ * ((g->T + kTileM - 1) / kTileM);
+    const unsigned band_grid = static_cast<unsigned>(band_items < num_sms ? band_items : num_sms);
+    fwd_ws_kernel<false><<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv);
+    if (a.part_o) {
+      SRSWA_CUDA_TRY(cudaGetLastError());
+      const int64_t rows = g->B * g->T * g->HQ;
+      merge_partials_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+    }
+  } else {
+    dim3 grid(static_cast<unsigned>((g->T + kTileM - 1) / kTileM), static_cast<unsigned>(g->HQ),
+              static_cast<unsigned>(g->B));
+    band_fwd_kernel<<<grid, kTcThreads, kBandSmem, st>>>(a);
+  }
   return srswa_last_launch_status();
 }
 

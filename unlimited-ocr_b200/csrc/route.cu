@@ -899,6 +899,185 @@ __global__ void pack_selection_kernel(const void* sel, int is64, int64_t rows, i
   }
 }
 
+// ============================================================================
+// a2 + a4 for prefill rows (many rows of one sequence, up to 512 blocks):
+// route_tile_kernel, one CTA per 32 consecutive rows of one sequence.
+//   scores  k_bar is staged in 64-block chunks in shared memory (rows padded
+//           to 132 floats: the float4 reads of 8 consecutive lanes hit
+//           distinct bank quads); thread = 4 rows x 2 blocks (lane, lane+32),
+//           fp32 FMAs over d; z = clamp(dot / sqrt(d)) for blocks below the
+//           row's remote bound, SCORE_NEG elsewhere (same values as
+//           route_kernel up to summation order);
+//   select  warp w takes rows 4w..4w+3 one after another: 64-bit keys (x
+//           descending, then block ascending), warp top-M by warp maxima,
+//           the exact entmax / top-K / bias epilogue.
+// ============================================================================
+constexpr int kRtRows = 32;
+constexpr int kRtChunk = 64;
+constexpr int kRtLd = 132;
+constexpr int64_t kRtMaxBlocks = 512;
+
+static size_t route_tile_smem(int64_t nblk) {
+  const size_t ab = static_cast<size_t>(kRtRows + kRtChunk) * kRtLd * 4;   // q tile + k_bar chunk
+  const size_t keys = static_cast<size_t>(8) * nblk * 8;                   // per-warp keys (aliases ab)
+  return (ab > keys ? ab : keys) + static_cast<size_t>(kRtRows) * nblk * 4;  // + scores
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteArgs a) {
+  extern __shared__ __align__(16) float rt_smem[];
+  const int64_t nblk = a.nblk;
+  float* qs = rt_smem;                       // [32][132]
+  float* kb = qs + kRtRows * kRtLd;          // [64][132]
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(rt_smem);  // [8][nblk], after the scores
+  const size_t ab = static_cast<size_t>(kRtRows + kRtChunk) * kRtLd;
+  const size_t kw = static_cast<size_t>(8) * nblk * 2;                        // keys in floats
+  float* zs = rt_smem + (ab > kw ? ab : kw);  // [32][nblk]
+  __shared__ int64_t chi[kRtRows];
+  __shared__ int64_t cmax_s;
+  __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kRtRows;
+  const int64_t seq = n0 / a.rows_per_seq;  // all 32 rows share it (rows_per_seq % 32 == 0)
+  if (tid < kRtRows) {
+    const int64_t n = n0 + tid;
+    int64_t c_hi = 0;
+    if (n < a.N) {
+      const int64_t p = a.q_pos ? a.q_pos[n]
+                                : static_cast<int64_t>(a.seq_lens[seq]) - a.rows_per_seq + n % a.rows_per_seq;
+      c_hi = p >= 0 ? p / a.BS - a.L + 1 : 0;
+      if (c_hi < 0) c_hi = 0;
+      if (c_hi > nblk) c_hi = nblk;
+      if (a.seq_lens) {
+        const int64_t nb = (static_cast<int64_t>(a.seq_lens[seq]) + a.BS - 1) / a.BS;
+        if (c_hi > nb) c_hi = nb;
+      }
+    }
+    chi[tid] = c_hi;
+    int64_t m = c_hi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int64_t y = __shfl_xor_sync(0xffffffffu, m, o);
+      m = y > m ? y : m;
+    }
+    if (tid == 0) cmax_s = m;
+  }
+  // q tile (fp32): 32 rows x 128 = 1024 float4
+  for (int i = tid; i < kRtRows * 32; i += kRouteThreads) {
+    const int r = i >> 5, u = i & 31;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (n0 + r < a.N) load4(a.q, (n0 + r) * a.s_q + 4 * u, a.q_dtype, v);
+    *reinterpret_cast<float4*>(qs + r * kRtLd + 4 * u) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+  __syncthreads();
+  const int64_t cmax = cmax_s;
+  const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
+  const int r0 = warp * 4;
+  for (int64_t c0 = 0; c0 < nblk; c0 += kRtChunk) {
+    if (c0 >= cmax) {  // no row has remote blocks here: sentinel scores only
+      for (int i = tid; i < kRtRows * kRtChunk; i += kRouteThreads) {
+        const int r = i / kRtChunk;
+        const int64_t c = c0 + i % kRtChunk;
+        if (c < nblk) zs[r * nblk + c] = kScoreNeg;
+      }
+      continue;
+    }
+    for (int i = tid; i < kRtChunk * 32; i += kRouteThreads) {
+      const int j = i >> 5, u = i & 31;
+      const int64_t c = c0 + j;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < cmax) v = __ldg(reinterpret_cast<const float4*>(a.kbar + seq * a.s_kbar_b + c * a.s_kbar_c + 4 * u));
+      *reinterpret_cast<float4*>(kb + j * kRtLd + 4 * u) = v;
+    }
+    __syncthreads();
+    float acc[4][2];
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) acc[rr][0] = acc[rr][1] = 0.f;
+#pragma unroll 4
+    for (int d4 = 0; d4 < 32; ++d4) {
+      const float4 k0v = *reinterpret_cast<const float4*>(kb + lane * kRtLd + 4 * d4);
+      const float4 k1v = *reinterpret_cast<const float4*>(kb + (lane + 32) * kRtLd + 4 * d4);
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+        const float4 qv = *reinterpret_cast<const float4*>(qs + (r0 + rr) * kRtLd + 4 * d4);
+        acc[rr][0] = fmaf(qv.x, k0v.x, acc[rr][0]);
+        acc[rr][0] = fmaf(qv.y, k0v.y, acc[rr][0]);
+        acc[rr][0] = fmaf(qv.z, k0v.z, acc[rr][0]);
+        acc[rr][0] = fmaf(qv.w, k0v.w, acc[rr][0]);
+        acc[rr][1] = fmaf(qv.x, k1v.x, acc[rr][1]);
+        acc[rr][1] = fmaf(qv.y, k1v.y, acc[rr][1]);
+        acc[rr][1] = fmaf(qv.z, k1v.z, acc[rr][1]);
+        acc[rr][1] = fmaf(qv.w, k1v.w, acc[rr][1]);
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const int r = r0 + rr;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int64_t c = c0 + lane + 32 * h;
+        if (c >= nblk) continue;
+        const float sdot = acc[rr][h];
+        float z = fminf(fmaxf(sdot * inv_sqrt_d, -kActClamp), kActClamp);
+        if (sdot != sdot) z = sdot;
+        zs[r * nblk + c] = c < chi[r] ? z : kScoreNeg;
+      }
+    }
+    __syncthreads();  // k_bar chunk reuse
+  }
+  __syncthreads();
+  // ---- selection: warp w, rows 4w .. 4w+3 ----
+  unsigned long long* wk = keys + static_cast<int64_t>(warp) * nblk;
+  const int M = static_cast<int>(a.M);
+  for (int rr = 0; rr < 4; ++rr) {
+    const int r = r0 + rr;
+    const int64_t n = n0 + r;
+    if (n >= a.N) break;  // warp-uniform
+    const float* z = zs + r * nblk;
+    int found = 1;
+    if (a.cand) {
+      int f = 0;
+      for (int64_t c = lane; c < nblk; c += 32) f |= (z[c] > kScoreNeg * 0.5f) && a.cand[n * a.s_cand + c] != 0;
+      found = __any_sync(0xffffffffu, f);
+    }
+    for (int64_t c = lane; c < nblk; c += 32) {
+      const float zc = z[c];
+      if (a.scores_out) a.scores_out[n * nblk + c] = zc;
+      const bool remote = zc > kScoreNeg * 0.5f;  // NaN -> not remote
+      const bool cm = remote && (a.cand == nullptr || !found || a.cand[n * a.s_cand + c] != 0);
+      float x = cm ? zc * a.idx_scale : kEntmaxNeg;
+      if (!isfinite(x)) x = kEntmaxNeg;
+      wk[c] = pack_key(x, c, cm);
+    }
+    __syncwarp();
+    warp_topm_smem(wk, static_cast<int>(nblk), M, lists[warp], lane);
+    __syncwarp();
+    float sel_v = 0.f;
+    int sel_i = -1;
+    bool sel_c = false;
+    if (lane < M) unpack_key(lists[warp][lane], sel_v, sel_i, sel_c);
+    route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+    __syncwarp();
+  }
+}
+
+static bool use_tile(const RouteArgs& a) {
+  return !a.from_scores && a.block_table == nullptr && a.d == 128 && a.nblk <= kRtMaxBlocks &&
+         a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0;
+}
+
+static int route_tile_launch(const RouteArgs& a, cudaStream_t st) {
+  const size_t smem = route_tile_smem(a.nblk);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(route_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  const int64_t grid = a.N / kRtRows;
+  if (grid >= (1ll << 31)) return SRSWA_ETOOLARGE;
+  route_tile_kernel<<<static_cast<unsigned>(grid), kRouteThreads, smem, st>>>(a);
+  return srswa_last_launch_status();
+}
+
 static bool use_wide(const RouteArgs& a) { return a.nblk >= 512 && a.nblk <= kWideMaxBlocks; }
 
 static size_t chunk_workspace(int64_t N, int64_t nblk) {
@@ -937,6 +1116,8 @@ static int route_chunk_launch(RouteArgs a, void* ws, size_t ws_bytes, cudaStream
 
 static int route_launch(RouteArgs a, cudaStream_t st, void* ws = nullptr, size_t ws_bytes = 0) {
   if (a.N == 0) return 0;
+  // prefill rows: many rows of one sequence sharing a contiguous k_bar
+  if (use_tile(a)) return route_tile_launch(a, st);
   // decode-shaped rows with many candidate blocks -> chunked score + merge
   if (use_chunked(a)) return route_chunk_launch(a, ws, ws_bytes, st);
   if (a.from_scores && use_wide(a)) return select_wide_launch(a, a.scores_in, a.s_sc, st);

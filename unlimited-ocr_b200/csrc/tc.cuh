@@ -184,6 +184,23 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// ------------------------------------------------------------------- TMA --
+// arrive on the barrier and add `bytes` to the transaction count of its phase
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// 4-D tiled TMA load (no multicast) of the tensor map's box at coordinates
+// (c0 innermost .. c3) into shared memory; completion counted in bytes on bar
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // byte offset of 16-byte chunk c (0..7) of row r inside a 128B-swizzled tile
 __host__ __device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) {
   return r * 128u + ((c ^ (r & 7u)) << 4);
