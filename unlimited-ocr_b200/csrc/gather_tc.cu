@@ -1902,6 +1902,360 @@ __global__ void __launch_bounds__(kTcThreads) bwd_remote_kernel(const TcBwdArgs 
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
+// ---- remote pairs, warp-specialised -------------------------------------
+// Same work items as bwd_remote_kernel: one item = one selected block of one
+// query head with all of its (query, slot) pairs, in tiles of 128.
+//   warps 0-3  compute (thread = pair row): P and dS = P (dP - delta) from
+//              S and dP in TMEM, the row's d_bias partial, P and dS (bf16)
+//              to shared memory, then the row's dQ partial from TMEM, and at
+//              the end of an item this block's dK / dV (thread = feature);
+//   warps 4-5  producers: cp.async gathers of the tile's q and dO rows into
+//              a double-buffered tile (warp 4 rows 0-63, warp 5 rows
+//              64-127), the rows' (query, slot) into shared memory, and (warp
+//              4) the item's K and V by TMA;
+//   warp 6     MMA issuer: S = Q K^T, dP = dO V^T; dQ = dS K; dV^T += dO^T P,
+//              dK^T += Q^T dS accumulated over the item's tiles in TMEM.  The
+//              next tile's S / dP (same item) is issued before this tile's
+//              dQ / dV / dK so the tensor pipe works while the compute warps do.
+// All waits bounded; abort protocol as in fwd_ws_kernel.
+constexpr int kRbThreads = 224;
+constexpr int kRbMma = 6;
+constexpr uint32_t kRbQD = 2 * kTile128;                        // q tile + dO tile
+constexpr uint32_t kRbSmem = 2 * kRbQD + 2 * kKVBytes + 2 * kPBytes + 1024;  // 193 KB
+
+struct RbCursor {  // the remote work items of the backward (same order for every role)
+  int64_t item, nitems, m, j, n, ntile, pbase, cnt, b, h, hk, blk;
+  bool done;
+  __device__ __forceinline__ void seek(const TcBwdArgs& a) {
+    const TcArgs& f = a.f;
+    const int64_t hpi = f.HQ / f.HI;
+    while (item < nitems) {
+      const int64_t bhc = item / hpi;
+      const int32_t c = a.count[bhc];
+      if (c > 0) {
+        cnt = c;
+        pbase = a.offs[bhc];
+        ntile = (c + kTileM - 1) / kTileM;
+        const int64_t bh = bhc / f.nblk;
+        blk = bhc % f.nblk;
+        b = bh / f.HI;
+        h = (bh % f.HI) * hpi + item % hpi;
+        hk = h / (f.HQ / f.Hkv);
+        j = 0;
+        done = false;
+        return;
+      }
+      item += gridDim.x;
+    }
+    done = true;
+  }
+  __device__ __forceinline__ void start(const TcBwdArgs& a) {
+    nitems = a.f.B * a.f.HI * a.f.nblk * (a.f.HQ / a.f.HI);
+    item = blockIdx.x;
+    m = 0;
+    n = 0;
+    seek(a);
+  }
+  __device__ __forceinline__ bool first() const { return j == 0; }
+  __device__ __forceinline__ bool last() const { return j == ntile - 1; }
+  __device__ __forceinline__ int64_t tile_first() const { return pbase + j * kTileM; }
+  __device__ __forceinline__ int64_t tile_rows() const {
+    const int64_t r = cnt - j * kTileM;
+    return r < kTileM ? r : kTileM;
+  }
+  __device__ __forceinline__ void advance(const TcBwdArgs& a) {
+    ++n;
+    if (j + 1 < ntile) {
+      ++j;
+      return;
+    }
+    ++m;
+    item += gridDim.x;
+    seek(a);
+  }
+};
+
+__global__ void __launch_bounds__(kRbThreads, 1)
+    bwd_remote_ws_kernel(const TcBwdArgs a, const __grid_constant__ CUtensorMap tmk,
+                         const __grid_constant__ CUtensorMap tmv) {
+  const TcArgs& f = a.f;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t kv_full, kv_empty, q_full[2], q_empty[2], info_full[2], info_empty[2];
+  __shared__ uint64_t s_full, p_full, pds_empty, o_full, dq_empty, dkv_full, dkv_empty, drain_bar;
+  __shared__ const __nv_bfloat16* qrows[kTileM];
+  __shared__ const __nv_bfloat16* grows[kTileM];
+  __shared__ int32_t r_t[2][kTileM], r_slot[2][kTileM];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  auto qd_buf = [&](int bq) { return sbase + static_cast<uint32_t>(bq) * kRbQD; };  // q tile, dO tile after it
+  const uint32_t k_s = sbase + 2 * kRbQD, v_s = k_s + kKVBytes;
+  const uint32_t p_s = v_s + kKVBytes, ds_s = p_s + kPBytes;
+  if (warp == kRbMma) {
+    tmem_alloc(&tmem_base, kWsTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&kv_full, 1);
+    mbar_init(&kv_empty, 1);
+    for (int bq = 0; bq < 2; ++bq) {
+      mbar_init(&q_full[bq], 64);
+      mbar_init(&q_empty[bq], 1);
+      mbar_init(&info_full[bq], 64);
+      mbar_init(&info_empty[bq], kTileM);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&p_full, kTileM);
+    mbar_init(&pds_empty, 1);
+    mbar_init(&o_full, 1);
+    mbar_init(&dq_empty, kTileM);
+    mbar_init(&dkv_full, 1);
+    mbar_init(&dkv_empty, kTileM);
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t tm_s = tmem, tm_dp = tmem + 64, tm_dq = tmem + 128, tm_dvt = tmem + 256, tm_dkt = tmem + 320;
+  volatile int* abort_p = &abort_flag;
+
+  if (warp == 4 || warp == 5) {
+    // ---------------------------------------------------------- producers
+    const int half = warp - 4;  // rows 64*half .. 64*half + 63
+    RbCursor cs;
+    cs.start(a);
+    int32_t ppk[2];
+    auto fetch = [&]() {
+      const int64_t fp = cs.tile_first(), nh = cs.tile_rows();
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int r = 64 * half + lane + 32 * k2;
+        ppk[k2] = r < nh ? a.f.pairs[fp + r] : -1;
+      }
+    };
+    if (!cs.done) fetch();
+    bool ok = true;
+    while (ok && !cs.done) {
+      if (cs.first()) {
+        if (cs.m > 0 && !__all_sync(0xffffffffu, ws_wait(&kv_empty, static_cast<uint32_t>((cs.m - 1) & 1), abort_p, 441))) {
+          ok = false;
+          break;
+        }
+        if (half == 0 && lane == 0) {
+          const int row0 = static_cast<int>(cs.blk * kBlk), hh = static_cast<int>(cs.hk), bb = static_cast<int>(cs.b);
+          mbar_arrive_expect_tx(&kv_full, 2 * kKVBytes);
+          tma_load_4d(k_s, &tmk, 0, row0, hh, bb, &kv_full);
+          tma_load_4d(k_s + kKVHalf, &tmk, 64, row0, hh, bb, &kv_full);
+          tma_load_4d(v_s, &tmv, 0, row0, hh, bb, &kv_full);
+          tma_load_4d(v_s + kKVHalf, &tmv, 64, row0, hh, bb, &kv_full);
+        }
+        __syncwarp();
+      }
+      const int bq = static_cast<int>(cs.n & 1);
+      if (cs.n >= 2) {
+        const uint32_t par = static_cast<uint32_t>(((cs.n >> 1) - 1) & 1);
+        if (!__all_sync(0xffffffffu, ws_wait(&q_empty[bq], par, abort_p, 442) &&
+                                         ws_wait(&info_empty[bq], par, abort_p, 443))) {
+          ok = false;
+          break;
+        }
+      }
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int r = 64 * half + lane + 32 * k2;
+        const int32_t pk = ppk[k2];
+        const int32_t tt = pk >= 0 ? pk / static_cast<int32_t>(f.S) : -1;
+        qrows[r] = pk >= 0 ? f.q + cs.b * f.sqb + static_cast<int64_t>(tt) * f.sqt + cs.h * f.sqh : nullptr;
+        grows[r] = pk >= 0 ? a.dout + cs.b * f.sob + static_cast<int64_t>(tt) * f.sot + cs.h * f.soh : nullptr;
+        r_t[bq][r] = tt;
+        r_slot[bq][r] = pk >= 0 ? pk - tt * static_cast<int32_t>(f.S) : 0;
+      }
+      mbar_arrive(&info_full[bq]);
+      __syncwarp();
+      const int cc = lane & 15;
+      const uint32_t qdst = qd_buf(bq) + (cc >> 3) * (kTile128 / 2);
+      const uint32_t gdst = qdst + kTile128;
+#pragma unroll 4
+      for (int i = 0; i < 32; ++i) {
+        const int r = 64 * half + (lane >> 4) + 2 * i;
+        const __nv_bfloat16* gq = qrows[r];
+        const __nv_bfloat16* gg = grows[r];
+        cp_async16_zfill(qdst + sw128_off(r, cc & 7), gq ? static_cast<const void*>(gq + cc * 8) : f.q, gq != nullptr);
+        cp_async16_zfill(gdst + sw128_off(r, cc & 7), gg ? static_cast<const void*>(gg + cc * 8) : f.q, gg != nullptr);
+      }
+      cp_async_mbar_arrive(&q_full[bq]);
+      __syncwarp();
+      cs.advance(a);
+      if (!cs.done) fetch();
+    }
+    cp_async_wait_all();
+  } else if (warp == kRbMma) {
+    // -------------------------------------------------------------------- MMA
+    if (lane == 0) {
+      RbCursor cs;
+      cs.start(a);
+      bool ok = !cs.done;
+      // S / dP of the cursor's current tile
+      auto issue_sdp = [&]() -> bool {
+        const int bq = static_cast<int>(cs.n & 1);
+        if (cs.first() && !ws_wait(&kv_full, static_cast<uint32_t>(cs.m & 1), abort_p, 444)) return false;
+        if (!ws_wait(&q_full[bq], static_cast<uint32_t>((cs.n >> 1) & 1), abort_p, 445)) return false;
+        tc_fence_after();
+        issue_qk(tm_s, qd_buf(bq), k_s);
+        issue_qk(tm_dp, qd_buf(bq) + kTile128, v_s);
+        mma_commit(&s_full);
+        return true;
+      };
+      if (ok) ok = issue_sdp();
+      while (ok && !cs.done) {
+        const int64_t n = cs.n, m = cs.m;
+        const int bq = static_cast<int>(n & 1);
+        const bool first = cs.first(), last = cs.last();
+        if (!ws_wait(&p_full, static_cast<uint32_t>(n & 1), abort_p, 446)) break;
+        cs.advance(a);  // cs now names the next tile
+        const bool next_same_item = !cs.done && cs.m == m;
+        if (next_same_item && !(ok = issue_sdp())) break;
+        if (n > 0 && !ws_wait(&dq_empty, static_cast<uint32_t>((n - 1) & 1), abort_p, 447)) break;
+        tc_fence_after();
+        issue_pv(tm_dq, ds_s, k_s, false);  // dQ = dS K
+        mma_commit(&o_full);
+        if (first && m > 0 && !ws_wait(&dkv_empty, static_cast<uint32_t>((m - 1) & 1), abort_p, 448)) break;
+        tc_fence_after();
+        issue_tn(tm_dvt, qd_buf(bq) + kTile128, kTile128 / 2, p_s, !first);  // dV^T += dO^T P
+        issue_tn(tm_dkt, qd_buf(bq), kTile128 / 2, ds_s, !first);            // dK^T += Q^T dS
+        mma_commit(&pds_empty);
+        mma_commit(&q_empty[bq]);
+        if (last) {
+          mma_commit(&dkv_full);
+          mma_commit(&kv_empty);
+        }
+        if (!cs.done && !next_same_item && !(ok = issue_sdp())) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ---------------------------------------------------------------- compute
+    const int r = tid;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    RbCursor cs;
+    cs.start(a);
+    while (!cs.done) {
+      const int64_t n = cs.n;
+      const int bq = static_cast<int>(n & 1);
+      if (!__all_sync(0xffffffffu, ws_wait(&info_full[bq], static_cast<uint32_t>((n >> 1) & 1), abort_p, 449))) break;
+      const int64_t t = r_t[bq][r], slot = r_slot[bq][r];
+      mbar_arrive(&info_empty[bq]);
+      const bool row_ok = t >= 0;
+      float lse2 = 0.f, dlt = 0.f, bias2 = 0.f;
+      int64_t rlo = 0, rhi = 0;
+      if (row_ok) {  // in flight while S and dP land
+        lse2 = a.lse[(cs.b * f.T + t) * f.HQ + cs.h] * kLog2e;
+        dlt = a.delta[(cs.b * f.T + t) * f.HQ + cs.h];
+        if (f.bias) bias2 = f.bias[(cs.b * f.T + t) * f.S + slot] * kLog2e;
+        remote_range(f, cs.b, t, cs.blk, rlo, rhi);
+      }
+      if (!__all_sync(0xffffffffu, ws_wait(&s_full, static_cast<uint32_t>(n & 1), abort_p, 450))) break;
+      tc_fence_after();
+      float sv[64], dp[64];
+      {
+        float x0[32], x1[32];
+        tmem_ld32(tm_s + lane_off, x0);
+        tmem_ld32(tm_s + lane_off + 32, x1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
+        tmem_ld32(tm_dp + lane_off, x0);
+        tmem_ld32(tm_dp + lane_off + 32, x1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
+      }
+      const int64_t k0 = cs.blk * kBlk;
+      const int klo = row_ok ? clamp_key(rlo - k0) : 0, khi = row_ok ? clamp_key(rhi - k0) : 0;
+      const float off = bias2 - lse2;
+      float dsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const bool valid = i >= klo && i < khi && lse2 != -INFINITY;
+        const float pv = valid ? fast_exp2(fmaf(sv[i], f.scale_log2, off)) : 0.f;
+        const float ds = pv * (dp[i] - dlt);
+        sv[i] = pv;
+        dp[i] = ds;
+        dsum += ds;
+      }
+      // P and dS of the previous tile are read by its dV / dK MMAs: wait for them
+      if (n > 0 && !__all_sync(0xffffffffu, ws_wait(&pds_empty, static_cast<uint32_t>((n - 1) & 1), abort_p, 451)))
+        break;
+      store_p_row(p_s, r, 0, sv);
+      store_p_row(p_s, r, 4, sv + 32);
+      store_p_row(ds_s, r, 0, dp);
+      store_p_row(ds_s, r, 4, dp + 32);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full);
+      if (row_ok && a.dbias_part) a.dbias_part[((cs.b * f.T + t) * f.S + slot) * f.HQ + cs.h] = dsum;
+      if (!__all_sync(0xffffffffu, ws_wait(&o_full, static_cast<uint32_t>(n & 1), abort_p, 452))) break;
+      tc_fence_after();
+      const int64_t prow = ((cs.b * f.T + (row_ok ? t : 0)) * f.S + slot) * f.HQ + cs.h;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(tm_dq + lane_off + 32 * c, ov);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            float tmp[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * a.scale;
+            store8(a.dq_part + prow * kD + 32 * c, 8 * q4, SRSWA_BF16, tmp);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&dq_empty);
+      if (cs.last()) {  // this block's remote dK / dV for the item's head: thread = feature
+        if (!__all_sync(0xffffffffu, ws_wait(&dkv_full, static_cast<uint32_t>(cs.m & 1), abort_p, 453))) break;
+        tc_fence_after();
+        float* dst = a.dkv_part + ((cs.b * f.HQ + cs.h) * f.nblk + cs.blk) * (2 * 64 * 128);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float kv[32], vv[32];
+          tmem_ld32(tm_dkt + lane_off + 32 * hf, kv);
+          tmem_ld32(tm_dvt + lane_off + 32 * hf, vv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            dst[(32 * hf + i) * 128 + r] = kv[i] * a.scale;
+            dst[8192 + (32 * hf + i) * 128 + r] = vv[i];
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&dkv_empty);
+      }
+      cs.advance(a);
+    }
+  }
+  // ------------------------------------------------------------------- exit
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kRbMma) {
+    if (*abort_p) {
+      if (lane == 0) {
+        mma_commit(&drain_bar);
+        mbar_wait(&drain_bar, 0, 454);
+      }
+      __syncwarp();
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, kWsTmemCols);
+  }
+}
+
 // ---- band dK / dV: one CTA per (batch, kv head, 128-key tile) -------------
 constexpr uint32_t kBDSmem = 6 * kTile128 + 1024;
 
@@ -2497,16 +2851,25 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   a.count = remote ? count : nullptr;
   a.offs = offs;
 
+  static int num_sms = 148;
   static bool attr_done = false;
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(bwd_remote_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRBSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(bwd_remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRbSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     e = cudaFuncSetAttribute(bwd_band_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBDSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     e = cudaFuncSetAttribute(bwd_band_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBQSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done = true;
   }
+  // TMA for the remote pass's K / V when the driver encodes the tensor maps
+  alignas(64) CUtensorMap tmk, tmv;
+  const bool use_tma = make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
+                       make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk);
   const int64_t nrows_h = g->B * g->T * g->HQ;
   tc_delta_kernel<<<static_cast<unsigned>((nrows_h + 7) / 8), 256, 0, st>>>(a);
   SRSWA_CUDA_TRY(cudaGetLastError());
@@ -2527,7 +2890,8 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     SRSWA_CUDA_TRY(cudaGetLastError());
     if (a.dbias_part)
       SRSWA_CUDA_TRY(cudaMemsetAsync(a.dbias_part, 0, static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4, st));
-    bwd_remote_kernel<<<148, kTcThreads, kRBSmem, st>>>(a);
+    if (use_tma) bwd_remote_ws_kernel<<<num_sms, kRbThreads, kRbSmem, st>>>(a, tmk, tmv);
+    else bwd_remote_kernel<<<148, kTcThreads, kRBSmem, st>>>(a);
     SRSWA_CUDA_TRY(cudaGetLastError());
   }
   const unsigned ntile = static_cast<unsigned>((g->T + kTileM - 1) / kTileM);
