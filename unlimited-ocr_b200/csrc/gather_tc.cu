@@ -1688,33 +1688,60 @@ __global__ void bwd_pairs_count_kernel(const TcArgs a, const uint32_t* bitmap, i
   if (lane == 0) count[seg] = n;
 }
 
-// one warp per list: emit (t * S + first slot holding the block) in t order
-__global__ void bwd_pairs_fill_kernel(const TcArgs a, const uint32_t* bitmap, int64_t T32, const int32_t* offs,
-                                      int32_t* pairs) {
-  const int lane = threadIdx.x & 31;
-  const int64_t seg = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (seg >= a.B * a.HI * a.nblk) return;
+// one CTA per list: emit (t * S + first slot holding the block) in t order.
+// Warp w owns a contiguous eighth of the list's words; the warps' counts are
+// scanned in shared memory, then each warp emits its pairs in order.
+__device__ __forceinline__ int32_t first_slot(const int32_t* srow, int64_t S, int64_t blk) {
+  int32_t found = static_cast<int32_t>(S);
+  if ((S & 3) == 0 && (reinterpret_cast<uintptr_t>(srow) & 15) == 0) {
+    const int4* v = reinterpret_cast<const int4*>(srow);
+    for (int64_t q = S / 4 - 1; q >= 0; --q) {  // backwards: the first match wins
+      const int4 x = v[q];
+      const int32_t b4 = static_cast<int32_t>(4 * q);
+      found = x.w == blk ? b4 + 3 : found;
+      found = x.z == blk ? b4 + 2 : found;
+      found = x.y == blk ? b4 + 1 : found;
+      found = x.x == blk ? b4 : found;
+    }
+  } else {
+    for (int64_t q = S - 1; q >= 0; --q) found = srow[q] == blk ? static_cast<int32_t>(q) : found;
+  }
+  return found;
+}
+
+__global__ void __launch_bounds__(256) bwd_pairs_fill_kernel(const TcArgs a, const uint32_t* bitmap, int64_t T32,
+                                                             const int32_t* offs, int32_t* pairs) {
+  __shared__ int32_t wcount[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t seg = blockIdx.x;
+  if (seg >= a.B * a.HI * a.nblk) return;  // CTA-uniform
   const int64_t blk = seg % a.nblk, bh = seg / a.nblk;
   const uint32_t* w = bitmap + seg * T32;
+  const int64_t per = (T32 + 7) / 8;
+  const int64_t wlo = warp * per, whi = min(T32, wlo + per);
+  int n = 0;
+  for (int64_t i = wlo + lane; i < whi; i += 32) n += __popc(w[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+  if (lane == 0) wcount[warp] = n;
+  __syncthreads();
   int64_t pos = offs[seg];
-  for (int64_t w0 = 0; w0 < T32; w0 += 32) {
-    uint32_t word = (w0 + lane < T32) ? w[w0 + lane] : 0u;
-    const int n = __popc(word);
-    int incl = n;
+  for (int u = 0; u < warp; ++u) pos += wcount[u];
+  for (int64_t w0 = wlo; w0 < whi; w0 += 32) {
+    uint32_t word = (w0 + lane < whi) ? w[w0 + lane] : 0u;
+    const int nb = __popc(word);
+    int incl = nb;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    int64_t p = pos + incl - n;
+    int64_t p = pos + incl - nb;
     while (word) {
       const int bit = __ffs(word) - 1;
       word &= word - 1;
       const int64_t t = (w0 + lane) * 32 + bit;
-      const int32_t* srow = a.sel + (bh * a.T + t) * a.S;
-      int64_t s = 0;
-      while (s < a.S && srow[s] != blk) ++s;
-      pairs[p++] = static_cast<int32_t>(t * a.S + s);
+      pairs[p++] = static_cast<int32_t>(t * a.S + first_slot(a.sel + (bh * a.T + t) * a.S, a.S, blk));
     }
     pos += __shfl_sync(0xffffffffu, incl, 31);
   }
@@ -2587,6 +2614,316 @@ __global__ void __launch_bounds__(kTcThreads) bwd_band_dq_kernel(const TcBwdArgs
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
+// ---- band dQ, warp-specialised: one work item = (b, h, 128-query tile) -----
+//   warps 0-3  compute (thread = query row): P = 2^(s c - lse), dS = P (dP -
+//              delta) over the window keys, dS (bf16) over the stage's dead V;
+//              after the item's last block, dQ (window part) from TMEM;
+//   warp 4     producer: TMA of the tile's q and dO (per item) and of each
+//              window block's K and V into a 3-stage ring;
+//   warp 5     MMA issuer: S = Q K^T and dP = dO V^T into one of two TMEM
+//              buffers (the next block's run while the compute warps work
+//              on this one), dQ += dS K.
+// The remote dQ partials are added by dq_merge_kernel.
+constexpr int kBqThreads = 192;
+constexpr int kBqStages = 3;
+constexpr uint32_t kBqSmem = 2 * kTile128 + kBqStages * 2 * kKVBytes + 1024;  // 161 KB
+
+__global__ void __launch_bounds__(kBqThreads, 1)
+    bwd_band_dq_ws_kernel(const TcBwdArgs a, const __grid_constant__ CUtensorMap tmq,
+                          const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmk,
+                          const __grid_constant__ CUtensorMap tmv) {
+  const TcArgs& f = a.f;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // p_full per S / dP buffer: the MMA issues the next block's S / dP before it
+  // waits for this block's dS, so one barrier could be completed twice ahead
+  __shared__ uint64_t q_full, q_empty, kv_full[kBqStages], kv_empty[kBqStages], s_full[2], p_full[2], o_full, dq_empty;
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t q_s = sbase, do_s = sbase + kTile128;
+  auto k_s = [&](int st) { return sbase + 2 * kTile128 + static_cast<uint32_t>(st) * 2 * kKVBytes; };
+  if (warp == 5) {
+    tmem_alloc(&tmem_base, kWsTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
+    for (int st = 0; st < kBqStages; ++st) {
+      mbar_init(&kv_full[st], 1);
+      mbar_init(&kv_empty[st], 1);
+    }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(&p_full[0], kTileM);
+    mbar_init(&p_full[1], kTileM);
+    mbar_init(&o_full, 1);
+    mbar_init(&dq_empty, kTileM);
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t tm_dq = tmem + 256;
+  volatile int* abort_p = &abort_flag;
+  const int64_t nitems = f.B * f.HQ * ((f.T + kTileM - 1) / kTileM);
+  // the CTA's items are blockIdx.x + k * gridDim.x, blocks blo..bhi of each
+  struct Cur {
+    int64_t item, m, n, j;
+    WsItem w;
+    bool done;
+  };
+  auto cur_start = [&](Cur& c) {
+    c.item = blockIdx.x;
+    c.m = 0;
+    c.n = 0;
+    c.done = c.item >= nitems;
+    if (!c.done) {
+      c.w = ws_item<false>(f, c.item);
+      c.j = c.w.blo;
+    }
+  };
+  auto cur_advance = [&](Cur& c) {
+    ++c.n;
+    if (c.j < c.w.bhi) {
+      ++c.j;
+      return;
+    }
+    ++c.m;
+    c.item += gridDim.x;
+    c.done = c.item >= nitems;
+    if (!c.done) {
+      c.w = ws_item<false>(f, c.item);
+      c.j = c.w.blo;
+    }
+  };
+
+  if (warp == 4) {
+    // -------------------------------------------------------------- producer
+    Cur c;
+    cur_start(c);
+    bool ok = true;
+    while (ok && !c.done) {
+      if (c.j == c.w.blo) {
+        if (c.m > 0 && !__all_sync(0xffffffffu, ws_wait(&q_empty, static_cast<uint32_t>((c.m - 1) & 1), abort_p, 461))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const int t0 = static_cast<int>(c.w.t0), hh = static_cast<int>(c.w.h), bb = static_cast<int>(c.w.b);
+          mbar_arrive_expect_tx(&q_full, 2 * kTile128);
+          tma_load_4d(q_s, &tmq, 0, t0, hh, bb, &q_full);
+          tma_load_4d(q_s + kTile128 / 2, &tmq, 64, t0, hh, bb, &q_full);
+          tma_load_4d(do_s, &tmdo, 0, t0, hh, bb, &q_full);
+          tma_load_4d(do_s + kTile128 / 2, &tmdo, 64, t0, hh, bb, &q_full);
+        }
+        __syncwarp();
+      }
+      const int st = static_cast<int>(c.n % kBqStages);
+      if (c.n >= kBqStages &&
+          !__all_sync(0xffffffffu, ws_wait(&kv_empty[st], static_cast<uint32_t>((c.n / kBqStages - 1) & 1), abort_p, 462))) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) {
+        const int row0 = static_cast<int>(c.j * kBlk), hh = static_cast<int>(c.w.hk), bb = static_cast<int>(c.w.b);
+        const uint32_t dst = k_s(st);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kKVBytes);
+        tma_load_4d(dst, &tmk, 0, row0, hh, bb, &kv_full[st]);
+        tma_load_4d(dst + kKVHalf, &tmk, 64, row0, hh, bb, &kv_full[st]);
+        tma_load_4d(dst + kKVBytes, &tmv, 0, row0, hh, bb, &kv_full[st]);
+        tma_load_4d(dst + kKVBytes + kKVHalf, &tmv, 64, row0, hh, bb, &kv_full[st]);
+      }
+      __syncwarp();
+      cur_advance(c);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------- MMA
+    if (lane == 0) {
+      Cur c;
+      cur_start(c);
+      auto issue_sdp = [&](const Cur& x) -> bool {
+        const int st = static_cast<int>(x.n % kBqStages), sb = static_cast<int>(x.n & 1);
+        if (x.j == x.w.blo && !ws_wait(&q_full, static_cast<uint32_t>(x.m & 1), abort_p, 463)) return false;
+        if (!ws_wait(&kv_full[st], static_cast<uint32_t>((x.n / kBqStages) & 1), abort_p, 464)) return false;
+        tc_fence_after();
+        issue_qk(tmem + 64 * sb, q_s, k_s(st));
+        issue_qk(tmem + 128 + 64 * sb, do_s, k_s(st) + kKVBytes);
+        mma_commit(&s_full[sb]);
+        if (x.j == x.w.bhi) mma_commit(&q_empty);  // the item's q / dO are read by S / dP only
+        return true;
+      };
+      bool ok = !c.done && issue_sdp(c);
+      while (ok && !c.done) {
+        Cur nx = c;
+        cur_advance(nx);
+        if (!nx.done && !(ok = issue_sdp(nx))) break;  // next block's S / dP overlap this block's dS
+        if (!ws_wait(&p_full[c.n & 1], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 465)) break;
+        const bool first = c.j == c.w.blo, last = c.j == c.w.bhi;
+        if (first && c.m > 0 && !ws_wait(&dq_empty, static_cast<uint32_t>((c.m - 1) & 1), abort_p, 466)) break;
+        const int st = static_cast<int>(c.n % kBqStages);
+        tc_fence_after();
+        issue_pv(tm_dq, k_s(st) + kKVBytes, k_s(st), !first);  // dQ += dS K, dS over the dead V
+        mma_commit(&kv_empty[st]);
+        if (last) mma_commit(&o_full);
+        c = nx;
+      }
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------------------------------- compute
+    const int r = tid;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    Cur c;
+    cur_start(c);
+    int64_t t = 0, ls = 0;
+    bool row_ok = false;
+    float lse2 = 0.f, dlt = 0.f;
+    while (!c.done) {
+      const bool first = c.j == c.w.blo, last = c.j == c.w.bhi;
+      if (first) {
+        t = c.w.t0 + r;
+        row_ok = t < f.T;
+        ls = row_ok ? win_start(f, c.w.b, t) : 0;
+        lse2 = row_ok ? a.lse[(c.w.b * f.T + t) * f.HQ + c.w.h] * kLog2e : 0.f;
+        dlt = row_ok ? a.delta[(c.w.b * f.T + t) * f.HQ + c.w.h] : 0.f;
+      }
+      const int sb = static_cast<int>(c.n & 1);
+      if (!__all_sync(0xffffffffu, ws_wait(&s_full[sb], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 467))) break;
+      tc_fence_after();
+      float sv[64], dp[64];
+      {
+        float x0[32], x1[32];
+        tmem_ld32(tmem + 64 * sb + lane_off, x0);
+        tmem_ld32(tmem + 64 * sb + lane_off + 32, x1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
+        tmem_ld32(tmem + 128 + 64 * sb + lane_off, x0);
+        tmem_ld32(tmem + 128 + 64 * sb + lane_off + 32, x1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
+      }
+      const int64_t k0 = c.j * kBlk;
+      const int klo = row_ok ? clamp_key(ls - k0) : 0, khi = row_ok ? clamp_key(t + 1 - k0) : 0;
+      const bool okl = lse2 != -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const bool valid = okl && i >= klo && i < khi;
+        const float pv = valid ? fast_exp2(fmaf(sv[i], f.scale_log2, -lse2)) : 0.f;
+        dp[i] = pv * (dp[i] - dlt);
+      }
+      const uint32_t ds_s = k_s(static_cast<int>(c.n % kBqStages)) + kKVBytes;  // over the dead V
+      store_p_row(ds_s, r, 0, dp);
+      store_p_row(ds_s, r, 4, dp + 32);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[sb]);
+      if (last) {
+        if (!__all_sync(0xffffffffu, ws_wait(&o_full, static_cast<uint32_t>(c.m & 1), abort_p, 468))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          float ov[32];
+          tmem_ld32(tm_dq + lane_off + 32 * cc, ov);
+          tmem_wait_ld();
+          if (row_ok) {
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              float tmp[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * a.scale;
+              store8(a.dq + c.w.b * f.sqb + t * f.sqt + c.w.h * f.sqh + 32 * cc, 8 * q4, SRSWA_BF16, tmp);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&dq_empty);
+      }
+      cur_advance(c);
+    }
+  }
+  // ------------------------------------------------------------------- exit
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    if (*abort_p) {
+      if (lane == 0) {
+        mma_commit(&drain_bar);
+        mbar_wait(&drain_bar, 0, 469);
+      }
+      __syncwarp();
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, kWsTmemCols);
+  }
+}
+
+// dq[b,t,h] += sum of the row's remote dQ partials (usable first-occurrence
+// slots, as in the pair lists); one warp per (b, t, h), lane = 4 features.
+// Slot validity is recomputed from the selection row with warp shuffles; all
+// partial loads of the row are issued together.
+__global__ void __launch_bounds__(256) dq_merge_kernel(const TcBwdArgs a) {
+  const TcArgs& f = a.f;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= f.B * f.T * f.HQ) return;
+  const int64_t h = row % f.HQ, bt = row / f.HQ, t = bt % f.T, b = bt / f.T;
+  const int64_t hi = h / (f.HQ / f.HI);
+  const int32_t* srow = f.sel + ((b * f.HI + hi) * f.T + t) * f.S;
+  const int ns = static_cast<int>(f.S < 64 ? f.S : 64);
+  int32_t blk0 = lane < ns ? srow[lane] : -1, blk1 = lane + 32 < ns ? srow[lane + 32] : -1;
+  auto usable = [&](int32_t blk) {
+    if (blk < 0 || blk >= f.nblk) return false;
+    int64_t lo, hi2;
+    remote_range(f, b, t, blk, lo, hi2);
+    return lo < hi2;
+  };
+  bool ok0 = usable(blk0), ok1 = usable(blk1);
+  for (int u = 0; u < 32; ++u) {  // drop repeats of an earlier slot
+    const int32_t o0 = __shfl_sync(0xffffffffu, blk0, u);
+    if (u < lane && o0 == blk0) ok0 = false;
+    if (o0 == blk1) ok1 = false;
+    const int32_t o1 = __shfl_sync(0xffffffffu, blk1, u);
+    if (u < lane && o1 == blk1) ok1 = false;
+  }
+  const uint32_t m0 = __ballot_sync(0xffffffffu, ok0), m1 = __ballot_sync(0xffffffffu, ok1);
+  if ((m0 | m1) == 0) return;
+  __nv_bfloat16* dqp = a.dq + b * f.sqb + t * f.sqt + h * f.sqh + lane * 4;
+  const uint2 d0 = *reinterpret_cast<const uint2*>(dqp);
+  float acc[4] = {bf16_lo(d0.x), bf16_hi(d0.x), bf16_lo(d0.y), bf16_hi(d0.y)};
+  const int64_t slot_base = (bt * f.S) * f.HQ + h;
+  for (int g0 = 0; g0 < ns; g0 += 8) {
+    uint2 u8[8];
+#pragma unroll
+    for (int k8 = 0; k8 < 8; ++k8) {
+      const int s2 = g0 + k8;
+      const bool use = s2 < ns && (((s2 < 32 ? m0 : m1) >> (s2 & 31)) & 1u);
+      u8[k8] = use ? __ldcs(reinterpret_cast<const uint2*>(a.dq_part + (slot_base + s2 * f.HQ) * kD + lane * 4))
+                   : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int k8 = 0; k8 < 8; ++k8) {
+      acc[0] += bf16_lo(u8[k8].x);
+      acc[1] += bf16_hi(u8[k8].x);
+      acc[2] += bf16_lo(u8[k8].y);
+      acc[3] += bf16_hi(u8[k8].y);
+    }
+  }
+  __nv_bfloat162 r0 = __floats2bfloat162_rn(acc[0], acc[1]);
+  __nv_bfloat162 r1 = __floats2bfloat162_rn(acc[2], acc[3]);
+  uint2 w2;
+  w2.x = *reinterpret_cast<uint32_t*>(&r0);
+  w2.y = *reinterpret_cast<uint32_t*>(&r1);
+  *reinterpret_cast<uint2*>(dqp) = w2;
+}
+
 // d_bias[b,t,s] = sum over query heads of the per-head partials (fixed order)
 __global__ void tc_dbias_reduce_kernel(const TcBwdArgs a) {
   const TcArgs& f = a.f;
@@ -2858,6 +3195,8 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     if (e != cudaSuccess) return static_cast<int>(e);
     e = cudaFuncSetAttribute(bwd_remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRbSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(bwd_band_dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBqSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     e = cudaFuncSetAttribute(bwd_band_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBDSmem);
@@ -2867,9 +3206,11 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     attr_done = true;
   }
   // TMA for the remote pass's K / V when the driver encodes the tensor maps
-  alignas(64) CUtensorMap tmk, tmv;
+  alignas(64) CUtensorMap tmk, tmv, tmq, tmdo;
   const bool use_tma = make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
-                       make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk);
+                       make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk) &&
+                       make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
+                       make_tmap(&tmdo, dout, g->B, g->T, g->HQ, sob, sot, soh, kTileM);
   const int64_t nrows_h = g->B * g->T * g->HQ;
   tc_delta_kernel<<<static_cast<unsigned>((nrows_h + 7) / 8), 256, 0, st>>>(a);
   SRSWA_CUDA_TRY(cudaGetLastError());
@@ -2885,7 +3226,7 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     pairs_scan_kernel<<<1, 1024, 0, st>>>(f, count, offs, reinterpret_cast<int32_t*>(ws + L.cursor),
                                           const_cast<int4*>(f.tiles), const_cast<int32_t*>(f.ntiles));
     SRSWA_CUDA_TRY(cudaGetLastError());
-    bwd_pairs_fill_kernel<<<static_cast<unsigned>((nbh + 7) / 8), 256, 0, st>>>(f, bitmap, L.T32, offs,
+    bwd_pairs_fill_kernel<<<static_cast<unsigned>(nbh), 256, 0, st>>>(f, bitmap, L.T32, offs,
                                                                               const_cast<int32_t*>(f.pairs));
     SRSWA_CUDA_TRY(cudaGetLastError());
     if (a.dbias_part)
@@ -2898,9 +3239,21 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   bwd_band_dkdv_kernel<<<dim3(ntile, static_cast<unsigned>(g->Hkv), static_cast<unsigned>(g->B)), kTcThreads,
                          kBDSmem, st>>>(a);
   SRSWA_CUDA_TRY(cudaGetLastError());
-  bwd_band_dq_kernel<<<dim3(ntile, static_cast<unsigned>(g->HQ), static_cast<unsigned>(g->B)), kTcThreads,
-                       kBQSmem, st>>>(a);
-  SRSWA_CUDA_TRY(cudaGetLastError());
+  if (use_tma) {
+    const int64_t items = g->B * g->HQ * static_cast<int64_t>(ntile);
+    const unsigned grid_q = static_cast<unsigned>(items < num_sms ? items : num_sms);
+    bwd_band_dq_ws_kernel<<<grid_q, kBqThreads, kBqSmem, st>>>(a, tmq, tmdo, tmk, tmv);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    if (remote) {
+      const int64_t rows = g->B * g->T * g->HQ;
+      dq_merge_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+      SRSWA_CUDA_TRY(cudaGetLastError());
+    }
+  } else {
+    bwd_band_dq_kernel<<<dim3(ntile, static_cast<unsigned>(g->HQ), static_cast<unsigned>(g->B)), kTcThreads,
+                         kBQSmem, st>>>(a);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+  }
   if (bias) {
     if (remote) {
       const int64_t n = g->B * g->T * g->S;

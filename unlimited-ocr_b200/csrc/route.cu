@@ -972,6 +972,19 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
   const int64_t cmax = cmax_s;
   const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
   const int r0 = warp * 4;
+  // k_bar chunks: this thread's 8 float4 of the next chunk are loaded into
+  // registers while the current chunk's FMAs run
+  float4 pf[kRtChunk * 32 / kRouteThreads];
+  auto load_chunk = [&](int64_t cb) {
+#pragma unroll
+    for (int k8 = 0; k8 < kRtChunk * 32 / kRouteThreads; ++k8) {
+      const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
+      const int64_t c = cb + j;
+      pf[k8] = c < cmax ? __ldg(reinterpret_cast<const float4*>(a.kbar + seq * a.s_kbar_b + c * a.s_kbar_c + 4 * u))
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if (cmax > 0) load_chunk(0);
   for (int64_t c0 = 0; c0 < nblk; c0 += kRtChunk) {
     if (c0 >= cmax) {  // no row has remote blocks here: sentinel scores only
       for (int i = tid; i < kRtRows * kRtChunk; i += kRouteThreads) {
@@ -981,14 +994,13 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
       }
       continue;
     }
-    for (int i = tid; i < kRtChunk * 32; i += kRouteThreads) {
-      const int j = i >> 5, u = i & 31;
-      const int64_t c = c0 + j;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c < cmax) v = __ldg(reinterpret_cast<const float4*>(a.kbar + seq * a.s_kbar_b + c * a.s_kbar_c + 4 * u));
-      *reinterpret_cast<float4*>(kb + j * kRtLd + 4 * u) = v;
+#pragma unroll
+    for (int k8 = 0; k8 < kRtChunk * 32 / kRouteThreads; ++k8) {
+      const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
+      *reinterpret_cast<float4*>(kb + j * kRtLd + 4 * u) = pf[k8];
     }
     __syncthreads();
+    if (c0 + kRtChunk < cmax) load_chunk(c0 + kRtChunk);
     float acc[4][2];
 #pragma unroll
     for (int rr = 0; rr < 4; ++rr) acc[rr][0] = acc[rr][1] = 0.f;
