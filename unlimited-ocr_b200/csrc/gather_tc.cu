@@ -2924,6 +2924,353 @@ __global__ void __launch_bounds__(256) dq_merge_kernel(const TcBwdArgs a) {
   *reinterpret_cast<uint2*>(dqp) = w2;
 }
 
+// ---- band dK / dV, warp-specialised: one work item = (b, kv head, 128-key
+// tile); steps = (query head of the group) x (64-query chunk of the window)
+//   warps 0-3  compute (thread = key row): P^T = 2^(s c - lse_q), dS^T =
+//              P^T (dP^T - delta_q) over the pairs with ls_q <= key <= q,
+//              P^T / dS^T (bf16) to a double-buffered shared tile; after the
+//              item's last step, dK (scaled) and dV from TMEM;
+//   warp 4     producer: TMA of the item's K / V tile and of each chunk's q /
+//              dO rows (2 stages), plus the chunk's per-query lse, delta and
+//              window bounds in shared memory and a whole-chunk-valid flag;
+//   warp 5     MMA issuer: S^T = K Q^T and dP^T = V dO^T into one of two TMEM
+//              buffers (the next step's run while the compute warps work),
+//              dV += P^T dO and dK += dS^T Q accumulated over the item.
+// The remote dK / dV partials are added by dkv_merge_kernel.
+constexpr int kBkThreads = 192;
+constexpr uint32_t kQc = 64 * 128 * 2;                                       // 64 rows x 128 bf16
+constexpr uint32_t kBkSmem = 2 * kTile128 + 2 * 2 * kQc + 2 * 2 * kPBytes + 1024;  // 193 KB
+
+__global__ void __launch_bounds__(kBkThreads, 1)
+    bwd_band_dkdv_ws_kernel(const TcBwdArgs a, const __grid_constant__ CUtensorMap tmq64,
+                            const __grid_constant__ CUtensorMap tmdo64, const __grid_constant__ CUtensorMap tmk,
+                            const __grid_constant__ CUtensorMap tmv) {
+  const TcArgs& f = a.f;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], s_full[2], p_full[2], pds_empty[2];
+  __shared__ uint64_t dkv_full, dkv_empty, drain_bar;
+  __shared__ __align__(16) int32_t v_lo[2][64], v_hi[2][64];
+  __shared__ __align__(16) float v_lse[2][64], v_dl[2][64];
+  __shared__ int v_full[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t k_s = sbase, v_s = sbase + kTile128;
+  auto qd_s = [&](int st) { return sbase + 2 * kTile128 + static_cast<uint32_t>(st) * 2 * kQc; };  // q, then dO
+  auto pds_s = [&](int pb) { return sbase + 2 * kTile128 + 4 * kQc + static_cast<uint32_t>(pb) * 2 * kPBytes; };
+  if (warp == 5) {
+    tmem_alloc(&tmem_base, kWsTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&kv_full, 1);
+    mbar_init(&kv_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 32);
+      mbar_init(&qd_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], kTileM);
+      mbar_init(&pds_empty[i], 1);
+    }
+    mbar_init(&dkv_full, 1);
+    mbar_init(&dkv_empty, kTileM);
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t tm_dk = tmem + 256, tm_dv = tmem + 384;
+  volatile int* abort_p = &abort_flag;
+  const int64_t G = f.HQ / f.Hkv;
+  const int64_t ntk = (f.T + kTileM - 1) / kTileM;
+  const int64_t nitems = f.B * f.Hkv * ntk;
+  struct Cur {
+    int64_t item, m, n, b, hk, k0, g, c, nch;
+    bool done;
+  };
+  auto load_item = [&](Cur& x) {
+    x.done = x.item >= nitems;
+    if (x.done) return;
+    const int64_t tile = x.item % ntk, bh = x.item / ntk;
+    x.b = bh / f.Hkv;
+    x.hk = bh % f.Hkv;
+    x.k0 = tile * kTileM;
+    const int64_t q_end = min(f.T, x.k0 + kTileM - 1 + f.LW);
+    x.nch = (q_end - x.k0 + 63) / 64;
+    x.g = 0;
+    x.c = 0;
+  };
+  auto cur_start = [&](Cur& x) {
+    x.item = blockIdx.x;
+    x.m = 0;
+    x.n = 0;
+    load_item(x);
+  };
+  auto is_first = [&](const Cur& x) { return x.g == 0 && x.c == 0; };
+  auto is_last = [&](const Cur& x) { return x.g == G - 1 && x.c == x.nch - 1; };
+  auto cur_advance = [&](Cur& x) {
+    ++x.n;
+    if (++x.c < x.nch) return;
+    x.c = 0;
+    if (++x.g < G) return;
+    ++x.m;
+    x.item += gridDim.x;
+    load_item(x);
+  };
+
+  if (warp == 4) {
+    // -------------------------------------------------------------- producer
+    Cur c;
+    cur_start(c);
+    bool ok = true;
+    while (ok && !c.done) {
+      const int bb = static_cast<int>(c.b);
+      if (is_first(c)) {
+        if (c.m > 0 && !__all_sync(0xffffffffu, ws_wait(&kv_empty, static_cast<uint32_t>((c.m - 1) & 1), abort_p, 481))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const int k0 = static_cast<int>(c.k0), hh = static_cast<int>(c.hk);
+          mbar_arrive_expect_tx(&kv_full, 2 * kTile128);
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+            for (int rb = 0; rb < 2; ++rb) {
+              const uint32_t off = hf * (kTile128 / 2) + rb * kKVHalf;
+              tma_load_4d(k_s + off, &tmk, 64 * hf, k0 + 64 * rb, hh, bb, &kv_full);
+              tma_load_4d(v_s + off, &tmv, 64 * hf, k0 + 64 * rb, hh, bb, &kv_full);
+            }
+          }
+        }
+        __syncwarp();
+      }
+      const int st = static_cast<int>(c.n & 1);
+      if (c.n >= 2 &&
+          !__all_sync(0xffffffffu, ws_wait(&qd_empty[st], static_cast<uint32_t>(((c.n >> 1) - 1) & 1), abort_p, 482))) {
+        ok = false;
+        break;
+      }
+      const int64_t h = c.hk * G + c.g, q0 = c.k0 + 64 * c.c;
+      bool all_ok = true;
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int i = lane + 32 * k2;
+        const int64_t q = q0 + i;
+        int32_t lo = 0x7fffffff, hi = -1;
+        float l2 = 0.f, dl = 0.f;
+        if (q < f.T) {
+          lo = static_cast<int32_t>(win_start(f, c.b, q));
+          hi = static_cast<int32_t>(q);
+          l2 = a.lse[(c.b * f.T + q) * f.HQ + h] * kLog2e;
+          dl = a.delta[(c.b * f.T + q) * f.HQ + h];
+        }
+        v_lo[st][i] = lo;
+        v_hi[st][i] = hi;
+        v_lse[st][i] = l2;
+        v_dl[st][i] = dl;
+        all_ok = all_ok && q < f.T && lo <= c.k0 && hi >= c.k0 + kTileM - 1 && c.k0 + kTileM <= f.T &&
+                 l2 != -INFINITY;
+      }
+      const bool full = __all_sync(0xffffffffu, all_ok);
+      if (lane == 0) v_full[st] = full ? 1 : 0;
+      __syncwarp();
+      if (lane == 0) {
+        const int hh = static_cast<int>(h), qq = static_cast<int>(q0);
+        mbar_arrive_expect_tx(&qd_full[st], 2 * kQc);
+        tma_load_4d(qd_s(st), &tmq64, 0, qq, hh, bb, &qd_full[st]);
+        tma_load_4d(qd_s(st) + kKVHalf, &tmq64, 64, qq, hh, bb, &qd_full[st]);
+        tma_load_4d(qd_s(st) + kQc, &tmdo64, 0, qq, hh, bb, &qd_full[st]);
+        tma_load_4d(qd_s(st) + kQc + kKVHalf, &tmdo64, 64, qq, hh, bb, &qd_full[st]);
+      } else {
+        mbar_arrive(&qd_full[st]);  // release: this lane's vectors above
+      }
+      cur_advance(c);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------- MMA
+    if (lane == 0) {
+      Cur c;
+      cur_start(c);
+      auto issue_sdp = [&](const Cur& x) -> bool {
+        const int st = static_cast<int>(x.n & 1);
+        if (is_first(x) && !ws_wait(&kv_full, static_cast<uint32_t>(x.m & 1), abort_p, 483)) return false;
+        if (!ws_wait(&qd_full[st], static_cast<uint32_t>((x.n >> 1) & 1), abort_p, 484)) return false;
+        tc_fence_after();
+        issue_qk(tmem + 64 * st, k_s, qd_s(st));               // S^T = K Q^T
+        issue_qk(tmem + 128 + 64 * st, v_s, qd_s(st) + kQc);   // dP^T = V dO^T
+        mma_commit(&s_full[st]);
+        if (is_last(x)) mma_commit(&kv_empty);  // K / V are read by S^T / dP^T only
+        return true;
+      };
+      bool ok = !c.done && issue_sdp(c);
+      while (ok && !c.done) {
+        Cur nx = c;
+        cur_advance(nx);
+        if (!nx.done && !(ok = issue_sdp(nx))) break;
+        const int st = static_cast<int>(c.n & 1);
+        if (!ws_wait(&p_full[st], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 485)) break;
+        const bool first = is_first(c), last = is_last(c);
+        if (first && c.m > 0 && !ws_wait(&dkv_empty, static_cast<uint32_t>((c.m - 1) & 1), abort_p, 486)) break;
+        tc_fence_after();
+        issue_pv(tm_dv, pds_s(st), qd_s(st) + kQc, !first);        // dV += P^T dO
+        issue_pv(tm_dk, pds_s(st) + kPBytes, qd_s(st), !first);    // dK += dS^T Q
+        mma_commit(&pds_empty[st]);
+        mma_commit(&qd_empty[st]);
+        if (last) mma_commit(&dkv_full);
+        c = nx;
+      }
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------------------------------- compute
+    const int r = tid;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    Cur c;
+    cur_start(c);
+    while (!c.done) {
+      const int st = static_cast<int>(c.n & 1);
+      const int64_t key = c.k0 + r;
+      const bool key_ok = key < f.T;
+      if (!__all_sync(0xffffffffu, ws_wait(&qd_full[st], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 487) &&
+                                       ws_wait(&s_full[st], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 488)))
+        break;
+      tc_fence_after();
+      float sv[64], dp[64];
+      {
+        float x0[32], x1[32];
+        tmem_ld32(tmem + 64 * st + lane_off, x0);
+        tmem_ld32(tmem + 64 * st + lane_off + 32, x1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
+        tmem_ld32(tmem + 128 + 64 * st + lane_off, x0);
+        tmem_ld32(tmem + 128 + 64 * st + lane_off + 32, x1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
+      }
+      const int32_t k32 = static_cast<int32_t>(key);
+      if (v_full[st]) {  // every (key, query) pair of the step is local
+#pragma unroll
+        for (int i4 = 0; i4 < 16; ++i4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(&v_lse[st][4 * i4]);
+          const float4 d4 = *reinterpret_cast<const float4*>(&v_dl[st][4 * i4]);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 4 * i4 + e;
+            const float pv = fast_exp2(fmaf(sv[i], f.scale_log2, -lv[e]));
+            sv[i] = pv;
+            dp[i] = pv * (dp[i] - dv4[e]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i4 = 0; i4 < 16; ++i4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(&v_lse[st][4 * i4]);
+          const float4 d4 = *reinterpret_cast<const float4*>(&v_dl[st][4 * i4]);
+          const int4 lo4 = *reinterpret_cast<const int4*>(&v_lo[st][4 * i4]);
+          const int4 hi4 = *reinterpret_cast<const int4*>(&v_hi[st][4 * i4]);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+          const int32_t lo[4] = {lo4.x, lo4.y, lo4.z, lo4.w}, hi[4] = {hi4.x, hi4.y, hi4.z, hi4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 4 * i4 + e;
+            const bool valid = key_ok && k32 >= lo[e] && k32 <= hi[e] && lv[e] != -INFINITY;
+            const float pv = valid ? fast_exp2(fmaf(sv[i], f.scale_log2, -lv[e])) : 0.f;
+            sv[i] = pv;
+            dp[i] = pv * (dp[i] - dv4[e]);
+          }
+        }
+      }
+      if (c.n >= 2 && !__all_sync(0xffffffffu, ws_wait(&pds_empty[st], static_cast<uint32_t>(((c.n >> 1) - 1) & 1),
+                                                       abort_p, 489)))
+        break;
+      store_p_row(pds_s(st), r, 0, sv);
+      store_p_row(pds_s(st), r, 4, sv + 32);
+      store_p_row(pds_s(st) + kPBytes, r, 0, dp);
+      store_p_row(pds_s(st) + kPBytes, r, 4, dp + 32);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[st]);
+      if (is_last(c)) {
+        if (!__all_sync(0xffffffffu, ws_wait(&dkv_full, static_cast<uint32_t>(c.m & 1), abort_p, 490))) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          float kv[32], vv[32];
+          tmem_ld32(tm_dk + lane_off + 32 * cc, kv);
+          tmem_ld32(tm_dv + lane_off + 32 * cc, vv);
+          tmem_wait_ld();
+          if (key_ok) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) kv[i] *= a.scale;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              store8(a.dk + c.b * f.skb + key * f.skt + c.hk * f.skh + 32 * cc, 8 * q4, SRSWA_BF16, kv + 8 * q4);
+              store8(a.dv + c.b * f.svb + key * f.svt + c.hk * f.svh + 32 * cc, 8 * q4, SRSWA_BF16, vv + 8 * q4);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&dkv_empty);
+      }
+      cur_advance(c);
+    }
+  }
+  // ------------------------------------------------------------------- exit
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    if (*abort_p) {
+      if (lane == 0) {
+        mma_commit(&drain_bar);
+        mbar_wait(&drain_bar, 0, 491);
+      }
+      __syncwarp();
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, kWsTmemCols);
+  }
+}
+
+// dk / dv += the remote partials of the key's block over the kv group's query
+// heads (blocks some query selected); thread = (b, key, kv head, 8 features),
+// 16 consecutive threads cover one 256-byte row.
+__global__ void __launch_bounds__(256) dkv_merge_kernel(const TcBwdArgs a) {
+  const TcArgs& f = a.f;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (idx >= f.B * f.T * f.Hkv * 16) return;
+  const int64_t ch = idx & 15, rest = idx >> 4;
+  const int64_t hk = rest % f.Hkv, bt = rest / f.Hkv, key = bt % f.T, b = bt / f.T;
+  const int64_t blk = key / kBlk, G = f.HQ / f.Hkv, hi = (hk * f.HI) / f.Hkv;
+  if (a.count[(b * f.HI + hi) * f.nblk + blk] == 0) return;
+  __nv_bfloat16* dkp = a.dk + b * f.skb + key * f.skt + hk * f.skh + ch * 8;
+  __nv_bfloat16* dvp = a.dv + b * f.svb + key * f.svt + hk * f.svh + ch * 8;
+  float kacc[8], vacc[8];
+  load8(dkp, 0, SRSWA_BF16, kacc);
+  load8(dvp, 0, SRSWA_BF16, vacc);
+  for (int64_t g = 0; g < G; ++g) {
+    const float* src =
+        a.dkv_part + ((b * f.HQ + hk * G + g) * f.nblk + blk) * (2 * 64 * 128) + (key % kBlk) * 128 + ch * 8;
+    const float4 k0 = __ldcs(reinterpret_cast<const float4*>(src));
+    const float4 k1 = __ldcs(reinterpret_cast<const float4*>(src + 4));
+    const float4 v0 = __ldcs(reinterpret_cast<const float4*>(src + 8192));
+    const float4 v1 = __ldcs(reinterpret_cast<const float4*>(src + 8196));
+    kacc[0] += k0.x; kacc[1] += k0.y; kacc[2] += k0.z; kacc[3] += k0.w;
+    kacc[4] += k1.x; kacc[5] += k1.y; kacc[6] += k1.z; kacc[7] += k1.w;
+    vacc[0] += v0.x; vacc[1] += v0.y; vacc[2] += v0.z; vacc[3] += v0.w;
+    vacc[4] += v1.x; vacc[5] += v1.y; vacc[6] += v1.z; vacc[7] += v1.w;
+  }
+  store8(dkp, 0, SRSWA_BF16, kacc);
+  store8(dvp, 0, SRSWA_BF16, vacc);
+}
+
 // d_bias[b,t,s] = sum over query heads of the per-head partials (fixed order)
 __global__ void tc_dbias_reduce_kernel(const TcBwdArgs a) {
   const TcArgs& f = a.f;
@@ -3197,6 +3544,8 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     if (e != cudaSuccess) return static_cast<int>(e);
     e = cudaFuncSetAttribute(bwd_band_dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBqSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(bwd_band_dkdv_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBkSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     e = cudaFuncSetAttribute(bwd_band_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBDSmem);
@@ -3206,11 +3555,13 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     attr_done = true;
   }
   // TMA for the remote pass's K / V when the driver encodes the tensor maps
-  alignas(64) CUtensorMap tmk, tmv, tmq, tmdo;
+  alignas(64) CUtensorMap tmk, tmv, tmq, tmdo, tmq64, tmdo64;
   const bool use_tma = make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
                        make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk) &&
                        make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
-                       make_tmap(&tmdo, dout, g->B, g->T, g->HQ, sob, sot, soh, kTileM);
+                       make_tmap(&tmdo, dout, g->B, g->T, g->HQ, sob, sot, soh, kTileM) &&
+                       make_tmap(&tmq64, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, 64) &&
+                       make_tmap(&tmdo64, dout, g->B, g->T, g->HQ, sob, sot, soh, 64);
   const int64_t nrows_h = g->B * g->T * g->HQ;
   tc_delta_kernel<<<static_cast<unsigned>((nrows_h + 7) / 8), 256, 0, st>>>(a);
   SRSWA_CUDA_TRY(cudaGetLastError());
@@ -3236,9 +3587,21 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     SRSWA_CUDA_TRY(cudaGetLastError());
   }
   const unsigned ntile = static_cast<unsigned>((g->T + kTileM - 1) / kTileM);
-  bwd_band_dkdv_kernel<<<dim3(ntile, static_cast<unsigned>(g->Hkv), static_cast<unsigned>(g->B)), kTcThreads,
-                         kBDSmem, st>>>(a);
-  SRSWA_CUDA_TRY(cudaGetLastError());
+  if (use_tma) {
+    const int64_t items = g->B * g->Hkv * static_cast<int64_t>(ntile);
+    const unsigned grid_k = static_cast<unsigned>(items < num_sms ? items : num_sms);
+    bwd_band_dkdv_ws_kernel<<<grid_k, kBkThreads, kBkSmem, st>>>(a, tmq64, tmdo64, tmk, tmv);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    if (remote) {
+      const int64_t n16 = g->B * g->T * g->Hkv * 16;
+      dkv_merge_kernel<<<static_cast<unsigned>((n16 + 255) / 256), 256, 0, st>>>(a);
+      SRSWA_CUDA_TRY(cudaGetLastError());
+    }
+  } else {
+    bwd_band_dkdv_kernel<<<dim3(ntile, static_cast<unsigned>(g->Hkv), static_cast<unsigned>(g->B)), kTcThreads,
+                           kBDSmem, st>>>(a);
+    SRSWA_CUDA_TRY(cudaGetLastError());
+  }
   if (use_tma) {
     const int64_t items = g->B * g->HQ * static_cast<int64_t>(ntile);
     const unsigned grid_q = static_cast<unsigned>(items < num_sms ? items : num_sms);
