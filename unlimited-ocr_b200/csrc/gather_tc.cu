@@ -1932,21 +1932,26 @@ __global__ void __launch_bounds__(kTcThreads) bwd_remote_kernel(const TcBwdArgs 
 // ---- remote pairs, warp-specialised -------------------------------------
 // Same work items as bwd_remote_kernel: one item = one selected block of one
 // query head with all of its (query, slot) pairs, in tiles of 128.
-//   warps 0-3  compute (thread = pair row): P and dS = P (dP - delta) from
-//              S and dP in TMEM, the row's d_bias partial, P and dS (bf16)
-//              to shared memory, then the row's dQ partial from TMEM, and at
-//              the end of an item this block's dK / dV (thread = feature);
-//   warps 4-5  producers: cp.async gathers of the tile's q and dO rows into
-//              a double-buffered tile (warp 4 rows 0-63, warp 5 rows
+//   warps 0-7  compute: warps w and w + 4 share TMEM lane quarter w (pair
+//              rows 32w ..) and split the columns (keys 0-31 / 32-63 of S and
+//              dP, features 0-63 / 64-127 of dQ): P and dS = P (dP - delta),
+//              the row's d_bias partial (the high half hands its sum to the
+//              low half through shared memory and an mbarrier), P and dS
+//              (bf16) to shared memory, the row's dQ
+//              partial, and at the end of an item this block's dK / dV
+//              (thread = feature);
+//   warps 8-9  producers: cp.async gathers of the tile's q and dO rows into
+//              a double-buffered tile (warp 8 rows 0-63, warp 9 rows
 //              64-127), the rows' (query, slot) into shared memory, and (warp
-//              4) the item's K and V by TMA;
-//   warp 6     MMA issuer: S = Q K^T, dP = dO V^T; dQ = dS K; dV^T += dO^T P,
+//              8) the item's K and V by TMA;
+//   warp 10    MMA issuer: S = Q K^T, dP = dO V^T; dQ = dS K; dV^T += dO^T P,
 //              dK^T += Q^T dS accumulated over the item's tiles in TMEM.  The
 //              next tile's S / dP (same item) is issued before this tile's
 //              dQ / dV / dK so the tensor pipe works while the compute warps do.
 // All waits bounded; abort protocol as in fwd_ws_kernel.
-constexpr int kRbThreads = 224;
-constexpr int kRbMma = 6;
+constexpr int kRbThreads = 352;
+constexpr int kRbCompute = 256;  // compute threads (8 warps)
+constexpr int kRbMma = 10;
 constexpr uint32_t kRbQD = 2 * kTile128;                        // q tile + dO tile
 constexpr uint32_t kRbSmem = 2 * kRbQD + 2 * kKVBytes + 2 * kPBytes + 1024;  // 193 KB
 
@@ -2012,6 +2017,8 @@ __global__ void __launch_bounds__(kRbThreads, 1)
   __shared__ const __nv_bfloat16* qrows[kTileM];
   __shared__ const __nv_bfloat16* grows[kTileM];
   __shared__ int32_t r_t[2][kTileM], r_slot[2][kTileM];
+  __shared__ float dsum_hi[2][kTileM];  // d_bias partial of the keys 32-63 half, by tile parity
+  __shared__ uint64_t dsum_full[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -2030,15 +2037,17 @@ __global__ void __launch_bounds__(kRbThreads, 1)
       mbar_init(&q_full[bq], 64);
       mbar_init(&q_empty[bq], 1);
       mbar_init(&info_full[bq], 64);
-      mbar_init(&info_empty[bq], kTileM);
+      mbar_init(&info_empty[bq], kRbCompute);
     }
     mbar_init(&s_full, 1);
-    mbar_init(&p_full, kTileM);
+    mbar_init(&p_full, kRbCompute);
     mbar_init(&pds_empty, 1);
     mbar_init(&o_full, 1);
-    mbar_init(&dq_empty, kTileM);
+    mbar_init(&dq_empty, kRbCompute);
     mbar_init(&dkv_full, 1);
-    mbar_init(&dkv_empty, kTileM);
+    mbar_init(&dkv_empty, kRbCompute);
+    mbar_init(&dsum_full[0], kRbCompute / 2);
+    mbar_init(&dsum_full[1], kRbCompute / 2);
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
     abort_flag = 0;
@@ -2050,9 +2059,9 @@ __global__ void __launch_bounds__(kRbThreads, 1)
   const uint32_t tm_s = tmem, tm_dp = tmem + 64, tm_dq = tmem + 128, tm_dvt = tmem + 256, tm_dkt = tmem + 320;
   volatile int* abort_p = &abort_flag;
 
-  if (warp == 4 || warp == 5) {
+  if (warp == 8 || warp == 9) {
     // ---------------------------------------------------------- producers
-    const int half = warp - 4;  // rows 64*half .. 64*half + 63
+    const int half = warp - 8;  // rows 64*half .. 64*half + 63
     RbCursor cs;
     cs.start(a);
     int32_t ppk[2];
@@ -2164,10 +2173,11 @@ __global__ void __launch_bounds__(kRbThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ---------------------------------------------------------------- compute
-    const int r = tid;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int q4 = warp & 3, ch = warp >> 2;  // lane quarter, column half
+    const int r = 32 * q4 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     RbCursor cs;
     cs.start(a);
     while (!cs.done) {
@@ -2177,89 +2187,92 @@ __global__ void __launch_bounds__(kRbThreads, 1)
       const int64_t t = r_t[bq][r], slot = r_slot[bq][r];
       mbar_arrive(&info_empty[bq]);
       const bool row_ok = t >= 0;
-      float lse2 = 0.f, dlt = 0.f, bias2 = 0.f;
+      float lse_raw = 0.f, dlt = 0.f, bias_raw = 0.f;
       int64_t rlo = 0, rhi = 0;
-      if (row_ok) {  // in flight while S and dP land
-        lse2 = a.lse[(cs.b * f.T + t) * f.HQ + cs.h] * kLog2e;
+      if (row_ok) {  // in flight while S and dP land; used after the wait
+        lse_raw = a.lse[(cs.b * f.T + t) * f.HQ + cs.h];
         dlt = a.delta[(cs.b * f.T + t) * f.HQ + cs.h];
-        if (f.bias) bias2 = f.bias[(cs.b * f.T + t) * f.S + slot] * kLog2e;
+        if (f.bias) bias_raw = f.bias[(cs.b * f.T + t) * f.S + slot];
         remote_range(f, cs.b, t, cs.blk, rlo, rhi);
       }
       if (!__all_sync(0xffffffffu, ws_wait(&s_full, static_cast<uint32_t>(n & 1), abort_p, 450))) break;
       tc_fence_after();
-      float sv[64], dp[64];
-      {
-        float x0[32], x1[32];
-        tmem_ld32(tm_s + lane_off, x0);
-        tmem_ld32(tm_s + lane_off + 32, x1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
-        tmem_ld32(tm_dp + lane_off, x0);
-        tmem_ld32(tm_dp + lane_off + 32, x1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
-      }
-      const int64_t k0 = cs.blk * kBlk;
+      float sv[32], dp[32];
+      tmem_ld32(tm_s + lane_off + 32 * ch, sv);
+      tmem_ld32(tm_dp + lane_off + 32 * ch, dp);
+      tmem_wait_ld();
+      const int64_t k0 = cs.blk * kBlk + 32 * ch;
       const int klo = row_ok ? clamp_key(rlo - k0) : 0, khi = row_ok ? clamp_key(rhi - k0) : 0;
-      const float off = bias2 - lse2;
-      float dsum = 0.f;
+      const float lse2 = lse_raw * kLog2e;
+      const float off = bias_raw * kLog2e - lse2;
+      const bool okl = lse2 != -INFINITY;
+      float ds4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const bool valid = i >= klo && i < khi && lse2 != -INFINITY;
+      for (int i = 0; i < 32; ++i) {
+        const bool valid = okl && i >= klo && i < khi;
         const float pv = valid ? fast_exp2(fmaf(sv[i], f.scale_log2, off)) : 0.f;
         const float ds = pv * (dp[i] - dlt);
         sv[i] = pv;
         dp[i] = ds;
-        dsum += ds;
+        ds4[i & 3] += ds;
       }
+      const float dsum = (ds4[0] + ds4[1]) + (ds4[2] + ds4[3]);
       // P and dS of the previous tile are read by its dV / dK MMAs: wait for them
       if (n > 0 && !__all_sync(0xffffffffu, ws_wait(&pds_empty, static_cast<uint32_t>((n - 1) & 1), abort_p, 451)))
         break;
-      store_p_row(p_s, r, 0, sv);
-      store_p_row(p_s, r, 4, sv + 32);
-      store_p_row(ds_s, r, 0, dp);
-      store_p_row(ds_s, r, 4, dp + 32);
+      store_p_row(p_s, r, 4 * ch, sv);
+      store_p_row(ds_s, r, 4 * ch, dp);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full);
-      if (row_ok && a.dbias_part) a.dbias_part[((cs.b * f.T + t) * f.S + slot) * f.HQ + cs.h] = dsum;
+      if (ch == 1) {
+        dsum_hi[bq][r] = dsum;
+        mbar_arrive(&dsum_full[bq]);  // release: the sum above
+      } else {
+        if (!__all_sync(0xffffffffu, ws_wait(&dsum_full[bq], static_cast<uint32_t>((n >> 1) & 1), abort_p, 455))) break;
+        if (row_ok && a.dbias_part)
+          a.dbias_part[((cs.b * f.T + t) * f.S + slot) * f.HQ + cs.h] = dsum + dsum_hi[bq][r];
+      }
       if (!__all_sync(0xffffffffu, ws_wait(&o_full, static_cast<uint32_t>(n & 1), abort_p, 452))) break;
       tc_fence_after();
       const int64_t prow = ((cs.b * f.T + (row_ok ? t : 0)) * f.S + slot) * f.HQ + cs.h;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float ov[32];
-        tmem_ld32(tm_dq + lane_off + 32 * c, ov);
+      {
+        float ov0[32], ov1[32];
+        tmem_ld32(tm_dq + lane_off + 64 * ch, ov0);
+        tmem_ld32(tm_dq + lane_off + 64 * ch + 32, ov1);
         tmem_wait_ld();
         if (row_ok) {
+          __nv_bfloat16* dst = a.dq_part + prow * kD + 64 * ch;
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
+          for (int q8 = 0; q8 < 4; ++q8) {
             float tmp[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * a.scale;
-            store8(a.dq_part + prow * kD + 32 * c, 8 * q4, SRSWA_BF16, tmp);
+            for (int e = 0; e < 8; ++e) tmp[e] = ov0[8 * q8 + e] * a.scale;
+            store8(dst, 8 * q8, SRSWA_BF16, tmp);
+          }
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            float tmp[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) tmp[e] = ov1[8 * q8 + e] * a.scale;
+            store8(dst + 32, 8 * q8, SRSWA_BF16, tmp);
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&dq_empty);
-      if (cs.last()) {  // this block's remote dK / dV for the item's head: thread = feature
+      if (cs.last()) {  // this block's remote dK / dV for the item's head: thread = feature, keys of half ch
         if (!__all_sync(0xffffffffu, ws_wait(&dkv_full, static_cast<uint32_t>(cs.m & 1), abort_p, 453))) break;
         tc_fence_after();
         float* dst = a.dkv_part + ((cs.b * f.HQ + cs.h) * f.nblk + cs.blk) * (2 * 64 * 128);
+        float kv[32], vv[32];
+        tmem_ld32(tm_dkt + lane_off + 32 * ch, kv);
+        tmem_ld32(tm_dvt + lane_off + 32 * ch, vv);
+        tmem_wait_ld();
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          float kv[32], vv[32];
-          tmem_ld32(tm_dkt + lane_off + 32 * hf, kv);
-          tmem_ld32(tm_dvt + lane_off + 32 * hf, vv);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            dst[(32 * hf + i) * 128 + r] = kv[i] * a.scale;
-            dst[8192 + (32 * hf + i) * 128 + r] = vv[i];
-          }
+        for (int i = 0; i < 32; ++i) {
+          dst[(32 * ch + i) * 128 + r] = kv[i] * a.scale;
+          dst[8192 + (32 * ch + i) * 128 + r] = vv[i];
         }
         tc_fence_before();
         mbar_arrive(&dkv_empty);
