@@ -1310,7 +1310,7 @@ struct RwCursor {
   }
 };
 
-constexpr int kRwThreads = 352;  // + a second producer warp (warp 10): one producer per slot
+constexpr int kRwThreads = 416;  // producers: warps 8 / 11 (slot 0 rows 0-63 / 64-127), 10 / 12 (slot 1)
 __global__ void __launch_bounds__(kRwThreads, 1)
     remote_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -1337,9 +1337,9 @@ __global__ void __launch_bounds__(kRwThreads, 1)
       mbar_init(&p_full[s], kTileM);
       mbar_init(&o_full[s], 1);
       for (int qb = 0; qb < 2; ++qb) {
-        mbar_init(&q_full[s][qb], 32);
+        mbar_init(&q_full[s][qb], 64);
         mbar_init(&q_empty[s][qb], kTileM);
-        mbar_init(&info_full[s][qb], 32);
+        mbar_init(&info_full[s][qb], 64);
         mbar_init(&info_empty[s][qb], kTileM);
       }
     }
@@ -1353,20 +1353,21 @@ __global__ void __launch_bounds__(kRwThreads, 1)
   const uint32_t tmem = tmem_base;
   volatile int* abort_p = &abort_flag;
 
-  if (warp == kWsProducer || warp == kWsProducer + 2) {
-    // ------------------------------------------------- producer of one slot
-    const int s = warp == kWsProducer ? 0 : 1;
+  if (warp == kWsProducer || warp >= kWsProducer + 2) {
+    // ---------------------------------------- producer of half a slot's rows
+    const int s = (warp == kWsProducer || warp == kWsProducer + 3) ? 0 : 1;
+    const int half = warp >= kWsProducer + 3 ? 1 : 0;  // rows 64*half .. 64*half + 63
     RwCursor cs;
     cs.start(a, s);
-    // this tile's rows (lane L: rows L, L+32, L+64, L+96), fetched one tile ahead
-    int64_t pq[4];
-    float pbz[4];
-    int32_t ppk[4];
+    // this tile's rows of the half (lane L: rows 64*half + L, + 32), fetched one tile ahead
+    int64_t pq[2];
+    float pbz[2];
+    int32_t ppk[2];
     auto fetch = [&]() {
       const int64_t fp = cs.tile_first(), nh = cs.tile_rows();
 #pragma unroll
-      for (int k4 = 0; k4 < 4; ++k4) {
-        const int r = lane + 32 * k4;
+      for (int k4 = 0; k4 < 2; ++k4) {
+        const int r = 64 * half + lane + 32 * k4;
         ppk[k4] = -1;
         if (r < nh) {
           pq[k4] = a.pair_q[fp + r];
@@ -1384,7 +1385,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
           ok = false;
           break;
         }
-        if (lane == 0) {
+        if (half == 0 && lane == 0) {
           const int row0 = static_cast<int>(cs.blk * kBlk), hh = static_cast<int>(cs.hk), bb = static_cast<int>(cs.b);
           const uint32_t dst = kv_buf(s);
           mbar_arrive_expect_tx(&kv_full[s], kWsStage);
@@ -1406,8 +1407,8 @@ __global__ void __launch_bounds__(kRwThreads, 1)
       }
       const int64_t hq = cs.h * a.sqh;
 #pragma unroll
-      for (int k4 = 0; k4 < 4; ++k4) {
-        const int r = lane + 32 * k4;
+      for (int k4 = 0; k4 < 2; ++k4) {
+        const int r = 64 * half + lane + 32 * k4;
         const int32_t pk = ppk[k4];
         const int32_t tt = pk >= 0 ? pk / static_cast<int32_t>(a.S) : -1;
         qrows[s][r] = pk >= 0 ? a.q + pq[k4] + hq : nullptr;
@@ -1420,8 +1421,8 @@ __global__ void __launch_bounds__(kRwThreads, 1)
       const int cc = lane & 15;
       const uint32_t dst0 = q_buf(s, qb) + (cc >> 3) * (kQBytes / 2);
 #pragma unroll 8
-      for (int i = 0; i < kTileM / 2; ++i) {
-        const int r = (lane >> 4) + 2 * i;
+      for (int i = 0; i < kTileM / 4; ++i) {
+        const int r = 64 * half + (lane >> 4) + 2 * i;
         const __nv_bfloat16* g = qrows[s][r];
         cp_async16_zfill(dst0 + sw128_off(r, cc & 7), g ? static_cast<const void*>(g + cc * 8) : a.q, g != nullptr);
       }
