@@ -530,28 +530,44 @@ __global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const Rou
   }
 }
 
-// Top-M of the 8 per-warp lists (M keys each, kMaxTopM apart) by warp 0;
-// lane m returns the m-th key.  The lists are consumed.
-__device__ unsigned long long merge8_topm(unsigned long long* flat, int M, int lane) {
-  unsigned long long best = 0ull;
-  for (int i = lane; i < 8 * kMaxTopM; i += 32)
-    if ((i % kMaxTopM) < M) best = flat[i] > best ? flat[i] : best;
+// Top-M of unique non-zero keys held in registers, NPL per lane, by one warp:
+// each lane sorts its keys descending (compare-swap network), then every
+// round takes the warp maximum of the lanes' heads and the owning lane shifts
+// its list.  Lane m returns the m-th key (0 past the last key).
+template <int NPL>
+__device__ __forceinline__ unsigned long long warp_topm_regs(unsigned long long (&v)[NPL], int M, int lane) {
+#pragma unroll
+  for (int i = 0; i < NPL; ++i) {
+#pragma unroll
+    for (int j = 0; j + 1 < NPL - i; ++j) {
+      const unsigned long long x = v[j], y = v[j + 1];
+      v[j] = x > y ? x : y;
+      v[j + 1] = x > y ? y : x;
+    }
+  }
   unsigned long long mine = 0ull;
   for (int m = 0; m < M; ++m) {
-    const unsigned long long w = warp_max_u64(best);
+    const unsigned long long w = warp_max_u64(v[0]);
     if (lane == m) mine = w;
-    if (w != 0ull && best == w) {
-      best = 0ull;
-      for (int i = lane; i < 8 * kMaxTopM; i += 32) {
-        if ((i % kMaxTopM) >= M) continue;
-        unsigned long long v = flat[i];
-        if (v == w) { flat[i] = 0ull; v = 0ull; }
-        best = v > best ? v : best;
-      }
+    if (w != 0ull && v[0] == w) {  // unique keys: exactly one owner
+#pragma unroll
+      for (int j = 0; j + 1 < NPL; ++j) v[j] = v[j + 1];
+      v[NPL - 1] = 0ull;
     }
-    __syncwarp();
   }
   return mine;
+}
+
+// Top-M of the 8 per-warp lists (M keys each, kMaxTopM apart) by warp 0;
+// lane m returns the m-th key.
+__device__ unsigned long long merge8_topm(unsigned long long* flat, int M, int lane) {
+  unsigned long long v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int i = lane + 32 * k;  // 256 entries: list i / 32, position i % 32
+    v[k] = (i % kMaxTopM) < M ? flat[i] : 0ull;
+  }
+  return warp_topm_regs<8>(v, M, lane);
 }
 __device__ __forceinline__ void unpack_key(unsigned long long k, float& x, int& blk, bool& cand) {
   x = from_ordered(static_cast<uint32_t>(k >> 32));
@@ -614,7 +630,18 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
   const int64_t wlo = warp * per;
   const int64_t rem = nblk - wlo;
   const int64_t wn = rem < 0 ? 0 : (rem < per ? rem : per);
-  warp_topm_smem(wk + wlo, static_cast<int>(wn), M, lists[warp], lane);
+  if (per <= 512) {  // the warp's slice fits 16 registers per lane
+    unsigned long long v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int64_t i = lane + 32 * k;
+      v[k] = i < wn ? wk[wlo + i] : 0ull;
+    }
+    const unsigned long long top = warp_topm_regs<16>(v, M, lane);
+    if (lane < M) lists[warp][lane] = top;
+  } else {
+    warp_topm_smem(wk + wlo, static_cast<int>(wn), M, lists[warp], lane);
+  }
   __syncthreads();
   if (warp != 0) return;
   const unsigned long long mine = merge8_topm(&lists[0][0], M, lane);
@@ -1037,8 +1064,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
     __syncthreads();  // k_bar chunk reuse
   }
   __syncthreads();
-  // ---- selection: warp w, rows 4w .. 4w+3 ----
-  unsigned long long* wk = keys + static_cast<int64_t>(warp) * nblk;
+  // ---- selection: warp w, rows 4w .. 4w+3; lane holds blocks lane + 32 i ----
+  (void)keys;
   const int M = static_cast<int>(a.M);
   for (int rr = 0; rr < 4; ++rr) {
     const int r = r0 + rr;
@@ -1051,22 +1078,26 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
       for (int64_t c = lane; c < nblk; c += 32) f |= (z[c] > kScoreNeg * 0.5f) && a.cand[n * a.s_cand + c] != 0;
       found = __any_sync(0xffffffffu, f);
     }
-    for (int64_t c = lane; c < nblk; c += 32) {
-      const float zc = z[c];
-      if (a.scores_out) a.scores_out[n * nblk + c] = zc;
-      const bool remote = zc > kScoreNeg * 0.5f;  // NaN -> not remote
-      const bool cm = remote && (a.cand == nullptr || !found || a.cand[n * a.s_cand + c] != 0);
-      float x = cm ? zc * a.idx_scale : kEntmaxNeg;
-      if (!isfinite(x)) x = kEntmaxNeg;
-      wk[c] = pack_key(x, c, cm);
+    unsigned long long v[kRtMaxBlocks / 32];
+#pragma unroll
+    for (int k = 0; k < kRtMaxBlocks / 32; ++k) {
+      const int64_t c = lane + 32 * k;
+      v[k] = 0ull;
+      if (c < nblk) {
+        const float zc = z[c];
+        if (a.scores_out) a.scores_out[n * nblk + c] = zc;
+        const bool remote = zc > kScoreNeg * 0.5f;  // NaN -> not remote
+        const bool cm = remote && (a.cand == nullptr || !found || a.cand[n * a.s_cand + c] != 0);
+        float x = cm ? zc * a.idx_scale : kEntmaxNeg;
+        if (!isfinite(x)) x = kEntmaxNeg;
+        v[k] = pack_key(x, c, cm);
+      }
     }
-    __syncwarp();
-    warp_topm_smem(wk, static_cast<int>(nblk), M, lists[warp], lane);
-    __syncwarp();
+    const unsigned long long mine = warp_topm_regs<kRtMaxBlocks / 32>(v, M, lane);
     float sel_v = 0.f;
     int sel_i = -1;
     bool sel_c = false;
-    if (lane < M) unpack_key(lists[warp][lane], sel_v, sel_i, sel_c);
+    if (lane < M) unpack_key(mine, sel_v, sel_i, sel_c);
     route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
     __syncwarp();
   }
