@@ -17,6 +17,11 @@ constexpr int kAttendMaxSlots = 64;  // remote slots + window blocks per row
 // and key position i inside it / kv head h add i * s_pos + h * s_head.
 // Workspace layout of the tensor-core gather forward (byte offsets); one
 // definition shared by gather.cu (sizing) and gather_tc.cu (use).
+// Internal status of the tensor-core entry points: the driver refused a
+// tensor map (TMA descriptor) for these operands; the caller takes the
+// CUDA-core kernels instead.  Never returned through the C ABI.
+constexpr int kTcNoTensorMap = -1000;
+
 struct TcLayout {
   size_t part_o, part_lse, count, offs, cursor, tiles, ntiles, pairs, lse, pair_q, pair_bias, total;
   int64_t max_tiles;

@@ -393,8 +393,13 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
 static bool tc_bwd_path(const srswa_gather_desc* g, int64_t sob, int64_t sot, int64_t soh) {
   return tc_eligible(g) && ((sob | sot | soh) & 7) == 0;
 }
+// The tensor-core workspace also fits the CUDA-core kernels, which take over
+// when the driver refuses a tensor map.
 static size_t bwd_need(const srswa_gather_desc* g, int64_t sob, int64_t sot, int64_t soh, bool with_bias) {
-  return tc_bwd_path(g, sob, sot, soh) ? tc_bwd_workspace(g, with_bias) : bwd_layout(g, with_bias).total;
+  const size_t cc = bwd_layout(g, with_bias).total;
+  if (!tc_bwd_path(g, sob, sot, soh)) return cc;
+  const size_t tc = tc_bwd_workspace(g, with_bias);
+  return tc > cc ? tc : cc;
 }
 }  // namespace srswa
 
@@ -414,9 +419,11 @@ extern "C" int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const
                     reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15) == 0, SRSWA_EALIGN);
   if (g->B * g->T == 0) return 0;
   // tensor-core path (bf16, D = 128, 64-token blocks); CUDA-core rows otherwise
-  if (tc_eligible(g) && o_dtype == SRSWA_BF16 && ((sob | sot | soh) & 7) == 0)
-    return tc_gather_fwd(g, q, k, v, sel, bias, seg, o, sob, sot, soh, lse, workspace, workspace_bytes,
-                         reinterpret_cast<cudaStream_t>(stream));
+  if (tc_eligible(g) && o_dtype == SRSWA_BF16 && ((sob | sot | soh) & 7) == 0) {
+    rc = tc_gather_fwd(g, q, k, v, sel, bias, seg, o, sob, sot, soh, lse, workspace, workspace_bytes,
+                       reinterpret_cast<cudaStream_t>(stream));
+    if (rc != kTcNoTensorMap) return rc;
+  }
   const int64_t nblk = (g->T + g->block_size - 1) / g->block_size;
   AttendArgs a = {};
   a.q = q; a.k = k; a.v = v; a.q_dtype = g->dtype; a.out_dtype = o_dtype;
@@ -461,8 +468,9 @@ extern "C" int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const
     SRSWA_CHECK_ARG(g->B * g->T < (1ll << 31) && g->HQ < 65536 && g->B * g->HI * g->T * g->S < (1ll << 31),
                     SRSWA_ETOOLARGE);
     if (g->B * g->T == 0) return 0;
-    return tc_gather_bwd(g, q, k, v, o, sob, sot, soh, dout, lse, sel, bias, seg, dq, dk, dv, d_bias, workspace,
-                         workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+    rc = tc_gather_bwd(g, q, k, v, o, sob, sot, soh, dout, lse, sel, bias, seg, dq, dk, dv, d_bias, workspace,
+                       workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+    if (rc != kTcNoTensorMap) return rc;
   }
   const BwdLayout L = bwd_layout(g, bias != nullptr);
   SRSWA_CHECK_ARG(workspace && workspace_bytes >= L.total, SRSWA_EWORKSPACE);

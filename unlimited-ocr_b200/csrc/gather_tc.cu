@@ -1,27 +1,36 @@
-// Gather-attention forward on the 5th-generation tensor cores (tcgen05 / TMEM).
+// Gather attention (forward and backward) on the 5th-generation tensor cores
+// (tcgen05 / TMEM), fed by TMA and cp.async gathers.
 //
-// Same semantics as the query-major forward (K1/K5 of the reference:
-// hf-model-code/sparse_gather_triton.py:35-122, sparse_gather_e2e_triton.py:36-121),
-// split in two passes so that every MMA has M = 128 real rows:
+// Same semantics as the query-major kernels (K1/K5 of the reference:
+// hf-model-code/sparse_gather_triton.py:35-122, sparse_gather_e2e_triton.py:36-121,
+// and their backward), split in two passes so that every MMA has M = 128
+// real rows:
 //
-//  1. remote pass (remote_fwd_kernel): the selection is inverted into per
+//  1. remote pass (remote_ws_kernel): the selection is inverted into per
 //     (batch, index head, block) lists of (query, slot) pairs; a work item is
-//     one block and up to 128 of its pairs for one query head.  The pairs' q
-//     rows are gathered into shared memory, S = Q_g K_blk^T (M=128, N=64,
+//     one selected block of one query head with all of its pairs, in tiles of
+//     128 rows gathered into shared memory.  S = Q_g K_blk^T (M=128, N=64,
 //     K=128) goes to TMEM, the per-row softmax (slot bias, keys below the
 //     query's window start) runs on the 128 rows, O = P V_blk (N=128) goes to
 //     TMEM and the normalised partial (o bf16, lse fp32 log2) is written to a
 //     [B, T, S, HQ, D] workspace.
-//  2. band pass (band_fwd_kernel): one CTA per (batch, head, 128-query tile)
-//     walks the ~LW/64 + 2 key blocks of the local window with an online
-//     softmax (lazy rescaling of O in TMEM when the running max grows by more
-//     than 2^8), then merges each row with its remote partials (log-sum-exp
-//     weights) and writes o and lse.
+//  2. band pass (fwd_ws_kernel): per (batch, head, 128-query tile) the ~LW/64
+//     + 2 key blocks of the local window go through an online softmax (lazy
+//     rescaling of O in TMEM when the running max grows by more than 2^8) and
+//     the window result (o, lse) is written.
+//  3. merge_partials_kernel folds each row's remote partials into the window
+//     result with log-sum-exp weights.
 //
+// The backward mirrors it: bwd_remote_ws_kernel (dK/dV/dq partials per
+// selected block), bwd_band_dq_ws_kernel and bwd_band_dkdv_ws_kernel (the
+// window), then bandwidth-bound merges of the dq and dK/dV partials.
+//
+// All kernels are warp-specialised and persistent: producer warps (TMA or
+// cp.async), one MMA-issuing thread, and softmax / compute warpgroups, tied
+// by mbarriers.  Every wait is bounded; an expired wait sets an abort flag,
+// the MMA warp drains the tensor pipe with a final commit and TMEM is freed.
 // Shared-memory operand layout: see tc.cuh (128-byte swizzle, K-major Q/K/P,
-// MN-major V).  Every mbarrier is waited on by thread 0 only, with a bounded
-// spin; the result is broadcast through __syncthreads so an expired wait takes
-// a CTA-uniform exit path that drains the tensor pipe and frees TMEM.
+// MN-major V).
 
 #include <cuda.h>  // CUtensorMap (the encoder is looked up at run time; libcuda is not linked)
 
@@ -31,11 +40,9 @@
 
 namespace srswa {
 
-constexpr int kTcThreads = 128;
 constexpr int kTileM = 128;
 constexpr int kBlk = 64;        // key block (BS)
 constexpr int kD = 128;         // head dim
-constexpr uint32_t kTmemCols = 256;
 constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (factor 256)
 
 // smem layout of the band kernel (bytes, 1024-aligned pieces)
@@ -44,9 +51,6 @@ constexpr uint32_t kKVHalf = kBlk * 128;        // [64 rows x 128 B]
 constexpr uint32_t kKVBytes = 2 * kKVHalf;      // one 64 x 128 operand
 constexpr uint32_t kPBytes = kTileM * 128;      // [128 x 64 keys] bf16 (fits a K operand's 16 KB)
 // P of a block is written over that block's K operand, dead once S is in TMEM
-constexpr uint32_t kBandSmem = kQBytes + 2 * 2 * kKVBytes + 1024;  // + alignment slack -> 2 CTAs/SM
-constexpr uint32_t kRemoteSmem = kQBytes + 2 * kKVBytes + 1024;     // -> 3 CTAs/SM
-constexpr uint32_t kRemoteTmemCols = 128;  // S (cols 0-63) is dead before O (cols 0-127) is written
 
 struct TcArgs {
   const __nv_bfloat16* q;
@@ -90,20 +94,6 @@ __device__ __forceinline__ void remote_range(const TcArgs& a, int64_t b, int64_t
   hi = min(min((blk + 1) * kBlk, ls), t + 1);
 }
 
-// 16-byte chunk loads of a [rows x 128] bf16 operand into the two swizzled
-// halves at sbase; row r of the operand comes from src(r) (null -> zeros).
-template <int ROWS, typename RowPtr>
-__device__ __forceinline__ void load_operand(uint32_t sbase, uint32_t half_bytes, RowPtr src, int tid,
-                                             const void* any_valid) {
-#pragma unroll
-  for (int i = 0; i < ROWS * 16 / kTcThreads; ++i) {
-    const int id = tid + i * kTcThreads;
-    const int r = id >> 4, c = id & 15;
-    const __nv_bfloat16* g = src(r);
-    const uint32_t dst = sbase + (c >> 3) * half_bytes + sw128_off(r, c & 7);
-    cp_async16_zfill(dst, g ? static_cast<const void*>(g + c * 8) : any_valid, g != nullptr);
-  }
-}
 
 // 32 fp32 -> 32 bf16 stored as four 16-byte chunks of a swizzled P row
 __device__ __forceinline__ void store_p_row(uint32_t pbase, int r, int chunk0, const float* p) {
@@ -141,229 +131,6 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t p_s, uint32_t
     const uint64_t bd = sw128_desc(v_s + ks * 2048u, kKVHalf, 1024);
     mma_bf16_ss(tmem_o, ad, bd, id, (accumulate || ks > 0) ? 1u : 0u);
   }
-}
-
-// ============================================================================
-// band pass
-// ============================================================================
-__global__ void __launch_bounds__(kTcThreads) band_fwd_kernel(const TcArgs a) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t bar_s, bar_o;
-  __shared__ uint32_t tmem_base;
-  __shared__ int ok_s;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int64_t G = a.HQ / a.Hkv;
-  const int64_t hk = h / G;
-  const int64_t t0 = tile * kTileM;
-
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t q_s = sbase;
-  const uint32_t kv_s = q_s + kQBytes;  // stage st: K at kv_s + st*2*kKVBytes, V after it
-
-  if (warp == 0) {
-    tmem_alloc(&tmem_base, kTmemCols);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    mbar_init(&bar_s, 1);
-    mbar_init(&bar_o, 1);
-    fence_mbar_init();
-    ok_s = 1;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_base;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t tm_s = tmem, tm_o = tmem + 128;
-
-  // this thread's row
-  const int64_t t = t0 + tid;
-  const bool row_ok = t < a.T;
-  const int64_t ls = row_ok ? win_start(a, b, t) : 0;
-
-  // key blocks of the tile's window
-  const int64_t tlast = min(a.T, t0 + kTileM) - 1;
-  int64_t key_lo = t0 - a.LW + 1;
-  if (key_lo < 0) key_lo = 0;
-  const int64_t blo = key_lo / kBlk, bhi = tlast / kBlk;
-
-  auto q_row = [&](int r) -> const __nv_bfloat16* {
-    const int64_t tt = t0 + r;
-    return tt < a.T ? a.q + b * a.sqb + tt * a.sqt + h * a.sqh : nullptr;
-  };
-  auto kv_rows = [&](int64_t blk, const __nv_bfloat16* base, int64_t sb, int64_t st, int64_t sh) {
-    return [=](int r) -> const __nv_bfloat16* {
-      const int64_t kk = blk * kBlk + r;
-      return kk < a.T ? base + b * sb + kk * st + hk * sh : nullptr;
-    };
-  };
-  load_operand<kTileM>(q_s, kQBytes / 2, q_row, tid, a.q);
-  load_operand<kBlk>(kv_s, kKVHalf, kv_rows(blo, a.k, a.skb, a.skt, a.skh), tid, a.k);
-  load_operand<kBlk>(kv_s + kKVBytes, kKVHalf, kv_rows(blo, a.v, a.svb, a.svt, a.svh), tid, a.v);
-  cp_async_commit();
-
-  float m_ref = -INFINITY, l = 0.f;
-  bool aborted = false;
-  for (int64_t j = blo; j <= bhi; ++j) {
-    const int jj = static_cast<int>(j - blo);
-    const int st = jj & 1;
-    // block j's operands have landed (its group; the prefetch group may pend)
-    cp_async_wait<0>();
-    fence_async_smem();
-    __syncthreads();
-    const uint32_t k_cur = kv_s + st * 2 * kKVBytes;
-    if (tid == 0) {
-      // S_j queues behind P.V_{j-1}; its completion implies P.V_{j-1} done
-      tc_fence_after();
-      issue_qk(tm_s, q_s, k_cur);
-      mma_commit(&bar_s);
-      ok_s = mbar_wait(&bar_s, jj & 1, 102) ? 1 : 0;
-    }
-    __syncthreads();
-    if (!ok_s) { aborted = true; break; }
-    // the other stage (block j-1, its P.V done) is free: prefetch block j+1
-    if (j + 1 <= bhi) {
-      const uint32_t nx = kv_s + (st ^ 1) * 2 * kKVBytes;
-      load_operand<kBlk>(nx, kKVHalf, kv_rows(j + 1, a.k, a.skb, a.skt, a.skh), tid, a.k);
-      load_operand<kBlk>(nx + kKVBytes, kKVHalf, kv_rows(j + 1, a.v, a.svb, a.svt, a.svh), tid, a.v);
-    }
-    cp_async_commit();
-    tc_fence_after();
-    // ---- softmax of this row over the block's 64 keys ----
-    float s[64];
-    {
-      float s0[32], s1[32];
-      tmem_ld32(tm_s + lane_off, s0);
-      tmem_ld32(tm_s + lane_off + 32, s1);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) { s[i] = s0[i]; s[32 + i] = s1[i]; }
-    }
-    const int64_t k0 = j * kBlk;
-    float mloc = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const int64_t key = k0 + i;
-      const bool valid = row_ok && key >= ls && key <= t;
-      s[i] = valid ? s[i] * a.scale_log2 : -INFINITY;
-      mloc = fmaxf(mloc, s[i]);
-    }
-    const bool need = mloc > m_ref + kRescaleLog2;  // also true on the first valid block
-    const float alpha = need ? (m_ref == -INFINITY ? 0.f : exp2f(m_ref - mloc)) : 1.f;
-    if (need) {
-      l *= alpha;
-      m_ref = mloc;
-    }
-    if (__any_sync(0xffffffffu, need && jj > 0)) {  // rescale O rows of this warp in TMEM
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float ov[32];
-        tmem_ld32(tm_o + lane_off + 32 * c, ov);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-        tmem_st32(tm_o + lane_off + 32 * c, ov);
-      }
-      tmem_wait_st();
-    }
-    float lsum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const float p = (s[i] == -INFINITY) ? 0.f : exp2f(s[i] - m_ref);
-      s[i] = p;
-      lsum += p;
-    }
-    l += lsum;
-    store_p_row(k_cur, tid, 0, s);  // P over the dead K operand of this stage
-    store_p_row(k_cur, tid, 4, s + 32);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      issue_pv(tm_o, k_cur, k_cur + kKVBytes, jj > 0);
-      mma_commit(&bar_o);
-    }
-  }
-  const int nblocks = static_cast<int>(bhi - blo + 1);
-  // drain: the last P.V (or, after an abort, whatever was committed)
-  if (tid == 0) ok_s = mbar_wait(&bar_o, (nblocks - 1) & 1, 103) ? 1 : 0;
-  __syncthreads();
-  cp_async_wait<0>();
-  if (!aborted && ok_s) {
-    tc_fence_after();
-    // ---- epilogue: merge with remote partials, write o and lse ----
-    const int64_t hi = (hk * a.HI) / a.Hkv;
-    float M = (l > 0.f) ? m_ref + log2f(l) : -INFINITY;
-    float lse_s[64];
-    int64_t slot_base = 0;
-    int nslot = 0;
-    if (row_ok && a.part_o) {
-      const int32_t* srow = a.sel + ((b * a.HI + hi) * a.T + t) * a.S;
-      slot_base = ((b * a.T + t) * a.S) * a.HQ + h;
-      for (int64_t s2 = 0; s2 < a.S && s2 < 64; ++s2) {
-        lse_s[s2] = -INFINITY;
-        const int64_t blk = srow[s2];
-        if (blk < 0 || blk >= a.nblk) continue;
-        int64_t lo, hi2;
-        remote_range(a, b, t, blk, lo, hi2);
-        if (lo >= hi2) continue;
-        bool dup = false;
-        for (int64_t u = 0; u < s2; ++u) dup |= srow[u] == blk;
-        if (dup) continue;
-        lse_s[s2] = a.part_lse[slot_base + s2 * a.HQ];
-        M = fmaxf(M, lse_s[s2]);
-      }
-      nslot = static_cast<int>(a.S < 64 ? a.S : 64);
-    }
-    const float Mu = (M == -INFINITY) ? 0.f : M;
-    const float wb = (l > 0.f) ? exp2f(m_ref - Mu) : 0.f;
-    float den = l * wb;
-    for (int s2 = 0; s2 < nslot; ++s2)
-      if (lse_s[s2] != -INFINITY) den += exp2f(lse_s[s2] - Mu);
-    const float inv = den > 0.f ? 1.f / den : 0.f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float ov[32];
-      tmem_ld32(tm_o + lane_off + 32 * c, ov);
-      tmem_wait_ld();
-      if (row_ok) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ov[i] *= wb;
-        for (int s2 = 0; s2 < nslot; ++s2) {
-          if (lse_s[s2] == -INFINITY) continue;
-          const float w = exp2f(lse_s[s2] - Mu);
-          const uint4* src = reinterpret_cast<const uint4*>(a.part_o + (slot_base + s2 * a.HQ) * kD + 32 * c);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const uint4 u = src[q4];
-            ov[8 * q4 + 0] = fmaf(w, bf16_lo(u.x), ov[8 * q4 + 0]);
-            ov[8 * q4 + 1] = fmaf(w, bf16_hi(u.x), ov[8 * q4 + 1]);
-            ov[8 * q4 + 2] = fmaf(w, bf16_lo(u.y), ov[8 * q4 + 2]);
-            ov[8 * q4 + 3] = fmaf(w, bf16_hi(u.y), ov[8 * q4 + 3]);
-            ov[8 * q4 + 4] = fmaf(w, bf16_lo(u.z), ov[8 * q4 + 4]);
-            ov[8 * q4 + 5] = fmaf(w, bf16_hi(u.z), ov[8 * q4 + 5]);
-            ov[8 * q4 + 6] = fmaf(w, bf16_lo(u.w), ov[8 * q4 + 6]);
-            ov[8 * q4 + 7] = fmaf(w, bf16_hi(u.w), ov[8 * q4 + 7]);
-          }
-        }
-        __nv_bfloat16* dst = a.o + b * a.sob + t * a.sot + h * a.soh + 32 * c;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float tmp[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
-          store8(dst, 8 * q4, SRSWA_BF16, tmp);
-        }
-      }
-    }
-    if (row_ok && a.lse) a.lse[(b * a.T + t) * a.HQ + h] = den > 0.f ? (Mu + log2f(den)) * kLn2 : -INFINITY;
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
 
 // ============================================================================
@@ -450,151 +217,6 @@ __global__ void pairs_fill_kernel(const TcArgs a, int32_t* cursor, int32_t* pair
       a.pair_bias[pos] = a.bias ? a.bias[(b * a.T + t) * a.S + s] * kLog2e : 0.f;
     }
   }
-}
-
-// One work item = (tile, query head of the tile's index head).  Persistent:
-// grid-stride over items; the item count comes from device memory.
-__global__ void __launch_bounds__(kTcThreads) remote_fwd_kernel(const TcArgs a) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t bar;
-  __shared__ uint32_t tmem_base;
-  __shared__ int ok_s;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t q_s = sbase;
-  const uint32_t k_s = q_s + kQBytes;
-  const uint32_t v_s = k_s + kKVBytes;
-  const uint32_t p_s = k_s;  // P over K (dead once S is in TMEM)
-  if (warp == 0) {
-    tmem_alloc(&tmem_base, kRemoteTmemCols);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-    ok_s = 1;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_base;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t tm_s = tmem, tm_o = tmem;  // O overwrites S after the softmax read it
-  const int64_t hpi = a.HQ / a.HI;  // query heads per index head
-  const int64_t nitems = static_cast<int64_t>(*a.ntiles) * hpi;
-  uint32_t phase = 0;
-  for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x) {
-    const int4 td = a.tiles[item / hpi];
-    const int64_t bh = td.x, blk = td.y, first = td.z, cnt = td.w;
-    const int64_t b = bh / a.HI, hi = bh % a.HI;
-    const int64_t h = hi * hpi + item % hpi;
-    const int64_t hk = h / (a.HQ / a.Hkv);
-    // this thread's pair
-    int64_t t = -1, slot = 0;
-    if (tid < cnt) {
-      const int32_t pk = a.pairs[first + tid];
-      t = pk / a.S;
-      slot = pk % a.S;
-    }
-    auto q_row = [&](int r) -> const __nv_bfloat16* {
-      if (r >= cnt) return nullptr;
-      const int32_t pk = a.pairs[first + r];
-      return a.q + b * a.sqb + static_cast<int64_t>(pk / a.S) * a.sqt + h * a.sqh;
-    };
-    auto k_row = [&](int r) -> const __nv_bfloat16* {
-      const int64_t kk = blk * kBlk + r;
-      return kk < a.T ? a.k + b * a.skb + kk * a.skt + hk * a.skh : nullptr;
-    };
-    auto v_row = [&](int r) -> const __nv_bfloat16* {
-      const int64_t kk = blk * kBlk + r;
-      return kk < a.T ? a.v + b * a.svb + kk * a.svt + hk * a.svh : nullptr;
-    };
-    load_operand<kTileM>(q_s, kQBytes / 2, q_row, tid, a.q);
-    load_operand<kBlk>(k_s, kKVHalf, k_row, tid, a.k);
-    load_operand<kBlk>(v_s, kKVHalf, v_row, tid, a.v);
-    cp_async_commit();
-    cp_async_wait<0>();
-    fence_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      issue_qk(tm_s, q_s, k_s);
-      mma_commit(&bar);
-      ok_s = mbar_wait(&bar, phase, 201) ? 1 : 0;
-    }
-    phase ^= 1;
-    __syncthreads();
-    if (!ok_s) break;
-    tc_fence_after();
-    float s[64];
-    {
-      float s0[32], s1[32];
-      tmem_ld32(tm_s + lane_off, s0);
-      tmem_ld32(tm_s + lane_off + 32, s1);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) { s[i] = s0[i]; s[32 + i] = s1[i]; }
-    }
-    float m = -INFINITY;
-    int64_t lo = 0, hi2 = 0;
-    float bias2 = 0.f;
-    if (t >= 0) {
-      remote_range(a, b, t, blk, lo, hi2);
-      if (a.bias) bias2 = a.bias[(b * a.T + t) * a.S + slot] * kLog2e;
-    }
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const int64_t key = blk * kBlk + i;
-      const bool valid = t >= 0 && key >= lo && key < hi2;
-      s[i] = valid ? s[i] * a.scale_log2 + bias2 : -INFINITY;
-      m = fmaxf(m, s[i]);
-    }
-    float lsum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const float p = (s[i] == -INFINITY) ? 0.f : exp2f(s[i] - m);
-      s[i] = p;
-      lsum += p;
-    }
-    store_p_row(p_s, tid, 0, s);
-    store_p_row(p_s, tid, 4, s + 32);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      issue_pv(tm_o, p_s, v_s, false);
-      mma_commit(&bar);
-      ok_s = mbar_wait(&bar, phase, 202) ? 1 : 0;
-    }
-    phase ^= 1;
-    __syncthreads();
-    if (!ok_s) break;
-    tc_fence_after();
-    const int64_t prow = ((b * a.T + (t < 0 ? 0 : t)) * a.S + slot) * a.HQ + h;
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float ov[32];
-      tmem_ld32(tm_o + lane_off + 32 * c, ov);
-      tmem_wait_ld();
-      if (t >= 0) {
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float tmp[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
-          store8(a.part_o + prow * kD + 32 * c, 8 * q4, SRSWA_BF16, tmp);
-        }
-      }
-    }
-    if (t >= 0) a.part_lse[prow] = lsum > 0.f ? m + log2f(lsum) : -INFINITY;
-    tc_fence_before();
-    __syncthreads();  // smem and TMEM reuse by the next item
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, kRemoteTmemCols);
 }
 
 // ============================================================================
@@ -685,45 +307,29 @@ __device__ __forceinline__ float block_row_exp(float (&sv)[64], float c, float o
 }
 __device__ __forceinline__ int clamp_key(int64_t v) { return static_cast<int>(v < 0 ? 0 : (v > kBlk ? kBlk : v)); }
 
+// A band work item: (b, h, 128-query tile) and its window's key blocks.
 struct WsItem {
   int64_t b, h, hk;
-  int64_t blo, bhi;     // key blocks, inclusive
-  int64_t t0;           // band: first query row
-  int64_t first, cnt;   // remote: pair range
+  int64_t blo, bhi;  // key blocks, inclusive
+  int64_t t0;        // first query row
 };
 
-template <bool kRemote>
 __device__ __forceinline__ int64_t ws_num_items(const TcArgs& a) {
-  if (kRemote) return static_cast<int64_t>(*a.ntiles) * (a.HQ / a.HI);
   return a.B * a.HQ * ((a.T + kTileM - 1) / kTileM);
 }
 
-template <bool kRemote>
 __device__ __forceinline__ WsItem ws_item(const TcArgs& a, int64_t item) {
   WsItem w;
-  if (kRemote) {
-    const int64_t hpi = a.HQ / a.HI;
-    const int4 td = a.tiles[item / hpi];
-    w.b = td.x / a.HI;
-    w.h = (td.x % a.HI) * hpi + item % hpi;
-    w.blo = w.bhi = td.y;
-    w.first = td.z;
-    w.cnt = td.w;
-    w.t0 = 0;
-  } else {
-    const int64_t nt = (a.T + kTileM - 1) / kTileM;
-    const int64_t tile = item % nt, bh = item / nt;
-    w.b = bh / a.HQ;
-    w.h = bh % a.HQ;
-    w.t0 = tile * kTileM;
-    const int64_t tlast = min(a.T, w.t0 + kTileM) - 1;
-    int64_t key_lo = w.t0 - a.LW + 1;
-    if (key_lo < 0) key_lo = 0;
-    w.blo = key_lo / kBlk;
-    w.bhi = tlast / kBlk;
-    w.first = 0;
-    w.cnt = 0;
-  }
+  const int64_t nt = (a.T + kTileM - 1) / kTileM;
+  const int64_t tile = item % nt, bh = item / nt;
+  w.b = bh / a.HQ;
+  w.h = bh % a.HQ;
+  w.t0 = tile * kTileM;
+  const int64_t tlast = min(a.T, w.t0 + kTileM) - 1;
+  int64_t key_lo = w.t0 - a.LW + 1;
+  if (key_lo < 0) key_lo = 0;
+  w.blo = key_lo / kBlk;
+  w.bhi = tlast / kBlk;
   w.hk = w.h / (a.HQ / a.Hkv);
   return w;
 }
@@ -731,7 +337,6 @@ __device__ __forceinline__ WsItem ws_item(const TcArgs& a, int64_t item) {
 // The step sequence of one slot: its items (blockIdx.x + (2m + slot) *
 // gridDim.x) and, inside each, the key blocks blo..bhi.  Every role walks the
 // same sequence.
-template <bool kRemote>
 struct WsCursor {
   int64_t item, nitems, m, j, n;
   WsItem w;
@@ -743,7 +348,7 @@ struct WsCursor {
     n = 0;
     done = item >= nitems;
     if (!done) {
-      w = ws_item<kRemote>(a, item);
+      w = ws_item(a, item);
       j = w.blo;
     }
   }
@@ -759,25 +364,11 @@ struct WsCursor {
     item += 2 * static_cast<int64_t>(gridDim.x);
     done = item >= nitems;
     if (!done) {
-      w = ws_item<kRemote>(a, item);
+      w = ws_item(a, item);
       j = w.blo;
     }
   }
 };
-
-// [ROWS x 128] bf16 operand rows -> swizzled halves, issued by one warp
-template <int ROWS, typename RowPtr>
-__device__ __forceinline__ void warp_load_operand(uint32_t sbase, uint32_t half_bytes, RowPtr src, int lane,
-                                                  const void* any_valid) {
-#pragma unroll 4
-  for (int i = 0; i < ROWS * 16 / 32; ++i) {
-    const int id = lane + i * 32;
-    const int r = id >> 4, c = id & 15;
-    const __nv_bfloat16* g = src(r);
-    const uint32_t dst = sbase + (c >> 3) * half_bytes + sw128_off(r, c & 7);
-    cp_async16_zfill(dst, g ? static_cast<const void*>(g + c * 8) : any_valid, g != nullptr);
-  }
-}
 
 // Band epilogue of one row in the warp-specialised kernel: the window-only
 // result, o = O / l (bf16) and lse (ln); merge_partials_kernel folds the
@@ -873,95 +464,11 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const TcArgs a) {
   if (lane == 0) *lse_p = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
 }
 
-// Band epilogue of one row: merge the window softmax state (m_ref, l in
-// log2 units) with the row's remote partials, write o (bf16) and lse (ln).
-// Called by whole warps (tcgen05.ld is warp-collective).
-__device__ __forceinline__ void band_row_epilogue(const TcArgs& a, int64_t b, int64_t h, int64_t hk, int64_t t,
-                                                  bool row_ok, float m_ref, float l, uint32_t tm_o_row) {
-  const int64_t hi = (hk * a.HI) / a.Hkv;
-  float M = (l > 0.f) ? m_ref + log2f(l) : -INFINITY;
-  float lse_s[64];
-  int64_t slot_base = 0;
-  int nslot = 0;
-  if (row_ok && a.part_o) {
-    const int32_t* srow = a.sel + ((b * a.HI + hi) * a.T + t) * a.S;
-    slot_base = ((b * a.T + t) * a.S) * a.HQ + h;
-    for (int64_t s2 = 0; s2 < a.S && s2 < 64; ++s2) {
-      lse_s[s2] = -INFINITY;
-      const int64_t blk = srow[s2];
-      if (blk < 0 || blk >= a.nblk) continue;
-      int64_t lo, hi2;
-      remote_range(a, b, t, blk, lo, hi2);
-      if (lo >= hi2) continue;
-      bool dup = false;
-      for (int64_t u = 0; u < s2; ++u) dup |= srow[u] == blk;
-      if (dup) continue;
-      lse_s[s2] = a.part_lse[slot_base + s2 * a.HQ];
-      M = fmaxf(M, lse_s[s2]);
-    }
-    nslot = static_cast<int>(a.S < 64 ? a.S : 64);
-  }
-  const float Mu = (M == -INFINITY) ? 0.f : M;
-  const float wb = (l > 0.f) ? exp2f(m_ref - Mu) : 0.f;
-  float den = l * wb;
-  for (int s2 = 0; s2 < nslot; ++s2)
-    if (lse_s[s2] != -INFINITY) den += exp2f(lse_s[s2] - Mu);
-  const float inv = den > 0.f ? 1.f / den : 0.f;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    float ov[32];
-    tmem_ld32(tm_o_row + 32 * c, ov);
-    tmem_wait_ld();
-    if (row_ok) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) ov[i] *= wb;
-      for (int s2 = 0; s2 < nslot; ++s2) {
-        if (lse_s[s2] == -INFINITY) continue;
-        const float w = exp2f(lse_s[s2] - Mu);
-        const uint4* src = reinterpret_cast<const uint4*>(a.part_o + (slot_base + s2 * a.HQ) * kD + 32 * c);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const uint4 u = src[q4];
-          ov[8 * q4 + 0] = fmaf(w, bf16_lo(u.x), ov[8 * q4 + 0]);
-          ov[8 * q4 + 1] = fmaf(w, bf16_hi(u.x), ov[8 * q4 + 1]);
-          ov[8 * q4 + 2] = fmaf(w, bf16_lo(u.y), ov[8 * q4 + 2]);
-          ov[8 * q4 + 3] = fmaf(w, bf16_hi(u.y), ov[8 * q4 + 3]);
-          ov[8 * q4 + 4] = fmaf(w, bf16_lo(u.z), ov[8 * q4 + 4]);
-          ov[8 * q4 + 5] = fmaf(w, bf16_hi(u.z), ov[8 * q4 + 5]);
-          ov[8 * q4 + 6] = fmaf(w, bf16_lo(u.w), ov[8 * q4 + 6]);
-          ov[8 * q4 + 7] = fmaf(w, bf16_hi(u.w), ov[8 * q4 + 7]);
-        }
-      }
-      __nv_bfloat16* dst = a.o + b * a.sob + t * a.sot + h * a.soh + 32 * c;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float tmp[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
-        store8(dst, 8 * q4, SRSWA_BF16, tmp);
-      }
-    }
-  }
-  if (row_ok && a.lse) a.lse[(b * a.T + t) * a.HQ + h] = den > 0.f ? (Mu + log2f(den)) * kLn2 : -INFINITY;
-}
-
-// tmq / tmk / tmv: 4-D tensor maps over q, k, v ([B,T,H,D] with their
-// strides; dims ordered D, T, H, B) with 128-byte swizzle: boxes of 64
-// features x 128 query rows (tmq) or x 64 key rows (tmk, tmv) land in shared
-// memory in the K-major layout the MMAs read.  The gathered q rows of the
-// remote pass are copied with cp.async through a per-tile row table.
-template <bool kRemote>
 __global__ void __launch_bounds__(kWsThreads, 1)
     fwd_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ uint64_t q_full[2], q_empty[2], kv_full[2][2], kv_empty[2][2], s_full[2], p_full[2], o_full[2];
-  __shared__ const __nv_bfloat16* qrows[2][kTileM];
-  // remote pass: each row's (query, slot, bias * log2 e), resolved by the
-  // producer per item (double-buffered by item parity) and published on info_full
-  __shared__ int32_t r_t[2][2][kTileM], r_slot[2][2][kTileM];
-  __shared__ float r_bias[2][2][kTileM];
-  __shared__ uint64_t info_full[2][2];
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -975,7 +482,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   }
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&q_full[s], kRemote ? 32 : 1);
+      mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], kTileM);
@@ -985,8 +492,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         mbar_init(&kv_empty[s][st], 1);
       }
     }
-    for (int s = 0; s < 2; ++s)
-      for (int pb = 0; pb < 2; ++pb) mbar_init(&info_full[s][pb], 32);
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
     abort_flag = 0;
@@ -996,17 +501,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base;
   volatile int* abort_p = &abort_flag;
-  const int64_t nitems = ws_num_items<kRemote>(a);
+  const int64_t nitems = ws_num_items(a);
 
   if (warp == kWsProducer) {
     // ---------------------------------------------------------------- producer
-    WsCursor<kRemote> c[2];
+    WsCursor c[2];
     c[0].start(a, 0, nitems);
     c[1].start(a, 1, nitems);
     bool ok = true;
     while (ok && !(c[0].done && c[1].done)) {
       for (int s = 0; s < 2 && ok; ++s) {
-        WsCursor<kRemote>& cs = c[s];
+        WsCursor& cs = c[s];
         if (cs.done) continue;
         const WsItem& w = cs.w;
         if (cs.first()) {
@@ -1015,41 +520,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             ok = false;
             break;
           }
-          if (kRemote) {
-            // row table: lane L resolves rows L, L+32, L+64, L+96 of the pair tile
-            const int pb = static_cast<int>(cs.m & 1);
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              const int r = lane + 32 * k4;
-              const __nv_bfloat16* p = nullptr;
-              int32_t tt = -1, sl = 0;
-              float bz = 0.f;
-              if (r < w.cnt) {
-                const int32_t pk = a.pairs[w.first + r];
-                tt = pk / static_cast<int32_t>(a.S);
-                sl = pk - tt * static_cast<int32_t>(a.S);
-                p = a.q + w.b * a.sqb + static_cast<int64_t>(tt) * a.sqt + w.h * a.sqh;
-                if (a.bias) bz = a.bias[(w.b * a.T + tt) * a.S + sl] * kLog2e;
-              }
-              qrows[s][r] = p;
-              r_t[s][pb][r] = tt;
-              r_slot[s][pb][r] = sl;
-              r_bias[s][pb][r] = bz;
-            }
-            mbar_arrive(&info_full[s][pb]);  // release: the row info above
-            __syncwarp();
-            const int c = lane & 15;
-            const uint32_t dst0 = q_s(s) + (c >> 3) * (kQBytes / 2);
-#pragma unroll 8
-            for (int i = 0; i < kTileM / 2; ++i) {
-              const int r = (lane >> 4) + 2 * i;
-              const __nv_bfloat16* g = qrows[s][r];
-              cp_async16_zfill(dst0 + sw128_off(r, c & 7), g ? static_cast<const void*>(g + c * 8) : a.q,
-                               g != nullptr);
-            }
-            cp_async_mbar_arrive(&q_full[s]);
-            __syncwarp();
-          } else if (lane == 0) {
+          if (lane == 0) {
             mbar_arrive_expect_tx(&q_full[s], kQBytes);
             tma_load_4d(q_s(s), &tmq, 0, static_cast<int>(w.t0), static_cast<int>(w.h), static_cast<int>(w.b),
                         &q_full[s]);
@@ -1077,18 +548,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         cs.advance(a);
       }
     }
-    cp_async_wait_all();
   } else if (warp == kWsMma) {
     // --------------------------------------------------------------------- MMA
     if (lane == 0) {
-      WsCursor<kRemote> c[2];
+      WsCursor c[2];
       c[0].start(a, 0, nitems);
       c[1].start(a, 1, nitems);
       bool pend[2] = {false, false}, pfirst[2] = {false, false}, plast[2] = {false, false};
       int64_t pn[2] = {0, 0};
       bool ok = true;
       auto issue_s = [&](int s) -> bool {
-        WsCursor<kRemote>& cs = c[s];
+        WsCursor& cs = c[s];
         const int st = static_cast<int>(cs.n & 1);
         if (!ws_wait(&kv_full[s][st], static_cast<uint32_t>((cs.n >> 1) & 1), abort_p, 403)) return false;
         if (cs.first() && !ws_wait(&q_full[s], static_cast<uint32_t>(cs.m & 1), abort_p, 404)) return false;
@@ -1129,10 +599,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const int r = tid & (kTileM - 1);
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tm_s = tmem + s * 256 + lane_off, tm_o = tmem + s * 256 + 128 + lane_off;
-    WsCursor<kRemote> cs;
+    WsCursor cs;
     cs.start(a, s, nitems);
-    float m_ref = -INFINITY, l = 0.f, bias2 = 0.f;
-    int64_t t = -1, slot = 0, ls = 0, rlo = 0, rhi = 0;
+    float m_ref = -INFINITY, l = 0.f;
+    int64_t t = -1, ls = 0;
     bool row_ok = false;
     while (!cs.done) {
       const WsItem& w = cs.w;
@@ -1140,22 +610,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (first) {
         m_ref = -INFINITY;
         l = 0.f;
-        bias2 = 0.f;
-        if (kRemote) {
-          const int pb = static_cast<int>(cs.m & 1);
-          if (!__all_sync(0xffffffffu, ws_wait(&info_full[s][pb], static_cast<uint32_t>((cs.m >> 1) & 1), abort_p,
-                                               409)))
-            break;
-          t = r_t[s][pb][r];
-          slot = r_slot[s][pb][r];
-          bias2 = r_bias[s][pb][r];
-          row_ok = t >= 0;
-          if (row_ok) remote_range(a, w.b, t, w.blo, rlo, rhi);
-        } else {
-          t = w.t0 + r;
-          row_ok = t < a.T;
-          ls = row_ok ? win_start(a, w.b, t) : 0;
-        }
+        t = w.t0 + r;
+        row_ok = t < a.T;
+        ls = row_ok ? win_start(a, w.b, t) : 0;
       }
       // warp-uniform outcome: the TMEM accesses below are warp-collective
       if (!__all_sync(0xffffffffu, ws_wait(&s_full[s], static_cast<uint32_t>(cs.n & 1), abort_p, 406))) break;
@@ -1172,19 +629,19 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int64_t k0 = cs.j * kBlk;
       int klo = 0, khi = 0;  // this row's valid keys of the block, relative
       if (row_ok) {
-        klo = clamp_key((kRemote ? rlo : ls) - k0);
-        khi = clamp_key((kRemote ? rhi : t + 1) - k0);
+        klo = clamp_key(ls - k0);
+        khi = clamp_key(t + 1 - k0);
       }
       const bool full = __all_sync(0xffffffffu, klo == 0 && khi == kBlk);
       const float mraw = block_row_max(sv, klo, khi, full);
-      const float mloc = mraw == -INFINITY ? -INFINITY : fmaf(mraw, a.scale_log2, bias2);
+      const float mloc = mraw == -INFINITY ? -INFINITY : mraw * a.scale_log2;
       const bool need = mloc > m_ref + kRescaleLog2;
       const float alpha = need ? (m_ref == -INFINITY ? 0.f : exp2f(m_ref - mloc)) : 1.f;
       if (need) {
         l *= alpha;
         m_ref = mloc;
       }
-      if (!kRemote && __any_sync(0xffffffffu, need && !first)) {
+      if (__any_sync(0xffffffffu, need && !first)) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float ov[32];
@@ -1196,7 +653,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         }
         tmem_wait_st();
       }
-      l += block_row_exp(sv, a.scale_log2, bias2 - (m_ref == -INFINITY ? 0.f : m_ref));
+      l += block_row_exp(sv, a.scale_log2, m_ref == -INFINITY ? 0.f : -m_ref);
       const uint32_t p_s = kv_s(s, static_cast<int>(cs.n & 1));  // P over this stage's dead K
       store_p_row(p_s, r, 0, sv);
       store_p_row(p_s, r, 4, sv + 32);
@@ -1206,28 +663,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (last) {
         if (!__all_sync(0xffffffffu, ws_wait(&o_full[s], static_cast<uint32_t>(cs.m & 1), abort_p, 407))) break;
         tc_fence_after();
-        if (kRemote) {
-          const int64_t prow = ((w.b * a.T + (row_ok ? t : 0)) * a.S + slot) * a.HQ + w.h;
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float ov[32];
-            tmem_ld32(tm_o + 32 * c, ov);
-            tmem_wait_ld();
-            if (row_ok) {
-#pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) {
-                float tmp[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
-                store8(a.part_o + prow * kD + 32 * c, 8 * q4, SRSWA_BF16, tmp);
-              }
-            }
-          }
-          if (row_ok) a.part_lse[prow] = l > 0.f ? m_ref + log2f(l) : -INFINITY;
-        } else {
-          band_row_store(a, w.b, w.h, t, row_ok, m_ref, l, tm_o);
-        }
+        band_row_store(a, w.b, w.h, t, row_ok, m_ref, l, tm_o);
         tc_fence_before();
       }
       cs.advance(a);
@@ -1615,32 +1051,8 @@ __device__ __forceinline__ void issue_tn(uint32_t tmem_d, uint32_t a_s, uint32_t
     mma_bf16_ss(tmem_d, ad, bd, id, (accumulate || ks > 0) ? 1u : 0u);
   }
 }
-// D = A B^T, A and B K-major [128 rows x 128]: M = N = K = 128
-__device__ __forceinline__ void issue_nt128(uint32_t tmem_d, uint32_t a_s, uint32_t b_s) {
-  constexpr uint32_t id = idesc_bf16(128, 128, 0);
-#pragma unroll
-  for (int ks = 0; ks < 8; ++ks) {
-    const uint32_t off = (ks >> 2) * (kTile128 / 2) + (ks & 3) * 32u;
-    mma_bf16_ss(tmem_d, sw128_desc(a_s + off, 16, 1024), sw128_desc(b_s + off, 16, 1024), id, ks > 0 ? 1u : 0u);
-  }
-}
-// D (+)= A B, A K-major [128 x 128 (K)], B MN-major [128 (K) rows x 128 (N)]
-__device__ __forceinline__ void issue_nn128(uint32_t tmem_d, uint32_t a_s, uint32_t b_s, bool accumulate) {
-  constexpr uint32_t id = idesc_bf16(128, 128, 1);
-#pragma unroll
-  for (int ks = 0; ks < 8; ++ks) {
-    const uint32_t aoff = (ks >> 2) * (kTile128 / 2) + (ks & 3) * 32u;
-    mma_bf16_ss(tmem_d, sw128_desc(a_s + aoff, 16, 1024), sw128_desc(b_s + ks * 2048u, kTile128 / 2, 1024), id,
-                (accumulate || ks > 0) ? 1u : 0u);
-  }
-}
 
-__device__ __forceinline__ void store_row128(uint32_t base, int r, const float* v) {
-  store_p_row(base, r, 0, v);
-  store_p_row(base, r, 4, v + 32);
-  store_p_row(base + kTile128 / 2, r, 0, v + 64);
-  store_p_row(base + kTile128 / 2, r, 4, v + 96);
-}
+
 
 __global__ void tc_delta_kernel(const TcBwdArgs a) {
   const int lane = threadIdx.x & 31;
@@ -1746,188 +1158,6 @@ __global__ void __launch_bounds__(256) bwd_pairs_fill_kernel(const TcArgs a, con
     }
     pos += __shfl_sync(0xffffffffu, incl, 31);
   }
-}
-
-// ---- remote pairs: one item = (batch, index head, block, query head) ------
-constexpr uint32_t kRBSmem = 2 * kKVBytes + 2 * kTile128 + 2 * kPBytes + 1024;
-
-__global__ void __launch_bounds__(kTcThreads) bwd_remote_kernel(const TcBwdArgs a) {
-  const TcArgs& f = a.f;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t bar;
-  __shared__ uint32_t tmem_base;
-  __shared__ int ok_s;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t k_s = sbase, v_s = k_s + kKVBytes;
-  const uint32_t q_s = v_s + kKVBytes, do_s = q_s + kTile128;
-  const uint32_t p_s = do_s + kTile128, ds_s = p_s + kPBytes;
-  if (warp == 0) {
-    tmem_alloc(&tmem_base, 256);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-    ok_s = 1;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_base;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t tm_s = tmem, tm_dp = tmem + 64, tm_dq = tmem, tm_dvt = tmem + 128, tm_dkt = tmem + 192;
-  const int64_t hpi = f.HQ / f.HI, G = f.HQ / f.Hkv;
-  const int64_t nitems = f.B * f.HI * f.nblk * hpi;
-  uint32_t phase = 0;
-  bool failed = false;
-  for (int64_t item = blockIdx.x; item < nitems && !failed; item += gridDim.x) {
-    const int64_t bhc = item / hpi;
-    const int64_t cnt = a.count[bhc];
-    if (cnt == 0) continue;
-    const int64_t first = a.offs[bhc];
-    const int64_t bh = bhc / f.nblk, blk = bhc % f.nblk, b = bh / f.HI, hi = bh % f.HI;
-    const int64_t h = hi * hpi + item % hpi, hk = h / G;
-    auto k_row = [&](int r) -> const __nv_bfloat16* {
-      const int64_t kk = blk * kBlk + r;
-      return kk < f.T ? f.k + b * f.skb + kk * f.skt + hk * f.skh : nullptr;
-    };
-    auto v_row = [&](int r) -> const __nv_bfloat16* {
-      const int64_t kk = blk * kBlk + r;
-      return kk < f.T ? f.v + b * f.svb + kk * f.svt + hk * f.svh : nullptr;
-    };
-    load_operand<kBlk>(k_s, kKVHalf, k_row, tid, f.k);
-    load_operand<kBlk>(v_s, kKVHalf, v_row, tid, f.v);
-    const int64_t ntile = (cnt + kTileM - 1) / kTileM;
-    for (int64_t tl = 0; tl < ntile; ++tl) {
-      const int64_t base = first + tl * kTileM, n_here = (cnt - tl * kTileM) < kTileM ? (cnt - tl * kTileM) : int64_t(kTileM);
-      int64_t t = -1, slot = 0;
-      if (tid < n_here) {
-        const int32_t pk = f.pairs[base + tid];
-        t = pk / f.S;
-        slot = pk % f.S;
-      }
-      auto q_row = [&](int r) -> const __nv_bfloat16* {
-        if (r >= n_here) return nullptr;
-        const int64_t tt = f.pairs[base + r] / f.S;
-        return f.q + b * f.sqb + tt * f.sqt + h * f.sqh;
-      };
-      auto g_row = [&](int r) -> const __nv_bfloat16* {
-        if (r >= n_here) return nullptr;
-        const int64_t tt = f.pairs[base + r] / f.S;
-        return a.dout + b * f.sob + tt * f.sot + h * f.soh;
-      };
-      load_operand<kTileM>(q_s, kTile128 / 2, q_row, tid, f.q);
-      load_operand<kTileM>(do_s, kTile128 / 2, g_row, tid, a.dout);
-      cp_async_commit();
-      cp_async_wait<0>();
-      fence_async_smem();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        issue_qk(tm_s, q_s, k_s);
-        issue_qk(tm_dp, do_s, v_s);
-        mma_commit(&bar);
-        ok_s = mbar_wait(&bar, phase, 301) ? 1 : 0;
-      }
-      phase ^= 1;
-      __syncthreads();
-      if (!ok_s) { failed = true; break; }
-      tc_fence_after();
-      float sv[64], dp[64];
-      {
-        float x0[32], x1[32];
-        tmem_ld32(tm_s + lane_off, x0);
-        tmem_ld32(tm_s + lane_off + 32, x1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
-        tmem_ld32(tm_dp + lane_off, x0);
-        tmem_ld32(tm_dp + lane_off + 32, x1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
-      }
-      float lse2 = 0.f, dlt = 0.f, bias2 = 0.f;
-      int64_t lo = 0, hi2 = 0;
-      if (t >= 0) {
-        lse2 = a.lse[(b * f.T + t) * f.HQ + h] * kLog2e;
-        dlt = a.delta[(b * f.T + t) * f.HQ + h];
-        if (f.bias) bias2 = f.bias[(b * f.T + t) * f.S + slot] * kLog2e;
-        remote_range(f, b, t, blk, lo, hi2);
-      }
-      float dsum = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int64_t key = blk * kBlk + i;
-        const bool valid = t >= 0 && key >= lo && key < hi2 && lse2 != -INFINITY;
-        const float p = valid ? exp2f(sv[i] * f.scale_log2 + bias2 - lse2) : 0.f;
-        const float ds = p * (dp[i] - dlt);
-        sv[i] = p;
-        dp[i] = ds;
-        dsum += ds;
-      }
-      if (t >= 0 && a.dbias_part) a.dbias_part[((b * f.T + t) * f.S + slot) * f.HQ + h] = dsum;
-      store_p_row(p_s, tid, 0, sv);
-      store_p_row(p_s, tid, 4, sv + 32);
-      store_p_row(ds_s, tid, 0, dp);
-      store_p_row(ds_s, tid, 4, dp + 32);
-      fence_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        issue_pv(tm_dq, ds_s, k_s, false);                 // dQ_g = dS K
-        issue_tn(tm_dvt, do_s, kTile128 / 2, p_s, tl > 0);  // dV^T += dO_g^T P
-        issue_tn(tm_dkt, q_s, kTile128 / 2, ds_s, tl > 0);  // dK^T += Q_g^T dS
-        mma_commit(&bar);
-        ok_s = mbar_wait(&bar, phase, 302) ? 1 : 0;
-      }
-      phase ^= 1;
-      __syncthreads();
-      if (!ok_s) { failed = true; break; }
-      tc_fence_after();
-      const int64_t prow = ((b * f.T + (t < 0 ? 0 : t)) * f.S + slot) * f.HQ + h;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float ov[32];
-        tmem_ld32(tm_dq + lane_off + 32 * c, ov);
-        tmem_wait_ld();
-        if (t >= 0) {
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            float tmp[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * a.scale;
-            store8(a.dq_part + prow * kD + 32 * c, 8 * q4, SRSWA_BF16, tmp);
-          }
-        }
-      }
-      tc_fence_before();
-      __syncthreads();
-    }
-    if (failed) break;
-    // this block's remote dK / dV for query head h: thread = feature d
-    tc_fence_after();
-    float* dst = a.dkv_part + ((b * f.HQ + h) * f.nblk + blk) * (2 * 64 * 128);
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      float kv[32], vv[32];
-      tmem_ld32(tm_dkt + lane_off + 32 * half, kv);
-      tmem_ld32(tm_dvt + lane_off + 32 * half, vv);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        dst[(32 * half + i) * 128 + tid] = kv[i] * a.scale;
-        dst[8192 + (32 * half + i) * 128 + tid] = vv[i];
-      }
-    }
-    tc_fence_before();
-    __syncthreads();
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 // ---- remote pairs, warp-specialised -------------------------------------
@@ -2297,337 +1527,6 @@ __global__ void __launch_bounds__(kRbThreads, 1)
   }
 }
 
-// ---- band dK / dV: one CTA per (batch, kv head, 128-key tile) -------------
-constexpr uint32_t kBDSmem = 6 * kTile128 + 1024;
-
-__global__ void __launch_bounds__(kTcThreads) bwd_band_dkdv_kernel(const TcBwdArgs a) {
-  const TcArgs& f = a.f;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t bar;
-  __shared__ uint32_t tmem_base;
-  __shared__ int ok_s;
-  __shared__ float lse2_s[128], dl_s[128];
-  __shared__ int64_t ls_s[128];
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t tile = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
-  const int64_t k0 = tile * 128, G = f.HQ / f.Hkv;
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t kt_s = sbase, vt_s = kt_s + kTile128, qt_s = vt_s + kTile128, dot_s = qt_s + kTile128;
-  const uint32_t pt_s = dot_s + kTile128, dst_s = pt_s + kTile128;
-  if (warp == 0) {
-    tmem_alloc(&tmem_base, 512);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-    ok_s = 1;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_base;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t tm_st = tmem, tm_dpt = tmem + 128, tm_dk = tmem + 256, tm_dv = tmem + 384;
-  auto kt_row = [&](int r) -> const __nv_bfloat16* {
-    const int64_t kk = k0 + r;
-    return kk < f.T ? f.k + b * f.skb + kk * f.skt + hk * f.skh : nullptr;
-  };
-  auto vt_row = [&](int r) -> const __nv_bfloat16* {
-    const int64_t kk = k0 + r;
-    return kk < f.T ? f.v + b * f.svb + kk * f.svt + hk * f.svh : nullptr;
-  };
-  load_operand<kTileM>(kt_s, kTile128 / 2, kt_row, tid, f.k);
-  load_operand<kTileM>(vt_s, kTile128 / 2, vt_row, tid, f.v);
-  const int64_t key = k0 + tid;
-  const int64_t q_hi = min(f.T, k0 + 127 + f.LW);  // exclusive end of queries seeing this tile locally
-  const int64_t nqt = (q_hi - k0 + 127) / 128;
-  uint32_t phase = 0;
-  bool failed = false, any = false;
-  for (int64_t gq = 0; gq < G && !failed; ++gq) {
-    const int64_t h = hk * G + gq;
-    for (int64_t qt = 0; qt < nqt; ++qt) {
-      const int64_t q0 = k0 + qt * 128;
-      auto q_row = [&](int r) -> const __nv_bfloat16* {
-        const int64_t tt = q0 + r;
-        return tt < f.T ? f.q + b * f.sqb + tt * f.sqt + h * f.sqh : nullptr;
-      };
-      auto g_row = [&](int r) -> const __nv_bfloat16* {
-        const int64_t tt = q0 + r;
-        return tt < f.T ? a.dout + b * f.sob + tt * f.sot + h * f.soh : nullptr;
-      };
-      load_operand<kTileM>(qt_s, kTile128 / 2, q_row, tid, f.q);
-      load_operand<kTileM>(dot_s, kTile128 / 2, g_row, tid, a.dout);
-      cp_async_commit();
-      {
-        const int64_t tq = q0 + tid;
-        const bool ok = tq < f.T;
-        lse2_s[tid] = ok ? a.lse[(b * f.T + tq) * f.HQ + h] * kLog2e : INFINITY;
-        dl_s[tid] = ok ? a.delta[(b * f.T + tq) * f.HQ + h] : 0.f;
-        ls_s[tid] = ok ? win_start(f, b, tq) : (int64_t(1) << 62);
-      }
-      cp_async_wait<0>();
-      fence_async_smem();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        issue_nt128(tm_st, kt_s, qt_s);   // S^T = K Q^T
-        issue_nt128(tm_dpt, vt_s, dot_s); // dP^T = V dO^T
-        mma_commit(&bar);
-        ok_s = mbar_wait(&bar, phase, 311) ? 1 : 0;
-      }
-      phase ^= 1;
-      __syncthreads();
-      if (!ok_s) { failed = true; break; }
-      tc_fence_after();
-      // row = key; columns = the tile's 128 queries, 32 at a time
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float sv[32], dp[32];
-        tmem_ld32(tm_st + lane_off + 32 * c, sv);
-        tmem_ld32(tm_dpt + lane_off + 32 * c, dp);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qi = 32 * c + i;
-          const int64_t tq = q0 + qi;
-          const bool local = key < f.T && key <= tq && key >= ls_s[qi];
-          const float p = local ? exp2f(sv[i] * f.scale_log2 - lse2_s[qi]) : 0.f;
-          sv[i] = p;
-          dp[i] = p * (dp[i] - dl_s[qi]);
-        }
-        const uint32_t half = (c >> 1) * (kTile128 / 2);
-        store_p_row(pt_s + half, tid, (c & 1) * 4, sv);
-        store_p_row(dst_s + half, tid, (c & 1) * 4, dp);
-      }
-      fence_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        issue_nn128(tm_dv, pt_s, dot_s, any);   // dV += P^T dO
-        issue_nn128(tm_dk, dst_s, qt_s, any);   // dK += dS^T Q
-        mma_commit(&bar);
-        ok_s = mbar_wait(&bar, phase, 312) ? 1 : 0;
-      }
-      phase ^= 1;
-      any = true;
-      __syncthreads();
-      if (!ok_s) { failed = true; break; }
-    }
-  }
-  if (!failed) {
-    tc_fence_after();
-    const int64_t blk = key / kBlk, hi = (hk * f.HI) / f.Hkv;
-    const int64_t bhc = (b * f.HI + hi) * f.nblk + blk;
-    const bool has_remote = key < f.T && a.count && a.count[bhc] > 0;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float kv[32], vv[32];
-      if (any) {
-        tmem_ld32(tm_dk + lane_off + 32 * c, kv);
-        tmem_ld32(tm_dv + lane_off + 32 * c, vv);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) kv[i] = vv[i] = 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) kv[i] *= a.scale;
-      if (has_remote) {
-        for (int64_t gq = 0; gq < G; ++gq) {
-          const float* src = a.dkv_part + ((b * f.HQ + hk * G + gq) * f.nblk + blk) * (2 * 64 * 128) +
-                             (key % kBlk) * 128 + 32 * c;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            kv[i] += src[i];
-            vv[i] += src[8192 + i];
-          }
-        }
-      }
-      if (key < f.T) {
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          store8(a.dk + b * f.skb + key * f.skt + hk * f.skh + 32 * c, 8 * q4, SRSWA_BF16, kv + 8 * q4);
-          store8(a.dv + b * f.svb + key * f.svt + hk * f.svh + 32 * c, 8 * q4, SRSWA_BF16, vv + 8 * q4);
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 512);
-}
-
-// ---- band dQ (+ remote dQ partials): one CTA per (batch, head, 128 queries)
-constexpr uint32_t kBQSmem = 2 * kTile128 + 2 * 2 * kKVBytes + 1024;
-
-__global__ void __launch_bounds__(kTcThreads) bwd_band_dq_kernel(const TcBwdArgs a) {
-  const TcArgs& f = a.f;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t bar_s, bar_o;
-  __shared__ uint32_t tmem_base;
-  __shared__ int ok_s;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int64_t hk = h / (f.HQ / f.Hkv);
-  const int64_t t0 = tile * kTileM;
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t q_s = sbase, do_s = q_s + kTile128, kv_s = do_s + kTile128;
-  if (warp == 0) {
-    tmem_alloc(&tmem_base, 256);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    mbar_init(&bar_s, 1);
-    mbar_init(&bar_o, 1);
-    fence_mbar_init();
-    ok_s = 1;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_base;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t tm_s = tmem, tm_dp = tmem + 64, tm_dq = tmem + 128;
-  const int64_t t = t0 + tid;
-  const bool row_ok = t < f.T;
-  const int64_t ls = row_ok ? win_start(f, b, t) : 0;
-  const float lse2 = row_ok ? a.lse[(b * f.T + t) * f.HQ + h] * kLog2e : INFINITY;
-  const float dlt = row_ok ? a.delta[(b * f.T + t) * f.HQ + h] : 0.f;
-  const int64_t tlast = min(f.T, t0 + kTileM) - 1;
-  int64_t key_lo = t0 - f.LW + 1;
-  if (key_lo < 0) key_lo = 0;
-  const int64_t blo = key_lo / kBlk, bhi = tlast / kBlk;
-  auto q_row = [&](int r) -> const __nv_bfloat16* {
-    const int64_t tt = t0 + r;
-    return tt < f.T ? f.q + b * f.sqb + tt * f.sqt + h * f.sqh : nullptr;
-  };
-  auto g_row = [&](int r) -> const __nv_bfloat16* {
-    const int64_t tt = t0 + r;
-    return tt < f.T ? a.dout + b * f.sob + tt * f.sot + h * f.soh : nullptr;
-  };
-  auto kv_rows = [&](int64_t blk, const __nv_bfloat16* base, int64_t sb, int64_t st, int64_t sh) {
-    return [=](int r) -> const __nv_bfloat16* {
-      const int64_t kk = blk * kBlk + r;
-      return kk < f.T ? base + b * sb + kk * st + hk * sh : nullptr;
-    };
-  };
-  load_operand<kTileM>(q_s, kTile128 / 2, q_row, tid, f.q);
-  load_operand<kTileM>(do_s, kTile128 / 2, g_row, tid, a.dout);
-  load_operand<kBlk>(kv_s, kKVHalf, kv_rows(blo, f.k, f.skb, f.skt, f.skh), tid, f.k);
-  load_operand<kBlk>(kv_s + kKVBytes, kKVHalf, kv_rows(blo, f.v, f.svb, f.svt, f.svh), tid, f.v);
-  cp_async_commit();
-  bool aborted = false;
-  for (int64_t j = blo; j <= bhi; ++j) {
-    const int jj = static_cast<int>(j - blo);
-    const int st = jj & 1;
-    cp_async_wait<0>();
-    fence_async_smem();
-    __syncthreads();
-    const uint32_t k_cur = kv_s + st * 2 * kKVBytes, v_cur = k_cur + kKVBytes;
-    if (tid == 0) {
-      tc_fence_after();
-      issue_qk(tm_s, q_s, k_cur);
-      issue_qk(tm_dp, do_s, v_cur);
-      mma_commit(&bar_s);
-      ok_s = mbar_wait(&bar_s, jj & 1, 321) ? 1 : 0;
-    }
-    __syncthreads();
-    if (!ok_s) { aborted = true; break; }
-    if (j + 1 <= bhi) {
-      const uint32_t nx = kv_s + (st ^ 1) * 2 * kKVBytes;
-      load_operand<kBlk>(nx, kKVHalf, kv_rows(j + 1, f.k, f.skb, f.skt, f.skh), tid, f.k);
-      load_operand<kBlk>(nx + kKVBytes, kKVHalf, kv_rows(j + 1, f.v, f.svb, f.svt, f.svh), tid, f.v);
-    }
-    cp_async_commit();
-    tc_fence_after();
-    float sv[64], dp[64];
-    {
-      float x0[32], x1[32];
-      tmem_ld32(tm_s + lane_off, x0);
-      tmem_ld32(tm_s + lane_off + 32, x1);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
-      tmem_ld32(tm_dp + lane_off, x0);
-      tmem_ld32(tm_dp + lane_off + 32, x1);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
-    }
-    const int64_t k0 = j * kBlk;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const int64_t kk = k0 + i;
-      const bool valid = row_ok && kk >= ls && kk <= t;
-      const float p = valid ? exp2f(sv[i] * f.scale_log2 - lse2) : 0.f;
-      dp[i] = p * (dp[i] - dlt);
-    }
-    store_p_row(v_cur, tid, 0, dp);  // dS over the dead V operand of this stage
-    store_p_row(v_cur, tid, 4, dp + 32);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      issue_pv(tm_dq, v_cur, k_cur, jj > 0);  // dQ += dS K (K MN-major)
-      mma_commit(&bar_o);
-    }
-  }
-  const int nblocks = static_cast<int>(bhi - blo + 1);
-  if (tid == 0) ok_s = mbar_wait(&bar_o, (nblocks - 1) & 1, 322) ? 1 : 0;
-  __syncthreads();
-  cp_async_wait<0>();
-  if (!aborted && ok_s) {
-    tc_fence_after();
-    const int64_t hi = (hk * f.HI) / f.Hkv;
-    int64_t slot_rows[64];
-    int nsl = 0;
-    if (row_ok && f.S > 0) {
-      const int32_t* srow = f.sel + ((b * f.HI + hi) * f.T + t) * f.S;
-      for (int64_t s2 = 0; s2 < f.S && s2 < 64; ++s2) {
-        const int64_t blk = srow[s2];
-        if (blk < 0 || blk >= f.nblk) continue;
-        int64_t lo, hi2;
-        remote_range(f, b, t, blk, lo, hi2);
-        if (lo >= hi2) continue;
-        bool dup = false;
-        for (int64_t u = 0; u < s2; ++u) dup |= srow[u] == blk;
-        if (dup) continue;
-        slot_rows[nsl++] = ((b * f.T + t) * f.S + s2) * f.HQ + h;
-      }
-    }
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float ov[32];
-      tmem_ld32(tm_dq + lane_off + 32 * c, ov);
-      tmem_wait_ld();
-      if (row_ok) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ov[i] *= a.scale;
-        for (int u = 0; u < nsl; ++u) {
-          const uint4* src = reinterpret_cast<const uint4*>(a.dq_part + slot_rows[u] * kD + 32 * c);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const uint4 w = src[q4];
-            ov[8 * q4 + 0] += bf16_lo(w.x); ov[8 * q4 + 1] += bf16_hi(w.x);
-            ov[8 * q4 + 2] += bf16_lo(w.y); ov[8 * q4 + 3] += bf16_hi(w.y);
-            ov[8 * q4 + 4] += bf16_lo(w.z); ov[8 * q4 + 5] += bf16_hi(w.z);
-            ov[8 * q4 + 6] += bf16_lo(w.w); ov[8 * q4 + 7] += bf16_hi(w.w);
-          }
-        }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          store8(a.dq + b * f.sqb + t * f.sqt + h * f.sqh + 32 * c, 8 * q4, SRSWA_BF16, ov + 8 * q4);
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
-}
-
 // ---- band dQ, warp-specialised: one work item = (b, h, 128-query tile) -----
 //   warps 0-3  compute (thread = query row): P = 2^(s c - lse), dS = P (dP -
 //              delta) over the window keys, dS (bf16) over the stage's dead V;
@@ -2698,7 +1597,7 @@ __global__ void __launch_bounds__(kBqThreads, 1)
     c.n = 0;
     c.done = c.item >= nitems;
     if (!c.done) {
-      c.w = ws_item<false>(f, c.item);
+      c.w = ws_item(f, c.item);
       c.j = c.w.blo;
     }
   };
@@ -2712,7 +1611,7 @@ __global__ void __launch_bounds__(kBqThreads, 1)
     c.item += gridDim.x;
     c.done = c.item >= nitems;
     if (!c.done) {
-      c.w = ws_item<false>(f, c.item);
+      c.w = ws_item(f, c.item);
       c.j = c.w.blo;
     }
   };
@@ -3412,23 +2311,19 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(fwd_ws_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(band_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBandSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(remote_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRemoteSmem);
+    e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     attr_done = true;
   }
-  // warp-specialised TMA path when the driver encodes the tensor maps; the
-  // cp.async tensor-core kernels otherwise
+  // the tensor maps of q, k and v; when the driver refuses one, the caller
+  // runs the CUDA-core kernels instead (nothing has been launched yet)
   alignas(64) CUtensorMap tmq, tmk, tmv;
-  const bool use_ws =
-      make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
-      make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
-      make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk);
+  if (!(make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
+        make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
+        make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk)))
+    return kTcNoTensorMap;
   if (g->S > 0) {
     const int64_t nbh = a.B * a.HI * a.nblk;
     SRSWA_CUDA_TRY(cudaMemsetAsync(count, 0, static_cast<size_t>(nbh) * 4, st));
@@ -3441,31 +2336,20 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     pairs_fill_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, cursor,
                                                                                const_cast<int32_t*>(a.pairs));
     SRSWA_CUDA_TRY(cudaGetLastError());
-    if (use_ws) {
-      // slots without a partial read as NaN in the merge
-      SRSWA_CUDA_TRY(cudaMemsetAsync(a.part_lse, 0xff, static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4, st));
-      remote_ws_kernel<<<num_sms, kRwThreads, kWsSmem, st>>>(a, tmk, tmv);
-    }
-    else {
-      remote_fwd_kernel<<<148 * 3, kTcThreads, kRemoteSmem, st>>>(a);
-    }
+    // slots without a partial read as NaN in the merge
+    SRSWA_CUDA_TRY(cudaMemsetAsync(a.part_lse, 0xff, static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4, st));
+    remote_ws_kernel<<<num_sms, kRwThreads, kWsSmem, st>>>(a, tmk, tmv);
     SRSWA_CUDA_TRY(cudaGetLastError());
   } else {
     a.part_o = nullptr;
   }
-  if (use_ws) {
-    const int64_t band_items = g->B * g->HQ * ((g->T + kTileM - 1) / kTileM);
-    const unsigned band_grid = static_cast<unsigned>(band_items < num_sms ? band_items : num_sms);
-    fwd_ws_kernel<false><<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv);
-    if (a.part_o) {
-      SRSWA_CUDA_TRY(cudaGetLastError());
-      const int64_t rows = g->B * g->T * g->HQ;
-      merge_partials_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
-    }
-  } else {
-    dim3 grid(static_cast<unsigned>((g->T + kTileM - 1) / kTileM), static_cast<unsigned>(g->HQ),
-              static_cast<unsigned>(g->B));
-    band_fwd_kernel<<<grid, kTcThreads, kBandSmem, st>>>(a);
+  const int64_t band_items = g->B * g->HQ * ((g->T + kTileM - 1) / kTileM);
+  const unsigned band_grid = static_cast<unsigned>(band_items < num_sms ? band_items : num_sms);
+  fwd_ws_kernel<<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv);
+  if (a.part_o) {
+    SRSWA_CUDA_TRY(cudaGetLastError());
+    const int64_t rows = g->B * g->T * g->HQ;
+    merge_partials_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
   }
   return srswa_last_launch_status();
 }
@@ -3552,9 +2436,7 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   static int num_sms = 148;
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(bwd_remote_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRBSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(bwd_remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRbSmem);
+    cudaError_t e = cudaFuncSetAttribute(bwd_remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRbSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     e = cudaFuncSetAttribute(bwd_band_dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBqSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -3562,20 +2444,18 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     if (e != cudaSuccess) return static_cast<int>(e);
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-    e = cudaFuncSetAttribute(bwd_band_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBDSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(bwd_band_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBQSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
     attr_done = true;
   }
-  // TMA for the remote pass's K / V when the driver encodes the tensor maps
+  // tensor maps of k, v, q and dO; when the driver refuses one, the caller
+  // runs the CUDA-core kernels instead (nothing has been launched yet)
   alignas(64) CUtensorMap tmk, tmv, tmq, tmdo, tmq64, tmdo64;
-  const bool use_tma = make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
-                       make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk) &&
-                       make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
-                       make_tmap(&tmdo, dout, g->B, g->T, g->HQ, sob, sot, soh, kTileM) &&
-                       make_tmap(&tmq64, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, 64) &&
-                       make_tmap(&tmdo64, dout, g->B, g->T, g->HQ, sob, sot, soh, 64);
+  if (!(make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
+        make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk) &&
+        make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
+        make_tmap(&tmdo, dout, g->B, g->T, g->HQ, sob, sot, soh, kTileM) &&
+        make_tmap(&tmq64, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, 64) &&
+        make_tmap(&tmdo64, dout, g->B, g->T, g->HQ, sob, sot, soh, 64)))
+    return kTcNoTensorMap;
   const int64_t nrows_h = g->B * g->T * g->HQ;
   tc_delta_kernel<<<static_cast<unsigned>((nrows_h + 7) / 8), 256, 0, st>>>(a);
   SRSWA_CUDA_TRY(cudaGetLastError());
@@ -3596,12 +2476,11 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     SRSWA_CUDA_TRY(cudaGetLastError());
     if (a.dbias_part)
       SRSWA_CUDA_TRY(cudaMemsetAsync(a.dbias_part, 0, static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4, st));
-    if (use_tma) bwd_remote_ws_kernel<<<num_sms, kRbThreads, kRbSmem, st>>>(a, tmk, tmv);
-    else bwd_remote_kernel<<<148, kTcThreads, kRBSmem, st>>>(a);
+    bwd_remote_ws_kernel<<<num_sms, kRbThreads, kRbSmem, st>>>(a, tmk, tmv);
     SRSWA_CUDA_TRY(cudaGetLastError());
   }
   const unsigned ntile = static_cast<unsigned>((g->T + kTileM - 1) / kTileM);
-  if (use_tma) {
+  {
     const int64_t items = g->B * g->Hkv * static_cast<int64_t>(ntile);
     const unsigned grid_k = static_cast<unsigned>(items < num_sms ? items : num_sms);
     bwd_band_dkdv_ws_kernel<<<grid_k, kBkThreads, kBkSmem, st>>>(a, tmq64, tmdo64, tmk, tmv);
@@ -3611,12 +2490,8 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
       dkv_merge_kernel<<<static_cast<unsigned>((n16 + 255) / 256), 256, 0, st>>>(a);
       SRSWA_CUDA_TRY(cudaGetLastError());
     }
-  } else {
-    bwd_band_dkdv_kernel<<<dim3(ntile, static_cast<unsigned>(g->Hkv), static_cast<unsigned>(g->B)), kTcThreads,
-                           kBDSmem, st>>>(a);
-    SRSWA_CUDA_TRY(cudaGetLastError());
   }
-  if (use_tma) {
+  {
     const int64_t items = g->B * g->HQ * static_cast<int64_t>(ntile);
     const unsigned grid_q = static_cast<unsigned>(items < num_sms ? items : num_sms);
     bwd_band_dq_ws_kernel<<<grid_q, kBqThreads, kBqSmem, st>>>(a, tmq, tmdo, tmk, tmv);
@@ -3626,10 +2501,6 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
       dq_merge_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
       SRSWA_CUDA_TRY(cudaGetLastError());
     }
-  } else {
-    bwd_band_dq_kernel<<<dim3(ntile, static_cast<unsigned>(g->HQ), static_cast<unsigned>(g->B)), kTcThreads,
-                         kBQSmem, st>>>(a);
-    SRSWA_CUDA_TRY(cudaGetLastError());
   }
   if (bias) {
     if (remote) {
