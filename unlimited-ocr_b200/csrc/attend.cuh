@@ -23,8 +23,8 @@ constexpr int kAttendMaxSlots = 64;  // remote slots + window blocks per row
 constexpr int kTcNoTensorMap = -1000;
 
 struct TcLayout {
-  size_t part_o, part_lse, count, offs, cursor, tiles, ntiles, pairs, lse, pair_q, pair_bias, total;
-  int64_t max_tiles;
+  size_t part_o, part_lse, count, cursor, work, totals, pair_t, pair_q, pair_bias, prow, lse, total;
+  int64_t max_tiles;  // tiles of partial rows (128 each) per query head of an index head
 };
 
 struct AttendArgs {

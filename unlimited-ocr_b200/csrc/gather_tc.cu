@@ -63,15 +63,23 @@ struct TcArgs {
   const int32_t* sel;         // [B, HI, T, S] packed
   const float* bias;          // [B, T, S] or null
   const int32_t* seg;         // [B, T] or null
-  __nv_bfloat16* part_o;      // [B, T, S, HQ, D]
-  float* part_lse;            // [B, T, S, HQ] log2 domain
+  // forward remote pass: every (b*HI + hi, block) list owns whole 128-row
+  // tiles of partial rows; a selection's partial row is prow[b, hi, t, s]
+  __nv_bfloat16* part_o;      // [HQ/HI, prow_cap, D] bf16, normalised
+  float* part_lse;            // [HQ/HI, prow_cap] log2 domain
+  int32_t* prow;              // [B, HI, T, S] partial row, -1 if none
+  int32_t* pair_t;            // per partial row: query t
+  int64_t* pair_q;            // per partial row: b * sqb + t * sqt (the query head's offset is added per unit)
+  float* pair_bias;           // per partial row: slot bias * log2 e (0 without bias)
+  const int4* work;           // nonempty lists: (b*HI + hi) * nblk + block, first tile, pair count, 0
+  const int32_t* totals;      // {tiles, nonempty lists}
+  int64_t prow_cap;           // partial rows per query head of an index head
+  // backward lists
   const int32_t* pairs;       // packed t * S + s, grouped by (b, hi, block)
   const int4* tiles;          // (b*HI + hi, block, first pair, count)
   const int32_t* ntiles;      // device count of tiles
   const int32_t* count;       // pairs per (b*HI + hi, block)
   const int32_t* offs;        // first pair of each (b*HI + hi, block)
-  int64_t* pair_q;            // per pair: b * sqb + t * sqt (the query head's offset is added per item)
-  float* pair_bias;           // per pair: slot bias * log2 e (0 without bias)
   int64_t B, T, HQ, Hkv, HI, S, LW, nblk;
   float scale_log2;
 };
@@ -196,41 +204,86 @@ __global__ void pairs_scan_kernel(const TcArgs a, const int32_t* count, int32_t*
   if (threadIdx.x == 0) *ntiles = base_t;
 }
 
-__global__ void pairs_fill_kernel(const TcArgs a, int32_t* cursor, int32_t* pairs) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+// Forward lists: single-CTA scans over the (b*HI + hi, block) lists.  Every
+// list gets whole 128-row tiles of partial rows: its first tile (exclusive
+// scan of ceil(count / 128)) sets its fill cursor to tile * 128, and the
+// nonempty lists are compacted into work[] = (list, first tile, count, 0).
+// totals = {tiles, nonempty lists}.
+__global__ void fwd_lists_scan_kernel(const TcArgs a, const int32_t* count, int32_t* cursor, int4* work,
+                                      int32_t* totals) {
+  __shared__ int32_t sh_t[1024], sh_w[1024];
+  const int64_t n = a.B * a.HI * a.nblk;
+  int32_t base_t = 0, base_w = 0;
+  for (int64_t c0 = 0; c0 < n; c0 += 1024) {
+    const int64_t i = c0 + threadIdx.x;
+    const int32_t cnt = i < n ? count[i] : 0;
+    const int32_t nt = (cnt + kTileM - 1) / kTileM;
+    sh_t[threadIdx.x] = nt;
+    sh_w[threadIdx.x] = cnt > 0 ? 1 : 0;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {  // inclusive Hillis-Steele scans
+      const int32_t vt = threadIdx.x >= static_cast<unsigned>(o) ? sh_t[threadIdx.x - o] : 0;
+      const int32_t vw = threadIdx.x >= static_cast<unsigned>(o) ? sh_w[threadIdx.x - o] : 0;
+      __syncthreads();
+      sh_t[threadIdx.x] += vt;
+      sh_w[threadIdx.x] += vw;
+      __syncthreads();
+    }
+    if (i < n) {
+      const int32_t ot = base_t + sh_t[threadIdx.x] - nt;
+      cursor[i] = ot * kTileM;
+      if (cnt > 0) work[base_w + sh_w[threadIdx.x] - 1] = make_int4(static_cast<int>(i), ot, cnt, 0);
+    }
+    __syncthreads();
+    base_t += sh_t[1023];
+    base_w += sh_w[1023];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    totals[0] = base_t;
+    totals[1] = base_w;
+  }
+}
+
+// Forward lists: each usable (t, slot) selection takes the next partial row
+// of its list and records the row's query, q offset and bias; prow maps
+// every selection to its row (-1: unused, repeated or without remote keys).
+__global__ void pairs_fill_kernel(const TcArgs a, int32_t* cursor) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, hi, t)
   if (i >= a.B * a.HI * a.T) return;
   const int64_t t = i % a.T, bh = i / a.T, b = bh / a.HI;
   const int32_t* srow = a.sel + i * a.S;
+  int32_t* prow = a.prow + i * a.S;
   for (int64_t s = 0; s < a.S; ++s) {
+    int32_t row = -1;
     const int64_t blk = srow[s];
-    if (blk < 0 || blk >= a.nblk) continue;
-    int64_t lo, hi;
-    remote_range(a, b, t, blk, lo, hi);
-    if (lo >= hi) continue;
-    bool dup = false;
-    for (int64_t u = 0; u < s; ++u) dup |= srow[u] == blk;
-    if (dup) continue;
-    const int32_t pos = atomicAdd(cursor + bh * a.nblk + blk, 1);
-    pairs[pos] = static_cast<int32_t>(t * a.S + s);
-    if (a.pair_q) {
-      a.pair_q[pos] = b * a.sqb + t * a.sqt;
-      a.pair_bias[pos] = a.bias ? a.bias[(b * a.T + t) * a.S + s] * kLog2e : 0.f;
+    if (blk >= 0 && blk < a.nblk) {
+      int64_t lo, hi;
+      remote_range(a, b, t, blk, lo, hi);
+      bool dup = false;
+      for (int64_t u = 0; u < s; ++u) dup |= srow[u] == blk;
+      if (lo < hi && !dup) {
+        row = atomicAdd(cursor + bh * a.nblk + blk, 1);
+        a.pair_t[row] = static_cast<int32_t>(t);
+        a.pair_q[row] = b * a.sqb + t * a.sqt;
+        a.pair_bias[row] = a.bias ? a.bias[(b * a.T + t) * a.S + s] * kLog2e : 0.f;
+      }
     }
+    prow[s] = row;
   }
 }
 
 // ============================================================================
-// Warp-specialised forward: both passes on one engine.
+// Warp-specialised band forward (the local window of every query).
 //
-// A CTA is persistent over work items (band: (b, h, 128-query tile); remote:
-// (pair tile, query head)) and runs two items at a time, one per slot.
+// A CTA is persistent over work items (b, h, 128-query tile) and runs two
+// items at a time, one per slot.
 //   warps 0-3 / 4-7  softmax warpgroup of slot 0 / 1 (thread = query row): S
-//                    from TMEM, mask, online softmax with lazy O rescale, P
-//                    (bf16) over the dead K operand, and the item's epilogue
-//                    from O in TMEM;
-//   warp 8           producer: cp.async of the slot's Q tile and of each key
-//                    block's K and V into the slot's 2-stage ring; completion
-//                    arrives on mbarriers (cp.async.mbarrier.arrive.noinc);
+//                    from TMEM, causal / window mask, online softmax with lazy
+//                    O rescale, P (bf16) over the dead K operand, and the
+//                    item's epilogue (o, lse) from O in TMEM;
+//   warp 8           producer: TMA loads of the slot's Q tile and of each key
+//                    block's K and V into the slot's 2-stage ring;
 //   warp 9           MMA issuer (one thread) and TMEM owner: S = Q K^T and
 //                    O += P V of the two slots in ping-pong order, so one
 //                    slot's MMAs run while the other slot's softmax does.
@@ -244,23 +297,26 @@ constexpr uint32_t kWsStage = 2 * kKVBytes;                              // K th
 constexpr uint32_t kWsSmem = 2 * kQBytes + 2 * 2 * kWsStage + 1024;      // 193 KB -> 1 CTA/SM
 constexpr uint32_t kWsTmemCols = 512;                                   // per slot: S 0-63, O 128-255
 
-__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
-  const uint32_t a = smem_u32(bar);
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((i & 31) == 31 && *abort_flag) return false;
+// Bounded wait of one role: suspended try_waits until the phase completes,
+// the CTA's abort flag is set (another role gave up) or the wall-clock bound
+// expires (error recorded, abort flag set).  The first test is inline; the
+// rest is one shared out-of-line function, which keeps the roles' loops small
+// in the instruction cache.
+__device__ __noinline__ bool ws_wait_slow(uint32_t a, uint32_t parity, volatile int* abort_flag, int code) {
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait(a, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) break;
   }
   atomicExch(&g_tc_error, code);
   *abort_flag = 1;
   return false;
+}
+__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  return ws_wait_slow(a, parity, abort_flag, code);
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -398,68 +454,77 @@ __device__ __forceinline__ void band_row_store(const TcArgs& a, int64_t b, int64
 
 // Row-wise log-sum-exp merge of the window result (o, lse, as written by the
 // band pass) with the row's remote partials; one warp per (b, t, h), lane =
-// 4 features.  part_lse is pre-filled with NaN, so a slot that produced no
-// partial (unused, repeated or empty) reads as NaN and needs no look at the
-// selection: every load of the row (window o and lse, the S slot lse values
-// and partial rows) is issued at once.  Partial rows of unused slots are
-// dropped by a select (their bytes are never multiplied in).  Rows without a
-// usable slot keep the window result.  Memory-bound.
+// 4 features.  Lane s (and s + 32) reads slot s's partial row from prow (-1:
+// no partial, i.e. unused, repeated or without remote keys) and that row's
+// lse; the first eight partial rows are requested together with the lse
+// values.  Rows without a partial keep the window result.  Memory-bound.
 __global__ void __launch_bounds__(256) merge_partials_kernel(const TcArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= a.B * a.T * a.HQ) return;
   const int64_t h = row % a.HQ, bt = row / a.HQ;
   const int64_t t = bt % a.T, b = bt / a.T;
-  const int64_t slot_base = (bt * a.S) * a.HQ + h;
+  const int64_t hpi = a.HQ / a.HI, hi = h / hpi, hl = h - hi * hpi;
+  const int32_t* pr = a.prow + ((b * a.HI + hi) * a.T + t) * a.S;
   const int ns = static_cast<int>(a.S < 64 ? a.S : 64);
+  const int32_t r0 = lane < ns ? __ldg(pr + lane) : -1;
+  const int32_t r1 = lane + 32 < ns ? __ldg(pr + lane + 32) : -1;
+  const float* plse = a.part_lse + hl * a.prow_cap;
+  const __nv_bfloat16* po = a.part_o + hl * a.prow_cap * kD + lane * 4;
   float* lse_p = a.lse + bt * a.HQ + h;
   __nv_bfloat16* op = a.o + b * a.sob + t * a.sot + h * a.soh + lane * 4;
-  // lane s (and s + 32) owns slot s's lse
-  const float ls0 = lane < ns ? __ldcs(a.part_lse + slot_base + lane * a.HQ) : __int_as_float(0x7fffffff);
-  const float ls1 = lane + 32 < ns ? __ldcs(a.part_lse + slot_base + (lane + 32) * a.HQ) : __int_as_float(0x7fffffff);
+  const float v0 = r0 >= 0 ? __ldcs(plse + r0) : -INFINITY;
+  const float v1 = r1 >= 0 ? __ldcs(plse + r1) : -INFINITY;
+  uint2 u[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {  // first group of partial rows, in flight with the lse loads
+    const int32_t rk = __shfl_sync(0xffffffffu, r0, k);
+    u[k] = (k < ns && rk >= 0) ? __ldcs(reinterpret_cast<const uint2*>(po + static_cast<int64_t>(rk) * kD))
+                               : make_uint2(0u, 0u);
+  }
   const float lb = *lse_p * kLog2e;
   const uint2 ob = *reinterpret_cast<const uint2*>(op);
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  float M = -INFINITY;
-  const float v0 = (ls0 == ls0) ? ls0 : -INFINITY, v1 = (ls1 == ls1) ? ls1 : -INFINITY;  // NaN -> no partial
-  M = warp_max(fmaxf(v0, v1));
-  if (M == -INFINITY) return;  // no remote slot: the window result stands (warp-uniform)
+  float M = warp_max(fmaxf(v0, v1));
+  if (M == -INFINITY) return;  // no remote partial: the window result stands (warp-uniform)
   M = fmaxf(M, lb);
   float den = (v0 == -INFINITY ? 0.f : exp2f(v0 - M)) + (v1 == -INFINITY ? 0.f : exp2f(v1 - M));
   den = warp_sum(den);
   const float wb = lb == -INFINITY ? 0.f : exp2f(lb - M);
   den += wb;
+  float acc[4];
   acc[0] = wb * bf16_lo(ob.x);
   acc[1] = wb * bf16_hi(ob.x);
   acc[2] = wb * bf16_lo(ob.y);
   acc[3] = wb * bf16_hi(ob.y);
   for (int g0 = 0; g0 < ns; g0 += 8) {
-    uint2 u[8];
-    float w[8];
+    if (g0 > 0) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int s2 = g0 + k;
+        const int32_t rk = __shfl_sync(0xffffffffu, s2 < 32 ? r0 : r1, s2 & 31);
+        u[k] = (s2 < ns && rk >= 0) ? __ldcs(reinterpret_cast<const uint2*>(po + static_cast<int64_t>(rk) * kD))
+                                    : make_uint2(0u, 0u);
+      }
+    }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int s2 = g0 + k;
       const float l2 = __shfl_sync(0xffffffffu, s2 < 32 ? v0 : v1, s2 & 31);
-      w[k] = (s2 < ns && l2 != -INFINITY) ? exp2f(l2 - M) : 0.f;
-      u[k] = s2 < ns ? __ldcs(reinterpret_cast<const uint2*>(a.part_o + (slot_base + s2 * a.HQ) * kD + lane * 4))
-                     : make_uint2(0u, 0u);
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (w[k] != 0.f) {
-        acc[0] = fmaf(w[k], bf16_lo(u[k].x), acc[0]);
-        acc[1] = fmaf(w[k], bf16_hi(u[k].x), acc[1]);
-        acc[2] = fmaf(w[k], bf16_lo(u[k].y), acc[2]);
-        acc[3] = fmaf(w[k], bf16_hi(u[k].y), acc[3]);
+      const float w = (s2 < ns && l2 != -INFINITY) ? exp2f(l2 - M) : 0.f;
+      if (w != 0.f) {
+        acc[0] = fmaf(w, bf16_lo(u[k].x), acc[0]);
+        acc[1] = fmaf(w, bf16_hi(u[k].x), acc[1]);
+        acc[2] = fmaf(w, bf16_lo(u[k].y), acc[2]);
+        acc[3] = fmaf(w, bf16_hi(u[k].y), acc[3]);
       }
     }
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
-  __nv_bfloat162 r0 = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
-  __nv_bfloat162 r1 = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
+  __nv_bfloat162 q0 = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
+  __nv_bfloat162 q1 = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
   uint2 w2;
-  w2.x = *reinterpret_cast<uint32_t*>(&r0);
-  w2.y = *reinterpret_cast<uint32_t*>(&r1);
+  w2.x = *reinterpret_cast<uint32_t*>(&q0);
+  w2.y = *reinterpret_cast<uint32_t*>(&q1);
   *reinterpret_cast<uint2*>(op) = w2;
   if (lane == 0) *lse_p = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
 }
@@ -686,252 +751,348 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 }
 
 // ============================================================================
-// Warp-specialised remote pass.  A work item is one selected block of one
-// query head with all of its (query, slot) pairs: K and V are loaded once
-// (TMA) and the pairs go through in tiles of 128 rows whose q rows are
-// gathered with cp.async into a double-buffered Q tile per slot; P overwrites
-// the dead Q tile.  The producer resolves each tile's rows (query, slot,
-// bias) into shared memory for the softmax warps.  Roles and bounded waits as
-// in fwd_ws_kernel; each tile writes its normalised partial (o bf16, lse
-// log2) at the end of its step.
+// Warp-specialised remote pass.  A unit is one 128-row tile of one
+// (b*HI + hi, block) pair list for one query head of the index head.  The
+// global unit sequence is ordered by list, head and tile, and each CTA takes
+// one contiguous, equal share of it: every CTA gets the same number of tiles,
+// and consecutive units mostly share their block, whose K and V are loaded
+// once per run (a run = the units of one list and head; two TMA stages).
+// Roles (thread = row inside the warpgroups):
+//   warps 0-3 / 4-7  row warpgroup 0 / 1, the CTA's even / odd units: S from
+//                    TMEM, masked to the row's remote keys, exp2 with the slot
+//                    bias, P (bf16) over the unit's dead Q tile; then O from
+//                    TMEM scaled by 1/l, bf16, staged over the same tile in the
+//                    128-byte-swizzled layout and sent to the unit's partial
+//                    rows by two TMA stores (one thread); lse (log2) per row.
+//                    Both warpgroups run the same code (one instruction
+//                    stream in the caches) and each has its own S and O
+//                    buffers in TMEM;
+//   warps 8-11       producers, 32 rows each: the rows' query and bias into
+//                    shared memory, the q rows gathered (cp.async) into a
+//                    4-deep Q ring; warp 8 also loads K and V (TMA) at each
+//                    run start;
+//   warp 12          MMA issuer (one thread) and TMEM owner: S = Q K^T and
+//                    O = P V, issuing whichever is ready first (S of unit n+1
+//                    may go before O of unit n).
+// Every wait is bounded and gives up once another role set the abort flag.
 // ============================================================================
-struct RwCursor {
-  int64_t item, nitems, m, j, n, ntile, pbase, cnt, b, h, hk, blk;
-  bool done;
-  __device__ __forceinline__ void seek(const TcArgs& a) {  // first item with pairs at or after `item`
-    const int64_t hpi = a.HQ / a.HI;
-    while (item < nitems) {
-      const int64_t bhc = item / hpi;
-      const int32_t c = a.count[bhc];
-      if (c > 0) {
-        cnt = c;
-        pbase = a.offs[bhc];
-        ntile = (c + kTileM - 1) / kTileM;
-        const int64_t bh = bhc / a.nblk;
-        blk = bhc % a.nblk;
-        b = bh / a.HI;
-        h = (bh % a.HI) * hpi + item % hpi;
-        hk = h / (a.HQ / a.Hkv);
-        j = 0;
-        done = false;
-        return;
-      }
-      item += 2 * static_cast<int64_t>(gridDim.x);
-    }
-    done = true;
+constexpr int kRwThreads = 416;
+constexpr int kRwProd = 8, kRwMma = 12;  // first warp of each role
+constexpr int kRwQ = 4;                  // Q ring depth (Q, then P, then the staged O of a unit)
+constexpr uint32_t kRwSmem = kRwQ * kQBytes + 2 * kWsStage + 1024;  // 193 KB
+
+// Walks a CTA's units in order (every role keeps its own copy); 32-bit
+// arithmetic (unit, tile and list counts are below 2^31, checked on the host).
+struct RwUnit {
+  int32_t u, uend, k, nw, toff, cnt, ntile, hl, j, hpi, grp, nblk, HI;
+  int32_t b, h, hk, blk;
+  int4 next;  // work[k + 1], loaded ahead
+  bool done, run_start;
+  __device__ __forceinline__ void take(const TcArgs& a, int4 w) {
+    toff = w.y;
+    cnt = w.z;
+    ntile = (cnt + kTileM - 1) / kTileM;
+    const int32_t bh = w.x / nblk;
+    blk = w.x - bh * nblk;
+    b = bh / HI;
+    h = (bh - b * HI) * hpi + hl;
+    hk = h / grp;
+    next = k + 1 < nw ? a.work[k + 1] : make_int4(0, 0, 0, 0);
   }
-  __device__ __forceinline__ void start(const TcArgs& a, int slot) {
-    nitems = a.B * a.HI * a.nblk * (a.HQ / a.HI);
-    item = blockIdx.x + static_cast<int64_t>(slot) * gridDim.x;
-    m = 0;
-    n = 0;
-    seek(a);
+  __device__ __forceinline__ void start(const TcArgs& a, int64_t u0, int64_t u1, int32_t k0, int32_t nwork) {
+    hpi = static_cast<int32_t>(a.HQ / a.HI);
+    grp = static_cast<int32_t>(a.HQ / a.Hkv);
+    nblk = static_cast<int32_t>(a.nblk);
+    HI = static_cast<int32_t>(a.HI);
+    u = static_cast<int32_t>(u0);
+    uend = static_cast<int32_t>(u1);
+    nw = nwork;
+    run_start = true;
+    done = u >= uend;
+    if (done) return;
+    k = k0;
+    const int4 w = a.work[k];
+    const int32_t nt = (w.z + kTileM - 1) / kTileM;
+    const int32_t v = u - hpi * w.y;
+    hl = v / nt;
+    j = v - hl * nt;
+    take(a, w);
   }
-  __device__ __forceinline__ bool first() const { return j == 0; }
-  __device__ __forceinline__ bool last() const { return j == ntile - 1; }
-  __device__ __forceinline__ int64_t tile_first() const { return pbase + j * kTileM; }
-  __device__ __forceinline__ int64_t tile_rows() const {
-    const int64_t r = cnt - j * kTileM;
+  __device__ __forceinline__ bool last_of_run() const { return j == ntile - 1 || u + 1 == uend; }
+  __device__ __forceinline__ int64_t row0() const { return static_cast<int64_t>(toff + j) * kTileM; }
+  __device__ __forceinline__ int rows() const {
+    const int r = cnt - j * kTileM;
     return r < kTileM ? r : kTileM;
   }
   __device__ __forceinline__ void advance(const TcArgs& a) {
-    ++n;
-    if (j + 1 < ntile) {
-      ++j;
+    ++u;
+    run_start = false;
+    if (u >= uend) {
+      done = true;
       return;
     }
-    ++m;
-    item += 2 * static_cast<int64_t>(gridDim.x);
-    seek(a);
+    if (++j < ntile) return;
+    j = 0;
+    run_start = true;
+    if (++hl < hpi) {
+      ++h;
+      hk = h / grp;
+      return;
+    }
+    hl = 0;
+    ++k;
+    take(a, next);
   }
 };
 
-constexpr int kRwThreads = 416;  // producers: warps 8 / 11 (slot 0 rows 0-63 / 64-127), 10 / 12 (slot 1)
+// 8 fp32 * inv -> 8 bf16 as one 16-byte shared-memory store
+__device__ __forceinline__ void store_o_chunk(uint32_t addr, const float* v, float inv) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e] * inv, v[2 * e + 1] * inv);
+    w[e] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+               : "memory");
+}
+
 __global__ void __launch_bounds__(kRwThreads, 1)
-    remote_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
+    remote_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                     const __grid_constant__ CUtensorMap tmp) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t kv_full[2], kv_empty[2], q_full[2][2], q_empty[2][2], info_full[2][2], info_empty[2][2];
-  __shared__ uint64_t s_full[2], p_full[2], o_full[2], drain_bar;
-  __shared__ const __nv_bfloat16* qrows[2][kTileM];
-  __shared__ int32_t r_t[2][2][kTileM], r_slot[2][2][kTileM];
-  __shared__ float r_bias[2][2][kTileM];
+  __shared__ uint64_t kv_full[2], kv_empty[2], q_full[kRwQ], q_empty[kRwQ], info_full[kRwQ], info_empty[kRwQ];
+  __shared__ uint64_t stg_full[kRwQ], s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2], drain_bar;
+  __shared__ int32_t r_t[kRwQ][kTileM];
+  __shared__ float r_bias[kRwQ][kTileM];
+  __shared__ int64_t sh_u0, sh_u1;
+  __shared__ int32_t sh_k0, sh_nw;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  auto q_buf = [&](int s, int qb) { return sbase + static_cast<uint32_t>(s * 2 + qb) * kQBytes; };
-  auto kv_buf = [&](int s) { return sbase + 4 * kQBytes + static_cast<uint32_t>(s) * kWsStage; };
-  if (warp == kWsMma) {
+  auto q_buf = [&](int qi) { return sbase + static_cast<uint32_t>(qi) * kQBytes; };
+  auto kv_buf = [&](int st) { return sbase + kRwQ * kQBytes + static_cast<uint32_t>(st) * kWsStage; };
+  const int64_t hpi = a.HQ / a.HI;
+  if (warp == kRwMma) {
     tmem_alloc(&tmem_base, kWsTmemCols);
     tmem_relinquish();
   }
   if (tid == 0) {
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], kTileM);
-      mbar_init(&o_full[s], 1);
-      for (int qb = 0; qb < 2; ++qb) {
-        mbar_init(&q_full[s][qb], 64);
-        mbar_init(&q_empty[s][qb], kTileM);
-        mbar_init(&info_full[s][qb], 64);
-        mbar_init(&info_empty[s][qb], kTileM);
-      }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], kTileM);
+      mbar_init(&p_full[i], kTileM);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], kTileM);
+    }
+    for (int i = 0; i < kRwQ; ++i) {
+      mbar_init(&q_full[i], kTileM);  // one cp.async arrival per producer lane
+      mbar_init(&q_empty[i], 1);      // the unit's stores have read the staged O
+      mbar_init(&info_full[i], kTileM);
+      mbar_init(&info_empty[i], kTileM);
+      mbar_init(&stg_full[i], kTileM);
     }
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
     abort_flag = 0;
+    // this CTA's share [u0, u1) of the unit sequence
+    const int32_t nw = a.totals[1];
+    const int64_t U = static_cast<int64_t>(a.totals[0]) * hpi;
+    const int64_t G = (U + gridDim.x - 1) / gridDim.x;
+    int64_t u0 = static_cast<int64_t>(blockIdx.x) * G;
+    if (u0 > U) u0 = U;
+    sh_u0 = u0;
+    sh_u1 = u0 + G < U ? u0 + G : U;
+    sh_nw = nw;
+    sh_k0 = 0;
+  }
+  __syncthreads();
+  {  // the last list starting at or before u0 (lists are in tile order)
+    const int64_t u0 = sh_u0;
+    const int32_t nw = sh_nw, per = (nw + kRwThreads - 1) / kRwThreads;
+    const int32_t i0 = tid * per, i1 = i0 + per < nw ? i0 + per : nw;
+    int32_t best = -1;
+    for (int32_t i = i0; i < i1; ++i)
+      if (hpi * static_cast<int64_t>(__ldg(&a.work[i].y)) <= u0) best = i;
+    if (best >= 0) atomicMax(&sh_k0, best);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
   volatile int* abort_p = &abort_flag;
+  const int64_t u0 = sh_u0, u1 = sh_u1;
+  const int32_t k0 = sh_k0, nw = sh_nw;
 
-  if (warp == kWsProducer || warp >= kWsProducer + 2) {
-    // ---------------------------------------- producer of half a slot's rows
-    const int s = (warp == kWsProducer || warp == kWsProducer + 3) ? 0 : 1;
-    const int half = warp >= kWsProducer + 3 ? 1 : 0;  // rows 64*half .. 64*half + 63
-    RwCursor cs;
-    cs.start(a, s);
-    // this tile's rows of the half (lane L: rows 64*half + L, + 32), fetched one tile ahead
-    int64_t pq[2];
-    float pbz[2];
-    int32_t ppk[2];
-    auto fetch = [&]() {
-      const int64_t fp = cs.tile_first(), nh = cs.tile_rows();
-#pragma unroll
-      for (int k4 = 0; k4 < 2; ++k4) {
-        const int r = 64 * half + lane + 32 * k4;
-        ppk[k4] = -1;
-        if (r < nh) {
-          pq[k4] = a.pair_q[fp + r];
-          pbz[k4] = a.pair_bias[fp + r];
-          ppk[k4] = a.pairs[fp + r];
-        }
+  if (warp >= kRwProd && warp < kRwMma) {
+    // -------------------------------------------------------------- producers
+    const int pw = warp - kRwProd;  // rows 32 pw .. 32 pw + 31
+    const int r = 32 * pw + lane;
+    RwUnit cs;
+    cs.start(a, u0, u1, k0, nw);
+    int32_t pt = -1;
+    int64_t pq = 0;
+    float pbz = 0.f;
+    auto fetch = [&]() {  // this lane's row of the unit (loaded one unit ahead)
+      const int64_t row = cs.row0() + r;
+      pt = -1;
+      if (r < cs.rows()) {
+        pt = a.pair_t[row];
+        pq = a.pair_q[row];
+        pbz = a.pair_bias[row];
       }
     };
     if (!cs.done) fetch();
+    int qi = 0;
+    uint32_t qph = 0;
+    int64_t n = 0, run = 0;
     bool ok = true;
     while (ok && !cs.done) {
-      if (cs.first()) {
-        if (cs.m > 0 &&
-            !__all_sync(0xffffffffu, ws_wait(&kv_empty[s], static_cast<uint32_t>((cs.m - 1) & 1), abort_p, 421))) {
-          ok = false;
-          break;
+      if (cs.run_start) {
+        if (pw == 0) {
+          const int st = static_cast<int>(run & 1);
+          if (run >= 2 && !__all_sync(0xffffffffu, ws_wait(&kv_empty[st], static_cast<uint32_t>(((run >> 1) - 1) & 1),
+                                                           abort_p, 421))) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {  // K and V of the block: four 64 x 64 boxes
+            const int row0 = cs.blk * kBlk;
+            const uint32_t dst = kv_buf(st);
+            mbar_arrive_expect_tx(&kv_full[st], kWsStage);
+            tma_load_4d(dst, &tmk, 0, row0, cs.hk, cs.b, &kv_full[st]);
+            tma_load_4d(dst + kKVHalf, &tmk, 64, row0, cs.hk, cs.b, &kv_full[st]);
+            tma_load_4d(dst + kKVBytes, &tmv, 0, row0, cs.hk, cs.b, &kv_full[st]);
+            tma_load_4d(dst + kKVBytes + kKVHalf, &tmv, 64, row0, cs.hk, cs.b, &kv_full[st]);
+          }
+          __syncwarp();
         }
-        if (half == 0 && lane == 0) {
-          const int row0 = static_cast<int>(cs.blk * kBlk), hh = static_cast<int>(cs.hk), bb = static_cast<int>(cs.b);
-          const uint32_t dst = kv_buf(s);
-          mbar_arrive_expect_tx(&kv_full[s], kWsStage);
-          tma_load_4d(dst, &tmk, 0, row0, hh, bb, &kv_full[s]);
-          tma_load_4d(dst + kKVHalf, &tmk, 64, row0, hh, bb, &kv_full[s]);
-          tma_load_4d(dst + kKVBytes, &tmv, 0, row0, hh, bb, &kv_full[s]);
-          tma_load_4d(dst + kKVBytes + kKVHalf, &tmv, 64, row0, hh, bb, &kv_full[s]);
-        }
-        __syncwarp();
+        ++run;
       }
-      const int qb = static_cast<int>(cs.n & 1);
-      if (cs.n >= 2) {
-        const uint32_t par = static_cast<uint32_t>(((cs.n >> 1) - 1) & 1);
-        if (!__all_sync(0xffffffffu, ws_wait(&q_empty[s][qb], par, abort_p, 422) &&
-                                         ws_wait(&info_empty[s][qb], par, abort_p, 423))) {
-          ok = false;
-          break;
-        }
+      if (n >= kRwQ && !__all_sync(0xffffffffu, ws_wait(&q_empty[qi], qph ^ 1u, abort_p, 422) &&
+                                                    ws_wait(&info_empty[qi], qph ^ 1u, abort_p, 423))) {
+        ok = false;
+        break;
       }
-      const int64_t hq = cs.h * a.sqh;
-#pragma unroll
-      for (int k4 = 0; k4 < 2; ++k4) {
-        const int r = 64 * half + lane + 32 * k4;
-        const int32_t pk = ppk[k4];
-        const int32_t tt = pk >= 0 ? pk / static_cast<int32_t>(a.S) : -1;
-        qrows[s][r] = pk >= 0 ? a.q + pq[k4] + hq : nullptr;
-        r_t[s][qb][r] = tt;
-        r_slot[s][qb][r] = pk >= 0 ? pk - tt * static_cast<int32_t>(a.S) : 0;
-        r_bias[s][qb][r] = pk >= 0 ? pbz[k4] : 0.f;
-      }
-      mbar_arrive(&info_full[s][qb]);  // release: the row info above
-      __syncwarp();
+      r_t[qi][r] = pt;
+      r_bias[qi][r] = pbz;
+      mbar_arrive(&info_full[qi]);  // release: the row info above
+      const unsigned long long src =
+          pt >= 0 ? reinterpret_cast<unsigned long long>(a.q + pq + cs.h * a.sqh) : 0ull;
       const int cc = lane & 15;
-      const uint32_t dst0 = q_buf(s, qb) + (cc >> 3) * (kQBytes / 2);
-#pragma unroll 8
-      for (int i = 0; i < kTileM / 4; ++i) {
-        const int r = 64 * half + (lane >> 4) + 2 * i;
-        const __nv_bfloat16* g = qrows[s][r];
-        cp_async16_zfill(dst0 + sw128_off(r, cc & 7), g ? static_cast<const void*>(g + cc * 8) : a.q, g != nullptr);
+      const uint32_t dst0 = q_buf(qi) + (cc >> 3) * (kQBytes / 2);
+#pragma unroll 1
+      for (int i = 0; i < 16; ++i) {
+        const int rr = 2 * i + (lane >> 4);
+        const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(__shfl_sync(0xffffffffu, src, rr));
+        cp_async16_zfill(dst0 + sw128_off(32 * pw + rr, cc & 7), g ? static_cast<const void*>(g + cc * 8) : a.q,
+                         g != nullptr);
       }
-      cp_async_mbar_arrive(&q_full[s][qb]);
-      __syncwarp();  // qrows is rewritten by the next tile
+      cp_async_mbar_arrive(&q_full[qi]);
       cs.advance(a);
-      if (!cs.done) fetch();  // next tile's rows in flight while this one's copies land
+      if (!cs.done) fetch();  // the next unit's rows in flight while this one's copies land
+      ++n;
+      if (++qi == kRwQ) {
+        qi = 0;
+        qph ^= 1u;
+      }
     }
     cp_async_wait_all();
-  } else if (warp == kWsMma) {
+  } else if (warp == kRwMma) {
     // --------------------------------------------------------------------- MMA
     if (lane == 0) {
-      RwCursor c[2];
-      c[0].start(a, 0);
-      c[1].start(a, 1);
-      bool pend[2] = {false, false}, plast[2] = {false, false};
-      int64_t pn[2] = {0, 0};
+      RwUnit cq;
+      cq.start(a, u0, u1, k0, nw);
+      int64_t nq = 0, np = 0, run = -1;  // units with S / O issued; KV run of the last S
+      int qi = 0;
+      uint32_t qph = 0;
+      // per unit between its S and O (byte n & 1): Q buffer | KV stage << 2 | last of run << 3
+      uint32_t pv_info = 0;
+      uint64_t idle_since = 0;  // start of the current idle stretch (0: busy)
       bool ok = true;
-      auto issue_s = [&](int s) -> bool {
-        RwCursor& cs = c[s];
-        const int qb = static_cast<int>(cs.n & 1);
-        if (cs.first() && !ws_wait(&kv_full[s], static_cast<uint32_t>(cs.m & 1), abort_p, 424)) return false;
-        if (!ws_wait(&q_full[s][qb], static_cast<uint32_t>((cs.n >> 1) & 1), abort_p, 425)) return false;
-        tc_fence_after();
-        issue_qk(tmem + s * 256, q_buf(s, qb), kv_buf(s));
-        mma_commit(&s_full[s]);
-        pend[s] = true;
-        plast[s] = cs.last();
-        pn[s] = cs.n;
-        cs.advance(a);
-        return true;
-      };
-      auto issue_pv_step = [&](int s) -> bool {
-        if (!ws_wait(&p_full[s], static_cast<uint32_t>(pn[s] & 1), abort_p, 426)) return false;
-        const int qb = static_cast<int>(pn[s] & 1);
-        tc_fence_after();
-        issue_pv(tmem + s * 256 + 128, q_buf(s, qb), kv_buf(s) + kKVBytes, false);  // P over the dead Q tile
-        mma_commit(&o_full[s]);
-        if (plast[s]) mma_commit(&kv_empty[s]);
-        pend[s] = false;
-        return true;
-      };
-      for (int s = 0; s < 2 && ok; ++s)
-        if (!c[s].done) ok = issue_s(s);
-      while (ok && (pend[0] || pend[1])) {
-        for (int s = 0; s < 2 && ok; ++s) {
-          if (pend[s]) ok = issue_pv_step(s);
-          if (ok && !c[s].done) ok = issue_s(s);
+      while (ok && (!cq.done || np < nq)) {
+        bool did = false;
+        if (!cq.done && nq < np + 2) {
+          const int sb = static_cast<int>(nq & 1);
+          const int64_t rn = cq.run_start ? run + 1 : run;
+          const int st = static_cast<int>(rn & 1);
+          if ((!cq.run_start || mbar_ready(&kv_full[st], static_cast<uint32_t>((rn >> 1) & 1))) &&
+              mbar_ready(&q_full[qi], qph) &&
+              (nq < 2 || mbar_ready(&s_empty[sb], static_cast<uint32_t>(((nq >> 1) - 1) & 1)))) {
+            tc_fence_after();
+            issue_qk(tmem + sb * 64, q_buf(qi), kv_buf(st));
+            mma_commit(&s_full[sb]);
+            run = rn;
+            const uint32_t inf = static_cast<uint32_t>(qi) | static_cast<uint32_t>(st) << 2 |
+                                 (cq.last_of_run() ? 8u : 0u);
+            pv_info = (pv_info & ~(0xffu << (8 * sb))) | inf << (8 * sb);
+            cq.advance(a);
+            ++nq;
+            if (++qi == kRwQ) {
+              qi = 0;
+              qph ^= 1u;
+            }
+            did = true;
+          }
+        }
+        if (np < nq) {
+          const int sb = static_cast<int>(np & 1);
+          if (mbar_ready(&p_full[sb], static_cast<uint32_t>((np >> 1) & 1)) &&
+              (np < 2 || mbar_ready(&o_empty[sb], static_cast<uint32_t>(((np >> 1) - 1) & 1)))) {
+            const uint32_t inf = (pv_info >> (8 * sb)) & 0xffu;
+            const int pq = static_cast<int>(inf & 3u), pst = static_cast<int>((inf >> 2) & 1u);
+            tc_fence_after();
+            issue_pv(tmem + 128 + sb * 128, q_buf(pq), kv_buf(pst) + kKVBytes, false);  // P over the dead Q tile
+            mma_commit(&o_full[sb]);
+            if (inf & 8u) mma_commit(&kv_empty[pst]);
+            ++np;
+            did = true;
+          }
+        }
+        if (did) {
+          idle_since = 0;
+        } else {  // nothing ready: back off so the other warps of this SM sub-partition can issue
+          const uint64_t now = global_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > kWaitLimitNs) {
+            atomicExch(&g_tc_error, 424);
+            *abort_p = 1;
+            ok = false;
+          } else if (*abort_p) {
+            ok = false;
+          }
+          __nanosleep(40);
         }
       }
     }
     __syncwarp();
   } else {
-    // ----------------------------------------------------------------- softmax
-    const int s = warp >> 2;
+    // ---------------------------------------------------- row warpgroups 0 / 1
+    const int wg = warp >> 2;
     const int r = tid & (kTileM - 1);
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tm_s = tmem + s * 256 + lane_off, tm_o = tmem + s * 256 + 128 + lane_off;
-    RwCursor cs;
-    cs.start(a, s);
+    const uint32_t tm_s = tmem + wg * 64 + lane_off, tm_o = tmem + 128 + wg * 128 + lane_off;
+    const bool elected = r == 0;
+    RwUnit cs;
+    cs.start(a, u0, u1, k0, nw);
+    if (wg == 1 && !cs.done) cs.advance(a);
+    int qi = wg;            // Q ring slot of unit n = 2 m + wg
+    uint32_t qph = 0;
+    uint32_t m = 0;         // this warpgroup's unit count
     while (!cs.done) {
-      const int qb = static_cast<int>(cs.n & 1);
-      if (!__all_sync(0xffffffffu,
-                      ws_wait(&info_full[s][qb], static_cast<uint32_t>((cs.n >> 1) & 1), abort_p, 427)))
-        break;
-      const int64_t t = r_t[s][qb][r];
-      const int64_t slot = r_slot[s][qb][r];
-      const float bias2 = r_bias[s][qb][r];
-      mbar_arrive(&info_empty[s][qb]);
+      const uint32_t ph = m & 1;
+      if (!__all_sync(0xffffffffu, ws_wait(&info_full[qi], qph, abort_p, 427))) break;
+      const int64_t t = r_t[qi][r];
+      const float bias2 = r_bias[qi][r];
+      mbar_arrive(&info_empty[qi]);
       const bool row_ok = t >= 0;
       int64_t rlo = 0, rhi = 0;
       if (row_ok) remote_range(a, cs.b, t, cs.blk, rlo, rhi);
-      if (!__all_sync(0xffffffffu, ws_wait(&s_full[s], static_cast<uint32_t>(cs.n & 1), abort_p, 428))) break;
+      if (!__all_sync(0xffffffffu, ws_wait(&s_full[wg], ph, abort_p, 428))) break;
       tc_fence_after();
       float sv[64];
       {
@@ -940,71 +1101,72 @@ __global__ void __launch_bounds__(kRwThreads, 1)
         tmem_ld32(tm_s + 32, s1);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) { sv[i] = s0[i]; sv[32 + i] = s1[i]; }
+        for (int i = 0; i < 32; ++i) {
+          sv[i] = s0[i];
+          sv[32 + i] = s1[i];
+        }
       }
-      const int64_t k0 = cs.blk * kBlk;
-      const int klo = row_ok ? clamp_key(rlo - k0) : 0, khi = row_ok ? clamp_key(rhi - k0) : 0;
+      tc_fence_before();
+      mbar_arrive(&s_empty[wg]);
+      const int64_t k0b = static_cast<int64_t>(cs.blk) * kBlk;
+      const int klo = row_ok ? clamp_key(rlo - k0b) : 0, khi = row_ok ? clamp_key(rhi - k0b) : 0;
       const bool full = __all_sync(0xffffffffu, klo == 0 && khi == kBlk);
       const float mraw = block_row_max(sv, klo, khi, full);
       const float mx = mraw == -INFINITY ? -INFINITY : fmaf(mraw, a.scale_log2, bias2);
       const float l = block_row_exp(sv, a.scale_log2, bias2 - (mx == -INFINITY ? 0.f : mx));
-      const uint32_t p_s = q_buf(s, qb);  // Q of this tile is dead once S is in TMEM
-      store_p_row(p_s, r, 0, sv);
-      store_p_row(p_s, r, 4, sv + 32);
+      const uint32_t tile = q_buf(qi);  // Q of this unit is dead once S is in TMEM
+      store_p_row(tile, r, 0, sv);
+      store_p_row(tile, r, 4, sv + 32);
       fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(&p_full[s]);
-      if (!__all_sync(0xffffffffu, ws_wait(&o_full[s], static_cast<uint32_t>(cs.n & 1), abort_p, 429))) break;
+      mbar_arrive(&p_full[wg]);
+      // O of the unit; P in the tile is dead once O is complete
+      if (!__all_sync(0xffffffffu, ws_wait(&o_full[wg], ph, abort_p, 429))) break;
       tc_fence_after();
-      const int64_t prow = row_ok ? ((cs.b * a.T + t) * a.S + slot) * a.HQ + cs.h : -1;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      // stage the normalised rows (bf16) in the dead Q tile, 16-byte chunks
-      // rotated by the row so the row-per-thread writes spread over the banks
-      const uint32_t stg = q_buf(s, qb);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float ov[32];
-        tmem_ld32(tm_o + 32 * c, ov);
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        float o0[32], o1[32];
+        tmem_ld32(tm_o + 64 * hf, o0);
+        tmem_ld32(tm_o + 64 * hf + 32, o1);
         tmem_wait_ld();
+        const uint32_t dst = tile + hf * (kQBytes / 2);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t w4[4];
+        for (int c = 0; c < 4; ++c) store_o_chunk(dst + sw128_off(r, c), o0 + 8 * c, inv);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 hv = __floats2bfloat162_rn(ov[8 * q4 + 2 * e] * inv, ov[8 * q4 + 2 * e + 1] * inv);
-            w4[e] = *reinterpret_cast<uint32_t*>(&hv);
-          }
-          const int k = 4 * c + q4;
-          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(stg + r * 256 + ((k ^ (r & 15)) << 4)),
-                       "r"(w4[0]), "r"(w4[1]), "r"(w4[2]), "r"(w4[3])
-                       : "memory");
+        for (int c = 0; c < 4; ++c) store_o_chunk(dst + sw128_off(r, 4 + c), o1 + 8 * c, inv);
+      }
+      tc_fence_before();
+      mbar_arrive(&o_empty[wg]);
+      fence_async_smem();
+      mbar_arrive(&stg_full[qi]);
+      const int64_t row0 = cs.row0();
+      if (r < cs.rows()) a.part_lse[cs.hl * a.prow_cap + row0 + r] = l > 0.f ? mx + log2f(l) : -INFINITY;
+      if (elected) {
+        if (ws_wait(&stg_full[qi], qph, abort_p, 432)) {
+          tma_store_3d(&tmp, tile, 0, static_cast<int>(row0), cs.hl);
+          tma_store_3d(&tmp, tile + kQBytes / 2, 64, static_cast<int>(row0), cs.hl);
+          bulk_commit();
+          bulk_wait_read<0>();
         }
+        mbar_arrive(&q_empty[qi]);  // the tile may be refilled
       }
       __syncwarp();
-      // this warp's 32 rows leave as whole 256-byte rows, two rows per instruction
-      const int wrow0 = 32 * (warp & 3);
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const int rl = 2 * i + (lane >> 4), rr = wrow0 + rl, k = lane & 15;
-        const int64_t pr = __shfl_sync(0xffffffffu, prow, rl);
-        uint4 val;
-        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
-                     : "r"(stg + rr * 256 + ((k ^ (rr & 15)) << 4))
-                     : "memory");
-        if (pr >= 0) *reinterpret_cast<uint4*>(a.part_o + pr * kD + k * 8) = val;
-      }
-      if (row_ok) a.part_lse[prow] = l > 0.f ? mx + log2f(l) : -INFINITY;
-      tc_fence_before();            // O read before the next step's P.V overwrites it
-      mbar_arrive(&q_empty[s][qb]);  // the Q tile (staging) may be refilled
       cs.advance(a);
+      if (!cs.done) cs.advance(a);  // the other warpgroup's unit
+      ++m;
+      qi += 2;
+      if (qi >= kRwQ) {
+        qi -= kRwQ;
+        qph ^= 1u;
+      }
     }
+    if (elected) bulk_wait<0>();
   }
   // ------------------------------------------------------------------- exit
   tc_fence_before();
   __syncthreads();
-  if (warp == kWsMma) {
-    if (*abort_p) {
+  if (warp == kRwMma) {
+    if (*abort_p) {  // MMAs may still be in flight: wait for all of them
       if (lane == 0) {
         mma_commit(&drain_bar);
         mbar_wait(&drain_bar, 0, 430);
@@ -2202,31 +2364,34 @@ TcLayout tc_layout(const srswa_gather_desc* g) {
   TcLayout L;
   const int64_t nblk = (g->T + kBlk - 1) / kBlk;
   const int64_t nbh = g->B * g->HI * nblk;
-  const int64_t npairs = g->B * g->HI * g->T * g->S;
-  L.max_tiles = npairs / kTileM + nbh + 1;
+  const int64_t nsel = g->B * g->HI * g->T * g->S;
+  const int64_t hpi = g->HI > 0 ? g->HQ / g->HI : 1;
+  // every nonempty list rounds its pairs up to whole tiles
+  L.max_tiles = nsel / kTileM + nbh + 1;
+  const size_t cap = static_cast<size_t>(L.max_tiles) * kTileM;
   size_t off = 0;
   L.part_o = off;
-  off += al256(static_cast<size_t>(g->B * g->T * g->S * g->HQ * kD) * 2);
+  off += al256(static_cast<size_t>(hpi) * cap * kD * 2);
   L.part_lse = off;
-  off += al256(static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4);
+  off += al256(static_cast<size_t>(hpi) * cap * 4);
   L.count = off;
-  off += al256(static_cast<size_t>(nbh) * 4);
-  L.offs = off;
   off += al256(static_cast<size_t>(nbh) * 4);
   L.cursor = off;
   off += al256(static_cast<size_t>(nbh) * 4);
-  L.tiles = off;
-  off += al256(static_cast<size_t>(L.max_tiles) * 16);
-  L.ntiles = off;
+  L.work = off;
+  off += al256(static_cast<size_t>(nbh) * 16);
+  L.totals = off;
   off += 256;
-  L.pairs = off;
-  off += al256(static_cast<size_t>(npairs) * 4);
+  L.pair_t = off;
+  off += al256(cap * 4);
+  L.pair_q = off;
+  off += al256(cap * 8);
+  L.pair_bias = off;
+  off += al256(cap * 4);
+  L.prow = off;
+  off += al256(static_cast<size_t>(nsel) * 4);
   L.lse = off;  // the window lse when the caller asks for none (the merge reads it)
   off += al256(static_cast<size_t>(g->B * g->T * g->HQ) * 4);
-  L.pair_q = off;
-  off += al256(static_cast<size_t>(npairs) * 8);
-  L.pair_bias = off;
-  off += al256(static_cast<size_t>(npairs) * 4);
   L.total = off;
   return L;
 }
@@ -2269,6 +2434,20 @@ static bool make_tmap(CUtensorMap* m, const void* base, int64_t B, int64_t T, in
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tensor map of the partial rows [hpi, cap, 128] bf16: box of 64 features x
+// 128 rows of one head, 128-byte swizzle (the stores of the remote pass).
+static bool make_tmap_rows(CUtensorMap* m, void* base, int64_t cap, int64_t hpi) {
+  EncodeTiledFn enc = tmap_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(cap), static_cast<cuuint64_t>(hpi)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(cap) * kD * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kTileM), 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool tc_eligible(const srswa_gather_desc* g) {
   return g->D == kD && g->block_size == kBlk && g->dtype == SRSWA_BF16 && g->S <= 64 && g->T > 0 && g->scale > 0.f &&
          ((g->sqb | g->sqt | g->sqh | g->skb | g->skt | g->skh | g->svb | g->svt | g->svh) & 7) == 0;
@@ -2289,27 +2468,30 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   a.o = static_cast<__nv_bfloat16*>(o); a.sob = sob; a.sot = sot; a.soh = soh;
   a.lse = lse ? lse : reinterpret_cast<float*>(ws + L.lse);
   a.sel = sel; a.bias = bias; a.seg = seg;
+  const int64_t hpi = g->HQ / g->HI;
   a.part_o = reinterpret_cast<__nv_bfloat16*>(ws + L.part_o);
   a.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
-  a.pairs = reinterpret_cast<int32_t*>(ws + L.pairs);
+  a.prow = reinterpret_cast<int32_t*>(ws + L.prow);
+  a.pair_t = reinterpret_cast<int32_t*>(ws + L.pair_t);
   a.pair_q = reinterpret_cast<int64_t*>(ws + L.pair_q);
   a.pair_bias = reinterpret_cast<float*>(ws + L.pair_bias);
-  a.tiles = reinterpret_cast<int4*>(ws + L.tiles);
-  a.ntiles = reinterpret_cast<int32_t*>(ws + L.ntiles);
+  a.work = reinterpret_cast<int4*>(ws + L.work);
+  a.totals = reinterpret_cast<int32_t*>(ws + L.totals);
+  a.prow_cap = L.max_tiles * kTileM;
   a.B = g->B; a.T = g->T; a.HQ = g->HQ; a.Hkv = g->Hkv; a.HI = g->HI; a.S = g->S;
   a.LW = g->local_window > 0 ? g->local_window : kBlk;
   a.nblk = (g->T + kBlk - 1) / kBlk;
   a.scale_log2 = g->scale * kLog2e;
   int32_t* count = reinterpret_cast<int32_t*>(ws + L.count);
-  int32_t* offs = reinterpret_cast<int32_t*>(ws + L.offs);
   int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
-  a.count = count;
-  a.offs = offs;
+  // partial rows and selections are indexed with 32-bit integers
+  if (a.prow_cap >= (1ll << 31) || L.max_tiles * hpi >= (1ll << 31) || g->B * g->HI * g->T * g->S >= (1ll << 31))
+    return SRSWA_ETOOLARGE;
 
   static bool attr_done = false;
   static int num_sms = 148;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
+    cudaError_t e = cudaFuncSetAttribute(remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -2317,12 +2499,13 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     attr_done = true;
   }
-  // the tensor maps of q, k and v; when the driver refuses one, the caller
-  // runs the CUDA-core kernels instead (nothing has been launched yet)
-  alignas(64) CUtensorMap tmq, tmk, tmv;
+  // the tensor maps of q, k, v and the partial rows; when the driver refuses
+  // one, the caller runs the CUDA-core kernels instead (nothing launched yet)
+  alignas(64) CUtensorMap tmq, tmk, tmv, tmp;
   if (!(make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
         make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
-        make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk)))
+        make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk) &&
+        make_tmap_rows(&tmp, a.part_o, a.prow_cap, hpi)))
     return kTcNoTensorMap;
   if (g->S > 0) {
     const int64_t nbh = a.B * a.HI * a.nblk;
@@ -2330,15 +2513,12 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     const int64_t rows = a.B * a.HI * a.T;
     pairs_count_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, count);
     SRSWA_CUDA_TRY(cudaGetLastError());
-    pairs_scan_kernel<<<1, 1024, 0, st>>>(a, count, offs, cursor, const_cast<int4*>(a.tiles),
-                                          const_cast<int32_t*>(a.ntiles));
+    fwd_lists_scan_kernel<<<1, 1024, 0, st>>>(a, count, cursor, const_cast<int4*>(a.work),
+                                              const_cast<int32_t*>(a.totals));
     SRSWA_CUDA_TRY(cudaGetLastError());
-    pairs_fill_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, cursor,
-                                                                               const_cast<int32_t*>(a.pairs));
+    pairs_fill_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, cursor);
     SRSWA_CUDA_TRY(cudaGetLastError());
-    // slots without a partial read as NaN in the merge
-    SRSWA_CUDA_TRY(cudaMemsetAsync(a.part_lse, 0xff, static_cast<size_t>(g->B * g->T * g->S * g->HQ) * 4, st));
-    remote_ws_kernel<<<num_sms, kRwThreads, kWsSmem, st>>>(a, tmk, tmv);
+    remote_ws_kernel<<<num_sms, kRwThreads, kRwSmem, st>>>(a, tmk, tmv, tmp);
     SRSWA_CUDA_TRY(cudaGetLastError());
   } else {
     a.part_o = nullptr;

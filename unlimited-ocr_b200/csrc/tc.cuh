@@ -35,10 +35,20 @@ static inline int tc_read_clear_error(int* out) {
   return 0;
 }
 
-constexpr uint32_t kSpinLimit = 1u << 22;  // try_wait rounds (each may suspend briefly)
+// Bound of every wait on an mbarrier (wall clock, %globaltimer ns).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Upper bound of one suspended try_wait (ns): the waiting warp sleeps until
+// the phase completes or this much time has passed, leaving its issue slots
+// to the other warps of the SM sub-partition.
+constexpr uint32_t kSuspendHintNs = 20000;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 // ---------------------------------------------------------------- mbarrier --
@@ -48,20 +58,27 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+// One suspended test of the phase with parity `parity` (true: completed).
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar_addr), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return done != 0;
+}
 // Wait for the phase with parity `parity` to complete; false if the bounded
 // wait expired (error recorded).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
   const uint32_t a = smem_u32(bar);
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
+  if (mbar_try_wait(a, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait(a, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) break;
   }
   atomicExch(&g_tc_error, code);
   return false;
@@ -199,6 +216,40 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int 
       "[%6];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 3-D tiled TMA store (no multicast) of a shared-memory box to the tensor
+// map's coordinates (c0 innermost); tracked by the issuing thread's bulk
+// async-group.  The writers of the box fence with fence_async_smem() first.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until at most N of this thread's bulk groups are still in flight
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Non-blocking test: has the phase with parity `parity` completed?
+__device__ __forceinline__ bool mbar_ready(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
 }
 
 // byte offset of 16-byte chunk c (0..7) of row r inside a 128B-swizzled tile
