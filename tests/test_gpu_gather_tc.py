@@ -115,6 +115,35 @@ def test_tc_forward_vs_row_kernel_large(cuda):
     np.testing.assert_allclose(lse_tc.cpu().numpy(), lse_rows.cpu().numpy(), rtol=1e-3, atol=1e-3)
 
 
+@pytest.mark.parametrize("layout", ["fused_qkv", "padded_heads"])
+def test_tc_forward_strided_q(cuda, layout):
+    """q as a view of a larger buffer (a fused q|k|v projection, or heads
+    padded to D + 8) gives the contiguous-q result bit for bit: the remote
+    pass gathers q rows through the caller's strides."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    B, T_, H, D, BS, LW, K = 2, 1536, 4, 128, 64, 256, 6
+    q = (torch.randn(B, T_, H, D, device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, T_, H, D, device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, T_, H, D, device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+    rng = np.random.default_rng(3)
+    _, _, _, sel, bias, nblk = _inputs(rng, B, T_, 1, 1, K)
+    sel_p = ops.pack_selection(T(sel, cuda), nblk)
+    bias_t = T(bias, cuda)
+    if layout == "fused_qkv":
+        buf = torch.cat([q, k, v], dim=2)           # [B, T, 3H, D]
+        qs = buf[:, :, :H]
+    else:
+        buf = torch.zeros(B, T_, H, D + 8, device=cuda, dtype=torch.bfloat16)
+        buf[..., :D] = q
+        qs = buf[..., :D]
+    o_ref, lse_ref = ops.gather_fwd(q, k, v, sel_p, bias_t, None, BS, 1 / math.sqrt(D), LW)
+    o, lse = ops.gather_fwd(qs, k, v, sel_p, bias_t, None, BS, 1 / math.sqrt(D), LW)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    assert torch.equal(o, o_ref)
+    assert torch.equal(lse, lse_ref)
+
+
 def _route_case(cuda, seed, B, T_, H, Hkv, K, LW, dtype=torch.bfloat16):
     g = torch.Generator(device="cuda").manual_seed(seed)
     D, BS = 128, 64
