@@ -65,15 +65,15 @@ struct TcArgs {
   const int32_t* seg;         // [B, T] or null
   // forward remote pass: every (b*HI + hi, block) list owns whole 128-row
   // tiles of partial rows; a selection's partial row is prow[b, hi, t, s]
-  __nv_bfloat16* part_o;      // [HQ/HI, prow_cap, D] bf16, normalised
-  float* part_lse;            // [HQ/HI, prow_cap] log2 domain
+  __nv_bfloat16* part_o;      // [prow_cap, HQ/HI, D] bf16, normalised
+  float* part_lse;            // [prow_cap, HQ/HI] log2 domain
   int32_t* prow;              // [B, HI, T, S] partial row, -1 if none
   int32_t* pair_t;            // per partial row: query t
   int64_t* pair_q;            // per partial row: b * sqb + t * sqt (the query head's offset is added per unit)
   float* pair_bias;           // per partial row: slot bias * log2 e (0 without bias)
   const int4* work;           // nonempty lists: (b*HI + hi) * nblk + block, first tile, pair count, 0
   const int32_t* totals;      // {tiles, nonempty lists}
-  int64_t prow_cap;           // partial rows per query head of an index head
+  int64_t prow_cap;           // partial rows (each holds the HQ/HI heads of an index head)
   // backward lists
   const int32_t* pairs;       // packed t * S + s, grouped by (b, hi, block)
   const int4* tiles;          // (b*HI + hi, block, first pair, count)
@@ -452,81 +452,86 @@ __device__ __forceinline__ void band_row_store(const TcArgs& a, int64_t b, int64
   if (row_ok && a.lse) a.lse[(b * a.T + t) * a.HQ + h] = l > 0.f ? (m_ref + log2f(l)) * kLn2 : -INFINITY;
 }
 
-// Row-wise log-sum-exp merge of the window result (o, lse, as written by the
-// band pass) with the row's remote partials; one warp per (b, t, h), lane =
-// 4 features.  Lane s (and s + 32) reads slot s's partial row from prow (-1:
-// no partial, i.e. unused, repeated or without remote keys) and that row's
-// lse; the first eight partial rows are requested together with the lse
-// values.  Rows without a partial keep the window result.  Memory-bound.
-__global__ void __launch_bounds__(256) merge_partials_kernel(const TcArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= a.B * a.T * a.HQ) return;
-  const int64_t h = row % a.HQ, bt = row / a.HQ;
+// Log-sum-exp merge of the window result (o, lse, as written by the band
+// pass) with the remote partials.  One CTA per (b, t) and up to 16 heads
+// (blockIdx.y), thread = (head, 8 features): a selection's partials of all
+// heads of its index head are one contiguous run of rows, so every load is a
+// coalesced 16-byte word.  prow (-1: no partial, i.e. unused, repeated or
+// without remote keys) is read by all threads of the index head; slots go in
+// groups of eight with an online rescale.  Heads without a partial keep the
+// window result.  Memory-bound.
+constexpr int kMgHeads = 16;  // heads per CTA
+__global__ void __launch_bounds__(kMgHeads * 16) merge_partials_kernel(const TcArgs a) {
+  const int64_t bt = blockIdx.x;
+  const int64_t h = static_cast<int64_t>(blockIdx.y) * kMgHeads + (threadIdx.x >> 4);
+  const int f8 = threadIdx.x & 15;
+  if (h >= a.HQ) return;
   const int64_t t = bt % a.T, b = bt / a.T;
   const int64_t hpi = a.HQ / a.HI, hi = h / hpi, hl = h - hi * hpi;
   const int32_t* pr = a.prow + ((b * a.HI + hi) * a.T + t) * a.S;
-  const int ns = static_cast<int>(a.S < 64 ? a.S : 64);
-  const int32_t r0 = lane < ns ? __ldg(pr + lane) : -1;
-  const int32_t r1 = lane + 32 < ns ? __ldg(pr + lane + 32) : -1;
-  const float* plse = a.part_lse + hl * a.prow_cap;
-  const __nv_bfloat16* po = a.part_o + hl * a.prow_cap * kD + lane * 4;
   float* lse_p = a.lse + bt * a.HQ + h;
-  __nv_bfloat16* op = a.o + b * a.sob + t * a.sot + h * a.soh + lane * 4;
-  const float v0 = r0 >= 0 ? __ldcs(plse + r0) : -INFINITY;
-  const float v1 = r1 >= 0 ? __ldcs(plse + r1) : -INFINITY;
-  uint2 u[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {  // first group of partial rows, in flight with the lse loads
-    const int32_t rk = __shfl_sync(0xffffffffu, r0, k);
-    u[k] = (k < ns && rk >= 0) ? __ldcs(reinterpret_cast<const uint2*>(po + static_cast<int64_t>(rk) * kD))
-                               : make_uint2(0u, 0u);
-  }
+  uint4* op = reinterpret_cast<uint4*>(a.o + b * a.sob + t * a.sot + h * a.soh) + f8;
   const float lb = *lse_p * kLog2e;
-  const uint2 ob = *reinterpret_cast<const uint2*>(op);
-  float M = warp_max(fmaxf(v0, v1));
-  if (M == -INFINITY) return;  // no remote partial: the window result stands (warp-uniform)
-  M = fmaxf(M, lb);
-  float den = (v0 == -INFINITY ? 0.f : exp2f(v0 - M)) + (v1 == -INFINITY ? 0.f : exp2f(v1 - M));
-  den = warp_sum(den);
-  const float wb = lb == -INFINITY ? 0.f : exp2f(lb - M);
-  den += wb;
-  float acc[4];
-  acc[0] = wb * bf16_lo(ob.x);
-  acc[1] = wb * bf16_hi(ob.x);
-  acc[2] = wb * bf16_lo(ob.y);
-  acc[3] = wb * bf16_hi(ob.y);
-  for (int g0 = 0; g0 < ns; g0 += 8) {
-    if (g0 > 0) {
+  const uint4 ob = *op;
+  const int ns = static_cast<int>(a.S);
+  float M = lb, den = lb == -INFINITY ? 0.f : 1.f;  // weights relative to M
+  float acc[8];
+  {
+    const uint32_t wv[4] = {ob.x, ob.y, ob.z, ob.w};
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int s2 = g0 + k;
-        const int32_t rk = __shfl_sync(0xffffffffu, s2 < 32 ? r0 : r1, s2 & 31);
-        u[k] = (s2 < ns && rk >= 0) ? __ldcs(reinterpret_cast<const uint2*>(po + static_cast<int64_t>(rk) * kD))
-                                    : make_uint2(0u, 0u);
-      }
+    for (int e = 0; e < 4; ++e) {
+      acc[2 * e] = lb == -INFINITY ? 0.f : bf16_lo(wv[e]);
+      acc[2 * e + 1] = lb == -INFINITY ? 0.f : bf16_hi(wv[e]);
+    }
+  }
+  bool any = false;
+  for (int g0 = 0; g0 < ns; g0 += 8) {
+    int32_t rk[8];
+    float lk[8];
+    uint4 uk[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) rk[k] = g0 + k < ns ? __ldg(pr + g0 + k) : -1;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t row = static_cast<int64_t>(rk[k]) * hpi + hl;
+      lk[k] = rk[k] >= 0 ? __ldcs(a.part_lse + row) : -INFINITY;
+      uk[k] = rk[k] >= 0 ? __ldcs(reinterpret_cast<const uint4*>(a.part_o + row * kD) + f8) : make_uint4(0, 0, 0, 0);
+    }
+    float gm = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) gm = fmaxf(gm, lk[k]);
+    if (gm == -INFINITY) continue;
+    any = true;
+    if (gm > M) {  // rescale what is accumulated so far
+      const float c = M == -INFINITY ? 0.f : exp2f(M - gm);
+      den *= c;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] *= c;
+      M = gm;
     }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int s2 = g0 + k;
-      const float l2 = __shfl_sync(0xffffffffu, s2 < 32 ? v0 : v1, s2 & 31);
-      const float w = (s2 < ns && l2 != -INFINITY) ? exp2f(l2 - M) : 0.f;
-      if (w != 0.f) {
-        acc[0] = fmaf(w, bf16_lo(u[k].x), acc[0]);
-        acc[1] = fmaf(w, bf16_hi(u[k].x), acc[1]);
-        acc[2] = fmaf(w, bf16_lo(u[k].y), acc[2]);
-        acc[3] = fmaf(w, bf16_hi(u[k].y), acc[3]);
+      if (lk[k] == -INFINITY) continue;
+      const float w = exp2f(lk[k] - M);
+      den += w;
+      const uint32_t wv[4] = {uk[k].x, uk[k].y, uk[k].z, uk[k].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] = fmaf(w, bf16_lo(wv[e]), acc[2 * e]);
+        acc[2 * e + 1] = fmaf(w, bf16_hi(wv[e]), acc[2 * e + 1]);
       }
     }
   }
+  if (!any) return;  // no remote partial: the window result stands
   const float inv = den > 0.f ? 1.f / den : 0.f;
-  __nv_bfloat162 q0 = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
-  __nv_bfloat162 q1 = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
-  uint2 w2;
-  w2.x = *reinterpret_cast<uint32_t*>(&q0);
-  w2.y = *reinterpret_cast<uint32_t*>(&q1);
-  *reinterpret_cast<uint2*>(op) = w2;
-  if (lane == 0) *lse_p = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __nv_bfloat162 hv = __floats2bfloat162_rn(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+    w[e] = *reinterpret_cast<uint32_t*>(&hv);
+  }
+  *op = make_uint4(w[0], w[1], w[2], w[3]);
+  if (f8 == 0) *lse_p = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
 }
 
 __global__ void __launch_bounds__(kWsThreads, 1)
@@ -1140,11 +1145,11 @@ __global__ void __launch_bounds__(kRwThreads, 1)
       fence_async_smem();
       mbar_arrive(&stg_full[qi]);
       const int64_t row0 = cs.row0();
-      if (r < cs.rows()) a.part_lse[cs.hl * a.prow_cap + row0 + r] = l > 0.f ? mx + log2f(l) : -INFINITY;
+      if (r < cs.rows()) a.part_lse[(row0 + r) * hpi + cs.hl] = l > 0.f ? mx + log2f(l) : -INFINITY;
       if (elected) {
         if (ws_wait(&stg_full[qi], qph, abort_p, 432)) {
-          tma_store_3d(&tmp, tile, 0, static_cast<int>(row0), cs.hl);
-          tma_store_3d(&tmp, tile + kQBytes / 2, 64, static_cast<int>(row0), cs.hl);
+          tma_store_3d(&tmp, tile, 0, cs.hl, static_cast<int>(row0));
+          tma_store_3d(&tmp, tile + kQBytes / 2, 64, cs.hl, static_cast<int>(row0));
           bulk_commit();
           bulk_wait_read<0>();
         }
@@ -2434,14 +2439,14 @@ static bool make_tmap(CUtensorMap* m, const void* base, int64_t B, int64_t T, in
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Tensor map of the partial rows [hpi, cap, 128] bf16: box of 64 features x
-// 128 rows of one head, 128-byte swizzle (the stores of the remote pass).
+// Tensor map of the partial rows [cap, hpi, 128] bf16: box of 64 features x
+// one head x 128 rows, 128-byte swizzle (the stores of the remote pass).
 static bool make_tmap_rows(CUtensorMap* m, void* base, int64_t cap, int64_t hpi) {
   EncodeTiledFn enc = tmap_encoder();
   if (!enc) return false;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(cap), static_cast<cuuint64_t>(hpi)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(cap) * kD * 2};
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kTileM), 1};
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(hpi), static_cast<cuuint64_t>(cap)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(hpi) * kD * 2};
+  cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kTileM)};
   cuuint32_t es[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -2528,8 +2533,9 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   fwd_ws_kernel<<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv);
   if (a.part_o) {
     SRSWA_CUDA_TRY(cudaGetLastError());
-    const int64_t rows = g->B * g->T * g->HQ;
-    merge_partials_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+    const int64_t hpc = g->HQ < kMgHeads ? g->HQ : kMgHeads;
+    const dim3 grid(static_cast<unsigned>(g->B * g->T), static_cast<unsigned>((g->HQ + kMgHeads - 1) / kMgHeads));
+    merge_partials_kernel<<<grid, static_cast<unsigned>(hpc * 16), 0, st>>>(a);
   }
   return srswa_last_launch_status();
 }
