@@ -144,23 +144,41 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t p_s, uint32_t
 // ============================================================================
 // remote pass: inverted selection lists
 // ============================================================================
-// count[b*HI+hi][blk] += 1 for every usable (t, slot) selection
-__global__ void pairs_count_kernel(const TcArgs a, int32_t* count) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, hi, t)
-  if (i >= a.B * a.HI * a.T) return;
-  const int64_t t = i % a.T, bh = i / a.T, b = bh / a.HI;
-  const int32_t* srow = a.sel + i * a.S;
-  for (int64_t s = 0; s < a.S; ++s) {
-    const int64_t blk = srow[s];
-    if (blk < 0 || blk >= a.nblk) continue;
-    int64_t lo, hi;
-    remote_range(a, b, t, blk, lo, hi);
-    if (lo >= hi) continue;
-    bool dup = false;
-    for (int64_t u = 0; u < s; ++u) dup |= srow[u] == blk;
-    if (dup) continue;
-    atomicAdd(count + bh * a.nblk + blk, 1);
+// Usable selection (t, slot) of row srow: a valid block with remote keys for
+// the query and not a repeat of an earlier slot (else -1).
+__device__ __forceinline__ int64_t usable_block(const TcArgs& a, const int32_t* srow, int64_t b, int64_t t,
+                                                int64_t s) {
+  const int64_t blk = srow[s];
+  if (blk < 0 || blk >= a.nblk) return -1;
+  int64_t lo, hi;
+  remote_range(a, b, t, blk, lo, hi);
+  if (lo >= hi) return -1;
+  for (int64_t u = 0; u < s; ++u)
+    if (srow[u] == blk) return -1;
+  return blk;
+}
+
+// count[b*HI+hi][blk] += 1 for every usable (t, slot) selection.  A CTA
+// takes 256 queries of one (b, hi) (thread = query) and counts into a
+// shared-memory histogram over the blocks first, so the global counters see
+// one atomic per nonzero bin and CTA.
+constexpr int kListRows = 256;
+__global__ void __launch_bounds__(kListRows) pairs_count_kernel(const TcArgs a, int32_t* count) {
+  extern __shared__ int32_t hist[];  // [nblk]
+  const int64_t bh = blockIdx.y, b = bh / a.HI;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kListRows + threadIdx.x;
+  for (int64_t i = threadIdx.x; i < a.nblk; i += kListRows) hist[i] = 0;
+  __syncthreads();
+  if (t < a.T) {
+    const int32_t* srow = a.sel + (bh * a.T + t) * a.S;
+    for (int64_t s = 0; s < a.S; ++s) {
+      const int64_t blk = usable_block(a, srow, b, t, s);
+      if (blk >= 0) atomicAdd(&hist[blk], 1);
+    }
   }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < a.nblk; i += kListRows)
+    if (hist[i]) atomicAdd(count + bh * a.nblk + i, hist[i]);
 }
 
 // single-CTA exclusive scans: pair offsets and tile offsets per (b*HI+hi, blk);
@@ -248,26 +266,38 @@ __global__ void fwd_lists_scan_kernel(const TcArgs a, const int32_t* count, int3
 // Forward lists: each usable (t, slot) selection takes the next partial row
 // of its list and records the row's query, q offset and bias; prow maps
 // every selection to its row (-1: unused, repeated or without remote keys).
-__global__ void pairs_fill_kernel(const TcArgs a, int32_t* cursor) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, hi, t)
-  if (i >= a.B * a.HI * a.T) return;
-  const int64_t t = i % a.T, bh = i / a.T, b = bh / a.HI;
-  const int32_t* srow = a.sel + i * a.S;
-  int32_t* prow = a.prow + i * a.S;
+// A CTA takes 256 queries of one (b, hi): it counts its selections per block
+// in shared memory, reserves each block's rows with one global atomic, then
+// hands out the rows from shared-memory counters.
+__global__ void __launch_bounds__(kListRows) pairs_fill_kernel(const TcArgs a, int32_t* cursor) {
+  extern __shared__ int32_t hist[];  // [2 * nblk]: counts, then reserved bases
+  int32_t* base = hist + a.nblk;
+  const int64_t bh = blockIdx.y, b = bh / a.HI;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kListRows + threadIdx.x;
+  for (int64_t i = threadIdx.x; i < a.nblk; i += kListRows) hist[i] = 0;
+  __syncthreads();
+  const int32_t* srow = a.sel + (bh * a.T + t) * a.S;
+  if (t < a.T)
+    for (int64_t s = 0; s < a.S; ++s) {
+      const int64_t blk = usable_block(a, srow, b, t, s);
+      if (blk >= 0) atomicAdd(&hist[blk], 1);
+    }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < a.nblk; i += kListRows) {
+    base[i] = hist[i] ? atomicAdd(cursor + bh * a.nblk + i, hist[i]) : 0;
+    hist[i] = 0;
+  }
+  __syncthreads();
+  if (t >= a.T) return;
+  int32_t* prow = a.prow + (bh * a.T + t) * a.S;
   for (int64_t s = 0; s < a.S; ++s) {
+    const int64_t blk = usable_block(a, srow, b, t, s);
     int32_t row = -1;
-    const int64_t blk = srow[s];
-    if (blk >= 0 && blk < a.nblk) {
-      int64_t lo, hi;
-      remote_range(a, b, t, blk, lo, hi);
-      bool dup = false;
-      for (int64_t u = 0; u < s; ++u) dup |= srow[u] == blk;
-      if (lo < hi && !dup) {
-        row = atomicAdd(cursor + bh * a.nblk + blk, 1);
-        a.pair_t[row] = static_cast<int32_t>(t);
-        a.pair_q[row] = b * a.sqb + t * a.sqt;
-        a.pair_bias[row] = a.bias ? a.bias[(b * a.T + t) * a.S + s] * kLog2e : 0.f;
-      }
+    if (blk >= 0) {
+      row = base[blk] + atomicAdd(&hist[blk], 1);
+      a.pair_t[row] = static_cast<int32_t>(t);
+      a.pair_q[row] = b * a.sqb + t * a.sqt;
+      a.pair_bias[row] = a.bias ? a.bias[(b * a.T + t) * a.S + s] * kLog2e : 0.f;
     }
     prow[s] = row;
   }
@@ -1949,59 +1979,93 @@ __global__ void __launch_bounds__(kBqThreads, 1)
 // slots, as in the pair lists); one warp per (b, t, h), lane = 4 features.
 // Slot validity is recomputed from the selection row with warp shuffles; all
 // partial loads of the row are issued together.
-__global__ void __launch_bounds__(256) dq_merge_kernel(const TcBwdArgs a) {
+// Adds the remote dQ partials ([B, T, S, HQ, D] bf16) to the band dQ.  One
+// CTA per (b, t) and up to 16 heads (blockIdx.y), thread = (head, 8
+// features); each warp first finds the usable slots of its two heads' index
+// heads (lane = slot: a valid block with remote keys for the query and not a
+// repeat of an earlier slot).  A slot's partials of all heads are contiguous,
+// so every load is a coalesced 16-byte word.  Memory-bound.
+constexpr int kDqHeads = 16;
+__global__ void __launch_bounds__(kDqHeads * 16) dq_merge_kernel(const TcBwdArgs a) {
   const TcArgs& f = a.f;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= f.B * f.T * f.HQ) return;
-  const int64_t h = row % f.HQ, bt = row / f.HQ, t = bt % f.T, b = bt / f.T;
-  const int64_t hi = h / (f.HQ / f.HI);
-  const int32_t* srow = f.sel + ((b * f.HI + hi) * f.T + t) * f.S;
+  const int lane = threadIdx.x & 31, f8 = threadIdx.x & 15;
+  const int64_t bt = blockIdx.x, t = bt % f.T, b = bt / f.T;
+  const int64_t h = static_cast<int64_t>(blockIdx.y) * kDqHeads + (threadIdx.x >> 4);
+  const int64_t hpi = f.HQ / f.HI;
   const int ns = static_cast<int>(f.S < 64 ? f.S : 64);
-  int32_t blk0 = lane < ns ? srow[lane] : -1, blk1 = lane + 32 < ns ? srow[lane + 32] : -1;
-  auto usable = [&](int32_t blk) {
-    if (blk < 0 || blk >= f.nblk) return false;
-    int64_t lo, hi2;
-    remote_range(f, b, t, blk, lo, hi2);
-    return lo < hi2;
+  // usable-slot masks of one index head (warp-collective)
+  auto slot_masks = [&](int64_t hi, uint32_t& m0, uint32_t& m1) {
+    const int32_t* srow = f.sel + ((b * f.HI + hi) * f.T + t) * f.S;
+    const int32_t blk0 = lane < ns ? srow[lane] : -1, blk1 = lane + 32 < ns ? srow[lane + 32] : -1;
+    auto usable = [&](int32_t blk) {
+      if (blk < 0 || blk >= f.nblk) return false;
+      int64_t lo, hi2;
+      remote_range(f, b, t, blk, lo, hi2);
+      return lo < hi2;
+    };
+    bool ok0 = usable(blk0), ok1 = usable(blk1);
+    for (int u = 0; u < 32; ++u) {  // drop repeats of an earlier slot
+      const int32_t o0 = __shfl_sync(0xffffffffu, blk0, u);
+      if (u < lane && o0 == blk0) ok0 = false;
+      if (o0 == blk1) ok1 = false;
+      const int32_t o1 = __shfl_sync(0xffffffffu, blk1, u);
+      if (u < lane && o1 == blk1) ok1 = false;
+    }
+    m0 = __ballot_sync(0xffffffffu, ok0);
+    m1 = __ballot_sync(0xffffffffu, ok1);
   };
-  bool ok0 = usable(blk0), ok1 = usable(blk1);
-  for (int u = 0; u < 32; ++u) {  // drop repeats of an earlier slot
-    const int32_t o0 = __shfl_sync(0xffffffffu, blk0, u);
-    if (u < lane && o0 == blk0) ok0 = false;
-    if (o0 == blk1) ok1 = false;
-    const int32_t o1 = __shfl_sync(0xffffffffu, blk1, u);
-    if (u < lane && o1 == blk1) ok1 = false;
+  // the warp's two heads (a head past HQ borrows the last one's index head)
+  const int64_t h_lo = static_cast<int64_t>(blockIdx.y) * kDqHeads + ((threadIdx.x & ~31u) >> 4);
+  const int64_t hi_lo = (h_lo < f.HQ ? h_lo : f.HQ - 1) / hpi;
+  const int64_t hi_hi = (h_lo + 1 < f.HQ ? h_lo + 1 : f.HQ - 1) / hpi;
+  uint32_t m0, m1;
+  slot_masks(hi_lo, m0, m1);
+  if (hi_hi != hi_lo) {
+    uint32_t n0, n1;
+    slot_masks(hi_hi, n0, n1);
+    if (lane >= 16) {
+      m0 = n0;
+      m1 = n1;
+    }
   }
-  const uint32_t m0 = __ballot_sync(0xffffffffu, ok0), m1 = __ballot_sync(0xffffffffu, ok1);
-  if ((m0 | m1) == 0) return;
-  __nv_bfloat16* dqp = a.dq + b * f.sqb + t * f.sqt + h * f.sqh + lane * 4;
-  const uint2 d0 = *reinterpret_cast<const uint2*>(dqp);
-  float acc[4] = {bf16_lo(d0.x), bf16_hi(d0.x), bf16_lo(d0.y), bf16_hi(d0.y)};
-  const int64_t slot_base = (bt * f.S) * f.HQ + h;
+  if (h >= f.HQ || (m0 | m1) == 0) return;
+  uint4* dqp = reinterpret_cast<uint4*>(a.dq + b * f.sqb + t * f.sqt + h * f.sqh) + f8;
+  const uint4 d0 = *dqp;
+  float acc[8];
+  {
+    const uint32_t wv[4] = {d0.x, d0.y, d0.z, d0.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[2 * e] = bf16_lo(wv[e]);
+      acc[2 * e + 1] = bf16_hi(wv[e]);
+    }
+  }
+  const uint4* part = reinterpret_cast<const uint4*>(a.dq_part + (bt * f.S * f.HQ + h) * kD) + f8;
   for (int g0 = 0; g0 < ns; g0 += 8) {
-    uint2 u8[8];
+    uint4 u8[8];
 #pragma unroll
     for (int k8 = 0; k8 < 8; ++k8) {
       const int s2 = g0 + k8;
       const bool use = s2 < ns && (((s2 < 32 ? m0 : m1) >> (s2 & 31)) & 1u);
-      u8[k8] = use ? __ldcs(reinterpret_cast<const uint2*>(a.dq_part + (slot_base + s2 * f.HQ) * kD + lane * 4))
-                   : make_uint2(0u, 0u);
+      u8[k8] = use ? __ldcs(part + static_cast<int64_t>(s2) * f.HQ * (kD / 8)) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int k8 = 0; k8 < 8; ++k8) {
-      acc[0] += bf16_lo(u8[k8].x);
-      acc[1] += bf16_hi(u8[k8].x);
-      acc[2] += bf16_lo(u8[k8].y);
-      acc[3] += bf16_hi(u8[k8].y);
+      const uint32_t wv[4] = {u8[k8].x, u8[k8].y, u8[k8].z, u8[k8].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] += bf16_lo(wv[e]);
+        acc[2 * e + 1] += bf16_hi(wv[e]);
+      }
     }
   }
-  __nv_bfloat162 r0 = __floats2bfloat162_rn(acc[0], acc[1]);
-  __nv_bfloat162 r1 = __floats2bfloat162_rn(acc[2], acc[3]);
-  uint2 w2;
-  w2.x = *reinterpret_cast<uint32_t*>(&r0);
-  w2.y = *reinterpret_cast<uint32_t*>(&r1);
-  *reinterpret_cast<uint2*>(dqp) = w2;
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __nv_bfloat162 hv = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+    w[e] = *reinterpret_cast<uint32_t*>(&hv);
+  }
+  *dqp = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // ---- band dK / dV, warp-specialised: one work item = (b, kv head, 128-key
@@ -2453,8 +2517,13 @@ static bool make_tmap_rows(CUtensorMap* m, void* base, int64_t cap, int64_t hpi)
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The list kernels keep two counters per key block in shared memory (up to
+// 227 KB), and their grid has one row per (b, index head).
+constexpr int64_t kMaxListBlocks = 227 * 1024 / 8;
+
 bool tc_eligible(const srswa_gather_desc* g) {
   return g->D == kD && g->block_size == kBlk && g->dtype == SRSWA_BF16 && g->S <= 64 && g->T > 0 && g->scale > 0.f &&
+         (g->T + kBlk - 1) / kBlk <= kMaxListBlocks && g->B * g->HI <= 65535 &&
          ((g->sqb | g->sqt | g->sqh | g->skb | g->skt | g->skh | g->svb | g->svt | g->svh) & 7) == 0;
 }
 
@@ -2515,13 +2584,19 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   if (g->S > 0) {
     const int64_t nbh = a.B * a.HI * a.nblk;
     SRSWA_CUDA_TRY(cudaMemsetAsync(count, 0, static_cast<size_t>(nbh) * 4, st));
-    const int64_t rows = a.B * a.HI * a.T;
-    pairs_count_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, count);
+    const dim3 lgrid(static_cast<unsigned>((a.T + kListRows - 1) / kListRows), static_cast<unsigned>(nbh / a.nblk));
+    if (a.nblk * 8 > 48 * 1024) {  // above the default dynamic shared-memory limit
+      SRSWA_CUDA_TRY(cudaFuncSetAttribute(pairs_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(a.nblk * 4)));
+      SRSWA_CUDA_TRY(cudaFuncSetAttribute(pairs_fill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(a.nblk * 8)));
+    }
+    pairs_count_kernel<<<lgrid, kListRows, static_cast<size_t>(a.nblk) * 4, st>>>(a, count);
     SRSWA_CUDA_TRY(cudaGetLastError());
     fwd_lists_scan_kernel<<<1, 1024, 0, st>>>(a, count, cursor, const_cast<int4*>(a.work),
                                               const_cast<int32_t*>(a.totals));
     SRSWA_CUDA_TRY(cudaGetLastError());
-    pairs_fill_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(a, cursor);
+    pairs_fill_kernel<<<lgrid, kListRows, static_cast<size_t>(a.nblk) * 8, st>>>(a, cursor);
     SRSWA_CUDA_TRY(cudaGetLastError());
     remote_ws_kernel<<<num_sms, kRwThreads, kRwSmem, st>>>(a, tmk, tmv, tmp);
     SRSWA_CUDA_TRY(cudaGetLastError());
@@ -2683,8 +2758,9 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     bwd_band_dq_ws_kernel<<<grid_q, kBqThreads, kBqSmem, st>>>(a, tmq, tmdo, tmk, tmv);
     SRSWA_CUDA_TRY(cudaGetLastError());
     if (remote) {
-      const int64_t rows = g->B * g->T * g->HQ;
-      dq_merge_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+      const int64_t hpc = g->HQ < kDqHeads ? g->HQ : kDqHeads;
+      const dim3 grid(static_cast<unsigned>(g->B * g->T), static_cast<unsigned>((g->HQ + kDqHeads - 1) / kDqHeads));
+      dq_merge_kernel<<<grid, static_cast<unsigned>((hpc * 16 + 31) / 32 * 32), 0, st>>>(a);
       SRSWA_CUDA_TRY(cudaGetLastError());
     }
   }
