@@ -558,6 +558,81 @@ __device__ __forceinline__ unsigned long long warp_topm_regs(unsigned long long 
   return mine;
 }
 
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v), m);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), m);
+  return (static_cast<unsigned long long>(hi) << 32) | lo;
+}
+__device__ __forceinline__ unsigned long long max_u64(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
+__device__ __forceinline__ unsigned long long min_u64(unsigned long long a, unsigned long long b) { return a > b ? b : a; }
+
+// Top-M (M <= 32) of unique keys held in registers, NPL per lane, by one warp,
+// with the same result as warp_topm_regs.  The M-th largest of the 32 lane
+// maxima (bitonic sort across the lanes) is a lower bound of the M-th largest
+// key, since at least M keys reach it; the keys at or above it (normally a
+// few more than M) go to the warp's 64-entry scratch and one 64-key bitonic
+// sort (two keys per lane) orders them.  More than 64 such keys: the
+// round-based warp_topm_regs.
+template <int NPL>
+__device__ __forceinline__ unsigned long long warp_topm_filtered(unsigned long long (&v)[NPL], int M, int lane,
+                                                               unsigned long long* scratch) {
+  unsigned long long lm = 0ull;
+#pragma unroll
+  for (int k = 0; k < NPL; ++k) lm = max_u64(lm, v[k]);
+  // lane i <- the i-th largest lane maximum (descending bitonic sort of 32)
+  unsigned long long srt = lm;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const unsigned long long p = shfl_xor_u64(srt, j);
+      const bool take_max = ((lane & j) == 0) == ((lane & k) == 0);
+      srt = take_max ? max_u64(srt, p) : min_u64(srt, p);
+    }
+  }
+  const uint32_t t_lo = __shfl_sync(0xffffffffu, static_cast<uint32_t>(srt), M - 1);
+  const uint32_t t_hi = __shfl_sync(0xffffffffu, static_cast<uint32_t>(srt >> 32), M - 1);
+  const unsigned long long t0 = (static_cast<unsigned long long>(t_hi) << 32) | t_lo;
+  // survivors: nonzero keys >= t0; exclusive prefix of the lanes' counts
+  int cnt = 0;
+#pragma unroll
+  for (int k = 0; k < NPL; ++k) cnt += (v[k] != 0ull && v[k] >= t0) ? 1 : 0;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  if (total > 64) return warp_topm_regs<NPL>(v, M, lane);  // warp-uniform
+  int pos = incl - cnt;
+#pragma unroll
+  for (int k = 0; k < NPL; ++k)
+    if (v[k] != 0ull && v[k] >= t0) scratch[pos++] = v[k];
+  for (int i = total + lane; i < 64; i += 32) scratch[i] = 0ull;
+  __syncwarp();
+  unsigned long long e0 = scratch[lane], e1 = scratch[lane + 32];  // element i = 32 * slot + lane
+  __syncwarp();
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 32) {  // partners in one lane (only in the final merge: descending)
+        const unsigned long long a = e0, b = e1;
+        e0 = max_u64(a, b);
+        e1 = min_u64(a, b);
+      } else {
+        const unsigned long long p0 = shfl_xor_u64(e0, j), p1 = shfl_xor_u64(e1, j);
+        const bool first = (lane & j) == 0;
+        const bool d0 = (lane & k) == 0, d1 = ((32 + lane) & k) == 0;  // descending blocks
+        e0 = (first == d0) ? max_u64(e0, p0) : min_u64(e0, p0);
+        e1 = (first == d1) ? max_u64(e1, p1) : min_u64(e1, p1);
+      }
+    }
+  }
+  return lane < M ? e0 : 0ull;
+}
+
 // Top-M of the 8 per-warp lists (M keys each, kMaxTopM apart) by warp 0;
 // lane m returns the m-th key.
 __device__ unsigned long long merge8_topm(unsigned long long* flat, int M, int lane) {
@@ -604,6 +679,7 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
                                                                     int64_t s_z) {
   extern __shared__ __align__(16) unsigned long long wk[];  // [nblk] keys
   __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
+  __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
   const int64_t n = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t nblk = a.nblk;
@@ -637,7 +713,7 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
       const int64_t i = lane + 32 * k;
       v[k] = i < wn ? wk[wlo + i] : 0ull;
     }
-    const unsigned long long top = warp_topm_regs<16>(v, M, lane);
+    const unsigned long long top = warp_topm_filtered<16>(v, M, lane, topm_scratch[warp]);
     if (lane < M) lists[warp][lane] = top;
   } else {
     warp_topm_smem(wk + wlo, static_cast<int>(wn), M, lists[warp], lane);
@@ -955,13 +1031,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
   const int64_t nblk = a.nblk;
   float* qs = rt_smem;                       // [32][132]
   float* kb = qs + kRtRows * kRtLd;          // [64][132]
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(rt_smem);  // [8][nblk], after the scores
   const size_t ab = static_cast<size_t>(kRtRows + kRtChunk) * kRtLd;
-  const size_t kw = static_cast<size_t>(8) * nblk * 2;                        // keys in floats
+  const size_t kw = static_cast<size_t>(8) * nblk * 2;
   float* zs = rt_smem + (ab > kw ? ab : kw);  // [32][nblk]
   __shared__ int64_t chi[kRtRows];
   __shared__ int64_t cmax_s;
-  __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
+  __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kRtRows;
   const int64_t seq = n0 / a.rows_per_seq;  // all 32 rows share it (rows_per_seq % 32 == 0)
@@ -1065,7 +1140,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
   }
   __syncthreads();
   // ---- selection: warp w, rows 4w .. 4w+3; lane holds blocks lane + 32 i ----
-  (void)keys;
   const int M = static_cast<int>(a.M);
   for (int rr = 0; rr < 4; ++rr) {
     const int r = r0 + rr;
@@ -1093,7 +1167,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
         v[k] = pack_key(x, c, cm);
       }
     }
-    const unsigned long long mine = warp_topm_regs<kRtMaxBlocks / 32>(v, M, lane);
+    const unsigned long long mine = warp_topm_filtered<kRtMaxBlocks / 32>(v, M, lane, topm_scratch[warp]);
     float sel_v = 0.f;
     int sel_i = -1;
     bool sel_c = false;
