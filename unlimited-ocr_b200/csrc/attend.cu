@@ -29,6 +29,7 @@
 //     keys); online softmax in the log2 domain; P.V accumulates 8 features per
 //     lane in fp32.
 
+#include <cmath>
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -321,6 +322,51 @@ static int launch_attend(const AttendArgs& a, cudaStream_t st) {
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
 
+// Split count of the (row, head) items when the caller leaves it open: the
+// items run in waves of (SMs x resident CTAs), each split adds a cluster
+// merge.  Modelled time = waves x (keys per CTA + merge cost), keys per item
+// = window + selected blocks.  A CTA streams at a fixed rate whatever the
+// load (a wave that is nearly empty still costs a full CTA time), and a
+// cluster merge costs about as much as streaming 175 keys: fitted to the cfg3
+// decode at 16 to 256 requests per GPU with fixed split counts (best: 2 at
+// 160 items, 1 from 320 items up).  Smallest modelled time wins, by at least
+// 3 % over a smaller split.
+static int auto_nsplit(const AttendArgs& a, int64_t D, int kv_dtype) {
+  static int sms[64] = {0}, per_sm[64][2][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (sms[dev] == 0) {
+    int v = 0;
+    sms[dev] = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0 ? v : 148;
+  }
+  const int di = D == 128 ? 1 : 0, ki = kv_dtype == SRSWA_BF16 ? 1 : 0;
+  if (per_sm[dev][di][ki] == 0) {
+    int nb = 0;
+    cudaError_t e = cudaErrorInvalidValue;
+    if (D == 128)
+      e = ki ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<128, SRSWA_BF16>, kAttendThreads, 0)
+             : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<128, SRSWA_F16>, kAttendThreads, 0);
+    else
+      e = ki ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<64, SRSWA_BF16>, kAttendThreads, 0)
+             : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<64, SRSWA_F16>, kAttendThreads, 0);
+    per_sm[dev][di][ki] = e == cudaSuccess && nb > 0 ? nb : 4;
+  }
+  const double slots = static_cast<double>(sms[dev]) * per_sm[dev][di][ki];
+  const double items = static_cast<double>(a.N) * a.H;
+  const double keys = static_cast<double>(a.LW) + static_cast<double>(a.K) * a.BS;
+  int best = 1;
+  double best_t = 0.0;
+  for (int n = 1; n <= 8; n *= 2) {
+    const double waves = std::ceil(items * n / slots);
+    const double t = waves * (keys / n + (n > 1 ? 175.0 : 0.0));
+    if (n == 1 || t < best_t * 0.97) {
+      best = n;
+      best_t = t;
+    }
+  }
+  return best;
+}
+
 int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   if (a.N == 0) return 0;
   if (!(D == 64 || D == 128)) return SRSWA_EUNSUPPORTED;
@@ -330,12 +376,7 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   if (a.K + a.LW / a.BS + 2 > kAttendMaxSlots) return SRSWA_ETOOLARGE;
   if (a.H >= 65536) return SRSWA_ETOOLARGE;
   int nsplit = a.nsplit;
-  if (nsplit <= 0) {
-    // enough CTAs for ~4 per SM on 148 SMs; at most 8 (portable cluster size)
-    const int64_t want = (148 * 4 + a.N * a.H - 1) / (a.N * a.H);
-    nsplit = 1;
-    while (nsplit * 2 <= want && nsplit < 8) nsplit *= 2;
-  }
+  if (nsplit <= 0) nsplit = auto_nsplit(a, D, kv_dtype);
   if (nsplit < 1 || nsplit > 8) return SRSWA_EUNSUPPORTED;
   if (a.N * nsplit >= (1ll << 31)) return SRSWA_ETOOLARGE;
   a.nsplit = nsplit;
