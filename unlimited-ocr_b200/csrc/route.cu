@@ -635,14 +635,15 @@ __device__ __forceinline__ unsigned long long warp_topm_filtered(unsigned long l
 
 // Top-M of the 8 per-warp lists (M keys each, kMaxTopM apart) by warp 0;
 // lane m returns the m-th key.
-__device__ unsigned long long merge8_topm(unsigned long long* flat, int M, int lane) {
+__device__ unsigned long long merge8_topm(unsigned long long* flat, int M, int lane,
+                                          unsigned long long* scratch = nullptr) {
   unsigned long long v[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int i = lane + 32 * k;  // 256 entries: list i / 32, position i % 32
     v[k] = (i % kMaxTopM) < M ? flat[i] : 0ull;
   }
-  return warp_topm_regs<8>(v, M, lane);
+  return scratch ? warp_topm_filtered<8>(v, M, lane, scratch) : warp_topm_regs<8>(v, M, lane);
 }
 __device__ __forceinline__ void unpack_key(unsigned long long k, float& x, int& blk, bool& cand) {
   x = from_ordered(static_cast<uint32_t>(k >> 32));
@@ -685,21 +686,45 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
   const int64_t nblk = a.nblk;
   const int M = static_cast<int>(a.M);
   const float* z = zin + n * s_z;
+  // the row's scores (and candidate flags), eight per thread in flight at once
+  constexpr int kBatch = 8 * kRouteThreads;
   int any = 1;
   if (a.cand) {
     int f = 0;
-    for (int64_t c = tid; c < nblk; c += kRouteThreads)
-      f |= (z[c] > kScoreNeg * 0.5f) && a.cand[n * a.s_cand + c] != 0;
+    for (int64_t c0 = 0; c0 < nblk; c0 += kBatch) {
+      float zc[8];
+      uint8_t cf[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int64_t c = c0 + tid + k * kRouteThreads;
+        zc[k] = c < nblk ? z[c] : kScoreNeg;
+        cf[k] = c < nblk ? a.cand[n * a.s_cand + c] : 0;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f |= (zc[k] > kScoreNeg * 0.5f) && cf[k] != 0;
+    }
     any = __syncthreads_or(f);
   }
-  for (int64_t c = tid; c < nblk; c += kRouteThreads) {
-    const float zc = z[c];
-    if (a.scores_out) a.scores_out[n * nblk + c] = zc;
-    const bool remote = zc > kScoreNeg * 0.5f;
-    const bool cm = remote && (a.cand == nullptr || !any || a.cand[n * a.s_cand + c] != 0);
-    float x = cm ? zc * a.idx_scale : kEntmaxNeg;
-    if (!isfinite(x)) x = kEntmaxNeg;
-    wk[c] = pack_key(x, c, cm);
+  for (int64_t c0 = 0; c0 < nblk; c0 += kBatch) {
+    float zc[8];
+    uint8_t cf[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t c = c0 + tid + k * kRouteThreads;
+      zc[k] = c < nblk ? z[c] : kScoreNeg;
+      cf[k] = (a.cand && c < nblk) ? a.cand[n * a.s_cand + c] : 1;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t c = c0 + tid + k * kRouteThreads;
+      if (c >= nblk) break;
+      if (a.scores_out) a.scores_out[n * nblk + c] = zc[k];
+      const bool remote = zc[k] > kScoreNeg * 0.5f;
+      const bool cm = remote && (a.cand == nullptr || !any || cf[k] != 0);
+      float x = cm ? zc[k] * a.idx_scale : kEntmaxNeg;
+      if (!isfinite(x)) x = kEntmaxNeg;
+      wk[c] = pack_key(x, c, cm);
+    }
   }
   __syncthreads();
   const int64_t per = (nblk + 7) / 8;
@@ -720,7 +745,7 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
   }
   __syncthreads();
   if (warp != 0) return;
-  const unsigned long long mine = merge8_topm(&lists[0][0], M, lane);
+  const unsigned long long mine = merge8_topm(&lists[0][0], M, lane, topm_scratch[0]);
   float sel_v = 0.f;
   int sel_i = -1;
   bool sel_c = false;
