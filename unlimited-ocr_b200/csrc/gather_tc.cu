@@ -482,6 +482,19 @@ __device__ __forceinline__ void band_row_store(const TcArgs& a, int64_t b, int64
   if (row_ok && a.lse) a.lse[(b * a.T + t) * a.HQ + h] = l > 0.f ? (m_ref + log2f(l)) * kLn2 : -INFINITY;
 }
 
+// 16 fp32 * scale -> 16 bf16 stored as one 32-byte word (dst 32-byte aligned)
+__device__ __forceinline__ void st_global_bf16x16(__nv_bfloat16* dst, const float* v, float scale) {
+  uint32_t w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e] * scale, v[2 * e + 1] * scale);
+    w[e] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 // Log-sum-exp merge of the window result (o, lse, as written by the band
 // pass) with the remote partials.  One CTA per (b, t) and up to 16 heads
 // (blockIdx.y), thread = (head, 8 features): a selection's partials of all
@@ -1669,21 +1682,12 @@ __global__ void __launch_bounds__(kRbThreads, 1)
         tmem_ld32(tm_dq + lane_off + 64 * ch, ov0);
         tmem_ld32(tm_dq + lane_off + 64 * ch + 32, ov1);
         tmem_wait_ld();
-        if (row_ok) {
+        if (row_ok) {  // this half row (128 bytes, 32-byte aligned) as four 32-byte stores
           __nv_bfloat16* dst = a.dq_part + prow * kD + 64 * ch;
 #pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) {
-            float tmp[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) tmp[e] = ov0[8 * q8 + e] * a.scale;
-            store8(dst, 8 * q8, SRSWA_BF16, tmp);
-          }
-#pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) {
-            float tmp[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) tmp[e] = ov1[8 * q8 + e] * a.scale;
-            store8(dst + 32, 8 * q8, SRSWA_BF16, tmp);
+          for (int q = 0; q < 2; ++q) {
+            st_global_bf16x16(dst + 16 * q, ov0 + 16 * q, a.scale);
+            st_global_bf16x16(dst + 32 + 16 * q, ov1 + 16 * q, a.scale);
           }
         }
       }
