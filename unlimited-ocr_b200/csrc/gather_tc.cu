@@ -456,6 +456,40 @@ struct WsCursor {
   }
 };
 
+// 16 fp32 * scale -> 16 bf16 stored as one 32-byte word (dst 32-byte aligned)
+__device__ __forceinline__ void st_global_bf16x16(__nv_bfloat16* dst, const float* v, float scale) {
+  uint32_t w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e] * scale, v[2 * e + 1] * scale);
+    w[e] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// 32 fp32 * scale -> 32 bf16 at dst (16-byte aligned): two 32-byte stores
+// where dst is 32-byte aligned, else four 16-byte ones.  A thread writes one
+// row, so each store of a warp touches 32 rows: wide stores halve the count.
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* v, float scale) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+    st_global_bf16x16(dst, v, scale);
+    st_global_bf16x16(dst + 16, v + 16, scale);
+    return;
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * q + 2 * e] * scale, v[8 * q + 2 * e + 1] * scale);
+      w[e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // Band epilogue of one row in the warp-specialised kernel: the window-only
 // result, o = O / l (bf16) and lse (ln); merge_partials_kernel folds the
 // remote partials in afterwards.  Called by whole warps (tcgen05.ld is
@@ -468,31 +502,9 @@ __device__ __forceinline__ void band_row_store(const TcArgs& a, int64_t b, int64
     float ov[32];
     tmem_ld32(tm_o_row + 32 * c, ov);
     tmem_wait_ld();
-    if (row_ok) {
-      __nv_bfloat16* dst = a.o + b * a.sob + t * a.sot + h * a.soh + 32 * c;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float tmp[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * inv;
-        store8(dst, 8 * q4, SRSWA_BF16, tmp);
-      }
-    }
+    if (row_ok) store_row32(a.o + b * a.sob + t * a.sot + h * a.soh + 32 * c, ov, inv);
   }
   if (row_ok && a.lse) a.lse[(b * a.T + t) * a.HQ + h] = l > 0.f ? (m_ref + log2f(l)) * kLn2 : -INFINITY;
-}
-
-// 16 fp32 * scale -> 16 bf16 stored as one 32-byte word (dst 32-byte aligned)
-__device__ __forceinline__ void st_global_bf16x16(__nv_bfloat16* dst, const float* v, float scale) {
-  uint32_t w[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e] * scale, v[2 * e + 1] * scale);
-    w[e] = *reinterpret_cast<uint32_t*>(&h);
-  }
-  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
-               : "memory");
 }
 
 // Log-sum-exp merge of the window result (o, lse, as written by the band
@@ -1947,15 +1959,7 @@ __global__ void __launch_bounds__(kBqThreads, 1)
           float ov[32];
           tmem_ld32(tm_dq + lane_off + 32 * cc, ov);
           tmem_wait_ld();
-          if (row_ok) {
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              float tmp[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) tmp[e] = ov[8 * q4 + e] * a.scale;
-              store8(a.dq + c.w.b * f.sqb + t * f.sqt + c.w.h * f.sqh + 32 * cc, 8 * q4, SRSWA_BF16, tmp);
-            }
-          }
+          if (row_ok) store_row32(a.dq + c.w.b * f.sqb + t * f.sqt + c.w.h * f.sqh + 32 * cc, ov, a.scale);
         }
         tc_fence_before();
         mbar_arrive(&dq_empty);
@@ -2356,13 +2360,8 @@ __global__ void __launch_bounds__(kBkThreads, 1)
           tmem_ld32(tm_dv + lane_off + 32 * cc, vv);
           tmem_wait_ld();
           if (key_ok) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) kv[i] *= a.scale;
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              store8(a.dk + c.b * f.skb + key * f.skt + c.hk * f.skh + 32 * cc, 8 * q4, SRSWA_BF16, kv + 8 * q4);
-              store8(a.dv + c.b * f.svb + key * f.svt + c.hk * f.svh + 32 * cc, 8 * q4, SRSWA_BF16, vv + 8 * q4);
-            }
+            store_row32(a.dk + c.b * f.skb + key * f.skt + c.hk * f.skh + 32 * cc, kv, a.scale);
+            store_row32(a.dv + c.b * f.svb + key * f.svt + c.hk * f.svh + 32 * cc, vv, 1.f);
           }
         }
         tc_fence_before();
