@@ -141,6 +141,28 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t p_s, uint32_t
   }
 }
 
+// O (+)= P V with P (bf16, [128 x 64 keys]) in TMEM: A from TMEM, 8 columns
+// per 16-key step; V MN-major in shared memory as in issue_pv
+__device__ __forceinline__ void issue_pv_tmem(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_s, bool accumulate) {
+  constexpr uint32_t id = idesc_bf16(128, 128, 1);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const uint64_t bd = sw128_desc(v_s + ks * 2048u, kKVHalf, 1024);
+    mma_bf16_ts(tmem_o, tmem_p + ks * 8u, bd, id, (accumulate || ks > 0) ? 1u : 0u);
+  }
+}
+// 64 fp32 -> 32 packed bf16 pairs (lower key in the low half) into a row's
+// 32 TMEM columns (warp-collective)
+__device__ __forceinline__ void store_p_tmem(uint32_t taddr, const float (&p)[64]) {
+  uint32_t w[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(p[2 * i], p[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  tmem_st32u(taddr, w);
+}
+
 // ============================================================================
 // remote pass: inverted selection lists
 // ============================================================================
@@ -325,7 +347,7 @@ constexpr int kWsThreads = 320;
 constexpr int kWsProducer = 8, kWsMma = 9;
 constexpr uint32_t kWsStage = 2 * kKVBytes;                              // K then V
 constexpr uint32_t kWsSmem = 2 * kQBytes + 2 * 2 * kWsStage + 1024;      // 193 KB -> 1 CTA/SM
-constexpr uint32_t kWsTmemCols = 512;                                   // per slot: S 0-63, O 128-255
+constexpr uint32_t kWsTmemCols = 512;  // per slot: S 0-63, P (bf16) 64-95, O 128-255
 
 // Bounded wait of one role: suspended try_waits until the phase completes,
 // the CTA's abort flag is set (another role gave up) or the wall-clock bound
@@ -702,7 +724,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (!ws_wait(&p_full[s], static_cast<uint32_t>(pn[s] & 1), abort_p, 405)) return false;
         const int st = static_cast<int>(pn[s] & 1);
         tc_fence_after();
-        issue_pv(tmem + s * 256 + 128, kv_s(s, st), kv_s(s, st) + kKVBytes, !pfirst[s]);
+        issue_pv_tmem(tmem + s * 256 + 128, tmem + s * 256 + 64, kv_s(s, st) + kKVBytes, !pfirst[s]);
         mma_commit(&kv_empty[s][st]);
         if (plast[s]) mma_commit(&o_full[s]);
         pend[s] = false;
@@ -779,10 +801,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         tmem_wait_st();
       }
       l += block_row_exp(sv, a.scale_log2, m_ref == -INFINITY ? 0.f : -m_ref);
-      const uint32_t p_s = kv_s(s, static_cast<int>(cs.n & 1));  // P over this stage's dead K
-      store_p_row(p_s, r, 0, sv);
-      store_p_row(p_s, r, 4, sv + 32);
-      fence_async_smem();
+      // P (bf16) into the slot's P columns of TMEM: the previous step's O += P V
+      // has read them (S of this step was committed after it)
+      store_p_tmem(tmem + s * 256 + 64 + lane_off, sv);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[s]);
       if (last) {
