@@ -842,8 +842,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 // Roles (thread = row inside the warpgroups):
 //   warps 0-3 / 4-7  row warpgroup 0 / 1, the CTA's even / odd units: S from
 //                    TMEM, masked to the row's remote keys, exp2 with the slot
-//                    bias, P (bf16) over the unit's dead Q tile; then O from
-//                    TMEM scaled by 1/l, bf16, staged over the same tile in the
+//                    bias, P (bf16) into the warpgroup's P columns of TMEM
+//                    (O += P V reads A from TMEM); then O from TMEM scaled by
+//                    1/l, bf16, staged over the unit's dead Q tile in the
 //                    128-byte-swizzled layout and sent to the unit's partial
 //                    rows by two TMA stores (one thread); lse (log2) per row.
 //                    Both warpgroups run the same code (one instruction
@@ -1091,7 +1092,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
       int64_t nq = 0, np = 0, run = -1;  // units with S / O issued; KV run of the last S
       int qi = 0;
       uint32_t qph = 0;
-      // per unit between its S and O (byte n & 1): Q buffer | KV stage << 2 | last of run << 3
+      // per unit between its S and O (byte n & 1): KV stage << 2 | last of run << 3
       uint32_t pv_info = 0;
       uint64_t idle_since = 0;  // start of the current idle stretch (0: busy)
       bool ok = true;
@@ -1108,7 +1109,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
             issue_qk(tmem + sb * 64, q_buf(qi), kv_buf(st));
             mma_commit(&s_full[sb]);
             run = rn;
-            const uint32_t inf = static_cast<uint32_t>(qi) | static_cast<uint32_t>(st) << 2 |
+            const uint32_t inf = static_cast<uint32_t>(st) << 2 |
                                  (cq.last_of_run() ? 8u : 0u);
             pv_info = (pv_info & ~(0xffu << (8 * sb))) | inf << (8 * sb);
             cq.advance(a);
@@ -1125,9 +1126,9 @@ __global__ void __launch_bounds__(kRwThreads, 1)
           if (mbar_ready(&p_full[sb], static_cast<uint32_t>((np >> 1) & 1)) &&
               (np < 2 || mbar_ready(&o_empty[sb], static_cast<uint32_t>(((np >> 1) - 1) & 1)))) {
             const uint32_t inf = (pv_info >> (8 * sb)) & 0xffu;
-            const int pq = static_cast<int>(inf & 3u), pst = static_cast<int>((inf >> 2) & 1u);
+            const int pst = static_cast<int>((inf >> 2) & 1u);
             tc_fence_after();
-            issue_pv(tmem + 128 + sb * 128, q_buf(pq), kv_buf(pst) + kKVBytes, false);  // P over the dead Q tile
+            issue_pv_tmem(tmem + 128 + sb * 128, tmem + 384 + sb * 32, kv_buf(pst) + kKVBytes, false);
             mma_commit(&o_full[sb]);
             if (inf & 8u) mma_commit(&kv_empty[pst]);
             ++np;
@@ -1196,12 +1197,13 @@ __global__ void __launch_bounds__(kRwThreads, 1)
       const float mraw = block_row_max(sv, klo, khi, full);
       const float mx = mraw == -INFINITY ? -INFINITY : fmaf(mraw, a.scale_log2, bias2);
       const float l = block_row_exp(sv, a.scale_log2, bias2 - (mx == -INFINITY ? 0.f : mx));
-      const uint32_t tile = q_buf(qi);  // Q of this unit is dead once S is in TMEM
-      store_p_row(tile, r, 0, sv);
-      store_p_row(tile, r, 4, sv + 32);
-      fence_async_smem();
+      // P (bf16) into this warpgroup's P columns of TMEM (its previous unit's
+      // O += P V has read them: S of this unit was committed after it)
+      store_p_tmem(tmem + 384 + wg * 32 + lane_off, sv);
+      tmem_wait_st();
+      tc_fence_before();
       mbar_arrive(&p_full[wg]);
-      // O of the unit; P in the tile is dead once O is complete
+      const uint32_t tile = q_buf(qi);  // Q of this unit is dead once S is in TMEM: staging for O
       if (!__all_sync(0xffffffffu, ws_wait(&o_full[wg], ph, abort_p, 429))) break;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
