@@ -2104,18 +2104,22 @@ __global__ void __launch_bounds__(kDqHeads * 16) dq_merge_kernel(const TcBwdArgs
 // tile); steps = (query head of the group) x (64-query chunk of the window)
 //   warps 0-3  compute (thread = key row): P^T = 2^(s c - lse_q), dS^T =
 //              P^T (dP^T - delta_q) over the pairs with ls_q <= key <= q,
-//              P^T / dS^T (bf16) to a double-buffered shared tile; after the
+//              P^T / dS^T (bf16 pairs) written back into the first 32
+//              columns of the step's S^T / dP^T buffer in TMEM; after the
 //              item's last step, dK (scaled) and dV from TMEM;
 //   warp 4     producer: TMA of the item's K / V tile and of each chunk's q /
-//              dO rows (2 stages), plus the chunk's per-query lse, delta and
+//              dO rows (4 stages), plus the chunk's per-query lse, delta and
 //              window bounds in shared memory and a whole-chunk-valid flag;
 //   warp 5     MMA issuer: S^T = K Q^T and dP^T = V dO^T into one of two TMEM
-//              buffers (the next step's run while the compute warps work),
-//              dV += P^T dO and dK += dS^T Q accumulated over the item.
+//              buffers (the next step's run while the compute warps work;
+//              a buffer is reused once the MMAs that read its P^T / dS^T are
+//              complete), dV += P^T dO and dK += dS^T Q accumulated over the
+//              item, A read from TMEM.
 // The remote dK / dV partials are added by dkv_merge_kernel.
 constexpr int kBkThreads = 192;
 constexpr uint32_t kQc = 64 * 128 * 2;                                       // 64 rows x 128 bf16
-constexpr uint32_t kBkSmem = 2 * kTile128 + 2 * 2 * kQc + 2 * 2 * kPBytes + 1024;  // 193 KB
+constexpr int kBkStages = 4;                                                 // q / dO chunk ring
+constexpr uint32_t kBkSmem = 2 * kTile128 + kBkStages * 2 * kQc + 1024;      // 193 KB
 
 __global__ void __launch_bounds__(kBkThreads, 1)
     bwd_band_dkdv_ws_kernel(const TcBwdArgs a, const __grid_constant__ CUtensorMap tmq64,
@@ -2123,18 +2127,17 @@ __global__ void __launch_bounds__(kBkThreads, 1)
                             const __grid_constant__ CUtensorMap tmv) {
   const TcArgs& f = a.f;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ uint64_t kv_full, kv_empty, qd_full[2], qd_empty[2], s_full[2], p_full[2], pds_empty[2];
+  __shared__ uint64_t kv_full, kv_empty, qd_full[kBkStages], qd_empty[kBkStages], s_full[2], p_full[2], pds_empty[2];
   __shared__ uint64_t dkv_full, dkv_empty, drain_bar;
-  __shared__ __align__(16) int32_t v_lo[2][64], v_hi[2][64];
-  __shared__ __align__(16) float v_lse[2][64], v_dl[2][64];
-  __shared__ int v_full[2];
+  __shared__ __align__(16) int32_t v_lo[kBkStages][64], v_hi[kBkStages][64];
+  __shared__ __align__(16) float v_lse[kBkStages][64], v_dl[kBkStages][64];
+  __shared__ int v_full[kBkStages];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t k_s = sbase, v_s = sbase + kTile128;
   auto qd_s = [&](int st) { return sbase + 2 * kTile128 + static_cast<uint32_t>(st) * 2 * kQc; };  // q, then dO
-  auto pds_s = [&](int pb) { return sbase + 2 * kTile128 + 4 * kQc + static_cast<uint32_t>(pb) * 2 * kPBytes; };
   if (warp == 5) {
     tmem_alloc(&tmem_base, kWsTmemCols);
     tmem_relinquish();
@@ -2142,9 +2145,11 @@ __global__ void __launch_bounds__(kBkThreads, 1)
   if (tid == 0) {
     mbar_init(&kv_full, 1);
     mbar_init(&kv_empty, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kBkStages; ++i) {
       mbar_init(&qd_full[i], 32);
       mbar_init(&qd_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kTileM);
       mbar_init(&pds_empty[i], 1);
@@ -2225,9 +2230,10 @@ __global__ void __launch_bounds__(kBkThreads, 1)
         }
         __syncwarp();
       }
-      const int st = static_cast<int>(c.n & 1);
-      if (c.n >= 2 &&
-          !__all_sync(0xffffffffu, ws_wait(&qd_empty[st], static_cast<uint32_t>(((c.n >> 1) - 1) & 1), abort_p, 482))) {
+      const int st = static_cast<int>(c.n % kBkStages);
+      if (c.n >= kBkStages &&
+          !__all_sync(0xffffffffu, ws_wait(&qd_empty[st], static_cast<uint32_t>(((c.n / kBkStages) - 1) & 1), abort_p,
+                                           482))) {
         ok = false;
         break;
       }
@@ -2273,13 +2279,16 @@ __global__ void __launch_bounds__(kBkThreads, 1)
       Cur c;
       cur_start(c);
       auto issue_sdp = [&](const Cur& x) -> bool {
-        const int st = static_cast<int>(x.n & 1);
+        const int sb = static_cast<int>(x.n & 1), qs = static_cast<int>(x.n % kBkStages);
         if (is_first(x) && !ws_wait(&kv_full, static_cast<uint32_t>(x.m & 1), abort_p, 483)) return false;
-        if (!ws_wait(&qd_full[st], static_cast<uint32_t>((x.n >> 1) & 1), abort_p, 484)) return false;
+        if (!ws_wait(&qd_full[qs], static_cast<uint32_t>((x.n / kBkStages) & 1), abort_p, 484)) return false;
+        // the buffer's P^T / dS^T of step n - 2 have been read by their MMAs
+        if (x.n >= 2 && !ws_wait(&pds_empty[sb], static_cast<uint32_t>(((x.n >> 1) - 1) & 1), abort_p, 489))
+          return false;
         tc_fence_after();
-        issue_qk(tmem + 64 * st, k_s, qd_s(st));               // S^T = K Q^T
-        issue_qk(tmem + 128 + 64 * st, v_s, qd_s(st) + kQc);   // dP^T = V dO^T
-        mma_commit(&s_full[st]);
+        issue_qk(tmem + 64 * sb, k_s, qd_s(qs));               // S^T = K Q^T
+        issue_qk(tmem + 128 + 64 * sb, v_s, qd_s(qs) + kQc);   // dP^T = V dO^T
+        mma_commit(&s_full[sb]);
         if (is_last(x)) mma_commit(&kv_empty);  // K / V are read by S^T / dP^T only
         return true;
       };
@@ -2288,15 +2297,15 @@ __global__ void __launch_bounds__(kBkThreads, 1)
         Cur nx = c;
         cur_advance(nx);
         if (!nx.done && !(ok = issue_sdp(nx))) break;
-        const int st = static_cast<int>(c.n & 1);
-        if (!ws_wait(&p_full[st], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 485)) break;
+        const int sb = static_cast<int>(c.n & 1), qs = static_cast<int>(c.n % kBkStages);
+        if (!ws_wait(&p_full[sb], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 485)) break;
         const bool first = is_first(c), last = is_last(c);
         if (first && c.m > 0 && !ws_wait(&dkv_empty, static_cast<uint32_t>((c.m - 1) & 1), abort_p, 486)) break;
         tc_fence_after();
-        issue_pv(tm_dv, pds_s(st), qd_s(st) + kQc, !first);        // dV += P^T dO
-        issue_pv(tm_dk, pds_s(st) + kPBytes, qd_s(st), !first);    // dK += dS^T Q
-        mma_commit(&pds_empty[st]);
-        mma_commit(&qd_empty[st]);
+        issue_pv_tmem(tm_dv, tmem + 64 * sb, qd_s(qs) + kQc, !first);        // dV += P^T dO
+        issue_pv_tmem(tm_dk, tmem + 128 + 64 * sb, qd_s(qs), !first);        // dK += dS^T Q
+        mma_commit(&pds_empty[sb]);
+        mma_commit(&qd_empty[qs]);
         if (last) mma_commit(&dkv_full);
         c = nx;
       }
@@ -2309,23 +2318,23 @@ __global__ void __launch_bounds__(kBkThreads, 1)
     Cur c;
     cur_start(c);
     while (!c.done) {
-      const int st = static_cast<int>(c.n & 1);
+      const int sb = static_cast<int>(c.n & 1), st = static_cast<int>(c.n % kBkStages);
       const int64_t key = c.k0 + r;
       const bool key_ok = key < f.T;
-      if (!__all_sync(0xffffffffu, ws_wait(&qd_full[st], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 487) &&
-                                       ws_wait(&s_full[st], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 488)))
+      if (!__all_sync(0xffffffffu, ws_wait(&qd_full[st], static_cast<uint32_t>((c.n / kBkStages) & 1), abort_p, 487) &&
+                                       ws_wait(&s_full[sb], static_cast<uint32_t>((c.n >> 1) & 1), abort_p, 488)))
         break;
       tc_fence_after();
       float sv[64], dp[64];
       {
         float x0[32], x1[32];
-        tmem_ld32(tmem + 64 * st + lane_off, x0);
-        tmem_ld32(tmem + 64 * st + lane_off + 32, x1);
+        tmem_ld32(tmem + 64 * sb + lane_off, x0);
+        tmem_ld32(tmem + 64 * sb + lane_off + 32, x1);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) { sv[i] = x0[i]; sv[32 + i] = x1[i]; }
-        tmem_ld32(tmem + 128 + 64 * st + lane_off, x0);
-        tmem_ld32(tmem + 128 + 64 * st + lane_off + 32, x1);
+        tmem_ld32(tmem + 128 + 64 * sb + lane_off, x0);
+        tmem_ld32(tmem + 128 + 64 * sb + lane_off + 32, x1);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) { dp[i] = x0[i]; dp[32 + i] = x1[i]; }
@@ -2364,16 +2373,12 @@ __global__ void __launch_bounds__(kBkThreads, 1)
           }
         }
       }
-      if (c.n >= 2 && !__all_sync(0xffffffffu, ws_wait(&pds_empty[st], static_cast<uint32_t>(((c.n >> 1) - 1) & 1),
-                                                       abort_p, 489)))
-        break;
-      store_p_row(pds_s(st), r, 0, sv);
-      store_p_row(pds_s(st), r, 4, sv + 32);
-      store_p_row(pds_s(st) + kPBytes, r, 0, dp);
-      store_p_row(pds_s(st) + kPBytes, r, 4, dp + 32);
-      fence_async_smem();
+      // P^T and dS^T over the first 32 columns of the buffers just read
+      store_p_tmem(tmem + 64 * sb + lane_off, sv);
+      store_p_tmem(tmem + 128 + 64 * sb + lane_off, dp);
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(&p_full[sb]);
       if (is_last(c)) {
         if (!__all_sync(0xffffffffu, ws_wait(&dkv_full, static_cast<uint32_t>(c.m & 1), abort_p, 490))) break;
         tc_fence_after();
