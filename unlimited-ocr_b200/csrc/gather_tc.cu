@@ -1494,6 +1494,11 @@ __global__ void __launch_bounds__(kRbThreads, 1)
   __shared__ const __nv_bfloat16* qrows[kTileM];
   __shared__ const __nv_bfloat16* grows[kTileM];
   __shared__ int32_t r_t[2][kTileM], r_slot[2][kTileM];
+  // per-row softmax metadata, fetched by the producers one tile ahead:
+  // exponent offset (bias - lse, log2), delta, and the row's remote key range
+  // inside the block (lo | hi << 8; empty for an absent row or lse = -inf)
+  __shared__ float r_off[2][kTileM], r_dlt[2][kTileM];
+  __shared__ int32_t r_kr[2][kTileM];
   __shared__ float dsum_hi[2][kTileM];  // d_bias partial of the keys 32-63 half, by tile parity
   __shared__ uint64_t dsum_full[2];
   __shared__ uint32_t tmem_base;
@@ -1577,17 +1582,25 @@ __global__ void __launch_bounds__(kRbThreads, 1)
           break;
         }
       }
+      float m_lse[2], m_dlt[2], m_bias[2];
+      int32_t m_seg[2];
 #pragma unroll
       for (int k2 = 0; k2 < 2; ++k2) {
         const int r = 64 * half + lane + 32 * k2;
         const int32_t pk = ppk[k2];
         const int32_t tt = pk >= 0 ? pk / static_cast<int32_t>(f.S) : -1;
+        const int32_t sl = pk >= 0 ? pk - tt * static_cast<int32_t>(f.S) : 0;
         qrows[r] = pk >= 0 ? f.q + cs.b * f.sqb + static_cast<int64_t>(tt) * f.sqt + cs.h * f.sqh : nullptr;
         grows[r] = pk >= 0 ? a.dout + cs.b * f.sob + static_cast<int64_t>(tt) * f.sot + cs.h * f.soh : nullptr;
         r_t[bq][r] = tt;
-        r_slot[bq][r] = pk >= 0 ? pk - tt * static_cast<int32_t>(f.S) : 0;
+        r_slot[bq][r] = sl;
+        // issued now, consumed after the gathers below are in flight
+        const int64_t bt = cs.b * f.T + (pk >= 0 ? tt : 0);
+        m_lse[k2] = pk >= 0 ? a.lse[bt * f.HQ + cs.h] : -INFINITY;
+        m_dlt[k2] = pk >= 0 ? a.delta[bt * f.HQ + cs.h] : 0.f;
+        m_bias[k2] = pk >= 0 && f.bias ? f.bias[bt * f.S + sl] : 0.f;
+        m_seg[k2] = pk >= 0 && f.seg ? f.seg[bt] : 0;
       }
-      mbar_arrive(&info_full[bq]);
       __syncwarp();
       const int cc = lane & 15;
       const uint32_t qdst = qd_buf(bq) + (cc >> 3) * (kTile128 / 2);
@@ -1601,6 +1614,26 @@ __global__ void __launch_bounds__(kRbThreads, 1)
         cp_async16_zfill(gdst + sw128_off(r, cc & 7), gg ? static_cast<const void*>(gg + cc * 8) : f.q, gg != nullptr);
       }
       cp_async_mbar_arrive(&q_full[bq]);
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int r = 64 * half + lane + 32 * k2;
+        const int64_t tt = r_t[bq][r];
+        int32_t kr = 0;
+        if (tt >= 0 && m_lse[k2] != -INFINITY) {
+          const int64_t sg = m_seg[k2];
+          int64_t ls = tt - f.LW + 1;
+          if (ls < sg) ls = sg;
+          if (ls < 0) ls = 0;
+          const int64_t k0 = cs.blk * kBlk;
+          const int64_t lo = (k0 > sg ? k0 : sg) - k0;
+          const int64_t hi = min(min(k0 + kBlk, ls), tt + 1) - k0;
+          kr = clamp_key(lo) | (clamp_key(hi) << 8);
+        }
+        r_off[bq][r] = (m_bias[k2] - m_lse[k2]) * kLog2e;
+        r_dlt[bq][r] = m_dlt[k2];
+        r_kr[bq][r] = kr;
+      }
+      mbar_arrive(&info_full[bq]);
       __syncwarp();
       cs.advance(a);
       if (!cs.done) fetch();
@@ -1662,31 +1695,21 @@ __global__ void __launch_bounds__(kRbThreads, 1)
       const int bq = static_cast<int>(n & 1);
       if (!__all_sync(0xffffffffu, ws_wait(&info_full[bq], static_cast<uint32_t>((n >> 1) & 1), abort_p, 449))) break;
       const int64_t t = r_t[bq][r], slot = r_slot[bq][r];
+      const float off = r_off[bq][r], dlt = r_dlt[bq][r];
+      const int32_t kr = r_kr[bq][r];
       mbar_arrive(&info_empty[bq]);
       const bool row_ok = t >= 0;
-      float lse_raw = 0.f, dlt = 0.f, bias_raw = 0.f;
-      int64_t rlo = 0, rhi = 0;
-      if (row_ok) {  // in flight while S and dP land; used after the wait
-        lse_raw = a.lse[(cs.b * f.T + t) * f.HQ + cs.h];
-        dlt = a.delta[(cs.b * f.T + t) * f.HQ + cs.h];
-        if (f.bias) bias_raw = f.bias[(cs.b * f.T + t) * f.S + slot];
-        remote_range(f, cs.b, t, cs.blk, rlo, rhi);
-      }
+      const int klo = max((kr & 0xff) - 32 * ch, 0), khi = max((kr >> 8) - 32 * ch, 0);
       if (!__all_sync(0xffffffffu, ws_wait(&s_full, static_cast<uint32_t>(n & 1), abort_p, 450))) break;
       tc_fence_after();
       float sv[32], dp[32];
       tmem_ld32(tm_s + lane_off + 32 * ch, sv);
       tmem_ld32(tm_dp + lane_off + 32 * ch, dp);
       tmem_wait_ld();
-      const int64_t k0 = cs.blk * kBlk + 32 * ch;
-      const int klo = row_ok ? clamp_key(rlo - k0) : 0, khi = row_ok ? clamp_key(rhi - k0) : 0;
-      const float lse2 = lse_raw * kLog2e;
-      const float off = bias_raw * kLog2e - lse2;
-      const bool okl = lse2 != -INFINITY;
       float ds4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const bool valid = okl && i >= klo && i < khi;
+        const bool valid = i >= klo && i < khi;
         const float pv = valid ? fast_exp2(fmaf(sv[i], f.scale_log2, off)) : 0.f;
         const float ds = pv * (dp[i] - dlt);
         sv[i] = pv;
