@@ -1656,19 +1656,30 @@ __global__ void __launch_bounds__(kRbThreads, 1)
         mma_commit(&s_full);
         return true;
       };
+      // operands of the cursor's tile already landed (no wait)
+      auto sdp_ready = [&]() -> bool {
+        const int bq = static_cast<int>(cs.n & 1);
+        if (cs.first() && !mbar_ready(&kv_full, static_cast<uint32_t>(cs.m & 1))) return false;
+        return mbar_ready(&q_full[bq], static_cast<uint32_t>((cs.n >> 1) & 1));
+      };
+      // Issuing a tcgen05.mma blocks while the tensor pipe is busy, so the
+      // issue order is the execution order: dQ of this tile first (the
+      // compute warps wait for it), then the next tile's S / dP if its rows
+      // are already in shared memory, else this tile's dV / dK first (which
+      // frees its Q / dO buffer for the next gather).
       if (ok) ok = issue_sdp();
       while (ok && !cs.done) {
         const int64_t n = cs.n, m = cs.m;
         const int bq = static_cast<int>(n & 1);
         const bool first = cs.first(), last = cs.last();
         if (!ws_wait(&p_full, static_cast<uint32_t>(n & 1), abort_p, 446)) break;
-        cs.advance(a);  // cs now names the next tile
-        const bool next_same_item = !cs.done && cs.m == m;
-        if (next_same_item && !(ok = issue_sdp())) break;
         if (n > 0 && !ws_wait(&dq_empty, static_cast<uint32_t>((n - 1) & 1), abort_p, 447)) break;
         tc_fence_after();
         issue_pv(tm_dq, ds_s, k_s, false);  // dQ = dS K
         mma_commit(&o_full);
+        cs.advance(a);  // cs now names the next tile
+        const bool early = !cs.done && cs.m == m && sdp_ready();
+        if (early && !(ok = issue_sdp())) break;
         if (first && m > 0 && !ws_wait(&dkv_empty, static_cast<uint32_t>((m - 1) & 1), abort_p, 448)) break;
         tc_fence_after();
         issue_tn(tm_dvt, qd_buf(bq) + kTile128, kTile128 / 2, p_s, !first);  // dV^T += dO^T P
@@ -1679,7 +1690,7 @@ __global__ void __launch_bounds__(kRbThreads, 1)
           mma_commit(&dkv_full);
           mma_commit(&kv_empty);
         }
-        if (!cs.done && !next_same_item && !(ok = issue_sdp())) break;
+        if (!cs.done && !early && !(ok = issue_sdp())) break;
       }
     }
     __syncwarp();
