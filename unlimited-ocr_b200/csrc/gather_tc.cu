@@ -1417,18 +1417,20 @@ __global__ void __launch_bounds__(256) bwd_pairs_fill_kernel(const TcArgs a, con
 //              (bf16) to shared memory, the row's dQ
 //              partial, and at the end of an item this block's dK / dV
 //              (thread = feature);
-//   warps 8-9  producers: cp.async gathers of the tile's q and dO rows into
-//              a double-buffered tile (warp 8 rows 0-63, warp 9 rows
-//              64-127), the rows' (query, slot) into shared memory, and (warp
-//              8) the item's K and V by TMA;
-//   warp 10    MMA issuer: S = Q K^T, dP = dO V^T; dQ = dS K; dV^T += dO^T P,
-//              dK^T += Q^T dS accumulated over the item's tiles in TMEM.  The
-//              next tile's S / dP (same item) is issued before this tile's
-//              dQ / dV / dK so the tensor pipe works while the compute warps do.
+//   warps 8-11 producers (one per SM sub-partition; a warp's cp.async issue
+//              rate bounds the gather): cp.async gathers of the tile's q and
+//              dO rows into a double-buffered tile (warp 8 + i rows 32i ..
+//              32i + 31), the rows' (query, slot) and softmax metadata into
+//              shared memory, and (warp 8) the item's K and V by TMA;
+//   warp 12    MMA issuer: S = Q K^T, dP = dO V^T; dQ = dS K; dV^T += dO^T P,
+//              dK^T += Q^T dS accumulated over the item's tiles in TMEM.
+//              dQ first, then the next tile's S / dP (same item) ahead of
+//              this tile's dV / dK when its rows have landed.
 // All waits bounded; abort protocol as in fwd_ws_kernel.
-constexpr int kRbThreads = 352;
+constexpr int kRbThreads = 416;
 constexpr int kRbCompute = 256;  // compute threads (8 warps)
-constexpr int kRbMma = 10;
+constexpr int kRbProd = 8;       // first of 4 gather warps (one per SM sub-partition)
+constexpr int kRbMma = 12;
 constexpr uint32_t kRbQD = 2 * kTile128;                        // q tile + dO tile
 constexpr uint32_t kRbSmem = 2 * kRbQD + 2 * kKVBytes + 2 * kPBytes + 1024;  // 193 KB
 
@@ -1516,9 +1518,9 @@ __global__ void __launch_bounds__(kRbThreads, 1)
     mbar_init(&kv_full, 1);
     mbar_init(&kv_empty, 1);
     for (int bq = 0; bq < 2; ++bq) {
-      mbar_init(&q_full[bq], 64);
+      mbar_init(&q_full[bq], 128);
       mbar_init(&q_empty[bq], 1);
-      mbar_init(&info_full[bq], 64);
+      mbar_init(&info_full[bq], 128);
       mbar_init(&info_empty[bq], kRbCompute);
     }
     mbar_init(&s_full, 1);
@@ -1541,29 +1543,28 @@ __global__ void __launch_bounds__(kRbThreads, 1)
   const uint32_t tm_s = tmem, tm_dp = tmem + 64, tm_dq = tmem + 128, tm_dvt = tmem + 256, tm_dkt = tmem + 320;
   volatile int* abort_p = &abort_flag;
 
-  if (warp == 8 || warp == 9) {
+  if (warp >= kRbProd && warp < kRbProd + 4) {
     // ---------------------------------------------------------- producers
-    const int half = warp - 8;  // rows 64*half .. 64*half + 63
+    // gathers are bound by the issue rate of each warp's cp.async, so four
+    // warps (one per SM sub-partition) share a tile: rows 32 * quarter + lane
+    const int quarter = warp - kRbProd;
+    const int r = 32 * quarter + lane;
     RbCursor cs;
     cs.start(a);
-    int32_t ppk[2];
+    int32_t ppk = -1;
     auto fetch = [&]() {
       const int64_t fp = cs.tile_first(), nh = cs.tile_rows();
-#pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2) {
-        const int r = 64 * half + lane + 32 * k2;
-        ppk[k2] = r < nh ? a.f.pairs[fp + r] : -1;
-      }
+      ppk = r < nh ? a.f.pairs[fp + r] : -1;
     };
     if (!cs.done) fetch();
     bool ok = true;
     while (ok && !cs.done) {
-      if (cs.first()) {
+      if (cs.first() && quarter == 0) {
         if (cs.m > 0 && !__all_sync(0xffffffffu, ws_wait(&kv_empty, static_cast<uint32_t>((cs.m - 1) & 1), abort_p, 441))) {
           ok = false;
           break;
         }
-        if (half == 0 && lane == 0) {
+        if (lane == 0) {
           const int row0 = static_cast<int>(cs.blk * kBlk), hh = static_cast<int>(cs.hk), bb = static_cast<int>(cs.b);
           mbar_arrive_expect_tx(&kv_full, 2 * kKVBytes);
           tma_load_4d(k_s, &tmk, 0, row0, hh, bb, &kv_full);
@@ -1582,57 +1583,45 @@ __global__ void __launch_bounds__(kRbThreads, 1)
           break;
         }
       }
-      float m_lse[2], m_dlt[2], m_bias[2];
-      int32_t m_seg[2];
-#pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2) {
-        const int r = 64 * half + lane + 32 * k2;
-        const int32_t pk = ppk[k2];
-        const int32_t tt = pk >= 0 ? pk / static_cast<int32_t>(f.S) : -1;
-        const int32_t sl = pk >= 0 ? pk - tt * static_cast<int32_t>(f.S) : 0;
-        qrows[r] = pk >= 0 ? f.q + cs.b * f.sqb + static_cast<int64_t>(tt) * f.sqt + cs.h * f.sqh : nullptr;
-        grows[r] = pk >= 0 ? a.dout + cs.b * f.sob + static_cast<int64_t>(tt) * f.sot + cs.h * f.soh : nullptr;
-        r_t[bq][r] = tt;
-        r_slot[bq][r] = sl;
-        // issued now, consumed after the gathers below are in flight
-        const int64_t bt = cs.b * f.T + (pk >= 0 ? tt : 0);
-        m_lse[k2] = pk >= 0 ? a.lse[bt * f.HQ + cs.h] : -INFINITY;
-        m_dlt[k2] = pk >= 0 ? a.delta[bt * f.HQ + cs.h] : 0.f;
-        m_bias[k2] = pk >= 0 && f.bias ? f.bias[bt * f.S + sl] : 0.f;
-        m_seg[k2] = pk >= 0 && f.seg ? f.seg[bt] : 0;
-      }
+      const int32_t tt = ppk >= 0 ? ppk / static_cast<int32_t>(f.S) : -1;
+      const int32_t sl = ppk >= 0 ? ppk - tt * static_cast<int32_t>(f.S) : 0;
+      qrows[r] = ppk >= 0 ? f.q + cs.b * f.sqb + static_cast<int64_t>(tt) * f.sqt + cs.h * f.sqh : nullptr;
+      grows[r] = ppk >= 0 ? a.dout + cs.b * f.sob + static_cast<int64_t>(tt) * f.sot + cs.h * f.soh : nullptr;
+      r_t[bq][r] = tt;
+      r_slot[bq][r] = sl;
+      // issued now, consumed after the gathers below are in flight
+      const int64_t bt = cs.b * f.T + (ppk >= 0 ? tt : 0);
+      const float m_lse = ppk >= 0 ? a.lse[bt * f.HQ + cs.h] : -INFINITY;
+      const float m_dlt = ppk >= 0 ? a.delta[bt * f.HQ + cs.h] : 0.f;
+      const float m_bias = ppk >= 0 && f.bias ? f.bias[bt * f.S + sl] : 0.f;
+      const int32_t m_seg = ppk >= 0 && f.seg ? f.seg[bt] : 0;
       __syncwarp();
       const int cc = lane & 15;
       const uint32_t qdst = qd_buf(bq) + (cc >> 3) * (kTile128 / 2);
       const uint32_t gdst = qdst + kTile128;
 #pragma unroll 4
-      for (int i = 0; i < 32; ++i) {
-        const int r = 64 * half + (lane >> 4) + 2 * i;
-        const __nv_bfloat16* gq = qrows[r];
-        const __nv_bfloat16* gg = grows[r];
-        cp_async16_zfill(qdst + sw128_off(r, cc & 7), gq ? static_cast<const void*>(gq + cc * 8) : f.q, gq != nullptr);
-        cp_async16_zfill(gdst + sw128_off(r, cc & 7), gg ? static_cast<const void*>(gg + cc * 8) : f.q, gg != nullptr);
+      for (int i = 0; i < 16; ++i) {
+        const int rr = 32 * quarter + (lane >> 4) + 2 * i;
+        const __nv_bfloat16* gq = qrows[rr];
+        const __nv_bfloat16* gg = grows[rr];
+        cp_async16_zfill(qdst + sw128_off(rr, cc & 7), gq ? static_cast<const void*>(gq + cc * 8) : f.q, gq != nullptr);
+        cp_async16_zfill(gdst + sw128_off(rr, cc & 7), gg ? static_cast<const void*>(gg + cc * 8) : f.q, gg != nullptr);
       }
       cp_async_mbar_arrive(&q_full[bq]);
-#pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2) {
-        const int r = 64 * half + lane + 32 * k2;
-        const int64_t tt = r_t[bq][r];
-        int32_t kr = 0;
-        if (tt >= 0 && m_lse[k2] != -INFINITY) {
-          const int64_t sg = m_seg[k2];
-          int64_t ls = tt - f.LW + 1;
-          if (ls < sg) ls = sg;
-          if (ls < 0) ls = 0;
-          const int64_t k0 = cs.blk * kBlk;
-          const int64_t lo = (k0 > sg ? k0 : sg) - k0;
-          const int64_t hi = min(min(k0 + kBlk, ls), tt + 1) - k0;
-          kr = clamp_key(lo) | (clamp_key(hi) << 8);
-        }
-        r_off[bq][r] = (m_bias[k2] - m_lse[k2]) * kLog2e;
-        r_dlt[bq][r] = m_dlt[k2];
-        r_kr[bq][r] = kr;
+      int32_t kr = 0;
+      if (tt >= 0 && m_lse != -INFINITY) {
+        const int64_t sg = m_seg;
+        int64_t ls = tt - f.LW + 1;
+        if (ls < sg) ls = sg;
+        if (ls < 0) ls = 0;
+        const int64_t k0 = cs.blk * kBlk;
+        const int64_t lo = (k0 > sg ? k0 : sg) - k0;
+        const int64_t hi = min(min(k0 + kBlk, ls), static_cast<int64_t>(tt) + 1) - k0;
+        kr = clamp_key(lo) | (clamp_key(hi) << 8);
       }
+      r_off[bq][r] = (m_bias - m_lse) * kLog2e;
+      r_dlt[bq][r] = m_dlt;
+      r_kr[bq][r] = kr;
       mbar_arrive(&info_full[bq]);
       __syncwarp();
       cs.advance(a);
