@@ -357,7 +357,10 @@ def main_dense(args):
                                 head_cls=torch.zeros(DI, device=dev), stage0="head_cls"))()
     pos = torch.arange(T, device=dev)[None].expand(Bl, T).contiguous()
     p = dict(idx_scale=IDX_SCALE, floor=FLOOR, sigma=SIGMA, K=Kk, topm=M)
-    do = torch.randn(Bl, H, T, D, device=dev, generator=g).to(torch.bfloat16) if train else None
+    # upstream gradient in the memory layout a model's o_proj hands back
+    # (attn_output.transpose(1, 2).reshape(B, T, H * D) -> [B, T, H, D] memory)
+    do = (torch.randn(Bl, T, H, D, device=dev, generator=g).to(torch.bfloat16).transpose(1, 2)
+          if train else None)
     state = {}
 
     def step():
@@ -409,7 +412,8 @@ def main_dense(args):
                 "config": {"workload": ("cfg4 train: route + gather-attention e2e fwd+bwd" if train else
                                         "cfg2 prefill: route + gather-attention fwd"),
                            "global_batch": Bl * world, "seq_len": T, "K": Kk, "LW": LW,
-                           "parallelism": f"batch/dp{world}", "l2": "flushed before every timed step"},
+                           "parallelism": f"batch/dp{world}", "l2": "flushed before every timed step",
+                           **({"dO_layout": "[B,T,H,D] memory (as from o_proj)"} if train else {})},
                 "roofline": {"bound": "tensor", "achieved": fl_all / world / (ms * 1e-3) / 1e12,
                              "peak": peak / 1e12, "unit": "TFLOP/s",
                              "frac": fl_all / world / (ms * 1e-3) / peak, "peak_source": src, "traffic": None},
