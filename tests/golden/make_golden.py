@@ -348,8 +348,138 @@ def case_paged(sgl):
          out=out, params=np.array([BS, L, 3, 4]), fparams=np.array([5.0 / math.sqrt(d), 1e-3, 1.0, 0.2]))
 
 
+PAGE_IMG, PAGE_MARK = 128815, 128827   # config.json image_token_id, page_token_id
+
+
+def page_gate_rows(g, per_page, text_vocab=1000):
+    """Seeded token rows covering the PageGate cases: <PAGE>-marked prompt
+    pages (marker mode) with an instruction and response pages; an unmarked
+    image run split every per_page tokens (per-page mode) with a marked
+    response; image tokens before the first marker; a text-only row."""
+    def txt(n):
+        return torch.randint(0, text_vocab, (n,), generator=g).tolist()
+
+    def img(n):
+        return [PAGE_IMG] * n
+
+    rows = []
+    r = [0]                                                   # marker mode
+    for _ in range(5):
+        r += [PAGE_MARK] + img(int(torch.randint(20, 90, (1,), generator=g))) + txt(3)
+    r += txt(40)
+    for _ in range(4):
+        r += [PAGE_MARK] + txt(int(torch.randint(10, 60, (1,), generator=g)))
+    rows.append(r)
+    r = [0] + img(per_page * 4 + 5) + txt(30)                 # per-page mode
+    for _ in range(3):
+        r += [PAGE_MARK] + txt(int(torch.randint(10, 70, (1,), generator=g)))
+    rows.append(r)
+    r = [0] + img(37) + txt(5) + [PAGE_MARK] + img(50) + [PAGE_MARK] + img(41) + txt(20)   # images before markers
+    r += [PAGE_MARK] + txt(33) + [PAGE_MARK] + txt(25)
+    rows.append(r)
+    rows.append([0] + txt(300))                               # text only
+    S = max(len(x) for x in rows)
+    ids = torch.full((len(rows), S), 7, dtype=torch.long)
+    for i, x in enumerate(rows):
+        ids[i, :len(x)] = torch.tensor(x)
+    return ids
+
+
+def case_page_gate(m):
+    """PageGate: _build_page_aware_ids, _build_flat_image_token_mask,
+    _build_kl_candidate_mask (both constraint settings) and
+    _uocr_dash_decode_allow (prefill state + decode steps)."""
+    base = importlib.import_module("uocr_ref._sparse_base_impl")
+    for name, attrs in (("easydict", {"EasyDict": dict}), ("addict", {"Dict": dict})):
+        if name not in sys.modules:      # vision-encoder deps, not on this path
+            mod = types.ModuleType(name)
+            for k_, v_ in attrs.items():
+                setattr(mod, k_, v_)
+            sys.modules[name] = mod
+    mu = importlib.import_module("uocr_ref.modeling_unlimitedocr")
+    Ix = base.DeepseekV2Indexer
+    g = torch.Generator().manual_seed(21)
+    per_page = 7
+    ids = page_gate_rows(g, per_page)
+    B, S = ids.shape
+    outs = dict(ids=ids, params=np.array([PAGE_IMG, PAGE_MARK, per_page]))
+
+    def indexer(bs, constraint):
+        ns = types.SimpleNamespace(block_size=bs, per_page_image_tokens=per_page, layer_idx=0,
+                                   image_bucket_constraint=constraint, _page_aware_diag_logged=True,
+                                   image_token_id=PAGE_IMG, page_token_id=PAGE_MARK,
+                                   q_proj=types.SimpleNamespace(weight=torch.zeros(1)))
+        for fn in ("_build_page_aware_ids", "_build_flat_image_token_mask", "_build_image_block_allow_mask",
+                   "_build_page_aware_image_block_mask", "_build_kl_candidate_mask"):
+            setattr(ns, fn, types.MethodType(getattr(Ix, fn), ns))
+        return ns
+
+    saved = base._PAGE_SCOPE_PREFILL
+    for scope in (0, 1):
+        base._PAGE_SCOPE_PREFILL = bool(scope)
+        for kl, tag in ((S, "full"), (S - 37, "trunc"), (S + 50, "pad")):
+            itm, ipi, qpi = indexer(16, True)._build_page_aware_ids(ids, PAGE_IMG, PAGE_MARK, kl)
+            outs[f"itm_s{scope}_{tag}"], outs[f"ipi_s{scope}_{tag}"], outs[f"qpi_s{scope}_{tag}"] = itm, ipi, qpi
+    base._PAGE_SCOPE_PREFILL = saved
+    # a text-only batch gives (None, None, None)
+    none = indexer(16, True)._build_page_aware_ids(ids[3:], PAGE_IMG, PAGE_MARK, S)
+    outs["none_text_only"] = np.array([x is None for x in none])
+    outs["flat_itm"] = indexer(16, False)._build_flat_image_token_mask(ids, PAGE_IMG, S)
+
+    # candidate masks: scope-1 page ids, two block sizes, a query chunk with an
+    # offset and positions beyond the page-id length (clamped by the reference)
+    itm, ipi, qpi = outs["itm_s1_full"], outs["ipi_s1_full"], outs["qpi_s1_full"]
+    pos = torch.arange(S)[None].expand(B, S).contiguous()
+    pos_chunk = (torch.arange(150) + S - 120)[None].expand(B, 150).contiguous()
+    outs["pos_chunk"] = pos_chunk
+    for bs in (16, 64):
+        nblk = -(-S // bs)
+        for constraint in (True, False):
+            ix = indexer(bs, constraint)
+            flat = outs["flat_itm"]
+            for ptag, pp_ in (("all", pos), ("chunk", pos_chunk)):
+                cq = pp_.shape[1]
+                cm = ix._build_kl_candidate_mask(pp_, nblk, itm if constraint else flat, B, cq,
+                                                 image_token_page_ids=ipi if constraint else None,
+                                                 query_token_page_ids=qpi if constraint else None)
+                outs[f"cand_bs{bs}_c{int(constraint)}_{ptag}"] = cm[:, 0]
+        cm = indexer(bs, False)._build_kl_candidate_mask(pos, nblk, None, B, S)
+        outs[f"cand_bs{bs}_none"] = cm[:, 0]
+
+    # decode allow: prefill state, then decode steps (a <PAGE> marker on step 2
+    # of row 0 and step 4 of row 1 advances that row's page)
+    for bs in (16, 64):
+        ix = indexer(bs, True)
+        cache = types.SimpleNamespace(n=S)
+        cache.get_seq_length = lambda c=cache: c.n
+        assert mu._uocr_dash_decode_allow(ix, ids, cache) is None
+        st = cache._uocr_pg
+        outs[f"dec_bs{bs}_bmin"], outs[f"dec_bs{bs}_bmax"] = st["bmin"].clone(), st["bmax"].clone()
+        outs[f"dec_bs{bs}_pp"], outs[f"dec_bs{bs}_mcum0"] = st["pp"].clone(), st["mcum"].clone()
+        steps = torch.randint(0, 1000, (B, 12), generator=g)
+        steps[0, 2] = PAGE_MARK
+        steps[1, 4] = PAGE_MARK
+        steps[2, 0] = PAGE_MARK
+        allows = []
+        for k_ in range(steps.shape[1]):
+            a = mu._uocr_dash_decode_allow(ix, steps[:, k_:k_ + 1], cache)
+            cache.n += 1
+            allows.append(a)
+        outs[f"dec_bs{bs}_steps"] = steps
+        width = max(a.shape[1] for a in allows)
+        outs[f"dec_bs{bs}_allow"] = torch.stack(
+            [torch.nn.functional.pad(a, (0, width - a.shape[1])) for a in allows])
+        outs[f"dec_bs{bs}_nblk"] = np.array([a.shape[1] for a in allows])
+    save("page_gate", **outs)
+
+
 def main():
+    only = sys.argv[1:]
     m = import_reference()
+    if only:   # regenerate the named cases only, e.g. `make_golden.py page_gate`
+        for name in only:
+            globals()[f"case_{name}"](m)
+        return
     sgl = import_sglang_ops()
     torch.manual_seed(0)
     case_route(m)
@@ -360,6 +490,7 @@ def main():
     case_gather_e2e(m)
     case_block_max(m)
     case_paged(sgl)
+    case_page_gate(m)
 
 
 if __name__ == "__main__":

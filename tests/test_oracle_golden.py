@@ -210,3 +210,54 @@ def test_lse_merge_matches_single_pass():
     o, lse = O.lse_merge(np.stack(parts_o), np.stack(parts_l))
     e = np.exp(s - s.max(-1, keepdims=True))
     np.testing.assert_allclose(o, (e @ v) / e.sum(-1, keepdims=True), rtol=1e-5, atol=1e-6)
+
+
+# ---------------------------------------------------------------- PageGate
+def test_page_gate_ids_golden():
+    from oracle import page_gate as PG
+    g = golden("page_gate")
+    img, mark, per_page = (int(x) for x in g["params"])
+    ids = g["ids"]
+    S = ids.shape[1]
+    for scope in (0, 1):
+        for tag, kl in (("full", S), ("trunc", S - 37), ("pad", S + 50)):
+            itm, ipi, qpi = PG.page_aware_ids(ids, img, mark, kl, per_page, bool(scope))
+            np.testing.assert_array_equal(itm, g[f"itm_s{scope}_{tag}"])
+            np.testing.assert_array_equal(ipi, g[f"ipi_s{scope}_{tag}"])
+            np.testing.assert_array_equal(qpi, g[f"qpi_s{scope}_{tag}"])
+    assert g["none_text_only"].all() and PG.page_aware_ids(ids[3:], img, mark, S, per_page, True) is None
+    np.testing.assert_array_equal(PG.flat_image_token_mask(ids, img, S), g["flat_itm"])
+
+
+@pytest.mark.parametrize("bs", [16, 64])
+def test_page_gate_cand_golden(bs):
+    from oracle import page_gate as PG
+    g = golden("page_gate")
+    B, S = g["ids"].shape
+    nblk = -(-S // bs)
+    pos = np.broadcast_to(np.arange(S), (B, S))
+    for constraint in (1, 0):
+        for ptag, pp in (("all", pos), ("chunk", g["pos_chunk"])):
+            c = PG.kl_candidate_mask(pp, nblk, g["itm_s1_full"] if constraint else g["flat_itm"], bs,
+                                     bool(constraint), g["ipi_s1_full"] if constraint else None,
+                                     g["qpi_s1_full"] if constraint else None)
+            np.testing.assert_array_equal(c, g[f"cand_bs{bs}_c{constraint}_{ptag}"])
+    np.testing.assert_array_equal(PG.kl_candidate_mask(pos, nblk, None, bs, False), g[f"cand_bs{bs}_none"])
+
+
+@pytest.mark.parametrize("bs", [16, 64])
+def test_page_gate_decode_allow_golden(bs):
+    from oracle import page_gate as PG
+    g = golden("page_gate")
+    img, mark, per_page = (int(x) for x in g["params"])
+    ids = g["ids"]
+    st = PG.decode_allow_prefill(ids, img, mark, per_page, bs)
+    for k in ("bmin", "bmax", "pp"):
+        np.testing.assert_array_equal(st[k], g[f"dec_bs{bs}_{k}"])
+    np.testing.assert_array_equal(st["mcum"], g[f"dec_bs{bs}_mcum0"])
+    n = ids.shape[1]
+    for k, nb in enumerate(g[f"dec_bs{bs}_nblk"]):
+        allow, st = PG.decode_allow_step(st, g[f"dec_bs{bs}_steps"][:, k], mark, n + 1, bs)
+        n += 1
+        assert allow.shape[1] == nb
+        np.testing.assert_array_equal(allow, g[f"dec_bs{bs}_allow"][k][:, :nb])
