@@ -56,10 +56,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx", "pagegate"],
                     help="decode = cfg3 (default, the headline); prefill = cfg2; train = cfg4 fwd+bwd; "
                          "route = the cfg3 router alone (k_bar cache + block table, no KV; for profiling); "
-                         "longctx = cfg5 attention share (12 layers, one 1M-token sequence, split-KV)")
+                         "longctx = cfg5 attention share (12 layers, one 1M-token sequence, split-KV); "
+                         "pagegate = PageGate candidate masks of a cfg2-shaped prefill")
     ap.add_argument("--layers", type=int, default=12, help="longctx: decoder layers")
     ap.add_argument("--batch", type=int, default=0, help="prefill/train batch override (smaller cases)")
     ap.add_argument("--seq", type=int, default=0, help="prefill/train sequence override")
@@ -455,6 +456,83 @@ def main_route(args):
     return 0
 
 
+def page_doc(B, T, seed, per_page=273, img=128815, mark=128827):
+    """Seeded document token rows: <PAGE> + per_page image tokens + a few text
+    tokens per prompt page (Base mode), an instruction, then <PAGE>-marked
+    response pages of 200-600 text tokens."""
+    rng = np.random.default_rng(seed)
+    out = np.full((B, T), 5, np.int64)
+    for b in range(B):
+        r = [0]
+        while len(r) < T * 0.6:
+            r += [mark] + [img] * per_page + list(rng.integers(0, 1000, int(rng.integers(2, 8))))
+        r += list(rng.integers(0, 1000, 60))
+        while len(r) < T:
+            r += [mark] + list(rng.integers(0, 1000, int(rng.integers(200, 600))))
+        out[b] = np.asarray(r[:T])
+    return out
+
+
+def main_pagegate(args):
+    """PageGate candidate masks for a prefill of cfg2's shape (B=4, T=16384,
+    block 64): page-aware ids -> block descriptors -> per-query candidate
+    mask [B, T, nblk], the router's input.  HBM-bound (the mask write)."""
+    from srswa import ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, T = (args.batch or 4), (args.seq or 16384)
+    nblk = T // BS
+    ids_np = page_doc(B, T, 5)
+    ids = torch.from_numpy(ids_np).to(dev)
+    pos = torch.arange(T, device=dev)[None].expand(B, T).contiguous()
+    state = {}
+
+    def step():
+        itm, ipi, qpi, _ = ops.page_ids(ids, 128815, 128827, T, 273, True)
+        desc = ops.page_block_desc(nblk, BS, ipi=ipi)
+        state["cand"] = ops.page_cand_mask(desc, BS, pos=pos, qpi=qpi, ipi=ipi)
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    times, g = timed_graph(step, args.steps, args.warmup, flush, not args.no_graph)
+    ms = sum(times) / len(times)
+    # dominant kernel alone
+    itm, ipi, qpi, _ = ops.page_ids(ids, 128815, 128827, T, 273, True)
+    desc = ops.page_block_desc(nblk, BS, ipi=ipi)
+    out = torch.empty(B, T, nblk, device=dev, dtype=torch.bool)
+    ct, g2 = timed_graph(lambda: ops.page_cand_mask(desc, BS, pos=pos, qpi=qpi, ipi=ipi, out=out),
+                         args.steps, args.warmup, flush, not args.no_graph)
+    cms = sum(ct) / len(ct)
+    cand_bytes = B * T * nblk + B * T * 16 + B * nblk * 16          # mask write, pos + qpi reads, descriptors
+    step_bytes = B * T * (8 + 8) + B * T * 17 + B * T * 8 + B * nblk * 16 + cand_bytes  # ids x2, outputs, ipi
+    peak, src = peaks()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import page_gate as PG
+        reps, t0 = 0, time.time()
+        while reps == 0 or time.time() - t0 < 3.0:
+            r_itm, r_ipi, r_qpi = PG.page_aware_ids(ids_np[:1], 128815, 128827, T, 273, True)
+            ref = PG.kl_candidate_mask(np.arange(T)[None], nblk, r_itm, BS, True, r_ipi, r_qpi)
+            reps += 1
+        tc = (time.time() - t0) / reps
+        assert (ref == state["cand"][:1].cpu().numpy()).all()
+        cpu = {"value": step_bytes / B / tc / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"1 of {B} rows (numpy restatement of _build_page_aware_ids + _build_kl_candidate_mask), "
+                         f"{reps} repetitions, {tc * 1e3:.1f} ms each"}
+    print(json.dumps({
+        "metric": "PageGate candidate masks (prefill): GB/s vs HBM", "value": step_bytes / (ms * 1e-3) / 1e9,
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "us_per_step": ms * 1e3, "higher_is_better": True, "dtype": "int64/u8", "data": "synthetic token ids",
+        "config": {"workload": "PageGate: page ids + block descriptors + [B,T,nblk] candidate mask",
+                   "global_batch": B, "seq_len": T, "block": BS, "per_page_image_tokens": 273,
+                   "l2": "flushed before every timed step", "bytes_per_step": step_bytes},
+        "roofline": {"bound": "hbm", "kernel": "page_cand_kernel", "achieved": cand_bytes / (cms * 1e-3) / 1e9,
+                     "peak": peak, "unit": "GB/s", "frac": cand_bytes / (cms * 1e-3) / 1e9 / peak,
+                     "peak_source": src, "us": cms * 1e3, "algorithmic_bytes_per_launch": cand_bytes},
+        "cpu_baseline": cpu, "gpu_launches": 4 * args.steps}), flush=True)
+    del g, g2
+    return 0
+
+
 def main_longctx(args):
     """cfg5 attention share: one decode step of a 1M-token sequence through
     the SR-SWA attention of 12 layers, split-KV over the ranks (rank g owns a
@@ -579,6 +657,8 @@ def main():
         return main_route(args)
     if args.workload == "longctx":
         return main_longctx(args)
+    if args.workload == "pagegate":
+        return main_pagegate(args)
     if args.workload != "decode" and args.impl != "reference":
         return main_dense(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))

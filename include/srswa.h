@@ -317,6 +317,80 @@ SRSWA_API int srswa_lse_merge(const float* o_parts, const float* lse_parts, int6
                     int64_t H, int64_t D, int64_t s_o_part, int64_t s_l_part, void* out,
                     int out_dtype, float* lse_out, srswa_stream_t stream);
 
+/* ------------------------------------------------------- PageGate ------
+ * Page-aware remote candidates.  Token ids are int64 [B, n] rows (row stride
+ * s_row); img_id / page_id are the <image> and <PAGE> token ids; per_page is
+ * the image tokens per page when the prompt carries no <PAGE> markers.
+ * Page ids must stay below 2^31. */
+
+/* Scratch of srswa_page_ids / srswa_decode_allow_state for B rows of n_tok
+ * tokens (16 bytes per 2048-token chunk and row). */
+SRSWA_API size_t srswa_page_scan_workspace_size(int64_t B, int64_t n_tok);
+
+/* Page-aware token ids: itm [B, key_length] (1 = image token), ipi [B,
+ * key_length] int64 (image page, -1 = not an image token), qpi [B,
+ * key_length] int64 (query page, -1 = unconstrained), all contiguous; ids
+ * beyond n_ids are padding (-1), beyond key_length ignored.  flags[0] /
+ * flags[1] (int32, zeroed here) become 1 when the rows hold an image token /
+ * a query with a page (the reference returns None otherwise).
+ * page_scope_prefill: prefill queries (up to the row's last image token) get
+ * their raw page (1) or stay unconstrained (0).
+ * Replaces DeepseekV2Indexer._build_page_aware_ids
+ * (hf-model-code/_sparse_base_impl.py:2404-2497). */
+SRSWA_API int srswa_page_ids(const int64_t* ids, int64_t s_row, int64_t B, int64_t n_ids,
+                             int64_t key_length, int64_t img_id, int64_t page_id, int64_t per_page,
+                             int page_scope_prefill, uint8_t* itm, int64_t* ipi, int64_t* qpi,
+                             int32_t* flags, void* workspace, size_t workspace_bytes,
+                             srswa_stream_t stream);
+
+/* Per key block of nblk blocks of block_size tokens: desc [B, nblk, 4] int32
+ * (16-byte aligned) = {min image page (-1: none), max page, page set low /
+ * high 32 bits}.  Source: page ids ipi [B, n_tok] (row stride s_row), or,
+ * for the any-page ("flat") candidates, an image-token mask itm [B, n_tok]
+ * (exactly one of the two non-null).  Tokens past n_tok are padding.
+ * Replaces the block reductions of _build_page_aware_image_block_mask and
+ * _build_image_block_allow_mask (_sparse_base_impl.py:2629-2648, 2392-2402). */
+SRSWA_API int srswa_page_block_desc(const int64_t* ipi, const uint8_t* itm, int64_t s_row, int64_t B,
+                                    int64_t n_tok, int64_t block_size, int64_t nblk, int32_t* desc,
+                                    srswa_stream_t stream);
+
+/* Candidate mask cand [B, cq, nblk] (uint8, contiguous) of cq query rows:
+ * query i of row b has page qpi[b, clamp(pos[b, i], 0, n_q - 1)] and block c
+ * is a candidate when it holds an image token of that page (flat = 1: when
+ * it holds any image token).  fallback = 1: a query without a candidate gets
+ * every block (the reference's per-query fallback).  ipi (the descriptors'
+ * source) is read only for blocks whose pages span 64 or more.
+ * Replaces _build_kl_candidate_mask (_sparse_base_impl.py:2697-2730) and the
+ * query-chunk loop of _dash_block_cand (modeling_deepseekv2.py:108-122). */
+SRSWA_API int srswa_page_cand_mask(const int32_t* desc, const int64_t* ipi, int64_t s_ipi, int64_t n_tok,
+                                   int64_t block_size, int64_t B, int64_t nblk, const int64_t* qpi,
+                                   int64_t s_qpi, int64_t n_q, const int64_t* pos, int64_t s_pos,
+                                   int64_t cq, int flat, int fallback, uint8_t* cand,
+                                   srswa_stream_t stream);
+
+/* Decode-allow state of a prefill of L tokens: per block of block_size
+ * (dividing 2048) the [min, max] image page it holds (bmin = bmax = -1
+ * without image tokens; [B, ceil(L/block_size)] int64 contiguous), the prompt
+ * page count pp [B] and the marker count mcum [B].
+ * Replaces the prefill branch of _uocr_dash_decode_allow
+ * (hf-model-code/modeling_unlimitedocr.py:497-514). */
+SRSWA_API int srswa_decode_allow_state(const int64_t* ids, int64_t s_row, int64_t B, int64_t L,
+                                       int64_t img_id, int64_t page_id, int64_t per_page,
+                                       int64_t block_size, int64_t* bmin, int64_t* bmax, int64_t* pp,
+                                       int64_t* mcum, void* workspace, size_t workspace_bytes,
+                                       srswa_stream_t stream);
+
+/* Decode allow mask of one new token per request: mcum[b] += (last_ids[b *
+ * s_ids] == page_id) in place; query page = mcum - 1 - pp (-1 if negative);
+ * allow [B, nblk] uint8 = block c < nblk_state with bmin <= page <= bmax, or
+ * every block when the query has no page or no such block.
+ * Replaces the decode branch of _uocr_dash_decode_allow
+ * (modeling_unlimitedocr.py:515-528). */
+SRSWA_API int srswa_decode_allow(const int64_t* last_ids, int64_t s_ids, int64_t B, int64_t page_id,
+                                 const int64_t* bmin, const int64_t* bmax, int64_t s_state,
+                                 int64_t nblk_state, const int64_t* pp, int64_t* mcum, int64_t nblk,
+                                 uint8_t* allow, srswa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,3 +80,18 @@ def test_route_topm_limit():
     dummy = 16
     rc = lib.srswa_route_select(dummy, 128, 1, 128, None, 0, p, None, None, None, None, None)
     assert rc == L.EUNSUPPORTED
+
+
+def test_page_gate_arguments_rejected_without_launch():
+    lib = L.lib()
+    assert lib.srswa_page_scan_workspace_size(2, 5000) == 2 * 3 * 16     # 16 B per 2048-token chunk and row
+    assert lib.srswa_page_ids(None, 0, 1, 1, 1, 1, 2, 7, 1, None, None, None, None, None, 0, None) == L.EINVAL
+    assert lib.srswa_page_block_desc(None, None, 0, 1, 1, 64, 1, 16, None) == L.EINVAL   # neither source
+    assert lib.srswa_page_block_desc(16, 16, 0, 1, 1, 64, 1, 16, None) == L.EINVAL       # both sources
+    assert lib.srswa_page_block_desc(16, None, 0, 1, 1, 64, 1, 24, None) == L.EALIGN     # desc not 16-aligned
+    assert lib.srswa_page_cand_mask(16, None, 0, 1, 64, 1, 1, None, 0, 0, None, 0, 1, 0, 1, 16,
+                                    None) == L.EINVAL                                     # page mode without qpi
+    # decode state: the block size must divide the 2048-token scan chunk
+    assert lib.srswa_decode_allow_state(16, 100, 1, 100, 1, 2, 7, 96, 16, 16, 16, 16, 16, 16,
+                                        None) == L.EUNSUPPORTED
+    assert lib.srswa_decode_allow(None, 1, 1, 2, None, None, 1, 1, None, None, 1, None, None) == L.EINVAL

@@ -1,0 +1,504 @@
+// PageGate: page-aware remote candidates of the SR-SWA router.
+//
+// Token ids -> per-token page ids (image pages, query pages) -> per-query
+// "same-page image block" candidate masks for the prefill router, and the
+// decode-side allow mask of one new token per request.  Integer work, bound
+// by HBM (the [B, Lq, nblk] mask write) or by launch latency.
+//
+// Reference: hf-model-code/_sparse_base_impl.py:2392-2402 (image block allow),
+// :2404-2497 (_build_page_aware_ids), :2609-2627 (flat image mask),
+// :2629-2648 (_build_page_aware_image_block_mask), :2697-2730
+// (_build_kl_candidate_mask); hf-model-code/modeling_unlimitedocr.py:482-528
+// (_uocr_dash_decode_allow).
+//
+// Row scans (page ids, decode state) run in two launches over 2048-token
+// chunks: page_count_kernel reduces each chunk (markers, image tokens, last
+// image token, markers up to it), page_scan_kernel combines the counts of the
+// chunks before its own and scans its chunk, so every SM works on one row.
+// Candidate masks test each key block against the query's page through a
+// 16-byte block descriptor {min page, max page, 64-bit page set}: image page
+// ids only rise along a row and a 64-token block spans at most 64 of them, so
+// the set is exact; a block whose pages span more (only possible with page
+// ids a caller built otherwise) is flagged and scanned token by token.
+#include "common.cuh"
+
+namespace srswa {
+
+constexpr int kPgThreads = 256;
+constexpr int kPgPer = 8;                         // consecutive tokens per thread
+constexpr int kPgChunk = kPgThreads * kPgPer;     // tokens per CTA
+constexpr uint8_t kCodeImg = 1, kCodeMark = 2;
+
+struct PgRow {
+  const int64_t* ids;
+  int64_t s_row, n_ids, n_tok;  // ids columns available, tokens scanned (pad: -1)
+  int64_t img_id, page_id, per_page;
+};
+
+// Chunk of one row: token codes into shared memory with coalesced loads.
+__device__ __forceinline__ void load_codes(const PgRow& r, int64_t b, int64_t c0, uint8_t* codes) {
+  const int64_t lim = min(r.n_ids, r.n_tok);
+  const int64_t* row = r.ids + b * r.s_row;
+#pragma unroll
+  for (int k = 0; k < kPgPer; ++k) {
+    const int i = k * kPgThreads + threadIdx.x;
+    const int64_t j = c0 + i;
+    const int64_t t = j < lim ? __ldg(row + j) : -1;
+    codes[i] = static_cast<uint8_t>((t == r.img_id ? kCodeImg : 0) | (t == r.page_id ? kCodeMark : 0));
+  }
+}
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, Op op, T* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5;
+  __syncthreads();  // red reused across calls
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  T x = red[0];
+#pragma unroll
+  for (int i = 1; i < kPgThreads / 32; ++i) x = op(x, red[i]);
+  return x;
+}
+struct OpAdd { template <typename T> __device__ T operator()(T a, T b) const { return a + b; } };
+struct OpMax { template <typename T> __device__ T operator()(T a, T b) const { return a > b ? a : b; } };
+
+// Per chunk {markers, image tokens, chunk-local index of the last image token
+// (-1: none), markers at or before it}.
+__global__ void __launch_bounds__(kPgThreads) page_count_kernel(const PgRow r, int64_t nchunk, int4* stats) {
+  __shared__ uint8_t codes[kPgChunk];
+  __shared__ int red[kPgThreads / 32];
+  const int64_t b = blockIdx.y, c0 = static_cast<int64_t>(blockIdx.x) * kPgChunk;
+  load_codes(r, b, c0, codes);
+  __syncthreads();
+  const int base = threadIdx.x * kPgPer;
+  int nm = 0, ni = 0, last = -1;
+#pragma unroll
+  for (int k = 0; k < kPgPer; ++k) {
+    const uint8_t c = codes[base + k];
+    nm += (c & kCodeMark) ? 1 : 0;
+    if (c & kCodeImg) {
+      ++ni;
+      last = base + k;
+    }
+  }
+  nm = block_reduce(nm, OpAdd(), red);
+  ni = block_reduce(ni, OpAdd(), red);
+  last = block_reduce(last, OpMax(), red);
+  int upto = 0;
+#pragma unroll
+  for (int k = 0; k < kPgPer; ++k) upto += (base + k <= last && (codes[base + k] & kCodeMark)) ? 1 : 0;
+  upto = block_reduce(upto, OpAdd(), red);
+  if (threadIdx.x == 0) stats[b * nchunk + blockIdx.x] = make_int4(nm, ni, last, upto);
+}
+
+struct PgOut {
+  // mode 0: page-aware ids
+  uint8_t* itm;
+  int64_t* ipi;
+  int64_t* qpi;
+  int32_t* flags;  // [0]: an image token seen, [1]: a query page >= 0 seen
+  int scope;       // page_scope_prefill
+  // mode 1: decode-allow prefill state
+  int64_t *bmin, *bmax, *pp, *mcum;
+  int64_t bs, nblk;
+};
+
+// Exclusive block scan of two counts packed in one 64-bit word (low: markers,
+// high: image tokens; each < 2^32 per chunk).
+__device__ __forceinline__ uint64_t block_excl_scan(uint64_t v, uint64_t* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint64_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) red[w] = x;
+  __syncthreads();
+  uint64_t off = 0;
+  for (int i = 0; i < w; ++i) off += red[i];
+  return off + x - v;
+}
+
+// Scan one chunk of a row with the counts of every chunk before it.
+//   MODE 0: itm / ipi / qpi of _build_page_aware_ids (marker mode per row).
+//   MODE 1: per-block [min, max] image page, pp and the marker count of
+//           _uocr_dash_decode_allow's prefill (image page: cum > 0 ? cum - 1 :
+//           (run - 1) / per_page per token).
+template <int MODE>
+__global__ void __launch_bounds__(kPgThreads) page_scan_kernel(const PgRow r, int64_t nchunk, const int4* stats,
+                                                             const PgOut o) {
+  __shared__ uint8_t codes[kPgChunk];
+  // MODE 0: image pages (buf[0]) and query pages (buf[1]) of the chunk's
+  // tokens; MODE 1: min / max image page per block of the chunk (as int)
+  __shared__ __align__(16) int64_t buf[2][kPgChunk];
+  __shared__ int64_t red64[kPgThreads / 32];
+  __shared__ uint64_t redu[kPgThreads / 32];
+  int* bmn = reinterpret_cast<int*>(buf[0]);
+  int* bmx = bmn + kPgChunk;
+  const int64_t b = blockIdx.y, chunk = blockIdx.x, c0 = chunk * kPgChunk;
+  const int4* st = stats + b * nchunk;
+  load_codes(r, b, c0, codes);
+  // ---- row-level combination of the chunk counts
+  int64_t mb = 0, ib = 0, mall = 0, lastc = -1;
+  for (int64_t c = threadIdx.x; c < nchunk; c += kPgThreads) {
+    const int4 s = __ldg(st + c);
+    mall += s.x;
+    if (c < chunk) {
+      mb += s.x;
+      ib += s.y;
+    }
+    if (s.z >= 0) lastc = c;
+  }
+  mb = block_reduce(mb, OpAdd(), red64);
+  ib = block_reduce(ib, OpAdd(), red64);
+  mall = block_reduce(mall, OpAdd(), red64);
+  lastc = block_reduce(lastc, OpMax(), red64);
+  int64_t pp = 0, last_img = -1;
+  if (lastc >= 0) {
+    int64_t m = 0;
+    for (int64_t c = threadIdx.x; c < lastc; c += kPgThreads) m += __ldg(st + c).x;
+    m = block_reduce(m, OpAdd(), red64);
+    const int4 s = __ldg(st + lastc);
+    pp = m + s.w;
+    last_img = lastc * kPgChunk + s.z;
+  }
+  const bool marker = pp > 0;
+  // ---- chunk scan
+  const int base = threadIdx.x * kPgPer;
+  uint64_t cnt = 0;
+  uint8_t cd[kPgPer];
+#pragma unroll
+  for (int k = 0; k < kPgPer; ++k) {
+    cd[k] = codes[base + k];
+    cnt += ((cd[k] & kCodeMark) ? 1ull : 0ull) + ((cd[k] & kCodeImg) ? (1ull << 32) : 0ull);
+  }
+  const uint64_t ex = block_excl_scan(cnt, redu);
+  int64_t cum = mb + static_cast<int64_t>(ex & 0xffffffffu);
+  int64_t run = ib + static_cast<int64_t>(ex >> 32);
+  if (MODE == 1) {
+    for (int i = threadIdx.x; i < kPgChunk; i += kPgThreads) {
+      bmn[i] = 0x7fffffff;
+      bmx[i] = -1;
+    }
+    __syncthreads();
+  }
+  bool any_q = false;
+#pragma unroll
+  for (int k = 0; k < kPgPer; ++k) {
+    const int64_t j = c0 + base + k;
+    const bool img = cd[k] & kCodeImg;
+    cum += (cd[k] & kCodeMark) ? 1 : 0;
+    run += img ? 1 : 0;
+    if (MODE == 0) {
+      const int64_t ip = img ? (marker ? cum - 1 : (run - 1) / r.per_page) : -1;
+      const int64_t raw = cum - 1;
+      int64_t q = j <= last_img ? (o.scope ? raw : -1) : raw - (marker ? pp : 0);
+      q = q < 0 ? -1 : q;
+      any_q |= (q >= 0 && j < r.n_tok);
+      buf[0][base + k] = ip;
+      buf[1][base + k] = q;
+    } else {
+      if (img) {
+        const int64_t pg = cum > 0 ? cum - 1 : (run - 1) / r.per_page;
+        const int blk = static_cast<int>((base + k) / o.bs);
+        atomicMin(&bmn[blk], static_cast<int>(pg));
+        atomicMax(&bmx[blk], static_cast<int>(pg));
+      }
+    }
+  }
+  __syncthreads();
+  const int64_t nvalid = min(static_cast<int64_t>(kPgChunk), r.n_tok - c0);
+  if (MODE == 0) {
+    const int64_t rowo = b * r.n_tok + c0;
+    for (int i = threadIdx.x; i < nvalid; i += kPgThreads) {
+      o.itm[rowo + i] = codes[i] & kCodeImg;
+      o.ipi[rowo + i] = buf[0][i];
+      o.qpi[rowo + i] = buf[1][i];
+    }
+    const int any_img = __syncthreads_or(ib + static_cast<int64_t>(ex >> 32) < run);
+    const int anyq = __syncthreads_or(any_q);
+    if (threadIdx.x == 0) {
+      if (any_img) atomicOr(&o.flags[0], 1);
+      if (anyq) atomicOr(&o.flags[1], 1);
+    }
+  } else {
+    const int nb = static_cast<int>((nvalid + o.bs - 1) / o.bs);
+    const int64_t blk0 = c0 / o.bs;
+    for (int i = threadIdx.x; i < nb; i += kPgThreads) {
+      const int mx = bmx[i];
+      o.bmax[b * o.nblk + blk0 + i] = mx;
+      o.bmin[b * o.nblk + blk0 + i] = mx >= 0 ? bmn[i] : -1;
+    }
+    if (chunk == 0 && threadIdx.x == 0) {
+      o.pp[b] = pp;
+      o.mcum[b] = mall;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Block descriptors {min page (-1: no image token), max page, page set lo,
+// page set hi}; the set holds bit (p - min) for every page p of the block when
+// max - min < 64, else it is empty (a wide block, scanned by the mask kernel).
+// Flat mode (image-token mask given instead of page ids): {0, 0, 1, 0} for a
+// block with an image token, {-1, -1, 0, 0} else.  One warp per block.
+__global__ void __launch_bounds__(256) page_block_desc_kernel(const int64_t* ipi, const uint8_t* itm, int64_t s_row,
+                                                              int64_t n_tok, int64_t bs, int64_t nblk, int64_t B,
+                                                              int4* desc) {
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= B * nblk) return;
+  const int64_t b = wid / nblk, c = wid - b * nblk;
+  const int64_t j0 = c * bs, j1 = min(j0 + bs, n_tok);
+  if (itm) {
+    bool any = false;
+    for (int64_t j = j0 + lane; j < j1; j += 32) any |= itm[b * s_row + j] != 0;
+    any = __any_sync(0xffffffffu, any);
+    if (lane == 0) desc[wid] = any ? make_int4(0, 0, 1, 0) : make_int4(-1, -1, 0, 0);
+    return;
+  }
+  int64_t mn = INT64_MAX, mx = -1;
+  for (int64_t j = j0 + lane; j < j1; j += 32) {
+    const int64_t p = __ldg(ipi + b * s_row + j);
+    if (p >= 0) {
+      mn = min(mn, p);
+      mx = max(mx, p);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if (mx < 0) {
+    if (lane == 0) desc[wid] = make_int4(-1, -1, 0, 0);
+    return;
+  }
+  uint64_t bits = 0;
+  if (mx - mn < 64) {
+    for (int64_t j = j0 + lane; j < j1; j += 32) {
+      const int64_t p = __ldg(ipi + b * s_row + j);
+      if (p >= 0) bits |= 1ull << (p - mn);
+    }
+    uint32_t lo = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(bits));
+    uint32_t hi = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(bits >> 32));
+    bits = (static_cast<uint64_t>(hi) << 32) | lo;
+  }
+  if (lane == 0)
+    desc[wid] = make_int4(static_cast<int>(mn), static_cast<int>(min(mx, static_cast<int64_t>(INT32_MAX))),
+                          static_cast<int>(static_cast<uint32_t>(bits)), static_cast<int>(static_cast<uint32_t>(bits >> 32)));
+}
+
+struct PgCand {
+  const int4* desc;
+  const int64_t* ipi;  // for wide blocks
+  int64_t s_ipi, n_tok, bs, B, nblk;
+  const int64_t* qpi;
+  int64_t s_qpi, n_q;
+  const int64_t* pos;
+  int64_t s_pos, cq;
+  int flat, fallback;
+  uint8_t* out;        // [B, cq, nblk]
+};
+
+__device__ __forceinline__ bool block_has_page(const PgCand& a, int64_t b, int64_t c, int4 d, int64_t qp) {
+  if (d.x < 0 || qp < d.x || qp > d.y) return false;
+  const uint64_t bits = (static_cast<uint64_t>(static_cast<uint32_t>(d.w)) << 32) | static_cast<uint32_t>(d.z);
+  if (bits) return qp - d.x < 64 && ((bits >> (qp - d.x)) & 1ull);
+  // wide block: token scan
+  const int64_t j1 = min((c + 1) * a.bs, a.n_tok);
+  for (int64_t j = c * a.bs; j < j1; ++j)
+    if (__ldg(a.ipi + b * a.s_ipi + j) == qp) return true;
+  return false;
+}
+
+// One warp per query row: 4 consecutive blocks per lane per step, one 32-bit
+// store (4-byte aligned rows) or four byte stores.  A row without a candidate
+// is rewritten with ones when `fallback` (the reference's per-query fallback).
+constexpr int kCandWarps = 8;
+__global__ void __launch_bounds__(kCandWarps * 32) page_cand_kernel(const PgCand a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kCandWarps + (threadIdx.x >> 5);
+  const int64_t b = blockIdx.y;
+  if (i >= a.cq) return;
+  uint8_t* row = a.out + (b * a.cq + i) * a.nblk;
+  const bool w32 = (a.nblk & 3) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 3) == 0;
+  int64_t qp = 0;
+  if (!a.flat) {
+    int64_t p = __ldg(a.pos + b * a.s_pos + i);
+    p = p < 0 ? 0 : (p > a.n_q - 1 ? a.n_q - 1 : p);
+    qp = __ldg(a.qpi + b * a.s_qpi + p);
+  }
+  bool any = false;
+  if (a.flat || qp >= 0) {
+    const int4* dr = a.desc + b * a.nblk;
+    for (int64_t c0 = 4 * lane; c0 < a.nblk; c0 += 128) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t c = c0 + e;
+        if (c < a.nblk) {
+          const int4 d = __ldg(dr + c);
+          const bool y = a.flat ? d.x >= 0 : block_has_page(a, b, c, d, qp);
+          word |= static_cast<uint32_t>(y) << (8 * e);
+        }
+      }
+      any |= word != 0;
+      if (w32) {
+        *reinterpret_cast<uint32_t*>(row + c0) = word;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (c0 + e < a.nblk) row[c0 + e] = static_cast<uint8_t>(word >> (8 * e));
+      }
+    }
+  }
+  any = __any_sync(0xffffffffu, any);
+  if (any) return;
+  const uint8_t fill = a.fallback ? 1 : 0;
+  if (!a.flat && qp >= 0 && !a.fallback) return;  // zeros already written
+  for (int64_t c = lane; c < a.nblk; c += 32) row[c] = fill;
+}
+
+// Decode allow of one new token per request: advances the marker count, then
+// allow[c] = (c < nblk_state and block c holds image pages [bmin, bmax] around
+// the query page) or the row is open (no page / no such block).  One CTA per
+// request.
+__global__ void __launch_bounds__(256) decode_allow_kernel(const int64_t* last_ids, int64_t s_ids, int64_t page_id,
+                                                           const int64_t* bmin, const int64_t* bmax, int64_t s_state,
+                                                           int64_t nblk_state, const int64_t* pp, int64_t* mcum,
+                                                           int64_t nblk, uint8_t* allow) {
+  __shared__ int64_t qps;
+  const int64_t b = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const int64_t m = mcum[b] + (__ldg(last_ids + b * s_ids) == page_id ? 1 : 0);
+    const int64_t q = m - 1 - pp[b];
+    qps = q >= 0 ? q : -1;
+    mcum[b] = m;
+  }
+  __syncthreads();
+  const int64_t qp = qps;
+  const int64_t n0 = min(nblk, nblk_state);
+  const int64_t* mn = bmin + b * s_state;
+  const int64_t* mx = bmax + b * s_state;
+  int any = 0;
+  if (qp >= 0)
+    for (int64_t c = threadIdx.x; c < n0; c += blockDim.x) {
+      const int64_t lo = __ldg(mn + c);
+      any |= (lo >= 0 && lo <= qp && __ldg(mx + c) >= qp);
+    }
+  any = __syncthreads_or(any);
+  const bool open = qp < 0 || !any;
+  uint8_t* out = allow + b * nblk;
+  for (int64_t c = threadIdx.x; c < nblk; c += blockDim.x) {
+    bool y = open;
+    if (!y && c < n0) {
+      const int64_t lo = __ldg(mn + c);
+      y = lo >= 0 && lo <= qp && __ldg(mx + c) >= qp;
+    }
+    out[c] = y;
+  }
+}
+
+}  // namespace srswa
+
+using namespace srswa;
+
+extern "C" size_t srswa_page_scan_workspace_size(int64_t B, int64_t n_tok) {
+  if (B <= 0 || n_tok <= 0) return 0;
+  return static_cast<size_t>(B) * static_cast<size_t>(cdiv<int64_t>(n_tok, kPgChunk)) * sizeof(int4);
+}
+
+static int page_scan_launch(const PgRow& r, int64_t B, int mode, const PgOut& o, void* ws, size_t ws_bytes,
+                            cudaStream_t s) {
+  const int64_t nchunk = cdiv<int64_t>(r.n_tok, kPgChunk);
+  SRSWA_CHECK_ARG(nchunk <= INT32_MAX && B <= 65535, SRSWA_ETOOLARGE);
+  SRSWA_CHECK_ARG(ws && ws_bytes >= srswa_page_scan_workspace_size(B, r.n_tok), SRSWA_EWORKSPACE);
+  SRSWA_CHECK_ARG((reinterpret_cast<uintptr_t>(ws) & 15) == 0, SRSWA_EALIGN);
+  int4* stats = static_cast<int4*>(ws);
+  const dim3 grid(static_cast<unsigned>(nchunk), static_cast<unsigned>(B));
+  page_count_kernel<<<grid, kPgThreads, 0, s>>>(r, nchunk, stats);
+  if (mode == 0) page_scan_kernel<0><<<grid, kPgThreads, 0, s>>>(r, nchunk, stats, o);
+  else page_scan_kernel<1><<<grid, kPgThreads, 0, s>>>(r, nchunk, stats, o);
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_page_ids(const int64_t* ids, int64_t s_row, int64_t B, int64_t n_ids, int64_t key_length,
+                              int64_t img_id, int64_t page_id, int64_t per_page, int page_scope_prefill,
+                              uint8_t* itm, int64_t* ipi, int64_t* qpi, int32_t* flags, void* workspace,
+                              size_t workspace_bytes, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(ids && itm && ipi && qpi && flags && B >= 0 && n_ids >= 0 && key_length >= 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(s_row >= n_ids || B <= 1, SRSWA_EINVAL);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  SRSWA_CUDA_TRY(cudaMemsetAsync(flags, 0, 2 * sizeof(int32_t), s));
+  if (B * key_length == 0) return 0;
+  PgRow r = {ids, s_row, n_ids, key_length, img_id, page_id, per_page < 1 ? 1 : per_page};
+  PgOut o = {};
+  o.itm = itm; o.ipi = ipi; o.qpi = qpi; o.flags = flags; o.scope = page_scope_prefill ? 1 : 0;
+  return page_scan_launch(r, B, 0, o, workspace, workspace_bytes, s);
+}
+
+extern "C" int srswa_decode_allow_state(const int64_t* ids, int64_t s_row, int64_t B, int64_t L, int64_t img_id,
+                                        int64_t page_id, int64_t per_page, int64_t block_size, int64_t* bmin,
+                                        int64_t* bmax, int64_t* pp, int64_t* mcum, void* workspace,
+                                        size_t workspace_bytes, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(ids && bmin && bmax && pp && mcum && B >= 0 && L > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(s_row >= L || B <= 1, SRSWA_EINVAL);
+  // per-block reductions stay inside one chunk: the block size must divide it
+  SRSWA_CHECK_ARG(block_size > 0 && block_size <= kPgChunk && kPgChunk % block_size == 0, SRSWA_EUNSUPPORTED);
+  if (B == 0) return 0;
+  PgRow r = {ids, s_row, L, L, img_id, page_id, per_page < 1 ? 1 : per_page};
+  PgOut o = {};
+  o.bmin = bmin; o.bmax = bmax; o.pp = pp; o.mcum = mcum; o.bs = block_size; o.nblk = cdiv<int64_t>(L, block_size);
+  return page_scan_launch(r, B, 1, o, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int srswa_page_block_desc(const int64_t* ipi, const uint8_t* itm, int64_t s_row, int64_t B,
+                                     int64_t n_tok, int64_t block_size, int64_t nblk, int32_t* desc,
+                                     srswa_stream_t stream) {
+  SRSWA_CHECK_ARG((ipi != nullptr) != (itm != nullptr) && desc && B >= 0 && n_tok >= 0 && nblk >= 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(block_size > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG((reinterpret_cast<uintptr_t>(desc) & 15) == 0, SRSWA_EALIGN);
+  const int64_t warps = B * nblk;
+  if (warps == 0) return 0;
+  SRSWA_CHECK_ARG(cdiv<int64_t>(warps, 8) <= INT32_MAX, SRSWA_ETOOLARGE);
+  page_block_desc_kernel<<<static_cast<unsigned>(cdiv<int64_t>(warps, 8)), 256, 0,
+                           reinterpret_cast<cudaStream_t>(stream)>>>(ipi, itm, s_row, n_tok, block_size, nblk, B,
+                                                                     reinterpret_cast<int4*>(desc));
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_page_cand_mask(const int32_t* desc, const int64_t* ipi, int64_t s_ipi, int64_t n_tok,
+                                    int64_t block_size, int64_t B, int64_t nblk, const int64_t* qpi, int64_t s_qpi,
+                                    int64_t n_q, const int64_t* pos, int64_t s_pos, int64_t cq, int flat,
+                                    int fallback, uint8_t* cand, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(desc && cand && B >= 0 && nblk >= 0 && cq >= 0 && block_size > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(flat || (ipi && qpi && pos && n_q > 0), SRSWA_EINVAL);
+  SRSWA_CHECK_ARG((reinterpret_cast<uintptr_t>(desc) & 15) == 0, SRSWA_EALIGN);
+  if (B * cq * nblk == 0) return 0;
+  SRSWA_CHECK_ARG(B <= 65535 && cdiv<int64_t>(cq, kCandWarps) <= INT32_MAX, SRSWA_ETOOLARGE);
+  PgCand a = {};
+  a.desc = reinterpret_cast<const int4*>(desc); a.ipi = ipi; a.s_ipi = s_ipi; a.n_tok = n_tok; a.bs = block_size;
+  a.B = B; a.nblk = nblk; a.qpi = qpi; a.s_qpi = s_qpi; a.n_q = n_q; a.pos = pos; a.s_pos = s_pos; a.cq = cq;
+  a.flat = flat ? 1 : 0; a.fallback = fallback ? 1 : 0; a.out = cand;
+  const dim3 grid(static_cast<unsigned>(cdiv<int64_t>(cq, kCandWarps)), static_cast<unsigned>(B));
+  page_cand_kernel<<<grid, kCandWarps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_decode_allow(const int64_t* last_ids, int64_t s_ids, int64_t B, int64_t page_id,
+                                  const int64_t* bmin, const int64_t* bmax, int64_t s_state, int64_t nblk_state,
+                                  const int64_t* pp, int64_t* mcum, int64_t nblk, uint8_t* allow,
+                                  srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(last_ids && bmin && bmax && pp && mcum && allow && B >= 0 && nblk >= 0 && nblk_state >= 0,
+                  SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(s_state >= nblk_state || B <= 1, SRSWA_EINVAL);
+  if (B == 0) return 0;
+  SRSWA_CHECK_ARG(B <= INT32_MAX, SRSWA_ETOOLARGE);
+  decode_allow_kernel<<<static_cast<unsigned>(B), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      last_ids, s_ids, page_id, bmin, bmax, s_state, nblk_state, pp, mcum, nblk, allow);
+  return srswa_last_launch_status();
+}

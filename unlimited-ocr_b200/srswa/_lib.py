@@ -77,6 +77,15 @@ _SIGS = {
                                       vp]),
     "srswa_device_status": (C.c_int, [C.POINTER(C.c_int)]),
     "srswa_lse_merge": (C.c_int, [vp, vp, i64, i64, i64, i64, i64, i64, vp, C.c_int, vp, vp]),
+    "srswa_page_scan_workspace_size": (C.c_size_t, [i64, i64]),
+    "srswa_page_ids": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, C.c_int, vp, vp, vp, vp, vp,
+                                 C.c_size_t, vp]),
+    "srswa_page_block_desc": (C.c_int, [vp, vp, i64, i64, i64, i64, i64, vp, vp]),
+    "srswa_page_cand_mask": (C.c_int, [vp, vp, i64, i64, i64, i64, i64, vp, i64, i64, vp, i64, i64, C.c_int,
+                                       C.c_int, vp, vp]),
+    "srswa_decode_allow_state": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp,
+                                           C.c_size_t, vp]),
+    "srswa_decode_allow": (C.c_int, [vp, i64, i64, i64, vp, vp, i64, i64, vp, vp, i64, vp, vp]),
 }
 
 _lib = None

@@ -8,6 +8,9 @@ After ``install``:
   * ``<pkg>.sparse_gather_e2e_triton``  -> ``srswa.sparse_gather_e2e``
   * ``<pkg>.modeling_deepseekv2._block_scores_infer / _infer_route_select /
     _decode_attend`` -> ``srswa.dash_infer`` (when that module is loaded)
+  * the PageGate candidate methods of ``<pkg>._sparse_base_impl.DeepseekV2Indexer``,
+    ``modeling_deepseekv2._dash_block_cand`` and
+    ``modeling_unlimitedocr._uocr_dash_decode_allow`` -> ``srswa.page_gate``
 so DashAttention._forward_triton, SlidingWindowLlamaAttention's sparse branch,
 the DSA indexer and the DASH inference overlay call the CUDA kernels without a
 source change.  ``install_sglang()`` does the same for the SGLang ops modules.
@@ -17,7 +20,10 @@ from __future__ import annotations
 
 import sys
 
-from . import dash_infer, paged, sparse_gather, sparse_gather_e2e
+from . import dash_infer, page_gate, paged, sparse_gather, sparse_gather_e2e
+
+_INDEXER_METHODS = ("_build_page_aware_ids", "_build_flat_image_token_mask", "_build_image_block_allow_mask",
+                    "_build_page_aware_image_block_mask", "_build_kl_candidate_mask")
 
 
 def install(pkg: str) -> None:
@@ -31,6 +37,17 @@ def install(pkg: str) -> None:
     if md is not None:
         for name in ("_block_scores_infer", "_infer_route_select", "_decode_attend"):
             setattr(md, name, getattr(dash_infer, name))
+        md._dash_block_cand = page_gate._dash_block_cand
+    base = sys.modules.get(f"{pkg}._sparse_base_impl")
+    if base is not None:
+        ix = getattr(base, "DeepseekV2Indexer", None)
+        if ix is not None:
+            for name in _INDEXER_METHODS:
+                setattr(ix, name, getattr(page_gate, name))
+        page_gate._scope_source = base      # _PAGE_SCOPE_PREFILL stays the reference's switch
+    mu = sys.modules.get(f"{pkg}.modeling_unlimitedocr")
+    if mu is not None:
+        mu._uocr_dash_decode_allow = page_gate._uocr_dash_decode_allow
 
 
 def install_sglang(prefix: str = "sglang.srt.layers.attention.unlimited_dash_ops") -> None:

@@ -18,7 +18,9 @@ def _cand_args(cand, N, nblk):
     if cand is None:
         return None, 0
     c = cand
-    if c.dtype != torch.uint8:
+    if c.dtype == torch.bool:
+        c = c.view(torch.uint8)
+    elif c.dtype != torch.uint8:
         c = c.to(torch.uint8)
     if c.dim() == 1:
         return c.contiguous(), 0
@@ -412,3 +414,108 @@ def lse_merge(o_parts, lse_parts, out_dtype=torch.float32, out=None, lse=None):
 
 
 INV_SQRT = lambda d: 1.0 / math.sqrt(d)  # noqa: E731
+
+
+# ------------------------------------------------------------------ PageGate
+def _ids64(ids: torch.Tensor) -> torch.Tensor:
+    if ids.dtype != torch.int64 or ids.stride(-1) != 1:
+        ids = ids.to(torch.int64).contiguous()
+    return ids
+
+
+def page_ids(ids, img_id, page_id, key_length, per_page, page_scope_prefill):
+    """ids [B, n] int -> (itm bool [B, key_length], ipi int64, qpi int64,
+    flags int32 [2] on the device: any image token, any query page)."""
+    ids = _ids64(ids)
+    B, n = ids.shape
+    dev = ids.device
+    itm = torch.empty(B, key_length, device=dev, dtype=torch.bool)
+    ipi = torch.empty(B, key_length, device=dev, dtype=torch.int64)
+    qpi = torch.empty(B, key_length, device=dev, dtype=torch.int64)
+    flags = torch.empty(2, device=dev, dtype=torch.int32)
+    wsb = L.lib().srswa_page_scan_workspace_size(B, key_length)
+    ws = torch.empty(max(wsb, 16), device=dev, dtype=torch.uint8)
+    rc = L.lib().srswa_page_ids(ids.data_ptr(), ids.stride(0), B, n, key_length, int(img_id), int(page_id),
+                                int(per_page), 1 if page_scope_prefill else 0, itm.data_ptr(), ipi.data_ptr(),
+                                qpi.data_ptr(), flags.data_ptr(), ws.data_ptr(), wsb, L.stream_of(ids))
+    L.check(rc, "srswa_page_ids")
+    return itm, ipi, qpi, flags
+
+
+def page_block_desc(nblk, block_size, ipi=None, itm=None):
+    """Block descriptors [B, nblk, 4] int32 from page ids ipi [B, n] int64 or
+    (flat) an image-token mask itm [B, n] bool."""
+    src = ipi if ipi is not None else itm
+    if (ipi is None) == (itm is None):
+        raise ValueError("page_block_desc: pass exactly one of ipi / itm")
+    if ipi is not None:
+        src = ipi = _ids64(ipi)
+    else:
+        src = itm = (itm if itm.dtype == torch.bool else itm.bool()).contiguous()
+    B, n = src.shape
+    desc = torch.empty(B, nblk, 4, device=src.device, dtype=torch.int32)
+    rc = L.lib().srswa_page_block_desc(L.ptr(ipi), None if itm is None else itm.view(torch.uint8).data_ptr(),
+                                       src.stride(0), B, n, int(block_size), int(nblk), desc.data_ptr(),
+                                       L.stream_of(src))
+    L.check(rc, "srswa_page_block_desc")
+    return desc
+
+
+def page_cand_mask(desc, block_size, pos=None, qpi=None, ipi=None, flat=False, fallback=True, out=None, cq=None):
+    """Candidate mask [B, cq, nblk] bool: block c of row b is a candidate for
+    query i when it holds an image token of page qpi[b, clamp(pos[b, i])]
+    (flat: any image token, cq rows); fallback: a query without one gets
+    every block."""
+    B, nblk, _ = desc.shape
+    if flat:
+        cq = int(cq) if cq is not None else (pos.shape[1] if pos is not None else 1)
+        pos = qpi = ipi = None
+        n_tok = n_q = 0
+        s_ipi = s_qpi = s_pos = 0
+    else:
+        pos, qpi, ipi = _ids64(pos), _ids64(qpi), _ids64(ipi)
+        cq, n_q, n_tok = pos.shape[1], qpi.shape[1], ipi.shape[1]
+        s_ipi, s_qpi, s_pos = ipi.stride(0), qpi.stride(0), pos.stride(0)
+    if out is None:
+        out = torch.empty(B, cq, nblk, device=desc.device, dtype=torch.bool)
+    assert out.is_contiguous() and out.shape == (B, cq, nblk)
+    rc = L.lib().srswa_page_cand_mask(desc.data_ptr(), L.ptr(ipi), s_ipi, n_tok, int(block_size), B, nblk,
+                                      L.ptr(qpi), s_qpi, n_q, L.ptr(pos), s_pos, cq, 1 if flat else 0,
+                                      1 if fallback else 0, out.view(torch.uint8).data_ptr(), L.stream_of(desc))
+    L.check(rc, "srswa_page_cand_mask")
+    return out
+
+
+def decode_allow_state(ids, img_id, page_id, per_page, block_size):
+    """Prefill ids [B, L] -> dict(bmin, bmax [B, ceil(L/bs)] int64, pp, mcum [B] int64)."""
+    ids = _ids64(ids)
+    B, Lk = ids.shape
+    dev = ids.device
+    nblk = -(-Lk // int(block_size))
+    st = dict(bmin=torch.empty(B, nblk, device=dev, dtype=torch.int64),
+              bmax=torch.empty(B, nblk, device=dev, dtype=torch.int64),
+              pp=torch.empty(B, device=dev, dtype=torch.int64), mcum=torch.empty(B, device=dev, dtype=torch.int64))
+    wsb = L.lib().srswa_page_scan_workspace_size(B, Lk)
+    ws = torch.empty(max(wsb, 16), device=dev, dtype=torch.uint8)
+    rc = L.lib().srswa_decode_allow_state(ids.data_ptr(), ids.stride(0), B, Lk, int(img_id), int(page_id),
+                                          int(per_page), int(block_size), st["bmin"].data_ptr(),
+                                          st["bmax"].data_ptr(), st["pp"].data_ptr(), st["mcum"].data_ptr(),
+                                          ws.data_ptr(), wsb, L.stream_of(ids))
+    L.check(rc, "srswa_decode_allow_state")
+    return st
+
+
+def decode_allow(state, last_ids, page_id, nblk, out=None):
+    """One decode token per request: advances state['mcum'] in place and
+    returns allow [B, nblk] bool."""
+    last_ids = _ids64(last_ids.reshape(last_ids.shape[0], -1))
+    bmin, bmax = state["bmin"], state["bmax"]
+    B = bmin.shape[0]
+    if out is None:
+        out = torch.empty(B, nblk, device=bmin.device, dtype=torch.bool)
+    rc = L.lib().srswa_decode_allow(last_ids[:, -1:].data_ptr(), last_ids.stride(0), B, int(page_id),
+                                    bmin.data_ptr(), bmax.data_ptr(), bmin.stride(0), bmin.shape[1],
+                                    state["pp"].data_ptr(), state["mcum"].data_ptr(), int(nblk),
+                                    out.view(torch.uint8).data_ptr(), L.stream_of(bmin))
+    L.check(rc, "srswa_decode_allow")
+    return out
