@@ -473,6 +473,94 @@ def case_page_gate(m):
     save("page_gate", **outs)
 
 
+def case_page_rope(m):
+    """page2d RoPE: _build_page_rope_pos (+ _page_rope_offsets, span 0 / 64),
+    DeepseekV2IndexerRotary2D.forward (bf16 and fp32 tables, two configs),
+    the rotary application of the DASH router, and the decode branch of
+    SlidingWindowLlamaAttention._main_rope_coords."""
+    base = importlib.import_module("uocr_ref._sparse_base_impl")
+    Ix, Rot, Attn = base.DeepseekV2Indexer, base.DeepseekV2IndexerRotary2D, base.SlidingWindowLlamaAttention
+    g = torch.Generator().manual_seed(31)
+    rows = page_gate_rows(g, 7)
+    # marker-mode rows only (the reference bails on a batch with a row without
+    # prompt markers): row 0, row 2, and a row whose response has more pages
+    # than its prompt
+    r3 = [0] + [PAGE_MARK] + [PAGE_IMG] * 40 + [PAGE_MARK] + [PAGE_IMG] * 33 + [5] * 30
+    for _ in range(8):
+        r3 += [PAGE_MARK] + [9] * int(torch.randint(5, 40, (1,), generator=g))
+    S = max(rows.shape[1], len(r3))
+    ids = torch.full((3, S), 7, dtype=torch.long)
+    ids[0, :rows.shape[1]] = rows[0]
+    ids[1, :rows.shape[1]] = rows[2]
+    ids[2, :len(r3)] = torch.tensor(r3)
+    outs = dict(ids=ids, bail_ids=rows[:2].clone(), text_ids=rows[3:].clone())
+
+    def indexer(span):
+        rot = Rot(128, 10000.0, 256.0, 1, tok_freq_mode="resample", page_mod=2)
+        ns = types.SimpleNamespace(image_token_id=PAGE_IMG, page_token_id=PAGE_MARK, rope_page_span=span,
+                                   rotary_emb_2d=rot, layer_idx=0, _page_rope_diag_logged=True,
+                                   _page_rope_bail_logged=True,
+                                   q_proj=types.SimpleNamespace(weight=torch.zeros(1)))
+        for fn in ("_build_page_rope_pos", "_page_rope_offsets", "_page_rope_bail"):
+            setattr(ns, fn, types.MethodType(getattr(Ix, fn), ns))
+        return ns
+
+    for span in (0, 64):
+        for tag, kl in (("full", S), ("trunc", S - 20), ("pad", S + 30)):
+            ix = indexer(span)
+            tok, page = ix._build_page_rope_pos(ids, kl)
+            outs[f"tok_sp{span}_{tag}"], outs[f"page_sp{span}_{tag}"] = tok, page
+            outs[f"pfcnt_sp{span}_{tag}"] = ix._page_rope_meta["pf_cnt"]
+    outs["bail"] = np.array([indexer(0)._build_page_rope_pos(outs["bail_ids"], S) is None,
+                             indexer(0)._build_page_rope_pos(outs["text_ids"], S) is None])
+    # rotary tables (two configs, bf16 and fp32) and the router's application
+    # (tables at every 5th position, first half only: the second repeats it;
+    # bf16 values stored as their 16-bit patterns)
+    tok, page = outs["tok_sp0_full"], outs["page_sp0_full"]
+    sub = torch.arange(0, S, 5)
+    b16 = lambda x: x.contiguous().view(torch.int16)  # noqa: E731
+    outs["rot_sub"] = sub
+    for ci, (bt, bp, pairs, mode, pmod) in enumerate(((10000.0, 256.0, 1, "resample", 2),
+                                                      (500000.0, 256.0, 8, "truncate", 0))):
+        rot = Rot(128, bt, bp, pairs, tok_freq_mode=mode, page_mod=pmod)
+        outs[f"rot{ci}_inv_tok"], outs[f"rot{ci}_inv_page"] = rot.inv_tok.clone(), rot.inv_page.clone()
+        for dt in (torch.bfloat16, torch.float32):
+            cos, sin = rot(torch.zeros(1, dtype=dt), tok, page)
+            cos, sin = cos[:, sub, :64], sin[:, sub, :64]
+            if dt == torch.bfloat16:
+                outs[f"rot{ci}_cos_bf16"], outs[f"rot{ci}_sin_bf16"] = b16(cos), b16(sin)
+            else:
+                outs[f"rot{ci}_cos_f32"], outs[f"rot{ci}_sin_f32"] = cos, sin
+    cos, sin = Rot(128, 10000.0, 256.0, 1, tok_freq_mode="resample", page_mod=2)(
+        torch.zeros(1, dtype=torch.bfloat16), tok, page)
+    P = 200                                  # the router's application on the first 200 positions
+    qx = torch.randn(3, 2, P, 128, generator=g).to(torch.bfloat16)
+    kx = torch.randn(3, 1, P, 128, generator=g).to(torch.bfloat16)
+    qe, ke = base._llama_apply_rotary_pos_emb(qx, kx, cos[:, :P], sin[:, :P])
+    outs.update(qx=b16(qx), kx=b16(kx), qe=b16(qe), ke=b16(ke))
+    # decode coordinates: prefill state, then 20 tokens (markers at steps 3, 9, 10)
+    ix = indexer(0)
+    attn = types.SimpleNamespace(indexer=ix, layer_idx=0, _main_rope_pos_2d=None, _sparse_source_input_ids=ids)
+    kv = types.SimpleNamespace()
+    coords = Attn._main_rope_coords(attn, S, kv)
+    st0 = kv._page_rope_state[0]
+    outs.update(dec_page0=st0["page"].clone(), dec_tok0=st0["tok"].clone(), dec_pfcnt=st0["pf_cnt"],
+                dec_npg=np.array(st0["n_pg"]))
+    steps = torch.randint(0, 1000, (3, 20), generator=g)
+    steps[:, 3] = PAGE_MARK
+    steps[0, 9] = PAGE_MARK
+    steps[1, 10] = PAGE_MARK
+    steps[2, 9:15] = PAGE_MARK           # past the last page: clamped to n_pg - 1
+    toks, pages = [], []
+    for k_ in range(steps.shape[1]):
+        attn._sparse_source_input_ids = steps[:, k_:k_ + 1]
+        t_, p_ = Attn._main_rope_coords(attn, 1, kv)
+        toks.append(t_[:, 0].clone())
+        pages.append(p_[:, 0].clone())
+    outs.update(dec_steps=steps, dec_tok=torch.stack(toks), dec_page=torch.stack(pages))
+    save("page_rope", **outs)
+
+
 def main():
     only = sys.argv[1:]
     m = import_reference()
@@ -491,6 +579,7 @@ def main():
     case_block_max(m)
     case_paged(sgl)
     case_page_gate(m)
+    case_page_rope(m)
 
 
 if __name__ == "__main__":

@@ -261,3 +261,57 @@ def test_page_gate_decode_allow_golden(bs):
         n += 1
         assert allow.shape[1] == nb
         np.testing.assert_array_equal(allow, g[f"dec_bs{bs}_allow"][k][:, :nb])
+
+
+# ---------------------------------------------------------------- page2d RoPE
+def _bf16_bits(a):
+    return (np.asarray(a).astype(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def test_page_rope_pos_golden():
+    from oracle import page_rope as PR
+    g = golden("page_rope")
+    ids = g["ids"]
+    S = ids.shape[1]
+    for span in (0, 64):
+        for tag, kl in (("full", S), ("trunc", S - 20), ("pad", S + 30)):
+            tok, page, pf, n_pg = PR.page_rope_pos(ids, 128815, 128827, kl, span)
+            np.testing.assert_array_equal(tok, g[f"tok_sp{span}_{tag}"])
+            np.testing.assert_array_equal(page, g[f"page_sp{span}_{tag}"])
+            np.testing.assert_array_equal(pf, g[f"pfcnt_sp{span}_{tag}"])
+    assert g["bail"].all()
+    assert PR.page_rope_pos(g["bail_ids"], 128815, 128827, S) is None
+    assert PR.page_rope_pos(g["text_ids"], 128815, 128827, S) is None
+
+
+def test_page_rope_tables_and_apply_golden():
+    from oracle import page_rope as PR
+    g = golden("page_rope")
+    tok, page, sub = g["tok_sp0_full"], g["page_sp0_full"], g["rot_sub"]
+    for ci, (bt, bp, pairs, mode, pmod) in enumerate(((10000.0, 256.0, 1, "resample", 2),
+                                                      (500000.0, 256.0, 8, "truncate", 0))):
+        it, ip = PR.rotary2d_inv_freq(128, bt, bp, pairs, mode)
+        np.testing.assert_allclose(it, g[f"rot{ci}_inv_tok"], rtol=2e-6)
+        np.testing.assert_allclose(ip, g[f"rot{ci}_inv_page"], rtol=2e-6)
+        cos, sin = PR.rotary2d_cos_sin(tok, page, g[f"rot{ci}_inv_tok"], g[f"rot{ci}_inv_page"], pmod)
+        np.testing.assert_allclose(cos[:, sub, :64], g[f"rot{ci}_cos_f32"], atol=2e-6)
+        np.testing.assert_allclose(sin[:, sub, :64], g[f"rot{ci}_sin_f32"], atol=2e-6)
+        np.testing.assert_allclose(cos[:, sub, :64], _bf16_bits(g[f"rot{ci}_cos_bf16"]), atol=4e-3)
+    cos, sin = PR.rotary2d_cos_sin(tok, page, g["rot0_inv_tok"], g["rot0_inv_page"], 2)
+    P = g["qx"].shape[2]
+    q = PR.apply_rotary(_bf16_bits(g["qx"]), cos[:, :P], sin[:, :P])
+    np.testing.assert_allclose(q, _bf16_bits(g["qe"]), atol=2e-2, rtol=1e-2)
+
+
+def test_page_rope_decode_golden():
+    from oracle import page_rope as PR
+    g = golden("page_rope")
+    st = dict(page=g["dec_page0"], tok=g["dec_tok0"], pf_cnt=g["dec_pfcnt"], n_pg=int(g["dec_npg"]))
+    tok, page, pf, n_pg = PR.page_rope_pos(g["ids"], 128815, 128827, g["ids"].shape[1])
+    np.testing.assert_array_equal(st["page"], page[:, -1])
+    np.testing.assert_array_equal(st["tok"], tok[:, -1])
+    assert n_pg == st["n_pg"]
+    for k in range(g["dec_steps"].shape[1]):
+        st = PR.decode_coords_step(st, g["dec_steps"][:, k], 128827)
+        np.testing.assert_array_equal(st["tok"], g["dec_tok"][k])
+        np.testing.assert_array_equal(st["page"], g["dec_page"][k])
