@@ -229,14 +229,18 @@ def build_rank(S_local, seed, dev):
     return st
 
 
-def run_step(st):
-    """One decode step through the library (device-resident inputs)."""
-    from srswa import ops
-    ops.kbar_paged(st["idx"], st["hc"], st["bt"], st["sl"], st["kbar"], tail_pages=1)
-    r = ops.route(st["iq"], st["kbar"], block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=IDX_SCALE,
-                  floor=FLOOR, sigma=SIGMA, seq_lens=st["sl"], block_table=st["bt"], want=("topi32", "bias"))
-    st["topi"], st["bias"] = r["topi32"], r["bias"]
-    run_attend(st)
+STEP_LAUNCHES = 6   # k_bar refresh, router scores + selection, window attend, selected-block attend, merge
+
+
+def run_step(st, q=None, iq=None):
+    """One decode step through the public paged API (device-resident inputs):
+    k_bar tail refresh + route + attend, the window half of the attend
+    overlapped with the router (srswa.paged.decode_step)."""
+    from srswa import paged
+    st["topi"], st["bias"] = paged.decode_step(
+        st["q"] if q is None else q, st["k"], st["v"], st["iq"] if iq is None else iq, st["kbar"], st["bt"],
+        st["sl"], st["out"], sm_scale=SM_SCALE, local_blocks=L, sparse_block_size=BS, idx_scale=IDX_SCALE,
+        prior_floor=FLOOR, sigma=SIGMA, topm=M, budget=K, idx_cache=st["idx"], head_cls=st["hc"], tail_pages=1)
 
 
 def run_attend(st):
@@ -791,8 +795,10 @@ def main():
             "cpu_baseline": cpu,
             "e2e": None if e2e is None else {
                 "value": bytes_all / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+                "how": "pinned H2D of the step's inputs, cache append, srswa.paged.decode_step, D2H of the "
+                       "output; one CUDA graph per step",
                 "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": STEP_LAUNCHES * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -803,60 +809,67 @@ def main():
 
 
 def e2e_measure(st, S_local, args, dev):
-    """Per step: H2D of this step's q, idx_q, the new token's K/V/index-key
-    rows and its cache slot (pinned host buffers), append to the paged caches,
-    then k_bar refresh, route_decode and dash_sparse_attn_decode through the
-    public paged API, D2H of the output."""
+    """Per step: one H2D copy of this step's inputs packed in a pinned host
+    buffer (q, idx_q, the new token's K / V / index-key rows and its cache
+    slot), the append to the paged caches, the decode step through the public
+    paged API (srswa.paged.decode_step), and the D2H copy of the output; the
+    step is captured once in a CUDA graph (as a serving loop's decode step)
+    and replayed, copies included."""
     from srswa import paged
     R = len(S_local)
     g = torch.Generator().manual_seed(77)
-    hq = torch.randn(R, H, D, generator=g).to(torch.bfloat16).pin_memory()
-    hiq = torch.randn(R, DI, generator=g).to(torch.bfloat16).float().pin_memory()
-    hk = torch.randn(R, HKV, D, generator=g).to(torch.bfloat16).pin_memory()
-    hv = torch.randn(R, HKV, D, generator=g).to(torch.bfloat16).pin_memory()
-    hik = torch.randn(R, DI, generator=g).to(torch.bfloat16).pin_memory()
+    hq = torch.randn(R, H, D, generator=g).to(torch.bfloat16)
+    hiq = torch.randn(R, DI, generator=g).to(torch.bfloat16).float()
+    hk = torch.randn(R, HKV, D, generator=g).to(torch.bfloat16)
+    hv = torch.randn(R, HKV, D, generator=g).to(torch.bfloat16)
+    hik = torch.randn(R, DI, generator=g).to(torch.bfloat16)
     bt = st["bt"].cpu()
     page = torch.tensor([int(bt[r, (s - 1) // BS]) for r, s in enumerate(S_local)], dtype=torch.int64)
     slot = torch.tensor([(s - 1) % BS for s in S_local], dtype=torch.int64)
-    hslot = torch.stack([page, slot]).pin_memory()
+    hslot = torch.stack([page, slot])
+    parts = [hq, hiq, hk, hv, hik, hslot]
+    raw = [x.contiguous().view(-1).view(torch.uint8) for x in parts]
+    hin = torch.cat(raw).pin_memory()                      # one pinned buffer, one H2D copy per step
+    din = torch.empty_like(hin, device=dev)
+    views, o = [], 0
+    for x, r_ in zip(parts, raw):
+        views.append(din[o:o + r_.numel()].view(x.dtype).view(x.shape))
+        o += r_.numel()
+    q, iq, nk, nv, nik, sl_ = views
     hout = torch.empty(R, H, D, dtype=torch.bfloat16).pin_memory()
-    q, iq = torch.empty_like(hq, device=dev), torch.empty_like(hiq, device=dev)
-    nk, nv, nik = (torch.empty_like(x, device=dev) for x in (hk, hv, hik))
-    sl_ = torch.empty_like(hslot, device=dev)
-    out = torch.empty(R, H, D, dtype=torch.bfloat16, device=dev)
-    idx_buf = torch.empty(R, M, dtype=torch.int32, device=dev)
-    bias_buf = torch.empty(R, M, dtype=torch.float32, device=dev)
-    h2d = sum(x.numel() * x.element_size() for x in (hq, hiq, hk, hv, hik, hslot))
+    h2d = hin.numel()
     d2h = hout.numel() * hout.element_size()
 
     def step():
-        for d_, h_ in ((q, hq), (iq, hiq), (nk, hk), (nv, hv), (nik, hik), (sl_, hslot)):
-            d_.copy_(h_, non_blocking=True)
+        din.copy_(hin, non_blocking=True)
         st["k"][sl_[0], sl_[1]] = nk
         st["v"][sl_[0], sl_[1]] = nv
         st["idx"][sl_[0], sl_[1]] = nik
-        paged.kbar_refresh_tail(kv_cache=st["idx"], k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"],
-                                head_cls=st["hc"], block_size=BS, tail_pages=1)
-        w = paged.route_decode(idx_q=iq, k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"],
-                               image_allow=None, out_idx=idx_buf, out_bias=bias_buf, max_block=st["bt"].shape[1],
-                               block_size=BS, local_blocks=L, decode_query_len=1, idx_scale=IDX_SCALE,
-                               prior_floor=FLOOR, sigma=SIGMA, topm=M, budget=K)
-        ti = idx_buf[:, :w].unsqueeze(0).expand(HKV, -1, -1)
-        tb = bias_buf[:, :w].unsqueeze(0).expand(HKV, -1, -1)
-        paged.dash_sparse_attn_decode(q, st["k"], st["v"], ti, tb, st["bt"], st["sl"], HKV, SM_SCALE, out, 1,
-                                      local_blocks=L, sparse_block_size=BS)
-        hout.copy_(out, non_blocking=True)
+        run_step(st, q=q, iq=iq)
+        hout.copy_(st["out"], non_blocking=True)
 
-    for _ in range(max(args.warmup, 1)):
+    s_ = torch.cuda.Stream()
+    s_.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s_):
+        for _ in range(max(args.warmup, 1)):
+            step()
+    torch.cuda.current_stream().wait_stream(s_)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
         step()
+    for _ in range(max(args.warmup, 1)):
+        graph.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        step()
+        graph.replay()
     e1.record()
     torch.cuda.synchronize()
-    return {"ms": e0.elapsed_time(e1) / args.steps, "h2d": h2d, "d2h": d2h}
+    ms = e0.elapsed_time(e1) / args.steps
+    del graph
+    return {"ms": ms, "h2d": h2d, "d2h": d2h}
 
 
 if __name__ == "__main__":

@@ -391,6 +391,62 @@ SRSWA_API int srswa_decode_allow(const int64_t* last_ids, int64_t s_ids, int64_t
                                  int64_t nblk_state, const int64_t* pp, int64_t* mcum, int64_t nblk,
                                  uint8_t* allow, srswa_stream_t stream);
 
+/* ---------------------------------------------------- page2d RoPE -------
+ * Two-axis rotary coordinates (token-in-page, page) of the indexer and the
+ * main branch.  Token ids as for PageGate. */
+
+/* Scratch of srswa_rope2d_pos for B rows of n_tok tokens. */
+SRSWA_API size_t srswa_rope2d_pos_workspace_size(int64_t B, int64_t n_tok);
+
+/* Coordinates of key_length tokens per row: page [B, key_length] int64 =
+ * marker count (prefill: up to the row's last image token) or marker count
+ * minus the prompt pages (response); tok [B, key_length] int64 = running
+ * count inside the token's page bucket (span > 0: each page's prefill mapped
+ * onto span steps, page 0 raw); pf_cnt [B, pf_cap] int64 (pf_cap >=
+ * key_length + 1) = prefill tokens of each page.  flags (int32 [4], zeroed
+ * here): [0] an image token, [1] a <PAGE> marker, [2] rows without prompt
+ * pages, [3] the page count n_pg; the reference returns None unless [0] and
+ * [1] are set and [2] is 0.
+ * Replaces DeepseekV2Indexer._build_page_rope_pos + _page_rope_offsets
+ * (hf-model-code/_sparse_base_impl.py:2511-2570). */
+SRSWA_API int srswa_rope2d_pos(const int64_t* ids, int64_t s_row, int64_t B, int64_t n_ids,
+                               int64_t key_length, int64_t img_id, int64_t page_id, int64_t span,
+                               int64_t* tok, int64_t* page, int64_t* pf_cnt, int64_t pf_cap,
+                               int32_t* flags, void* workspace, size_t workspace_bytes,
+                               srswa_stream_t stream);
+
+/* cos / sin tables [B, S, 2 * (n_tok + page_pairs)] (dtype, contiguous) of
+ * coordinates tok / page [B, S] (row stride s_pos): pair i < n_tok turns by
+ * tok * inv_tok[i], pair n_tok + i by (page mod page_mod, if > 0) *
+ * inv_page[i]; the table is [angles, angles].
+ * Replaces DeepseekV2IndexerRotary2D.forward (_sparse_base_impl.py:2043-2058). */
+SRSWA_API int srswa_rope2d_table(const int64_t* tok, const int64_t* page, int64_t s_pos, int64_t B,
+                                 int64_t S, const float* inv_tok, int64_t n_tok, const float* inv_page,
+                                 int64_t page_pairs, int64_t page_mod, void* cos_out, void* sin_out,
+                                 int dtype, srswa_stream_t stream);
+
+/* In place x <- x * cos + rotate_half(x) * sin over x [B, S, H, D] (fp32 or
+ * bf16; strides s_b, s_s, s_h, D contiguous, D % 16 == 0), feature f using
+ * pair f mod (n_tok + page_pairs), with the table values rounded to
+ * table_dtype first.  Fuses srswa_rope2d_table with the rotary application
+ * of the reference (apply_rotary_pos_emb at _sparse_base_impl.py:1537, and
+ * modeling_deepseekv2.py:183, 374, 508) without materialising the tables. */
+SRSWA_API int srswa_rope2d_apply(void* x, int dtype, int64_t B, int64_t S, int64_t H, int64_t D,
+                                 int64_t s_b, int64_t s_s, int64_t s_h, const int64_t* tok,
+                                 const int64_t* page, int64_t s_pos, const float* inv_tok, int64_t n_tok,
+                                 const float* inv_page, int64_t page_pairs, int64_t page_mod,
+                                 int table_dtype, srswa_stream_t stream);
+
+/* Decode update of one new token per row, in place on page [B] / tok [B]: a
+ * <PAGE> token moves to the next page (at most n_pg - 1) and restarts tok at
+ * that page's prefill count pf_cnt[b, page] (row stride s_pf); any other
+ * token advances tok.
+ * Replaces the decode branch of SlidingWindowLlamaAttention._main_rope_coords
+ * (_sparse_base_impl.py:1482-1489). */
+SRSWA_API int srswa_rope2d_decode(const int64_t* new_ids, int64_t s_ids, int64_t B, int64_t page_id,
+                                  int64_t* page, int64_t* tok, const int64_t* pf_cnt, int64_t s_pf,
+                                  int64_t n_pg, srswa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

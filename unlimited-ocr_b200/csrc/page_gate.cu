@@ -103,7 +103,24 @@ struct PgOut {
   // mode 1: decode-allow prefill state
   int64_t *bmin, *bmax, *pp, *mcum;
   int64_t bs, nblk;
+  // modes 2 / 3: page2d RoPE coordinates
+  int64_t* mpos;      // [B, s_mpos]: position of the k-th <PAGE> marker of the row (k >= 1)
+  int64_t s_mpos;
+  int64_t *tok, *page;  // [B, n_tok]
+  int64_t* pf;        // [B, pf_cap]: prefill tokens of each page
+  int64_t pf_cap;
+  int64_t span;       // > 0: page prefill spans mapped onto `span` token steps
+  int32_t* rflags;    // [0] image token seen, [1] marker seen, [2] rows without prompt pages, [3] page count
 };
+
+// Prefill tokens of page p of a row with pp prompt pages (pp >= 1): the BOS
+// prefix before the first marker (p = 0), the run from marker p to the next
+// one (or to the last image token) for p <= pp, none above.
+__device__ __forceinline__ int64_t prefill_count(const int64_t* mp, int64_t p, int64_t pp, int64_t last_img) {
+  if (p > pp) return 0;
+  if (p == 0) return mp[1];
+  return (p < pp ? mp[p + 1] : last_img + 1) - mp[p];
+}
 
 // Exclusive block scan of two counts packed in one 64-bit word (low: markers,
 // high: image tokens; each < 2^32 per chunk).
@@ -200,13 +217,34 @@ __global__ void __launch_bounds__(kPgThreads) page_scan_kernel(const PgRow r, in
       any_q |= (q >= 0 && j < r.n_tok);
       buf[0][base + k] = ip;
       buf[1][base + k] = q;
-    } else {
+    } else if (MODE == 1) {
       if (img) {
         const int64_t pg = cum > 0 ? cum - 1 : (run - 1) / r.per_page;
         const int blk = static_cast<int>((base + k) / o.bs);
         atomicMin(&bmn[blk], static_cast<int>(pg));
         atomicMax(&bmx[blk], static_cast<int>(pg));
       }
+    } else if (MODE == 2) {
+      if ((cd[k] & kCodeMark) && j < r.n_tok) o.mpos[b * o.s_mpos + cum] = j;
+    } else if (pp > 0) {  // MODE 3 (rows without prompt pages make the call return None)
+      const int64_t* mp = o.mpos + b * o.s_mpos;
+      const bool pre = j <= last_img;
+      const int64_t pg = pre ? cum : cum - pp;
+      int64_t rs = cum >= 1 ? mp[cum] : 0;  // the run of a page starts at its marker
+      if (!pre && rs <= last_img) rs = last_img + 1;
+      const int64_t pf = prefill_count(mp, pg, pp, last_img);
+      int64_t t = pre ? j - rs : pf + (j - rs);
+      if (o.span > 0 && pg > 0) {
+        const float sp = static_cast<float>(o.span);
+        const float v = pre ? rintf(static_cast<float>(t) * sp / static_cast<float>(pf > 1 ? pf : 1))
+                            : sp + static_cast<float>(t - pf);
+        t = static_cast<int64_t>(v);
+      }
+      buf[0][base + k] = t;
+      buf[1][base + k] = pg;
+    } else {
+      buf[0][base + k] = 0;
+      buf[1][base + k] = 0;
     }
   }
   __syncthreads();
@@ -224,6 +262,26 @@ __global__ void __launch_bounds__(kPgThreads) page_scan_kernel(const PgRow r, in
       if (any_img) atomicOr(&o.flags[0], 1);
       if (anyq) atomicOr(&o.flags[1], 1);
     }
+  } else if (MODE == 2) {
+    if (chunk == 0 && threadIdx.x == 0) {
+      if (lastc >= 0) atomicOr(&o.rflags[0], 1);
+      if (mall > 0) atomicOr(&o.rflags[1], 1);
+      if (pp == 0) atomicAdd(&o.rflags[2], 1);
+      const int64_t top = (pp > mall - pp ? pp : mall - pp) + 1;
+      atomicMax(&o.rflags[3], static_cast<int>(top));
+    }
+  } else if (MODE == 3) {
+    const int64_t rowo = b * r.n_tok + c0;
+    for (int i = threadIdx.x; i < nvalid; i += kPgThreads) {
+      o.tok[rowo + i] = buf[0][i];
+      o.page[rowo + i] = buf[1][i];
+    }
+    // this chunk's share of the per-page prefill counts (the last chunk also
+    // covers the rest of the capacity)
+    const int64_t p1 = chunk == nchunk - 1 ? o.pf_cap : min(o.pf_cap, c0 + kPgChunk);
+    const int64_t* mp = o.mpos + b * o.s_mpos;
+    for (int64_t pg = c0 + threadIdx.x; pg < p1; pg += kPgThreads)
+      o.pf[b * o.pf_cap + pg] = pp > 0 ? prefill_count(mp, pg, pp, last_img) : 0;
   } else {
     const int nb = static_cast<int>((nvalid + o.bs - 1) / o.bs);
     const int64_t blk0 = c0 / o.bs;
@@ -315,52 +373,73 @@ __device__ __forceinline__ bool block_has_page(const PgCand& a, int64_t b, int64
   return false;
 }
 
-// One warp per query row: 4 consecutive blocks per lane per step, one 32-bit
-// store (4-byte aligned rows) or four byte stores.  A row without a candidate
-// is rewritten with ones when `fallback` (the reference's per-query fallback).
+// One warp per 16 consecutive query rows of one batch row, 4 consecutive
+// blocks per lane per 128-block step.  A step's mask word is computed once
+// per run of rows with the same query page (consecutive queries nearly
+// always share it) and stored for every row of the run, so the kernel is
+// bound by the mask write rather than the descriptor reads.  Rows with a
+// query page < 0 have no candidate; rows without one get every block when
+// `fallback` (the reference's per-query fallback), else stay zero.
 constexpr int kCandWarps = 8;
+constexpr int kCandRows = 16;
+__device__ __forceinline__ uint32_t cand_word(const PgCand& a, int64_t b, const int4* dr, int64_t c0, int64_t qp) {
+  uint32_t word = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int64_t c = c0 + e;
+    if (c < a.nblk) {
+      const int4 d = __ldg(dr + c);
+      const bool y = a.flat ? d.x >= 0 : block_has_page(a, b, c, d, qp);
+      word |= static_cast<uint32_t>(y) << (8 * e);
+    }
+  }
+  return word;
+}
 __global__ void __launch_bounds__(kCandWarps * 32) page_cand_kernel(const PgCand a) {
   const int lane = threadIdx.x & 31;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * kCandWarps + (threadIdx.x >> 5);
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * kCandWarps + (threadIdx.x >> 5)) * kCandRows;
   const int64_t b = blockIdx.y;
-  if (i >= a.cq) return;
-  uint8_t* row = a.out + (b * a.cq + i) * a.nblk;
-  const bool w32 = (a.nblk & 3) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 3) == 0;
-  int64_t qp = 0;
-  if (!a.flat) {
-    int64_t p = __ldg(a.pos + b * a.s_pos + i);
+  if (row0 >= a.cq) return;  // warp-uniform
+  const int nr = static_cast<int>(min(static_cast<int64_t>(kCandRows), a.cq - row0));
+  int64_t my_qp = 0;  // lane r < nr: query page of row row0 + r
+  if (!a.flat && lane < nr) {
+    int64_t p = __ldg(a.pos + b * a.s_pos + row0 + lane);
     p = p < 0 ? 0 : (p > a.n_q - 1 ? a.n_q - 1 : p);
-    qp = __ldg(a.qpi + b * a.s_qpi + p);
+    my_qp = __ldg(a.qpi + b * a.s_qpi + p);
   }
-  bool any = false;
-  if (a.flat || qp >= 0) {
-    const int4* dr = a.desc + b * a.nblk;
-    for (int64_t c0 = 4 * lane; c0 < a.nblk; c0 += 128) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int64_t c = c0 + e;
-        if (c < a.nblk) {
-          const int4 d = __ldg(dr + c);
-          const bool y = a.flat ? d.x >= 0 : block_has_page(a, b, c, d, qp);
-          word |= static_cast<uint32_t>(y) << (8 * e);
-        }
+  const bool w32 = (a.nblk & 3) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 3) == 0;
+  const int4* dr = a.desc + b * a.nblk;
+  uint32_t anyrows = 0;  // bit r: row r has a candidate among this lane's blocks
+  for (int64_t base = 0; base < a.nblk; base += 128) {
+    const int64_t c0 = base + 4 * lane;
+    int64_t prev = 0;
+    uint32_t word = 0;
+    for (int r = 0; r < nr; ++r) {
+      const int64_t qp = a.flat ? 0 : static_cast<int64_t>(__shfl_sync(0xffffffffu, my_qp, r));
+      if (r == 0 || qp != prev) {  // warp-uniform
+        word = (a.flat || qp >= 0) ? cand_word(a, b, dr, c0, qp) : 0u;
+        prev = qp;
       }
-      any |= word != 0;
-      if (w32) {
-        *reinterpret_cast<uint32_t*>(row + c0) = word;
-      } else {
+      anyrows |= (word != 0 ? 1u : 0u) << r;
+      uint8_t* row = a.out + (b * a.cq + row0 + r) * a.nblk;
+      if (c0 < a.nblk) {
+        if (w32) {
+          *reinterpret_cast<uint32_t*>(row + c0) = word;
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (c0 + e < a.nblk) row[c0 + e] = static_cast<uint8_t>(word >> (8 * e));
+          for (int e = 0; e < 4; ++e)
+            if (c0 + e < a.nblk) row[c0 + e] = static_cast<uint8_t>(word >> (8 * e));
+        }
       }
     }
   }
-  any = __any_sync(0xffffffffu, any);
-  if (any) return;
-  const uint8_t fill = a.fallback ? 1 : 0;
-  if (!a.flat && qp >= 0 && !a.fallback) return;  // zeros already written
-  for (int64_t c = lane; c < a.nblk; c += 32) row[c] = fill;
+  if (!a.fallback) return;  // rows without a candidate stay zero
+  const uint32_t any = __reduce_or_sync(0xffffffffu, anyrows);
+  for (int r = 0; r < nr; ++r) {
+    if ((any >> r) & 1u) continue;
+    uint8_t* row = a.out + (b * a.cq + row0 + r) * a.nblk;
+    for (int64_t c = lane; c < a.nblk; c += 32) row[c] = 1;
+  }
 }
 
 // Decode allow of one new token per request: advances the marker count, then
@@ -407,6 +486,8 @@ __global__ void __launch_bounds__(256) decode_allow_kernel(const int64_t* last_i
 
 using namespace srswa;
 
+static size_t al16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
+
 extern "C" size_t srswa_page_scan_workspace_size(int64_t B, int64_t n_tok) {
   if (B <= 0 || n_tok <= 0) return 0;
   return static_cast<size_t>(B) * static_cast<size_t>(cdiv<int64_t>(n_tok, kPgChunk)) * sizeof(int4);
@@ -421,8 +502,14 @@ static int page_scan_launch(const PgRow& r, int64_t B, int mode, const PgOut& o,
   int4* stats = static_cast<int4*>(ws);
   const dim3 grid(static_cast<unsigned>(nchunk), static_cast<unsigned>(B));
   page_count_kernel<<<grid, kPgThreads, 0, s>>>(r, nchunk, stats);
-  if (mode == 0) page_scan_kernel<0><<<grid, kPgThreads, 0, s>>>(r, nchunk, stats, o);
-  else page_scan_kernel<1><<<grid, kPgThreads, 0, s>>>(r, nchunk, stats, o);
+  if (mode == 0) {
+    page_scan_kernel<0><<<grid, kPgThreads, 0, s>>>(r, nchunk, stats, o);
+  } else if (mode == 1) {
+    page_scan_kernel<1><<<grid, kPgThreads, 0, s>>>(r, nchunk, stats, o);
+  } else {  // RoPE coordinates: marker positions first, then the tokens
+    page_scan_kernel<2><<<grid, kPgThreads, 0, s>>>(r, nchunk, stats, o);
+    page_scan_kernel<3><<<grid, kPgThreads, 0, s>>>(r, nchunk, stats, o);
+  }
   return srswa_last_launch_status();
 }
 
@@ -479,12 +566,12 @@ extern "C" int srswa_page_cand_mask(const int32_t* desc, const int64_t* ipi, int
   SRSWA_CHECK_ARG(flat || (ipi && qpi && pos && n_q > 0), SRSWA_EINVAL);
   SRSWA_CHECK_ARG((reinterpret_cast<uintptr_t>(desc) & 15) == 0, SRSWA_EALIGN);
   if (B * cq * nblk == 0) return 0;
-  SRSWA_CHECK_ARG(B <= 65535 && cdiv<int64_t>(cq, kCandWarps) <= INT32_MAX, SRSWA_ETOOLARGE);
+  SRSWA_CHECK_ARG(B <= 65535 && cdiv<int64_t>(cq, kCandWarps * kCandRows) <= INT32_MAX, SRSWA_ETOOLARGE);
   PgCand a = {};
   a.desc = reinterpret_cast<const int4*>(desc); a.ipi = ipi; a.s_ipi = s_ipi; a.n_tok = n_tok; a.bs = block_size;
   a.B = B; a.nblk = nblk; a.qpi = qpi; a.s_qpi = s_qpi; a.n_q = n_q; a.pos = pos; a.s_pos = s_pos; a.cq = cq;
   a.flat = flat ? 1 : 0; a.fallback = fallback ? 1 : 0; a.out = cand;
-  const dim3 grid(static_cast<unsigned>(cdiv<int64_t>(cq, kCandWarps)), static_cast<unsigned>(B));
+  const dim3 grid(static_cast<unsigned>(cdiv<int64_t>(cq, kCandWarps * kCandRows)), static_cast<unsigned>(B));
   page_cand_kernel<<<grid, kCandWarps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return srswa_last_launch_status();
 }
@@ -500,5 +587,190 @@ extern "C" int srswa_decode_allow(const int64_t* last_ids, int64_t s_ids, int64_
   SRSWA_CHECK_ARG(B <= INT32_MAX, SRSWA_ETOOLARGE);
   decode_allow_kernel<<<static_cast<unsigned>(B), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       last_ids, s_ids, page_id, bmin, bmax, s_state, nblk_state, pp, mcum, nblk, allow);
+  return srswa_last_launch_status();
+}
+
+namespace srswa {
+
+// ---------------------------------------------------------------------------
+// page2d RoPE: the two-axis rotary of the indexer and main branch
+// (hf-model-code/_sparse_base_impl.py:1984-2058).  Pair i < n_tok turns by
+// tok * inv_tok[i], pair n_tok + i by (page mod page_mod) * inv_page[i]; the
+// table is [angles, angles] over dim = 2 * (n_tok + page_pairs) features.
+struct Rope2D {
+  const int64_t* tok;
+  const int64_t* page;
+  int64_t s_pos;  // row stride of tok / page ([B, S])
+  const float* inv_tok;
+  const float* inv_page;
+  int n_tok, half, page_mod;
+};
+
+__device__ __forceinline__ float rope_angle(const Rope2D& r, int64_t t, int64_t p, int pair) {
+  if (pair < r.n_tok) return static_cast<float>(t) * __ldg(r.inv_tok + pair);
+  if (r.page_mod > 0) {
+    p %= r.page_mod;
+    if (p < 0) p += r.page_mod;
+  }
+  return static_cast<float>(p) * __ldg(r.inv_page + pair - r.n_tok);
+}
+
+// cos / sin tables [B, S, 2 * half] (fp32 or bf16), one thread per (row, pair)
+__global__ void __launch_bounds__(256) rope2d_table_kernel(const Rope2D r, int64_t B, int64_t S, void* cos_out,
+                                                           void* sin_out, int dtype) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= B * S * r.half) return;
+  const int pair = static_cast<int>(i % r.half);
+  const int64_t row = i / r.half, b = row / S, s = row - b * S;
+  float sn, cs;
+  sincosf(rope_angle(r, __ldg(r.tok + b * r.s_pos + s), __ldg(r.page + b * r.s_pos + s), pair), &sn, &cs);
+  const int64_t o = row * 2 * r.half + pair;
+  store_elem(cos_out, o, dtype, cs);
+  store_elem(cos_out, o + r.half, dtype, cs);
+  store_elem(sin_out, o, dtype, sn);
+  store_elem(sin_out, o + r.half, dtype, sn);
+}
+
+// In place x <- x * cos + rotate_half(x) * sin over the first D features of
+// x [B, S, H, D] (strides s_b, s_s, s_h; D contiguous), feature f using pair
+// f mod half; cos / sin are rounded to table_dtype first (the reference casts
+// its tables to the activation dtype).  One thread per (b, s, h) and 8 pairs
+// (f, f + D/2).
+template <typename T>
+__global__ void __launch_bounds__(256) rope2d_apply_kernel(const Rope2D r, T* x, int64_t B, int64_t S, int64_t H,
+                                                           int D, int64_t s_b, int64_t s_s, int64_t s_h,
+                                                           int table_bf16) {
+  const int g8 = D / 16;  // groups of 8 pairs per row
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= B * S * H * g8) return;
+  const int g = static_cast<int>(i % g8);
+  const int64_t rw = i / g8, h = rw % H, bs_ = rw / H, s = bs_ % S, b = bs_ / S;
+  const int64_t t = __ldg(r.tok + b * r.s_pos + s), p = __ldg(r.page + b * r.s_pos + s);
+  T* row = x + b * s_b + s * s_s + h * s_h;
+  const int hd = D / 2;
+  float lo[8], hi[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    lo[e] = static_cast<float>(row[8 * g + e]);
+    hi[e] = static_cast<float>(row[hd + 8 * g + e]);
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int f = 8 * g + e;
+    float s1, c1, s2, c2;
+    sincosf(rope_angle(r, t, p, f % r.half), &s1, &c1);
+    sincosf(rope_angle(r, t, p, (f + hd) % r.half), &s2, &c2);
+    if (table_bf16) {
+      c1 = __bfloat162float(__float2bfloat16_rn(c1));
+      s1 = __bfloat162float(__float2bfloat16_rn(s1));
+      c2 = __bfloat162float(__float2bfloat16_rn(c2));
+      s2 = __bfloat162float(__float2bfloat16_rn(s2));
+    }
+    const float a = lo[e], bb = hi[e];
+    lo[e] = a * c1 - bb * s1;
+    hi[e] = bb * c2 + a * s2;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    row[8 * g + e] = static_cast<T>(lo[e]);
+    row[hd + 8 * g + e] = static_cast<T>(hi[e]);
+  }
+}
+
+// Decode update of the (tok, page) coordinates of one new token per row
+// (_main_rope_coords, _sparse_base_impl.py:1482-1489).
+__global__ void rope2d_decode_kernel(const int64_t* new_ids, int64_t s_ids, int64_t B, int64_t page_id,
+                                     int64_t* page, int64_t* tok, const int64_t* pf, int64_t s_pf, int64_t n_pg) {
+  const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const bool is_pg = __ldg(new_ids + b * s_ids) == page_id;
+  int64_t pg = page[b];
+  if (is_pg) pg = pg + 1 < n_pg - 1 ? pg + 1 : n_pg - 1;
+  page[b] = pg;
+  tok[b] = is_pg ? __ldg(pf + b * s_pf + (pg > 0 ? pg : 0)) : tok[b] + 1;
+}
+
+}  // namespace srswa (page2d RoPE)
+
+extern "C" size_t srswa_rope2d_pos_workspace_size(int64_t B, int64_t n_tok) {
+  if (B <= 0 || n_tok <= 0) return 0;
+  return al16(srswa_page_scan_workspace_size(B, n_tok)) + static_cast<size_t>(B) * (n_tok + 2) * sizeof(int64_t);
+}
+
+extern "C" int srswa_rope2d_pos(const int64_t* ids, int64_t s_row, int64_t B, int64_t n_ids, int64_t key_length,
+                                int64_t img_id, int64_t page_id, int64_t span, int64_t* tok, int64_t* page,
+                                int64_t* pf_cnt, int64_t pf_cap, int32_t* flags, void* workspace,
+                                size_t workspace_bytes, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(ids && tok && page && pf_cnt && flags && B >= 0 && n_ids >= 0 && key_length >= 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(s_row >= n_ids || B <= 1, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(pf_cap >= key_length + 1, SRSWA_EINVAL);  // pages <= markers <= tokens
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  SRSWA_CHECK_ARG(workspace_bytes >= srswa_rope2d_pos_workspace_size(B, key_length), SRSWA_EWORKSPACE);
+  SRSWA_CUDA_TRY(cudaMemsetAsync(flags, 0, 4 * sizeof(int32_t), s));
+  if (B * key_length == 0) return 0;
+  PgRow r = {ids, s_row, n_ids, key_length, img_id, page_id, 1};
+  PgOut o = {};
+  const size_t stats_bytes = al16(srswa_page_scan_workspace_size(B, key_length));
+  o.mpos = reinterpret_cast<int64_t*>(static_cast<unsigned char*>(workspace) + stats_bytes);
+  o.s_mpos = key_length + 2;
+  o.tok = tok; o.page = page; o.pf = pf_cnt; o.pf_cap = pf_cap; o.span = span; o.rflags = flags;
+  return page_scan_launch(r, B, 2, o, workspace, stats_bytes, s);
+}
+
+static int rope2d_check(const Rope2D& r) {
+  SRSWA_CHECK_ARG(r.tok && r.page && r.inv_tok && r.n_tok >= 0 && r.half > r.n_tok, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(r.half == r.n_tok || r.inv_page, SRSWA_EINVAL);
+  return 0;
+}
+
+extern "C" int srswa_rope2d_table(const int64_t* tok, const int64_t* page, int64_t s_pos, int64_t B, int64_t S,
+                                  const float* inv_tok, int64_t n_tok, const float* inv_page, int64_t page_pairs,
+                                  int64_t page_mod, void* cos_out, void* sin_out, int dtype, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(cos_out && sin_out && B >= 0 && S >= 0 && n_tok >= 0 && page_pairs >= 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(dtype == SRSWA_F32 || dtype == SRSWA_BF16 || dtype == SRSWA_F16, SRSWA_EUNSUPPORTED);
+  Rope2D r = {tok, page, s_pos, inv_tok, inv_page, static_cast<int>(n_tok), static_cast<int>(n_tok + page_pairs),
+              static_cast<int>(page_mod)};
+  if (int rc = rope2d_check(r)) return rc;
+  const int64_t n = B * S * r.half;
+  if (n == 0) return 0;
+  SRSWA_CHECK_ARG(cdiv<int64_t>(n, 256) <= INT32_MAX, SRSWA_ETOOLARGE);
+  rope2d_table_kernel<<<static_cast<unsigned>(cdiv<int64_t>(n, 256)), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      r, B, S, cos_out, sin_out, dtype);
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_rope2d_apply(void* x, int dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t s_b,
+                                  int64_t s_s, int64_t s_h, const int64_t* tok, const int64_t* page, int64_t s_pos,
+                                  const float* inv_tok, int64_t n_tok, const float* inv_page, int64_t page_pairs,
+                                  int64_t page_mod, int table_dtype, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(x && B >= 0 && S >= 0 && H >= 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(D > 0 && D % 16 == 0 && D <= 2 * (n_tok + page_pairs), SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG(dtype == SRSWA_F32 || dtype == SRSWA_BF16, SRSWA_EUNSUPPORTED);
+  Rope2D r = {tok, page, s_pos, inv_tok, inv_page, static_cast<int>(n_tok), static_cast<int>(n_tok + page_pairs),
+              static_cast<int>(page_mod)};
+  if (int rc = rope2d_check(r)) return rc;
+  const int64_t n = B * S * H * (D / 16);
+  if (n == 0) return 0;
+  SRSWA_CHECK_ARG(cdiv<int64_t>(n, 256) <= INT32_MAX, SRSWA_ETOOLARGE);
+  const unsigned grid = static_cast<unsigned>(cdiv<int64_t>(n, 256));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int tb = table_dtype == SRSWA_BF16 ? 1 : 0;
+  if (dtype == SRSWA_BF16)
+    rope2d_apply_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(r, static_cast<__nv_bfloat16*>(x), B, S, H,
+                                                            static_cast<int>(D), s_b, s_s, s_h, tb);
+  else
+    rope2d_apply_kernel<float><<<grid, 256, 0, s>>>(r, static_cast<float*>(x), B, S, H, static_cast<int>(D), s_b,
+                                                    s_s, s_h, tb);
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_rope2d_decode(const int64_t* new_ids, int64_t s_ids, int64_t B, int64_t page_id,
+                                   int64_t* page, int64_t* tok, const int64_t* pf_cnt, int64_t s_pf, int64_t n_pg,
+                                   srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(new_ids && page && tok && pf_cnt && B >= 0 && n_pg >= 1 && s_pf >= n_pg, SRSWA_EINVAL);
+  if (B == 0) return 0;
+  rope2d_decode_kernel<<<static_cast<unsigned>(cdiv<int64_t>(B, 128)), 128, 0,
+                         reinterpret_cast<cudaStream_t>(stream)>>>(new_ids, s_ids, B, page_id, page, tok, pf_cnt,
+                                                                   s_pf, n_pg);
   return srswa_last_launch_status();
 }

@@ -86,6 +86,13 @@ _SIGS = {
     "srswa_decode_allow_state": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp,
                                            C.c_size_t, vp]),
     "srswa_decode_allow": (C.c_int, [vp, i64, i64, i64, vp, vp, i64, i64, vp, vp, i64, vp, vp]),
+    "srswa_rope2d_pos_workspace_size": (C.c_size_t, [i64, i64]),
+    "srswa_rope2d_pos": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, vp, vp, vp, i64, vp, vp, C.c_size_t,
+                                   vp]),
+    "srswa_rope2d_table": (C.c_int, [vp, vp, i64, i64, i64, vp, i64, vp, i64, i64, vp, vp, C.c_int, vp]),
+    "srswa_rope2d_apply": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, i64, i64, i64, vp, vp, i64, vp, i64, vp,
+                                     i64, i64, C.c_int, vp]),
+    "srswa_rope2d_decode": (C.c_int, [vp, i64, i64, i64, vp, vp, vp, i64, i64, vp]),
 }
 
 _lib = None

@@ -11,6 +11,8 @@ After ``install``:
   * the PageGate candidate methods of ``<pkg>._sparse_base_impl.DeepseekV2Indexer``,
     ``modeling_deepseekv2._dash_block_cand`` and
     ``modeling_unlimitedocr._uocr_dash_decode_allow`` -> ``srswa.page_gate``
+  * ``DeepseekV2Indexer._build_page_rope_pos``, ``DeepseekV2IndexerRotary2D.forward``
+    and ``SlidingWindowLlamaAttention._main_rope_coords`` -> ``srswa.page_rope``
 so DashAttention._forward_triton, SlidingWindowLlamaAttention's sparse branch,
 the DSA indexer and the DASH inference overlay call the CUDA kernels without a
 source change.  ``install_sglang()`` does the same for the SGLang ops modules.
@@ -20,7 +22,7 @@ from __future__ import annotations
 
 import sys
 
-from . import dash_infer, page_gate, paged, sparse_gather, sparse_gather_e2e
+from . import dash_infer, page_gate, page_rope, paged, sparse_gather, sparse_gather_e2e
 
 _INDEXER_METHODS = ("_build_page_aware_ids", "_build_flat_image_token_mask", "_build_image_block_allow_mask",
                     "_build_page_aware_image_block_mask", "_build_kl_candidate_mask")
@@ -45,6 +47,14 @@ def install(pkg: str) -> None:
             for name in _INDEXER_METHODS:
                 setattr(ix, name, getattr(page_gate, name))
         page_gate._scope_source = base      # _PAGE_SCOPE_PREFILL stays the reference's switch
+        if ix is not None:
+            ix._build_page_rope_pos = page_rope._build_page_rope_pos
+        rot = getattr(base, "DeepseekV2IndexerRotary2D", None)
+        if rot is not None:
+            rot.forward = page_rope.rotary2d_forward
+        attn = getattr(base, "SlidingWindowLlamaAttention", None)
+        if attn is not None:
+            attn._main_rope_coords = page_rope._main_rope_coords
     mu = sys.modules.get(f"{pkg}.modeling_unlimitedocr")
     if mu is not None:
         mu._uocr_dash_decode_allow = page_gate._uocr_dash_decode_allow

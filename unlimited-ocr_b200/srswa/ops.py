@@ -519,3 +519,73 @@ def decode_allow(state, last_ids, page_id, nblk, out=None):
                                     out.view(torch.uint8).data_ptr(), L.stream_of(bmin))
     L.check(rc, "srswa_decode_allow")
     return out
+
+
+# --------------------------------------------------------------- page2d RoPE
+def rope2d_pos(ids, img_id, page_id, key_length, span=0):
+    """ids [B, n] -> (tok, page [B, key_length] int64, pf_cnt [B, key_length + 1]
+    int64, flags int32 [4] on the device: image seen, marker seen, rows
+    without prompt pages, page count)."""
+    ids = _ids64(ids)
+    B, n = ids.shape
+    dev = ids.device
+    tok = torch.empty(B, key_length, device=dev, dtype=torch.int64)
+    page = torch.empty(B, key_length, device=dev, dtype=torch.int64)
+    pf = torch.empty(B, key_length + 1, device=dev, dtype=torch.int64)
+    flags = torch.empty(4, device=dev, dtype=torch.int32)
+    wsb = L.lib().srswa_rope2d_pos_workspace_size(B, key_length)
+    ws = torch.empty(max(wsb, 16), device=dev, dtype=torch.uint8)
+    rc = L.lib().srswa_rope2d_pos(ids.data_ptr(), ids.stride(0), B, n, key_length, int(img_id), int(page_id),
+                                  int(span), tok.data_ptr(), page.data_ptr(), pf.data_ptr(), key_length + 1,
+                                  flags.data_ptr(), ws.data_ptr(), wsb, L.stream_of(ids))
+    L.check(rc, "srswa_rope2d_pos")
+    return tok, page, pf, flags
+
+
+def _rope_freqs(inv_tok, inv_page):
+    it = inv_tok.float().contiguous()
+    ip = inv_page.float().contiguous() if inv_page is not None and inv_page.numel() else None
+    return it, ip, (0 if ip is None else ip.numel())
+
+
+def rope2d_table(tok, page, inv_tok, inv_page, page_mod=0, dtype=torch.float32):
+    """cos, sin [B, S, 2 * (n_tok + page_pairs)] of coordinates tok / page [B, S]."""
+    tok, page = _ids64(tok), _ids64(page)
+    assert tok.stride(0) == page.stride(0)
+    B, S = tok.shape
+    it, ip, pairs = _rope_freqs(inv_tok.to(tok.device), None if inv_page is None else inv_page.to(tok.device))
+    dim = 2 * (it.numel() + pairs)
+    cos = torch.empty(B, S, dim, device=tok.device, dtype=dtype)
+    sin = torch.empty_like(cos)
+    rc = L.lib().srswa_rope2d_table(tok.data_ptr(), page.data_ptr(), tok.stride(0), B, S, it.data_ptr(), it.numel(),
+                                    L.ptr(ip), pairs, int(page_mod), cos.data_ptr(), sin.data_ptr(),
+                                    L.dtype_code(cos), L.stream_of(tok))
+    L.check(rc, "srswa_rope2d_table")
+    return cos, sin
+
+
+def rope2d_apply_(x, tok, page, inv_tok, inv_page, page_mod=0, table_dtype=None):
+    """In place x <- x * cos + rotate_half(x) * sin on x [B, S, H, D] (any
+    strides with D contiguous; a [B, H, S, D] tensor goes in as
+    x.transpose(1, 2)); the tables are rounded to table_dtype (default:
+    x's dtype, as the reference casts them)."""
+    tok, page = _ids64(tok), _ids64(page)
+    assert tok.stride(0) == page.stride(0) and x.stride(-1) == 1
+    B, S, H, D = x.shape
+    it, ip, pairs = _rope_freqs(inv_tok.to(x.device), None if inv_page is None else inv_page.to(x.device))
+    td = L.dtype_code(x if table_dtype is None else torch.empty(0, dtype=table_dtype))
+    rc = L.lib().srswa_rope2d_apply(x.data_ptr(), L.dtype_code(x), B, S, H, D, x.stride(0), x.stride(1), x.stride(2),
+                                    tok.data_ptr(), page.data_ptr(), tok.stride(0), it.data_ptr(), it.numel(),
+                                    L.ptr(ip), pairs, int(page_mod), td, L.stream_of(x))
+    L.check(rc, "srswa_rope2d_apply")
+    return x
+
+
+def rope2d_decode_(new_ids, page_id, page, tok, pf_cnt, n_pg):
+    """One new token per row: updates page [B] and tok [B] (int64) in place."""
+    new_ids = _ids64(new_ids.reshape(new_ids.shape[0], -1))
+    assert page.dtype == torch.int64 and tok.dtype == torch.int64 and pf_cnt.dtype == torch.int64
+    rc = L.lib().srswa_rope2d_decode(new_ids[:, -1:].data_ptr(), new_ids.stride(0), page.shape[0], int(page_id),
+                                     page.data_ptr(), tok.data_ptr(), pf_cnt.data_ptr(), pf_cnt.stride(0),
+                                     int(n_pg), L.stream_of(page))
+    L.check(rc, "srswa_rope2d_decode")
