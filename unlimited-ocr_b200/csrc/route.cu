@@ -262,13 +262,22 @@ __device__ __forceinline__ void route_epilogue(const RouteArgs& a, int64_t n, in
   // mean - sqrt(max(0, (1 - rho(meansq - mean^2))/rho)); support = #(tau <= X)
   const float xmax = __shfl_sync(0xffffffffu, sel_v, 0);
   const float X = (sel_v - xmax) / 2.0f;
+  // every lane gathers 8 values at a time (independent shuffles), then runs
+  // the same left-to-right float64 sums: no shuffle latency inside the chain
   double acc1 = 0.0, acc2 = 0.0;
   float my_cs = 0.f, my_cs2 = 0.f;
-  for (int j = 0; j < M; ++j) {
-    const float xj = __shfl_sync(0xffffffffu, X, j);
-    acc1 += static_cast<double>(xj);
-    acc2 += static_cast<double>(xj * xj);
-    if (lane == j) { my_cs = static_cast<float>(acc1); my_cs2 = static_cast<float>(acc2); }
+  for (int j0 = 0; j0 < M; j0 += 8) {
+    float xs[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) xs[e] = __shfl_sync(0xffffffffu, X, (j0 + e) & 31);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (j0 + e < M) {
+        acc1 += static_cast<double>(xs[e]);
+        acc2 += static_cast<double>(xs[e] * xs[e]);
+        if (lane == j0 + e) { my_cs = static_cast<float>(acc1); my_cs2 = static_cast<float>(acc2); }
+      }
+    }
   }
   const float rho = static_cast<float>(lane + 1);
   const float mean = my_cs / rho;
@@ -289,10 +298,15 @@ __device__ __forceinline__ void route_epilogue(const RouteArgs& a, int64_t n, in
   const float logp = logf(fmaxf(prior, a.floor_));
   float sum = 0.f;
   int cnt = 0;
-  for (int j = 0; j < K; ++j) {
-    const float lj = __shfl_sync(0xffffffffu, logp, j);
-    const int vj = __shfl_sync(0xffffffffu, static_cast<int>(vld), j);
-    if (vj) { sum += lj; ++cnt; }
+  const unsigned vmask = __ballot_sync(0xffffffffu, vld);
+  for (int j0 = 0; j0 < K; j0 += 8) {
+    float ls[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ls[e] = __shfl_sync(0xffffffffu, logp, (j0 + e) & 31);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (j0 + e < K && ((vmask >> (j0 + e)) & 1u)) { sum += ls[e]; ++cnt; }
+    }
   }
   const float mu = sum / static_cast<float>(cnt > 0 ? cnt : 1);
   const float bias = vld ? (logp - mu) * a.inv_sigma : 0.f;
@@ -1051,6 +1065,49 @@ static size_t route_tile_smem(int64_t nblk) {
   return (ab > keys ? ab : keys) + static_cast<size_t>(kRtRows) * nblk * 4;  // + scores
 }
 
+// Selection of route_tile_kernel for the 4 rows of one warp (NPL keys per
+// lane: blocks lane + 32 i, i < NPL, NPL * 32 >= nblk).
+template <int NPL>
+__device__ __forceinline__ void route_tile_select(const RouteArgs& a, const float* zs, int64_t n0, int r0, int lane,
+                                                  unsigned long long* scratch) {
+  const int64_t nblk = a.nblk;
+  const int M = static_cast<int>(a.M);
+  for (int rr = 0; rr < 4; ++rr) {
+    const int r = r0 + rr;
+    const int64_t n = n0 + r;
+    if (n >= a.N) break;  // warp-uniform
+    const float* z = zs + r * nblk;
+    int found = 1;
+    if (a.cand) {
+      int f = 0;
+      for (int64_t c = lane; c < nblk; c += 32) f |= (z[c] > kScoreNeg * 0.5f) && a.cand[n * a.s_cand + c] != 0;
+      found = __any_sync(0xffffffffu, f);
+    }
+    unsigned long long v[NPL];
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+      const int64_t c = lane + 32 * k;
+      v[k] = 0ull;
+      if (c < nblk) {
+        const float zc = z[c];
+        if (a.scores_out) a.scores_out[n * nblk + c] = zc;
+        const bool remote = zc > kScoreNeg * 0.5f;  // NaN -> not remote
+        const bool cm = remote && (a.cand == nullptr || !found || a.cand[n * a.s_cand + c] != 0);
+        float x = cm ? zc * a.idx_scale : kEntmaxNeg;
+        if (!isfinite(x)) x = kEntmaxNeg;
+        v[k] = pack_key(x, c, cm);
+      }
+    }
+    const unsigned long long mine = warp_topm_filtered<NPL>(v, M, lane, scratch);
+    float sel_v = 0.f;
+    int sel_i = -1;
+    bool sel_c = false;
+    if (lane < M) unpack_key(mine, sel_v, sel_i, sel_c);
+    route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+    __syncwarp();
+  }
+}
+
 __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteArgs a) {
   extern __shared__ __align__(16) float rt_smem[];
   const int64_t nblk = a.nblk;
@@ -1165,41 +1222,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
   }
   __syncthreads();
   // ---- selection: warp w, rows 4w .. 4w+3; lane holds blocks lane + 32 i ----
-  const int M = static_cast<int>(a.M);
-  for (int rr = 0; rr < 4; ++rr) {
-    const int r = r0 + rr;
-    const int64_t n = n0 + r;
-    if (n >= a.N) break;  // warp-uniform
-    const float* z = zs + r * nblk;
-    int found = 1;
-    if (a.cand) {
-      int f = 0;
-      for (int64_t c = lane; c < nblk; c += 32) f |= (z[c] > kScoreNeg * 0.5f) && a.cand[n * a.s_cand + c] != 0;
-      found = __any_sync(0xffffffffu, f);
-    }
-    unsigned long long v[kRtMaxBlocks / 32];
-#pragma unroll
-    for (int k = 0; k < kRtMaxBlocks / 32; ++k) {
-      const int64_t c = lane + 32 * k;
-      v[k] = 0ull;
-      if (c < nblk) {
-        const float zc = z[c];
-        if (a.scores_out) a.scores_out[n * nblk + c] = zc;
-        const bool remote = zc > kScoreNeg * 0.5f;  // NaN -> not remote
-        const bool cm = remote && (a.cand == nullptr || !found || a.cand[n * a.s_cand + c] != 0);
-        float x = cm ? zc * a.idx_scale : kEntmaxNeg;
-        if (!isfinite(x)) x = kEntmaxNeg;
-        v[k] = pack_key(x, c, cm);
-      }
-    }
-    const unsigned long long mine = warp_topm_filtered<kRtMaxBlocks / 32>(v, M, lane, topm_scratch[warp]);
-    float sel_v = 0.f;
-    int sel_i = -1;
-    bool sel_c = false;
-    if (lane < M) unpack_key(mine, sel_v, sel_i, sel_c);
-    route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
-    __syncwarp();
-  }
+  if (nblk <= 128) route_tile_select<4>(a, zs, n0, r0, lane, topm_scratch[warp]);
+  else if (nblk <= 256) route_tile_select<8>(a, zs, n0, r0, lane, topm_scratch[warp]);
+  else route_tile_select<kRtMaxBlocks / 32>(a, zs, n0, r0, lane, topm_scratch[warp]);
 }
 
 static bool use_tile(const RouteArgs& a) {
