@@ -112,8 +112,11 @@ def test_rope_decode_golden(cuda):
     ids = t(g["ids"], cuda)
     S = ids.shape[1]
 
+    class Ix(Indexer):     # the reference indexer's method, as srswa.dropin installs it
+        _build_page_rope_pos = P._build_page_rope_pos
+
     class Attn:
-        indexer = Indexer()
+        indexer = Ix()
         layer_idx = 0
         _main_rope_pos_2d = None
         _sparse_source_input_ids = ids
