@@ -229,18 +229,36 @@ def build_rank(S_local, seed, dev):
     return st
 
 
-STEP_LAUNCHES = 6   # k_bar refresh, router scores + selection, window attend, selected-block attend, merge
+STEP_LAUNCHES = 4   # k_bar tail refresh, router scores, router selection, attend
 
 
-def run_step(st, q=None, iq=None):
-    """One decode step through the public paged API (device-resident inputs):
-    k_bar tail refresh + route + attend, the window half of the attend
-    overlapped with the router (srswa.paged.decode_step)."""
+def run_step(st):
+    """One decode step through the library (device-resident inputs)."""
+    from srswa import ops
+    ops.kbar_paged(st["idx"], st["hc"], st["bt"], st["sl"], st["kbar"], tail_pages=1)
+    r = ops.route(st["iq"], st["kbar"], block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=IDX_SCALE,
+                  floor=FLOOR, sigma=SIGMA, seq_lens=st["sl"], block_table=st["bt"], want=("topi32", "bias"))
+    st["topi"], st["bias"] = r["topi32"], r["bias"]
+    run_attend(st)
+
+
+def run_step_public(st, q, iq):
+    """The same decode step through the public paged API (SGLang signatures):
+    kbar_refresh_tail, route_decode, dash_sparse_attn_decode."""
     from srswa import paged
-    st["topi"], st["bias"] = paged.decode_step(
-        st["q"] if q is None else q, st["k"], st["v"], st["iq"] if iq is None else iq, st["kbar"], st["bt"],
-        st["sl"], st["out"], sm_scale=SM_SCALE, local_blocks=L, sparse_block_size=BS, idx_scale=IDX_SCALE,
-        prior_floor=FLOOR, sigma=SIGMA, topm=M, budget=K, idx_cache=st["idx"], head_cls=st["hc"], tail_pages=1)
+    if "idx_buf" not in st:
+        st["idx_buf"] = torch.empty(q.shape[0], M, dtype=torch.int32, device=q.device)
+        st["bias_buf"] = torch.empty(q.shape[0], M, dtype=torch.float32, device=q.device)
+    paged.kbar_refresh_tail(kv_cache=st["idx"], k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"],
+                            head_cls=st["hc"], block_size=BS, tail_pages=1)
+    w = paged.route_decode(idx_q=iq, k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"], image_allow=None,
+                           out_idx=st["idx_buf"], out_bias=st["bias_buf"], max_block=st["bt"].shape[1],
+                           block_size=BS, local_blocks=L, decode_query_len=1, idx_scale=IDX_SCALE,
+                           prior_floor=FLOOR, sigma=SIGMA, topm=M, budget=K)
+    ti = st["idx_buf"][:, :w].unsqueeze(0).expand(HKV, -1, -1)
+    tb = st["bias_buf"][:, :w].unsqueeze(0).expand(HKV, -1, -1)
+    paged.dash_sparse_attn_decode(q, st["k"], st["v"], ti, tb, st["bt"], st["sl"], HKV, SM_SCALE, st["out"], 1,
+                                  local_blocks=L, sparse_block_size=BS)
 
 
 def run_attend(st):
@@ -795,8 +813,8 @@ def main():
             "cpu_baseline": cpu,
             "e2e": None if e2e is None else {
                 "value": bytes_all / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
-                "how": "pinned H2D of the step's inputs, cache append, srswa.paged.decode_step, D2H of the "
-                       "output; one CUDA graph per step",
+                "how": "one pinned H2D of the step's packed inputs, cache append, kbar_refresh_tail + "
+                       "route_decode + dash_sparse_attn_decode, D2H of the output; one CUDA graph per step",
                 "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all},
             "gpu_launches": STEP_LAUNCHES * args.steps,
             "clocks": clk,
@@ -812,10 +830,9 @@ def e2e_measure(st, S_local, args, dev):
     """Per step: one H2D copy of this step's inputs packed in a pinned host
     buffer (q, idx_q, the new token's K / V / index-key rows and its cache
     slot), the append to the paged caches, the decode step through the public
-    paged API (srswa.paged.decode_step), and the D2H copy of the output; the
+    paged API, and the D2H copy of the output; the
     step is captured once in a CUDA graph (as a serving loop's decode step)
     and replayed, copies included."""
-    from srswa import paged
     R = len(S_local)
     g = torch.Generator().manual_seed(77)
     hq = torch.randn(R, H, D, generator=g).to(torch.bfloat16)
@@ -845,7 +862,7 @@ def e2e_measure(st, S_local, args, dev):
         st["k"][sl_[0], sl_[1]] = nk
         st["v"][sl_[0], sl_[1]] = nv
         st["idx"][sl_[0], sl_[1]] = nik
-        run_step(st, q=q, iq=iq)
+        run_step_public(st, q, iq)
         hout.copy_(st["out"], non_blocking=True)
 
     s_ = torch.cuda.Stream()

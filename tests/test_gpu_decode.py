@@ -128,62 +128,3 @@ def test_lse_merge_vs_oracle(cuda):
     fin = np.isfinite(ref_l)
     np.testing.assert_allclose(l.cpu().numpy()[fin], ref_l[fin], rtol=1e-5, atol=1e-5)
 
-
-@pytest.mark.parametrize("graph", [False, True])
-def test_decode_step_overlapped_equals_sequential(cuda, graph):
-    """paged.decode_step (window attend on a side stream while the k_bar
-    refresh and the router run, then the selected blocks and an LSE merge)
-    against k_bar refresh + route + attend in sequence, eagerly and replayed
-    from a CUDA graph.  Selections bit-identical; outputs: fp32 within 1e-4
-    of the oracle on the same selection, bf16 within 2e-2 / 1e-2."""
-    rng = np.random.default_rng(12)
-    BS, L, K, M, H, D, d = 64, 8, 8, 16, 10, 128, 128
-    seqs = [40000, 3000, 700, 70000, 12345]
-    W = max(-(-s // BS) for s in seqs)
-    P = len(seqs) * W
-    bt = T(rng.permutation(P).astype(np.int32).reshape(len(seqs), W), cuda)
-    kc = T(O.bf16_round(rng.standard_normal((P, BS, H, D)).astype(np.float32)), cuda, torch.bfloat16)
-    vc = T(O.bf16_round(rng.standard_normal((P, BS, H, D)).astype(np.float32)), cuda, torch.bfloat16)
-    ic = T(O.bf16_round(rng.standard_normal((P, BS, d)).astype(np.float32)), cuda, torch.bfloat16)
-    q = T(O.bf16_round(rng.standard_normal((len(seqs), H, D)).astype(np.float32)), cuda, torch.bfloat16)
-    iq = T(O.bf16_round(rng.standard_normal((len(seqs), d)).astype(np.float32)), cuda)
-    sl = T(np.asarray(seqs, np.int32), cuda)
-    hc = torch.zeros(d, device=cuda)
-    kbar0 = torch.zeros(P, d, device=cuda)
-    ops.kbar_paged(ic, hc, bt, sl, kbar0, tail_pages=0)
-    prm = dict(idx_scale=128 / math.sqrt(d), prior_floor=1e-4, sigma=1.0, topm=M, budget=K)
-    # sequential reference path (public paged API)
-    kb_a = kbar0.clone()
-    paged.kbar_refresh_tail(kv_cache=ic, k_bar=kb_a, block_table=bt, seq_lens=sl, head_cls=hc, block_size=BS)
-    oi = torch.empty(len(seqs), M, dtype=torch.int32, device=cuda)
-    ob = torch.empty(len(seqs), M, device=cuda)
-    w = paged.route_decode(idx_q=iq, k_bar=kb_a, block_table=bt, seq_lens=sl, image_allow=None, out_idx=oi,
-                           out_bias=ob, max_block=W, block_size=BS, local_blocks=L, decode_query_len=1,
-                           idx_scale=prm["idx_scale"], prior_floor=prm["prior_floor"], sigma=1.0, topm=M, budget=K)
-    for dt, tol in ((torch.float32, (1e-4, 1e-4)), (torch.bfloat16, (1e-2, 2e-2))):
-        ref = torch.empty(len(seqs), H, D, device=cuda, dtype=dt)
-        paged.dash_sparse_attn_decode(q, kc, vc, oi[:, :w][None], ob[:, :w][None], bt, sl, H, 0.088, ref, 1,
-                                      local_blocks=L, sparse_block_size=BS)
-        out = torch.empty_like(ref)
-        kb_b = kbar0.clone()
-        fn = lambda: paged.decode_step(q, kc, vc, iq, kb_b, bt, sl, out, sm_scale=0.088, local_blocks=L,  # noqa: E731
-                                       sparse_block_size=BS, idx_cache=ic, head_cls=hc, **prm)
-        if graph:
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                fn()
-            torch.cuda.current_stream().wait_stream(s)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                res = fn()
-            out.zero_()
-            kb_b.copy_(kbar0)
-            g.replay()
-        else:
-            res = fn()
-        torch.cuda.synchronize()
-        ti, tb = res
-        assert torch.equal(ti, oi[:, :w]) and torch.allclose(tb, ob[:, :w])
-        assert torch.equal(kb_b, kb_a)
-        np.testing.assert_allclose(out.float().cpu().numpy(), ref.float().cpu().numpy(), rtol=tol[0], atol=tol[1])

@@ -83,64 +83,3 @@ def route_decode(*, idx_q, k_bar, block_table, seq_lens, image_allow, out_idx, o
         out_bias[:, k:].zero_()
     return out_slots or k
 
-
-_side_streams: dict = {}
-_no_remote: dict = {}
-
-
-def _side_stream(dev: torch.device) -> torch.cuda.Stream:
-    s = _side_streams.get(dev)
-    if s is None:
-        s = _side_streams[dev] = torch.cuda.Stream(device=dev)
-    return s
-
-
-def _window_only_selection(n: int, dev: torch.device) -> torch.Tensor:
-    """[n, 1] int32 of -1: an attend over the local window alone."""
-    t = _no_remote.get((dev, n))
-    if t is None:
-        t = _no_remote[(dev, n)] = torch.full((n, 1), -1, dtype=torch.int32, device=dev)
-    return t
-
-
-@torch.no_grad()
-def decode_step(q, k_cache, v_cache, idx_q, k_bar, block_table, seq_lens, output, *, sm_scale, local_blocks,
-                sparse_block_size, idx_scale, prior_floor, sigma, topm, budget, idx_cache=None, head_cls=None,
-                tail_pages=1, image_allow=None, decode_query_len=1):
-    """One SR-SWA decode step of every request: k_bar tail refresh (when
-    idx_cache / head_cls are given), route over the k_bar cache, sparse attend;
-    writes ``output`` [R*dql, H, D] in place and returns (topk_idx, bias).
-
-    The same result as ``kbar_refresh_tail`` + ``route_decode`` +
-    ``dash_sparse_attn_decode`` in sequence, up to the rounding of one
-    log-sum-exp merge: the local window's keys do not depend on the
-    selection, so the window half of the attend runs on a side stream while
-    the k_bar refresh and the router run, then the selected blocks are
-    attended and the two partial results (fp32 o, lse) are merged.  Both
-    halves read HBM; the overlap fills the router's latency-bound phases
-    (selection, launches) with window traffic.  Capturable in a CUDA graph.
-    """
-    dev = q.device
-    N, H, D = q.shape
-    main = torch.cuda.current_stream(dev)
-    side = _side_stream(dev)
-    parts = torch.empty(2, N, H, D, device=dev, dtype=torch.float32)
-    lses = torch.empty(2, N, H, device=dev, dtype=torch.float32)
-    common = dict(block_size=sparse_block_size, local_blocks=local_blocks, sm_scale=sm_scale,
-                  block_table=block_table, seq_lens=seq_lens, rows_per_req=decode_query_len, lse=True)
-    side.wait_stream(main)
-    with torch.cuda.stream(side):
-        ops.decode_attend(q, k_cache, v_cache, _window_only_selection(N, dev), None, out=parts[0],
-                          lse_out=lses[0], **common)
-    if idx_cache is not None:
-        ops.kbar_paged(idx_cache, head_cls, block_table, seq_lens, k_bar, tail_pages)
-    K = max(1, min(int(budget or topm), int(topm)))
-    r = ops.route(idx_q, k_bar, block_size=sparse_block_size, local_blocks=local_blocks, topk=K, topm=topm,
-                  idx_scale=idx_scale, floor=prior_floor, sigma=sigma, seq_lens=seq_lens,
-                  rows_per_seq=max(1, int(decode_query_len)), block_table=block_table, cand=image_allow,
-                  want=("topi32", "bias"))
-    ops.decode_attend(q, k_cache, v_cache, r["topi32"], r["bias"], out=parts[1], lse_out=lses[1], skip_local=True,
-                      **common)
-    main.wait_stream(side)
-    ops.lse_merge(parts, lses, out_dtype=output.dtype, out=output)
-    return r["topi32"], r["bias"]
