@@ -232,14 +232,30 @@ def build_rank(S_local, seed, dev):
 STEP_LAUNCHES = 4   # k_bar tail refresh, router scores, router selection, attend
 
 
+def fork_kbar_refresh(st, fn):
+    """Run this step's k_bar tail-page refresh on a second stream.  The tail
+    page holds the newest token, so it is inside the local window and never a
+    remote candidate of this step's router: the refresh only has to land
+    before the next step, and its latency-bound launch overlaps the router's
+    score pass.  Returns the stream to join at the end of the step."""
+    main = torch.cuda.current_stream()
+    side = st.setdefault("side", torch.cuda.Stream())
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        fn()
+    return side
+
+
 def run_step(st):
     """One decode step through the library (device-resident inputs)."""
     from srswa import ops
-    ops.kbar_paged(st["idx"], st["hc"], st["bt"], st["sl"], st["kbar"], tail_pages=1)
+    side = fork_kbar_refresh(st, lambda: ops.kbar_paged(st["idx"], st["hc"], st["bt"], st["sl"], st["kbar"],
+                                                        tail_pages=1))
     r = ops.route(st["iq"], st["kbar"], block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=IDX_SCALE,
                   floor=FLOOR, sigma=SIGMA, seq_lens=st["sl"], block_table=st["bt"], want=("topi32", "bias"))
     st["topi"], st["bias"] = r["topi32"], r["bias"]
     run_attend(st)
+    torch.cuda.current_stream().wait_stream(side)
 
 
 def run_step_public(st, q, iq):
@@ -249,8 +265,9 @@ def run_step_public(st, q, iq):
     if "idx_buf" not in st:
         st["idx_buf"] = torch.empty(q.shape[0], M, dtype=torch.int32, device=q.device)
         st["bias_buf"] = torch.empty(q.shape[0], M, dtype=torch.float32, device=q.device)
-    paged.kbar_refresh_tail(kv_cache=st["idx"], k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"],
-                            head_cls=st["hc"], block_size=BS, tail_pages=1)
+    side = fork_kbar_refresh(st, lambda: paged.kbar_refresh_tail(
+        kv_cache=st["idx"], k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"], head_cls=st["hc"],
+        block_size=BS, tail_pages=1))
     w = paged.route_decode(idx_q=iq, k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"], image_allow=None,
                            out_idx=st["idx_buf"], out_bias=st["bias_buf"], max_block=st["bt"].shape[1],
                            block_size=BS, local_blocks=L, decode_query_len=1, idx_scale=IDX_SCALE,
@@ -259,6 +276,7 @@ def run_step_public(st, q, iq):
     tb = st["bias_buf"][:, :w].unsqueeze(0).expand(HKV, -1, -1)
     paged.dash_sparse_attn_decode(q, st["k"], st["v"], ti, tb, st["bt"], st["sl"], HKV, SM_SCALE, st["out"], 1,
                                   local_blocks=L, sparse_block_size=BS)
+    torch.cuda.current_stream().wait_stream(side)
 
 
 def run_attend(st):
