@@ -584,8 +584,9 @@ __device__ __forceinline__ unsigned long long min_u64(unsigned long long a, unsi
 // with the same result as warp_topm_regs.  The M-th largest of the 32 lane
 // maxima (bitonic sort across the lanes) is a lower bound of the M-th largest
 // key, since at least M keys reach it; the keys at or above it (normally a
-// few more than M) go to the warp's 64-entry scratch and one 64-key bitonic
-// sort (two keys per lane) orders them.  More than 64 such keys: the
+// few more than M) go to the warp's 64-entry scratch and one bitonic sort
+// orders them: 32 keys, one per lane, when at most 32 survive (the usual
+// case), else 64 keys, two per lane.  More than 64 such keys: the
 // round-based warp_topm_regs.
 template <int NPL>
 __device__ __forceinline__ unsigned long long warp_topm_filtered(unsigned long long (&v)[NPL], int M, int lane,
@@ -623,6 +624,21 @@ __device__ __forceinline__ unsigned long long warp_topm_filtered(unsigned long l
 #pragma unroll
   for (int k = 0; k < NPL; ++k)
     if (v[k] != 0ull && v[k] >= t0) scratch[pos++] = v[k];
+  if (total <= 32) {  // warp-uniform: one key per lane, a 32-key descending bitonic sort
+    __syncwarp();
+    unsigned long long e = lane < total ? scratch[lane] : 0ull;
+    __syncwarp();
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        const unsigned long long p = shfl_xor_u64(e, j);
+        const bool take_max = ((lane & j) == 0) == ((lane & k) == 0);
+        e = take_max ? max_u64(e, p) : min_u64(e, p);
+      }
+    }
+    return lane < M ? e : 0ull;
+  }
   for (int i = total + lane; i < 64; i += 32) scratch[i] = 0ull;
   __syncwarp();
   unsigned long long e0 = scratch[lane], e1 = scratch[lane + 32];  // element i = 32 * slot + lane
