@@ -128,3 +128,29 @@ def test_lse_merge_vs_oracle(cuda):
     fin = np.isfinite(ref_l)
     np.testing.assert_allclose(l.cpu().numpy()[fin], ref_l[fin], rtol=1e-5, atol=1e-5)
 
+
+
+@pytest.mark.parametrize("R", [70, 256])
+def test_decode_many_rows_split_last_wave(cuda, R):
+    """Enough (row, head) items for several waves of CTAs: the rows of a
+    nearly empty last wave are attended split over clusters (the split left
+    open), the others unsplit.  Same outputs and lse as every row unsplit
+    (fp32, within 1e-5) and as the oracle on a sample of rows (1e-4).  Two
+    KV heads and short requests keep the host-side cache small."""
+    rng = np.random.default_rng(R)
+    H, Hkv, D, BS, L, K = 10, 2, 128, 64, 8, 8
+    seqs = list(rng.integers(520, 800, R))
+    bt, kc, vc, q, idx, bias = _paged_case(rng, R, H, Hkv, D, BS, L, K, seqs, extra_pages=0)
+    args = [T(q, cuda, torch.bfloat16), T(kc, cuda, torch.bfloat16), T(vc, cuda, torch.bfloat16), T(idx, cuda),
+            T(bias, cuda)]
+    kw = dict(block_size=BS, local_blocks=L, sm_scale=0.088, block_table=T(bt, cuda),
+              seq_lens=T(np.asarray(seqs, np.int32), cuda), lse=True)
+    out_auto, lse_auto = ops.decode_attend(*args, out=torch.empty(R, H, D, device=cuda), **kw)
+    out_one, lse_one = ops.decode_attend(*args, out=torch.empty(R, H, D, device=cuda), nsplit=1, **kw)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out_auto.cpu().numpy(), out_one.cpu().numpy(), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(lse_auto.cpu().numpy(), lse_one.cpu().numpy(), rtol=1e-5, atol=1e-5)
+    rows = np.unique(np.concatenate([np.arange(5), np.arange(R - 30, R)]))
+    ref, _ = O.paged_decode(q[rows], kc, vc, O.dedup_rows(idx[rows])[None], bias[rows][None], bt[rows],
+                            np.asarray(seqs)[rows], 0.088, 1, L, BS)
+    np.testing.assert_allclose(out_auto.cpu().numpy()[rows], ref, rtol=1e-4, atol=1e-4)

@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(kAttendThreads) attend_rows_kernel(const Atten
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nsplit = a.nsplit;
-  const int64_t row = blockIdx.x / nsplit;
+  const int64_t row = a.row0 + blockIdx.x / nsplit;
   const int split = blockIdx.x % nsplit;
   const int h = blockIdx.y;
   const int hk = static_cast<int>(h / (a.H / a.Hkv));
@@ -331,7 +331,8 @@ static int launch_attend(const AttendArgs& a, cudaStream_t st) {
 // decode at 16 to 256 requests per GPU with fixed split counts (best: 2 at
 // 160 items, 1 from 320 items up).  Smallest modelled time wins, by at least
 // 3 % over a smaller split.
-static int auto_nsplit(const AttendArgs& a, int64_t D, int kv_dtype) {
+// Resident CTAs of the attend kernel per SM and the SM count (cached per device).
+static double attend_slots(int64_t D, int kv_dtype) {
   static int sms[64] = {0}, per_sm[64][2][2] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
@@ -351,7 +352,11 @@ static int auto_nsplit(const AttendArgs& a, int64_t D, int kv_dtype) {
              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<64, SRSWA_F16>, kAttendThreads, 0);
     per_sm[dev][di][ki] = e == cudaSuccess && nb > 0 ? nb : 4;
   }
-  const double slots = static_cast<double>(sms[dev]) * per_sm[dev][di][ki];
+  return static_cast<double>(sms[dev]) * per_sm[dev][di][ki];
+}
+
+static int auto_nsplit(const AttendArgs& a, int64_t D, int kv_dtype) {
+  const double slots = attend_slots(D, kv_dtype);
   const double items = static_cast<double>(a.N) * a.H;
   const double keys = static_cast<double>(a.LW) + static_cast<double>(a.K) * a.BS;
   int best = 1;
@@ -367,6 +372,38 @@ static int auto_nsplit(const AttendArgs& a, int64_t D, int kv_dtype) {
   return best;
 }
 
+template <int D, int KVT>
+static int launch_attend_rows(AttendArgs a, cudaStream_t st);
+
+// With unsplit items the last wave of CTAs can run nearly empty (cfg3: 2560
+// (row, head) items on 592 resident CTAs = 4.32 waves, the fifth a third
+// full).  When the caller leaves the split open and the model picks 1, the
+// rows that fill whole waves run unsplit and the remaining rows run first,
+// split over clusters so that they cover the GPU for a fraction of a CTA's
+// time: e.g. 20 tail rows x 10 heads x 2 CTAs, then 236 rows in 4 full
+// waves.  Same results (the split merges in a cluster as any split does).
+template <int D, int KVT>
+static int launch_attend_rows(AttendArgs a, cudaStream_t st) {
+  if (a.nsplit == 1 && a.split_tail) {
+    const double slots = attend_slots(D, KVT);
+    const int64_t items = a.N * a.H;
+    const int64_t full = static_cast<int64_t>(items / slots);
+    const int64_t r1 = static_cast<int64_t>((static_cast<double>(full) * slots) / static_cast<double>(a.H));
+    const int64_t tail_rows = a.N - r1;
+    const int64_t nt = tail_rows > 0 ? static_cast<int64_t>(slots / static_cast<double>(tail_rows * a.H)) : 0;
+    if (full >= 1 && r1 > 0 && tail_rows > 0 && nt >= 2) {
+      AttendArgs t = a;
+      t.row0 = a.row0 + r1;
+      t.N = tail_rows;
+      t.nsplit = static_cast<int>(nt > 8 ? 8 : nt);
+      int rc = launch_attend<D, KVT>(t, st);
+      if (rc) return rc;
+      a.N = r1;
+    }
+  }
+  return launch_attend<D, KVT>(a, st);
+}
+
 int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   if (a.N == 0) return 0;
   if (!(D == 64 || D == 128)) return SRSWA_EUNSUPPORTED;
@@ -376,16 +413,17 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   if (a.K + a.LW / a.BS + 2 > kAttendMaxSlots) return SRSWA_ETOOLARGE;
   if (a.H >= 65536) return SRSWA_ETOOLARGE;
   int nsplit = a.nsplit;
+  a.split_tail = nsplit <= 0 ? 1 : 0;
   if (nsplit <= 0) nsplit = auto_nsplit(a, D, kv_dtype);
   if (nsplit < 1 || nsplit > 8) return SRSWA_EUNSUPPORTED;
-  if (a.N * nsplit >= (1ll << 31)) return SRSWA_ETOOLARGE;
+  if (a.N * 8 >= (1ll << 31)) return SRSWA_ETOOLARGE;
   a.nsplit = nsplit;
   if (D == 128) {
-    if (kv_dtype == SRSWA_BF16) return launch_attend<128, SRSWA_BF16>(a, st);
-    return launch_attend<128, SRSWA_F16>(a, st);
+    if (kv_dtype == SRSWA_BF16) return launch_attend_rows<128, SRSWA_BF16>(a, st);
+    return launch_attend_rows<128, SRSWA_F16>(a, st);
   }
-  if (kv_dtype == SRSWA_BF16) return launch_attend<64, SRSWA_BF16>(a, st);
-  return launch_attend<64, SRSWA_F16>(a, st);
+  if (kv_dtype == SRSWA_BF16) return launch_attend_rows<64, SRSWA_BF16>(a, st);
+  return launch_attend_rows<64, SRSWA_F16>(a, st);
 }
 
 __global__ void lse_merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ lse_parts,

@@ -55,6 +55,8 @@ struct AttendArgs {
   int64_t s_l_seq, s_l_t;
   int nsplit;      // CTAs per (row, head); 0 = choose
   int skip_local;  // 1: attend remote selections only
+  int64_t row0;    // first row of this launch (rows row0 .. row0 + N - 1)
+  int split_tail;  // the split was left open: a nearly empty last wave may be split
 };
 
 template <int KVT>
