@@ -407,37 +407,43 @@ __global__ void __launch_bounds__(kCandWarps * 32) page_cand_kernel(const PgCand
     p = p < 0 ? 0 : (p > a.n_q - 1 ? a.n_q - 1 : p);
     my_qp = __ldg(a.qpi + b * a.s_qpi + p);
   }
+  // runs of consecutive rows with the same page: bit r set where a run starts
+  const int64_t up = __shfl_up_sync(0xffffffffu, my_qp, 1);
+  const unsigned starts = __ballot_sync(0xffffffffu, lane < nr && (lane == 0 || up != my_qp));
+  const unsigned rows_mask = nr >= 32 ? 0xffffffffu : ((1u << nr) - 1u);
   const bool w32 = (a.nblk & 3) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 3) == 0;
   const int4* dr = a.desc + b * a.nblk;
-  uint32_t anyrows = 0;  // bit r: row r has a candidate among this lane's blocks
+  uint8_t* const out0 = a.out + (b * a.cq + row0) * a.nblk;
+  unsigned anyrows = 0;  // bit r: row r has a candidate among this lane's blocks
   for (int64_t base = 0; base < a.nblk; base += 128) {
     const int64_t c0 = base + 4 * lane;
-    int64_t prev = 0;
-    uint32_t word = 0;
-    for (int r = 0; r < nr; ++r) {
-      const int64_t qp = a.flat ? 0 : static_cast<int64_t>(__shfl_sync(0xffffffffu, my_qp, r));
-      if (r == 0 || qp != prev) {  // warp-uniform
-        word = (a.flat || qp >= 0) ? cand_word(a, b, dr, c0, qp) : 0u;
-        prev = qp;
-      }
-      anyrows |= (word != 0 ? 1u : 0u) << r;
-      uint8_t* row = a.out + (b * a.cq + row0 + r) * a.nblk;
+    unsigned todo = starts;
+    while (todo) {  // warp-uniform: one mask word per run, stored to each of its rows
+      const int rs = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int re = todo ? __ffs(todo) - 1 : nr;
+      const int64_t qp = a.flat ? 0 : static_cast<int64_t>(__shfl_sync(0xffffffffu, my_qp, rs));
+      const uint32_t word = (a.flat || qp >= 0) ? cand_word(a, b, dr, c0, qp) : 0u;
+      if (word) anyrows |= rows_mask & ((re >= 32 ? 0xffffffffu : ((1u << re) - 1u)) & ~((1u << rs) - 1u));
       if (c0 < a.nblk) {
+        uint8_t* p = out0 + static_cast<int64_t>(rs) * a.nblk + c0;
         if (w32) {
-          *reinterpret_cast<uint32_t*>(row + c0) = word;
+          for (int r = rs; r < re; ++r, p += a.nblk) *reinterpret_cast<uint32_t*>(p) = word;
         } else {
+          for (int r = rs; r < re; ++r, p += a.nblk) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (c0 + e < a.nblk) row[c0 + e] = static_cast<uint8_t>(word >> (8 * e));
+            for (int e = 0; e < 4; ++e)
+              if (c0 + e < a.nblk) p[e] = static_cast<uint8_t>(word >> (8 * e));
+          }
         }
       }
     }
   }
   if (!a.fallback) return;  // rows without a candidate stay zero
-  const uint32_t any = __reduce_or_sync(0xffffffffu, anyrows);
+  const unsigned any = __reduce_or_sync(0xffffffffu, anyrows);
   for (int r = 0; r < nr; ++r) {
     if ((any >> r) & 1u) continue;
-    uint8_t* row = a.out + (b * a.cq + row0 + r) * a.nblk;
+    uint8_t* row = out0 + static_cast<int64_t>(r) * a.nblk;
     for (int64_t c = lane; c < a.nblk; c += 32) row[c] = 1;
   }
 }
