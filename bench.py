@@ -56,11 +56,12 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx", "pagegate"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx", "pagegate", "rope"],
                     help="decode = cfg3 (default, the headline); prefill = cfg2; train = cfg4 fwd+bwd; "
                          "route = the cfg3 router alone (k_bar cache + block table, no KV; for profiling); "
                          "longctx = cfg5 attention share (12 layers, one 1M-token sequence, split-KV); "
-                         "pagegate = PageGate candidate masks of a cfg2-shaped prefill")
+                         "pagegate = PageGate candidate masks of a cfg2-shaped prefill; "
+                         "rope = page2d RoPE coordinates + fused rotary of a cfg2-shaped prefill")
     ap.add_argument("--layers", type=int, default=12, help="longctx: decoder layers")
     ap.add_argument("--batch", type=int, default=0, help="prefill/train batch override (smaller cases)")
     ap.add_argument("--seq", type=int, default=0, help="prefill/train sequence override")
@@ -573,6 +574,58 @@ def main_pagegate(args):
     return 0
 
 
+def main_rope(args):
+    """page2d RoPE of a cfg2-shaped prefill (B=4, T=16384, 10 heads x 128 and
+    the single-head index projections): page-bucket coordinates from the
+    token ids, then the two-axis rotary applied in place to q, k, idx_q and
+    idx_k (bf16, tables rounded to bf16 as the reference casts them).
+    HBM-bound: every activation is read and written once."""
+    from srswa import ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, T = (args.batch or 4), (args.seq or 16384)
+    ids = torch.from_numpy(page_doc(B, T, 5)).to(dev)
+    g = torch.Generator(device=dev).manual_seed(6)
+    mk = lambda h: torch.randn(B, h, T, D, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
+    q, k, iq, ik = mk(H), mk(HKV), mk(1), mk(1)
+    inv_tok = (1.0 / (10000.0 ** (torch.arange(63, dtype=torch.float32) / 63))).to(dev)
+    inv_page = torch.ones(1, device=dev)
+    state = {}
+
+    def coords():
+        tok, page, _, _ = ops.rope2d_pos(ids, 128815, 128827, T)
+        state["tok"], state["page"] = tok, page
+
+    def step():
+        coords()
+        for x in (q, k, iq, ik):
+            ops.rope2d_apply_(x.transpose(1, 2), state["tok"], state["page"], inv_tok, inv_page, 2)
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    times, g1 = timed_graph(step, args.steps, args.warmup, flush, not args.no_graph)
+    ms = sum(times) / len(times)
+    at, g2 = timed_graph(lambda: ops.rope2d_apply_(q.transpose(1, 2), state["tok"], state["page"], inv_tok,
+                                                   inv_page, 2), args.steps, args.warmup, flush, not args.no_graph)
+    ams = sum(at) / len(at)
+    act = sum(x.numel() * 2 for x in (q, k, iq, ik))
+    step_bytes = 2 * act + B * T * (8 * 3 + 16)          # activations read + written; ids, tok, page
+    q_bytes = 2 * q.numel() * 2 + B * T * 16
+    peak, src = peaks()
+    print(json.dumps({
+        "metric": "page2d RoPE (prefill): GB/s vs HBM", "value": step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_step": ms * 1e3,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic token ids and activations",
+        "config": {"workload": "page2d RoPE: coordinates + fused rotary of q, k, idx_q, idx_k",
+                   "global_batch": B, "seq_len": T, "heads": H, "head_dim": D,
+                   "l2": "flushed before every timed step", "bytes_per_step": step_bytes},
+        "roofline": {"bound": "hbm", "kernel": "rope2d_apply_kernel (q)", "achieved": q_bytes / (ams * 1e-3) / 1e9,
+                     "peak": peak, "unit": "GB/s", "frac": q_bytes / (ams * 1e-3) / 1e9 / peak,
+                     "peak_source": src, "us": ams * 1e3, "algorithmic_bytes_per_launch": q_bytes},
+        "gpu_launches": 7 * args.steps}), flush=True)
+    del g1, g2
+    return 0
+
+
 def main_longctx(args):
     """cfg5 attention share: one decode step of a 1M-token sequence through
     the SR-SWA attention of 12 layers, split-KV over the ranks (rank g owns a
@@ -699,6 +752,8 @@ def main():
         return main_longctx(args)
     if args.workload == "pagegate":
         return main_pagegate(args)
+    if args.workload == "rope":
+        return main_rope(args)
     if args.workload != "decode" and args.impl != "reference":
         return main_dense(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -171,6 +171,12 @@ def test_rope_long_rows_vs_oracle(cuda, span):
     sb = f32_to_bf16_bits(rs[:, kl - Sx:kl]).float().numpy()
     ref = PR.apply_rotary(xb.float().numpy(), cb, sb)
     np.testing.assert_allclose(x.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+    # fp32 activations with fp32 tables, [B, S, H, D] layout (heads_first=False)
+    xf = torch.from_numpy(rng.standard_normal((B, 512, 3, 128)).astype(np.float32))
+    xg = xf.to(cuda)
+    P.apply_rotary2d_(xg, tok[:, :512].contiguous(), page[:, :512].contiguous(), rot, heads_first=False)
+    reff = PR.apply_rotary(xf.numpy().transpose(0, 2, 1, 3), rc[:, :512], rs[:, :512]).transpose(0, 2, 1, 3)
+    np.testing.assert_allclose(xg.cpu().numpy(), reff, atol=1e-4, rtol=1e-4)
     # decode: 300 tokens with markers
     st = dict(page=r_page[:, -1].copy(), tok=r_tok[:, -1].copy(), pf_cnt=r_pf, n_pg=r_npg)
     dpage, dtok = page[:, -1].clone(), tok[:, -1].clone()

@@ -640,46 +640,87 @@ __global__ void __launch_bounds__(256) rope2d_table_kernel(const Rope2D r, int64
 // In place x <- x * cos + rotate_half(x) * sin over the first D features of
 // x [B, S, H, D] (strides s_b, s_s, s_h; D contiguous), feature f using pair
 // f mod half; cos / sin are rounded to table_dtype first (the reference casts
-// its tables to the activation dtype).  One thread per (b, s, h) and 8 pairs
-// (f, f + D/2).
+// its tables to the activation dtype).  One thread per (b, s) and 8 pairs
+// (f, f + D/2): the angles of a token are shared by its heads, so they are
+// computed once (once per pair when D covers the table) and every head is
+// rotated with them; 16-byte loads and stores where the rows allow.
+template <typename T>
+__device__ __forceinline__ void rope_load8(const T* p, bool vec, float* v) {
+  if constexpr (sizeof(T) == 2) {
+    if (vec) {
+      const uint4 u = *reinterpret_cast<const uint4*>(p);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { v[2 * e] = bf16_lo(w[e]); v[2 * e + 1] = bf16_hi(w[e]); }
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = static_cast<float>(p[e]);
+}
+template <typename T>
+__device__ __forceinline__ void rope_store8(T* p, bool vec, const float* v) {
+  if constexpr (sizeof(T) == 2) {
+    if (vec) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+        w[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) p[e] = static_cast<T>(v[e]);
+}
 template <typename T>
 __global__ void __launch_bounds__(256) rope2d_apply_kernel(const Rope2D r, T* x, int64_t B, int64_t S, int64_t H,
                                                            int D, int64_t s_b, int64_t s_s, int64_t s_h,
                                                            int table_bf16) {
   const int g8 = D / 16;  // groups of 8 pairs per row
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= B * S * H * g8) return;
+  if (i >= B * S * g8) return;
   const int g = static_cast<int>(i % g8);
-  const int64_t rw = i / g8, h = rw % H, bs_ = rw / H, s = bs_ % S, b = bs_ / S;
+  const int64_t bs_ = i / g8, s = bs_ % S, b = bs_ / S;
   const int64_t t = __ldg(r.tok + b * r.s_pos + s), p = __ldg(r.page + b * r.s_pos + s);
-  T* row = x + b * s_b + s * s_s + h * s_h;
   const int hd = D / 2;
-  float lo[8], hi[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    lo[e] = static_cast<float>(row[8 * g + e]);
-    hi[e] = static_cast<float>(row[hd + 8 * g + e]);
-  }
+  const bool same = hd == r.half;  // both halves of a pair use the same angle
+  float c1[8], s1[8], c2[8], s2[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int f = 8 * g + e;
-    float s1, c1, s2, c2;
-    sincosf(rope_angle(r, t, p, f % r.half), &s1, &c1);
-    sincosf(rope_angle(r, t, p, (f + hd) % r.half), &s2, &c2);
-    if (table_bf16) {
-      c1 = __bfloat162float(__float2bfloat16_rn(c1));
-      s1 = __bfloat162float(__float2bfloat16_rn(s1));
-      c2 = __bfloat162float(__float2bfloat16_rn(c2));
-      s2 = __bfloat162float(__float2bfloat16_rn(s2));
+    sincosf(rope_angle(r, t, p, f % r.half), &s1[e], &c1[e]);
+    if (same) {
+      c2[e] = c1[e];
+      s2[e] = s1[e];
+    } else {
+      sincosf(rope_angle(r, t, p, (f + hd) % r.half), &s2[e], &c2[e]);
     }
-    const float a = lo[e], bb = hi[e];
-    lo[e] = a * c1 - bb * s1;
-    hi[e] = bb * c2 + a * s2;
+    if (table_bf16) {
+      c1[e] = __bfloat162float(__float2bfloat16_rn(c1[e]));
+      s1[e] = __bfloat162float(__float2bfloat16_rn(s1[e]));
+      c2[e] = __bfloat162float(__float2bfloat16_rn(c2[e]));
+      s2[e] = __bfloat162float(__float2bfloat16_rn(s2[e]));
+    }
   }
+  T* base = x + b * s_b + s * s_s;
+  const bool vec = ((reinterpret_cast<uintptr_t>(base) | static_cast<uintptr_t>(s_h * sizeof(T)) |
+                     static_cast<uintptr_t>(hd * sizeof(T))) & 15) == 0;
+  for (int64_t h = 0; h < H; ++h) {
+    T* row = base + h * s_h;
+    float lo[8], hi[8];
+    rope_load8(row + 8 * g, vec, lo);
+    rope_load8(row + hd + 8 * g, vec, hi);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    row[8 * g + e] = static_cast<T>(lo[e]);
-    row[hd + 8 * g + e] = static_cast<T>(hi[e]);
+    for (int e = 0; e < 8; ++e) {
+      const float a = lo[e], bb = hi[e];
+      lo[e] = a * c1[e] - bb * s1[e];
+      hi[e] = bb * c2[e] + a * s2[e];
+    }
+    rope_store8(row + 8 * g, vec, lo);
+    rope_store8(row + hd + 8 * g, vec, hi);
   }
 }
 
@@ -755,8 +796,8 @@ extern "C" int srswa_rope2d_apply(void* x, int dtype, int64_t B, int64_t S, int6
   Rope2D r = {tok, page, s_pos, inv_tok, inv_page, static_cast<int>(n_tok), static_cast<int>(n_tok + page_pairs),
               static_cast<int>(page_mod)};
   if (int rc = rope2d_check(r)) return rc;
-  const int64_t n = B * S * H * (D / 16);
-  if (n == 0) return 0;
+  const int64_t n = B * S * (D / 16);  // threads: (token, 8 pairs); heads looped inside
+  if (n == 0 || H == 0) return 0;
   SRSWA_CHECK_ARG(cdiv<int64_t>(n, 256) <= INT32_MAX, SRSWA_ETOOLARGE);
   const unsigned grid = static_cast<unsigned>(cdiv<int64_t>(n, 256));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
