@@ -259,9 +259,10 @@ def run_step(st):
     torch.cuda.current_stream().wait_stream(side)
 
 
-def run_step_public(st, q, iq):
+def run_step_public(st, q, iq, kv_ready=None):
     """The same decode step through the public paged API (SGLang signatures):
-    kbar_refresh_tail, route_decode, dash_sparse_attn_decode."""
+    kbar_refresh_tail, route_decode, dash_sparse_attn_decode.  kv_ready: a
+    stream whose work (q and the new K/V rows) the attend must wait for."""
     from srswa import paged
     if "idx_buf" not in st:
         st["idx_buf"] = torch.empty(q.shape[0], M, dtype=torch.int32, device=q.device)
@@ -275,6 +276,8 @@ def run_step_public(st, q, iq):
                            prior_floor=FLOOR, sigma=SIGMA, topm=M, budget=K)
     ti = st["idx_buf"][:, :w].unsqueeze(0).expand(HKV, -1, -1)
     tb = st["bias_buf"][:, :w].unsqueeze(0).expand(HKV, -1, -1)
+    if kv_ready is not None:
+        torch.cuda.current_stream().wait_stream(kv_ready)
     paged.dash_sparse_attn_decode(q, st["k"], st["v"], ti, tb, st["bt"], st["sl"], HKV, SM_SCALE, st["out"], 1,
                                   local_blocks=L, sparse_block_size=BS)
     torch.cuda.current_stream().wait_stream(side)
@@ -886,7 +889,8 @@ def main():
             "cpu_baseline": cpu,
             "e2e": None if e2e is None else {
                 "value": bytes_all / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
-                "how": "one pinned H2D of the step's packed inputs, cache append, kbar_refresh_tail + "
+                "how": "pinned H2D of the step's inputs (router's inputs first; q and the new K/V rows "
+                       "on a second stream beside the router), cache append, kbar_refresh_tail + "
                        "route_decode + dash_sparse_attn_decode, D2H of the output; one CUDA graph per step",
                 "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all},
             "gpu_launches": STEP_LAUNCHES * args.steps,
@@ -900,12 +904,14 @@ def main():
 
 
 def e2e_measure(st, S_local, args, dev):
-    """Per step: one H2D copy of this step's inputs packed in a pinned host
-    buffer (q, idx_q, the new token's K / V / index-key rows and its cache
-    slot), the append to the paged caches, the decode step through the public
-    paged API, and the D2H copy of the output; the
-    step is captured once in a CUDA graph (as a serving loop's decode step)
-    and replayed, copies included."""
+    """Per step: the H2D copies of this step's inputs from pinned host
+    buffers, the append of the new token to the paged caches, the decode step
+    through the public paged API, and the D2H copy of the output; the step is
+    captured once in a CUDA graph (as a serving loop's decode step) and
+    replayed, copies included.  The inputs travel in two packed copies: the
+    router's (idx_q, the new index-key row, the cache slots) first, then q
+    and the new K / V rows on a second stream, appended while the router
+    runs and joined before the attend."""
     R = len(S_local)
     g = torch.Generator().manual_seed(77)
     hq = torch.randn(R, H, D, generator=g).to(torch.bfloat16)
@@ -917,25 +923,34 @@ def e2e_measure(st, S_local, args, dev):
     page = torch.tensor([int(bt[r, (s - 1) // BS]) for r, s in enumerate(S_local)], dtype=torch.int64)
     slot = torch.tensor([(s - 1) % BS for s in S_local], dtype=torch.int64)
     hslot = torch.stack([page, slot])
-    parts = [hq, hiq, hk, hv, hik, hslot]
-    raw = [x.contiguous().view(-1).view(torch.uint8) for x in parts]
-    hin = torch.cat(raw).pin_memory()                      # one pinned buffer, one H2D copy per step
-    din = torch.empty_like(hin, device=dev)
-    views, o = [], 0
-    for x, r_ in zip(parts, raw):
-        views.append(din[o:o + r_.numel()].view(x.dtype).view(x.shape))
-        o += r_.numel()
-    q, iq, nk, nv, nik, sl_ = views
+
+    def pack(parts):
+        raw = [x.contiguous().view(-1).view(torch.uint8) for x in parts]
+        hbuf = torch.cat(raw).pin_memory()
+        dbuf = torch.empty_like(hbuf, device=dev)
+        views, o = [], 0
+        for x, r_ in zip(parts, raw):
+            views.append(dbuf[o:o + r_.numel()].view(x.dtype).view(x.shape))
+            o += r_.numel()
+        return hbuf, dbuf, views
+
+    ha, da, (iq, nik, sl_) = pack([hiq, hik, hslot])   # the router's inputs
+    hb, db, (q, nk, nv) = pack([hq, hk, hv])           # the attend's inputs
     hout = torch.empty(R, H, D, dtype=torch.bfloat16).pin_memory()
-    h2d = hin.numel()
+    h2d = ha.numel() + hb.numel()
     d2h = hout.numel() * hout.element_size()
+    kv_stream = torch.cuda.Stream()
 
     def step():
-        din.copy_(hin, non_blocking=True)
-        st["k"][sl_[0], sl_[1]] = nk
-        st["v"][sl_[0], sl_[1]] = nv
+        main = torch.cuda.current_stream()
+        da.copy_(ha, non_blocking=True)
+        kv_stream.wait_stream(main)
+        with torch.cuda.stream(kv_stream):
+            db.copy_(hb, non_blocking=True)
+            st["k"][sl_[0], sl_[1]] = nk
+            st["v"][sl_[0], sl_[1]] = nv
         st["idx"][sl_[0], sl_[1]] = nik
-        run_step_public(st, q, iq)
+        run_step_public(st, q, iq, kv_ready=kv_stream)
         hout.copy_(st["out"], non_blocking=True)
 
     s_ = torch.cuda.Stream()

@@ -76,9 +76,12 @@ __global__ void __launch_bounds__(kAttendThreads) attend_rows_kernel(const Atten
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nsplit = a.nsplit;
-  const int64_t row = a.row0 + blockIdx.x / nsplit;
+  // heads_inner: grid (heads x splits, rows), so that the CTAs of one row's
+  // heads are launched together and read the same key rows (whole 2560-byte
+  // rows of a page between them); else grid (rows x splits, heads)
+  const int64_t row = a.row0 + (a.heads_inner ? static_cast<int64_t>(blockIdx.y) : blockIdx.x / nsplit);
   const int split = blockIdx.x % nsplit;
-  const int h = blockIdx.y;
+  const int h = a.heads_inner ? static_cast<int>(blockIdx.x / nsplit) : static_cast<int>(blockIdx.y);
   const int hk = static_cast<int>(h / (a.H / a.Hkv));
   const int hi = static_cast<int>((static_cast<int64_t>(hk) * a.HI) / a.Hkv);
   int64_t seq, t, p, sg;
@@ -307,7 +310,8 @@ __global__ void __launch_bounds__(kAttendThreads) attend_rows_kernel(const Atten
 template <int D, int KVT>
 static int launch_attend(const AttendArgs& a, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(a.N * a.nsplit), static_cast<unsigned>(a.H), 1);
+  cfg.gridDim = a.heads_inner ? dim3(static_cast<unsigned>(a.H * a.nsplit), static_cast<unsigned>(a.N), 1)
+                              : dim3(static_cast<unsigned>(a.N * a.nsplit), static_cast<unsigned>(a.H), 1);
   cfg.blockDim = dim3(kAttendThreads, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
@@ -418,6 +422,7 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   if (nsplit < 1 || nsplit > 8) return SRSWA_EUNSUPPORTED;
   if (a.N * 8 >= (1ll << 31)) return SRSWA_ETOOLARGE;
   a.nsplit = nsplit;
+  a.heads_inner = (a.N <= 65535 && a.H * 8 <= 65535) ? 1 : 0;
   if (D == 128) {
     if (kv_dtype == SRSWA_BF16) return launch_attend_rows<128, SRSWA_BF16>(a, st);
     return launch_attend_rows<128, SRSWA_F16>(a, st);

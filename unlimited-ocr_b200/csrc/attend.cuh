@@ -57,6 +57,7 @@ struct AttendArgs {
   int skip_local;  // 1: attend remote selections only
   int64_t row0;    // first row of this launch (rows row0 .. row0 + N - 1)
   int split_tail;  // the split was left open: a nearly empty last wave may be split
+  int heads_inner; // grid (heads x splits, rows) instead of (rows x splits, heads)
 };
 
 template <int KVT>
