@@ -487,10 +487,15 @@ __device__ void warp_topm_smem(unsigned long long* k, int n, int M, unsigned lon
 // 16-byte loads per lane, 8 warps).  Register-capped for 3 CTAs per SM.
 constexpr int kChunkBlocks = 128;
 
+// Chunks of kChunkBlocks blocks per CTA: the row position and the block-table
+// slice are loaded once for all of them (two dependent round trips), then
+// the k_bar loads of one chunk after the other.
+constexpr int kScoreReps = 2;
 __global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const RouteArgs a, float* zout) {
-  __shared__ int32_t bts[kChunkBlocks];
+  constexpr int kSpan = kChunkBlocks * kScoreReps;
+  __shared__ int32_t bts[kSpan];
   const int64_t n = blockIdx.y;
-  const int64_t lo = static_cast<int64_t>(blockIdx.x) * kChunkBlocks;
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * kSpan;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t seq = n / a.rows_per_seq;
   const int64_t p = a.q_pos ? a.q_pos[n]
@@ -502,44 +507,47 @@ __global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const Rou
     const int64_t nb = (static_cast<int64_t>(a.seq_lens[seq]) + a.BS - 1) / a.BS;
     if (c_hi > nb) c_hi = nb;
   }
-  const int64_t hi = min(lo + kChunkBlocks, a.nblk);
+  const int64_t hi = min(lo + kSpan, a.nblk);
   const int64_t dhi = max(lo, min(hi, c_hi));  // blocks [lo, dhi) are remote
   float* zrow = zout + n * a.nblk;
   for (int64_t c = dhi + tid; c < hi; c += kRouteThreads) zrow[c] = kScoreNeg;
-  if (dhi == lo) return;  // CTA-uniform: nothing remote in this chunk
-  if (a.block_table && tid < dhi - lo) bts[tid] = a.block_table[seq * a.s_bt + lo + tid];
+  if (dhi == lo) return;  // CTA-uniform: nothing remote in this span
+  if (a.block_table)
+    for (int64_t i = tid; i < dhi - lo; i += kRouteThreads) bts[i] = a.block_table[seq * a.s_bt + lo + i];
   __syncthreads();
   const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
   float qv[4];
   load4(a.q, n * a.s_q + 4 * lane, a.q_dtype, qv);
-  const int64_t c0 = lo + warp * 16;
-  if (c0 >= dhi) return;  // warp-uniform
-  float4 f[16];
+  for (int rep = 0; rep < kScoreReps; ++rep) {
+    const int64_t c0 = lo + static_cast<int64_t>(rep) * kChunkBlocks + warp * 16;
+    if (c0 >= dhi) break;  // warp-uniform
+    float4 f[16];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int64_t c = c0 + i;
-    f[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (c < dhi) {
-      const int64_t off = a.block_table ? static_cast<int64_t>(bts[c - lo]) * a.s_kbar_c
-                                        : seq * a.s_kbar_b + c * a.s_kbar_c;
-      f[i] = __ldg(reinterpret_cast<const float4*>(a.kbar + off + 4 * lane));
+    for (int i = 0; i < 16; ++i) {
+      const int64_t c = c0 + i;
+      f[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < dhi) {
+        const int64_t off = a.block_table ? static_cast<int64_t>(bts[c - lo]) * a.s_kbar_c
+                                          : seq * a.s_kbar_b + c * a.s_kbar_c;
+        f[i] = __ldg(reinterpret_cast<const float4*>(a.kbar + off + 4 * lane));
+      }
     }
-  }
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    float part[8];
+    for (int h = 0; h < 2; ++h) {
+      float part[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 v = f[8 * h + i];
-      part[i] = qv[0] * v.x + qv[1] * v.y + qv[2] * v.z + qv[3] * v.w;
-    }
-    const float sdot = transpose_reduce8<32>(part, lane);
-    const int my = 4 * ((lane & 16) != 0) + 2 * ((lane & 8) != 0) + ((lane & 4) != 0);
-    const int64_t c = c0 + 8 * h + my;
-    if ((lane & 3) == 0 && c < dhi) {
-      float z = fminf(fmaxf(sdot * inv_sqrt_d, -kActClamp), kActClamp);
-      if (sdot != sdot) z = sdot;  // NaN stays NaN (then "not remote")
-      zrow[c] = z;
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = f[8 * h + i];
+        part[i] = qv[0] * v.x + qv[1] * v.y + qv[2] * v.z + qv[3] * v.w;
+      }
+      const float sdot = transpose_reduce8<32>(part, lane);
+      const int my = 4 * ((lane & 16) != 0) + 2 * ((lane & 8) != 0) + ((lane & 4) != 0);
+      const int64_t c = c0 + 8 * h + my;
+      if ((lane & 3) == 0 && c < dhi) {
+        float z = fminf(fmaxf(sdot * inv_sqrt_d, -kActClamp), kActClamp);
+        if (sdot != sdot) z = sdot;  // NaN stays NaN (then "not remote")
+        zrow[c] = z;
+      }
     }
   }
 }
@@ -1288,7 +1296,7 @@ static int route_chunk_launch(RouteArgs a, void* ws, size_t ws_bytes, cudaStream
     if (!ws || ws_bytes < chunk_workspace(a.N, a.nblk)) return SRSWA_EWORKSPACE;
     z = static_cast<float*>(ws);
   }
-  const int64_t nch = (a.nblk + kChunkBlocks - 1) / kChunkBlocks;
+  const int64_t nch = (a.nblk + kChunkBlocks * kScoreReps - 1) / (kChunkBlocks * kScoreReps);
   if (a.N >= 65536) return SRSWA_ETOOLARGE;
   route_score_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(a.N)), kRouteThreads, 0, st>>>(a, z);
   cudaError_t e = cudaGetLastError();
