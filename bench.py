@@ -264,9 +264,9 @@ def run_step_public(st, q, iq, kv_ready=None):
     kbar_refresh_tail, route_decode, dash_sparse_attn_decode.  kv_ready: a
     stream whose work (q and the new K/V rows) the attend must wait for."""
     from srswa import paged
-    if "idx_buf" not in st:
-        st["idx_buf"] = torch.empty(q.shape[0], M, dtype=torch.int32, device=q.device)
-        st["bias_buf"] = torch.empty(q.shape[0], M, dtype=torch.float32, device=q.device)
+    if "idx_buf" not in st:   # K slots wide: route_decode writes them in place
+        st["idx_buf"] = torch.empty(q.shape[0], K, dtype=torch.int32, device=q.device)
+        st["bias_buf"] = torch.empty(q.shape[0], K, dtype=torch.float32, device=q.device)
     side = fork_kbar_refresh(st, lambda: paged.kbar_refresh_tail(
         kv_cache=st["idx"], k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"], head_cls=st["hc"],
         block_size=BS, tail_pages=1))

@@ -155,6 +155,15 @@ def test_paged_kbar_and_route_golden(cuda):
     assert ties_only(oi[:, :Kb], ref_i, valid, g["scores"]) == 0
     np.testing.assert_allclose(ob[:, :Kb], ref_b, rtol=1e-5, atol=5e-4)
     assert (oi[:, Kb:] == -1).all() and (ob[:, Kb:] == 0).all()
+    # buffers exactly K slots wide are written in place by the kernel: same values
+    di = torch.full((R, Kb), 7, dtype=torch.int32, device=cuda)
+    db = torch.full((R, Kb), 3.0, device=cuda)
+    k2 = paged.route_decode(idx_q=T(g["idx_q"], cuda), k_bar=T(g["kbar"], cuda), block_table=bt, seq_lens=sl,
+                            image_allow=None, out_idx=di, out_bias=db, max_block=W, block_size=BS,
+                            local_blocks=L, decode_query_len=1, idx_scale=idx_scale, prior_floor=floor,
+                            sigma=sigma, topm=M, budget=Kb)
+    assert k2 == Kb
+    assert np.array_equal(di.cpu().numpy(), oi[:, :Kb]) and np.array_equal(db.cpu().numpy(), ob[:, :Kb])
 
 
 @pytest.mark.parametrize("S_list", [[16384, 131072, 50001, 700, 130]])

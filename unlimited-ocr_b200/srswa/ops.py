@@ -98,12 +98,13 @@ def kbar_paged(idx_cache, head_cls, block_table, seq_lens, kbar_cache, tail_page
 
 def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor, sigma,
           q_pos=None, seq_lens=None, rows_per_seq=1, block_table=None, cand=None,
-          want=("topi64", "bias", "valid"), nblk=None):
+          want=("topi64", "bias", "valid"), nblk=None, out=None):
     """Fused scores + selection for query rows idx_q [N, d].
 
     kbar: contiguous [B, nblk, d] (block_table None) or paged cache [P, d].
     Returns a dict with the requested outputs among topi64, topi32, bias,
-    valid, scores."""
+    valid, scores.  out: caller-owned tensors for some of them (contiguous,
+    [N, K] or [N, nblk], the output's dtype), written in place."""
     N, d = idx_q.shape
     if idx_q.stride(-1) != 1:
         idx_q = idx_q.contiguous()
@@ -119,11 +120,18 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
         nblk = bt.shape[1] if nblk is None else nblk
     _check_rows(N, rows_per_seq, kbar, bt, nblk)
     K, M = effective_km(topk, topm, nblk)
+    given = out or {}
     out = {}
     for name, dt, shape in (("topi64", torch.int64, (N, K)), ("topi32", torch.int32, (N, K)),
                             ("bias", torch.float32, (N, K)), ("valid", torch.uint8, (N, K)),
                             ("scores", torch.float32, (N, nblk))):
-        out[name] = torch.empty(shape, device=dev, dtype=dt) if name in want else None
+        t = given.get(name)
+        if t is not None:
+            if t.dtype != dt or tuple(t.shape) != shape or not t.is_contiguous() or t.device != dev:
+                raise ValueError(f"route: out[{name!r}] must be a contiguous {dt} {shape} tensor on {dev}")
+            out[name] = t
+        else:
+            out[name] = torch.empty(shape, device=dev, dtype=dt) if name in want else None
     qp = None if q_pos is None else q_pos.to(device=dev, dtype=torch.int64).contiguous().view(-1)
     sl = None if seq_lens is None else seq_lens.to(device=dev, dtype=torch.int32).contiguous()
     cnd, s_cand = _cand_args(cand, N, nblk)

@@ -68,14 +68,21 @@ def route_decode(*, idx_q, k_bar, block_table, seq_lens, image_allow, out_idx, o
     """Route decode rows idx_q [R*dql, d] against the k_bar cache.  Writes the
     first K = min(budget, topm) slots of out_idx (int32, -1 unused) and
     out_bias (fp32, 0 unused); remaining slots are set to -1 / 0.  Returns the
-    slot width written."""
+    slot width written.  Contiguous buffers exactly K slots wide are written
+    by the kernel directly (no copies)."""
     W = min(int(max_block), int(block_table.shape[1]))
     K = max(1, min(int(budget or topm), int(topm)))
+    Ke, _ = ops.effective_km(K, topm, W)
+    direct = (out_idx.dtype == torch.int32 and out_bias.dtype == torch.float32 and out_idx.is_contiguous()
+              and out_bias.is_contiguous() and out_idx.shape[-1] == Ke and out_bias.shape[-1] == Ke)
     r = ops.route(idx_q, k_bar, block_size=block_size, local_blocks=local_blocks, topk=K, topm=topm,
                   idx_scale=idx_scale, floor=prior_floor, sigma=sigma, seq_lens=seq_lens,
                   rows_per_seq=max(1, int(decode_query_len)), block_table=block_table[:, :W],
-                  cand=image_allow, want=("topi32", "bias"), nblk=W)
+                  cand=image_allow, want=("topi32", "bias"), nblk=W,
+                  out={"topi32": out_idx, "bias": out_bias} if direct else None)
     k = r["topi32"].shape[-1]
+    if direct:   # written in place: buffers exactly K slots wide
+        return out_slots or k
     out_idx[:, :k].copy_(r["topi32"])
     out_bias[:, :k].copy_(r["bias"])
     if out_idx.shape[-1] > k:
