@@ -64,3 +64,21 @@ def test_cpu_tensors_fail_loudly():
 def test_effective_km(topk, topm, nblk, K, M):
     # _infer_route_select: M = max(1, min(topm, nblk)) if topm > 0 else nblk; K = max(1, min(K, M))
     assert ops.effective_km(topk, topm, nblk) == (K, M)
+
+
+def test_arange_check_follows_tensor_and_version():
+    """The packing test of triton_gather_attention_e2e is kept per position_ids
+    tensor object and re-run after an in-place change or for a new tensor."""
+    import torch
+    from srswa.sparse_gather_e2e import _positions_are_arange
+    p = torch.arange(10)[None].repeat(2, 1)
+    assert _positions_are_arange(p, 10)
+    assert _positions_are_arange(p, 10)          # same object, same version
+    p[1, 3] = 0                                  # in place: the version counter moves
+    assert not _positions_are_arange(p, 10)
+    v = p[1:]                                    # a view shares the version counter
+    assert not _positions_are_arange(v, 10)
+    p[1, 3] = 3
+    assert _positions_are_arange(p, 10)
+    q = torch.arange(10)[None].repeat(2, 1) * 2  # another tensor
+    assert not _positions_are_arange(q, 10)

@@ -12,12 +12,33 @@ first slot, whose gradient is the block's, and the repeats get zero gradient.
 
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from . import ops
 from .sparse_gather import _btHd, _check_head_dim, _GatherAttnFn
 
 SPARSE_E2E_SENTINEL = 1
+
+
+_arange_check = None  # (weak reference to the position_ids tensor, its version, result)
+
+
+def _positions_are_arange(position_ids, T):
+    """position_ids == arange(T) on every row (the reference's packing test,
+    which reads the device).  The model passes one position_ids tensor to every
+    layer of a forward, so the answer is kept for that tensor object while its
+    in-place version counter is unchanged; a new or modified tensor is tested
+    again (a weak reference: a freed tensor can never match)."""
+    global _arange_check
+    c = _arange_check
+    if c is not None and c[0]() is position_ids and c[1] == position_ids._version:
+        return c[2]
+    ar = torch.arange(T, device=position_ids.device)
+    res = bool((position_ids == ar).all())
+    _arange_check = (weakref.ref(position_ids), position_ids._version, res)
+    return res
 
 
 def triton_gather_attention_e2e(query_states, key_states, value_states, block_indices, blk_bias_slots,
@@ -33,8 +54,7 @@ def triton_gather_attention_e2e(query_states, key_states, value_states, block_in
         return None
     if position_ids is None or position_ids.dim() != 2 or position_ids.shape[-1] != T:
         return None
-    ar = torch.arange(T, device=position_ids.device)
-    if not bool((position_ids == ar).all()):
+    if not _positions_are_arange(position_ids, T):
         return None
     _check_head_dim(query_states)
     nblk = (T + block_size - 1) // block_size
