@@ -79,7 +79,7 @@ def kbar_contig(idx_k: torch.Tensor, head_cls: torch.Tensor, block_size: int, ou
                                    B, S, d, block_size, hc.data_ptr(), out.data_ptr(), L.ptr(cv),
                                    L.stream_of(idx_k))
     L.check(rc, "srswa_kbar_contig")
-    return out, (cv.bool() if cv is not None else None)
+    return out, (cv.view(torch.bool) if cv is not None else None)
 
 
 def kbar_paged(idx_cache, head_cls, block_table, seq_lens, kbar_cache, tail_pages=0):
@@ -146,7 +146,7 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
                          L.ptr(out["valid"]), L.ptr(out["scores"]), L.ptr(ws), ws_n, L.stream_of(idx_q))
     L.check(rc, "srswa_route")
     if out["valid"] is not None:
-        out["valid"] = out["valid"].bool()
+        out["valid"] = out["valid"].view(torch.bool)  # 0 / 1 bytes: no copy
     return {k: v for k, v in out.items() if v is not None}
 
 
@@ -211,7 +211,7 @@ def route_merge_keys(keys, *, nblk_total, topk, topm, idx_scale, floor, sigma, o
                                         L.stream_of(keys))
     L.check(rc, "srswa_route_merge_keys")
     if out["valid"] is not None:
-        out["valid"] = out["valid"].bool()
+        out["valid"] = out["valid"].view(torch.bool)  # 0 / 1 bytes: no copy
     return {k: v for k, v in out.items() if v is not None}
 
 
@@ -240,7 +240,7 @@ def route_select(scores, cand, *, topk, topm, idx_scale, floor, sigma, want=("to
         if v is None:
             continue
         v = v.view(*shape[:-1], K)
-        res[k] = v.bool() if k == "valid" else v
+        res[k] = v.view(torch.bool) if k == "valid" else v
     return res
 
 
