@@ -259,17 +259,23 @@ def run_step(st):
     torch.cuda.current_stream().wait_stream(side)
 
 
-def run_step_public(st, q, iq, kv_ready=None):
+def run_step_public(st, q, iq, kv_ready=None, before_refresh=None):
     """The same decode step through the public paged API (SGLang signatures):
     kbar_refresh_tail, route_decode, dash_sparse_attn_decode.  kv_ready: a
-    stream whose work (q and the new K/V rows) the attend must wait for."""
+    stream whose work (q and the new K/V rows) the attend must wait for;
+    before_refresh: work the k_bar refresh depends on (the new index-key row),
+    run on the refresh's stream."""
     from srswa import paged
     if "idx_buf" not in st:   # K slots wide: route_decode writes them in place
         st["idx_buf"] = torch.empty(q.shape[0], K, dtype=torch.int32, device=q.device)
         st["bias_buf"] = torch.empty(q.shape[0], K, dtype=torch.float32, device=q.device)
-    side = fork_kbar_refresh(st, lambda: paged.kbar_refresh_tail(
-        kv_cache=st["idx"], k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"], head_cls=st["hc"],
-        block_size=BS, tail_pages=1))
+    def refresh():
+        if before_refresh is not None:
+            before_refresh()
+        paged.kbar_refresh_tail(kv_cache=st["idx"], k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"],
+                                head_cls=st["hc"], block_size=BS, tail_pages=1)
+
+    side = fork_kbar_refresh(st, refresh)
     w = paged.route_decode(idx_q=iq, k_bar=st["kbar"], block_table=st["bt"], seq_lens=st["sl"], image_allow=None,
                            out_idx=st["idx_buf"], out_bias=st["bias_buf"], max_block=st["bt"].shape[1],
                            block_size=BS, local_blocks=L, decode_query_len=1, idx_scale=IDX_SCALE,
@@ -949,8 +955,10 @@ def e2e_measure(st, S_local, args, dev):
             db.copy_(hb, non_blocking=True)
             st["k"][sl_[0], sl_[1]] = nk
             st["v"][sl_[0], sl_[1]] = nv
-        st["idx"][sl_[0], sl_[1]] = nik
-        run_step_public(st, q, iq, kv_ready=kv_stream)
+        def append_index_key():   # only the k_bar refresh reads it: off the router's path
+            st["idx"][sl_[0], sl_[1]] = nik
+
+        run_step_public(st, q, iq, kv_ready=kv_stream, before_refresh=append_index_key)
         hout.copy_(st["out"], non_blocking=True)
 
     s_ = torch.cuda.Stream()
