@@ -230,7 +230,24 @@ def build_rank(S_local, seed, dev):
     return st
 
 
-STEP_LAUNCHES = 4   # k_bar tail refresh, router scores, router selection, attend
+STEP_LAUNCHES = 5   # k_bar tail refresh, router scores, router selection, attend (last-wave rows, the rest)
+
+
+def count_launches(fn, default):
+    """Kernels of this library (names in the srswa namespace) that one call
+    of fn launches, counted by the profiler on an untimed call; `default` if
+    the profiler is unavailable."""
+    try:
+        from torch.autograd import DeviceType
+        from torch.profiler import ProfilerActivity, profile
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        n = sum(1 for e in prof.events() if e.device_type == DeviceType.CUDA and "srswa::" in e.name)
+        return n if n > 0 else default
+    except Exception:
+        return default
 
 
 def fork_kbar_refresh(st, fn):
@@ -845,6 +862,8 @@ def main():
                                args.steps, args.warmup, flush, not args.no_graph)
     rt_ms = sum(rt_times) / len(rt_times)
 
+    launches = count_launches(lambda: run_step(st), STEP_LAUNCHES)
+
     # e2e: host buffers through the public API, copies inside the timed region
     e2e = None
     if not args.no_e2e:
@@ -852,13 +871,13 @@ def main():
 
     # reduce across ranks: max time, sum bytes
     vec = torch.tensor([step_ms, att_ms, rt_ms, e2e["ms"] if e2e else 0.0], device=dev, dtype=torch.float64)
-    tot = torch.tensor([bytes_rank, a_b, e2e["h2d"] if e2e else 0, e2e["d2h"] if e2e else 0],
+    tot = torch.tensor([bytes_rank, a_b, e2e["h2d"] if e2e else 0, e2e["d2h"] if e2e else 0, launches],
                        device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(vec, op=dist.ReduceOp.MAX)
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
     step_ms, att_ms, rt_ms, e2e_ms = vec.tolist()
-    bytes_all, att_bytes_all, h2d_all, d2h_all = tot.tolist()
+    bytes_all, att_bytes_all, h2d_all, d2h_all, launches_all = tot.tolist()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -899,7 +918,7 @@ def main():
                        "on a second stream beside the router), cache append, kbar_refresh_tail + "
                        "route_decode + dash_sparse_attn_decode, D2H of the output; one CUDA graph per step",
                 "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all},
-            "gpu_launches": STEP_LAUNCHES * args.steps,
+            "gpu_launches": int(launches_all) * args.steps,   # all ranks, counted on one profiled step
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
