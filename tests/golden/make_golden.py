@@ -1,14 +1,14 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Runs ONLY in the build container, where the reference checkout is mounted
-read-only (default ``/root/reference``; override with ``SRSWA_REFERENCE``).  It
+Runs only where a read-only checkout of the reference is available (its
+location in ``SRSWA_REFERENCE``, else the build container's mount point).  It
 imports the reference's own code -- the HF PyTorch SR-SWA path, its Triton
 kernels under the Triton CPU interpreter, and the SGLang serving ops from the
 reference's wheel -- runs them on small seeded inputs and writes
-``tests/golden/<case>.npz`` (inputs + outputs + version metadata).  The GPU box
-never runs this script; tests there read the committed ``.npz`` files.
+``tests/golden/<case>.npz`` (inputs + outputs + version metadata).  GPU runs
+never execute this script; the tests there read the committed ``.npz`` files.
 
-Usage:  python tests/golden/make_golden.py
+Usage:  python tests/golden/make_golden.py [case ...]
 """
 
 from __future__ import annotations
