@@ -250,13 +250,18 @@ SRSWA_API int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const 
  * SRSWA_ETOOLARGE.  The first call on a device looks up the array's device
  * address (make it outside stream capture).  Calls share the array: calls
  * whose GPU work overlaps race and must be serialised by the caller.
- * Results equal srswa_gather_bwd's. */
+ * Results equal srswa_gather_bwd's, bit for bit.  The looked-up address is
+ * kept for the life of the process: a cudaDeviceReset (or any teardown of the
+ * device's primary context) while this library is loaded is not supported.
+ * srswa_gather_bwd_noalloc_status reads the last call's status word (the head
+ * of the array), as srswa_workspace_status does for a workspace. */
 SRSWA_API size_t srswa_gather_bwd_noalloc_max_scratch(void);
 SRSWA_API int srswa_gather_bwd_noalloc(const srswa_gather_desc* g, const void* q, const void* k,
                                        const void* v, const void* o, int64_t sob, int64_t sot, int64_t soh,
                                        const void* dout, const float* lse, const int32_t* sel,
                                        const float* bias, const int32_t* seg, void* dq, void* dk, void* dv,
                                        float* d_bias, srswa_stream_t stream);
+SRSWA_API int srswa_gather_bwd_noalloc_status(int* out, srswa_stream_t stream);
 
 /* ------------------------------------------------------------------ a9 --
  * Block-sparse decode attend over a paged (or contiguous) KV cache.
@@ -300,10 +305,15 @@ SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, co
                         const float* bias, const uint8_t* valid, void* out, float* lse_out,
                         srswa_stream_t stream);
 
-/* Reads and clears the library's device error word: non-zero when a kernel's
- * bounded wait on a tensor-core completion barrier expired (the kernel then
- * skipped its outputs and exited cleanly).  No reference counterpart. */
-SRSWA_API int srswa_device_status(int* out);
+/* Status of the last gather call that used `workspace`: the first 4 bytes of
+ * every gather workspace (srswa_gather_fwd / srswa_gather_bwd; the workspace
+ * sizes include them) are that call's status word, cleared when the call is
+ * enqueued.  0 = ok; otherwise the code of a tensor-core kernel's bounded
+ * wait on a completion barrier that expired (the kernel then skipped its
+ * outputs and exited cleanly).  Reads the word on `stream` and waits for that
+ * stream only.  Status is per call: concurrent calls on other workspaces never
+ * see each other's codes.  No reference counterpart. */
+SRSWA_API int srswa_workspace_status(const void* workspace, int* out, srswa_stream_t stream);
 
 /* Log-sum-exp merge of C split-KV partials: part c of o at o_parts + c *
  * s_o_part ([N,H,D] fp32, contiguous inside the part), of the log-sum-exp at

@@ -1,14 +1,14 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Runs only where a read-only checkout of the reference is available (its
-location in ``SRSWA_REFERENCE``, else the build container's mount point).  It
+Runs only where a read-only checkout of the reference is available; its
+location must be given in ``SRSWA_REFERENCE`` (the script refuses to guess).  It
 imports the reference's own code -- the HF PyTorch SR-SWA path, its Triton
 kernels under the Triton CPU interpreter, and the SGLang serving ops from the
 reference's wheel -- runs them on small seeded inputs and writes
 ``tests/golden/<case>.npz`` (inputs + outputs + version metadata).  GPU runs
 never execute this script; the tests there read the committed ``.npz`` files.
 
-Usage:  python tests/golden/make_golden.py [case ...]
+Usage:  SRSWA_REFERENCE=<reference checkout> python tests/golden/make_golden.py [case ...]
 """
 
 from __future__ import annotations
@@ -30,7 +30,9 @@ os.environ.setdefault("CODE_STAMP_LOG", "0")
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = os.environ.get("SRSWA_REFERENCE", "/root/reference")
+REF = os.environ.get("SRSWA_REFERENCE", "")
+# what the fixtures record as their source: the project, not a machine path
+REF_NAME = "dongf9527/Unlimited-OCR (hf-model-code/, wheel/sglang-0.5.20.dev10)"
 OUT = os.path.dirname(os.path.abspath(__file__))
 WHEEL = "wheel/sglang-0.5.20.dev10+g8d62f5fb9c-py3-none-any.whl"
 
@@ -101,7 +103,7 @@ def save(name, **arrs):
     meta = dict(torch=torch.__version__, numpy=np.__version__,
                 transformers=__import__("transformers").__version__,
                 triton=__import__("triton").__version__, triton_interpret=True,
-                reference=REF, shim="transformers 4-symbol shim (see import_reference)")
+                reference=REF_NAME, shim="transformers 4-symbol shim (see import_reference)")
     arrs = {k: (v.detach().cpu().numpy() if torch.is_tensor(v) else np.asarray(v))
             for k, v in arrs.items()}
     np.savez_compressed(os.path.join(OUT, name + ".npz"), meta=json.dumps(meta), **arrs)
@@ -561,25 +563,21 @@ def case_page_rope(m):
     save("page_rope", **outs)
 
 
+# cases run on the SGLang ops of the wheel; all others on the HF modules
+_SGL_CASES = {"paged"}
+_ORDER = ("route", "entmax", "decode_attend", "forward_dense", "gather_triton", "gather_e2e", "block_max",
+          "paged", "page_gate", "page_rope")
+
+
 def main():
-    only = sys.argv[1:]
+    if not REF or not os.path.isdir(REF):
+        sys.exit("set SRSWA_REFERENCE to a checkout of the reference (hf-model-code/ and wheel/ inside)")
+    names = sys.argv[1:] or list(_ORDER)   # e.g. `make_golden.py page_gate` regenerates one case
     m = import_reference()
-    if only:   # regenerate the named cases only, e.g. `make_golden.py page_gate`
-        for name in only:
-            globals()[f"case_{name}"](m)
-        return
-    sgl = import_sglang_ops()
+    sgl = import_sglang_ops() if any(n in _SGL_CASES for n in names) else None
     torch.manual_seed(0)
-    case_route(m)
-    case_entmax(m)
-    case_decode_attend(m)
-    case_forward_dense(m)
-    case_gather_triton(m)
-    case_gather_e2e(m)
-    case_block_max(m)
-    case_paged(sgl)
-    case_page_gate(m)
-    case_page_rope(m)
+    for name in names:
+        globals()[f"case_{name}"](sgl if name in _SGL_CASES else m)
 
 
 if __name__ == "__main__":

@@ -217,6 +217,24 @@ def test_window_must_stay_on_one_shard():
         dec.window_owner(20 * BS + 3, 20 * BS + 3)    # window starts in block 18 (rank 0), ends in 20 (rank 1)
 
 
+class _RecordingBackend:
+    """Fails the test if the step reaches any launch or collective."""
+
+    def __getattr__(self, name):
+        raise AssertionError(f"backend.{name} called before the plan was checked")
+
+
+def test_bad_plan_rejected_before_any_launch():
+    dec = SplitKVDecode(nblk_total=40, nblk_filled=40, block_size=BS, local_blocks=L, topk=K, topm=M,
+                        idx_scale=IDX_SCALE, floor=FLOOR, sigma=SIGMA, sm_scale=SCALE, rank=0, world=2,
+                        backend=_RecordingBackend())
+    p = 20 * BS + 3      # window straddles the two shards
+    with pytest.raises(ValueError, match="spans two shards"):
+        dec.step(None, None, None, {}, p_range=(p, p))
+    with pytest.raises(ValueError, match="p_range"):
+        dec.step(None, None, None, {}, p_range=None)   # positions must come from the host, not the device
+
+
 def test_shard_plan_covers_blocks_once():
     for total, filled, world in ((16388, 16384, 8), (41, 40, 2), (10, 3, 4)):
         cover = []

@@ -6,13 +6,15 @@ over only input and output buffers): its scratch is an array inside the
 library instead of a caller workspace.  This test calls it through the C ABI
 twice in a row and checks each result against the workspace entry point
 srswa_gather_bwd on the same inputs (the second call also checks that the
-shared scratch left by the first call does not leak into the result).  It runs
-last (file name) so a failure here cannot hide the other tests, and it passes
-both alone in a fresh process and after the rest of the suite."""
+shared scratch left by the first call does not leak into the result).  Both
+entry points run the same deterministic kernels, so the results must be equal
+bit for bit.  Before the compared calls, a backward of another shape fills
+the shared array with unrelated data.  It runs last (file name) so a failure
+here cannot hide the other tests, and it passes both alone in a fresh process
+and after the rest of the suite."""
 
 import ctypes as C
 
-import numpy as np
 import pytest
 import torch
 
@@ -20,8 +22,6 @@ pytestmark = pytest.mark.gpu
 
 from srswa import _lib as L  # noqa: E402
 from srswa import ops  # noqa: E402
-
-RTOL, ATOL = 1e-2, 2e-2  # bf16 gradient tolerance used by the gather tests
 
 
 def _case(dev, seed, T=900, B=2, H=4, Hkv=2, D=128, BS=64, LW=256, S=6):
@@ -53,19 +53,30 @@ def _call(lib, name, desc, q, k, v, o, lse, do, sel, bias, ws=None):
     return dq, dk, dv, db
 
 
+def _noalloc_status(lib):
+    v = C.c_int(-1)
+    assert lib.srswa_gather_bwd_noalloc_status(C.byref(v), torch.cuda.current_stream().cuda_stream) == 0
+    return v.value
+
+
 def test_noalloc_backward_matches_workspace_backward(cuda):
     lib = L.lib()
     assert lib.srswa_gather_bwd_noalloc_max_scratch() == 32 << 20
+    # a different shape first, so the shared array holds stale, unrelated data
+    junk = _case(cuda, 9, T=1300, B=1, H=2, Hkv=2, S=8)
+    _call(lib, "srswa_gather_bwd_noalloc", junk[-1], *junk[:-1])
     for seed in (1, 2):  # two calls in a row, different inputs
         q, k, v, o, lse, do, sel, bias, desc = _case(cuda, seed)
         ws_n = lib.srswa_gather_bwd_workspace_size(C.byref(desc))
         assert 0 < ws_n <= lib.srswa_gather_bwd_noalloc_max_scratch()
         ws = torch.empty(ws_n, dtype=torch.uint8, device=cuda)
         ref = _call(lib, "srswa_gather_bwd", desc, q, k, v, o, lse, do, sel, bias, ws)
+        assert ops.workspace_status(ws) == 0
         got = _call(lib, "srswa_gather_bwd_noalloc", desc, q, k, v, o, lse, do, sel, bias)
+        assert _noalloc_status(lib) == 0
         for a, b in zip(got, ref):
             assert torch.isfinite(a).all()
-            np.testing.assert_allclose(a.float().cpu().numpy(), b.float().cpu().numpy(), rtol=RTOL, atol=ATOL)
+            assert torch.equal(a, b)
 
 
 def test_noalloc_rejects_oversized_problem(cuda):

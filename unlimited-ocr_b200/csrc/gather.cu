@@ -380,12 +380,33 @@ TcLayout tc_layout(const srswa_gather_desc* g);
 bool tc_eligible(const srswa_gather_desc* g);
 int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const int32_t* sel,
                   const float* bias, const int32_t* seg, void* o, int64_t sob, int64_t sot, int64_t soh, float* lse,
-                  void* workspace, size_t workspace_bytes, cudaStream_t st);
+                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t st);
 size_t tc_bwd_workspace(const srswa_gather_desc* g, bool with_bias);
 int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const void* o,
                   int64_t sob, int64_t sot, int64_t soh, const void* dout, const float* lse, const int32_t* sel,
                   const float* bias, const int32_t* seg, void* dq, void* dk, void* dv, float* d_bias,
-                  void* workspace, size_t workspace_bytes, cudaStream_t st);
+                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t st);
+
+// The first kStatusBytes of every gather workspace hold the call's status
+// word (int32): cleared at the start of the call, set by a tensor-core kernel
+// whose bounded wait expired.  The rest of the workspace follows.
+constexpr size_t kStatusBytes = 256;
+
+// Clears the status word at the workspace head and returns it (null when the
+// caller gave no workspace); advances the workspace past it.
+static int take_status(void** workspace, size_t* bytes, int** status, cudaStream_t st) {
+  *status = nullptr;
+  if (*workspace == nullptr || *bytes < kStatusBytes) {
+    *workspace = nullptr;
+    *bytes = 0;
+    return 0;
+  }
+  *status = static_cast<int*>(*workspace);
+  SRSWA_CUDA_TRY(cudaMemsetAsync(*status, 0, sizeof(int), st));
+  *workspace = static_cast<char*>(*workspace) + kStatusBytes;
+  *bytes -= kStatusBytes;
+  return 0;
+}
 
 // The tensor-core backward takes bf16 / head dim 128 / 64-token blocks with
 // 8-element-aligned strides (o and do included); other shapes use the
@@ -404,8 +425,8 @@ static size_t bwd_need(const srswa_gather_desc* g, int64_t sob, int64_t sot, int
 }  // namespace srswa
 
 extern "C" size_t srswa_gather_fwd_workspace_size(const srswa_gather_desc* g) {
-  if (check_gather_desc(g) || !tc_eligible(g)) return 0;
-  return tc_layout(g).total;
+  if (check_gather_desc(g)) return 0;
+  return kStatusBytes + (tc_eligible(g) ? tc_layout(g).total : 0);
 }
 
 extern "C" int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v,
@@ -418,9 +439,12 @@ extern "C" int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const
   SRSWA_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                     reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15) == 0, SRSWA_EALIGN);
   if (g->B * g->T == 0) return 0;
+  int* status = nullptr;
+  rc = take_status(&workspace, &workspace_bytes, &status, reinterpret_cast<cudaStream_t>(stream));
+  if (rc) return rc;
   // tensor-core path (bf16, D = 128, 64-token blocks); CUDA-core rows otherwise
   if (tc_eligible(g) && o_dtype == SRSWA_BF16 && ((sob | sot | soh) & 7) == 0) {
-    rc = tc_gather_fwd(g, q, k, v, sel, bias, seg, o, sob, sot, soh, lse, workspace, workspace_bytes,
+    rc = tc_gather_fwd(g, q, k, v, sel, bias, seg, o, sob, sot, soh, lse, workspace, workspace_bytes, status,
                        reinterpret_cast<cudaStream_t>(stream));
     if (rc != kTcNoTensorMap) return rc;
   }
@@ -447,7 +471,7 @@ extern "C" int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const
 
 extern "C" size_t srswa_gather_bwd_workspace_size(const srswa_gather_desc* g) {
   if (check_gather_desc(g)) return 0;
-  return bwd_need(g, 8, 8, 8, true);
+  return kStatusBytes + bwd_need(g, 8, 8, 8, true);
 }
 
 extern "C" int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v,
@@ -464,17 +488,19 @@ extern "C" int srswa_gather_bwd(const srswa_gather_desc* g, const void* q, const
                     reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(dq) |
                     reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15) == 0,
                   SRSWA_EALIGN);
+  if (g->B * g->T == 0) return 0;
+  int* status = nullptr;
+  rc = take_status(&workspace, &workspace_bytes, &status, reinterpret_cast<cudaStream_t>(stream));
+  if (rc) return rc;
   if (tc_bwd_path(g, sob, sot, soh)) {
     SRSWA_CHECK_ARG(g->B * g->T < (1ll << 31) && g->HQ < 65536 && g->B * g->HI * g->T * g->S < (1ll << 31),
                     SRSWA_ETOOLARGE);
-    if (g->B * g->T == 0) return 0;
     rc = tc_gather_bwd(g, q, k, v, o, sob, sot, soh, dout, lse, sel, bias, seg, dq, dk, dv, d_bias, workspace,
-                       workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+                       workspace_bytes, status, reinterpret_cast<cudaStream_t>(stream));
     if (rc != kTcNoTensorMap) return rc;
   }
   const BwdLayout L = bwd_layout(g, bias != nullptr);
   SRSWA_CHECK_ARG(workspace && workspace_bytes >= L.total, SRSWA_EWORKSPACE);
-  if (g->B * g->T == 0) return 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   BwdArgs a = {};
   a.q = q; a.k = k; a.v = v; a.o = o; a.dout = dout; a.lse = lse; a.sel = sel; a.bias = bias;
@@ -573,11 +599,29 @@ extern "C" int srswa_gather_bwd_noalloc(const srswa_gather_desc* g, const void* 
                                         float* d_bias, srswa_stream_t stream) {
   int rc = check_gather_desc(g);
   if (rc) return rc;
-  const size_t need = srswa::bwd_need(g, sob, sot, soh, bias != nullptr);
+  const size_t need = srswa::kStatusBytes + srswa::bwd_need(g, sob, sot, soh, bias != nullptr);
   if (need > srswa::kNoAllocScratchBytes) return SRSWA_ETOOLARGE;
   void* scratch = nullptr;
   rc = srswa::bwd_scratch_address(&scratch);
   if (rc) return rc;
   return srswa_gather_bwd(g, q, k, v, o, sob, sot, soh, dout, lse, sel, bias, seg, dq, dk, dv, d_bias,
                           scratch, srswa::kNoAllocScratchBytes, stream);
+}
+
+extern "C" int srswa_gather_bwd_noalloc_status(int* out, srswa_stream_t stream) {
+  if (!out) return SRSWA_EINVAL;
+  void* scratch = nullptr;
+  const int rc = srswa::bwd_scratch_address(&scratch);
+  if (rc) return rc;
+  return srswa_workspace_status(scratch, out, stream);
+}
+
+extern "C" int srswa_workspace_status(const void* workspace, int* out, srswa_stream_t stream) {
+  if (!workspace || !out) return SRSWA_EINVAL;
+  int v = 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  SRSWA_CUDA_TRY(cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, st));
+  SRSWA_CUDA_TRY(cudaStreamSynchronize(st));
+  *out = v;
+  return 0;
 }

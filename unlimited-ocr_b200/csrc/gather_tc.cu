@@ -32,6 +32,8 @@
 // Shared-memory operand layout: see tc.cuh (128-byte swizzle, K-major Q/K/P,
 // MN-major V).
 
+#include <mutex>
+
 #include <cuda.h>  // CUtensorMap (the encoder is looked up at run time; libcuda is not linked)
 
 #include "attend.cuh"
@@ -73,6 +75,7 @@ struct TcArgs {
   float* pair_bias;           // per partial row: slot bias * log2 e (0 without bias)
   const int4* work;           // nonempty lists: (b*HI + hi) * nblk + block, first tile, pair count, 0
   const int32_t* totals;      // {tiles, nonempty lists}
+  int* status;                // the call's status word: 0, or the code of the first expired wait
   int64_t prow_cap;           // partial rows (each holds the HQ/HI heads of an index head)
   // backward lists
   const int32_t* pairs;       // packed t * S + s, grouped by (b, hi, block)
@@ -361,8 +364,7 @@ __device__ __noinline__ bool ws_wait_slow(uint32_t a, uint32_t parity, volatile 
     if (*abort_flag) return false;
     if (global_ns() - t0 > kWaitLimitNs) break;
   }
-  atomicExch(&g_tc_error, code);
-  *abort_flag = 1;
+  atomicCAS(const_cast<int*>(abort_flag), 0, code);
   return false;
 }
 __device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
@@ -819,11 +821,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   // ------------------------------------------------------------------- exit
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) report_status(a.status, abort_p);
   if (warp == kWsMma) {
     if (*abort_p) {  // MMAs may still be in flight: wait for all of them
       if (lane == 0) {
         mma_commit(&drain_bar);
-        mbar_wait(&drain_bar, 0, 408);
+        mbar_wait(&drain_bar, 0, 408, abort_p);
       }
       __syncwarp();
     }
@@ -1142,8 +1145,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
           if (idle_since == 0) {
             idle_since = now;
           } else if (now - idle_since > kWaitLimitNs) {
-            atomicExch(&g_tc_error, 424);
-            *abort_p = 1;
+            atomicCAS(const_cast<int*>(abort_p), 0, 424);
             ok = false;
           } else if (*abort_p) {
             ok = false;
@@ -1249,11 +1251,12 @@ __global__ void __launch_bounds__(kRwThreads, 1)
   // ------------------------------------------------------------------- exit
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) report_status(a.status, abort_p);
   if (warp == kRwMma) {
     if (*abort_p) {  // MMAs may still be in flight: wait for all of them
       if (lane == 0) {
         mma_commit(&drain_bar);
-        mbar_wait(&drain_bar, 0, 430);
+        mbar_wait(&drain_bar, 0, 430, abort_p);
       }
       __syncwarp();
     }
@@ -1774,11 +1777,12 @@ __global__ void __launch_bounds__(kRbThreads, 1)
   // ------------------------------------------------------------------- exit
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) report_status(a.f.status, abort_p);
   if (warp == kRbMma) {
     if (*abort_p) {
       if (lane == 0) {
         mma_commit(&drain_bar);
-        mbar_wait(&drain_bar, 0, 454);
+        mbar_wait(&drain_bar, 0, 454, abort_p);
       }
       __syncwarp();
     }
@@ -2017,11 +2021,12 @@ __global__ void __launch_bounds__(kBqThreads, 1)
   // ------------------------------------------------------------------- exit
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) report_status(a.f.status, abort_p);
   if (warp == 5) {
     if (*abort_p) {
       if (lane == 0) {
         mma_commit(&drain_bar);
-        mbar_wait(&drain_bar, 0, 469);
+        mbar_wait(&drain_bar, 0, 469, abort_p);
       }
       __syncwarp();
     }
@@ -2425,11 +2430,12 @@ __global__ void __launch_bounds__(kBkThreads, 1)
   // ------------------------------------------------------------------- exit
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) report_status(a.f.status, abort_p);
   if (warp == 5) {
     if (*abort_p) {
       if (lane == 0) {
         mma_commit(&drain_bar);
-        mbar_wait(&drain_bar, 0, 491);
+        mbar_wait(&drain_bar, 0, 491, abort_p);
       }
       __syncwarp();
     }
@@ -2582,9 +2588,51 @@ bool tc_eligible(const srswa_gather_desc* g) {
          ((g->sqb | g->sqt | g->sqh | g->skb | g->skt | g->skh | g->svb | g->svt | g->svh) & 7) == 0;
 }
 
+// Launch properties per device: the SM count, and whether the kernels'
+// shared-memory limits have been raised there (a per-context setting).  The
+// only process-wide state of the tensor-core path; filled under a mutex on
+// the first call made on each device.
+struct TcDeviceProps {
+  int num_sms = 0;
+  bool fwd_ready = false, bwd_ready = false;
+};
+constexpr int kTcMaxDevices = 64;
+static TcDeviceProps g_tc_props[kTcMaxDevices];
+static std::mutex g_tc_props_mu;
+
+static int tc_device_props(bool bwd, int* num_sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kTcMaxDevices) return SRSWA_EUNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_tc_props_mu);
+  TcDeviceProps& p = g_tc_props[dev];
+  if (p.num_sms == 0) {
+    e = cudaDeviceGetAttribute(&p.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  if (!bwd && !p.fwd_ready) {
+    e = cudaFuncSetAttribute(remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    p.fwd_ready = true;
+  }
+  if (bwd && !p.bwd_ready) {
+    e = cudaFuncSetAttribute(bwd_remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRbSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(bwd_band_dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBqSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(bwd_band_dkdv_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBkSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    p.bwd_ready = true;
+  }
+  *num_sms = p.num_sms;
+  return 0;
+}
+
 int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const int32_t* sel,
                   const float* bias, const int32_t* seg, void* o, int64_t sob, int64_t sot, int64_t soh, float* lse,
-                  void* workspace, size_t workspace_bytes, cudaStream_t st) {
+                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t st) {
   const TcLayout L = tc_layout(g);
   if (!workspace || workspace_bytes < L.total) return SRSWA_EWORKSPACE;
   char* ws = static_cast<char*>(workspace);
@@ -2606,6 +2654,7 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   a.pair_bias = reinterpret_cast<float*>(ws + L.pair_bias);
   a.work = reinterpret_cast<int4*>(ws + L.work);
   a.totals = reinterpret_cast<int32_t*>(ws + L.totals);
+  a.status = status;
   a.prow_cap = L.max_tiles * kTileM;
   a.B = g->B; a.T = g->T; a.HQ = g->HQ; a.Hkv = g->Hkv; a.HI = g->HI; a.S = g->S;
   a.LW = g->local_window > 0 ? g->local_window : kBlk;
@@ -2617,17 +2666,8 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   if (a.prow_cap >= (1ll << 31) || L.max_tiles * hpi >= (1ll << 31) || g->B * g->HI * g->T * g->S >= (1ll << 31))
     return SRSWA_ETOOLARGE;
 
-  static bool attr_done = false;
-  static int num_sms = 148;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-    attr_done = true;
-  }
+  int num_sms = 0;
+  if (const int prc = tc_device_props(false, &num_sms)) return prc;
   // the tensor maps of q, k, v and the partial rows; when the driver refuses
   // one, the caller runs the CUDA-core kernels instead (nothing launched yet)
   alignas(64) CUtensorMap tmq, tmk, tmv, tmp;
@@ -2711,7 +2751,7 @@ size_t tc_bwd_workspace(const srswa_gather_desc* g, bool with_bias) { return tc_
 int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const void* o,
                   int64_t sob, int64_t sot, int64_t soh, const void* dout, const float* lse, const int32_t* sel,
                   const float* bias, const int32_t* seg, void* dq, void* dk, void* dv, float* d_bias,
-                  void* workspace, size_t workspace_bytes, cudaStream_t st) {
+                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t st) {
   const TcBwdLayout L = tc_bwd_layout(g, bias != nullptr);
   if (!workspace || workspace_bytes < L.total) return SRSWA_EWORKSPACE;
   char* ws = static_cast<char*>(workspace);
@@ -2728,6 +2768,7 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   f.pairs = reinterpret_cast<int32_t*>(ws + L.pairs);
   f.tiles = reinterpret_cast<int4*>(ws + L.tiles);
   f.ntiles = reinterpret_cast<int32_t*>(ws + L.ntiles);
+  f.status = status;
   f.B = g->B; f.T = g->T; f.HQ = g->HQ; f.Hkv = g->Hkv; f.HI = g->HI; f.S = g->S;
   f.LW = g->local_window > 0 ? g->local_window : kBlk;
   f.nblk = (g->T + kBlk - 1) / kBlk;
@@ -2749,19 +2790,8 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   a.count = remote ? count : nullptr;
   a.offs = offs;
 
-  static int num_sms = 148;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(bwd_remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRbSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(bwd_band_dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBqSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaFuncSetAttribute(bwd_band_dkdv_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBkSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-    attr_done = true;
-  }
+  int num_sms = 0;
+  if (const int prc = tc_device_props(true, &num_sms)) return prc;
   // tensor maps of k, v, q and dO; when the driver refuses one, the caller
   // runs the CUDA-core kernels instead (nothing has been launched yet)
   alignas(64) CUtensorMap tmk, tmv, tmq, tmdo, tmq64, tmdo64;
@@ -2828,8 +2858,3 @@ int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   return srswa_last_launch_status();
 }
 }  // namespace srswa
-
-extern "C" int srswa_device_status(int* out) {
-  if (!out) return SRSWA_EINVAL;
-  return srswa::tc_read_clear_error(out);
-}

@@ -10,7 +10,10 @@
 //     with keys as rows; the two 64-feature halves are LBO bytes apart;
 //   * accumulators are fp32 in TMEM, row i of an M = 128 tile in lane i;
 //   * every wait on an mbarrier is bounded: on expiry the kernel records an
-//     error code in g_tc_error and takes its exit path instead of hanging.
+//     error code in its CTA's abort word (shared memory) and takes its exit
+//     path instead of hanging; at exit the CTA copies that code into the
+//     call's status word (the head of the caller's workspace), so errors stay
+//     with the call that raised them.
 #pragma once
 
 #include <stdint.h>
@@ -18,22 +21,6 @@
 #include "common.cuh"
 
 namespace srswa {
-
-// Set by a kernel of this translation unit whose bounded wait expired; each
-// unit including this header has its own copy and reports it through
-// tc_read_clear_error().
-static __device__ int g_tc_error = 0;
-
-static inline int tc_read_clear_error(int* out) {
-  int v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
-  if (e != cudaSuccess) return static_cast<int>(e);
-  const int zero = 0;
-  e = cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(int));
-  if (e != cudaSuccess) return static_cast<int>(e);
-  *out = v;
-  return 0;
-}
 
 // Bound of every wait on an mbarrier (wall clock, %globaltimer ns).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
@@ -71,8 +58,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return done != 0;
 }
 // Wait for the phase with parity `parity` to complete; false if the bounded
-// wait expired (error recorded).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+// wait expired (code recorded in the CTA's abort word unless one is there).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* abort_flag) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_ns();
@@ -80,8 +67,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
     if (mbar_try_wait(a, parity)) return true;
     if (global_ns() - t0 > kWaitLimitNs) break;
   }
-  atomicExch(&g_tc_error, code);
+  atomicCAS(const_cast<int*>(abort_flag), 0, code);
   return false;
+}
+// At kernel exit (after the final barrier): one thread hands the CTA's abort
+// code, if any, to the call's status word (first code wins).
+__device__ __forceinline__ void report_status(int* status, volatile int* abort_flag) {
+  const int code = *abort_flag;
+  if (code != 0 && status != nullptr) atomicCAS(status, 0, code);
 }
 
 // ------------------------------------------------------------------ fences --

@@ -75,7 +75,8 @@ _SIGS = {
                                            vp, vp, vp, vp, vp, vp, vp]),
     "srswa_decode_attend": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                       vp]),
-    "srswa_device_status": (C.c_int, [C.POINTER(C.c_int)]),
+    "srswa_workspace_status": (C.c_int, [vp, C.POINTER(C.c_int), vp]),
+    "srswa_gather_bwd_noalloc_status": (C.c_int, [C.POINTER(C.c_int), vp]),
     "srswa_lse_merge": (C.c_int, [vp, vp, i64, i64, i64, i64, i64, i64, vp, C.c_int, vp, vp]),
     "srswa_page_scan_workspace_size": (C.c_size_t, [i64, i64]),
     "srswa_page_ids": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, C.c_int, vp, vp, vp, vp, vp,

@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import os
 
 import torch
 
@@ -290,24 +291,56 @@ def _gather_desc(q, k, v, sel, block_size, scale, local_window):
                         v.stride(0), v.stride(1), v.stride(2))
 
 
-def gather_fwd(q, k, v, sel, bias, seg, block_size, scale, local_window):
+_CHECK_STATUS = os.environ.get("SRSWA_CHECK_STATUS", "0") not in ("", "0")
+
+
+def workspace_status(ws) -> int:
+    """Status word of the last gather call made with workspace ``ws`` (a
+    uint8 CUDA tensor): 0, or the code of a tensor-core kernel's bounded wait
+    that expired.  Waits for the current stream."""
+    v = C.c_int(0)
+    L.check(L.lib().srswa_workspace_status(ws.data_ptr(), C.byref(v), L.stream_of(ws)), "srswa_workspace_status")
+    return v.value
+
+
+def _workspace(n, dev, given):
+    if given is None:
+        return torch.empty(max(n, 1), device=dev, dtype=torch.uint8)
+    if given.dtype != torch.uint8 or given.numel() < n or not given.is_contiguous():
+        raise ValueError(f"workspace must be a contiguous uint8 tensor of at least {n} bytes")
+    return given
+
+
+def _after_gather(ws, what):
+    # opt-in (SRSWA_CHECK_STATUS=1): wait for the call and raise on an expired wait
+    if _CHECK_STATUS:
+        code = workspace_status(ws)
+        if code:
+            raise L.SrswaError(f"{what}: a bounded wait expired in a tensor-core kernel (code {code})")
+
+
+def gather_fwd(q, k, v, sel, bias, seg, block_size, scale, local_window, workspace=None):
     """q/k/v [B,T,H,D] (D contiguous), sel [B,HI,T,S] int32 packed, bias [B,T,S]
-    fp32 or None, seg [B,T] int32 or None -> (o [B,T,HQ,D] q.dtype, lse [B,T,HQ])."""
+    fp32 or None, seg [B,T] int32 or None -> (o [B,T,HQ,D] q.dtype, lse [B,T,HQ]).
+    workspace: optional caller uint8 tensor (srswa_gather_fwd_workspace_size
+    bytes); its first 4 bytes hold the call's status word afterwards."""
     B, T, HQ, D = q.shape
     o = torch.empty(B, T, HQ, D, device=q.device, dtype=q.dtype)
     lse = torch.empty(B, T, HQ, device=q.device, dtype=torch.float32)
     g = _gather_desc(q, k, v, sel, block_size, scale, local_window)
     lib = L.lib()
     ws_n = lib.srswa_gather_fwd_workspace_size(C.byref(g))
-    ws = torch.empty(max(ws_n, 1), device=q.device, dtype=torch.uint8)
+    ws = _workspace(ws_n, q.device, workspace)
     rc = lib.srswa_gather_fwd(C.byref(g), q.data_ptr(), k.data_ptr(), v.data_ptr(), sel.data_ptr(),
                               L.ptr(bias), L.ptr(seg), o.data_ptr(), L.dtype_code(o), o.stride(0),
                               o.stride(1), o.stride(2), lse.data_ptr(), ws.data_ptr(), ws_n, L.stream_of(q))
     L.check(rc, "srswa_gather_fwd")
+    _after_gather(ws, "srswa_gather_fwd")
     return o, lse
 
 
-def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_window):
+def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_window, workspace=None):
+    """Gradients (dq, dk, dv, d_bias or None) of gather_fwd; workspace as there."""
     g = _gather_desc(q, k, v, sel, block_size, scale, local_window)
     lib = L.lib()
     if do.stride() != o.stride():
@@ -322,12 +355,13 @@ def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_win
     if bias is not None:
         d_bias = torch.empty(bias.shape, device=q.device, dtype=torch.float32)
     ws_n = lib.srswa_gather_bwd_workspace_size(C.byref(g))
-    ws = torch.empty(max(ws_n, 1), device=q.device, dtype=torch.uint8)
+    ws = _workspace(ws_n, q.device, workspace)
     rc = lib.srswa_gather_bwd(C.byref(g), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                               o.stride(0), o.stride(1), o.stride(2), do.data_ptr(), lse.data_ptr(),
                               sel.data_ptr(), L.ptr(bias), L.ptr(seg), dq.data_ptr(), dk.data_ptr(),
                               dv.data_ptr(), L.ptr(d_bias), ws.data_ptr(), ws_n, L.stream_of(q))
     L.check(rc, "srswa_gather_bwd")
+    _after_gather(ws, "srswa_gather_bwd")
     return dq, dk, dv, d_bias
 
 

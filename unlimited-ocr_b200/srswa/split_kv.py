@@ -148,19 +148,20 @@ class SplitKVDecode:
                              "local_blocks + 1 blocks before the current one")
         return own
 
-    def step(self, q, idx_q, q_pos, layer, p_range=None, out_dtype=torch.bfloat16):
+    def step(self, q, idx_q, q_pos, layer, p_range, out_dtype=torch.bfloat16):
         """q [N,H,D], idx_q [N,d], q_pos [N] int64 (device), layer: this
         rank's {kbar, k_cache, v_cache, block_table (global block ids, [1, W]),
-        optional kbar_table}.  p_range = (min, max) of q_pos known on the host
-        (avoids a device read).  Returns o [N,H,D] (out_dtype)."""
+        optional kbar_table}.  p_range = (min, max) of q_pos, known on the
+        host (a decode loop knows its positions; reading them back from the
+        device would stall every layer).  Returns o [N,H,D] (out_dtype)."""
         be, plan, world = self.backend, self.plan, self.plan.world
         if p_range is None:
-            qp = q_pos.cpu()
-            p_range = (int(qp.min()), int(qp.max()))
+            raise ValueError("SplitKVDecode.step needs p_range = (min, max) of q_pos on the host")
+        # host-only check first: a bad plan fails before any launch or collective
+        owner = self.window_owner(int(p_range[1]), int(p_range[0]))
         keys = be.shard_keys(idx_q, layer, plan, q_pos, self.rp)            # [N, M]
         all_keys = be.all_gather(keys, world)                                # [world, N, M]
         sel = be.merge_keys(all_keys, plan, self.rp)
-        owner = self.window_owner(p_range[1], p_range[0])
         # one rank: its output is final, written in out_dtype; else fp32 partials
         o_part, lse_part = be.attend(q, layer, sel["topi32_own"], sel["bias"], q_pos,
                                      block_size=self.block_size, local_blocks=self.local_blocks,
