@@ -373,6 +373,142 @@ def gather_attention_bwd(q, k, v, do, sel, seg, block_size, scale, local_window,
     return dq, dk, dv, dbias
 
 
+# ---------------------------------------------------------------------------
+# a6/a7 at full size: the same math for a few sampled query rows or key blocks
+# of one (b, index head = 0), so that the oracle finishes in seconds where the
+# dense [T, Sk] masks above would not fit (T = 16k .. 32k).
+# ---------------------------------------------------------------------------
+def gather_row_keys(t, sel_row, seg_t, block_size, local_window, Sk):
+    """Keys attended by query t and the slot of each one's remote block (-1:
+    local key).  Row t of ``_key_masks``: remote keys are those of the
+    selected blocks in [seg_t, ls) with ls = max(t - LW + 1, seg_t), local keys
+    [ls, t]; a repeated block keeps its first slot
+    (sparse_gather_e2e_triton.py:82-98, dash_attention.py:1230-1260)."""
+    lw = block_size if local_window is None else max(1, int(local_window))
+    t, seg_t = int(t), int(seg_t)
+    ls = max(t - lw + 1, seg_t)
+    keys, slots, seen = [], [], set()
+    for s_, c in enumerate(np.asarray(sel_row).tolist()):
+        if c < 0 or c in seen:
+            continue
+        seen.add(c)
+        j = np.arange(c * block_size, min((c + 1) * block_size, Sk))
+        j = j[(j >= seg_t) & (j < ls) & (j <= t)]
+        keys.append(j)
+        slots.append(np.full(len(j), s_, np.int64))
+    loc = np.arange(ls, min(t + 1, Sk))
+    keys.append(loc)
+    slots.append(np.full(len(loc), -1, np.int64))
+    return np.concatenate(keys).astype(np.int64), np.concatenate(slots)
+
+
+def _row_probs(qr, kk, keys_slot, bias_row, scale, G):
+    """Softmax row of one query over its keys: qr [HQ,D], kk [n,Hkv,D] ->
+    (p [HQ,n], s [HQ,n], lse [HQ]) with the slot bias on remote keys."""
+    kq = np.repeat(kk, G, axis=1) if G > 1 else kk            # [n, HQ, D]
+    s = np.einsum("hd,nhd->hn", qr.astype(F32), kq.astype(F32)).astype(F32) * F32(scale)
+    if bias_row is not None:
+        add = np.where(keys_slot >= 0, np.asarray(bias_row, F32)[np.maximum(keys_slot, 0)], F32(0.0))
+        s = s + add[None, :]
+    if s.shape[1] == 0:
+        return s, s, np.full(qr.shape[0], -np.inf, F32)
+    m = s.max(-1, keepdims=True)
+    p = np.exp(s - m).astype(F32)
+    l = p.sum(-1, keepdims=True, dtype=F32)
+    return p / l, s, (m + np.log(l))[:, 0].astype(F32)
+
+
+def gather_rows_fwd(q_b, k_b, v_b, sel_b, seg_b, rows, block_size, scale, local_window, bias_b=None):
+    """Forward of ``gather_attention_fwd`` for the sampled query rows of one
+    batch element with one index head.  q_b [T,HQ,D], k_b/v_b [Sk,Hkv,D],
+    sel_b [T,S] (-1 pad), seg_b [T], bias_b [T,S] or None ->
+    (o [R,HQ,D], lse [R,HQ]) fp32."""
+    HQ, Hkv = q_b.shape[1], k_b.shape[1]
+    G = HQ // Hkv
+    o = np.zeros((len(rows), HQ, v_b.shape[-1]), F32)
+    lse = np.full((len(rows), HQ), -np.inf, F32)
+    for i, t in enumerate(rows):
+        keys, slot = gather_row_keys(t, sel_b[t], seg_b[t], block_size, local_window, k_b.shape[0])
+        if len(keys) == 0:
+            continue
+        p, _, lse[i] = _row_probs(q_b[t], k_b[keys], slot, None if bias_b is None else bias_b[t], scale, G)
+        vq = np.repeat(v_b[keys], G, axis=1) if G > 1 else v_b[keys]
+        o[i] = np.einsum("hn,nhd->hd", p, vq.astype(F32))
+    return o, lse
+
+
+def gather_rows_bwd(q_b, k_b, v_b, do_b, sel_b, seg_b, rows, block_size, scale, local_window, bias_b=None):
+    """dQ and d_bias of ``gather_attention_bwd`` for sampled query rows (one
+    batch element, one index head): -> (dq [R,HQ,D], d_bias [R,S] or None)."""
+    HQ, Hkv = q_b.shape[1], k_b.shape[1]
+    G = HQ // Hkv
+    S = sel_b.shape[-1]
+    dq = np.zeros((len(rows), HQ, q_b.shape[-1]), F32)
+    db = np.zeros((len(rows), S), F32) if bias_b is not None else None
+    for i, t in enumerate(rows):
+        keys, slot = gather_row_keys(t, sel_b[t], seg_b[t], block_size, local_window, k_b.shape[0])
+        if len(keys) == 0:
+            continue
+        p, _, _ = _row_probs(q_b[t], k_b[keys], slot, None if bias_b is None else bias_b[t], scale, G)
+        kq = (np.repeat(k_b[keys], G, axis=1) if G > 1 else k_b[keys]).astype(F32)
+        vq = (np.repeat(v_b[keys], G, axis=1) if G > 1 else v_b[keys]).astype(F32)
+        o = np.einsum("hn,nhd->hd", p, vq)
+        dor = do_b[t].astype(F32)
+        dp = np.einsum("hd,nhd->hn", dor, vq)
+        delta = (o * dor).sum(-1, keepdims=True, dtype=F32)
+        ds = p * (dp - delta)
+        dq[i] = F32(scale) * np.einsum("hn,nhd->hd", ds, kq)
+        if db is not None:
+            dsum = ds.sum(0, dtype=F32)
+            for s_ in range(S):
+                db[i, s_] = dsum[slot == s_].sum(dtype=F32)
+    return dq, db
+
+
+def gather_block_bwd(q_b, k_b, v_b, do_b, o_b, lse_b, sel_b, seg_b, c, block_size, scale, local_window,
+                     bias_b=None):
+    """dK and dV of ``gather_attention_bwd`` for the keys of key block c (one
+    batch element, one index head), given the forward's o [T,HQ,D] and lse
+    [T,HQ] (natural log) -- the tensors the reference's autograd saves and
+    hands its dK/dV kernels (K3 / K7, sparse_gather_e2e_triton.py:209-275).
+    Every query whose key set holds a key of block c contributes:
+    dV_j = sum_t P_tj dO_t, dK_j = scale sum_t dS_tj q_t, with P from lse and
+    dS = P (dP - Delta), Delta = rowsum(o * dO).  -> (dk, dv) [n, Hkv, D]."""
+    T, HQ = q_b.shape[0], q_b.shape[1]
+    Hkv = k_b.shape[1]
+    G = HQ // Hkv
+    Sk = k_b.shape[0]
+    lw = block_size if local_window is None else max(1, int(local_window))
+    j0, j1 = c * block_size, min((c + 1) * block_size, Sk)
+    kj = k_b[j0:j1].astype(F32)
+    vj = v_b[j0:j1].astype(F32)
+    dk = np.zeros_like(kj)
+    dv = np.zeros_like(vj)
+    cand = set(range(j0, min(T, j1 + lw)))
+    cand.update(np.nonzero((sel_b == c).any(-1))[0].tolist())
+    for t in sorted(cand):
+        if t < j0:
+            continue
+        keys, slot = gather_row_keys(t, sel_b[t], seg_b[t], block_size, lw, Sk)
+        inb = (keys >= j0) & (keys < j1)
+        if not inb.any():
+            continue
+        kk, ks = keys[inb] - j0, slot[inb]
+        s = np.einsum("hd,nhd->hn", q_b[t].astype(F32), np.repeat(kj[kk], G, axis=1)).astype(F32) * F32(scale)
+        if bias_b is not None:
+            s = s + np.where(ks >= 0, np.asarray(bias_b[t], F32)[np.maximum(ks, 0)], F32(0.0))[None, :]
+        p = np.exp(s - lse_b[t][:, None]).astype(F32)                     # [HQ, n]
+        dor = do_b[t].astype(F32)
+        dp = np.einsum("hd,nhd->hn", dor, np.repeat(vj[kk], G, axis=1))
+        delta = (o_b[t].astype(F32) * dor).sum(-1, keepdims=True, dtype=F32)
+        ds = p * (dp - delta)
+        for hq in range(HQ):
+            hk = hq // G
+            dv[kk, hk] += p[hq][:, None] * dor[hq][None, :]
+            dk[kk, hk] += F32(scale) * ds[hq][:, None] * q_b[t, hq].astype(F32)[None, :]
+    return dk, dv
+
+
 def decode_attend(q, k_all, v_all, topi, bias, valid, q_pos, block_size, local_window, scale):
     """``_decode_attend`` (hf-model-code/modeling_deepseekv2.py:455-481), fp32.
 

@@ -93,6 +93,7 @@ def test_forward_dense_golden(cuda):
 
 
 @pytest.mark.parametrize("B,T_,H,Hkv,D,BS,LW,K,packed", [(2, 1536, 4, 4, 128, 64, 512, 8, False),
+                                                          (1, 2560, 10, 10, 128, 64, 1024, 16, False),  # cfg4
                                                           (1, 1000, 4, 2, 128, 64, 200, 6, True),
                                                           (2, 700, 2, 2, 64, 32, 96, 4, False)])
 def test_gather_vs_oracle_router_selection(cuda, B, T_, H, Hkv, D, BS, LW, K, packed):

@@ -58,6 +58,8 @@ def _inputs(rng, B, T_, H, Hkv, K, scale=0.5):
     (2, 700, 4, 4, 6, 256, False, True),       # T not a multiple of 128, bias
     (1, 1000, 4, 2, 8, 512, True, False),      # GQA + packed segments
     (1, 1536, 10, 10, 8, 512, False, True),    # BASELINE head layout
+    (1, 2560, 10, 10, 16, 1024, False, True),  # cfg4 selection geometry: K = 16, LW = 1024
+    (2, 1100, 4, 4, 16, 1024, True, True),     # K = 16, LW = 1024 with packing and T % 128 != 0
 ])
 def test_tc_forward_vs_oracle(cuda, B, T_, H, Hkv, K, LW, packed, use_bias):
     rng = np.random.default_rng(T_ + K)
@@ -167,6 +169,8 @@ def _route_case(cuda, seed, B, T_, H, Hkv, K, LW, dtype=torch.bfloat16):
     (2, 700, 4, 4, 6, 256, False, True),       # T not a multiple of 128, bias
     (1, 1000, 4, 2, 8, 512, True, False),      # GQA + packed segments
     (1, 1536, 10, 10, 8, 512, False, True),    # BASELINE head layout
+    (1, 2560, 10, 10, 16, 1024, False, True),  # cfg4 selection geometry: K = 16, LW = 1024
+    (2, 1100, 4, 4, 16, 1024, True, True),     # K = 16, LW = 1024 with packing and T % 128 != 0
 ])
 def test_tc_backward_vs_oracle(cuda, B, T_, H, Hkv, K, LW, packed, use_bias):
     rng = np.random.default_rng(100 + T_ + K)
