@@ -81,6 +81,15 @@ SRSWA_API int srswa_kbar_paged(const void* idx_cache, int dtype, int64_t s_page,
                      const float* head_cls, float* kbar_cache, int64_t s_kbar,
                      srswa_stream_t stream);
 
+/* k_bar of an explicit page plan: page pages[i] (int64) from its first tok[i]
+ * tokens (int32); entries with tok[i] <= 0 store nothing (plan padding, other
+ * requests' pages).  The plans are the reference's kbar_tail_plan /
+ * kbar_all_plan outputs.  Replaces _kbar_page_kernel driven by a plan
+ * (whl:.../unlimited_dash_ops/route_triton.py:36-72, 706-726). */
+SRSWA_API int srswa_kbar_pages(const void* idx_cache, int dtype, int64_t s_page, int64_t s_tok, int64_t d,
+                     int64_t block_size, const int64_t* pages, const int32_t* tok, int64_t n,
+                     const float* head_cls, float* kbar_cache, int64_t s_kbar, srswa_stream_t stream);
+
 /* --------------------------------------------------------------- a2+a4 --
  * Router parameters (the per-layer _infer_params dict of
  * configure_dash_inference, hf-model-code/modeling_deepseekv2.py:296-335). */
@@ -99,7 +108,9 @@ typedef struct {
  * c <= q_pos[n]/BS - L that hold a token, SCORE_NEG (-1e9) elsewhere.  kbar_c
  * comes either from a contiguous kbar [B, nblk, d] (block_table == NULL; row n
  * belongs to batch n / rows_per_seq) or from a paged kbar cache [P, d] through
- * block_table [R, W] (row n belongs to request n / rows_per_seq).
+ * block_table [R, W] (row n belongs to request n / rows_per_seq, or to
+ * row_seq[n] when row_seq [N] int32 is given: varlen prefill rows, which then
+ * need q_pos).
  * q_pos [N] int64, or NULL to use seq_lens[r] - rows_per_seq + n % rows_per_seq.
  * seq_lens (NULL allowed when q_pos is given and blocks are contiguous) bounds
  * blocks holding tokens.  cand [N, nblk] uint8 (row stride s_cand, 0 = shared
@@ -120,8 +131,8 @@ SRSWA_API size_t srswa_route_workspace_size(int64_t N, int64_t nblk, int64_t d, 
 SRSWA_API int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
                 const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk,
                 const int32_t* block_table, int64_t s_bt, const int32_t* seq_lens,
-                int64_t rows_per_seq, const int64_t* q_pos, const uint8_t* cand,
-                int64_t s_cand, srswa_route_params params, int64_t* topi64, int32_t* topi32,
+                int64_t rows_per_seq, const int32_t* row_seq, const int64_t* q_pos,
+                const uint8_t* cand, int64_t s_cand, srswa_route_params params, int64_t* topi64, int32_t* topi32,
                 float* bias, uint8_t* valid, float* scores, void* workspace,
                 size_t workspace_bytes, srswa_stream_t stream);
 
@@ -305,6 +316,20 @@ SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, co
                         const float* bias, const uint8_t* valid, void* out, float* lse_out,
                         srswa_stream_t stream);
 
+/* Paged varlen prefill attend (the SGLang prefill op): rows n of request r
+ * are cu_seqlens_q[r] <= n < cu_seqlens_q[r + 1] (int32 [R + 1], device), row
+ * n sits at position prefix_lens[r] + n - cu_seqlens_q[r] (prefix_lens int32
+ * [R], device) and reads block table row r.  Per row, remote keys are the
+ * selected blocks' keys below the window start, local keys the window
+ * [p - LW + 1, p]; bias on remote keys only.  The descriptor is the decode
+ * one with N = total rows and R = requests (rows_per_req, s_req ignored).
+ * Replaces _dash_sparse_fwd_kernel / dash_sparse_attn
+ * (whl:.../unlimited_dash_ops/attend_triton.py:88-292, 523-597). */
+SRSWA_API int srswa_prefill_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache,
+                         const void* v_cache, const int32_t* block_table, const int32_t* cu_seqlens_q,
+                         const int32_t* prefix_lens, const void* topk_idx, const float* bias, void* out,
+                         float* lse_out, srswa_stream_t stream);
+
 /* Status of the last gather call that used `workspace`: the first 4 bytes of
  * every gather workspace (srswa_gather_fwd / srswa_gather_bwd; the workspace
  * sizes include them) are that call's status word, cleared when the call is
@@ -400,6 +425,19 @@ SRSWA_API int srswa_decode_allow(const int64_t* last_ids, int64_t s_ids, int64_t
                                  const int64_t* bmin, const int64_t* bmax, int64_t s_state,
                                  int64_t nblk_state, const int64_t* pp, int64_t* mcum, int64_t nblk,
                                  uint8_t* allow, srswa_stream_t stream);
+
+/* Decode scan window: for each decode row (row of request row / dql at
+ * position seq_lens[r] - dql + row % dql), the span [lo, hi) of blocks
+ * allowed by allow [nd, WQ] uint8 (row stride s_allow) among the live remote
+ * blocks (c <= q_blk - L, c * bs < seq_len, c < min(W, WQ)); with none,
+ * lo = 0 and hi = 0 (no remote block) or the live width min(W, max(nblk, 1));
+ * fit = (hi - lo) <= tile.  lo / hi int32 [nd], fit int8 [nd].  Replaces
+ * _win_bounds_kernel / win_bounds_decode
+ * (whl:.../unlimited_dash_ops/route_triton.py:466-526). */
+SRSWA_API int srswa_win_bounds_decode(const uint8_t* allow, int64_t s_allow, int64_t WQ, const int32_t* seq_lens,
+                            int64_t nd, int64_t W, int64_t block_size, int64_t local_blocks,
+                            int64_t decode_query_len, int64_t tile, int32_t* lo, int32_t* hi, int8_t* fit,
+                            srswa_stream_t stream);
 
 /* ---------------------------------------------------- page2d RoPE -------
  * Two-axis rotary coordinates (token-in-page, page) of the indexer and the

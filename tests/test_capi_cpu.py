@@ -55,7 +55,7 @@ def test_invalid_arguments_rejected_without_launch():
     # NULL pointers -> EINVAL before any CUDA call
     assert lib.srswa_kbar_contig(None, 1, 0, 0, 1, 1, 128, 64, None, None, None, None) == L.EINVAL
     p = L.RouteParams(64, 8, 8, 16, 11.3, 1e-4, 1.0)
-    assert lib.srswa_route(None, 0, 128, 1, 128, None, 0, 0, 1, None, 0, None, 1, None, None, 0, p,
+    assert lib.srswa_route(None, 0, 128, 1, 128, None, 0, 0, 1, None, 0, None, 1, None, None, None, 0, p,
                            None, None, None, None, None, None, 0, None) == L.EINVAL
     assert lib.srswa_route_workspace_size(256, 2048, 128, p, 0) > 0      # decode rows: chunked router
     assert lib.srswa_route_workspace_size(65536, 256, 128, p, 0) == 0    # prefill rows: no scratch

@@ -82,3 +82,36 @@ def test_arange_check_follows_tensor_and_version():
     assert _positions_are_arange(p, 10)
     q = torch.arange(10)[None].repeat(2, 1) * 2  # another tensor
     assert not _positions_are_arange(q, 10)
+
+
+def test_install_sglang_reaches_the_backend(monkeypatch):
+    """The SGLang backend imports the ops by `from ... import` at its own
+    import (whl:.../unlimited_ocr_v2_backend.py:18-52); after install_sglang
+    both the ops modules and the backend's copies are srswa.paged's."""
+    import sys
+    import types
+
+    from srswa import dropin, paged
+    pre = "sglang.srt.layers.attention.unlimited_dash_ops"
+    ref = lambda *a, **k: "reference"  # noqa: E731
+    at = types.ModuleType(pre + ".attend_triton")
+    rt = types.ModuleType(pre + ".route_triton")
+    for m, names in ((at, ("dash_sparse_attn", "dash_sparse_attn_decode")),
+                     (rt, ("route_decode_triton", "route_prefill_triton", "kbar_refresh_tail_triton",
+                           "win_bounds_decode", "kbar_tail_plan"))):
+        for n in names:
+            setattr(m, n, ref)
+    be = types.ModuleType("sglang.srt.layers.attention.unlimited_ocr_v2_backend")
+    for n in ("dash_sparse_attn", "dash_sparse_attn_decode", "route_decode_triton", "route_prefill_triton",
+              "kbar_refresh_tail_triton", "win_bounds_decode", "kbar_tail_plan"):
+        setattr(be, n, ref)        # the backend's own `from ... import` copies
+    for m in (at, rt, be):
+        monkeypatch.setitem(sys.modules, m.__name__, m)
+    done = dropin.install_sglang()
+    for n in ("dash_sparse_attn", "dash_sparse_attn_decode", "route_decode_triton", "route_prefill_triton",
+              "kbar_refresh_tail_triton", "win_bounds_decode"):
+        assert getattr(be, n) is getattr(paged, n), n
+        mod = at if hasattr(at, n) else rt
+        assert getattr(mod, n) is getattr(paged, n), n
+    assert be.kbar_tail_plan is ref          # torch-only planning helpers stay the reference's
+    assert len(done) == 12

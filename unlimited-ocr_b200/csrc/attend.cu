@@ -48,6 +48,19 @@ struct SlotInfo {
 
 __device__ __forceinline__ void attend_row_position(const AttendArgs& a, int64_t row, int64_t& seq,
                                                     int64_t& t, int64_t& p, int64_t& sg) {
+  if (a.pos_mode == 3) {  // varlen rows: the request holding this row (binary search)
+    int64_t lo = 0, hi = a.nreq;
+    while (hi - lo > 1) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (a.cu_rows[mid] <= row) lo = mid;
+      else hi = mid;
+    }
+    seq = lo;
+    t = row;
+    p = static_cast<int64_t>(a.prefix_lens[lo]) + row - a.cu_rows[lo];
+    sg = 0;
+    return;
+  }
   seq = row / a.rps;
   t = row % a.rps;
   if (a.pos_mode == 0) p = a.q_pos[row];
@@ -493,6 +506,39 @@ extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, c
   a.s_q_seq = d.rows_per_req * d.s_qn; a.s_q_t = d.s_qn; a.s_qh = d.s_qh;
   a.out = out; a.s_o_seq = d.rows_per_req * d.s_on; a.s_o_t = d.s_on; a.s_oh = d.s_oh;
   a.lse_out = lse_out; a.s_l_seq = d.rows_per_req * d.H; a.s_l_t = d.H;
+  a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0;
+  return attend_rows_launch(a, d.D, d.kv_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int srswa_prefill_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache,
+                                    const void* v_cache, const int32_t* block_table, const int32_t* cu_seqlens_q,
+                                    const int32_t* prefix_lens, const void* topk_idx, const float* bias,
+                                    void* out, float* lse_out, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(dd && q && k_cache && v_cache && out && block_table && cu_seqlens_q && prefix_lens,
+                  SRSWA_EINVAL);
+  const srswa_decode_desc& d = *dd;
+  SRSWA_CHECK_ARG(d.N >= 0 && d.H > 0 && d.Hkv > 0 && d.H % d.Hkv == 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(d.K >= 0 && (d.K == 0 || topk_idx), SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(d.R > 0 && d.block_size > 0 && d.local_blocks >= 0 && d.W > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(aligned16(q) && aligned16(k_cache) && aligned16(v_cache), SRSWA_EALIGN);
+  SRSWA_CHECK_ARG(((d.s_page | d.s_pos | d.s_head) & 7) == 0, SRSWA_EALIGN);
+  SRSWA_CHECK_ARG(((d.s_qn | d.s_qh) & (d.q_dtype == SRSWA_F32 ? 3 : 7)) == 0, SRSWA_EALIGN);
+  AttendArgs a = {};
+  a.q = q; a.k = k_cache; a.v = v_cache; a.q_dtype = d.q_dtype; a.out_dtype = d.out_dtype;
+  a.N = d.N; a.rps = 1; a.H = d.H; a.Hkv = d.Hkv;
+  a.seq_lens = nullptr; a.q_pos = nullptr; a.seg = nullptr;
+  a.pos_mode = 3; a.cu_rows = cu_seqlens_q; a.prefix_lens = prefix_lens; a.nreq = d.R;
+  a.block_table = block_table; a.s_bt = d.W; a.W = d.W;
+  a.s_page = d.s_page; a.s_seq = 0; a.s_blk = d.s_page;
+  a.s_pos = d.s_pos; a.s_head = d.s_head;
+  a.sel = topk_idx; a.idx_is64 = d.idx_is64; a.K = d.K; a.valid = nullptr;
+  a.s_sel_seq = 0; a.s_sel_t = d.s_ti_n; a.s_sel_h = d.s_ti_h; a.HI = d.Hkv;
+  a.bias = bias; a.s_b_seq = 0; a.s_b_t = d.s_b_n; a.s_b_h = d.s_b_h;
+  a.BS = d.block_size; a.LW = d.local_blocks * d.block_size;
+  a.q_scale_log2 = d.sm_scale * kLog2e;
+  a.s_q_seq = 0; a.s_q_t = d.s_qn; a.s_qh = d.s_qh;
+  a.out = out; a.s_o_seq = 0; a.s_o_t = d.s_on; a.s_oh = d.s_oh;
+  a.lse_out = lse_out; a.s_l_seq = 0; a.s_l_t = d.H;
   a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0;
   return attend_rows_launch(a, d.D, d.kv_dtype, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -11,6 +11,9 @@ constexpr int kAttendMaxSlots = 64;  // remote slots + window blocks per row
 
 // Row n is (seq = n / rps, t = n % rps).  Its query position p is q_pos[n]
 // (pos_mode 0), seq_lens[seq] - rps + t (pos_mode 1) or t (pos_mode 2).
+// pos_mode 3 (varlen prefill): seq is the request r with cu_rows[r] <= n <
+// cu_rows[r + 1], t = n (per-row strides, request strides 0) and
+// p = prefix_lens[r] + n - cu_rows[r].
 // A key block blk of sequence seq starts at element
 //   block_table[seq * s_bt + blk] * s_page      (paged), or
 //   seq * s_seq + blk * s_blk                   (contiguous),
@@ -37,6 +40,9 @@ struct AttendArgs {
   const int64_t* q_pos;
   const int32_t* seg;  // per row segment start (NULL = 0)
   int pos_mode;
+  const int32_t* cu_rows;      // pos_mode 3: [nreq + 1] first row of each request
+  const int32_t* prefix_lens;  // pos_mode 3: [nreq] cached tokens before the request's first row
+  int64_t nreq;
   const int32_t* block_table;
   int64_t s_bt, W;
   int64_t s_page, s_seq, s_blk, s_pos, s_head;

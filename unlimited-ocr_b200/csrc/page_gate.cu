@@ -598,6 +598,90 @@ extern "C" int srswa_decode_allow(const int64_t* last_ids, int64_t s_ids, int64_
 
 namespace srswa {
 
+// ------------------------------------------------------------ scan window --
+// Remote page span of each decode row (K14): one warp per row scans the
+// row's allow mask with 16-byte loads and reduces the first / last allowed
+// live remote block.  Mask columns at or past min(W, WQ) are never read.
+__global__ void __launch_bounds__(256) win_bounds_kernel(const uint8_t* __restrict__ allow, int64_t s_allow,
+                                                         int64_t WQ, const int32_t* __restrict__ seq_lens,
+                                                         int64_t nd, int64_t W, int64_t bs, int64_t L, int64_t dql,
+                                                         int64_t tile, int32_t* lo_out, int32_t* hi_out,
+                                                         int8_t* fit_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= nd) return;
+  const int64_t seq = seq_lens[row / dql];
+  const int64_t q_pos = seq - dql + row % dql;
+  const int64_t q_blk = q_pos / bs;  // truncating, as the reference's integer division
+  // allowed live remote blocks: off <= q_blk - L and off * bs < seq
+  int64_t lim = q_blk - L + 1;
+  const int64_t live = (seq + bs - 1) / bs;
+  if (lim > live) lim = live;
+  const int64_t width = W < WQ ? W : WQ;
+  if (lim > width) lim = width;
+  int64_t lo = W, hi = -1;
+  const uint8_t* a = allow + row * s_allow;
+  if (lim > 0) {
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(a) | static_cast<uintptr_t>(s_allow)) & 15) == 0;
+    const int64_t nvec = vec_ok ? lim / 16 : 0;
+    for (int64_t v = lane; v < nvec; v += 32) {
+      const uint4 u = *reinterpret_cast<const uint4*>(a + v * 16);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        if ((w[e >> 2] >> ((e & 3) * 8)) & 0xffu) {
+          const int64_t off = v * 16 + e;
+          lo = off < lo ? off : lo;
+          hi = off > hi ? off : hi;
+        }
+      }
+    }
+    for (int64_t off = nvec * 16 + lane; off < lim; off += 32) {
+      if (a[off]) {
+        lo = off < lo ? off : lo;
+        hi = off > hi ? off : hi;
+      }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const int64_t l2 = __shfl_xor_sync(0xffffffffu, lo, o);
+    const int64_t h2 = __shfl_xor_sync(0xffffffffu, hi, o);
+    lo = l2 < lo ? l2 : lo;
+    hi = h2 > hi ? h2 : hi;
+  }
+  if (lane == 0) {
+    const bool any_r = hi >= 0;
+    const int64_t nb = (seq + bs - 1) / bs;
+    const int64_t nb1 = nb > 1 ? nb : 1;
+    const int64_t w_seq = W < nb1 ? W : nb1;
+    const bool no_remote = seq <= 0 || (q_blk - L) < 0;
+    const int64_t lo_v = any_r ? lo : 0;
+    const int64_t hi_v = any_r ? hi + 1 : (no_remote ? 0 : w_seq);
+    lo_out[row] = static_cast<int32_t>(lo_v);
+    hi_out[row] = static_cast<int32_t>(hi_v);
+    fit_out[row] = (hi_v - lo_v) <= tile ? 1 : 0;
+  }
+}
+
+}  // namespace srswa
+
+extern "C" int srswa_win_bounds_decode(const uint8_t* allow, int64_t s_allow, int64_t WQ, const int32_t* seq_lens,
+                                       int64_t nd, int64_t W, int64_t block_size, int64_t local_blocks,
+                                       int64_t decode_query_len, int64_t tile, int32_t* lo, int32_t* hi,
+                                       int8_t* fit, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(nd >= 0 && W > 0 && WQ >= 0 && block_size > 0 && local_blocks >= 0 && decode_query_len > 0,
+                  SRSWA_EINVAL);
+  if (nd == 0) return 0;
+  SRSWA_CHECK_ARG(allow && seq_lens && lo && hi && fit, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG((nd + 7) / 8 < (1ll << 31), SRSWA_ETOOLARGE);
+  srswa::win_bounds_kernel<<<static_cast<unsigned>((nd + 7) / 8), 256, 0,
+                             reinterpret_cast<cudaStream_t>(stream)>>>(
+      allow, s_allow, WQ, seq_lens, nd, W, block_size, local_blocks, decode_query_len, tile, lo, hi, fit);
+  return srswa_last_launch_status();
+}
+
+namespace srswa {
+
 // ---------------------------------------------------------------------------
 // page2d RoPE: the two-axis rotary of the indexer and main branch
 // (hf-model-code/_sparse_base_impl.py:1984-2058).  Pair i < n_tok turns by

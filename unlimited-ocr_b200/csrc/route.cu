@@ -31,7 +31,12 @@ struct KbarArgs {
   const int32_t* block_table;
   const int32_t* seq_lens;
   int64_t s_page, s_bt, W, R, tail, s_kbar;
-  int paged;
+  int paged;  // 0 contiguous, 1 block table (all / tail pages), 2 explicit page plan
+  // page plan (paged == 2): item i summarizes page plan_pages[i] from its
+  // first plan_tok[i] tokens; items with no token store nothing
+  const int64_t* plan_pages;
+  const int32_t* plan_tok;
+  int64_t plan_n;
 };
 
 __device__ __forceinline__ void load4(const void* p, int64_t i, int dtype, float* o) {
@@ -65,6 +70,14 @@ __device__ __forceinline__ void kbar_item(const KbarArgs& a, int64_t item, int64
     base = b * a.sb + c * a.bs * a.st;
     ntok = min(a.bs, a.S - c * a.bs);
     out_row = item * a.d;
+  } else if (a.paged == 2) {
+    if (item >= a.plan_n) return;
+    const int64_t nt = min(a.bs, static_cast<int64_t>(a.plan_tok[item]));
+    if (nt <= 0) return;  // not a page slot of the plan (padding): store nothing
+    const int64_t page = a.plan_pages[item];
+    base = page * a.s_page;
+    out_row = page * a.s_kbar;
+    ntok = nt;
   } else {
     const int64_t per = a.tail > 0 ? a.tail : a.W;
     if (item >= a.R * per) return;
@@ -185,6 +198,7 @@ struct RouteArgs {
   int64_t s_bt;
   const int32_t* seq_lens;
   int64_t rows_per_seq;
+  const int32_t* row_seq;  // sequence of each row (varlen prefill rows); NULL = n / rows_per_seq
   const int64_t* q_pos;
   const float* scores_in;
   int64_t s_sc;
@@ -200,6 +214,10 @@ struct RouteArgs {
   float* scores_out;
   int rows_per_cta;
 };
+
+__device__ __forceinline__ int64_t route_row_seq(const RouteArgs& a, int64_t n) {
+  return a.row_seq ? static_cast<int64_t>(a.row_seq[n]) : n / a.rows_per_seq;
+}
 
 struct Best {
   float v;
@@ -338,7 +356,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
 
   int64_t seq = 0, p = 0, c_hi = 0;
   if (row_ok) {
-    seq = n / a.rows_per_seq;
+    seq = route_row_seq(a, n);
     if (!a.from_scores) {
       p = a.q_pos ? a.q_pos[n] : static_cast<int64_t>(a.seq_lens[seq]) - a.rows_per_seq + n % a.rows_per_seq;
       // remote blocks: c <= p/BS - L, holding a token (c*BS < seq_len)
@@ -497,7 +515,7 @@ __global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const Rou
   const int64_t n = blockIdx.y;
   const int64_t lo = static_cast<int64_t>(blockIdx.x) * kSpan;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t seq = n / a.rows_per_seq;
+  const int64_t seq = route_row_seq(a, n);
   const int64_t p = a.q_pos ? a.q_pos[n]
                             : static_cast<int64_t>(a.seq_lens[seq]) - a.rows_per_seq + n % a.rows_per_seq;
   int64_t c_hi = p >= 0 ? p / a.BS - a.L + 1 : 0;
@@ -820,7 +838,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
   const int64_t n = blockIdx.y;
   const int64_t lo = static_cast<int64_t>(blockIdx.x) * kChunkBlocks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t seq = n / a.rows_per_seq;
+  const int64_t seq = route_row_seq(a, n);
   const int64_t p = a.q_pos ? a.q_pos[n]
                             : static_cast<int64_t>(a.seq_lens[seq]) - a.rows_per_seq + n % a.rows_per_seq;
   int64_t c_hi = p >= 0 ? p / a.BS - a.L + 1 : 0;  // global: remote blocks are [0, c_hi)
@@ -1252,8 +1270,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
 }
 
 static bool use_tile(const RouteArgs& a) {
-  return !a.from_scores && a.block_table == nullptr && a.d == 128 && a.nblk <= kRtMaxBlocks &&
-         a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0;
+  return !a.from_scores && a.block_table == nullptr && a.row_seq == nullptr && a.d == 128 &&
+         a.nblk <= kRtMaxBlocks && a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0;
 }
 
 static int route_tile_launch(const RouteArgs& a, cudaStream_t st) {
@@ -1388,15 +1406,34 @@ extern "C" int srswa_kbar_paged(const void* idx_cache, int dtype, int64_t s_page
   return kbar_launch(a, R * per, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int srswa_kbar_pages(const void* idx_cache, int dtype, int64_t s_page, int64_t s_tok, int64_t d,
+                                int64_t block_size, const int64_t* pages, const int32_t* tok, int64_t n,
+                                const float* head_cls, float* kbar_cache, int64_t s_kbar, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(idx_cache && head_cls && kbar_cache && n >= 0 && (n == 0 || (pages && tok)), SRSWA_EINVAL);
+  const int64_t align = dtype == SRSWA_F32 ? 4 : 8;  // 16-byte vector loads
+  SRSWA_CHECK_ARG(d > 0 && d <= 128 && d % align == 0, SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG(block_size > 0 && block_size <= kMaxBlockSize, SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG((s_page % align) == 0 && (s_tok % align) == 0 &&
+                      (reinterpret_cast<uintptr_t>(idx_cache) & 15) == 0,
+                  SRSWA_EALIGN);
+  if (n == 0) return 0;
+  KbarArgs a = {};
+  a.keys = idx_cache; a.dtype = dtype; a.d = d; a.bs = block_size; a.hc = head_cls; a.out = kbar_cache;
+  a.st = s_tok; a.s_page = s_page; a.s_kbar = s_kbar; a.paged = 2;
+  a.plan_pages = pages; a.plan_tok = tok; a.plan_n = n;
+  return kbar_launch(a, n, reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
                            const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk,
                            const int32_t* block_table, int64_t s_bt, const int32_t* seq_lens,
-                           int64_t rows_per_seq, const int64_t* q_pos, const uint8_t* cand,
-                           int64_t s_cand, srswa_route_params params, int64_t* topi64,
+                           int64_t rows_per_seq, const int32_t* row_seq, const int64_t* q_pos,
+                           const uint8_t* cand, int64_t s_cand, srswa_route_params params, int64_t* topi64,
                            int32_t* topi32, float* bias, uint8_t* valid, float* scores,
                            void* workspace, size_t workspace_bytes, srswa_stream_t stream) {
   SRSWA_CHECK_ARG(idx_q && kbar && N >= 0 && nblk > 0 && rows_per_seq > 0, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(q_pos || seq_lens, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(!row_seq || q_pos, SRSWA_EINVAL);  // varlen rows carry their positions
   SRSWA_CHECK_ARG(d == 128 || d == 64, SRSWA_EUNSUPPORTED);
   SRSWA_CHECK_ARG((reinterpret_cast<uintptr_t>(kbar) & 15) == 0 && (s_kbar_b % 4) == 0 &&
                       (s_kbar_c % 4) == 0 && (s_q % 4) == 0,
@@ -1406,7 +1443,7 @@ extern "C" int srswa_route(const void* idx_q, int q_dtype, int64_t s_q, int64_t 
   if (rc) return rc;
   a.from_scores = 0; a.q = idx_q; a.q_dtype = q_dtype; a.s_q = s_q; a.d = d; a.kbar = kbar;
   a.s_kbar_b = s_kbar_b; a.s_kbar_c = s_kbar_c; a.block_table = block_table; a.s_bt = s_bt;
-  a.seq_lens = seq_lens; a.rows_per_seq = rows_per_seq; a.q_pos = q_pos; a.cand = cand;
+  a.seq_lens = seq_lens; a.rows_per_seq = rows_per_seq; a.row_seq = row_seq; a.q_pos = q_pos; a.cand = cand;
   a.s_cand = s_cand; a.N = N; a.nblk = nblk; a.topi64 = topi64; a.topi32 = topi32; a.bias = bias;
   a.valid = valid; a.scores_out = scores;
   return route_launch(a, reinterpret_cast<cudaStream_t>(stream), workspace, workspace_bytes);

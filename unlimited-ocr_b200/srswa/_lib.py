@@ -52,8 +52,9 @@ _SIGS = {
     "srswa_kbar_contig": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp]),
     "srswa_kbar_paged": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, vp, i64, i64, vp, i64, i64, vp, vp,
                                    i64, vp]),
+    "srswa_kbar_pages": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, vp, vp, i64, vp, vp, i64, vp]),
     "srswa_route_workspace_size": (C.c_size_t, [i64, i64, i64, RouteParams, C.c_int]),
-    "srswa_route": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp, i64, vp, vp, i64,
+    "srswa_route": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp, i64, vp, vp, vp, i64,
                               RouteParams, vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),
     "srswa_route_select": (C.c_int, [vp, i64, i64, i64, vp, i64, RouteParams, vp, vp, vp, vp, vp]),
     "srswa_route_shard_workspace_size": (C.c_size_t, [i64, i64, RouteParams]),
@@ -75,6 +76,7 @@ _SIGS = {
                                            vp, vp, vp, vp, vp, vp, vp]),
     "srswa_decode_attend": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                       vp]),
+    "srswa_prefill_attend": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "srswa_workspace_status": (C.c_int, [vp, C.POINTER(C.c_int), vp]),
     "srswa_gather_bwd_noalloc_status": (C.c_int, [C.POINTER(C.c_int), vp]),
     "srswa_lse_merge": (C.c_int, [vp, vp, i64, i64, i64, i64, i64, i64, vp, C.c_int, vp, vp]),
@@ -87,6 +89,7 @@ _SIGS = {
     "srswa_decode_allow_state": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp,
                                            C.c_size_t, vp]),
     "srswa_decode_allow": (C.c_int, [vp, i64, i64, i64, vp, vp, i64, i64, vp, vp, i64, vp, vp]),
+    "srswa_win_bounds_decode": (C.c_int, [vp, i64, i64, vp, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp]),
     "srswa_rope2d_pos_workspace_size": (C.c_size_t, [i64, i64]),
     "srswa_rope2d_pos": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, vp, vp, vp, i64, vp, vp, C.c_size_t,
                                    vp]),

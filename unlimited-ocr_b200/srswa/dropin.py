@@ -15,7 +15,8 @@ After ``install``:
     and ``SlidingWindowLlamaAttention._main_rope_coords`` -> ``srswa.page_rope``
 so DashAttention._forward_triton, SlidingWindowLlamaAttention's sparse branch,
 the DSA indexer and the DASH inference overlay call the CUDA kernels without a
-source change.  ``install_sglang()`` does the same for the SGLang ops modules.
+source change.  ``install_sglang()`` does the same for the SGLang ops modules
+and for the DASH attention backend's own imported copies of them.
 """
 
 from __future__ import annotations
@@ -60,10 +61,39 @@ def install(pkg: str) -> None:
         mu._uocr_dash_decode_allow = page_gate._uocr_dash_decode_allow
 
 
-def install_sglang(prefix: str = "sglang.srt.layers.attention.unlimited_dash_ops") -> None:
-    at = sys.modules.get(f"{prefix}.attend_triton")
-    if at is not None:
-        at.dash_sparse_attn_decode = paged.dash_sparse_attn_decode
-    rt = sys.modules.get(f"{prefix}.route_triton")
-    if rt is not None:
-        rt.kbar_refresh_tail_triton = paged.kbar_refresh_tail
+# SGLang names this library provides, per reference module that defines them
+_SGLANG_OPS = {
+    "attend_triton": ("dash_sparse_attn", "dash_sparse_attn_decode"),
+    "route_triton": ("route_decode_triton", "route_prefill_triton", "kbar_refresh_tail_triton",
+                     "win_bounds_decode"),
+}
+_SGLANG_BACKEND = "sglang.srt.layers.attention.unlimited_ocr_v2_backend"
+
+
+def install_sglang(prefix: str = "sglang.srt.layers.attention.unlimited_dash_ops",
+                   backend: str = _SGLANG_BACKEND) -> list[str]:
+    """Point SGLang's DASH serving ops at ``srswa.paged``.
+
+    The backend binds the ops by ``from ... import`` when it is imported
+    (whl:sglang/srt/layers/attention/unlimited_ocr_v2_backend.py:18-52), so the
+    names are rebound both in the ops modules and in the already-imported
+    backend module, which holds its own copies.  A module imported later picks
+    up the ops modules' (already rebound) attributes.  The torch-only planning
+    helpers (kbar_tail_plan, kbar_all_plan, prefill_row2req) stay the
+    reference's.  Returns the qualified names rebound."""
+    done = []
+    for mod_name, names in _SGLANG_OPS.items():
+        mod = sys.modules.get(f"{prefix}.{mod_name}")
+        if mod is None:
+            continue
+        for name in names:
+            setattr(mod, name, getattr(paged, name))
+            done.append(f"{mod.__name__}.{name}")
+    be = sys.modules.get(backend)
+    if be is not None:
+        for names in _SGLANG_OPS.values():
+            for name in names:
+                if hasattr(be, name):
+                    setattr(be, name, getattr(paged, name))
+                    done.append(f"{be.__name__}.{name}")
+    return done

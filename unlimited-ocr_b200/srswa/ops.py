@@ -25,12 +25,16 @@ def _cand_args(cand, N, nblk):
         c = c.to(torch.uint8)
     if c.dim() == 1:
         return c.contiguous(), 0
-    c = c.reshape(-1, nblk)
+    if c.dim() == 2 and c.shape[1] > nblk:
+        c = c[:, :nblk]          # a mask wider than the scored blocks (the serving [rows, WQ] layout)
+    else:
+        c = c.reshape(-1, nblk)
     if c.shape[0] == 1:
         return c.contiguous(), 0
-    c = c.contiguous()
+    if c.stride(-1) != 1:
+        c = c.contiguous()
     assert c.shape[0] == N
-    return c, nblk
+    return c, c.stride(0)
 
 
 def _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma):
@@ -97,12 +101,30 @@ def kbar_paged(idx_cache, head_cls, block_table, seq_lens, kbar_cache, tail_page
     L.check(rc, "srswa_kbar_paged")
 
 
+def kbar_pages(idx_cache, head_cls, pages, tok, kbar_cache):
+    """k_bar of an explicit page plan: pages [n] (page ids), tok [n] (tokens
+    in use; <= 0: skipped) -> kbar_cache rows written in place."""
+    P, BS, d = idx_cache.shape
+    assert idx_cache.stride(-1) == 1 and kbar_cache.stride(-1) == 1
+    pg = pages.to(device=idx_cache.device, dtype=torch.int64).contiguous().view(-1)
+    tk = tok.to(device=idx_cache.device, dtype=torch.int32).contiguous().view(-1)
+    assert pg.numel() == tk.numel()
+    hc = head_cls.to(device=idx_cache.device, dtype=torch.float32).contiguous()
+    rc = L.lib().srswa_kbar_pages(idx_cache.data_ptr(), L.dtype_code(idx_cache), idx_cache.stride(0),
+                                  idx_cache.stride(1), d, BS, pg.data_ptr(), tk.data_ptr(), pg.numel(),
+                                  hc.data_ptr(), kbar_cache.data_ptr(), kbar_cache.stride(0),
+                                  L.stream_of(idx_cache))
+    L.check(rc, "srswa_kbar_pages")
+
+
 def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor, sigma,
           q_pos=None, seq_lens=None, rows_per_seq=1, block_table=None, cand=None,
-          want=("topi64", "bias", "valid"), nblk=None, out=None):
+          want=("topi64", "bias", "valid"), nblk=None, out=None, row_seq=None):
     """Fused scores + selection for query rows idx_q [N, d].
 
     kbar: contiguous [B, nblk, d] (block_table None) or paged cache [P, d].
+    Row n belongs to sequence n // rows_per_seq, or row_seq[n] (int32 [N],
+    varlen prefill rows; needs q_pos).
     Returns a dict with the requested outputs among topi64, topi32, bias,
     valid, scores.  out: caller-owned tensors for some of them (contiguous,
     [N, K] or [N, nblk], the output's dtype), written in place."""
@@ -119,7 +141,12 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
         s_b, s_c = 0, kbar.stride(0)
         bt = block_table.to(torch.int32).contiguous()
         nblk = bt.shape[1] if nblk is None else nblk
-    _check_rows(N, rows_per_seq, kbar, bt, nblk)
+    if row_seq is None:
+        _check_rows(N, rows_per_seq, kbar, bt, nblk)
+    else:
+        if q_pos is None:
+            raise ValueError("route: varlen rows (row_seq) need q_pos")
+        row_seq = row_seq.to(device=dev, dtype=torch.int32).contiguous()
     K, M = effective_km(topk, topm, nblk)
     given = out or {}
     out = {}
@@ -142,7 +169,7 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
     ws = torch.empty(ws_n, device=dev, dtype=torch.uint8) if ws_n else None
     rc = lib.srswa_route(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
                          kbar.data_ptr(), s_b, s_c, nblk, L.ptr(bt), 0 if bt is None else bt.stride(0),
-                         L.ptr(sl), int(rows_per_seq), L.ptr(qp), L.ptr(cnd), s_cand, p,
+                         L.ptr(sl), int(rows_per_seq), L.ptr(row_seq), L.ptr(qp), L.ptr(cnd), s_cand, p,
                          L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
                          L.ptr(out["valid"]), L.ptr(out["scores"]), L.ptr(ws), ws_n, L.stream_of(idx_q))
     L.check(rc, "srswa_route")
@@ -431,6 +458,48 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
                                      L.ptr(bt), L.ptr(sl), L.ptr(qp), ti.data_ptr(), L.ptr(b), L.ptr(vd),
                                      out.data_ptr(), L.ptr(lse_t), L.stream_of(q))
     L.check(rc, "srswa_decode_attend")
+    return (out, lse_t) if lse else out
+
+
+def prefill_attend(q, k_cache, v_cache, topk_idx, bias, *, block_table, cu_seqlens_q, prefix_lens, block_size,
+                   local_blocks, sm_scale, out=None, lse=False):
+    """Paged varlen prefill attend: q [total_q, H, D]; caches [P, BS, Hkv, D];
+    rows of request r are cu_seqlens_q[r] .. cu_seqlens_q[r+1]-1 at positions
+    prefix_lens[r] + i; topk_idx / bias [Hkv or 1 (stride 0 ok), total_q, K]
+    or [total_q, K] (-1 = unused slot)."""
+    N, H, D = q.shape
+    assert k_cache.stride() == v_cache.stride()
+    P, BS, Hkv, _ = k_cache.shape
+    assert BS == block_size
+    ti = topk_idx.unsqueeze(0) if topk_idx.dim() == 2 else topk_idx
+    if ti.dtype not in (torch.int32, torch.int64):
+        raise NotImplementedError("topk_idx must be int32 or int64")
+    if ti.stride(-1) != 1:
+        ti = ti.contiguous()
+    s_ti_h = ti.stride(0) if ti.shape[0] > 1 else 0
+    b = None
+    s_b_h = s_b_n = 0
+    if bias is not None:
+        b = bias.unsqueeze(0) if bias.dim() == 2 else bias
+        if b.dtype != torch.float32 or b.stride(-1) != 1:
+            b = b.float().contiguous()
+        s_b_h = b.stride(0) if b.shape[0] > 1 else 0
+        s_b_n = b.stride(1)
+    if out is None:
+        out = torch.empty(N, H, D, device=q.device, dtype=q.dtype)
+    lse_t = torch.empty(N, H, device=q.device, dtype=torch.float32) if lse else None
+    bt = block_table.to(torch.int32).contiguous()
+    cu = cu_seqlens_q.to(device=q.device, dtype=torch.int32).contiguous()
+    pl = prefix_lens.to(device=q.device, dtype=torch.int32).contiguous()
+    R, W = bt.shape
+    d = L.DecodeDesc(N, H, Hkv, D, ti.shape[-1], block_size, local_blocks, float(sm_scale),
+                     L.dtype_code(q), L.dtype_code(k_cache), L.dtype_code(out), q.stride(0), q.stride(1),
+                     k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), out.stride(0), out.stride(1),
+                     R, W, 0, 1, 1 if ti.dtype == torch.int64 else 0, s_ti_h, ti.stride(1), s_b_h, s_b_n, 0, 0)
+    rc = L.lib().srswa_prefill_attend(C.byref(d), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                      bt.data_ptr(), cu.data_ptr(), pl.data_ptr(), ti.data_ptr(), L.ptr(b),
+                                      out.data_ptr(), L.ptr(lse_t), L.stream_of(q))
+    L.check(rc, "srswa_prefill_attend")
     return (out, lse_t) if lse else out
 
 

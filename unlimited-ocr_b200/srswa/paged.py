@@ -4,17 +4,29 @@
 * ``dash_sparse_attn_decode`` (attend_triton.py:600-715): split-KV decode with
   the merge done on-chip (thread-block cluster) instead of a second kernel;
   writes ``output`` in place.
-* ``kbar_refresh_tail`` (route_triton.py:706-726) and ``KBarCache``
-  (dash_stage0.py:106-150): one fp32 head_cls summary per KV page.
-* ``route_decode`` (route_triton.py:729-847): fused scores over the k_bar cache
-  + top-M entmax + top-K + bias into caller-owned ``out_idx`` / ``out_bias``
-  (score-descending slots, -1 / 0 on unused slots).
+* ``dash_sparse_attn`` (attend_triton.py:523-597): varlen paged prefill
+  attend, one row per query token; writes ``output`` in place.
+* ``kbar_refresh_tail`` / ``kbar_refresh_tail_triton`` (route_triton.py:706-726)
+  and ``KBarCache`` (dash_stage0.py:106-150): one fp32 head_cls summary per KV
+  page, for the tail pages or for an explicit (pages, tokens) plan.
+* ``route_decode`` / ``route_decode_triton`` (route_triton.py:729-847) and
+  ``route_prefill_triton`` (:624-680): fused scores over the k_bar cache +
+  top-M entmax + top-K + bias into caller-owned ``out_idx`` / ``out_bias``
+  (score-descending slots, -1 / 0 on unused slots).  The slots hold the
+  reference HF router's selection (top-M exact entmax); the wheel's
+  bisection entmax over every candidate selects the same set (the attend
+  reads the slots as a set), its bias can differ when the entmax support
+  exceeds M.
+* ``win_bounds_decode`` (route_triton.py:466-526): each decode row's remote
+  page span from its allow mask.  The router here scans the whole live
+  width in one pass, so the span is an output for the caller only.
 """
 
 from __future__ import annotations
 
 import torch
 
+from . import _lib as L
 from . import ops
 
 SPARSE_BLOCK_SIZE = 128
@@ -34,6 +46,25 @@ def dash_sparse_attn_decode(q, k_cache, v_cache, topk_idx, blk_bias, block_table
     ops.decode_attend(q, k_cache, v_cache, topk_idx, blk_bias, block_size=sparse_block_size,
                       local_blocks=local_blocks, sm_scale=sm_scale, out=output, block_table=block_table,
                       seq_lens=seq_lens, rows_per_req=decode_query_len)
+
+
+@torch.no_grad()
+def dash_sparse_attn(q, k_cache, v_cache, topk_idx, blk_bias, block_table, cu_seqlens_q, seq_lens, prefix_lens,
+                     max_query_len, num_kv_heads, sm_scale, output, local_blocks=0,
+                     sparse_block_size=SPARSE_BLOCK_SIZE):
+    """Bias-aware block-sparse prefill attention over the paged cache.  q
+    [total_q, H, D]; row i of request r (cu_seqlens_q[r] <= i < cu_seqlens_q[r+1])
+    sits at position prefix_lens[r] + i - cu_seqlens_q[r]; topk_idx / blk_bias
+    [Hkv, total_q, K] (stride 0 over heads allowed; -1 = unused slot).
+    seq_lens and max_query_len are accepted for signature compatibility (the
+    rows carry their positions; no grid is sized on the host)."""
+    del seq_lens, max_query_len
+    assert k_cache.shape[2] == num_kv_heads
+    if blk_bias is not None:
+        assert blk_bias.shape == topk_idx.shape and blk_bias.dtype == torch.float32
+    ops.prefill_attend(q, k_cache, v_cache, topk_idx, blk_bias, block_table=block_table,
+                       cu_seqlens_q=cu_seqlens_q, prefix_lens=prefix_lens, block_size=sparse_block_size,
+                       local_blocks=local_blocks, sm_scale=sm_scale, out=output)
 
 
 class KBarCache:
@@ -57,8 +88,44 @@ class KBarCache:
 @torch.no_grad()
 def kbar_refresh_tail(*, kv_cache, k_bar, block_table, seq_lens, head_cls, block_size: int, tail_pages: int = 1,
                       plan=None):
-    del plan
+    """Refresh k_bar of the last ``tail_pages`` pages of every request, or of
+    the pages of ``plan`` = (pages, tokens) when given (the reference's
+    kbar_tail_plan / kbar_all_plan output; entries with no token are
+    skipped)."""
+    assert kv_cache.shape[1] == block_size
+    if plan is not None:
+        pages, tok = plan
+        ops.kbar_pages(kv_cache, head_cls, pages, tok, k_bar)
+        return
     ops.kbar_paged(kv_cache, head_cls, block_table, seq_lens, k_bar, tail_pages)
+
+
+kbar_refresh_tail_triton = kbar_refresh_tail
+
+
+@torch.no_grad()
+def win_bounds_decode(*, allow, seq_lens, lo, hi, fit, max_block: int, block_size: int, local_blocks: int,
+                      decode_query_len: int, tile: int):
+    """Fill lo / hi / fit (int32 / int32 / int8 [nd]) in place from the
+    per-decode-row allow mask [>= nd, WQ] (bool or uint8)."""
+    nd = int(lo.numel())
+    if nd <= 0:
+        return
+    a = allow.view(torch.uint8) if allow.dtype == torch.bool else allow
+    if a.dtype not in (torch.uint8, torch.int8):
+        a = (a != 0).to(torch.uint8)
+    if a.stride(-1) != 1:
+        a = a.contiguous()
+    for t, dt in ((lo, torch.int32), (hi, torch.int32), (fit, torch.int8)):
+        if t.dtype != dt or not t.is_contiguous():
+            raise ValueError("win_bounds_decode: lo / hi must be contiguous int32, fit contiguous int8")
+    sl = seq_lens if (seq_lens.dtype == torch.int32 and seq_lens.is_contiguous()) else \
+        seq_lens.to(torch.int32).contiguous()
+    rc = L.lib().srswa_win_bounds_decode(a.data_ptr(), a.stride(0), a.shape[1], sl.data_ptr(), nd, int(max_block),
+                                         int(block_size), int(local_blocks), max(1, int(decode_query_len)),
+                                         int(tile), lo.data_ptr(), hi.data_ptr(), fit.data_ptr(),
+                                         L.stream_of(lo))
+    L.check(rc, "srswa_win_bounds_decode")
 
 
 @torch.no_grad()
@@ -89,4 +156,60 @@ def route_decode(*, idx_q, k_bar, block_table, seq_lens, image_allow, out_idx, o
         out_idx[:, k:].fill_(-1)
         out_bias[:, k:].zero_()
     return out_slots or k
+
+
+def route_decode_triton(*, idx_q, k_bar, block_table, seq_lens, image_allow, out_idx, out_bias, max_block: int,
+                        block_size: int, local_blocks: int, decode_query_len: int, idx_scale: float,
+                        prior_floor: float, sigma: float, topm: int, score_buf=None, budget: int | None = None,
+                        out_slots: int | None = None, entmax_base=None, entmax_fit=None, entmax_width: int = 0,
+                        score_buf_win=None, bounds=None):
+    """The reference's decode router signature.  score_buf and the scan-window
+    arguments (bounds, entmax_base / fit / width, score_buf_win) only choose
+    how the reference's kernels tile the scan; the selection does not depend
+    on them, and the kernels here scan the live width in one pass."""
+    del score_buf, entmax_base, entmax_fit, entmax_width, score_buf_win, bounds
+    return route_decode(idx_q=idx_q, k_bar=k_bar, block_table=block_table, seq_lens=seq_lens,
+                        image_allow=image_allow, out_idx=out_idx, out_bias=out_bias, max_block=max_block,
+                        block_size=block_size, local_blocks=local_blocks, decode_query_len=decode_query_len,
+                        idx_scale=idx_scale, prior_floor=prior_floor, sigma=sigma, topm=topm, budget=budget,
+                        out_slots=out_slots)
+
+
+@torch.no_grad()
+def route_prefill_triton(*, idx_q, k_bar, block_table, seq_lens, cu_seqlens_q, context_lens, row2req, image_allow,
+                         out_idx, out_bias, max_block: int, block_size: int, local_blocks: int, idx_scale: float,
+                         prior_floor: float, sigma: float, topm: int, budget: int | None = None,
+                         q_chunk: int = 2048, out_slots: int | None = None, score_buf=None):
+    """Route varlen prefill rows idx_q [total_q, d]: row i of request
+    r = row2req[i] sits at position context_lens[r] + i - cu_seqlens_q[r].
+    Writes out_idx / out_bias like route_decode; returns (slot width, None,
+    0): all rows are routed in one launch (no q_chunk loop, so no last score
+    chunk to hand back)."""
+    del q_chunk, score_buf
+    dev = idx_q.device
+    N = int(idx_q.shape[0])
+    W = min(int(max_block), int(block_table.shape[1]))
+    K = max(1, min(int(budget or topm), int(topm)))
+    Ke, _ = ops.effective_km(K, topm, W)
+    width = out_slots or Ke
+    if N == 0:
+        return width, None, 0
+    r = row2req.to(device=dev, dtype=torch.int64)
+    rows = torch.arange(N, device=dev, dtype=torch.int64)
+    q_pos = (context_lens.to(device=dev, dtype=torch.int64)[r] + rows
+             - cu_seqlens_q.to(device=dev, dtype=torch.int64)[r])
+    direct = (out_idx.dtype == torch.int32 and out_bias.dtype == torch.float32 and out_idx.is_contiguous()
+              and out_bias.is_contiguous() and tuple(out_idx.shape) == (N, Ke) and tuple(out_bias.shape) == (N, Ke))
+    res = ops.route(idx_q, k_bar, block_size=block_size, local_blocks=local_blocks, topk=K, topm=topm,
+                    idx_scale=idx_scale, floor=prior_floor, sigma=sigma, seq_lens=seq_lens, q_pos=q_pos,
+                    row_seq=row2req, block_table=block_table[:, :W], cand=image_allow, want=("topi32", "bias"),
+                    nblk=W, out={"topi32": out_idx, "bias": out_bias} if direct else None)
+    if not direct:
+        k = res["topi32"].shape[-1]
+        out_idx[:N, :k].copy_(res["topi32"])
+        out_bias[:N, :k].copy_(res["bias"])
+        if out_idx.shape[-1] > k:
+            out_idx[:N, k:].fill_(-1)
+            out_bias[:N, k:].zero_()
+    return width, None, 0
 
