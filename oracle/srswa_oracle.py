@@ -558,16 +558,45 @@ def paged_decode(q, k_cache, v_cache, topk_idx, blk_bias, block_table, seq_lens,
     pos <= p and pos < max(0, p - LW + 1), biased; local keys: blocks
     p//BS - j (j = 0..L), max(0, p-LW+1) <= pos <= p, unbiased.
     Returns (out [R*dql,H,D] fp32, lse [R*dql,H] natural log)."""
+    N = q.shape[0]
+    dql = decode_query_len
+    req = np.arange(N) // dql
+    pos = np.asarray(seq_lens, np.int64)[req] - dql + np.arange(N) % dql
+    return _paged_rows(q, k_cache, v_cache, topk_idx, blk_bias, block_table, req, pos, sm_scale, local_blocks,
+                       block_size)
+
+
+def paged_prefill(q, k_cache, v_cache, topk_idx, blk_bias, block_table, cu_seqlens_q, prefix_lens, sm_scale,
+                  local_blocks, block_size):
+    """``dash_sparse_attn`` semantics, one program per query token
+    (whl:sglang/srt/layers/attention/unlimited_dash_ops/attend_triton.py:88-292,
+    523-597): row i of request r (cu_seqlens_q[r] <= i < cu_seqlens_q[r+1])
+    sits at p = prefix_lens[r] + i - cu_seqlens_q[r]; remote keys of its
+    selected blocks below the window start (pos <= p - LW), biased; local
+    keys [p - LW + 1, p], unbiased.  The reference walks the first
+    count(slot >= 0) slots, so valid slots must come first (as its router
+    packs them).  Returns (out [N,H,D] fp32, lse [N,H] natural log)."""
+    cu = np.asarray(cu_seqlens_q, np.int64)
+    N = int(cu[-1])
+    req = np.searchsorted(cu, np.arange(N), side="right") - 1
+    pos = np.asarray(prefix_lens, np.int64)[req] + np.arange(N) - cu[req]
+    return _paged_rows(q, k_cache, v_cache, topk_idx, blk_bias, block_table, req, pos, sm_scale, local_blocks,
+                       block_size)
+
+
+def _paged_rows(q, k_cache, v_cache, topk_idx, blk_bias, block_table, req, pos_of_row, sm_scale, local_blocks,
+                block_size):
+    """One softmax per (row, head) over the row's remote keys (selected
+    blocks, pos <= p and pos < p - LW + 1, slot bias) and window keys."""
     N, H, D = q.shape
     Hkv = k_cache.shape[2]
     G = H // Hkv
     lw = local_blocks * block_size
     out = np.zeros((N, H, v_cache.shape[-1]), F32)
     lse = np.full((N, H), -np.inf, F32)
-    dql = decode_query_len
     for n in range(N):
-        r = n // dql
-        p = int(seq_lens[r]) - dql + (n % dql)
+        r = int(req[n])
+        p = int(pos_of_row[n])
         lws = max(0, p - lw + 1)
         for h in range(H):
             hk = h // G
@@ -608,6 +637,34 @@ def paged_decode(q, k_cache, v_cache, topk_idx, blk_bias, block_table, seq_lens,
             out[n, h] = (e @ V_) / l
             lse[n, h] = mx + np.log(l)
     return out, lse
+
+
+def win_bounds_decode(allow, seq_lens, nd, max_block, block_size, local_blocks, decode_query_len, tile):
+    """Remote page span of each decode row from its allow mask [nd, WQ]
+    (whl:.../unlimited_dash_ops/route_triton.py:466-526): (lo, hi) = first
+    and one past the last allowed block among the live remote blocks
+    (c <= q_blk - L, c * bs < seq_len, c < min(W, WQ)); with none, (0, 0)
+    when the row has no remote block at all, else (0, live width
+    min(W, max(nblk, 1))); fit = hi - lo <= tile.  q_blk truncates toward
+    zero (Triton integer division).  -> lo, hi int32 [nd], fit int8 [nd]."""
+    W, WQ = int(max_block), allow.shape[1]
+    lo = np.zeros(nd, np.int32)
+    hi = np.zeros(nd, np.int32)
+    fit = np.zeros(nd, np.int8)
+    for row in range(nd):
+        seq = int(seq_lens[row // decode_query_len])
+        q_pos = seq - decode_query_len + row % decode_query_len
+        q_blk = int(q_pos / block_size)            # truncation toward zero
+        off = np.arange(min(W, WQ))
+        keep = (allow[row, :len(off)] != 0) & (off <= q_blk - local_blocks) & (off * block_size < seq)
+        nb = (seq + block_size - 1) // block_size
+        if keep.any():
+            lo_v, hi_v = int(off[keep].min()), int(off[keep].max()) + 1
+        else:
+            no_remote = seq <= 0 or (q_blk - local_blocks) < 0
+            lo_v, hi_v = 0, (0 if no_remote else min(W, max(nb, 1)))
+        lo[row], hi[row], fit[row] = lo_v, hi_v, int(hi_v - lo_v <= tile)
+    return lo, hi, fit
 
 
 def lse_merge(o_parts, lse_parts):

@@ -81,7 +81,7 @@ def import_sglang_ops():
         m.__path__ = [os.path.join(tmp, *pk.split("."))]
         sys.modules[pk] = m
     out = {}
-    for name in ("common", "dash_router", "dash_stage0", "attend_triton"):
+    for name in ("common", "dash_router", "dash_stage0", "attend_triton", "route_triton"):
         full = f"sglang.srt.layers.attention.unlimited_dash_ops.{name}"
         spec = importlib.util.spec_from_file_location(full, os.path.join(tmp, sub, name + ".py"))
         mod = importlib.util.module_from_spec(spec)
@@ -350,6 +350,79 @@ def case_paged(sgl):
          out=out, params=np.array([BS, L, 3, 4]), fparams=np.array([5.0 / math.sqrt(d), 1e-3, 1.0, 0.2]))
 
 
+def case_paged_prefill(sgl):
+    """SGLang prefill serving ops on a shuffled page pool of three requests
+    with cached prefixes: the k_bar refresh driven by kbar_all_plan, the
+    varlen router route_prefill_triton (with an image-allow mask) and the
+    paged prefill attend dash_sparse_attn (K8) on its selection, plus the
+    decode scan window win_bounds_decode (K14) -- all interpreted."""
+    at, rt, st = sgl["attend_triton"], sgl["route_triton"], sgl["dash_stage0"]
+    g = torch.Generator().manual_seed(23)
+    R, H, Hkv, D, d, BS, L, W = 3, 4, 2, 64, 64, 32, 2, 14
+    P = R * W + 5
+    ctx = torch.tensor([0, 70, 20], dtype=torch.int32)
+    qlen = torch.tensor([90, 40, 130], dtype=torch.int32)
+    seq = ctx + qlen
+    cu = torch.zeros(R + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(qlen, 0)
+    N = int(cu[-1])
+    perm = torch.randperm(P, generator=g)[: R * W].view(R, W).to(torch.int32)
+    k_cache = bf16r(torch.randn(P, BS, Hkv, D, generator=g))
+    v_cache = bf16r(torch.randn(P, BS, Hkv, D, generator=g))
+    idx_cache = bf16r(torch.randn(P, BS, d, generator=g))
+    q = bf16r(torch.randn(N, H, D, generator=g))
+    idx_q = bf16r(torch.randn(N, d, generator=g))
+    hc = torch.randn(d, generator=g) * 0.2
+    # summaries of the prefix pages (as a previous step left them), then the
+    # refresh of the pages this prefill step writes, driven by kbar_all_plan
+    cache = st.KBarCache(P, d, "cpu")
+    for r in range(R):
+        nb = (int(ctx[r]) + BS - 1) // BS
+        if nb:
+            pages = perm[r, :nb].long()
+            pos = torch.arange(nb)[:, None] * BS + torch.arange(BS)[None, :]
+            cache.put(pages, st._summary_keys(idx_cache[pages].float(), pos < int(ctx[r]), hc,
+                                              1.0 / math.sqrt(d)))
+    kbar_before = cache.k_bar.clone()
+    plan = rt.kbar_all_plan(block_table=perm, seq_lens=seq, context_lens=ctx, block_size=BS, max_block=W,
+                            max_query_len=int(qlen.max()), device="cpu")
+    rt.kbar_refresh_tail_triton(kv_cache=idx_cache, k_bar=cache.k_bar, block_table=perm, seq_lens=seq,
+                                head_cls=hc, block_size=BS, plan=plan)
+    kbar = cache.k_bar.clone()
+    row2req = rt.prefill_row2req(cu_seqlens_q=cu, device="cpu")
+    # image-allow mask [N, WQ] (WQ > W)
+    WQ = W + 2
+    allow = torch.rand(N, WQ, generator=g) < 0.6
+    topm, budget = 16, 4
+    out_idx = torch.full((N, topm), -7, dtype=torch.int32)
+    out_bias = torch.full((N, topm), 9.0)
+    width, _, _ = rt.route_prefill_triton(
+        idx_q=idx_q, k_bar=kbar, block_table=perm, seq_lens=seq, cu_seqlens_q=cu, context_lens=ctx,
+        row2req=row2req, image_allow=allow, out_idx=out_idx, out_bias=out_bias, max_block=W, block_size=BS,
+        local_blocks=L, idx_scale=5.0, prior_floor=1e-3, sigma=1.0, topm=topm, budget=budget)
+    # the wheel packs the active blocks at the front of out_idx
+    ti = out_idx[:, :budget].contiguous()
+    tb = out_bias[:, :budget].contiguous()
+    out = torch.zeros(N, H, D)
+    at.dash_sparse_attn(q, k_cache, v_cache, ti.unsqueeze(0).expand(Hkv, -1, -1),
+                        tb.unsqueeze(0).expand(Hkv, -1, -1), perm, cu, seq, ctx, int(qlen.max()), Hkv, 0.125,
+                        out, local_blocks=L, sparse_block_size=BS)
+    # decode scan window over decode rows of the same requests (2 per request)
+    dql = 2
+    dallow = torch.rand(R * dql, WQ, generator=g) < 0.3
+    dallow[1] = False                      # a row with no allowed block
+    lo = torch.zeros(R * dql, dtype=torch.int32)
+    hi = torch.zeros(R * dql, dtype=torch.int32)
+    fit = torch.zeros(R * dql, dtype=torch.int8)
+    rt.win_bounds_decode(allow=dallow, seq_lens=seq, lo=lo, hi=hi, fit=fit, max_block=W, block_size=BS,
+                         local_blocks=L, decode_query_len=dql, tile=4)
+    save("paged_prefill", q=q, k_cache=k_cache, v_cache=v_cache, idx_cache=idx_cache, idx_q=idx_q, hc=hc,
+         block_table=perm, seq_lens=seq, context_lens=ctx, cu_seqlens_q=cu, row2req=row2req,
+         plan_pages=plan[0], plan_tok=plan[1], kbar_before=kbar_before, kbar=kbar, allow=allow,
+         out_idx=out_idx, out_bias=out_bias, width=np.array(width), out=out, dallow=dallow, lo=lo, hi=hi,
+         fit=fit, params=np.array([BS, L, topm, budget, dql, 4]), fparams=np.array([5.0, 1e-3, 1.0, 0.125]))
+
+
 PAGE_IMG, PAGE_MARK = 128815, 128827   # config.json image_token_id, page_token_id
 
 
@@ -564,9 +637,9 @@ def case_page_rope(m):
 
 
 # cases run on the SGLang ops of the wheel; all others on the HF modules
-_SGL_CASES = {"paged"}
+_SGL_CASES = {"paged", "paged_prefill"}
 _ORDER = ("route", "entmax", "decode_attend", "forward_dense", "gather_triton", "gather_e2e", "block_max",
-          "paged", "page_gate", "page_rope")
+          "paged", "paged_prefill", "page_gate", "page_rope")
 
 
 def main():

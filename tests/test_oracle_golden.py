@@ -315,3 +315,53 @@ def test_page_rope_decode_golden():
         st = PR.decode_coords_step(st, g["dec_steps"][:, k], 128827)
         np.testing.assert_array_equal(st["tok"], g["dec_tok"][k])
         np.testing.assert_array_equal(st["page"], g["dec_page"][k])
+
+
+def _prefill_router_rows(g):
+    """The oracle's HF router (_block_scores_infer + _infer_route_select) on
+    the varlen prefill rows of the paged_prefill fixture."""
+    BS, L, topm, budget = (int(x) for x in g["params"][:4])
+    idx_scale, floor, sigma = (float(x) for x in g["fparams"][:3])
+    bt, seq, ctx, cu = g["block_table"], g["seq_lens"], g["context_lens"], g["cu_seqlens_q"]
+    W = bt.shape[1]
+    N = int(cu[-1])
+    out = []
+    for n in range(N):
+        r = int(g["row2req"][n])
+        p = int(ctx[r]) + n - int(cu[r])
+        kb = g["kbar"][bt[r]][None]
+        cv = (np.arange(W) * BS < int(seq[r]))[None]
+        sc = O.block_scores_headcls(g["idx_q"][n][None, None], kb, cv, np.array([[p]]), BS, L)
+        cand = g["allow"][n, :W][None, None].astype(bool)
+        topi, bias, valid = O.infer_route_select(sc, cand, idx_scale, floor, sigma, budget, topm)
+        out.append((topi[0, 0], bias[0, 0], valid[0, 0]))
+    return out
+
+
+def test_paged_prefill_golden():
+    """SGLang prefill serving ops (interpreted from the wheel): the varlen
+    paged attend K8, the k_bar refresh of a kbar_all_plan, the decode scan
+    window K14, and the varlen router, whose selected sets equal the HF
+    router's (with W <= topm the entmax runs over every candidate in both, so
+    the biases agree too)."""
+    g = golden("paged_prefill")
+    BS, L, topm, budget, dql, tile = (int(x) for x in g["params"])
+    scale = float(g["fparams"][3])
+    ti, tb = g["out_idx"][:, :budget], g["out_bias"][:, :budget]
+    out, _ = O.paged_prefill(g["q"], g["k_cache"], g["v_cache"], ti[None], tb[None], g["block_table"],
+                             g["cu_seqlens_q"], g["context_lens"], scale, L, BS)
+    np.testing.assert_allclose(out, g["out"], rtol=1e-5, atol=1e-5)
+    kb = g["kbar_before"].copy()
+    for pg, tk in zip(g["plan_pages"], g["plan_tok"]):
+        if tk > 0:
+            kb[pg] = O.kbar_summary(g["idx_cache"][pg][None], (np.arange(BS) < tk)[None], g["hc"])[0]
+    np.testing.assert_allclose(kb, g["kbar"], rtol=1e-6, atol=1e-6)
+    lo, hi, fit = O.win_bounds_decode(g["dallow"], g["seq_lens"], len(g["lo"]), g["block_table"].shape[1], BS, L,
+                                      dql, tile)
+    assert (lo == g["lo"]).all() and (hi == g["hi"]).all() and (fit == g["fit"]).all()
+    for n, (topi, bias, valid) in enumerate(_prefill_router_rows(g)):
+        ref = {int(b): float(x) for b, x in zip(g["out_idx"][n], g["out_bias"][n]) if b >= 0}
+        mine = {int(b): float(x) for b, x, v in zip(topi, bias, valid) if v}
+        assert set(ref) == set(mine), n
+        for b in ref:
+            assert abs(ref[b] - mine[b]) < 1e-4, (n, b)
