@@ -567,7 +567,7 @@ def paged_decode(q, k_cache, v_cache, topk_idx, blk_bias, block_table, seq_lens,
 
 
 def paged_prefill(q, k_cache, v_cache, topk_idx, blk_bias, block_table, cu_seqlens_q, prefix_lens, sm_scale,
-                  local_blocks, block_size):
+                  local_blocks, block_size, rows=None):
     """``dash_sparse_attn`` semantics, one program per query token
     (whl:sglang/srt/layers/attention/unlimited_dash_ops/attend_triton.py:88-292,
     523-597): row i of request r (cu_seqlens_q[r] <= i < cu_seqlens_q[r+1])
@@ -575,17 +575,18 @@ def paged_prefill(q, k_cache, v_cache, topk_idx, blk_bias, block_table, cu_seqle
     selected blocks below the window start (pos <= p - LW), biased; local
     keys [p - LW + 1, p], unbiased.  The reference walks the first
     count(slot >= 0) slots, so valid slots must come first (as its router
-    packs them).  Returns (out [N,H,D] fp32, lse [N,H] natural log)."""
+    packs them).  rows: compute only these rows (the others stay 0 / -inf).
+    Returns (out [N,H,D] fp32, lse [N,H] natural log)."""
     cu = np.asarray(cu_seqlens_q, np.int64)
     N = int(cu[-1])
     req = np.searchsorted(cu, np.arange(N), side="right") - 1
     pos = np.asarray(prefix_lens, np.int64)[req] + np.arange(N) - cu[req]
     return _paged_rows(q, k_cache, v_cache, topk_idx, blk_bias, block_table, req, pos, sm_scale, local_blocks,
-                       block_size)
+                       block_size, rows)
 
 
 def _paged_rows(q, k_cache, v_cache, topk_idx, blk_bias, block_table, req, pos_of_row, sm_scale, local_blocks,
-                block_size):
+                block_size, rows=None):
     """One softmax per (row, head) over the row's remote keys (selected
     blocks, pos <= p and pos < p - LW + 1, slot bias) and window keys."""
     N, H, D = q.shape
@@ -594,7 +595,7 @@ def _paged_rows(q, k_cache, v_cache, topk_idx, blk_bias, block_table, req, pos_o
     lw = local_blocks * block_size
     out = np.zeros((N, H, v_cache.shape[-1]), F32)
     lse = np.full((N, H), -np.inf, F32)
-    for n in range(N):
+    for n in (range(N) if rows is None else rows):
         r = int(req[n])
         p = int(pos_of_row[n])
         lws = max(0, p - lw + 1)

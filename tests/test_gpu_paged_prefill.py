@@ -146,5 +146,5 @@ def test_paged_prefill_long_prefix_vs_oracle(cuda):
             continue
         for b in ref:
             assert abs(ref[b] - mine[b]) < 1e-4, (n, b)
-    ref_o, _ = O.paged_prefill(q, kc, vc, oi[None], ob[None], bt, cu, ctx, 1 / math.sqrt(D), L, BS)
+    ref_o, _ = O.paged_prefill(q, kc, vc, oi[None], ob[None], bt, cu, ctx, 1 / math.sqrt(D), L, BS, rows=rows)
     np.testing.assert_allclose(out.float().cpu().numpy()[rows], ref_o[rows], rtol=1e-2, atol=2e-2)
