@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode: skip the cfg2 / cfg4 / cfg5 results that ride along in the line")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx", "pagegate", "rope"],
                     help="decode = cfg3 (default, the headline); prefill = cfg2; train = cfg4 fwd+bwd; "
                          "route = the cfg3 router alone (k_bar cache + block table, no KV; for profiling); "
@@ -343,45 +345,62 @@ def timed_graph(fn, steps, warmup, flush, use_graph=True):
 
 # ---------------------------------------------------------------------------
 def cpu_decode_sample(S, budget_s=20.0, max_req=4):
-    """The reference's CPU decode step (oracle port of _block_scores_infer ->
-    _infer_route_select -> _decode_attend, dense over the whole cache) on a
-    bounded sample of the workload's requests.  Returns (GB/s, cores, sample,
-    seconds per request list)."""
-    from oracle import srswa_oracle as O
-    rng = np.random.default_rng(2)
-    done, t_all, bytes_all, lens = 0, 0.0, 0, []
-    for s in S[:max_req]:
-        k = rng.standard_normal((HKV, s, D), dtype=np.float32)
-        v = rng.standard_normal((HKV, s, D), dtype=np.float32)
-        ik = rng.standard_normal((1, s, DI), dtype=np.float32)
-        q = rng.standard_normal((H, D), dtype=np.float32)
-        iq = rng.standard_normal((1, 1, DI), dtype=np.float32)
-        p = s - 1
+    """The reference's CPU decode step (_block_scores_infer ->
+    _infer_route_select -> _decode_attend: summaries of every block, scores,
+    selection, dense masked attend over the whole cache; fp32 torch on all
+    host cores, oracle/torch_cpu.py) on a bounded sample of the workload's
+    requests.  Returns (GB/s of the step's algorithmic bytes, host info,
+    sample, seconds)."""
+    from oracle import torch_cpu as TC
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(2)
+    t_all, bytes_all, lens = 0.0, 0, []
+    for s_ in S[:max_req]:
+        q = torch.randn(1, H, 1, D, generator=g)
+        k = torch.randn(1, HKV, s_, D, generator=g)
+        v = torch.randn(1, HKV, s_, D, generator=g)
+        iq = torch.randn(1, 1, DI, generator=g)
+        ik = torch.randn(1, s_, DI, generator=g)
+        pos = torch.tensor([[s_ - 1]])
+        TC.decode_step(q, k, v, iq, ik, torch.zeros(DI), pos, BS, L, K, M, IDX_SCALE, FLOOR, SIGMA, SM_SCALE)
         t0 = time.perf_counter()
-        nblk = math.ceil(s / BS)
-        kb, cv = O.kbar_contiguous(ik, np.zeros(DI, np.float32), BS, nblk)
-        sc = O.block_scores_headcls(iq, kb, cv, np.array([[p]]), BS, L)
-        topi, bias, valid = O.infer_route_select(sc, None, IDX_SCALE, FLOOR, SIGMA, K, M)
-        O.decode_attend_one(q, k, v, topi[0, 0], bias[0, 0], valid[0, 0], p, BS, L * BS, SM_SCALE)
+        _, topi, valid = TC.decode_step(q, k, v, iq, ik, torch.zeros(DI), pos, BS, L, K, M, IDX_SCALE, FLOOR,
+                                        SIGMA, SM_SCALE)
         t_all += time.perf_counter() - t0
-        sel = np.where(valid[0, 0], topi[0, 0], -1)[None].astype(np.int32)
-        a, r_, kk = step_bytes([s], torch.from_numpy(sel))
+        sel = torch.where(valid[0, 0], topi[0, 0], torch.full_like(topi[0, 0], -1))[None].to(torch.int32)
+        a, r_, kk = step_bytes([s_], sel)
         bytes_all += a + r_ + kk
-        lens.append(s)
-        done += 1
+        lens.append(s_)
         if t_all > budget_s:
             break
-    cores = os.cpu_count()
-    return bytes_all / t_all / 1e9, cores, lens, t_all
+    return bytes_all / t_all / 1e9, TC.host_info(), lens, t_all
+
+
+def cpu_cfg1_ms(reps=20):
+    """BASELINE config 1 on the host: one fp32 decode step, B=1, S=8192
+    (32 pages x 256 tokens), seed 0, through the same CPU path."""
+    from oracle import torch_cpu as TC
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    S0 = 8192
+    q, k, v = (torch.randn(1, H, n, D, generator=g) for n in (1, S0, S0))
+    iq, ik = torch.randn(1, 1, DI, generator=g), torch.randn(1, S0, DI, generator=g)
+    pos = torch.tensor([[S0 - 1]])
+    args = (q, k, v, iq, ik, torch.zeros(DI), pos, BS, L, K, M, IDX_SCALE, FLOOR, SIGMA, SM_SCALE)
+    TC.decode_step(*args)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        TC.decode_step(*args)
+    return (time.perf_counter() - t0) / reps * 1e3
 
 
 # ---------------------------------------------------------------------------
-def attend_flops(T, LW, sel, BS):
+def attend_flops(T, LW, sel, BS, t0=0):
     """Exact forward flops of the gather-attention: 4*D per (query, head,
     attended key); attended keys = window + unique remote keys of the
-    selection (sel [B, T, K] int, -1 unused)."""
+    selection (sel [B, T - t0, K] int for queries t0 .. T-1, -1 unused)."""
     B = sel.shape[0]
-    t = torch.arange(T, device=sel.device)
+    t = torch.arange(t0, T, device=sel.device)
     ls = (t - LW + 1).clamp(min=0)
     n = (t - ls + 1).to(torch.float64).sum() * B
     s = sel.clone()
@@ -394,60 +413,201 @@ def attend_flops(T, LW, sel, BS):
     return float(n) * 4 * D * H
 
 
-def main_dense(args):
-    """cfg2 prefill (route + gather fwd) or cfg4 training (route + gather fwd
-    + bwd), 1 GPU per rank, batch sharded across ranks (weak: per-rank work
-    fixed)."""
+def init_dist(dev, world):
     import torch.distributed as dist
-    from srswa import dash_infer, ops  # noqa: F401
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+
+def rank_env():
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def bf16_peak():
+    try:
+        pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(pk["bf16_tflops"]) * 1e12, "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        return 1.59e15, "fallback 1.59 PFLOP/s"
+
+
+def dense_setup(train, B, T, rank, dev):
+    """cfg2 / cfg4 inputs as the benchmark draws them (seeded N(0,1) * scale,
+    bf16) and the router's selection of them (head_cls = 0)."""
+    from srswa import dash_infer
+    Kk, LW, seed, sc = (16, 1024, 3, 1.0) if train else (8, 512, 1, 0.5)
+    g = torch.Generator(device=dev).manual_seed(seed * 100 + rank)
+    mk = lambda *shape: (torch.randn(*shape, device=dev, generator=g) * sc).to(torch.bfloat16)  # noqa: E731
+    x = dict(q=mk(B, H, T, D), k=mk(B, HKV, T, D), v=mk(B, HKV, T, D))
+    x["iq"] = mk(B, T, DI).float()
+    x["ik"] = mk(B, T, DI)
+    # upstream gradient in the memory layout a model's o_proj hands back
+    # (attn_output.transpose(1, 2).reshape(B, T, H * D) -> [B, T, H, D] memory)
+    x["do"] = (torch.randn(B, T, H, D, device=dev, generator=g).to(torch.bfloat16).transpose(1, 2)
+               if train else None)
+    x["router"] = type("R", (), dict(block_size=BS, local_blocks=LW // BS, local_window=LW,
+                                     head_cls=torch.zeros(DI, device=dev), stage0="head_cls"))()
+    x["pos"] = torch.arange(T, device=dev)[None].expand(B, T).contiguous()
+    x["p"] = dict(idx_scale=IDX_SCALE, floor=FLOOR, sigma=SIGMA, K=Kk, topm=M)
+    x.update(K=Kk, LW=LW, nblk=T // BS, dash_infer=dash_infer)
+    return x
+
+
+def dense_step(x, train, q=None, k=None, v=None, iq=None, ik=None, do=None, outs=None):
+    """One cfg2 / cfg4 step through the public drop-ins: route
+    (_block_scores_infer + _infer_route_select fused) -> triton_gather_attention_e2e
+    forward (and backward with autograd for cfg4)."""
     from srswa.sparse_gather_e2e import triton_gather_attention_e2e
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    q = x["q"] if q is None else q
+    k = x["k"] if k is None else k
+    v = x["v"] if v is None else v
+    iq = x["iq"] if iq is None else iq
+    ik = x["ik"] if ik is None else ik
+    topi, bias, valid = x["dash_infer"].route(x["router"], iq, ik, x["pos"], x["nblk"], None, x["p"])
+    sel = torch.where(valid, topi, torch.full_like(topi, -1))[:, None]
+    b = (bias * valid).float()
+    if train:
+        qq, kk, vv, bb = (t.detach().requires_grad_(True) for t in (q, k, v, b))
+        o = triton_gather_attention_e2e(qq, kk, vv, sel, bb, x["pos"], None, BS, SM_SCALE, x["LW"])
+        o.backward(x["do"] if do is None else do)
+        res = (o, qq.grad, kk.grad, vv.grad)
+    else:
+        o = triton_gather_attention_e2e(q, k, v, sel, b, x["pos"], None, BS, SM_SCALE, x["LW"])
+        res = (o,)
+    x["sel"], x["b"] = sel, b
+    if outs is not None:
+        for dst, src in zip(outs, res):
+            dst.copy_(src, non_blocking=True)
+    return res
+
+
+def dense_check(x, train, res):
+    """Correctness of the timed workload, outside the timed region: a few
+    query rows of the first and last batch element (o, and dQ for cfg4)
+    against the CPU oracle on the same bf16 values and selection."""
+    from oracle import srswa_oracle as O
+    T, LW = x["q"].shape[2], x["LW"]
+    rows = np.array([0, BS, LW, T // 2 + 7, T - 1])
+    err, worst = 0.0, 0.0
+    for bi in (0, x["q"].shape[0] - 1):
+        qb, kb, vb = (t[bi].transpose(0, 1).float().cpu().numpy() for t in (x["q"], x["k"], x["v"]))
+        sel = x["sel"][bi, 0].cpu().numpy()
+        bias = x["b"][bi].cpu().numpy()
+        seg = np.zeros(T, np.int64)
+        o_r, _ = O.gather_rows_fwd(qb, kb, vb, sel, seg, rows, BS, SM_SCALE, LW, bias)
+        got = res[0][bi][:, rows].transpose(0, 1).float().cpu().numpy()
+        d = np.abs(got - o_r)
+        err = max(err, float(d.max()))
+        worst = max(worst, float((d / (2e-2 + 1e-2 * np.abs(o_r))).max()))
+        if train:
+            dob = x["do"][bi].transpose(0, 1).float().cpu().numpy()
+            dq_r, _ = O.gather_rows_bwd(qb, kb, vb, dob, sel, seg, rows, BS, SM_SCALE, LW, bias)
+            got = res[1][bi][:, rows].transpose(0, 1).float().cpu().numpy()
+            d = np.abs(got - dq_r)
+            err = max(err, float(d.max()))
+            worst = max(worst, float((d / (2e-2 + 1e-2 * np.abs(dq_r))).max()))
+    ok = worst <= 1.0
+    if not ok:
+        raise SystemExit(f"bench correctness check failed: max abs err {err} (tolerance ratio {worst})")
+    return {"rows": int(len(rows) * 2), "outputs": "o, dq" if train else "o", "max_abs_err": err,
+            "tolerance": "2e-2 abs + 1e-2 rel vs the CPU oracle", "ok": ok}
+
+
+def dense_cpu_baseline(x, train, budget_rows):
+    """The reference's CPU path on a sub-slice of batch element 0: routing of
+    the last `budget_rows` queries (block summaries of every block, scores,
+    selection) and DashAttention._forward_dense for them, fp32 on the host
+    cores (oracle/torch_cpu.py restates the reference's torch ops); cfg4 adds
+    the autograd backward.  Reported as TFLOP/s of the same attended work."""
+    from oracle import torch_cpu as TC
+    torch.set_num_threads(os.cpu_count() or 1)
+    T, LW, Kk = x["q"].shape[2], x["LW"], x["K"]
+    q0 = T - budget_rows
+    q, k, v = (t[:1].float().cpu() for t in (x["q"], x["k"], x["v"]))
+    iq, ik = x["iq"][:1].float().cpu(), x["ik"][:1].float().cpu()
+    pos = torch.arange(T)[None]
+    t0 = time.perf_counter()
+    with torch.set_grad_enabled(train):
+        sc = TC.block_scores(iq[:, q0:], ik, torch.zeros(DI), pos[:, q0:], BS, LW // BS)
+        topi, bias, valid = TC.route_select(sc, None, IDX_SCALE, FLOOR, SIGMA, Kk, M)
+        full = lambda t_, fill: torch.cat([torch.full((1, q0, t_.shape[-1]), fill, dtype=t_.dtype), t_], 1)  # noqa
+        topi, bias, valid = full(topi, 0), full(bias, 0.0), full(valid, False)
+        if train:
+            q, k, v, bias = (t_.requires_grad_(True) for t_ in (q, k, v, bias))
+        o = TC.dense_forward(q, k, v, topi, bias, valid, BS, LW, SM_SCALE, q_start=q0)
+        if train:
+            o.backward(torch.ones_like(o))
+    dt = time.perf_counter() - t0
+    sel = torch.where(valid[:, q0:], topi[:, q0:], torch.full_like(topi[:, q0:], -1))
+    fl = attend_flops(T, LW, sel, BS, t0=q0) * (3.5 if train else 1.0)
+    info = __import__("oracle.torch_cpu", fromlist=["host_info"]).host_info()
+    return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": info["threads"], "kind": "port",
+            "cpu_model": info["cpu_model"], "seconds": dt,
+            "sample": f"batch element 0, last {budget_rows} of {T} queries (all {T} keys): routing + "
+                      f"_forward_dense{' + autograd backward' if train else ''}, fp32 torch on the host cores"}
+
+
+def dense_e2e(x, train, steps, warmup):
+    """The step through the public API from pinned host buffers: H2D of the
+    step's inputs (q, k, v, idx_q, idx_k; dO for cfg4), the step, D2H of its
+    results (o; dq, dk, dv for cfg4), every step."""
+    dev = x["q"].device
+    names = ["q", "k", "v", "iq", "ik"] + (["do"] if train else [])
+    # dO travels in the memory layout it has on the device ([B, T, H, D])
+    src = {n: (x[n].transpose(1, 2) if n == "do" else x[n]) for n in names}
+    host = {n: torch.empty(src[n].shape, dtype=src[n].dtype).pin_memory() for n in names}
+    for n in names:
+        host[n].copy_(src[n])
+    devb = {n: torch.empty(src[n].shape, dtype=src[n].dtype, device=dev) for n in names}
+    out_shapes = [x["q"].shape] + ([x["q"].shape, x["k"].shape, x["v"].shape] if train else [])
+    houts = [torch.empty(s_, dtype=torch.bfloat16).pin_memory() for s_ in out_shapes]
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = sum(t.numel() * t.element_size() for t in houts)
+
+    def step():
+        for n in names:
+            devb[n].copy_(host[n], non_blocking=True)
+        res = dense_step(x, train, q=devb["q"], k=devb["k"], v=devb["v"], iq=devb["iq"], ik=devb["ik"],
+                         do=devb["do"].transpose(1, 2) if train else None)
+        for dst, src in zip(houts, res):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(max(warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, h2d, d2h
+
+
+def dense_measure(args, train, extras=True):
+    """cfg2 prefill (route + gather fwd) or cfg4 training (route + gather fwd
+    + bwd), one GPU per rank, batch sharded across ranks (weak: per-rank work
+    fixed).  Returns this workload's result dict (rank 0) or None."""
+    import torch.distributed as dist
+    world, rank, local = rank_env()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    train = args.workload == "train"
-    B, T, Kk, LW, seed, sc = (8, 32768, 16, 1024, 3, 1.0) if train else (4, 16384, 8, 512, 1, 0.5)
+    init_dist(dev, world)
+    B, T = (8, 32768) if train else (4, 16384)
     if args.batch:
         B = args.batch
     if args.seq:
         T = args.seq
     Bl = max(1, B // world)
-    g = torch.Generator(device=dev).manual_seed(seed * 100 + rank)
-    mk = lambda *shape: (torch.randn(*shape, device=dev, generator=g) * sc).to(torch.bfloat16)  # noqa: E731
-    q, k, v = mk(Bl, H, T, D), mk(Bl, HKV, T, D), mk(Bl, HKV, T, D)
-    iq = mk(Bl, T, DI).float()
-    ik = mk(Bl, T, DI)
-    nblk = T // BS
-    router = type("R", (), dict(block_size=BS, local_blocks=LW // BS, local_window=LW,
-                                head_cls=torch.zeros(DI, device=dev), stage0="head_cls"))()
-    pos = torch.arange(T, device=dev)[None].expand(Bl, T).contiguous()
-    p = dict(idx_scale=IDX_SCALE, floor=FLOOR, sigma=SIGMA, K=Kk, topm=M)
-    # upstream gradient in the memory layout a model's o_proj hands back
-    # (attn_output.transpose(1, 2).reshape(B, T, H * D) -> [B, T, H, D] memory)
-    do = (torch.randn(Bl, T, H, D, device=dev, generator=g).to(torch.bfloat16).transpose(1, 2)
-          if train else None)
-    state = {}
-
-    def step():
-        topi, bias, valid = dash_infer.route(router, iq, ik, pos, nblk, None, p)
-        sel = torch.where(valid, topi, torch.full_like(topi, -1))[:, None]
-        b = (bias * valid).float()
-        if train:
-            qq, kk, vv, bb = (x.detach().requires_grad_(True) for x in (q, k, v, b))
-            o = triton_gather_attention_e2e(qq, kk, vv, sel, bb, pos, None, BS, SM_SCALE, LW)
-            o.backward(do)
-        else:
-            o = triton_gather_attention_e2e(q, k, v, sel, b, pos, None, BS, SM_SCALE, LW)
-        state["sel"] = sel
-
+    x = dense_setup(train, Bl, T, rank, dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    for _ in range(max(args.warmup, 1)):
-        step()
+    for _ in range(max(args.warmup, 3)):
+        res = dense_step(x, train)
     torch.cuda.synchronize()
-    fl = attend_flops(T, LW, state["sel"][:, 0], BS) * (3.5 if train else 1.0)  # fwd 4, bwd 10 per D
+    check = dense_check(x, train, res) if (extras and rank == 0) else None
+    del res
+    fl = attend_flops(T, x["LW"], x["sel"][:, 0], BS) * (3.5 if train else 1.0)  # fwd 4, bwd 10 per D
     if world > 1:
         dist.barrier()
     clocks = Clocks(local)
@@ -456,38 +616,64 @@ def main_dense(args):
     for a_, b_ in ev:
         flush.zero_()
         a_.record()
-        step()
+        dense_step(x, train)
         b_.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = sum(a_.elapsed_time(b_) for a_, b_ in ev) / args.steps
-    vec = torch.tensor([ms], device=dev, dtype=torch.float64)
-    fl_t = torch.tensor([fl], device=dev, dtype=torch.float64)
+    e2e_ms, h2d, d2h = dense_e2e(x, train, args.steps, args.warmup) if extras else (0.0, 0, 0)
+    vec = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+    tot = torch.tensor([fl, h2d, d2h], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(vec, op=dist.ReduceOp.MAX)
-        dist.all_reduce(fl_t, op=dist.ReduceOp.SUM)
-    ms, fl_all = vec.item(), fl_t.item()
-    try:
-        pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        peak = float(pk["bf16_tflops"]) * 1e12
-        src = "measured"
-    except Exception:
-        peak, src = 1.59e15, "fallback"
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    ms, e2e_ms = vec.tolist()
+    fl_all, h2d, d2h = tot.tolist()
+    cpu = None
+    if extras and rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = dense_cpu_baseline(x, train, 256 if train else 2048)
+    peak, src = bf16_peak()
+    del x
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    out = {"value": fl_all / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "n_gpus": world,
+           "steps": args.steps, "scaling": "weak", "dtype": "bf16",
+           "config": {"workload": ("cfg4 train: route + gather-attention e2e fwd+bwd" if train else
+                                   "cfg2 prefill: route + gather-attention fwd"),
+                      "global_batch": Bl * world, "seq_len": T, "K": x_k(train), "LW": 1024 if train else 512,
+                      "parallelism": f"batch/dp{world}", "l2": "flushed before every timed step",
+                      "flops_per_step": fl_all,
+                      **({"dO_layout": "[B,T,H,D] memory (as from o_proj)"} if train else {})},
+           "roofline": {"bound": "tensor", "achieved": fl_all / world / (ms * 1e-3) / 1e12, "peak": peak / 1e12,
+                        "unit": "TFLOP/s", "frac": fl_all / world / (ms * 1e-3) / peak, "peak_source": src,
+                        "traffic": None},
+           "clocks": clk}
+    if extras:
+        out["check"] = check
+        out["cpu_baseline"] = cpu
+        out["e2e"] = {"value": fl_all / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                      "how": "pinned H2D of q, k, v, idx_q, idx_k" + (", dO" if train else "") +
+                             " -> route + triton_gather_attention_e2e" + (" fwd + bwd" if train else "") +
+                             " -> D2H of o" + (", dq, dk, dv" if train else "") + ", every step",
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    return out
+
+
+def x_k(train):
+    return 16 if train else 8
+
+
+def main_dense(args):
+    world, rank, _ = rank_env()
+    r = dense_measure(args, args.workload == "train")
     if rank == 0:
-        line = {"metric": METRIC, "value": fl_all / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic seeded N(0,1)",
-                "config": {"workload": ("cfg4 train: route + gather-attention e2e fwd+bwd" if train else
-                                        "cfg2 prefill: route + gather-attention fwd"),
-                           "global_batch": Bl * world, "seq_len": T, "K": Kk, "LW": LW,
-                           "parallelism": f"batch/dp{world}", "l2": "flushed before every timed step",
-                           **({"dO_layout": "[B,T,H,D] memory (as from o_proj)"} if train else {})},
-                "roofline": {"bound": "tensor", "achieved": fl_all / world / (ms * 1e-3) / 1e12,
-                             "peak": peak / 1e12, "unit": "TFLOP/s",
-                             "frac": fl_all / world / (ms * 1e-3) / peak, "peak_source": src, "traffic": None},
-                "clocks": clk}
+        line = {"metric": METRIC, **r, "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
+                "data": "synthetic seeded N(0,1)"}
+        line["n_gpus"] = world
         print(json.dumps(line), flush=True)
     if world > 1:
+        import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
     return 0
@@ -653,6 +839,19 @@ def main_rope(args):
 
 
 def main_longctx(args):
+    world, rank, _ = rank_env()
+    r = longctx_measure(args)
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, **r, "warmup": max(args.warmup, 3), "higher_is_better": True,
+                          "vs_baseline": None, "data": "synthetic seeded N(0,1) (pooled)"}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def longctx_measure(args):
     """cfg5 attention share: one decode step of a 1M-token sequence through
     the SR-SWA attention of 12 layers, split-KV over the ranks (rank g owns a
     contiguous block range of every layer's K/V, index keys and k_bar; the
@@ -664,14 +863,11 @@ def main_longctx(args):
     import torch.distributed as dist
     from srswa import ops
     from srswa.split_kv import SplitKVDecode
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    world, rank, local = rank_env()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    S0 = args.seq or 1_048_576
+    init_dist(dev, world)
+    S0 = (args.seq if args.workload == "longctx" and args.seq else 0) or 1_048_576
     nblk_filled = S0 // BS
     nblk_total = nblk_filled + 4                     # room for 256 decoded tokens
     p = S0 - 1                                       # the step decodes the last position
@@ -750,24 +946,20 @@ def main_longctx(args):
         dist.all_reduce(b, op=dist.ReduceOp.SUM)
     ms, byts = t.item(), b.item()
     hbm = peaks()[0]
-    if rank == 0:
-        line = {"metric": METRIC, "value": byts / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world,
-                "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms, "us_per_step": ms * 1e3,
-                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic seeded N(0,1) (pooled)",
-                "config": {"workload": "cfg5 attention share: 12-layer split-KV decode, one 1M-token sequence",
-                           "seq_len": S0, "layers": nl, "K": K, "LW": L * BS, "parallelism": f"split-kv{world}",
-                           "l2": "flushed before every timed step", "graph": not args.no_graph},
-                "roofline": {"bound": "latency", "achieved": byts / (ms * 1e-3) / 1e9, "peak": hbm * world,
-                             "unit": "GB/s", "frac": byts / (ms * 1e-3) / 1e9 / (hbm * world), "traffic": None},
-                "clocks": clk}
-        print(json.dumps(line), flush=True)
     if g is not None:
         del g
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    del layers, decs, outs
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    return {"value": byts / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "ms_per_step": ms, "us_per_step": ms * 1e3, "scaling": "strong", "dtype": "bf16",
+            "config": {"workload": "cfg5 attention share: 12-layer split-KV decode, one 1M-token sequence",
+                       "seq_len": S0, "layers": nl, "K": K, "LW": L * BS, "parallelism": f"split-kv{world}",
+                       "l2": "flushed before every timed step", "graph": not args.no_graph},
+            "roofline": {"bound": "latency", "achieved": byts / (ms * 1e-3) / 1e9, "peak": hbm * world,
+                         "unit": "GB/s", "frac": byts / (ms * 1e-3) / 1e9 / (hbm * world), "traffic": None},
+            "clocks": clk}
 
 
 def main():
@@ -790,16 +982,16 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        # the reference's own CPU implementation (oracle port), one request per step
-        from oracle import srswa_oracle as O  # noqa: F401
+        # the reference's CPU path (its torch ops restated), one request per step
         order = S[: max(1, args.steps + args.warmup)]
         per, byts = [], []
         for i in range(args.warmup + args.steps):
-            gbs, cores, lens, t = cpu_decode_sample([order[i % len(order)]], budget_s=1e9, max_req=1)
+            gbs, info, lens, t = cpu_decode_sample([order[i % len(order)]], budget_s=1e9, max_req=1)
             if i >= args.warmup:
                 per.append(t)
                 byts.append(gbs * t * 1e9)
         val = sum(byts) / sum(per) / 1e9
+        cores = info["threads"]
         line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(per) / len(per),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -808,7 +1000,9 @@ def main():
                                        "_infer_route_select -> _decode_attend, dense over the cache)",
                            "requests_per_step": 1, "parallelism": "host cores"},
                 "cpu_baseline": {"value": val, "unit": "GB/s", "cores": cores, "kind": "port",
-                                 "sample": f"{args.steps} request decode steps, S from the cfg3 draw"},
+                                 "cpu_model": info["cpu_model"],
+                                 "sample": f"{args.steps} request decode steps, S from the cfg3 draw: "
+                                           "the reference's fp32 torch CPU path (oracle/torch_cpu.py)"},
                 "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
@@ -817,8 +1011,7 @@ def main():
     from srswa import ops  # noqa: F401  (fails loudly without libsrswa.so)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    init_dist(dev, world)
     parts = shard(S, world)
     mine = parts[rank]
     S_local = [S[i] for i in mine]
@@ -881,10 +1074,14 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, cores, lens, t = cpu_decode_sample(S)
-        cpu = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
-               "sample": f"{len(lens)} of {len(S)} requests (S={lens}): full HF CPU decode step "
-                         f"(k_bar of every block, scores, top-M entmax, dense attend), {t:.1f} s"}
+        gbs, info, lens, t = cpu_decode_sample(S)
+        cfg1_ms = cpu_cfg1_ms()
+        cpu = {"value": gbs, "unit": "GB/s", "cores": info["threads"], "kind": "port",
+               "cpu_model": info["cpu_model"], "logical_cpus": info["logical_cpus"],
+               "sample": f"{len(lens)} of {len(S)} requests (S={lens}): the HF CPU decode step in fp32 torch "
+                         f"(k_bar of every block, scores, top-M entmax, dense attend over the cache), {t:.1f} s",
+               "cfg1_ms_per_step": cfg1_ms,
+               "cfg1": "BASELINE config 1: one decode step at S=8192 (B=1, H=10, D=128, K=8, LW=512), fp32"}
 
     peak, src = peaks()
     att_gbs = (a_b / (att_ms * 1e-3)) / 1e9     # this rank's attend kernel
@@ -921,6 +1118,19 @@ def main():
             "gpu_launches": int(launches_all) * args.steps,   # all ranks, counted on one profiled step
             "clocks": clk,
         }
+    # the metric's other half and the long-context config, measured after the
+    # headline (the decode state is freed first): cfg2 prefill and cfg4
+    # training TFLOP/s against the bf16 peak, the cfg5 split-KV step
+    st.clear()
+    del st
+    torch.cuda.empty_cache()
+    extras = {}
+    if not args.no_extras:
+        extras["prefill"] = dense_measure(args, False)
+        extras["train"] = dense_measure(args, True)
+        extras["longctx"] = longctx_measure(args)
+    if rank == 0:
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

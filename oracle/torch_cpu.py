@@ -131,12 +131,13 @@ def decode_step(q, k_all, v_all, idx_q, idx_k, head_cls, q_pos, block_size, loca
                              scale), topi, valid
 
 
-def dense_forward(q, k, v, topi, bias, valid, block_size, local_window, scale, q_chunk=2048, q_rows=None):
+def dense_forward(q, k, v, topi, bias, valid, block_size, local_window, scale, q_chunk=2048, q_rows=None,
+                  q_start=0):
     """DashAttention._forward_dense (dash_attention.py:1230-1260): per query
     chunk, the [B,1,Lq,S] additive mask (0 on the window, the slot bias on
     selected remote blocks, MASK_NEG elsewhere) and one SDPA; q [B,H,T,D],
-    k / v [B,H,S,D]; topi / bias / valid [B,T,K].  q_rows: compute only
-    query rows [0, q_rows) (a timed sub-slice; keys stay [0, S))."""
+    k / v [B,H,S,D]; topi / bias / valid [B,T,K].  q_start / q_rows: compute
+    only query rows [q_start, q_rows) (a timed sub-slice; keys stay [0, S))."""
     B, H, T, D = q.shape
     S = k.shape[2]
     nblk = -(-S // block_size)
@@ -146,7 +147,7 @@ def dense_forward(q, k, v, topi, bias, valid, block_size, local_window, scale, q
     logp = torch.full((B, bias.shape[1], nblk), MASK_NEG, dtype=bias.dtype).scatter(-1, topi, src)
     n = T if q_rows is None else min(T, int(q_rows))
     outs = []
-    for qs in range(0, n, q_chunk):
+    for qs in range(int(q_start), n, q_chunk):
         qe = min(qs + q_chunk, n)
         qi = torch.arange(qs, qe)
         base = logp[:, qs:qe].index_select(-1, kb)[:, None]
