@@ -65,6 +65,8 @@ def parse():
                          "pagegate = PageGate candidate masks of a cfg2-shaped prefill; "
                          "rope = page2d RoPE coordinates + fused rotary of a cfg2-shaped prefill")
     ap.add_argument("--layers", type=int, default=12, help="longctx: decoder layers")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="longctx with N > 1: peer-memory exchange (default) or NCCL all-gathers")
     ap.add_argument("--batch", type=int, default=0, help="prefill/train batch override (smaller cases)")
     ap.add_argument("--seq", type=int, default=0, help="prefill/train sequence override")
     return ap.parse_args()
@@ -874,12 +876,16 @@ def longctx_measure(args):
     nl = args.layers
     gen = torch.Generator().manual_seed(4 * 100 + rank)
     decs, layers = [], []
+    backend = None
+    if world > 1 and args.exchange == "p2p":
+        from srswa.split_kv import PeerBackend
+        backend = PeerBackend(rows=1, topm=M, heads=H, head_dim=D)   # one for all layers
     pool = torch.randn(64 << 20, generator=gen).to(torch.bfloat16).to(dev)
     hc = torch.zeros(DI, device=dev)
     for _ in range(nl):
         dec = SplitKVDecode(nblk_total=nblk_total, nblk_filled=nblk_filled, block_size=BS, local_blocks=L, topk=K,
                             topm=M, idx_scale=IDX_SCALE, floor=FLOOR, sigma=SIGMA, sm_scale=SM_SCALE, rank=rank,
-                            world=world)
+                            world=world, backend=backend)
         lo, hi = dec.plan.lo, dec.plan.hi
         nloc = hi - lo
         kc = torch.empty(nloc, BS, HKV, D, device=dev, dtype=torch.bfloat16)
@@ -948,6 +954,9 @@ def longctx_measure(args):
     hbm = peaks()[0]
     if g is not None:
         del g
+    if backend is not None:
+        backend.check()
+        backend.close()            # collective: every rank
     del layers, decs, outs
     torch.cuda.empty_cache()
     if rank != 0:
@@ -956,6 +965,8 @@ def longctx_measure(args):
             "ms_per_step": ms, "us_per_step": ms * 1e3, "scaling": "strong", "dtype": "bf16",
             "config": {"workload": "cfg5 attention share: 12-layer split-KV decode, one 1M-token sequence",
                        "seq_len": S0, "layers": nl, "K": K, "LW": L * BS, "parallelism": f"split-kv{world}",
+                       "exchange": ("peer-memory push + bounded flag wait (CUDA IPC over NVLink)"
+                                    if backend is not None else ("NCCL all-gather" if world > 1 else "none")),
                        "l2": "flushed before every timed step", "graph": not args.no_graph},
             "roofline": {"bound": "latency", "achieved": byts / (ms * 1e-3) / 1e9, "peak": hbm * world,
                          "unit": "GB/s", "frac": byts / (ms * 1e-3) / 1e9 / (hbm * world), "traffic": None},

@@ -352,6 +352,39 @@ SRSWA_API int srswa_lse_merge(const float* o_parts, const float* lse_parts, int6
                     int64_t H, int64_t D, int64_t s_o_part, int64_t s_l_part, void* out,
                     int out_dtype, float* lse_out, srswa_stream_t stream);
 
+/* --------------------------------------------------- peer exchange ------
+ * All-gather through peer memory for the split-KV decode across the GPUs of
+ * one node (the two exchanges per layer of the reference plan's per-GPU
+ * top-M + LSE combine; no reference counterpart: the reference decodes on
+ * one GPU).  Every rank owns one exchange region of
+ * srswa_peer_region_size(world, slot_bytes) bytes: 256 bytes of flags (one
+ * uint64 epoch per source rank), then one slot_bytes slot per source rank.
+ * Set-up (outside the decode loop; the only entry points here that
+ * allocate): srswa_peer_region_alloc (cudaMalloc + zero fill, so the IPC
+ * handle maps exactly the region), srswa_peer_ipc_handle (64 bytes to send to
+ * the peers), srswa_peer_ipc_open / _close on each peer's handle.
+ * srswa_peer_allgather: regions = device array [world] of the regions' base
+ * addresses as mapped in this process (own region at index rank); copies
+ * nbytes (multiple of 16, <= slot_bytes) from src into slot `rank` of every
+ * region with plain stores, publishes epoch = *counter + 1 in flag `rank` of
+ * each (release, system scope), then waits until every source has published
+ * that epoch in own_region (acquire, bounded: 2 s, then code 501 in *status)
+ * and advances *counter (a device uint64, zero at set-up, one per region,
+ * advanced identically on every rank).  The gathered payloads are then slot
+ * r of own_region.  Two launches, graph-capturable; no NCCL, no TMA, no
+ * multicast.  A rank must not start exchange e+1 on a region before its
+ * consumers of exchange e have read it (stream order gives this when two
+ * regions alternate). */
+SRSWA_API int srswa_peer_region_size(int64_t world, int64_t slot_bytes, size_t* out);
+SRSWA_API int srswa_peer_region_alloc(size_t bytes, void** out);
+SRSWA_API int srswa_peer_region_free(void* region);
+SRSWA_API int srswa_peer_ipc_handle(const void* region, void* handle64);
+SRSWA_API int srswa_peer_ipc_open(const void* handle64, void** mapped);
+SRSWA_API int srswa_peer_ipc_close(void* mapped);
+SRSWA_API int srswa_peer_allgather(const void* src, int64_t nbytes, void* const* regions, const void* own_region,
+                         int64_t slot_bytes, int64_t rank, int64_t world, uint64_t* counter, int* status,
+                         srswa_stream_t stream);
+
 /* ------------------------------------------------------- PageGate ------
  * Page-aware remote candidates.  Token ids are int64 [B, n] rows (row stride
  * s_row); img_id / page_id are the <image> and <PAGE> token ids; per_page is

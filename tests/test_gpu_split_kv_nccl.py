@@ -1,6 +1,9 @@
-"""Split-KV decode over NCCL (2 GPUs; skipped with fewer): each rank keeps
-only its own pages of K/V and its k_bar rows; the combined output of
-SplitKVDecode.step must match one GPU decoding the whole sequence."""
+"""Split-KV decode on 2 GPUs (skipped with fewer): each rank keeps only its
+own pages of K/V and its k_bar rows; the combined output of
+SplitKVDecode.step must match one GPU decoding the whole sequence.  Both
+exchange paths: NCCL all-gathers, and the library's peer-memory exchange
+(PeerBackend: plain stores into the peers' IPC-mapped regions + bounded flag
+waits), eagerly and replayed from a captured CUDA graph.  NVLS is off."""
 
 import datetime
 import math
@@ -28,7 +31,8 @@ def _problem():
     return k, v, kbar, q, iq
 
 
-def _worker(rank, world, port, result_q):
+def _worker(rank, world, port, result_q, exchange="nccl"):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -39,14 +43,36 @@ def _worker(rank, world, port, result_q):
         k, v, kbar, q, iq = _problem()
         S = NBLK * BS - 5
         q_pos = torch.tensor([S - 2, S - 1], device=dev, dtype=torch.int64)
+        backend = None
+        if exchange == "p2p":
+            from srswa.split_kv import PeerBackend
+            backend = PeerBackend(rows=2, topm=RP["topm"], heads=H, head_dim=D)
         dec = SplitKVDecode(nblk_total=NBLK, nblk_filled=NBLK, sm_scale=1 / math.sqrt(D), rank=rank, world=world,
-                            **RP)
+                            backend=backend, **RP)
         lo, hi = dec.plan.lo, dec.plan.hi
         table = torch.zeros(1, NBLK, dtype=torch.int32, device=dev)
         table[0, lo:hi] = torch.arange(hi - lo, dtype=torch.int32, device=dev)
         layer = dict(kbar=kbar[:, lo:hi].contiguous().to(dev), k_cache=k[lo:hi].to(dev), v_cache=v[lo:hi].to(dev),
                      block_table=table)
-        out = dec.step(q.to(dev), iq.to(dev), q_pos, layer, p_range=(S - 2, S - 1), out_dtype=torch.float32)
+        qd, iqd = q.to(dev), iq.to(dev)
+        outs = [dec.step(qd, iqd, q_pos, layer, p_range=(S - 2, S - 1), out_dtype=torch.float32).clone()
+                for _ in range(2)]          # two steps: the exchange epochs advance
+        if exchange == "p2p":
+            # captured once, replayed: the epochs advance on the device
+            s_ = torch.cuda.Stream()
+            s_.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s_):
+                with torch.cuda.graph(graph):
+                    g_out = dec.step(qd, iqd, q_pos, layer, p_range=(S - 2, S - 1), out_dtype=torch.float32)
+            torch.cuda.current_stream().wait_stream(s_)
+            for _ in range(3):
+                graph.replay()
+                outs.append(g_out.clone())
+            torch.cuda.synchronize()
+            dec.backend.check()
+            del graph
+        out = outs[0]
         if rank == 0:
             full_t = torch.arange(NBLK, dtype=torch.int32, device=dev)[None]
             sel = ops.route(iq.to(dev), kbar.to(dev), q_pos=q_pos, rows_per_seq=2, want=("topi32", "bias"), **RP)
@@ -55,8 +81,10 @@ def _worker(rank, world, port, result_q):
                               local_blocks=RP["local_blocks"], sm_scale=1 / math.sqrt(D), out=ref,
                               block_table=full_t, q_pos=q_pos, rows_per_req=2)
             torch.cuda.synchronize()
-            result_q.put(("ok", float((out - ref).abs().max())))
+            result_q.put(("ok", max(float((o - ref).abs().max()) for o in outs)))
         torch.cuda.synchronize()
+        if exchange == "p2p":
+            dec.backend.close()
         dist.barrier()
     except Exception as e:
         result_q.put(("error", repr(e)))
@@ -65,7 +93,8 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
-def test_split_kv_two_gpus_matches_one_gpu():
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_split_kv_two_gpus_matches_one_gpu(exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     with socket.socket() as s:
@@ -73,7 +102,7 @@ def test_split_kv_two_gpus_matches_one_gpu():
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    mp.start_processes(_worker, args=(2, port, q), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(2, port, q, exchange), nprocs=2, join=True, start_method="spawn")
     msg = q.get(timeout=60)
     assert msg[0] == "ok", msg
     assert msg[1] < 1e-5

@@ -127,6 +127,9 @@ class NumpyBackend:
                 lse[n, h] = mx + np.log(e.sum())
         return torch.from_numpy(o), torch.from_numpy(lse)
 
+    def gather_keys(self, keys, world):
+        return self.all_gather(keys, world)
+
     def exchange_partials(self, o_part, lse_part, world):
         return self.all_gather(o_part, world), self.all_gather(lse_part, world)
 

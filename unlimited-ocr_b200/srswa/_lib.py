@@ -90,6 +90,13 @@ _SIGS = {
                                            C.c_size_t, vp]),
     "srswa_decode_allow": (C.c_int, [vp, i64, i64, i64, vp, vp, i64, i64, vp, vp, i64, vp, vp]),
     "srswa_win_bounds_decode": (C.c_int, [vp, i64, i64, vp, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp]),
+    "srswa_peer_region_size": (C.c_int, [i64, i64, C.POINTER(C.c_size_t)]),
+    "srswa_peer_region_alloc": (C.c_int, [C.c_size_t, C.POINTER(vp)]),
+    "srswa_peer_region_free": (C.c_int, [vp]),
+    "srswa_peer_ipc_handle": (C.c_int, [vp, vp]),
+    "srswa_peer_ipc_open": (C.c_int, [vp, C.POINTER(vp)]),
+    "srswa_peer_ipc_close": (C.c_int, [vp]),
+    "srswa_peer_allgather": (C.c_int, [vp, i64, vp, vp, i64, i64, i64, vp, vp, vp]),
     "srswa_rope2d_pos_workspace_size": (C.c_size_t, [i64, i64]),
     "srswa_rope2d_pos": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, vp, vp, vp, i64, vp, vp, C.c_size_t,
                                    vp]),

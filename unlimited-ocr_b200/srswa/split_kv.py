@@ -93,8 +93,9 @@ class CudaBackend:
                out_dtype=torch.float32):
         N, H, D = q.shape
         if out_dtype == torch.float32:
-            # partial o and its lse packed in one buffer: one all-gather moves both
-            buf = torch.empty(N * H * D + N * H, device=q.device, dtype=torch.float32)
+            # partial o and its lse packed in one buffer (padded to 16 bytes):
+            # one all-gather moves both
+            buf = torch.empty(-(-(N * H * D + N * H) // 4) * 4, device=q.device, dtype=torch.float32)
             out, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:].view(N, H)
         else:
             out, lse = torch.empty(q.shape, device=q.device, dtype=out_dtype), None
@@ -103,12 +104,20 @@ class CudaBackend:
                                       block_table=layer["block_table"], q_pos=q_pos, rows_per_req=N,
                                       lse=True, skip_local=skip_local, lse_out=lse)
 
+    def gather_keys(self, keys, world):
+        """All-gather of the router keys [N, M] -> [world, N, M]."""
+        return self.all_gather(keys, world)
+
     def exchange_partials(self, o_part, lse_part, world):
         """All-gather of the packed partials -> ([world,N,H,D], [world,N,H]) views."""
         N, H, D = o_part.shape
-        buf = torch.as_strided(o_part, (N * H * D + N * H,), (1,))   # the packed buffer of attend()
-        g = self.all_gather(buf, world)
-        return g[:, :N * H * D].view(world, N, H, D), g[:, N * H * D:].view(world, N, H)
+        n = N * H * D + N * H
+        buf = torch.as_strided(o_part, (-(-n // 4) * 4,), (1,))   # the packed buffer of attend()
+        g = self.gather_partials(buf, world)
+        return g[:, :N * H * D].view(world, N, H, D), g[:, N * H * D:n].view(world, N, H)
+
+    def gather_partials(self, buf, world):
+        return self.all_gather(buf, world)
 
     def lse_merge(self, o_parts, lse_parts, out_dtype):
         return self.ops.lse_merge(o_parts, lse_parts, out_dtype=out_dtype)[0]
@@ -120,6 +129,44 @@ class CudaBackend:
         out = torch.empty((world,) + tuple(x.shape), device=x.device, dtype=x.dtype)
         dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
         return out
+
+
+class PeerBackend(CudaBackend):
+    """CudaBackend whose two exchanges per layer go through peer memory
+    (srswa.peer.PeerAllGather over CUDA IPC): one push and one bounded wait
+    launch each instead of a library all-gather, and no collective after
+    set-up.  One object serves every layer of a step (the two regions
+    alternate, which keeps a rank from overwriting data a peer still reads).
+    rows / topm / heads / head_dim bound the payloads."""
+
+    def __init__(self, group=None, *, rows, topm, heads, head_dim):
+        super().__init__(group)
+        from .peer import PeerAllGather
+        self.keys_x = PeerAllGather(rows * topm * 8, group)
+        self.part_x = PeerAllGather(-(-(rows * heads * head_dim + rows * heads) // 4) * 16, group)
+
+    def gather_keys(self, keys, world):
+        return self.keys_x(keys)
+
+    def gather_partials(self, buf, world):
+        return self.part_x(buf)
+
+    def check(self):
+        self.keys_x.check()
+        self.part_x.check()
+
+    def close(self):
+        """Collective: every rank calls it once its GPU work is done."""
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        if dist.is_initialized():
+            dist.barrier(group=self.group)
+        for x in (self.keys_x, self.part_x):
+            x.close_mappings()
+        if dist.is_initialized():
+            dist.barrier(group=self.group)
+        for x in (self.keys_x, self.part_x):
+            x.close()
 
 
 class SplitKVDecode:
@@ -160,7 +207,7 @@ class SplitKVDecode:
         # host-only check first: a bad plan fails before any launch or collective
         owner = self.window_owner(int(p_range[1]), int(p_range[0]))
         keys = be.shard_keys(idx_q, layer, plan, q_pos, self.rp)            # [N, M]
-        all_keys = be.all_gather(keys, world)                                # [world, N, M]
+        all_keys = be.gather_keys(keys, world)                               # [world, N, M]
         sel = be.merge_keys(all_keys, plan, self.rp)
         # one rank: its output is final, written in out_dtype; else fp32 partials
         o_part, lse_part = be.attend(q, layer, sel["topi32_own"], sel["bias"], q_pos,
