@@ -498,14 +498,14 @@ def dense_check(x, train, res):
         bias = x["b"][bi].cpu().numpy()
         seg = np.zeros(T, np.int64)
         o_r, _ = O.gather_rows_fwd(qb, kb, vb, sel, seg, rows, BS, SM_SCALE, LW, bias)
-        got = res[0][bi][:, rows].transpose(0, 1).float().cpu().numpy()
+        got = res[0][bi][:, rows].transpose(0, 1).detach().float().cpu().numpy()
         d = np.abs(got - o_r)
         err = max(err, float(d.max()))
         worst = max(worst, float((d / (2e-2 + 1e-2 * np.abs(o_r))).max()))
         if train:
             dob = x["do"][bi].transpose(0, 1).float().cpu().numpy()
             dq_r, _ = O.gather_rows_bwd(qb, kb, vb, dob, sel, seg, rows, BS, SM_SCALE, LW, bias)
-            got = res[1][bi][:, rows].transpose(0, 1).float().cpu().numpy()
+            got = res[1][bi][:, rows].transpose(0, 1).detach().float().cpu().numpy()
             d = np.abs(got - dq_r)
             err = max(err, float(d.max()))
             worst = max(worst, float((d / (2e-2 + 1e-2 * np.abs(dq_r))).max()))
