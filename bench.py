@@ -80,15 +80,28 @@ def workload(args):
     return S, g
 
 
+def request_cost(s):
+    """Algorithmic bytes of one request's decode step: the attend reads about
+    the same keys for every request (the window + K selected blocks, K and V
+    of every kv head), the router one k_bar row and one block-table entry per
+    remote candidate block (O(S_r))."""
+    attend = (L * BS + K * BS) * HKV * D * 2 * 2
+    route = max(0, (s - 1) // BS - L + 1) * (DI * 4 + 4)
+    return attend + route
+
+
 def shard(S, world):
-    """Greedy balance of sum S_r over ranks (the k_bar scan is O(S_r))."""
-    order = sorted(range(len(S)), key=lambda i: -S[i])
+    """Greedy balance (largest first) of the per-request step cost over ranks:
+    request counts stay even (the attend's constant part dominates) and the
+    router's O(S_r) part is spread."""
+    cost = [request_cost(s) for s in S]
+    order = sorted(range(len(S)), key=lambda i: -cost[i])
     load = [0] * world
     parts = [[] for _ in range(world)]
     for i in order:
-        r = min(range(world), key=lambda j: load[j])
+        r = min(range(world), key=lambda j: (load[j], len(parts[j])))
         parts[r].append(i)
-        load[r] += S[i]
+        load[r] += cost[i]
     return [sorted(p) for p in parts]
 
 

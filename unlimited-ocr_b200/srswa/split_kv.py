@@ -96,7 +96,7 @@ class CudaBackend:
             # partial o and its lse packed in one buffer (padded to 16 bytes):
             # one all-gather moves both
             buf = torch.empty(-(-(N * H * D + N * H) // 4) * 4, device=q.device, dtype=torch.float32)
-            out, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:].view(N, H)
+            out, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:N * H * D + N * H].view(N, H)
         else:
             out, lse = torch.empty(q.shape, device=q.device, dtype=out_dtype), None
         return self.ops.decode_attend(q, layer["k_cache"], layer["v_cache"], topi, bias, block_size=block_size,
