@@ -51,6 +51,17 @@ enum {
   SRSWA_ETOOLARGE = -5     /* size above a compiled-in maximum */
 };
 
+/* A peer-memory exchange region (see "peer exchange" below); entry points
+ * that take one accept NULL = no exchange. */
+typedef struct {
+  void* const* regions;
+  void* own_region;
+  int64_t slot_bytes, rank, world;
+  uint64_t* counter;
+  uint32_t* tickets;
+  int32_t* status;
+} srswa_peer;
+
 /* Library version (major*10000 + minor*100 + patch) and status text. */
 SRSWA_API int srswa_version(void);
 SRSWA_API const char* srswa_status_string(int status);
@@ -164,6 +175,10 @@ SRSWA_API int srswa_route_select(const float* scores, int64_t s_sc, int64_t N, i
  * block id, bit 0 = candidate flag.  A larger key ranks first (x descending,
  * then block id ascending, the reference's tie order); 0 = no key.
  *
+ * push (optional): the row keys also go into slot `rank` of every region of
+ * that exchange (the producer side of the split-KV key all-gather), keys
+ * [N, M] per slot.
+ *
  * Stage 2: srswa_route_merge_keys reads nlists key lists per row (list l of
  * row n at keys[l * s_list + n * s_row], M keys each), keeps the global top-M
  * and runs the selection epilogue of srswa_route (exact entmax over the M,
@@ -173,7 +188,8 @@ SRSWA_API int srswa_route_select(const float* scores, int64_t s_sc, int64_t N, i
  * the whole row.  topi32_own (optional, [N, K]) is topi32 with -1 for blocks
  * outside [own_lo, own_hi): the slots the calling shard attends.
  * No candidate mask in this form (the reference's empty-row fallback needs
- * the whole row).
+ * the whole row).  wait (optional): every CTA first acquires the flags of
+ * that exchange (keys then point at own_region's slots), bounded.
  * Serves the per-GPU local top-M + global merge of the 1M-token split-KV
  * decode, over _infer_route_select semantics
  * (hf-model-code/modeling_deepseekv2.py:339-362) and
@@ -184,11 +200,13 @@ SRSWA_API int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_q
                            int64_t block_offset, int64_t nblk_total, const int32_t* block_table,
                            int64_t s_bt, const int32_t* seq_lens, int64_t rows_per_seq,
                            const int64_t* q_pos, srswa_route_params params, uint64_t* keys_out,
-                           void* workspace, size_t workspace_bytes, srswa_stream_t stream);
+                           void* workspace, size_t workspace_bytes, const srswa_peer* push,
+                           srswa_stream_t stream);
 SRSWA_API int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int64_t s_list, int64_t s_row,
                            int64_t N, int64_t nblk_total, srswa_route_params params, int64_t* topi64,
                            int32_t* topi32, float* bias, uint8_t* valid, int64_t own_lo,
-                           int64_t own_hi, int32_t* topi32_own, srswa_stream_t stream);
+                           int64_t own_hi, int32_t* topi32_own, const srswa_peer* wait,
+                           srswa_stream_t stream);
 
 /* ------------------------------------------------------------------ a3 --
  * Token block-max scores.  q [B,C,D] (strides), k [B,Sk,D], pos/seg [B,C]
@@ -347,10 +365,11 @@ SRSWA_API int srswa_workspace_status(const void* workspace, int* out, srswa_stre
  * (0 = tightly stacked: N*H*D and N*H).  -> out [N,H,D] (out_dtype,
  * contiguous) and lse_out [N,H] (optional).  Replaces
  * _merge_topk_attn_out_kernel (whl:.../unlimited_dash_ops/common.py:43-89);
- * also the cross-GPU combine of the split-KV decode. */
+ * also the cross-GPU combine of the split-KV decode, where wait (optional)
+ * makes every CTA first acquire the flags of the partials' exchange. */
 SRSWA_API int srswa_lse_merge(const float* o_parts, const float* lse_parts, int64_t C, int64_t N,
                     int64_t H, int64_t D, int64_t s_o_part, int64_t s_l_part, void* out,
-                    int out_dtype, float* lse_out, srswa_stream_t stream);
+                    int out_dtype, float* lse_out, const srswa_peer* wait, srswa_stream_t stream);
 
 /* --------------------------------------------------- peer exchange ------
  * All-gather through peer memory for the split-KV decode across the GPUs of
@@ -363,27 +382,40 @@ SRSWA_API int srswa_lse_merge(const float* o_parts, const float* lse_parts, int6
  * allocate): srswa_peer_region_alloc (cudaMalloc + zero fill, so the IPC
  * handle maps exactly the region), srswa_peer_ipc_handle (64 bytes to send to
  * the peers), srswa_peer_ipc_open / _close on each peer's handle.
- * srswa_peer_allgather: regions = device array [world] of the regions' base
- * addresses as mapped in this process (own region at index rank); copies
- * nbytes (multiple of 16, <= slot_bytes) from src into slot `rank` of every
- * region with plain stores, publishes epoch = *counter + 1 in flag `rank` of
- * each (release, system scope), then waits until every source has published
- * that epoch in own_region (acquire, bounded: 2 s, then code 501 in *status)
- * and advances *counter (a device uint64, zero at set-up, one per region,
- * advanced identically on every rank).  The gathered payloads are then slot
- * r of own_region.  Two launches, graph-capturable; no NCCL, no TMA, no
- * multicast.  A rank must not start exchange e+1 on a region before its
- * consumers of exchange e have read it (stream order gives this when two
- * regions alternate). */
+ *
+ * A region is described by srswa_peer (declared above; all pointers device
+ * memory):
+ *   regions     [world] the regions' base addresses as mapped in this process
+ *               (regions[rank] = own_region);
+ *   counter     exchanges completed on this region (zero at set-up; the
+ *               producer publishes epoch = *counter + 1, the consumer waits
+ *               for it on every source's flag and then advances *counter);
+ *   tickets     2 words, zero at set-up: the producer units' and the
+ *               consumer CTAs' arrival counts (reset by the last arrival);
+ *   status      0, or 501 when a wait expired (2 s bound; the kernel then
+ *               goes on with whatever the slots hold and returns).
+ * Producers copy their payload with plain stores into slot `rank` of every
+ * region, and the last producer unit releases flag `rank` of every region
+ * (system scope); consumers acquire all flags before reading the slots.  The
+ * payload of rank r is then slot r of own_region.  Producers and consumers
+ * are the library's kernels themselves: srswa_route_shard_keys (push of the
+ * router keys), srswa_route_merge_keys and srswa_lse_merge (wait), or the
+ * stand-alone srswa_peer_push / srswa_peer_allgather (push; push + wait).
+ * No NCCL, no TMA, no multicast: peer bytes move only by plain stores.  A
+ * rank must not start exchange e+1 on a region before its consumers of e
+ * have read it; stream order gives this when two regions alternate (router
+ * keys, then attention partials). */
 SRSWA_API int srswa_peer_region_size(int64_t world, int64_t slot_bytes, size_t* out);
 SRSWA_API int srswa_peer_region_alloc(size_t bytes, void** out);
 SRSWA_API int srswa_peer_region_free(void* region);
 SRSWA_API int srswa_peer_ipc_handle(const void* region, void* handle64);
 SRSWA_API int srswa_peer_ipc_open(const void* handle64, void** mapped);
 SRSWA_API int srswa_peer_ipc_close(void* mapped);
-SRSWA_API int srswa_peer_allgather(const void* src, int64_t nbytes, void* const* regions, const void* own_region,
-                         int64_t slot_bytes, int64_t rank, int64_t world, uint64_t* counter, int* status,
-                         srswa_stream_t stream);
+/* nbytes (multiple of 16, <= slot_bytes) from src into slot `rank` of every
+ * region, then the flags; srswa_peer_allgather also waits (one more launch)
+ * and advances the counter. */
+SRSWA_API int srswa_peer_push(const void* src, int64_t nbytes, const srswa_peer* peer, srswa_stream_t stream);
+SRSWA_API int srswa_peer_allgather(const void* src, int64_t nbytes, const srswa_peer* peer, srswa_stream_t stream);
 
 /* ------------------------------------------------------- PageGate ------
  * Page-aware remote candidates.  Token ids are int64 [B, n] rows (row stride

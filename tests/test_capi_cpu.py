@@ -59,7 +59,7 @@ def test_invalid_arguments_rejected_without_launch():
                            None, None, None, None, None, None, 0, None) == L.EINVAL
     assert lib.srswa_route_workspace_size(256, 2048, 128, p, 0) > 0      # decode rows: chunked router
     assert lib.srswa_route_workspace_size(65536, 256, 128, p, 0) == 0    # prefill rows: no scratch
-    assert lib.srswa_lse_merge(None, None, 1, 1, 1, 1, 0, 0, None, 0, None, None) == L.EINVAL
+    assert lib.srswa_lse_merge(None, None, 1, 1, 1, 1, 0, 0, None, 0, None, None, None) == L.EINVAL
     d = L.DecodeDesc()
     assert lib.srswa_decode_attend(C.byref(d), None, None, None, None, None, None, None, None, None, None,
                                    None, None) == L.EINVAL

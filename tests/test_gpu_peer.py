@@ -41,10 +41,11 @@ def test_peer_wait_expires_with_status(cuda):
     # region is never set, so the wait must expire (2 s) with code 501
     regions = torch.tensor(regs, dtype=torch.int64, device=cuda)
     counter = torch.zeros(1, dtype=torch.int64, device=cuda)
+    tickets = torch.zeros(2, dtype=torch.int32, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    peer = L.Peer(regions.data_ptr(), regs[0], 256, 0, 2, counter.data_ptr(), tickets.data_ptr(), status.data_ptr())
     x = torch.ones(64, device=cuda, dtype=torch.int32)
-    rc = lib.srswa_peer_allgather(x.data_ptr(), 256, regions.data_ptr(), regs[0], 256, 0, 2, counter.data_ptr(),
-                                  status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    rc = lib.srswa_peer_allgather(x.data_ptr(), 256, C.byref(peer), torch.cuda.current_stream().cuda_stream)
     assert rc == 0
     torch.cuda.synchronize()
     assert int(status.item()) == 501

@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "attend.cuh"
+#include "peer.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -446,8 +447,12 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
 
 __global__ void lse_merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ lse_parts,
                                  int64_t C, int64_t NH, int64_t D, int64_t s_o, int64_t s_l, void* out,
-                                 int out_dtype, float* lse_out) {
+                                 int out_dtype, float* lse_out, const srswa_peer wait) {
   const int64_t nh = blockIdx.x;
+  if (wait.regions) {  // the parts are the peers' pushes into this rank's region
+    if (threadIdx.x == 0) peer_wait_all(wait, gridDim.x);
+    __syncthreads();
+  }
   float M = -INFINITY;
   for (int64_t c = 0; c < C; ++c) M = fmaxf(M, lse_parts[c * s_l + nh]);
   const float Mu = (M == -INFINITY) ? 0.f : M;
@@ -545,14 +550,21 @@ extern "C" int srswa_prefill_attend(const srswa_decode_desc* dd, const void* q, 
 
 extern "C" int srswa_lse_merge(const float* o_parts, const float* lse_parts, int64_t C, int64_t N,
                                int64_t H, int64_t D, int64_t s_o_part, int64_t s_l_part, void* out,
-                               int out_dtype, float* lse_out, srswa_stream_t stream) {
+                               int out_dtype, float* lse_out, const srswa_peer* wait, srswa_stream_t stream) {
   SRSWA_CHECK_ARG(o_parts && lse_parts && out && C > 0 && N >= 0 && H > 0 && D > 0, SRSWA_EINVAL);
+  srswa_peer pw = {};
+  if (wait) {
+    SRSWA_CHECK_ARG(wait->regions && wait->own_region && wait->counter && wait->tickets && wait->world >= 1 &&
+                        wait->world <= 32,
+                    SRSWA_EINVAL);
+    pw = *wait;
+  }
   if (s_o_part == 0) s_o_part = N * H * D;
   if (s_l_part == 0) s_l_part = N * H;
   SRSWA_CHECK_ARG(s_o_part >= N * H * D && s_l_part >= N * H, SRSWA_EINVAL);
   if (N == 0) return 0;
   SRSWA_CHECK_ARG(N * H < (1ll << 31), SRSWA_ETOOLARGE);
   lse_merge_kernel<<<static_cast<unsigned>(N * H), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      o_parts, lse_parts, C, N * H, D, s_o_part, s_l_part, out, out_dtype, lse_out);
+      o_parts, lse_parts, C, N * H, D, s_o_part, s_l_part, out, out_dtype, lse_out, pw);
   return srswa_last_launch_status();
 }

@@ -3,9 +3,11 @@
 // every peer's exchange region (CUDA IPC mappings), then releases a
 // per-source flag there at system scope; a rank's consumers run after a
 // bounded wait on the flags of its own region.  This replaces a library
-// all-gather per exchange (two per layer of a decode step) with one push and
-// one wait launch, both capturable in a CUDA graph: the epoch each exchange
-// waits for lives in device memory and advances on the device.
+// all-gather per exchange (two per layer of a decode step): the router's
+// shard kernel pushes its keys itself, the key merge and the log-sum-exp
+// merge wait themselves, and the attention partials take one push launch.
+// All of it is capturable in a CUDA graph: the epoch each exchange waits for
+// lives in device memory and advances on the device.
 //
 // Region layout (one per rank, all ranks the same size):
 //   [0, 8 * world)            flags: uint64 epoch last published by source r
@@ -21,71 +23,39 @@
 // moved only by the plain stores of peer_push_kernel.
 #include <cstring>
 
-#include "common.cuh"
+#include "peer.cuh"
 
 namespace srswa {
 
 constexpr int kPeerThreads = 256;
-constexpr int64_t kPeerHeader = 256;  // flag bytes reserved at the head of a region (world <= 32)
-// bound of a wait (wall clock, %globaltimer ns)
-constexpr uint64_t kPeerWaitNs = 2000000000ull;
 
-__device__ __forceinline__ uint64_t peer_now() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// CTA d copies the payload into slot `rank` of peer d's region (d == rank:
-// the local region), then publishes epoch = *counter + 1 in that region's
-// flag `rank`.  nbytes is a multiple of 16 and all addresses 16-byte aligned.
+// CTA d copies the payload into slot `rank` of region d (d == rank: the
+// local region); the last CTA to finish publishes the flags.  nbytes is a
+// multiple of 16 and all addresses 16-byte aligned.
 __global__ void __launch_bounds__(kPeerThreads) peer_push_kernel(const uint4* __restrict__ src, int64_t n16,
-                                                                 char* const* __restrict__ regions, int64_t slot,
-                                                                 int rank, const uint64_t* __restrict__ counter) {
-  const int d = blockIdx.x;
-  char* region = regions[d];
-  uint4* dst = reinterpret_cast<uint4*>(region + kPeerHeader + static_cast<int64_t>(rank) * slot);
+                                                                 const srswa_peer p) {
+  uint4* dst = reinterpret_cast<uint4*>(peer_slot(p, blockIdx.x));
   for (int64_t i = threadIdx.x; i < n16; i += kPeerThreads) dst[i] = __ldg(src + i);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint64_t epoch = *counter + 1;
-    __threadfence_system();  // the payload stores above (all threads, via the barrier) before the flag
-    uint64_t* flag = reinterpret_cast<uint64_t*>(region) + rank;
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(epoch) : "memory");
-  }
+  if (threadIdx.x == 0) peer_unit_done(p, gridDim.x);
 }
 
-// One warp: lane r waits until source r has published epoch *counter + 1 in
-// this rank's region (acquire, system scope), bounded in wall-clock time; on
-// expiry it records `code` in *status.  Then the counter advances.
-__global__ void peer_wait_kernel(const char* region, int world, uint64_t* counter, int* status, int code) {
-  const int r = threadIdx.x;
-  const uint64_t epoch = *counter + 1;
-  bool ok = true;
-  if (r < world) {
-    const uint64_t* flag = reinterpret_cast<const uint64_t*>(region) + r;
-    const uint64_t t0 = peer_now();
-    for (;;) {
-      uint64_t v;
-      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
-      if (v >= epoch) break;
-      if (peer_now() - t0 > kPeerWaitNs) {
-        ok = false;
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
-  const bool all_ok = __all_sync(0xffffffffu, ok);
-  if (r == 0) {
-    if (!all_ok && status) atomicCAS(status, 0, code);
-    *counter = epoch;  // advance even on expiry: the next exchange does not wait for a stale epoch
-  }
+// One thread: wait for every source's flag, then advance the counter.
+__global__ void peer_wait_kernel(const srswa_peer p) {
+  if (threadIdx.x == 0) peer_wait_all(p, 1u);
 }
 
 }  // namespace srswa
 
 using namespace srswa;
+
+static int check_peer(const srswa_peer* p) {
+  if (!p || !p->regions || !p->own_region || !p->counter || !p->tickets) return SRSWA_EINVAL;
+  if (p->world < 1 || p->world > 32 || p->rank < 0 || p->rank >= p->world || p->slot_bytes < 0) return SRSWA_EINVAL;
+  if (((reinterpret_cast<uintptr_t>(p->own_region) | static_cast<uintptr_t>(p->slot_bytes)) & 15) != 0)
+    return SRSWA_EALIGN;
+  return 0;
+}
 
 extern "C" int srswa_peer_region_size(int64_t world, int64_t slot_bytes, size_t* out) {
   if (!out || world < 1 || world > 32 || slot_bytes < 0 || (slot_bytes & 15)) return SRSWA_EINVAL;
@@ -137,21 +107,19 @@ extern "C" int srswa_peer_ipc_close(void* mapped) {
   return 0;
 }
 
-extern "C" int srswa_peer_allgather(const void* src, int64_t nbytes, void* const* regions, const void* own_region,
-                                    int64_t slot_bytes, int64_t rank, int64_t world, uint64_t* counter,
-                                    int* status, srswa_stream_t stream) {
-  SRSWA_CHECK_ARG(src && regions && own_region && counter && world >= 1 && world <= 32 && rank >= 0 &&
-                      rank < world && nbytes >= 0 && nbytes <= slot_bytes,
-                  SRSWA_EINVAL);
-  SRSWA_CHECK_ARG(((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(own_region) |
-                    static_cast<uintptr_t>(nbytes) | static_cast<uintptr_t>(slot_bytes)) & 15) == 0,
-                  SRSWA_EALIGN);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  peer_push_kernel<<<static_cast<unsigned>(world), kPeerThreads, 0, st>>>(
-      static_cast<const uint4*>(src), nbytes / 16, reinterpret_cast<char* const*>(regions), slot_bytes,
-      static_cast<int>(rank), counter);
-  SRSWA_CUDA_TRY(cudaGetLastError());
-  peer_wait_kernel<<<1, 32, 0, st>>>(static_cast<const char*>(own_region), static_cast<int>(world), counter, status,
-                                     501);
+extern "C" int srswa_peer_push(const void* src, int64_t nbytes, const srswa_peer* peer, srswa_stream_t stream) {
+  int rc = check_peer(peer);
+  if (rc) return rc;
+  SRSWA_CHECK_ARG(src && nbytes >= 0 && nbytes <= peer->slot_bytes, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(((reinterpret_cast<uintptr_t>(src) | static_cast<uintptr_t>(nbytes)) & 15) == 0, SRSWA_EALIGN);
+  peer_push_kernel<<<static_cast<unsigned>(peer->world), kPeerThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), nbytes / 16, *peer);
+  return srswa_last_launch_status();
+}
+
+extern "C" int srswa_peer_allgather(const void* src, int64_t nbytes, const srswa_peer* peer, srswa_stream_t stream) {
+  int rc = srswa_peer_push(src, nbytes, peer, stream);
+  if (rc) return rc;
+  peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*peer);
   return srswa_last_launch_status();
 }

@@ -7,6 +7,7 @@
 // have to round like the reference's CPU path).
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace srswa {
 
@@ -828,7 +829,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
                                                                          int64_t nblk_local,
                                                                          unsigned long long* chunk_out,
                                                                          unsigned int* counters,
-                                                                         unsigned long long* keys_out) {
+                                                                         unsigned long long* keys_out,
+                                                                         const srswa_peer push) {
   extern __shared__ __align__(16) unsigned long long mk[];  // [nch * M] (last CTA of a row)
   __shared__ int32_t bts[kChunkBlocks];
   __shared__ float zs[kChunkBlocks];
@@ -904,7 +906,15 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
   const int M = static_cast<int>(a.M);
   const int64_t nch = gridDim.x;
   if (warp == 0) warp_topm_smem(keys, kChunkBlocks, M, chunk_out + (n * nch + blockIdx.x) * M, lane);
-  if (nch == 1) return;  // chunk_out is the row's output
+  if (nch == 1) {  // chunk_out is the row's output
+    if (push.regions) {  // and this rank's keys of the row go to every peer
+      __syncthreads();
+      if (tid < M) peer_put8(push, (n * M + tid) * 8, chunk_out[n * M + tid]);
+      __syncthreads();
+      if (tid == 0) peer_unit_done(push, gridDim.y);
+    }
+    return;
+  }
   // the last CTA of the row to finish merges the row's chunk lists
   __threadfence();
   __syncthreads();
@@ -917,8 +927,15 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
   for (int64_t i = tid; i < total; i += kRouteThreads) mk[i] = __ldcg(src + i);
   __syncthreads();
   const unsigned long long mine = block_topm(mk, total, M, lists, warp, lane);
-  if (warp == 0 && lane < M) keys_out[n * M + lane] = mine;
+  if (warp == 0 && lane < M) {
+    keys_out[n * M + lane] = mine;
+    if (push.regions) peer_put8(push, (n * M + lane) * 8, mine);  // this rank's keys of the row, to every peer
+  }
   if (tid == 0) counters[n] = 0u;
+  if (push.regions) {
+    __syncthreads();
+    if (tid == 0) peer_unit_done(push, gridDim.y);  // one unit per row
+  }
 }
 
 constexpr int64_t kMergeMaxKeys = 24576;  // nlists * M per row (192 KiB of shared memory)
@@ -926,11 +943,16 @@ constexpr int64_t kMergeMaxKeys = 24576;  // nlists * M per row (192 KiB of shar
 __global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteArgs a, const unsigned long long* keys,
                                                                    int64_t nlists, int64_t s_list, int64_t s_row,
                                                                    unsigned long long* keys_out, int64_t own_lo,
-                                                                   int64_t own_hi, int32_t* topi32_own) {
+                                                                   int64_t own_hi, int32_t* topi32_own,
+                                                                   const srswa_peer wait) {
   extern __shared__ __align__(16) unsigned long long mk[];
   __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
   const int64_t n = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (wait.regions) {  // the lists are the peers' pushes into this rank's region
+    if (tid == 0) peer_wait_all(wait, gridDim.x);
+    __syncthreads();
+  }
   const int M = static_cast<int>(a.M);
   const int64_t total = nlists * M;
   for (int64_t l = warp; l < nlists; l += kRouteThreads / 32)
@@ -1483,7 +1505,7 @@ static int64_t shard_topm_bound(const srswa_route_params& p) {
 
 static int keys_merge_launch(const RouteArgs& a, const unsigned long long* keys, int64_t nlists, int64_t s_list,
                              int64_t s_row, unsigned long long* keys_out, int64_t own_lo, int64_t own_hi,
-                             int32_t* topi32_own, cudaStream_t st) {
+                             int32_t* topi32_own, const srswa_peer& wait, cudaStream_t st) {
   if (nlists * a.M > kMergeMaxKeys) return SRSWA_ETOOLARGE;
   if (a.N >= (1ll << 31)) return SRSWA_ETOOLARGE;
   const size_t smem = static_cast<size_t>(nlists * a.M) * 8;
@@ -1493,7 +1515,7 @@ static int keys_merge_launch(const RouteArgs& a, const unsigned long long* keys,
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   keys_merge_kernel<<<static_cast<unsigned>(a.N), kRouteThreads, smem, st>>>(a, keys, nlists, s_list, s_row, keys_out,
-                                                                             own_lo, own_hi, topi32_own);
+                                                                             own_lo, own_hi, topi32_own, wait);
   return srswa_last_launch_status();
 }
 
@@ -1510,8 +1532,16 @@ extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_
                                       int64_t block_offset, int64_t nblk_total, const int32_t* block_table,
                                       int64_t s_bt, const int32_t* seq_lens, int64_t rows_per_seq,
                                       const int64_t* q_pos, srswa_route_params params, uint64_t* keys_out,
-                                      void* workspace, size_t workspace_bytes, srswa_stream_t stream) {
+                                      void* workspace, size_t workspace_bytes, const srswa_peer* push,
+                                      srswa_stream_t stream) {
   SRSWA_CHECK_ARG(idx_q && kbar && keys_out && N >= 0 && rows_per_seq > 0, SRSWA_EINVAL);
+  srswa_peer pp = {};
+  if (push) {
+    SRSWA_CHECK_ARG(push->regions && push->own_region && push->counter && push->tickets && push->world >= 1 &&
+                        push->world <= 32 && push->rank >= 0 && push->rank < push->world,
+                    SRSWA_EINVAL);
+    pp = *push;
+  }
   SRSWA_CHECK_ARG(nblk_local > 0 && block_offset >= 0 && block_offset + nblk_local <= nblk_total, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(q_pos || seq_lens, SRSWA_EINVAL);
   SRSWA_CHECK_ARG(d == 128, SRSWA_EUNSUPPORTED);
@@ -1529,9 +1559,10 @@ extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t nch = (nblk_local + kChunkBlocks - 1) / kChunkBlocks;
   unsigned long long* out = reinterpret_cast<unsigned long long*>(keys_out);
+  SRSWA_CHECK_ARG(!push || N * a.M * 8 <= push->slot_bytes, SRSWA_EINVAL);
   if (nch == 1) {
     route_chunk_keys_kernel<<<dim3(1, static_cast<unsigned>(N)), kRouteThreads, 0, st>>>(a, block_offset, nblk_local,
-                                                                                      out, nullptr, nullptr);
+                                                                                      out, nullptr, nullptr, pp);
     return srswa_last_launch_status();
   }
   SRSWA_CHECK_ARG(nch * a.M <= kMergeMaxKeys, SRSWA_ETOOLARGE);
@@ -1548,15 +1579,22 @@ extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   route_chunk_keys_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(N)), kRouteThreads, smem, st>>>(
-      a, block_offset, nblk_local, ck, counters, out);
+      a, block_offset, nblk_local, ck, counters, out, pp);
   return srswa_last_launch_status();
 }
 
 extern "C" int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int64_t s_list, int64_t s_row, int64_t N,
                                       int64_t nblk_total, srswa_route_params params, int64_t* topi64,
                                       int32_t* topi32, float* bias, uint8_t* valid, int64_t own_lo, int64_t own_hi,
-                                      int32_t* topi32_own, srswa_stream_t stream) {
+                                      int32_t* topi32_own, const srswa_peer* wait, srswa_stream_t stream) {
   SRSWA_CHECK_ARG(keys && nlists > 0 && N >= 0 && nblk_total > 0, SRSWA_EINVAL);
+  srswa_peer pw = {};
+  if (wait) {
+    SRSWA_CHECK_ARG(wait->regions && wait->own_region && wait->counter && wait->tickets && wait->world >= 1 &&
+                        wait->world <= 32,
+                    SRSWA_EINVAL);
+    pw = *wait;
+  }
   RouteArgs a = {};
   int rc = fill_route_params(a, params, nblk_total);
   if (rc) return rc;
@@ -1564,7 +1602,7 @@ extern "C" int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int6
   a.N = N; a.nblk = nblk_total; a.topi64 = topi64; a.topi32 = topi32; a.bias = bias; a.valid = valid;
   if (N == 0) return 0;
   return keys_merge_launch(a, reinterpret_cast<const unsigned long long*>(keys), nlists, s_list, s_row, nullptr,
-                           own_lo, own_hi, topi32_own, reinterpret_cast<cudaStream_t>(stream));
+                           own_lo, own_hi, topi32_own, pw, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int srswa_block_max_score(const void* q, int q_dtype, int64_t sqb, int64_t sqc, const void* k,

@@ -46,6 +46,12 @@ class DecodeDesc(C.Structure):
                 ("s_b_h", i64), ("s_b_n", i64), ("nsplit", C.c_int), ("skip_local", C.c_int)]
 
 
+class Peer(C.Structure):
+    """srswa_peer: one peer-memory exchange region (device pointers)."""
+    _fields_ = [("regions", vp), ("own_region", vp), ("slot_bytes", i64), ("rank", i64), ("world", i64),
+                ("counter", vp), ("tickets", vp), ("status", vp)]
+
+
 _SIGS = {
     "srswa_version": (C.c_int, []),
     "srswa_status_string": (C.c_char_p, [C.c_int]),
@@ -59,9 +65,9 @@ _SIGS = {
     "srswa_route_select": (C.c_int, [vp, i64, i64, i64, vp, i64, RouteParams, vp, vp, vp, vp, vp]),
     "srswa_route_shard_workspace_size": (C.c_size_t, [i64, i64, RouteParams]),
     "srswa_route_shard_keys": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, i64, i64, i64, i64, i64, vp, i64, vp,
-                                         i64, vp, RouteParams, vp, vp, C.c_size_t, vp]),
+                                         i64, vp, RouteParams, vp, vp, C.c_size_t, vp, vp]),
     "srswa_route_merge_keys": (C.c_int, [vp, i64, i64, i64, i64, i64, RouteParams, vp, vp, vp, vp, i64, i64,
-                                         vp, vp]),
+                                         vp, vp, vp]),
     "srswa_block_max_score": (C.c_int, [vp, C.c_int, i64, i64, vp, C.c_int, i64, i64, vp, vp, i64, i64,
                                         i64, i64, i64, i64, i64, C.c_int, vp, vp]),
     "srswa_pack_selection": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, vp]),
@@ -79,7 +85,7 @@ _SIGS = {
     "srswa_prefill_attend": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "srswa_workspace_status": (C.c_int, [vp, C.POINTER(C.c_int), vp]),
     "srswa_gather_bwd_noalloc_status": (C.c_int, [C.POINTER(C.c_int), vp]),
-    "srswa_lse_merge": (C.c_int, [vp, vp, i64, i64, i64, i64, i64, i64, vp, C.c_int, vp, vp]),
+    "srswa_lse_merge": (C.c_int, [vp, vp, i64, i64, i64, i64, i64, i64, vp, C.c_int, vp, vp, vp]),
     "srswa_page_scan_workspace_size": (C.c_size_t, [i64, i64]),
     "srswa_page_ids": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, C.c_int, vp, vp, vp, vp, vp,
                                  C.c_size_t, vp]),
@@ -96,7 +102,8 @@ _SIGS = {
     "srswa_peer_ipc_handle": (C.c_int, [vp, vp]),
     "srswa_peer_ipc_open": (C.c_int, [vp, C.POINTER(vp)]),
     "srswa_peer_ipc_close": (C.c_int, [vp]),
-    "srswa_peer_allgather": (C.c_int, [vp, i64, vp, vp, i64, i64, i64, vp, vp, vp]),
+    "srswa_peer_push": (C.c_int, [vp, i64, vp, vp]),
+    "srswa_peer_allgather": (C.c_int, [vp, i64, vp, vp]),
     "srswa_rope2d_pos_workspace_size": (C.c_size_t, [i64, i64]),
     "srswa_rope2d_pos": (C.c_int, [vp, i64, i64, i64, i64, i64, i64, i64, vp, vp, vp, i64, vp, vp, C.c_size_t,
                                    vp]),

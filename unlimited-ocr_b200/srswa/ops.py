@@ -180,7 +180,7 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
 
 def route_shard_keys(idx_q, kbar, *, block_offset, nblk_local, nblk_total, block_size, local_blocks, topk, topm,
                      idx_scale, floor, sigma, q_pos=None, seq_lens=None, rows_per_seq=1, block_table=None,
-                     out=None):
+                     out=None, push=None, workspace=None):
     """Split-KV router stage 1: packed top-M keys [N, M] (int64 storage of
     the uint64 keys) of the blocks this shard owns, global ids
     [block_offset, block_offset + nblk_local).  kbar: the shard's contiguous
@@ -207,18 +207,18 @@ def route_shard_keys(idx_q, kbar, *, block_offset, nblk_local, nblk_total, block
     p = _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma)
     lib = L.lib()
     ws_n = lib.srswa_route_shard_workspace_size(N, int(nblk_local), p)
-    ws = torch.empty(ws_n, device=dev, dtype=torch.uint8) if ws_n else None
+    ws = _workspace(ws_n, dev, workspace) if ws_n else None
     rc = lib.srswa_route_shard_keys(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
                                     kbar.data_ptr(), s_b, s_c, int(nblk_local), int(block_offset),
                                     int(nblk_total), L.ptr(bt), 0 if bt is None else bt.stride(0), L.ptr(sl),
                                     int(rows_per_seq), L.ptr(qp), p, out.data_ptr(), L.ptr(ws), ws_n,
-                                    L.stream_of(idx_q))
+                                    None if push is None else C.byref(push), L.stream_of(idx_q))
     L.check(rc, "srswa_route_shard_keys")
     return out
 
 
 def route_merge_keys(keys, *, nblk_total, topk, topm, idx_scale, floor, sigma, own=None,
-                     want=("topi64", "bias", "valid")):
+                     want=("topi64", "bias", "valid"), wait=None):
     """Split-KV router stage 2: keys [nlists, N, M] (the all-gathered stage-1
     outputs) -> the selection of the whole row, as srswa_route.  own =
     (lo, hi) adds "topi32_own": topi32 with -1 outside the owned range."""
@@ -236,7 +236,7 @@ def route_merge_keys(keys, *, nblk_total, topk, topm, idx_scale, floor, sigma, o
     rc = L.lib().srswa_route_merge_keys(keys.data_ptr(), nl, keys.stride(0), keys.stride(1), N, int(nblk_total), p,
                                         L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
                                         L.ptr(out["valid"]), int(lo), int(hi), L.ptr(out["topi32_own"]),
-                                        L.stream_of(keys))
+                                        None if wait is None else C.byref(wait), L.stream_of(keys))
     L.check(rc, "srswa_route_merge_keys")
     if out["valid"] is not None:
         out["valid"] = out["valid"].view(torch.bool)  # 0 / 1 bytes: no copy
@@ -503,14 +503,19 @@ def prefill_attend(q, k_cache, v_cache, topk_idx, bias, *, block_table, cu_seqle
     return (out, lse_t) if lse else out
 
 
-def lse_merge(o_parts, lse_parts, out_dtype=torch.float32, out=None, lse=None):
+def lse_merge(o_parts, lse_parts, out_dtype=torch.float32, out=None, lse=None, wait=None):
     """o_parts [C,N,H,D], lse_parts [C,N,H] fp32 (each part contiguous; the
     parts may be strided, e.g. views into one packed all-gather buffer) ->
     (out [N,H,D] out_dtype, lse [N,H])."""
     Cn, N, H, D = o_parts.shape
-    if o_parts.dtype != torch.float32 or o_parts[0].stride() != (H * D, D, 1):
+    copy_o = o_parts.dtype != torch.float32 or o_parts[0].stride() != (H * D, D, 1)
+    copy_l = lse_parts.dtype != torch.float32 or lse_parts[0].stride() != (H, 1)
+    if wait is not None and (copy_o or copy_l):
+        # the parts arrive from peers during the kernel's own wait: no copy may read them earlier
+        raise ValueError("lse_merge with wait: parts must be fp32 views with contiguous parts")
+    if copy_o:
         o_parts = o_parts.float().contiguous()
-    if lse_parts.dtype != torch.float32 or lse_parts[0].stride() != (H, 1):
+    if copy_l:
         lse_parts = lse_parts.float().contiguous()
     if out is None:
         out = torch.empty(N, H, D, device=o_parts.device, dtype=out_dtype)
@@ -519,7 +524,7 @@ def lse_merge(o_parts, lse_parts, out_dtype=torch.float32, out=None, lse=None):
         lse = torch.empty(N, H, device=o_parts.device, dtype=torch.float32)
     rc = L.lib().srswa_lse_merge(o_parts.data_ptr(), lse_parts.data_ptr(), Cn, N, H, D, o_parts.stride(0),
                                  lse_parts.stride(0), out.data_ptr(), L.dtype_code(out), lse.data_ptr(),
-                                 L.stream_of(o_parts))
+                                 None if wait is None else C.byref(wait), L.stream_of(o_parts))
     L.check(rc, "srswa_lse_merge")
     return out, lse
 

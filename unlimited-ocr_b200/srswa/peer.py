@@ -5,11 +5,14 @@ decode: see srswa_peer_allgather in include/srswa.h.
     out = ex(payload)                         # [world, *payload.shape] view of this rank's region
 
 Set-up exchanges the regions' IPC handles with one all_gather_object over the
-process group (any backend); after that no collective runs: each call is one
-push launch (plain stores into every peer's slot + a released flag) and one
-bounded wait launch, both capturable in a CUDA graph.  The returned view is
-valid until the next call on the same object (the next push overwrites it),
-so a decode step alternates two objects (router keys, attention partials).
+process group (any backend); after that no collective runs.  A call is one
+push launch (plain stores into every peer's slot + released flags) and one
+bounded wait launch, both capturable in a CUDA graph; ``push`` is the push
+alone, for a consumer kernel that waits itself (the library's key merge and
+log-sum-exp merge take ``self.peer`` for that), and ``self.peer`` also makes
+the router's shard kernel push its keys itself.  A returned view is valid
+until the next exchange on the same object overwrites it, so a decode step
+alternates two objects (router keys, attention partials).
 """
 
 from __future__ import annotations
@@ -58,23 +61,41 @@ class PeerAllGather:
                 ptrs.append(p.value)
         self.regions = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
         self.counter = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.tickets = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # the srswa_peer descriptor the library's producers / consumers take
+        self.peer = L.Peer(self.regions.data_ptr(), self.region, self.slot, self.rank, self.world,
+                           self.counter.data_ptr(), self.tickets.data_ptr(), self.status.data_ptr())
         # this rank's region as bytes: slot r (after the 256-byte flag header) = rank r's payload
         self._slots = _RegionView(self.region, self.size, self.device).tensor[256:].view(self.world, self.slot)
 
-    def __call__(self, payload: torch.Tensor) -> torch.Tensor:
+    def _check_payload(self, payload):
         x = payload if payload.is_contiguous() else payload.contiguous()
         nbytes = x.numel() * x.element_size()
         if nbytes > self.slot:
             raise ValueError(f"payload of {nbytes} B exceeds the {self.slot} B slot")
-        pad = (-nbytes) % 16
-        if pad:
+        if nbytes % 16:
             raise ValueError("payload size must be a multiple of 16 bytes")
-        rc = L.lib().srswa_peer_allgather(x.data_ptr(), nbytes, self.regions.data_ptr(), self.region, self.slot,
-                                          self.rank, self.world, self.counter.data_ptr(), self.status.data_ptr(),
-                                          L.stream_of(x))
-        L.check(rc, "srswa_peer_allgather")
-        return self._slots[:, :nbytes].view(x.dtype).view((self.world,) + tuple(x.shape))
+        return x, nbytes
+
+    def slots(self, shape, dtype) -> torch.Tensor:
+        """[world, *shape] view of this rank's region: slot r = rank r's payload."""
+        nbytes = torch.Size(shape).numel() * torch.empty(0, dtype=dtype).element_size()
+        return self._slots[:, :nbytes].view(dtype).view((self.world,) + tuple(shape))
+
+    def push(self, payload: torch.Tensor) -> torch.Tensor:
+        """Producer half only (one launch); a consumer kernel given
+        ``self.peer`` as its wait reads the returned view."""
+        x, nbytes = self._check_payload(payload)
+        L.check(L.lib().srswa_peer_push(x.data_ptr(), nbytes, C.byref(self.peer), L.stream_of(x)), "srswa_peer_push")
+        return self.slots(x.shape, x.dtype)
+
+    def __call__(self, payload: torch.Tensor) -> torch.Tensor:
+        """Push + wait (two launches): the gathered [world, *payload.shape]."""
+        x, nbytes = self._check_payload(payload)
+        L.check(L.lib().srswa_peer_allgather(x.data_ptr(), nbytes, C.byref(self.peer), L.stream_of(x)),
+                "srswa_peer_allgather")
+        return self.slots(x.shape, x.dtype)
 
     def check(self):
         """Raise if a bounded wait expired (reads the device status: syncs)."""
