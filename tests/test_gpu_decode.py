@@ -130,11 +130,13 @@ def test_lse_merge_vs_oracle(cuda):
 
 
 
-@pytest.mark.parametrize("R", [70, 256])
+@pytest.mark.parametrize("R", [32, 70, 256])
 def test_decode_many_rows_split_last_wave(cuda, R):
     """Enough (row, head) items for several waves of CTAs: the rows of a
     nearly empty last wave are attended split over clusters (the split left
-    open), the others unsplit.  Same outputs and lse as every row unsplit
+    open), the others unsplit.  R = 32 (320 items: one wave unsplit, not
+    2-way split) takes the light-load instantiation (5 CTAs per SM, 2-way
+    split).  Same outputs and lse as every row unsplit
     (fp32, within 1e-5) and as the oracle on a sample of rows (1e-4).  Two
     KV heads and short requests keep the host-side cache small."""
     rng = np.random.default_rng(R)

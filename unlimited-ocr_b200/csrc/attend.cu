@@ -75,8 +75,11 @@ __device__ __forceinline__ int64_t block_offset(const AttendArgs& a, int64_t seq
   return seq * a.s_seq + blk * a.s_blk;
 }
 
-template <int D, int KVT>
-__global__ void __launch_bounds__(kAttendThreads) attend_rows_kernel(const AttendArgs a) {
+// MINB = CTAs per SM the register allocation must allow: 4 (128 registers)
+// for the bandwidth-bound loads; 5 (96 registers, a few spills) for light
+// loads, where a whole 2-way split then fits in one wave.
+template <int D, int KVT, int MINB>
+__global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const AttendArgs a) {
   constexpr int LPK = D / 8;     // lanes per key row
   constexpr int KPI = 32 / LPK;  // key rows per warp load instruction
   constexpr int KPC = KPI * 8;   // keys per chunk (8 loads per lane)
@@ -321,7 +324,7 @@ __global__ void __launch_bounds__(kAttendThreads) attend_rows_kernel(const Atten
   cluster.sync();
 }
 
-template <int D, int KVT>
+template <int D, int KVT, int MINB = 4>
 static int launch_attend(const AttendArgs& a, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = a.heads_inner ? dim3(static_cast<unsigned>(a.H * a.nsplit), static_cast<unsigned>(a.N), 1)
@@ -336,7 +339,7 @@ static int launch_attend(const AttendArgs& a, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attend_rows_kernel<D, KVT>, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attend_rows_kernel<D, KVT, MINB>, a);
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
 
@@ -350,28 +353,35 @@ static int launch_attend(const AttendArgs& a, cudaStream_t st) {
 // 160 items, 1 from 320 items up).  Smallest modelled time wins, by at least
 // 3 % over a smaller split.
 // Resident CTAs of the attend kernel per SM and the SM count (cached per device).
-static double attend_slots(int64_t D, int kv_dtype) {
-  static int sms[64] = {0}, per_sm[64][2][2] = {};
+// Resident CTAs of a kernel instantiation on the current device (cached per
+// device and instantiation).
+template <typename K>
+static double kernel_slots(K kern, int idx) {
+  static int sms[64] = {0}, per_sm[64][8] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   if (sms[dev] == 0) {
     int v = 0;
     sms[dev] = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0 ? v : 148;
   }
-  const int di = D == 128 ? 1 : 0, ki = kv_dtype == SRSWA_BF16 ? 1 : 0;
-  if (per_sm[dev][di][ki] == 0) {
+  if (per_sm[dev][idx] == 0) {
     int nb = 0;
-    cudaError_t e = cudaErrorInvalidValue;
-    if (D == 128)
-      e = ki ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<128, SRSWA_BF16>, kAttendThreads, 0)
-             : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<128, SRSWA_F16>, kAttendThreads, 0);
-    else
-      e = ki ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<64, SRSWA_BF16>, kAttendThreads, 0)
-             : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attend_rows_kernel<64, SRSWA_F16>, kAttendThreads, 0);
-    per_sm[dev][di][ki] = e == cudaSuccess && nb > 0 ? nb : 4;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kAttendThreads, 0);
+    per_sm[dev][idx] = e == cudaSuccess && nb > 0 ? nb : 4;
   }
-  return static_cast<double>(sms[dev]) * per_sm[dev][di][ki];
+  return static_cast<double>(sms[dev]) * per_sm[dev][idx];
 }
+
+static double attend_slots(int64_t D, int kv_dtype) {
+  if (D == 128)
+    return kv_dtype == SRSWA_BF16 ? kernel_slots(attend_rows_kernel<128, SRSWA_BF16, 4>, 0)
+                                  : kernel_slots(attend_rows_kernel<128, SRSWA_F16, 4>, 1);
+  return kv_dtype == SRSWA_BF16 ? kernel_slots(attend_rows_kernel<64, SRSWA_BF16, 4>, 2)
+                                : kernel_slots(attend_rows_kernel<64, SRSWA_F16, 4>, 3);
+}
+
+// The light-load instantiation (5 CTAs per SM), bf16, head dim 128.
+static double attend_slots_light() { return kernel_slots(attend_rows_kernel<128, SRSWA_BF16, 5>, 4); }
 
 static int auto_nsplit(const AttendArgs& a, int64_t D, int kv_dtype) {
   const double slots = attend_slots(D, kv_dtype);
@@ -438,7 +448,19 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   a.nsplit = nsplit;
   a.heads_inner = (a.N <= 65535 && a.H * 8 <= 65535) ? 1 : 0;
   if (D == 128) {
-    if (kv_dtype == SRSWA_BF16) return launch_attend_rows<128, SRSWA_BF16>(a, st);
+    if (kv_dtype == SRSWA_BF16) {
+      // A light load that one wave holds unsplit but not 2-way split (e.g.
+      // 32 requests x 10 heads per GPU): with 5 CTAs per SM the 2-way split
+      // fits in one wave, halving each CTA's keys.
+      const double items = static_cast<double>(a.N) * a.H;
+      if (a.split_tail && nsplit == 1 && items <= attend_slots(D, kv_dtype) &&
+          2.0 * items > attend_slots(D, kv_dtype) && 2.0 * items <= attend_slots_light()) {
+        a.nsplit = 2;
+        a.split_tail = 0;
+        return launch_attend<128, SRSWA_BF16, 5>(a, st);
+      }
+      return launch_attend_rows<128, SRSWA_BF16>(a, st);
+    }
     return launch_attend_rows<128, SRSWA_F16>(a, st);
   }
   if (kv_dtype == SRSWA_BF16) return launch_attend_rows<64, SRSWA_BF16>(a, st);
