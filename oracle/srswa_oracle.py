@@ -509,6 +509,80 @@ def gather_block_bwd(q_b, k_b, v_b, do_b, o_b, lse_b, sel_b, seg_b, c, block_siz
     return dk, dv
 
 
+# ---------------------------------------------------------------------------
+# f4: DSA gather-KL distillation (training stage "sparse", one index head)
+# ---------------------------------------------------------------------------
+def _kl_row_keys(sel_row, pos, seg, block_size, local_window, Sk):
+    """Keys of one query row in the KL: the selected blocks' keys (a repeated
+    block counts once) below the local window start and not in the future,
+    same segment: the token-level keep of _kl_chunk_core
+    (_sparse_base_impl.py:2071-2120) for keep_block = the row's blocks."""
+    ls = max(int(pos) - (int(local_window) - 1), 0)
+    out, seen = [], set()
+    for b in np.asarray(sel_row).tolist():
+        if b < 0 or b in seen:
+            continue
+        seen.add(b)
+        j = np.arange(b * block_size, min((b + 1) * block_size, Sk))
+        out.append(j[(j <= pos) & (j < ls) & (j >= seg)])
+    return np.concatenate(out).astype(np.int64) if out else np.zeros(0, np.int64)
+
+
+def _bf16_if(x, flag):
+    return bf16_round(x) if flag else x
+
+
+def gather_kl(idx_q, idx_k, q_main, k_main, sel, pos, seg, block_size, local_window, scaling, bf16_logits=True,
+              g=None):
+    """Per-row KL(P_teacher || P_student) over each query row's selected
+    remote keys, and (with g, dLoss/dkl per row) its gradients to the index
+    q / k.  _kl_chunk_core and the gather branch of select_and_kl_loss
+    (hf-model-code/_sparse_base_impl.py:2071-2137, 3397-3450):
+      student s_j = idx_q . idx_k[j] (bf16 matmul output when the index
+      tensors are bf16), log-softmax over the row's kept keys;
+      teacher t_hj = (q_main[h] . k_main[j, h // group]) (bf16 output) *
+      scaling, softmax per head over the same keys, averaged over the heads;
+      kl = sum_j p_j (log max(p_j, 1e-12) - log p_idx_j); valid = any key.
+    idx_q [B,C,d], idx_k [B,Sk,d], q_main [B,C,H,D], k_main [B,Sk,Hkv,D],
+    sel [B,C,S] (-1 pad), pos / seg [B,C] (global position, segment start).
+    Returns (kl [B,C], valid [B,C]) or, with g [B,C], also (d_idx_q
+    [B,C,d], d_idx_k [B,Sk,d]): ds_j = g (P p_idx_j - p_j) on kept keys,
+    P = sum of p over them."""
+    B, C, d = idx_q.shape
+    Sk = idx_k.shape[1]
+    H, Hkv = q_main.shape[2], k_main.shape[2]
+    G = H // Hkv
+    kl = np.zeros((B, C), F32)
+    valid = np.zeros((B, C), bool)
+    dq = np.zeros(idx_q.shape, F32) if g is not None else None
+    dk = np.zeros(idx_k.shape, F32) if g is not None else None
+    for b in range(B):
+        for c in range(C):
+            keys = _kl_row_keys(sel[b, c], pos[b, c], 0 if seg is None else seg[b, c], block_size, local_window, Sk)
+            if len(keys) == 0:
+                continue
+            valid[b, c] = True
+            s = _bf16_if((idx_k[b, keys].astype(F32) @ idx_q[b, c].astype(F32)).astype(F32), bf16_logits)
+            lse_s = s.max() + np.log(np.exp(s - s.max()).sum(dtype=F32))
+            logp_idx = (s - lse_s).astype(F32)
+            p = np.zeros(len(keys), F32)
+            for h in range(H):
+                t = _bf16_if((k_main[b, keys, h // G].astype(F32) @ q_main[b, c, h].astype(F32)).astype(F32),
+                             bf16_logits) * F32(scaling)
+                e = np.exp(t - t.max()).astype(F32)
+                p += e / e.sum(dtype=F32)
+            p /= F32(H)
+            kl[b, c] = (p * (np.log(np.maximum(p, F32(1e-12))) - logp_idx)).sum(dtype=F32)
+            if g is not None:
+                p_idx = np.exp(logp_idx).astype(F32)
+                ds = (F32(g[b, c]) * (p.sum(dtype=F32) * p_idx - p)).astype(F32)
+                dq[b, c] = ds @ idx_k[b, keys].astype(F32)
+                np.add.at(dk[b], keys, ds[:, None] * idx_q[b, c].astype(F32)[None, :])
+    if g is None:
+        return kl, valid
+    return kl, valid, dq, dk
+
+
 def decode_attend(q, k_all, v_all, topi, bias, valid, q_pos, block_size, local_window, scale):
     """``_decode_attend`` (hf-model-code/modeling_deepseekv2.py:455-481), fp32.
 

@@ -423,6 +423,47 @@ def case_paged_prefill(sgl):
          fit=fit, params=np.array([BS, L, topm, budget, dql, 4]), fparams=np.array([5.0, 1e-3, 1.0, 0.125]))
 
 
+def case_gather_kl(m):
+    """DSA sparse-stage KL distillation: _kl_chunk_core (the KL of
+    select_and_kl_loss over the selected blocks, one index head) in bf16 with
+    its autograd gradients to the index q / k; batch 0 unpacked, batch 1
+    packed (two samples, cross-sample keys dropped through same_seg)."""
+    sb = importlib.import_module("uocr_ref._sparse_base_impl")
+    g = torch.Generator().manual_seed(31)
+    B, C, H, Hkv, D, d, BS, LW, S = 2, 300, 4, 2, 32, 32, 16, 48, 5
+    nblk = (C + BS - 1) // BS
+    q_main = torch.randn(B, H, C, D, generator=g).to(torch.bfloat16)
+    k_main = torch.randn(B, Hkv, C, D, generator=g).to(torch.bfloat16)
+    idx_q = (torch.randn(B, 1, C, d, generator=g) * 0.3).to(torch.bfloat16)
+    idx_k = (torch.randn(B, 1, C, d, generator=g) * 0.3).to(torch.bfloat16)
+    pos = torch.arange(C)[None].repeat(B, 1)
+    seg_start = torch.zeros(B, C, dtype=torch.long)
+    seg_start[1, 170:] = 170                      # batch 1: a second sample from token 170
+    sel = torch.full((B, C, S), -1, dtype=torch.long)
+    for b in range(B):
+        for c in range(C):
+            cands = torch.arange(0, max(c // BS, 0))
+            if len(cands):
+                pick = cands[torch.randperm(len(cands), generator=g)[:S]]
+                sel[b, c, :len(pick)] = pick
+    sel[0, 200, 2] = sel[0, 200, 0]              # a repeated block counts once
+    keep_block = torch.zeros(B, 1, C, nblk + 1, dtype=torch.bool)
+    keep_block.scatter_(-1, sel.masked_fill(sel < 0, nblk)[:, None], True)
+    keep_block = keep_block[..., :nblk]
+    kpos = torch.arange(C)
+    same_seg = (kpos[None, None, :] >= seg_start[:, :, None])[:, None]    # [B,1,C,Sk]
+    scaling = 1.0 / math.sqrt(D)
+    qi = idx_q.clone().requires_grad_(True)
+    ki = idx_k.clone().requires_grad_(True)
+    kl = sb._kl_chunk_core(qi, ki, q_main, k_main, keep_block, pos, BS, scaling, H, H // Hkv, LW, same_seg)
+    gout = torch.randn(kl.shape, generator=g)
+    kl.backward(gout)
+    save("gather_kl", idx_q=idx_q.float()[:, 0], idx_k=idx_k.float()[:, 0], q_main=q_main.float().transpose(1, 2),
+         k_main=k_main.float().transpose(1, 2), sel=sel, pos=pos, seg=seg_start, kl=kl.detach()[:, 0],
+         gout=gout[:, 0], d_idx_q=qi.grad.float()[:, 0], d_idx_k=ki.grad.float()[:, 0],
+         params=np.array([BS, LW]), scaling=np.array(scaling))
+
+
 PAGE_IMG, PAGE_MARK = 128815, 128827   # config.json image_token_id, page_token_id
 
 
@@ -639,7 +680,7 @@ def case_page_rope(m):
 # cases run on the SGLang ops of the wheel; all others on the HF modules
 _SGL_CASES = {"paged", "paged_prefill"}
 _ORDER = ("route", "entmax", "decode_attend", "forward_dense", "gather_triton", "gather_e2e", "block_max",
-          "paged", "paged_prefill", "page_gate", "page_rope")
+          "paged", "paged_prefill", "page_gate", "page_rope", "gather_kl")
 
 
 def main():

@@ -365,3 +365,18 @@ def test_paged_prefill_golden():
         assert set(ref) == set(mine), n
         for b in ref:
             assert abs(ref[b] - mine[b]) < 1e-4, (n, b)
+
+
+def test_gather_kl_golden():
+    """DSA sparse-stage KL distillation (_kl_chunk_core, one index head) and
+    its gradients to the index q / k: the oracle restatement against the
+    reference's own bf16 outputs (packed batch included)."""
+    g = golden("gather_kl")
+    BS, LW = (int(x) for x in g["params"])
+    kl, valid, dq, dk = O.gather_kl(g["idx_q"], g["idx_k"], g["q_main"], g["k_main"], g["sel"], g["pos"], g["seg"],
+                                    BS, LW, float(g["scaling"]), bf16_logits=True, g=g["gout"])
+    np.testing.assert_allclose(kl, g["kl"], rtol=1e-3, atol=1e-4)
+    assert (g["kl"][~valid] == 0).all()
+    # the reference's gradients pass through bf16 casts: bf16 tolerance
+    np.testing.assert_allclose(dq, g["d_idx_q"], rtol=1e-2, atol=2e-2)
+    np.testing.assert_allclose(dk, g["d_idx_k"], rtol=1e-2, atol=2e-2)
