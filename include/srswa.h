@@ -371,6 +371,41 @@ SRSWA_API int srswa_lse_merge(const float* o_parts, const float* lse_parts, int6
                     int64_t H, int64_t D, int64_t s_o_part, int64_t s_l_part, void* out,
                     int out_dtype, float* lse_out, const srswa_peer* wait, srswa_stream_t stream);
 
+/* ------------------------------------------------------------------ f4 --
+ * DSA gather-KL distillation (training stage "sparse", one index head).
+ * Per query row (b, c): KL(P || P_idx) over the keys of the row's selected
+ * blocks sel [B,C,S] (int32, -1 pad; a repeated block counts once) that lie
+ * in [seg, pos] and below max(pos - LW + 1, 0): P_idx = softmax of
+ * idx_q . idx_k[j], P = the mean over the H main heads of the softmaxes of
+ * (q_main[h] . k_main[j, h / (H/Hkv)]) * scaling; both logits rounded to bf16
+ * first when logits_bf16 (the reference's bf16 matmul outputs).
+ * idx_q [B,C,d], idx_k [B,Sk,d], q_main [B,C,H,D], k_main [B,Sk,Hkv,D] (the
+ * strides below; features contiguous; any of f32 / bf16 / f16), pos / seg
+ * [B,C] int64 (global position, segment start; seg may be NULL = 0); d, D
+ * multiples of 8 up to 128; block_size <= 64, S * block_size <= 2048.
+ * fwd -> kl [B,C] fp32 (0 for rows with no key), valid [B,C] uint8.
+ * bwd: grad [B,C] = dLoss/dkl per row -> d_idx_q [B,C,d], d_idx_k [B,Sk,d]
+ * fp32 (contiguous, fully written; deterministic, no atomics); workspace of
+ * srswa_gather_kl_bwd_workspace_size bytes.  Replaces the gather-KL of
+ * select_and_kl_loss and _kl_chunk_core / _KLChunkFn
+ * (hf-model-code/_sparse_base_impl.py:3397-3450, 2071-2191). */
+typedef struct {
+  int64_t B, C, Sk, H, Hkv, D, d, S, block_size, local_window;
+  float scaling;
+  int logits_bf16;
+  int iq_dtype, ik_dtype, qm_dtype, km_dtype;
+  int64_t s_iq_b, s_iq_c, s_ik_b, s_ik_s, s_qm_b, s_qm_c, s_qm_h, s_km_b, s_km_s, s_km_h;
+} srswa_kl_desc;
+
+SRSWA_API int srswa_gather_kl_fwd(const srswa_kl_desc* g, const void* idx_q, const void* idx_k, const void* q_main,
+                        const void* k_main, const int32_t* sel, const int64_t* pos, const int64_t* seg,
+                        float* kl, uint8_t* valid, srswa_stream_t stream);
+SRSWA_API size_t srswa_gather_kl_bwd_workspace_size(const srswa_kl_desc* g);
+SRSWA_API int srswa_gather_kl_bwd(const srswa_kl_desc* g, const void* idx_q, const void* idx_k, const void* q_main,
+                        const void* k_main, const int32_t* sel, const int64_t* pos, const int64_t* seg,
+                        const float* grad, float* d_idx_q, float* d_idx_k, void* workspace,
+                        size_t workspace_bytes, srswa_stream_t stream);
+
 /* --------------------------------------------------- peer exchange ------
  * All-gather through peer memory for the split-KV decode across the GPUs of
  * one node (the two exchanges per layer of the reference plan's per-GPU

@@ -21,7 +21,7 @@ ROOT = os.path.dirname(PKG)
 OUT = os.path.join(PKG, "srswa", "libsrswa.so")
 BUILD = os.path.join(HERE, "_build")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-SOURCES = ["api.cu", "route.cu", "attend.cu", "gather.cu", "gather_tc.cu", "page_gate.cu", "peer.cu"]
+SOURCES = ["api.cu", "route.cu", "attend.cu", "gather.cu", "gather_tc.cu", "page_gate.cu", "peer.cu", "kl.cu"]
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -46,6 +46,14 @@ class DecodeDesc(C.Structure):
                 ("s_b_h", i64), ("s_b_n", i64), ("nsplit", C.c_int), ("skip_local", C.c_int)]
 
 
+class KlDesc(C.Structure):
+    _fields_ = [(n, i64) for n in ("B", "C", "Sk", "H", "Hkv", "D", "d", "S", "block_size", "local_window")] + \
+               [("scaling", C.c_float), ("logits_bf16", C.c_int), ("iq_dtype", C.c_int), ("ik_dtype", C.c_int),
+                ("qm_dtype", C.c_int), ("km_dtype", C.c_int)] + \
+               [(n, i64) for n in ("s_iq_b", "s_iq_c", "s_ik_b", "s_ik_s", "s_qm_b", "s_qm_c", "s_qm_h", "s_km_b",
+                                   "s_km_s", "s_km_h")]
+
+
 class Peer(C.Structure):
     """srswa_peer: one peer-memory exchange region (device pointers)."""
     _fields_ = [("regions", vp), ("own_region", vp), ("slot_bytes", i64), ("rank", i64), ("world", i64),
@@ -96,6 +104,10 @@ _SIGS = {
                                            C.c_size_t, vp]),
     "srswa_decode_allow": (C.c_int, [vp, i64, i64, i64, vp, vp, i64, i64, vp, vp, i64, vp, vp]),
     "srswa_win_bounds_decode": (C.c_int, [vp, i64, i64, vp, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp]),
+    "srswa_gather_kl_fwd": (C.c_int, [C.POINTER(KlDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "srswa_gather_kl_bwd_workspace_size": (C.c_size_t, [C.POINTER(KlDesc)]),
+    "srswa_gather_kl_bwd": (C.c_int, [C.POINTER(KlDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t,
+                                      vp]),
     "srswa_peer_region_size": (C.c_int, [i64, i64, C.POINTER(C.c_size_t)]),
     "srswa_peer_region_alloc": (C.c_int, [C.c_size_t, C.POINTER(vp)]),
     "srswa_peer_region_free": (C.c_int, [vp]),

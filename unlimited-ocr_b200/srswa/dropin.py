@@ -8,6 +8,8 @@ After ``install``:
   * ``<pkg>.sparse_gather_e2e_triton``  -> ``srswa.sparse_gather_e2e``
   * ``<pkg>.modeling_deepseekv2._block_scores_infer / _infer_route_select /
     _decode_attend`` -> ``srswa.dash_infer`` (when that module is loaded)
+  * ``DeepseekV2Indexer.select_and_kl_loss`` -> ``srswa.dsa`` (one index
+    head on CUDA; other cases keep the reference's method)
   * the PageGate candidate methods of ``<pkg>._sparse_base_impl.DeepseekV2Indexer``,
     ``modeling_deepseekv2._dash_block_cand`` and
     ``modeling_unlimitedocr._uocr_dash_decode_allow`` -> ``srswa.page_gate``
@@ -23,7 +25,7 @@ from __future__ import annotations
 
 import sys
 
-from . import dash_infer, page_gate, page_rope, paged, sparse_gather, sparse_gather_e2e
+from . import dash_infer, dsa, page_gate, page_rope, paged, sparse_gather, sparse_gather_e2e
 
 _INDEXER_METHODS = ("_build_page_aware_ids", "_build_flat_image_token_mask", "_build_image_block_allow_mask",
                     "_build_page_aware_image_block_mask", "_build_kl_candidate_mask")
@@ -50,6 +52,9 @@ def install(pkg: str) -> None:
         page_gate._scope_source = base      # _PAGE_SCOPE_PREFILL stays the reference's switch
         if ix is not None:
             ix._build_page_rope_pos = page_rope._build_page_rope_pos
+            if ix.select_and_kl_loss is not dsa.select_and_kl_loss:   # the reference's, for the cases it keeps
+                dsa._ORIGINAL[ix] = ix.select_and_kl_loss
+            ix.select_and_kl_loss = dsa.select_and_kl_loss
         rot = getattr(base, "DeepseekV2IndexerRotary2D", None)
         if rot is not None:
             rot.forward = page_rope.rotary2d_forward
