@@ -906,17 +906,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
   const int M = static_cast<int>(a.M);
   const int64_t nch = gridDim.x;
   if (warp == 0) warp_topm_smem(keys, kChunkBlocks, M, chunk_out + (n * nch + blockIdx.x) * M, lane);
-  if (nch == 1 && keys_out == nullptr) {  // the row's selection right here (whole-row router)
-    __syncthreads();
-    if (warp == 0) {
-      float sel_v = 0.f;
-      int sel_i = -1;
-      bool sel_c = false;
-      if (lane < M) unpack_key(chunk_out[n * M + lane], sel_v, sel_i, sel_c);
-      route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
-    }
-    return;
-  }
   if (nch == 1) {  // chunk_out is the row's output
     if (push.regions) {  // and this rank's keys of the row go to every peer
       __syncthreads();
@@ -938,17 +927,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
   for (int64_t i = tid; i < total; i += kRouteThreads) mk[i] = __ldcg(src + i);
   __syncthreads();
   const unsigned long long mine = block_topm(mk, total, M, lists, warp, lane);
-  if (keys_out == nullptr) {  // whole-row router: the selection epilogue of the merged top-M
-    if (tid == 0) counters[n] = 0u;
-    if (warp == 0) {
-      float sel_v = 0.f;
-      int sel_i = -1;
-      bool sel_c = false;
-      if (lane < M) unpack_key(mine, sel_v, sel_i, sel_c);
-      route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
-    }
-    return;
-  }
   if (warp == 0 && lane < M) {
     keys_out[n * M + lane] = mine;
     if (push.regions) peer_put8(push, (n * M + lane) * 8, mine);  // this rank's keys of the row, to every peer
@@ -1367,46 +1345,12 @@ static int route_chunk_launch(RouteArgs a, void* ws, size_t ws_bytes, cudaStream
   return select_wide_launch(a, z, a.nblk, st);
 }
 
-// Few decode rows (fewer than the SMs): one launch of route_chunk_keys_kernel
-// over (row, 128-block chunk) CTAs, each keeping its chunk's top-M; the last
-// CTA of a row merges the row's lists and runs the selection epilogue.  The
-// top-M of the row is inside the union of the chunks' top-Ms, so the result
-// equals the score + wide-select path; it only spreads the selection over
-// the chunks' CTAs where one CTA per row would leave most SMs idle.
-static int route_keys_launch(RouteArgs a, void* ws, size_t ws_bytes, cudaStream_t st) {
-  const int64_t nch = (a.nblk + kChunkBlocks - 1) / kChunkBlocks;
-  const size_t cnt_bytes = (static_cast<size_t>(a.N) * 4 + 255) & ~static_cast<size_t>(255);
-  const size_t need = cnt_bytes + static_cast<size_t>(a.N * nch * a.M) * 8;
-  if (!ws || ws_bytes < need) return SRSWA_EWORKSPACE;
-  unsigned int* counters = static_cast<unsigned int*>(ws);
-  unsigned long long* ck = reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + cnt_bytes);
-  SRSWA_CUDA_TRY(cudaMemsetAsync(counters, 0, static_cast<size_t>(a.N) * 4, st));
-  const size_t smem = static_cast<size_t>(nch * a.M) * 8;
-  if (smem > 40 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(route_chunk_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return static_cast<int>(e);
-  }
-  const srswa_peer none = {};
-  route_chunk_keys_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(a.N)), kRouteThreads, smem, st>>>(
-      a, 0, a.nblk, ck, counters, nullptr, none);
-  return srswa_last_launch_status();
-}
-
-static bool use_keys_path(const RouteArgs& a) {
-  const int64_t nch = (a.nblk + kChunkBlocks - 1) / kChunkBlocks;
-  return a.cand == nullptr && a.scores_out == nullptr && a.N < 148 && nch > 1 && nch * a.M <= kMergeMaxKeys;
-}
-
 static int route_launch(RouteArgs a, cudaStream_t st, void* ws = nullptr, size_t ws_bytes = 0) {
   if (a.N == 0) return 0;
   // prefill rows: many rows of one sequence sharing a contiguous k_bar
   if (use_tile(a)) return route_tile_launch(a, st);
   // decode-shaped rows with many candidate blocks -> chunked score + merge
-  if (use_chunked(a)) {
-    if (use_keys_path(a) && ws && ws_bytes >= chunk_workspace(a.N, a.nblk)) return route_keys_launch(a, ws, ws_bytes, st);
-    return route_chunk_launch(a, ws, ws_bytes, st);
-  }
+  if (use_chunked(a)) return route_chunk_launch(a, ws, ws_bytes, st);
   if (a.from_scores && use_wide(a)) return select_wide_launch(a, a.scores_in, a.s_sc, st);
   int rpc = 1;
   while (rpc < 8 && a.nblk * rpc * 2 <= 2048) rpc *= 2;
