@@ -65,8 +65,9 @@ def parse():
                          "pagegate = PageGate candidate masks of a cfg2-shaped prefill; "
                          "rope = page2d RoPE coordinates + fused rotary of a cfg2-shaped prefill")
     ap.add_argument("--layers", type=int, default=12, help="longctx: decoder layers")
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
-                    help="longctx with N > 1: peer-memory exchange (default) or NCCL all-gathers")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "p2p-launch", "nccl"],
+                    help="longctx with N > 1: peer-memory exchange fused into the router / merge kernels "
+                         "(default), the same exchange as separate push + wait launches, or NCCL all-gathers")
     ap.add_argument("--batch", type=int, default=0, help="prefill/train batch override (smaller cases)")
     ap.add_argument("--seq", type=int, default=0, help="prefill/train sequence override")
     return ap.parse_args()
@@ -890,9 +891,10 @@ def longctx_measure(args):
     gen = torch.Generator().manual_seed(4 * 100 + rank)
     decs, layers = [], []
     backend = None
-    if world > 1 and args.exchange == "p2p":
+    if world > 1 and args.exchange != "nccl":
         from srswa.split_kv import PeerBackend
-        backend = PeerBackend(rows=1, topm=M, heads=H, head_dim=D)   # one for all layers
+        backend = PeerBackend(rows=1, topm=M, heads=H, head_dim=D,   # one for all layers
+                              fused=args.exchange == "p2p")
     pool = torch.randn(64 << 20, generator=gen).to(torch.bfloat16).to(dev)
     hc = torch.zeros(DI, device=dev)
     for _ in range(nl):
@@ -978,7 +980,8 @@ def longctx_measure(args):
             "ms_per_step": ms, "us_per_step": ms * 1e3, "scaling": "strong", "dtype": "bf16",
             "config": {"workload": "cfg5 attention share: 12-layer split-KV decode, one 1M-token sequence",
                        "seq_len": S0, "layers": nl, "K": K, "LW": L * BS, "parallelism": f"split-kv{world}",
-                       "exchange": ("peer-memory push + bounded flag wait (CUDA IPC over NVLink)"
+                       "exchange": (("peer-memory push + bounded flag wait (CUDA IPC over NVLink), "
+                                     + ("in the router / merge kernels" if backend.fused else "own launches"))
                                     if backend is not None else ("NCCL all-gather" if world > 1 else "none")),
                        "l2": "flushed before every timed step", "graph": not args.no_graph},
             "roofline": {"bound": "latency", "achieved": byts / (ms * 1e-3) / 1e9, "peak": hbm * world,

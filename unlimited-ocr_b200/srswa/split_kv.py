@@ -139,33 +139,39 @@ class PeerBackend(CudaBackend):
     alternate, which keeps a rank from overwriting data a peer still reads).
     rows / topm / heads / head_dim bound the payloads."""
 
-    def __init__(self, group=None, *, rows, topm, heads, head_dim):
+    def __init__(self, group=None, *, rows, topm, heads, head_dim, fused=True):
         super().__init__(group)
         from .peer import PeerAllGather
+        self.fused = fused
         self.keys_x = PeerAllGather(rows * topm * 8, group)
         self.part_x = PeerAllGather(-(-(rows * heads * head_dim + rows * heads) // 4) * 16, group)
 
-    # the router's shard kernel pushes its keys into every peer's region itself
+    # fused: the router's shard kernel pushes its keys into every peer's
+    # region itself, the key merge and the log-sum-exp merge wait themselves;
+    # else each exchange is a push launch + a wait launch
     def shard_keys(self, idx_q, layer, plan, q_pos, rp):
         return self.ops.route_shard_keys(
             idx_q, layer["kbar"], block_offset=plan.lo, nblk_local=plan.hi - plan.lo,
             nblk_total=plan.nblk_total, q_pos=q_pos, rows_per_seq=idx_q.shape[0],
-            block_table=layer.get("kbar_table"), push=self.keys_x.peer, **rp)
+            block_table=layer.get("kbar_table"), push=self.keys_x.peer if self.fused else None, **rp)
 
     def gather_keys(self, keys, world):
+        if not self.fused:
+            return self.keys_x(keys)
         return self.keys_x.slots(keys.shape, keys.dtype)   # filled by the peers' shard kernels
 
-    # and the key merge waits for the peers' keys itself
     def merge_keys(self, keys, plan, rp):
         p = {k: v for k, v in rp.items() if k not in ("block_size", "local_blocks")}
         return self.ops.route_merge_keys(keys, nblk_total=plan.nblk_total, own=(plan.lo, plan.hi),
-                                         want=("topi32", "bias"), wait=self.keys_x.peer, **p)
+                                         want=("topi32", "bias"), wait=self.keys_x.peer if self.fused else None,
+                                         **p)
 
     def gather_partials(self, buf, world):
-        return self.part_x.push(buf)                        # one push launch; lse_merge waits
+        return self.part_x.push(buf) if self.fused else self.part_x(buf)
 
     def lse_merge(self, o_parts, lse_parts, out_dtype):
-        return self.ops.lse_merge(o_parts, lse_parts, out_dtype=out_dtype, wait=self.part_x.peer)[0]
+        return self.ops.lse_merge(o_parts, lse_parts, out_dtype=out_dtype,
+                                  wait=self.part_x.peer if self.fused else None)[0]
 
     def check(self):
         self.keys_x.check()
