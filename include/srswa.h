@@ -207,6 +207,24 @@ SRSWA_API int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int64
                            int32_t* topi32, float* bias, uint8_t* valid, int64_t own_lo,
                            int64_t own_hi, int32_t* topi32_own, const srswa_peer* wait,
                            srswa_stream_t stream);
+/* Both stages in one launch: stage 1 as srswa_route_shard_keys (same
+ * arguments and workspace), then the last CTA of each row merges the lists
+ * and writes the outputs of srswa_route_merge_keys.  exchange NULL: this
+ * shard covers [0, nblk_total) alone.  exchange given: that CTA pushes the
+ * row's keys into every region of the exchange, waits (bounded, status 501
+ * on expiry) for every rank's keys in its own region and merges the world
+ * lists; every rank of the exchange makes the same call.  N <= 128 with an
+ * exchange (each waiting CTA stays resident), else SRSWA_ETOOLARGE.  No
+ * reference counterpart: it fuses the two stages above and the key
+ * all-gather between them. */
+SRSWA_API int srswa_route_shard_select(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
+                           const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk_local,
+                           int64_t block_offset, int64_t nblk_total, const int32_t* block_table,
+                           int64_t s_bt, const int32_t* seq_lens, int64_t rows_per_seq,
+                           const int64_t* q_pos, srswa_route_params params, int64_t* topi64,
+                           int32_t* topi32, float* bias, uint8_t* valid, int64_t own_lo, int64_t own_hi,
+                           int32_t* topi32_own, void* workspace, size_t workspace_bytes,
+                           const srswa_peer* exchange, srswa_stream_t stream);
 
 /* ------------------------------------------------------------------ a3 --
  * Token block-max scores.  q [B,C,D] (strides), k [B,Sk,D], pos/seg [B,C]

@@ -63,6 +63,37 @@ def test_sharded_route_equals_whole_row(cuda, nblk, nshard, paged):
         torch.testing.assert_close(merged["bias"], full["bias"], rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("nblk,exchange", [(16384, False), (16384, True), (100, False), (100, True),
+                                            (3000, True)])
+def test_shard_select_equals_two_stages(cuda, nblk, exchange):
+    """srswa_route_shard_select (one launch: shard keys, optional exchange of
+    one rank, merge and epilogue) = shard keys + merge, bit for bit."""
+    from srswa.peer import PeerAllGather
+    g = torch.Generator(device="cuda").manual_seed(nblk + 3)
+    d, N = 128, 3
+    kbar = torch.randn(1, nblk, d, device=cuda, generator=g)
+    idx_q = torch.randn(N, d, device=cuda, generator=g).to(torch.bfloat16)
+    S = nblk * 64
+    q_pos = torch.tensor([S - 1, S // 3, 9 * 64 + 1], device=cuda, dtype=torch.int64)
+    p = {k: v for k, v in RP.items() if k not in ("block_size", "local_blocks")}
+    own = (nblk // 4, nblk // 2)
+    ex = PeerAllGather(N * RP["topm"] * 8, None, cuda) if exchange else None
+    for rep in range(3):   # the exchange's epochs advance from call to call
+        keys = ops.route_shard_keys(idx_q, kbar, block_offset=0, nblk_local=nblk, nblk_total=nblk, q_pos=q_pos,
+                                    rows_per_seq=N, **RP)
+        two = ops.route_merge_keys(keys[None], nblk_total=nblk, own=own,
+                                   want=("topi64", "topi32", "bias", "valid"), **p)
+        one = ops.route_shard_select(idx_q, kbar, block_offset=0, nblk_local=nblk, nblk_total=nblk, q_pos=q_pos,
+                                     rows_per_seq=N, own=own, want=("topi64", "topi32", "bias", "valid"),
+                                     exchange=None if ex is None else ex.peer, **RP)
+        torch.cuda.synchronize()
+        for name in ("topi64", "topi32", "bias", "valid", "topi32_own"):
+            assert torch.equal(one[name], two[name]), name
+    if ex is not None:
+        ex.check()
+        ex.close()
+
+
 def test_sharded_attend_equals_single_call(cuda):
     g = torch.Generator(device="cuda").manual_seed(11)
     nblk, BS, H, Hkv, D, d, nshard = 4096, 64, 10, 10, 128, 128, 4

@@ -607,69 +607,9 @@ __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v,
 __device__ __forceinline__ unsigned long long max_u64(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
 __device__ __forceinline__ unsigned long long min_u64(unsigned long long a, unsigned long long b) { return a > b ? b : a; }
 
-// Top-M (M <= 32) of unique keys held in registers, NPL per lane, by one warp,
-// with the same result as warp_topm_regs.  The M-th largest of the 32 lane
-// maxima (bitonic sort across the lanes) is a lower bound of the M-th largest
-// key, since at least M keys reach it; the keys at or above it (normally a
-// few more than M) go to the warp's 64-entry scratch and one bitonic sort
-// orders them: 32 keys, one per lane, when at most 32 survive (the usual
-// case), else 64 keys, two per lane.  More than 64 such keys: the
-// round-based warp_topm_regs.
-template <int NPL>
-__device__ __forceinline__ unsigned long long warp_topm_filtered(unsigned long long (&v)[NPL], int M, int lane,
-                                                               unsigned long long* scratch) {
-  unsigned long long lm = 0ull;
-#pragma unroll
-  for (int k = 0; k < NPL; ++k) lm = max_u64(lm, v[k]);
-  // lane i <- the i-th largest lane maximum (descending bitonic sort of 32)
-  unsigned long long srt = lm;
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const unsigned long long p = shfl_xor_u64(srt, j);
-      const bool take_max = ((lane & j) == 0) == ((lane & k) == 0);
-      srt = take_max ? max_u64(srt, p) : min_u64(srt, p);
-    }
-  }
-  const uint32_t t_lo = __shfl_sync(0xffffffffu, static_cast<uint32_t>(srt), M - 1);
-  const uint32_t t_hi = __shfl_sync(0xffffffffu, static_cast<uint32_t>(srt >> 32), M - 1);
-  const unsigned long long t0 = (static_cast<unsigned long long>(t_hi) << 32) | t_lo;
-  // survivors: nonzero keys >= t0; exclusive prefix of the lanes' counts
-  int cnt = 0;
-#pragma unroll
-  for (int k = 0; k < NPL; ++k) cnt += (v[k] != 0ull && v[k] >= t0) ? 1 : 0;
-  int incl = cnt;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  const int total = __shfl_sync(0xffffffffu, incl, 31);
-  if (total > 64) return warp_topm_regs<NPL>(v, M, lane);  // warp-uniform
-  int pos = incl - cnt;
-#pragma unroll
-  for (int k = 0; k < NPL; ++k)
-    if (v[k] != 0ull && v[k] >= t0) scratch[pos++] = v[k];
-  if (total <= 32) {  // warp-uniform: one key per lane, a 32-key descending bitonic sort
-    __syncwarp();
-    unsigned long long e = lane < total ? scratch[lane] : 0ull;
-    __syncwarp();
-#pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-      for (int j = k >> 1; j > 0; j >>= 1) {
-        const unsigned long long p = shfl_xor_u64(e, j);
-        const bool take_max = ((lane & j) == 0) == ((lane & k) == 0);
-        e = take_max ? max_u64(e, p) : min_u64(e, p);
-      }
-    }
-    return lane < M ? e : 0ull;
-  }
-  for (int i = total + lane; i < 64; i += 32) scratch[i] = 0ull;
-  __syncwarp();
-  unsigned long long e0 = scratch[lane], e1 = scratch[lane + 32];  // element i = 32 * slot + lane
-  __syncwarp();
+// Descending bitonic sort of 64 keys held two per lane (element i = 32 *
+// slot + lane: e0 = slot 0, e1 = slot 1).
+__device__ __forceinline__ void bitonic64_desc(unsigned long long& e0, unsigned long long& e1, int lane) {
 #pragma unroll
   for (int k = 2; k <= 64; k <<= 1) {
 #pragma unroll
@@ -687,20 +627,109 @@ __device__ __forceinline__ unsigned long long warp_topm_filtered(unsigned long l
       }
     }
   }
+}
+
+// Descending bitonic sort of 32 keys, one per lane.
+__device__ __forceinline__ unsigned long long bitonic32_desc(unsigned long long e, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const unsigned long long p = shfl_xor_u64(e, j);
+      const bool take_max = ((lane & j) == 0) == ((lane & k) == 0);
+      e = take_max ? max_u64(e, p) : min_u64(e, p);
+    }
+  }
+  return e;
+}
+
+// Second half of the threshold top-M: the keys >= t0 (t0 a lower bound of
+// the M-th largest key) go to the warp's 64-entry scratch and one bitonic
+// sort orders them: 32 keys, one per lane, when at most 32 survive, else 64
+// keys, two per lane.  More than 64 such keys: the round-based
+// warp_topm_regs.  Lane m returns the m-th key.
+template <int NPL>
+__device__ __forceinline__ unsigned long long topm_above(unsigned long long (&v)[NPL], unsigned long long t0, int M,
+                                                         int lane, unsigned long long* scratch) {
+  // survivors: nonzero keys >= t0; exclusive prefix of the lanes' counts
+  int cnt = 0;
+#pragma unroll
+  for (int k = 0; k < NPL; ++k) cnt += (v[k] != 0ull && v[k] >= t0) ? 1 : 0;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  if (total > 64) return warp_topm_regs<NPL>(v, M, lane);  // warp-uniform
+  int pos = incl - cnt;
+#pragma unroll
+  for (int k = 0; k < NPL; ++k)
+    if (v[k] != 0ull && v[k] >= t0) scratch[pos++] = v[k];
+  if (total <= 32) {  // warp-uniform: one key per lane
+    __syncwarp();
+    unsigned long long e = lane < total ? scratch[lane] : 0ull;
+    __syncwarp();
+    e = bitonic32_desc(e, lane);
+    return lane < M ? e : 0ull;
+  }
+  for (int i = total + lane; i < 64; i += 32) scratch[i] = 0ull;
+  __syncwarp();
+  unsigned long long e0 = scratch[lane], e1 = scratch[lane + 32];
+  __syncwarp();
+  bitonic64_desc(e0, e1, lane);
   return lane < M ? e0 : 0ull;
 }
 
-// Top-M of the 8 per-warp lists (M keys each, kMaxTopM apart) by warp 0;
-// lane m returns the m-th key.
-__device__ unsigned long long merge8_topm(unsigned long long* flat, int M, int lane,
-                                          unsigned long long* scratch = nullptr) {
+__device__ __forceinline__ unsigned long long shfl_u64(unsigned long long v, int src) {
+  const uint32_t lo = __shfl_sync(0xffffffffu, static_cast<uint32_t>(v), src);
+  const uint32_t hi = __shfl_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), src);
+  return (static_cast<unsigned long long>(hi) << 32) | lo;
+}
+
+// Top-M (M <= 32) of unique keys held in registers, NPL per lane, by one warp,
+// with the same result as warp_topm_regs.  The M-th largest of the 32 lane
+// maxima (bitonic sort across the lanes) is a lower bound of the M-th largest
+// key, since at least M keys reach it; the keys at or above it (normally a
+// few more than M for keys in no particular order) are sorted by topm_above.
+template <int NPL>
+__device__ __forceinline__ unsigned long long warp_topm_filtered(unsigned long long (&v)[NPL], int M, int lane,
+                                                               unsigned long long* scratch) {
+  unsigned long long lm = 0ull;
+#pragma unroll
+  for (int k = 0; k < NPL; ++k) lm = max_u64(lm, v[k]);
+  // lane i <- the i-th largest lane maximum
+  const unsigned long long srt = bitonic32_desc(lm, lane);
+  return topm_above<NPL>(v, shfl_u64(srt, M - 1), M, lane, scratch);
+}
+
+// As warp_topm_filtered for keys sorted descending within each lane (pieces
+// of sorted lists): the threshold is the M-th largest of every lane's first
+// two keys (a 64-key bitonic sort), which keeps few keys even when the lanes'
+// maxima are few or all near the top.
+template <int NPL>
+__device__ __forceinline__ unsigned long long warp_topm_sorted(unsigned long long (&v)[NPL], int M, int lane,
+                                                             unsigned long long* scratch) {
+  static_assert(NPL >= 2, "two keys per lane sample the threshold");
+  unsigned long long e0 = v[0], e1 = v[1];
+  bitonic64_desc(e0, e1, lane);
+  return topm_above<NPL>(v, shfl_u64(e0, M - 1), M, lane, scratch);
+}
+
+// Top-M of the 8 per-warp lists (M keys each, sorted descending, kMaxTopM
+// apart) by warp 0; lane m returns the m-th key.  Lane l holds ranks
+// l / 8 + 4k of list l % 8 (descending within the lane), so the sampled
+// threshold is drawn from the first eight ranks of every list.
+__device__ unsigned long long merge8_topm(const unsigned long long* flat, int M, int lane,
+                                          unsigned long long* scratch) {
   unsigned long long v[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const int i = lane + 32 * k;  // 256 entries: list i / 32, position i % 32
-    v[k] = (i % kMaxTopM) < M ? flat[i] : 0ull;
+    const int r = (lane >> 3) + 4 * k;
+    v[k] = r < M ? flat[(lane & 7) * kMaxTopM + r] : 0ull;
   }
-  return scratch ? warp_topm_filtered<8>(v, M, lane, scratch) : warp_topm_regs<8>(v, M, lane);
+  return warp_topm_sorted<8>(v, M, lane, scratch);
 }
 __device__ __forceinline__ void unpack_key(unsigned long long k, float& x, int& blk, bool& cand) {
   x = from_ordered(static_cast<uint32_t>(k >> 32));
@@ -713,7 +742,8 @@ __device__ __forceinline__ void unpack_key(unsigned long long k, float& x, int& 
 // one warp for short lists, else a per-warp top-M of each eighth and a merge
 // of the 8 lists.  Called by all threads; lane m of warp 0 gets key m.
 __device__ unsigned long long block_topm(unsigned long long* mk, int64_t total, int M,
-                                         unsigned long long (*lists)[kMaxTopM], int warp, int lane) {
+                                         unsigned long long (*lists)[kMaxTopM],
+                                         unsigned long long (*scratch)[64], int warp, int lane) {
   unsigned long long mine = 0ull;
   if (total <= 256) {  // CTA-uniform
     if (warp == 0) {
@@ -729,7 +759,62 @@ __device__ unsigned long long block_topm(unsigned long long* mk, int64_t total, 
   const int64_t wn = rem < 0 ? 0 : (rem < per ? rem : per);
   warp_topm_smem(mk + wlo, static_cast<int>(wn), M, lists[warp], lane);
   __syncthreads();
-  if (warp == 0) mine = merge8_topm(&lists[0][0], M, lane);
+  if (warp == 0) mine = merge8_topm(&lists[0][0], M, lane, scratch[0]);
+  return mine;
+}
+
+// Top-M of nlists (<= 256) key lists, each sorted descending (M keys,
+// 0-padded), list l at src + l * stride (global memory), by the whole CTA:
+// the lists are staged in shared memory (one batch of loads per thread),
+// then one warp runs M rounds of an arg-max over the lists' current heads
+// (lane j tracks lists j + 32 i).  The merge runs once per row from a cold
+// instruction cache, so it is a short loop rather than sorting networks.
+// Called by all threads; lane m of warp 0 gets key m.
+constexpr int64_t kSortedListsMax = 8 * 32;
+__device__ unsigned long long block_merge_lists(const unsigned long long* src, int64_t stride, int64_t nlists,
+                                                int M, unsigned long long* mk, int tid, int warp, int lane) {
+  const int64_t total = nlists * M;
+  for (int64_t i0 = 0; i0 < total; i0 += 8 * kRouteThreads) {
+    unsigned long long t[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t i = i0 + tid + k * kRouteThreads;
+      t[k] = i < total ? __ldcg(src + (i / M) * stride + i % M) : 0ull;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t i = i0 + tid + k * kRouteThreads;
+      if (i < total) mk[i] = t[k];
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return 0ull;
+  unsigned long long h[8];
+  int r[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t l = lane + 32 * i;
+    r[i] = 0;
+    h[i] = l < nlists ? mk[l * M] : 0ull;
+  }
+  unsigned long long mine = 0ull;
+  for (int m = 0; m < M; ++m) {
+    unsigned long long best = 0ull;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) best = max_u64(best, h[i]);
+    const unsigned long long w = warp_max_u64(best);
+    if (lane == m) mine = w;
+    if (w == 0ull) break;  // warp-uniform: every list is spent
+    if (best == w) {       // unique keys: one owner lane and list
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (h[i] == w) {
+          ++r[i];
+          h[i] = r[i] < M ? mk[(lane + 32 * i) * M + r[i]] : 0ull;
+        }
+      }
+    }
+  }
   return mine;
 }
 
@@ -824,18 +909,44 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
 //   / bias epilogue (plus the shard-owned copy of topi32).
 // The top-M of a union of disjoint sets is contained in the union of the
 // sets' top-Ms, so both stages are exact.
+// With ShardFinish.on the row's last CTA of route_chunk_keys_kernel also does
+// the second stage: alone (one shard), or after pushing its keys to every
+// peer and a bounded wait for theirs (the lists sit in this rank's region).
 // ============================================================================
+struct ShardFinish {
+  int on;
+  int64_t own_lo, own_hi;
+  int32_t* topi32_own;
+};
+
+__device__ __forceinline__ void finish_row(const RouteArgs& a, const ShardFinish& fin, int64_t n, int lane,
+                                           unsigned long long key) {
+  float sel_v = 0.f;
+  int sel_i = -1;
+  bool sel_c = false;
+  if (lane < a.M) unpack_key(key, sel_v, sel_i, sel_c);
+  route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+  if (fin.topi32_own && lane < a.K) {
+    const bool own = sel_c && sel_i >= fin.own_lo && sel_i < fin.own_hi;
+    fin.topi32_own[n * a.K + lane] = own ? sel_i : -1;
+  }
+}
+
 __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const RouteArgs a, int64_t blk_off,
                                                                          int64_t nblk_local,
                                                                          unsigned long long* chunk_out,
                                                                          unsigned int* counters,
                                                                          unsigned long long* keys_out,
-                                                                         const srswa_peer push) {
-  extern __shared__ __align__(16) unsigned long long mk[];  // [nch * M] (last CTA of a row)
+                                                                         const srswa_peer push,
+                                                                         const ShardFinish fin) {
+  // [max(nch, world) * M]: the chunk lists (last CTA of a row), then the ranks' lists
+  extern __shared__ __align__(16) unsigned long long mk[];
   __shared__ int32_t bts[kChunkBlocks];
   __shared__ float zs[kChunkBlocks];
   __shared__ unsigned long long keys[kChunkBlocks];
   __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
+  __shared__ unsigned long long rowk[kMaxTopM];
+  __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
   __shared__ unsigned int ticket;
   const int64_t n = blockIdx.y;
   const int64_t lo = static_cast<int64_t>(blockIdx.x) * kChunkBlocks;
@@ -905,40 +1016,69 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
   __syncthreads();
   const int M = static_cast<int>(a.M);
   const int64_t nch = gridDim.x;
-  if (warp == 0) warp_topm_smem(keys, kChunkBlocks, M, chunk_out + (n * nch + blockIdx.x) * M, lane);
-  if (nch == 1) {  // chunk_out is the row's output
-    if (push.regions) {  // and this rank's keys of the row go to every peer
+  if (warp == 0) {  // the chunk's top-M (4 keys per lane, threshold filter)
+    unsigned long long v[kChunkBlocks / 32];
+#pragma unroll
+    for (int k = 0; k < kChunkBlocks / 32; ++k) v[k] = keys[lane + 32 * k];
+    const unsigned long long top = warp_topm_filtered<kChunkBlocks / 32>(v, M, lane, topm_scratch[0]);
+    if (lane < M) {
+      if (nch == 1) rowk[lane] = top;  // the chunk is the whole shard row
+      else chunk_out[(n * nch + blockIdx.x) * M + lane] = top;
+    }
+  }
+  if (nch > 1) {
+    // the last CTA of the row to finish merges the row's chunk lists
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket = atomicAdd(counters + n, 1u);
+    __syncthreads();
+    if (ticket != static_cast<unsigned int>(nch - 1)) return;
+    __threadfence();
+    const int64_t total = nch * M;
+    const unsigned long long* src = chunk_out + n * total;
+    unsigned long long mine;
+    if (nch <= kSortedListsMax) {  // CTA-uniform
+      mine = block_merge_lists(src, M, nch, M, mk, tid, warp, lane);
+    } else {
+      for (int64_t i = tid; i < total; i += kRouteThreads) mk[i] = __ldcg(src + i);
       __syncthreads();
-      if (tid < M) peer_put8(push, (n * M + tid) * 8, chunk_out[n * M + tid]);
+      mine = block_topm(mk, total, M, lists, topm_scratch, warp, lane);
+    }
+    if (warp == 0 && lane < M) rowk[lane] = mine;
+    if (tid == 0) counters[n] = 0u;
+  }
+  __syncthreads();
+  // rowk: this rank's top-M keys of the row
+  if (push.regions && tid < M) peer_put8(push, (n * M + tid) * 8, rowk[tid]);  // to every peer
+  if (!fin.on) {
+    if (keys_out && tid < M) keys_out[n * M + tid] = rowk[tid];
+    if (push.regions) {
       __syncthreads();
-      if (tid == 0) peer_unit_done(push, gridDim.y);
+      if (tid == 0) peer_unit_done(push, gridDim.y);  // one unit per row
     }
     return;
   }
-  // the last CTA of the row to finish merges the row's chunk lists
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) ticket = atomicAdd(counters + n, 1u);
-  __syncthreads();
-  if (ticket != static_cast<unsigned int>(nch - 1)) return;
-  __threadfence();
-  const int64_t total = nch * M;
-  const unsigned long long* src = chunk_out + n * total;
-  for (int64_t i = tid; i < total; i += kRouteThreads) mk[i] = __ldcg(src + i);
-  __syncthreads();
-  const unsigned long long mine = block_topm(mk, total, M, lists, warp, lane);
-  if (warp == 0 && lane < M) {
-    keys_out[n * M + lane] = mine;
-    if (push.regions) peer_put8(push, (n * M + lane) * 8, mine);  // this rank's keys of the row, to every peer
+  if (!push.regions) {  // one shard: its list is the row's
+    if (warp == 0) finish_row(a, fin, n, lane, lane < M ? rowk[lane] : 0ull);
+    return;
   }
-  if (tid == 0) counters[n] = 0u;
-  if (push.regions) {
-    __syncthreads();
-    if (tid == 0) peer_unit_done(push, gridDim.y);  // one unit per row
+  // every rank's list of the row, from this rank's region (bounded wait)
+  __syncthreads();
+  if (tid == 0) {
+    peer_unit_done(push, gridDim.y);
+    peer_wait_all(push, gridDim.y);
   }
+  __syncthreads();
+  const int world = static_cast<int>(push.world);
+  const unsigned long long* base =
+      reinterpret_cast<const unsigned long long*>(static_cast<const char*>(push.own_region) + kPeerHeader) + n * M;
+  const int64_t s_list = push.slot_bytes / 8;  // slot r = rank r's keys
+  const unsigned long long merged = block_merge_lists(base, s_list, world, M, mk, tid, warp, lane);
+  if (warp == 0) finish_row(a, fin, n, lane, merged);
 }
 
 constexpr int64_t kMergeMaxKeys = 24576;  // nlists * M per row (192 KiB of shared memory)
+constexpr int64_t kShardSelectMaxRowsPeer = 128;  // rows of srswa_route_shard_select with an exchange
 
 __global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteArgs a, const unsigned long long* keys,
                                                                    int64_t nlists, int64_t s_list, int64_t s_row,
@@ -947,6 +1087,7 @@ __global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteAr
                                                                    const srswa_peer wait) {
   extern __shared__ __align__(16) unsigned long long mk[];
   __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
+  __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
   const int64_t n = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (wait.regions) {  // the lists are the peers' pushes into this rank's region
@@ -955,10 +1096,15 @@ __global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteAr
   }
   const int M = static_cast<int>(a.M);
   const int64_t total = nlists * M;
-  for (int64_t l = warp; l < nlists; l += kRouteThreads / 32)
-    if (lane < M) mk[l * M + lane] = keys[l * s_list + n * s_row + lane];
-  __syncthreads();
-  const unsigned long long mine = block_topm(mk, total, M, lists, warp, lane);
+  unsigned long long mine;
+  if (nlists <= kSortedListsMax) {  // CTA-uniform
+    mine = block_merge_lists(keys + n * s_row, s_list, nlists, M, mk, tid, warp, lane);
+  } else {
+    for (int64_t l = warp; l < nlists; l += kRouteThreads / 32)
+      if (lane < M) mk[l * M + lane] = __ldcg(keys + l * s_list + n * s_row + lane);
+    __syncthreads();
+    mine = block_topm(mk, total, M, lists, topm_scratch, warp, lane);
+  }
   if (warp != 0) return;
   if (keys_out) {
     if (lane < M) keys_out[n * M + lane] = mine;
@@ -1527,14 +1673,15 @@ extern "C" size_t srswa_route_shard_workspace_size(int64_t N, int64_t nblk_local
   return cnt_bytes + ((static_cast<size_t>(N * nch * shard_topm_bound(params)) * 8 + 255) & ~static_cast<size_t>(255));
 }
 
-extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
-                                      const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk_local,
-                                      int64_t block_offset, int64_t nblk_total, const int32_t* block_table,
-                                      int64_t s_bt, const int32_t* seq_lens, int64_t rows_per_seq,
-                                      const int64_t* q_pos, srswa_route_params params, uint64_t* keys_out,
-                                      void* workspace, size_t workspace_bytes, const srswa_peer* push,
-                                      srswa_stream_t stream) {
-  SRSWA_CHECK_ARG(idx_q && kbar && keys_out && N >= 0 && rows_per_seq > 0, SRSWA_EINVAL);
+// Stage 1 (and with fin.on the stage-2 merge and epilogue) of the split-KV
+// router for this shard's blocks; checks shared by the two entry points.
+static int shard_launch(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d, const float* kbar,
+                        int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk_local, int64_t block_offset,
+                        int64_t nblk_total, const int32_t* block_table, int64_t s_bt, const int32_t* seq_lens,
+                        int64_t rows_per_seq, const int64_t* q_pos, const srswa_route_params& params,
+                        RouteArgs& a, uint64_t* keys_out, void* workspace, size_t workspace_bytes,
+                        const srswa_peer* push, const ShardFinish& fin, cudaStream_t st) {
+  SRSWA_CHECK_ARG(idx_q && kbar && N >= 0 && rows_per_seq > 0, SRSWA_EINVAL);
   srswa_peer pp = {};
   if (push) {
     SRSWA_CHECK_ARG(push->regions && push->own_region && push->counter && push->tickets && push->world >= 1 &&
@@ -1548,7 +1695,6 @@ extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_
   SRSWA_CHECK_ARG((reinterpret_cast<uintptr_t>(kbar) & 15) == 0 && (s_kbar_b % 4) == 0 && (s_kbar_c % 4) == 0 &&
                       (s_q % 4) == 0,
                   SRSWA_EALIGN);
-  RouteArgs a = {};
   int rc = fill_route_params(a, params, nblk_total);
   if (rc) return rc;
   a.from_scores = 0; a.q = idx_q; a.q_dtype = q_dtype; a.s_q = s_q; a.d = d; a.kbar = kbar;
@@ -1556,31 +1702,67 @@ extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_
   a.seq_lens = seq_lens; a.rows_per_seq = rows_per_seq; a.q_pos = q_pos; a.N = N; a.nblk = nblk_total;
   if (N == 0) return 0;
   SRSWA_CHECK_ARG(N < 65536, SRSWA_ETOOLARGE);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t nch = (nblk_local + kChunkBlocks - 1) / kChunkBlocks;
   unsigned long long* out = reinterpret_cast<unsigned long long*>(keys_out);
   SRSWA_CHECK_ARG(!push || N * a.M * 8 <= push->slot_bytes, SRSWA_EINVAL);
-  if (nch == 1) {
-    route_chunk_keys_kernel<<<dim3(1, static_cast<unsigned>(N)), kRouteThreads, 0, st>>>(a, block_offset, nblk_local,
-                                                                                      out, nullptr, nullptr, pp);
-    return srswa_last_launch_status();
-  }
-  SRSWA_CHECK_ARG(nch * a.M <= kMergeMaxKeys, SRSWA_ETOOLARGE);
-  const size_t cnt_bytes = (static_cast<size_t>(N) * 4 + 255) & ~static_cast<size_t>(255);
-  const size_t need = cnt_bytes + static_cast<size_t>(N * nch * a.M) * 8;
-  SRSWA_CHECK_ARG(workspace && workspace_bytes >= need, SRSWA_EWORKSPACE);
-  unsigned int* counters = static_cast<unsigned int*>(workspace);
-  unsigned long long* ck = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + cnt_bytes);
-  SRSWA_CUDA_TRY(cudaMemsetAsync(counters, 0, static_cast<size_t>(N) * 4, st));
-  const size_t smem = static_cast<size_t>(nch * a.M) * 8;
+  // the ranks' lists of a row are merged in the same shared array as its chunk lists
+  const int64_t lists = fin.on && push ? (nch > push->world ? nch : push->world) : (nch > 1 ? nch : 0);
+  SRSWA_CHECK_ARG(lists * a.M <= kMergeMaxKeys, SRSWA_ETOOLARGE);
+  const size_t smem = static_cast<size_t>(lists * a.M) * 8;
   if (smem > 40 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(route_chunk_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
   }
+  unsigned int* counters = nullptr;
+  unsigned long long* ck = nullptr;
+  if (nch > 1) {
+    const size_t cnt_bytes = (static_cast<size_t>(N) * 4 + 255) & ~static_cast<size_t>(255);
+    const size_t need = cnt_bytes + static_cast<size_t>(N * nch * a.M) * 8;
+    SRSWA_CHECK_ARG(workspace && workspace_bytes >= need, SRSWA_EWORKSPACE);
+    counters = static_cast<unsigned int*>(workspace);
+    ck = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + cnt_bytes);
+    SRSWA_CUDA_TRY(cudaMemsetAsync(counters, 0, static_cast<size_t>(N) * 4, st));
+  }
   route_chunk_keys_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(N)), kRouteThreads, smem, st>>>(
-      a, block_offset, nblk_local, ck, counters, out, pp);
+      a, block_offset, nblk_local, ck, counters, out, pp, fin);
   return srswa_last_launch_status();
+}
+
+extern "C" int srswa_route_shard_keys(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
+                                      const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk_local,
+                                      int64_t block_offset, int64_t nblk_total, const int32_t* block_table,
+                                      int64_t s_bt, const int32_t* seq_lens, int64_t rows_per_seq,
+                                      const int64_t* q_pos, srswa_route_params params, uint64_t* keys_out,
+                                      void* workspace, size_t workspace_bytes, const srswa_peer* push,
+                                      srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(keys_out, SRSWA_EINVAL);
+  RouteArgs a = {};
+  const ShardFinish fin = {};
+  return shard_launch(idx_q, q_dtype, s_q, N, d, kbar, s_kbar_b, s_kbar_c, nblk_local, block_offset, nblk_total,
+                      block_table, s_bt, seq_lens, rows_per_seq, q_pos, params, a, keys_out, workspace,
+                      workspace_bytes, push, fin, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int srswa_route_shard_select(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, int64_t d,
+                                        const float* kbar, int64_t s_kbar_b, int64_t s_kbar_c, int64_t nblk_local,
+                                        int64_t block_offset, int64_t nblk_total, const int32_t* block_table,
+                                        int64_t s_bt, const int32_t* seq_lens, int64_t rows_per_seq,
+                                        const int64_t* q_pos, srswa_route_params params, int64_t* topi64,
+                                        int32_t* topi32, float* bias, uint8_t* valid, int64_t own_lo,
+                                        int64_t own_hi, int32_t* topi32_own, void* workspace,
+                                        size_t workspace_bytes, const srswa_peer* exchange,
+                                        srswa_stream_t stream) {
+  // the row's last CTA waits for the peers: every such CTA must be resident
+  // while the other CTAs of the grid still run
+  SRSWA_CHECK_ARG(!exchange || N <= kShardSelectMaxRowsPeer, SRSWA_ETOOLARGE);
+  RouteArgs a = {};
+  a.topi64 = topi64; a.topi32 = topi32; a.bias = bias; a.valid = valid;
+  ShardFinish fin = {};
+  fin.on = 1; fin.own_lo = own_lo; fin.own_hi = own_hi; fin.topi32_own = topi32_own;
+  return shard_launch(idx_q, q_dtype, s_q, N, d, kbar, s_kbar_b, s_kbar_c, nblk_local, block_offset, nblk_total,
+                      block_table, s_bt, seq_lens, rows_per_seq, q_pos, params, a, nullptr, workspace,
+                      workspace_bytes, exchange, fin, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int64_t s_list, int64_t s_row, int64_t N,

@@ -76,6 +76,9 @@ _SIGS = {
                                          i64, vp, RouteParams, vp, vp, C.c_size_t, vp, vp]),
     "srswa_route_merge_keys": (C.c_int, [vp, i64, i64, i64, i64, i64, RouteParams, vp, vp, vp, vp, i64, i64,
                                          vp, vp, vp]),
+    "srswa_route_shard_select": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, i64, i64, i64, i64, i64, vp, i64, vp,
+                                           i64, vp, RouteParams, vp, vp, vp, vp, i64, i64, vp, vp, C.c_size_t,
+                                           vp, vp]),
     "srswa_block_max_score": (C.c_int, [vp, C.c_int, i64, i64, vp, C.c_int, i64, i64, vp, vp, i64, i64,
                                         i64, i64, i64, i64, i64, C.c_int, vp, vp]),
     "srswa_pack_selection": (C.c_int, [vp, C.c_int, i64, i64, i64, vp, vp]),

@@ -217,6 +217,52 @@ def route_shard_keys(idx_q, kbar, *, block_offset, nblk_local, nblk_total, block
     return out
 
 
+def route_shard_select(idx_q, kbar, *, block_offset, nblk_local, nblk_total, block_size, local_blocks, topk, topm,
+                       idx_scale, floor, sigma, q_pos=None, seq_lens=None, rows_per_seq=1, block_table=None,
+                       own=None, want=("topi64", "bias", "valid"), exchange=None, workspace=None):
+    """Both split-KV router stages in one launch (srswa_route_shard_select):
+    this shard's keys, then -- alone, or merged with every rank's keys through
+    the peer exchange ``exchange`` (an srswa_peer; every rank calls) -- the
+    selection of the whole row, outputs as route_merge_keys."""
+    N, d = idx_q.shape
+    if idx_q.stride(-1) != 1:
+        idx_q = idx_q.contiguous()
+    dev = idx_q.device
+    if block_table is None:
+        s_b, s_c, bt = kbar.stride(0), kbar.stride(1), None
+    else:
+        s_b, s_c = 0, kbar.stride(0)
+        bt = block_table if block_table.dtype == torch.int32 and block_table.is_contiguous() else \
+            block_table.to(torch.int32).contiguous()
+    _check_rows(N, rows_per_seq, kbar, bt, nblk_total)
+    if bt is None and kbar.shape[1] < nblk_local:
+        raise ValueError(f"k_bar holds {kbar.shape[1]} blocks, shard has {nblk_local}")
+    K, _ = effective_km(topk, topm, nblk_total)
+    out = {}
+    for name, dt in (("topi64", torch.int64), ("topi32", torch.int32), ("bias", torch.float32),
+                     ("valid", torch.uint8), ("topi32_own", torch.int32)):
+        req = name in want or (name == "topi32_own" and own is not None)
+        out[name] = torch.empty(N, K, device=dev, dtype=dt) if req else None
+    lo, hi = own if own is not None else (0, 0)
+    qp = None if q_pos is None else q_pos.to(device=dev, dtype=torch.int64).contiguous().view(-1)
+    sl = None if seq_lens is None else seq_lens.to(device=dev, dtype=torch.int32).contiguous()
+    p = _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma)
+    lib = L.lib()
+    ws_n = lib.srswa_route_shard_workspace_size(N, int(nblk_local), p)
+    ws = _workspace(ws_n, dev, workspace) if ws_n else None
+    rc = lib.srswa_route_shard_select(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
+                                      kbar.data_ptr(), s_b, s_c, int(nblk_local), int(block_offset),
+                                      int(nblk_total), L.ptr(bt), 0 if bt is None else bt.stride(0), L.ptr(sl),
+                                      int(rows_per_seq), L.ptr(qp), p, L.ptr(out["topi64"]), L.ptr(out["topi32"]),
+                                      L.ptr(out["bias"]), L.ptr(out["valid"]), int(lo), int(hi),
+                                      L.ptr(out["topi32_own"]), L.ptr(ws), ws_n,
+                                      None if exchange is None else C.byref(exchange), L.stream_of(idx_q))
+    L.check(rc, "srswa_route_shard_select")
+    if out["valid"] is not None:
+        out["valid"] = out["valid"].view(torch.bool)
+    return {k: v for k, v in out.items() if v is not None}
+
+
 def route_merge_keys(keys, *, nblk_total, topk, topm, idx_scale, floor, sigma, own=None,
                      want=("topi64", "bias", "valid"), wait=None):
     """Split-KV router stage 2: keys [nlists, N, M] (the all-gathered stage-1

@@ -89,6 +89,20 @@ class CudaBackend:
         return self.ops.route_merge_keys(keys, nblk_total=plan.nblk_total, own=(plan.lo, plan.hi),
                                          want=("topi32", "bias"), **p)
 
+    def select(self, idx_q, layer, plan, q_pos, rp):
+        """The merged selection of the whole row (topi32, bias, topi32_own):
+        one launch on a single rank, else shard keys -> all-gather -> merge."""
+        if plan.world == 1:
+            return self._shard_select(idx_q, layer, plan, q_pos, rp, None)
+        keys = self.shard_keys(idx_q, layer, plan, q_pos, rp)               # [N, M]
+        return self.merge_keys(self.gather_keys(keys, plan.world), plan, rp)
+
+    def _shard_select(self, idx_q, layer, plan, q_pos, rp, exchange):
+        return self.ops.route_shard_select(
+            idx_q, layer["kbar"], block_offset=plan.lo, nblk_local=plan.hi - plan.lo, nblk_total=plan.nblk_total,
+            q_pos=q_pos, rows_per_seq=idx_q.shape[0], block_table=layer.get("kbar_table"),
+            own=(plan.lo, plan.hi), want=("topi32", "bias"), exchange=exchange, **rp)
+
     def attend(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local,
                out_dtype=torch.float32):
         N, H, D = q.shape
@@ -166,6 +180,13 @@ class PeerBackend(CudaBackend):
                                          want=("topi32", "bias"), wait=self.keys_x.peer if self.fused else None,
                                          **p)
 
+    def select(self, idx_q, layer, plan, q_pos, rp):
+        # fused: one launch per layer does the shard keys, the key exchange
+        # and the merge (up to 128 rows: each row's merging CTA waits resident)
+        if self.fused and plan.world > 1 and idx_q.shape[0] <= 128:
+            return self._shard_select(idx_q, layer, plan, q_pos, rp, self.keys_x.peer)
+        return super().select(idx_q, layer, plan, q_pos, rp)
+
     def gather_partials(self, buf, world):
         return self.part_x.push(buf) if self.fused else self.part_x(buf)
 
@@ -228,9 +249,12 @@ class SplitKVDecode:
             raise ValueError("SplitKVDecode.step needs p_range = (min, max) of q_pos on the host")
         # host-only check first: a bad plan fails before any launch or collective
         owner = self.window_owner(int(p_range[1]), int(p_range[0]))
-        keys = be.shard_keys(idx_q, layer, plan, q_pos, self.rp)            # [N, M]
-        all_keys = be.gather_keys(keys, world)                               # [world, N, M]
-        sel = be.merge_keys(all_keys, plan, self.rp)
+        select = getattr(be, "select", None)                                 # steps 1-3
+        if select is not None:
+            sel = select(idx_q, layer, plan, q_pos, self.rp)
+        else:
+            keys = be.shard_keys(idx_q, layer, plan, q_pos, self.rp)        # [N, M]
+            sel = be.merge_keys(be.gather_keys(keys, world), plan, self.rp)  # [world, N, M] -> selection
         # one rank: its output is final, written in out_dtype; else fp32 partials
         o_part, lse_part = be.attend(q, layer, sel["topi32_own"], sel["bias"], q_pos,
                                      block_size=self.block_size, local_blocks=self.local_blocks,
