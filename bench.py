@@ -290,7 +290,7 @@ def run_step(st):
     r = ops.route(st["iq"], st["kbar"], block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=IDX_SCALE,
                   floor=FLOOR, sigma=SIGMA, seq_lens=st["sl"], block_table=st["bt"], want=("topi32", "bias"))
     st["topi"], st["bias"] = r["topi32"], r["bias"]
-    run_attend(st)
+    run_attend(st, overlap=True)   # starts on the window keys while the router finishes
     torch.cuda.current_stream().wait_stream(side)
 
 
@@ -320,14 +320,14 @@ def run_step_public(st, q, iq, kv_ready=None, before_refresh=None):
     if kv_ready is not None:
         torch.cuda.current_stream().wait_stream(kv_ready)
     paged.dash_sparse_attn_decode(q, st["k"], st["v"], ti, tb, st["bt"], st["sl"], HKV, SM_SCALE, st["out"], 1,
-                                  local_blocks=L, sparse_block_size=BS)
+                                  local_blocks=L, sparse_block_size=BS, overlap_router=True)
     torch.cuda.current_stream().wait_stream(side)
 
 
-def run_attend(st):
+def run_attend(st, overlap=False):
     from srswa import ops
     ops.decode_attend(st["q"], st["k"], st["v"], st["topi"], st["bias"], block_size=BS, local_blocks=L,
-                      sm_scale=SM_SCALE, out=st["out"], block_table=st["bt"], seq_lens=st["sl"])
+                      sm_scale=SM_SCALE, out=st["out"], block_table=st["bt"], seq_lens=st["sl"], overlap=overlap)
 
 
 def timed_graph(fn, steps, warmup, flush, use_graph=True):

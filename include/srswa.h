@@ -344,6 +344,15 @@ typedef struct {
   int nsplit;
   int skip_local; /* 1: attend the selected remote blocks only, not the window
                      (split-KV shards that do not own the window) */
+  int overlap;    /* 1: the launch may begin before the kernel issued just
+                     before it on the stream has finished (programmatic
+                     dependent launch) and attends the window keys meanwhile:
+                     q, the caches, block_table and seq_lens / q_pos must have
+                     been written before that kernel began; topk_idx, bias and
+                     valid are read after it has completed.  The library's
+                     routers, called right before on the same stream, are such
+                     kernels.  0: nothing is read before that kernel has
+                     completed.  Results are identical either way. */
 } srswa_decode_desc;
 
 SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache,

@@ -156,3 +156,54 @@ def test_decode_many_rows_split_last_wave(cuda, R):
     ref, _ = O.paged_decode(q[rows], kc, vc, O.dedup_rows(idx[rows])[None], bias[rows][None], bt[rows],
                             np.asarray(seqs)[rows], 0.088, 1, L, BS)
     np.testing.assert_allclose(out_auto.cpu().numpy()[rows], ref, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("R,nsplit", [(32, 0), (256, 0), (40, 2)])
+def test_decode_overlap_after_router_equals_plain(cuda, R, nsplit):
+    """overlap=True (the attend launched to start on its window keys while
+    the router ahead of it on the stream finishes) gives the same bits as the
+    plain launch.  The newest K/V row of every request is written on a side
+    stream behind a long kernel and joined by an event just before the
+    attend: the early window reads must still see it."""
+    rng = np.random.default_rng(R + 7)
+    H, Hkv, D, BS, L, K, d = 10, 2, 128, 64, 8, 8, 128
+    seqs = list(rng.integers(2000, 6000, R))
+    bt, kc, vc, q, _, _ = _paged_case(rng, R, H, Hkv, D, BS, L, K, seqs, extra_pages=0)
+    P = kc.shape[0]
+    kbar = T(rng.standard_normal((P, d)).astype(np.float32), cuda)
+    iq = T(rng.standard_normal((R, d)).astype(np.float32), cuda, torch.bfloat16)
+    bt_t, sl_t = T(bt, cuda), T(np.asarray(seqs, np.int32), cuda)
+    k_t, v_t = T(kc, cuda, torch.bfloat16), T(vc, cuda, torch.bfloat16)
+    qt = T(q, cuda, torch.bfloat16)
+    last = [(int(bt[r, (s - 1) // BS]), (s - 1) % BS) for r, s in enumerate(seqs)]
+    pg = torch.tensor([a for a, _ in last], device=cuda)
+    ps = torch.tensor([b for _, b in last], device=cuda)
+    new_k, new_v = k_t[pg, ps].clone(), v_t[pg, ps].clone()
+    rp = dict(block_size=BS, local_blocks=L, topk=K, topm=16, idx_scale=128 / math.sqrt(d), floor=1e-4, sigma=1.0)
+    kw = dict(block_size=BS, local_blocks=L, sm_scale=0.088, block_table=bt_t, seq_lens=sl_t, nsplit=nsplit)
+    side = torch.cuda.Stream()
+    ev = torch.cuda.Event()
+    busy = torch.randn(4096, 4096, device=cuda)
+    outs = []
+    for overlap in (False, True):
+        k_t[pg, ps] = 0
+        v_t[pg, ps] = 0
+        torch.cuda.synchronize()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(8):        # keeps the side stream busy well past the router
+                busy = busy @ busy * 1e-3
+            k_t[pg, ps] = new_k
+            v_t[pg, ps] = new_v
+            ev.record(side)
+        sel = ops.route(iq, kbar, block_table=bt_t, seq_lens=sl_t, want=("topi32", "bias"), **rp)
+        torch.cuda.current_stream().wait_event(ev)
+        outs.append(ops.decode_attend(qt, k_t, v_t, sel["topi32"], sel["bias"], overlap=overlap,
+                                      out=torch.empty(R, H, D, device=cuda), **kw))
+        torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    rows = np.arange(min(R, 6))
+    sel_np = {k: v.cpu().numpy() for k, v in sel.items()}
+    ref, _ = O.paged_decode(q[rows], kc, vc, O.dedup_rows(sel_np["topi32"][rows])[None], sel_np["bias"][rows][None],
+                            bt[rows], np.asarray(seqs)[rows], 0.088, 1, L, BS)
+    np.testing.assert_allclose(outs[1].cpu().numpy()[rows], ref, rtol=1e-4, atol=1e-4)

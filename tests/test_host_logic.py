@@ -110,8 +110,12 @@ def test_install_sglang_reaches_the_backend(monkeypatch):
     done = dropin.install_sglang()
     for n in ("dash_sparse_attn", "dash_sparse_attn_decode", "route_decode_triton", "route_prefill_triton",
               "kbar_refresh_tail_triton", "win_bounds_decode"):
-        assert getattr(be, n) is getattr(paged, n), n
+        # the backend issues its decode attend right after its router: the overlapping variant
+        want = paged.dash_sparse_attn_decode_after_router if n == "dash_sparse_attn_decode" else getattr(paged, n)
+        assert getattr(be, n) is want, n
         mod = at if hasattr(at, n) else rt
         assert getattr(mod, n) is getattr(paged, n), n
     assert be.kbar_tail_plan is ref          # torch-only planning helpers stay the reference's
     assert len(done) == 12
+    dropin.install_sglang(overlap_router=False)
+    assert be.dash_sparse_attn_decode is paged.dash_sparse_attn_decode

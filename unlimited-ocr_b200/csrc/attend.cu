@@ -85,13 +85,17 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
   constexpr int KPC = KPI * 8;   // keys per chunk (8 loads per lane)
 
   __shared__ SlotInfo slots[kAttendMaxSlots];
-  __shared__ int n_slots;
+  __shared__ int n_win, n_slots;
   __shared__ float w_m[kAttendWarps], w_l[kAttendWarps];
   __shared__ __align__(16) float w_o[kAttendWarps][D];
   __shared__ float c_m, c_l;
   __shared__ __align__(16) float c_o[D];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // without overlap nothing is read before the kernel ahead on the stream
+  // has completed; with it only the selection waits (srswa_decode_desc.overlap)
+  if (!a.overlap) pdl_wait();
+  pdl_launch_dependents();
   const int nsplit = a.nsplit;
   // heads_inner: grid (heads x splits, rows), so that the CTAs of one row's
   // heads are launched together and read the same key rows (whole 2560-byte
@@ -107,13 +111,128 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
   int64_t ls = p - a.LW + 1;
   if (ls < sg) ls = sg;
   if (ls < 0) ls = 0;
+  const bool live = p >= 0 && p >= sg;
 
-  // ---- slot list: remote selections (deduped, useful only), then window.
-  //      Built by warp 0 with one lane per slot: the index, block-table and
-  //      bias loads of all slots are issued together. ----
+  // ---- window slots first: they do not depend on the selection ----
   if (warp == 0) {
     int n = 0;
-    if (p >= 0 && p >= sg) {
+    if (live && !a.skip_local) {
+      const int64_t b_lo = ls / BS, b_hi = min(p / BS, a.W - 1);
+      for (int64_t b0 = b_lo; b0 <= b_hi; b0 += 32) {
+        const int64_t blk = b0 + lane;
+        const bool ok = blk <= b_hi;
+        const int64_t off = ok ? block_offset(a, seq, blk) : 0;
+        const unsigned msk = __ballot_sync(0xffffffffu, ok);
+        const int pos = n + lane;
+        if (ok && pos < kAttendMaxSlots) {
+          slots[pos].page_off = off;
+          slots[pos].key0 = blk * BS;
+          slots[pos].bias2 = 0.f;
+          slots[pos].remote = 0;
+        }
+        n += __popc(msk);
+        if (n > kAttendMaxSlots) n = kAttendMaxSlots;
+      }
+    }
+    if (lane == 0) n_win = n;
+  }
+  __syncthreads();
+
+  // ---- this lane's slice of q (pre-scaled into the log2 domain) ----
+  const int g = lane / LPK, u = lane % LPK;
+  float qv[8];
+  load8(a.q, seq * a.s_q_seq + t * a.s_q_t + static_cast<int64_t>(h) * a.s_qh + u * 8, a.q_dtype, qv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) qv[e] *= a.q_scale_log2;
+
+  const int cpb = static_cast<int>(BS / KPC);  // chunks per block
+
+  float m = -INFINITY, lsum = 0.f;
+  float o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = 0.f;
+  // after transpose_reduce8 each key's score sits in LPK/8 lanes; count it once
+  const int count_lane = (u & (LPK / 8 - 1)) == 0;
+  const int my_idx = 4 * ((u & (LPK / 2)) != 0) + 2 * ((u & (LPK / 4)) != 0) + ((u & (LPK / 8)) != 0);
+
+  // chunks of slots [s_lo, s_hi): this split's share, one warp per chunk
+  auto stream_slots = [&](int s_lo, int s_hi) {
+    const int nch = (s_hi - s_lo) * cpb;
+    const int c_begin = static_cast<int>((static_cast<int64_t>(nch) * split) / nsplit);
+    const int c_end = static_cast<int>((static_cast<int64_t>(nch) * (split + 1)) / nsplit);
+    for (int ch = c_begin + warp; ch < c_end; ch += kAttendWarps) {
+      const SlotInfo si = slots[s_lo + ch / cpb];
+      const int sub = ch % cpb;
+      const int64_t k0 = si.key0 + static_cast<int64_t>(sub) * KPC;
+      int64_t lo, hi_;  // valid absolute key range [lo, hi_)
+      if (si.remote) {
+        lo = k0 > sg ? k0 : sg;
+        hi_ = min(min(k0 + KPC, p + 1), ls);
+      } else {
+        lo = k0 > ls ? k0 : ls;
+        hi_ = min(k0 + KPC, p + 1);
+      }
+      if (lo >= hi_) continue;  // warp-uniform
+
+      const int64_t base = si.page_off + static_cast<int64_t>(hk) * a.s_head +
+                           static_cast<int64_t>(sub) * KPC * a.s_pos + u * 8;
+      uint4 kr[8], vr[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int j = i * KPI + g;
+        const int64_t pos = k0 + j;
+        if (pos >= lo && pos < hi_) {
+          const int64_t off = base + j * a.s_pos;
+          kr[i] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(a.k) + off));
+          vr[i] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(a.v) + off));
+        } else {
+          kr[i] = make_uint4(0, 0, 0, 0);
+          vr[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      float part[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float f[8];
+        unpack8<KVT>(kr[i], f);
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(qv[e], f[e], acc);
+        part[i] = acc;
+      }
+      const float dot = transpose_reduce8<LPK>(part, u);
+      const int64_t my_pos = k0 + my_idx * KPI + g;
+      const float s2 = (my_pos >= lo && my_pos < hi_) ? dot + si.bias2 : -INFINITY;
+      const float cmax = warp_max(s2);
+      const float m_new = fmaxf(m, cmax);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = exp2f(m - m_use);
+      const float pr = exp2f(s2 - m_use);
+      lsum = lsum * alpha + (count_lane ? pr : 0.f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] *= alpha;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float pi = __shfl_sync(0xffffffffu, pr, g * LPK + transpose_owner<LPK>(i));
+        float f[8];
+        unpack8<KVT>(vr[i], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = fmaf(pi, f[e], o[e]);
+      }
+      m = m_new;
+    }
+  };
+
+  const int nw = n_win;
+  stream_slots(0, nw);
+  if (a.overlap) pdl_wait();  // the selection comes from the kernel ahead
+
+  // ---- remote slots: the selections (deduped, useful only), after the
+  //      window.  Built by warp 0 with one lane per slot: the index,
+  //      block-table and bias loads of all slots are issued together. ----
+  if (warp == 0) {
+    int n = nw;
+    if (live) {
       const int64_t ibase = seq * a.s_sel_seq + t * a.s_sel_t + hi * a.s_sel_h;
       const int64_t bbase = seq * a.s_b_seq + t * a.s_b_t + hi * a.s_b_h;
       for (int64_t s0 = 0; s0 < a.K; s0 += 32) {
@@ -129,13 +248,14 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
             ok = lo < hi_ && lo <= p;
           }
         }
-        // drop repeats of an earlier usable slot (this batch, then earlier batches)
+        // drop repeats of an earlier usable slot (this batch, then earlier
+        // batches; window slots cover other keys of a block and stay)
         for (int j = 0; j < 32; ++j) {
           const int64_t ob = __shfl_sync(0xffffffffu, blk, j);
           const bool ook = __shfl_sync(0xffffffffu, ok, j);
           if (j < lane && ook && ob == blk) ok = false;
         }
-        for (int j = 0; j < n; ++j)
+        for (int j = nw; j < n; ++j)
           if (ok && slots[j].key0 == blk * BS) ok = false;
         int64_t off = 0;
         float b2 = 0.f;
@@ -157,110 +277,11 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
         if (n > kAttendMaxSlots) n = kAttendMaxSlots;
         __syncwarp();
       }
-      if (!a.skip_local) {
-        const int64_t b_lo = ls / BS, b_hi = min(p / BS, a.W - 1);
-        for (int64_t b0 = b_lo; b0 <= b_hi; b0 += 32) {
-          const int64_t blk = b0 + lane;
-          const bool ok = blk <= b_hi;
-          const int64_t off = ok ? block_offset(a, seq, blk) : 0;
-          const unsigned msk = __ballot_sync(0xffffffffu, ok);
-          const int pos = n + lane;
-          if (ok && pos < kAttendMaxSlots) {
-            slots[pos].page_off = off;
-            slots[pos].key0 = blk * BS;
-            slots[pos].bias2 = 0.f;
-            slots[pos].remote = 0;
-          }
-          n += __popc(msk);
-          if (n > kAttendMaxSlots) n = kAttendMaxSlots;
-        }
-      }
     }
     if (lane == 0) n_slots = n;
   }
   __syncthreads();
-
-  // ---- this lane's slice of q (pre-scaled into the log2 domain) ----
-  const int g = lane / LPK, u = lane % LPK;
-  float qv[8];
-  load8(a.q, seq * a.s_q_seq + t * a.s_q_t + static_cast<int64_t>(h) * a.s_qh + u * 8, a.q_dtype, qv);
-#pragma unroll
-  for (int e = 0; e < 8; ++e) qv[e] *= a.q_scale_log2;
-
-  const int cpb = static_cast<int>(BS / KPC);  // chunks per block
-  const int nch = n_slots * cpb;
-  const int c_begin = static_cast<int>((static_cast<int64_t>(nch) * split) / nsplit);
-  const int c_end = static_cast<int>((static_cast<int64_t>(nch) * (split + 1)) / nsplit);
-
-  float m = -INFINITY, lsum = 0.f;
-  float o[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) o[e] = 0.f;
-  // after transpose_reduce8 each key's score sits in LPK/8 lanes; count it once
-  const int count_lane = (u & (LPK / 8 - 1)) == 0;
-  const int my_idx = 4 * ((u & (LPK / 2)) != 0) + 2 * ((u & (LPK / 4)) != 0) + ((u & (LPK / 8)) != 0);
-
-  for (int ch = c_begin + warp; ch < c_end; ch += kAttendWarps) {
-    const SlotInfo si = slots[ch / cpb];
-    const int sub = ch % cpb;
-    const int64_t k0 = si.key0 + static_cast<int64_t>(sub) * KPC;
-    int64_t lo, hi_;  // valid absolute key range [lo, hi_)
-    if (si.remote) {
-      lo = k0 > sg ? k0 : sg;
-      hi_ = min(min(k0 + KPC, p + 1), ls);
-    } else {
-      lo = k0 > ls ? k0 : ls;
-      hi_ = min(k0 + KPC, p + 1);
-    }
-    if (lo >= hi_) continue;  // warp-uniform
-
-    const int64_t base = si.page_off + static_cast<int64_t>(hk) * a.s_head +
-                         static_cast<int64_t>(sub) * KPC * a.s_pos + u * 8;
-    uint4 kr[8], vr[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int j = i * KPI + g;
-      const int64_t pos = k0 + j;
-      if (pos >= lo && pos < hi_) {
-        const int64_t off = base + j * a.s_pos;
-        kr[i] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(a.k) + off));
-        vr[i] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(a.v) + off));
-      } else {
-        kr[i] = make_uint4(0, 0, 0, 0);
-        vr[i] = make_uint4(0, 0, 0, 0);
-      }
-    }
-    float part[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float f[8];
-      unpack8<KVT>(kr[i], f);
-      float acc = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc = fmaf(qv[e], f[e], acc);
-      part[i] = acc;
-    }
-    const float dot = transpose_reduce8<LPK>(part, u);
-    const int64_t my_pos = k0 + my_idx * KPI + g;
-    const float s2 = (my_pos >= lo && my_pos < hi_) ? dot + si.bias2 : -INFINITY;
-    const float cmax = warp_max(s2);
-    const float m_new = fmaxf(m, cmax);
-    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-    const float alpha = exp2f(m - m_use);
-    const float pr = exp2f(s2 - m_use);
-    lsum = lsum * alpha + (count_lane ? pr : 0.f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] *= alpha;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float pi = __shfl_sync(0xffffffffu, pr, g * LPK + transpose_owner<LPK>(i));
-      float f[8];
-      unpack8<KVT>(vr[i], f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = fmaf(pi, f[e], o[e]);
-    }
-    m = m_new;
-  }
+  stream_slots(nw, n_slots);
 
   // ---- warp combine: sum l over lanes, o over key groups ----
   lsum = warp_sum(lsum);
@@ -332,13 +353,17 @@ static int launch_attend(const AttendArgs& a, cudaStream_t st) {
   cfg.blockDim = dim3(kAttendThreads, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = a.nsplit;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // may start while the kernel ahead on the stream runs: the kernel waits
+  // for it (pdl_wait) before reading what it writes
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, attend_rows_kernel<D, KVT, MINB>, a);
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
@@ -533,7 +558,7 @@ extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, c
   a.s_q_seq = d.rows_per_req * d.s_qn; a.s_q_t = d.s_qn; a.s_qh = d.s_qh;
   a.out = out; a.s_o_seq = d.rows_per_req * d.s_on; a.s_o_t = d.s_on; a.s_oh = d.s_oh;
   a.lse_out = lse_out; a.s_l_seq = d.rows_per_req * d.H; a.s_l_t = d.H;
-  a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0;
+  a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0; a.overlap = d.overlap ? 1 : 0;
   return attend_rows_launch(a, d.D, d.kv_dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -566,7 +591,7 @@ extern "C" int srswa_prefill_attend(const srswa_decode_desc* dd, const void* q, 
   a.s_q_seq = 0; a.s_q_t = d.s_qn; a.s_qh = d.s_qh;
   a.out = out; a.s_o_seq = 0; a.s_o_t = d.s_on; a.s_oh = d.s_oh;
   a.lse_out = lse_out; a.s_l_seq = 0; a.s_l_t = d.H;
-  a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0;
+  a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0; a.overlap = d.overlap ? 1 : 0;
   return attend_rows_launch(a, d.D, d.kv_dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 

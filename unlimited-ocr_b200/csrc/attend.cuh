@@ -64,6 +64,7 @@ struct AttendArgs {
   int64_t row0;    // first row of this launch (rows row0 .. row0 + N - 1)
   int split_tail;  // the split was left open: a nearly empty last wave may be split
   int heads_inner; // grid (heads x splits, rows) instead of (rows x splits, heads)
+  int overlap;     // window keys before pdl_wait (srswa_decode_desc.overlap)
 };
 
 template <int KVT>

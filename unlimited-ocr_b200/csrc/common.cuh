@@ -20,6 +20,17 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 // ---------------------------------------------------------------------------
+// programmatic dependent launch (sm_90+).  A kernel launched with the
+// attribute cudaLaunchAttributeProgrammaticStreamSerialization may start once
+// every CTA of the kernel before it on the stream has called
+// pdl_launch_dependents (or exited); pdl_wait then blocks until that kernel
+// has completed and its writes are visible.  Both are no-ops for a kernel
+// launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // element loads (fp32 / bf16 / fp16 selected by a runtime dtype code)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_lo(uint32_t x) { return __uint_as_float(x << 16); }

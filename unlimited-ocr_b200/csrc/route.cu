@@ -272,6 +272,10 @@ __device__ void route_dots(const RouteArgs& a, int64_t n, int64_t seq, int64_t c
 // M holds the j-th largest x, its block sel_i and whether it is a candidate),
 // then the first K slots and their centred log-prior bias, written for row n.
 // Called by one warp.
+// kCompact: short loops instead of unrolled gathers, for a single run from
+// a cold instruction cache (once per row of a few-row kernel); the unrolled
+// form keeps shuffle latency out of the sums for kernels that loop over rows.
+template <bool kCompact = false>
 __device__ __forceinline__ void route_epilogue(const RouteArgs& a, int64_t n, int lane, float sel_v, int sel_i,
                                                bool sel_cand) {
   const int M = static_cast<int>(a.M);
@@ -281,20 +285,29 @@ __device__ __forceinline__ void route_epilogue(const RouteArgs& a, int64_t n, in
   // mean - sqrt(max(0, (1 - rho(meansq - mean^2))/rho)); support = #(tau <= X)
   const float xmax = __shfl_sync(0xffffffffu, sel_v, 0);
   const float X = (sel_v - xmax) / 2.0f;
-  // every lane gathers 8 values at a time (independent shuffles), then runs
-  // the same left-to-right float64 sums: no shuffle latency inside the chain
+  // every lane runs the same left-to-right float64 sums
   double acc1 = 0.0, acc2 = 0.0;
   float my_cs = 0.f, my_cs2 = 0.f;
-  for (int j0 = 0; j0 < M; j0 += 8) {
-    float xs[8];
+  if (kCompact) {
+#pragma unroll 1
+    for (int j = 0; j < M; ++j) {
+      const float xj = __shfl_sync(0xffffffffu, X, j);
+      acc1 += static_cast<double>(xj);
+      acc2 += static_cast<double>(xj * xj);
+      if (lane == j) { my_cs = static_cast<float>(acc1); my_cs2 = static_cast<float>(acc2); }
+    }
+  } else {  // 8 values gathered at a time (independent shuffles)
+    for (int j0 = 0; j0 < M; j0 += 8) {
+      float xs[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) xs[e] = __shfl_sync(0xffffffffu, X, (j0 + e) & 31);
+      for (int e = 0; e < 8; ++e) xs[e] = __shfl_sync(0xffffffffu, X, (j0 + e) & 31);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (j0 + e < M) {
-        acc1 += static_cast<double>(xs[e]);
-        acc2 += static_cast<double>(xs[e] * xs[e]);
-        if (lane == j0 + e) { my_cs = static_cast<float>(acc1); my_cs2 = static_cast<float>(acc2); }
+      for (int e = 0; e < 8; ++e) {
+        if (j0 + e < M) {
+          acc1 += static_cast<double>(xs[e]);
+          acc2 += static_cast<double>(xs[e] * xs[e]);
+          if (lane == j0 + e) { my_cs = static_cast<float>(acc1); my_cs2 = static_cast<float>(acc2); }
+        }
       }
     }
   }
@@ -318,13 +331,21 @@ __device__ __forceinline__ void route_epilogue(const RouteArgs& a, int64_t n, in
   float sum = 0.f;
   int cnt = 0;
   const unsigned vmask = __ballot_sync(0xffffffffu, vld);
-  for (int j0 = 0; j0 < K; j0 += 8) {
-    float ls[8];
+  if (kCompact) {
+#pragma unroll 1
+    for (int j = 0; j < K; ++j) {
+      const float lj = __shfl_sync(0xffffffffu, logp, j);
+      if ((vmask >> j) & 1u) { sum += lj; ++cnt; }
+    }
+  } else {
+    for (int j0 = 0; j0 < K; j0 += 8) {
+      float ls[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ls[e] = __shfl_sync(0xffffffffu, logp, (j0 + e) & 31);
+      for (int e = 0; e < 8; ++e) ls[e] = __shfl_sync(0xffffffffu, logp, (j0 + e) & 31);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (j0 + e < K && ((vmask >> (j0 + e)) & 1u)) { sum += ls[e]; ++cnt; }
+      for (int e = 0; e < 8; ++e) {
+        if (j0 + e < K && ((vmask >> (j0 + e)) & 1u)) { sum += ls[e]; ++cnt; }
+      }
     }
   }
   const float mu = sum / static_cast<float>(cnt > 0 ? cnt : 1);
@@ -340,6 +361,7 @@ __device__ __forceinline__ void route_epilogue(const RouteArgs& a, int64_t n, in
 
 
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
+  pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int rpc = a.rows_per_cta;
   const int64_t nblk = a.nblk;
@@ -511,6 +533,7 @@ constexpr int kChunkBlocks = 128;
 // the k_bar loads of one chunk after the other.
 constexpr int kScoreReps = 2;
 __global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const RouteArgs a, float* zout) {
+  pdl_launch_dependents();  // lets the selection kernel launch early
   constexpr int kSpan = kChunkBlocks * kScoreReps;
   __shared__ int32_t bts[kSpan];
   const int64_t n = blockIdx.y;
@@ -763,63 +786,52 @@ __device__ unsigned long long block_topm(unsigned long long* mk, int64_t total, 
   return mine;
 }
 
-// Top-M of nlists (<= 256) key lists, each sorted descending (M keys,
-// 0-padded), list l at src + l * stride (global memory), by the whole CTA:
-// the lists are staged in shared memory (one batch of loads per thread),
-// then one warp runs M rounds of an arg-max over the lists' current heads
-// (lane j tracks lists j + 32 i).  The merge runs once per row from a cold
-// instruction cache, so it is a short loop rather than sorting networks.
-// Called by all threads; lane m of warp 0 gets key m.
-constexpr int64_t kSortedListsMax = 8 * 32;
-__device__ unsigned long long block_merge_lists(const unsigned long long* src, int64_t stride, int64_t nlists,
-                                                int M, unsigned long long* mk, int tid, int warp, int lane) {
-  const int64_t total = nlists * M;
-  for (int64_t i0 = 0; i0 < total; i0 += 8 * kRouteThreads) {
-    unsigned long long t[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int64_t i = i0 + tid + k * kRouteThreads;
-      t[k] = i < total ? __ldcg(src + (i / M) * stride + i % M) : 0ull;
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int64_t i = i0 + tid + k * kRouteThreads;
-      if (i < total) mk[i] = t[k];
-    }
-  }
-  __syncthreads();
-  if (warp != 0) return 0ull;
-  unsigned long long h[8];
-  int r[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int64_t l = lane + 32 * i;
-    r[i] = 0;
-    h[i] = l < nlists ? mk[l * M] : 0ull;
-  }
+// Top-M of up to 32 key lists held one per lane (v, sorted descending,
+// 0-padded) by one warp: M rounds of a warp arg-max over the list heads, the
+// owner lane shifts its list.  Lane m returns the m-th key.
+__device__ __forceinline__ unsigned long long warp_merge_heads(unsigned long long (&v)[16], int M, int lane) {
   unsigned long long mine = 0ull;
+#pragma unroll 1
   for (int m = 0; m < M; ++m) {
-    unsigned long long best = 0ull;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) best = max_u64(best, h[i]);
-    const unsigned long long w = warp_max_u64(best);
+    const unsigned long long w = warp_max_u64(v[0]);
     if (lane == m) mine = w;
-    if (w == 0ull) break;  // warp-uniform: every list is spent
-    if (best == w) {       // unique keys: one owner lane and list
+    if (w != 0ull && v[0] == w) {  // unique keys: one owner lane
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (h[i] == w) {
-          ++r[i];
-          h[i] = r[i] < M ? mk[(lane + 32 * i) * M + r[i]] : 0ull;
-        }
-      }
+      for (int k = 0; k + 1 < 16; ++k) v[k] = v[k + 1];
+      v[15] = 0ull;
     }
   }
   return mine;
 }
 
+// Top-M (M <= 16) of nlists (<= 256) key lists, each sorted descending (M
+// keys, 0-padded), list l at src + l * stride (global memory), by the whole
+// CTA: lane j of warp w loads list w * per + j into registers and the warp
+// merges its lists (warp_merge_heads), then warp 0 merges the 8 warps'
+// lists.  Two short loops: the merge runs once per row, from a cold
+// instruction cache.  Called by all threads; lane m of warp 0 gets key m.
+constexpr int64_t kSortedListsMax = 8 * 32;
+__device__ unsigned long long block_merge_lists(const unsigned long long* src, int64_t stride, int64_t nlists,
+                                                int M, unsigned long long (*lists)[kMaxTopM], int warp, int lane) {
+  const int64_t per = (nlists + 7) / 8;
+  const int64_t l = static_cast<int64_t>(warp) * per + lane;
+  const bool has = lane < per && l < nlists;
+  unsigned long long v[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = (has && k < M) ? __ldcg(src + l * stride + k) : 0ull;
+  const unsigned long long top = warp_merge_heads(v, M, lane);
+  if (lane < M) lists[warp][lane] = top;
+  __syncthreads();
+  if (warp != 0) return 0ull;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = (lane < 8 && k < M) ? lists[lane][k] : 0ull;
+  return warp_merge_heads(v, M, lane);
+}
+
 __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteArgs a, const float* zin,
                                                                     int64_t s_z) {
+  pdl_launch_dependents();  // lets an overlapping attend start on its window
+  pdl_wait();               // the scores of the kernel ahead
   extern __shared__ __align__(16) unsigned long long wk[];  // [nblk] keys
   __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
   __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
@@ -887,12 +899,20 @@ __global__ void __launch_bounds__(kRouteThreads) select_wide_kernel(const RouteA
   }
   __syncthreads();
   if (warp != 0) return;
-  const unsigned long long mine = merge8_topm(&lists[0][0], M, lane, topm_scratch[0]);
+  unsigned long long mine;
+  if (M <= 16) {  // the 8 warps' sorted lists: a short head-merge loop
+    unsigned long long v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = (lane < 8 && k < M) ? lists[lane][k] : 0ull;
+    mine = warp_merge_heads(v, M, lane);
+  } else {
+    mine = merge8_topm(&lists[0][0], M, lane, topm_scratch[0]);
+  }
   float sel_v = 0.f;
   int sel_i = -1;
   bool sel_c = false;
   if (lane < M) unpack_key(mine, sel_v, sel_i, sel_c);
-  route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+  route_epilogue<true>(a, n, lane, sel_v, sel_i, sel_c);  // once per CTA
 }
 
 // ============================================================================
@@ -925,7 +945,7 @@ __device__ __forceinline__ void finish_row(const RouteArgs& a, const ShardFinish
   int sel_i = -1;
   bool sel_c = false;
   if (lane < a.M) unpack_key(key, sel_v, sel_i, sel_c);
-  route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+  route_epilogue<true>(a, n, lane, sel_v, sel_i, sel_c);
   if (fin.topi32_own && lane < a.K) {
     const bool own = sel_c && sel_i >= fin.own_lo && sel_i < fin.own_hi;
     fin.topi32_own[n * a.K + lane] = own ? sel_i : -1;
@@ -939,6 +959,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
                                                                          unsigned long long* keys_out,
                                                                          const srswa_peer push,
                                                                          const ShardFinish fin) {
+  pdl_launch_dependents();  // lets an overlapping attend start on its window
   // [max(nch, world) * M]: the chunk lists (last CTA of a row), then the ranks' lists
   extern __shared__ __align__(16) unsigned long long mk[];
   __shared__ int32_t bts[kChunkBlocks];
@@ -1037,8 +1058,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
     const int64_t total = nch * M;
     const unsigned long long* src = chunk_out + n * total;
     unsigned long long mine;
-    if (nch <= kSortedListsMax) {  // CTA-uniform
-      mine = block_merge_lists(src, M, nch, M, mk, tid, warp, lane);
+    if (nch <= kSortedListsMax && M <= 16) {  // CTA-uniform
+      mine = block_merge_lists(src, M, nch, M, lists, warp, lane);
     } else {
       for (int64_t i = tid; i < total; i += kRouteThreads) mk[i] = __ldcg(src + i);
       __syncthreads();
@@ -1073,7 +1094,15 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
   const unsigned long long* base =
       reinterpret_cast<const unsigned long long*>(static_cast<const char*>(push.own_region) + kPeerHeader) + n * M;
   const int64_t s_list = push.slot_bytes / 8;  // slot r = rank r's keys
-  const unsigned long long merged = block_merge_lists(base, s_list, world, M, mk, tid, warp, lane);
+  unsigned long long merged;
+  if (M <= 16) {  // CTA-uniform
+    merged = block_merge_lists(base, s_list, world, M, lists, warp, lane);
+  } else {
+    for (int l = warp; l < world; l += kRouteThreads / 32)
+      if (lane < M) mk[l * M + lane] = __ldcg(base + l * s_list + lane);
+    __syncthreads();
+    merged = block_topm(mk, static_cast<int64_t>(world) * M, M, lists, topm_scratch, warp, lane);
+  }
   if (warp == 0) finish_row(a, fin, n, lane, merged);
 }
 
@@ -1085,6 +1114,7 @@ __global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteAr
                                                                    unsigned long long* keys_out, int64_t own_lo,
                                                                    int64_t own_hi, int32_t* topi32_own,
                                                                    const srswa_peer wait) {
+  pdl_launch_dependents();
   extern __shared__ __align__(16) unsigned long long mk[];
   __shared__ unsigned long long lists[kRouteThreads / 32][kMaxTopM];
   __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
@@ -1097,8 +1127,8 @@ __global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteAr
   const int M = static_cast<int>(a.M);
   const int64_t total = nlists * M;
   unsigned long long mine;
-  if (nlists <= kSortedListsMax) {  // CTA-uniform
-    mine = block_merge_lists(keys + n * s_row, s_list, nlists, M, mk, tid, warp, lane);
+  if (nlists <= kSortedListsMax && M <= 16) {  // CTA-uniform
+    mine = block_merge_lists(keys + n * s_row, s_list, nlists, M, lists, warp, lane);
   } else {
     for (int64_t l = warp; l < nlists; l += kRouteThreads / 32)
       if (lane < M) mk[l * M + lane] = __ldcg(keys + l * s_list + n * s_row + lane);
@@ -1114,7 +1144,7 @@ __global__ void __launch_bounds__(kRouteThreads) keys_merge_kernel(const RouteAr
   int sel_i = -1;
   bool sel_c = false;
   if (lane < M) unpack_key(mine, sel_v, sel_i, sel_c);
-  route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+  route_epilogue<true>(a, n, lane, sel_v, sel_i, sel_c);  // once per CTA
   if (topi32_own && lane < a.K) {
     const bool own = sel_c && sel_i >= own_lo && sel_i < own_hi;
     topi32_own[n * a.K + lane] = own ? sel_i : -1;
@@ -1319,6 +1349,7 @@ __device__ __forceinline__ void route_tile_select(const RouteArgs& a, const floa
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteArgs a) {
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float rt_smem[];
   const int64_t nblk = a.nblk;
   float* qs = rt_smem;                       // [32][132]
@@ -1471,8 +1502,19 @@ static int select_wide_launch(RouteArgs a, const float* z, int64_t s_z, cudaStre
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   if (a.N >= (1ll << 31)) return SRSWA_ETOOLARGE;
-  select_wide_kernel<<<static_cast<unsigned>(a.N), kRouteThreads, smem, st>>>(a, z, s_z);
-  return srswa_last_launch_status();
+  // may start while the score kernel runs (it waits for the scores itself)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.N), 1, 1);
+  cfg.blockDim = dim3(kRouteThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, select_wide_kernel, a, z, s_z);
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
 
 static int route_chunk_launch(RouteArgs a, void* ws, size_t ws_bytes, cudaStream_t st) {

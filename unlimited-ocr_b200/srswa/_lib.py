@@ -43,7 +43,8 @@ class DecodeDesc(C.Structure):
                 ("s_qn", i64), ("s_qh", i64), ("s_page", i64), ("s_pos", i64), ("s_head", i64),
                 ("s_on", i64), ("s_oh", i64), ("R", i64), ("W", i64), ("s_req", i64),
                 ("rows_per_req", i64), ("idx_is64", C.c_int), ("s_ti_h", i64), ("s_ti_n", i64),
-                ("s_b_h", i64), ("s_b_n", i64), ("nsplit", C.c_int), ("skip_local", C.c_int)]
+                ("s_b_h", i64), ("s_b_n", i64), ("nsplit", C.c_int), ("skip_local", C.c_int),
+                ("overlap", C.c_int)]
 
 
 class KlDesc(C.Structure):

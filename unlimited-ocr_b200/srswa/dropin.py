@@ -76,7 +76,7 @@ _SGLANG_BACKEND = "sglang.srt.layers.attention.unlimited_ocr_v2_backend"
 
 
 def install_sglang(prefix: str = "sglang.srt.layers.attention.unlimited_dash_ops",
-                   backend: str = _SGLANG_BACKEND) -> list[str]:
+                   backend: str = _SGLANG_BACKEND, overlap_router: bool = True) -> list[str]:
     """Point SGLang's DASH serving ops at ``srswa.paged``.
 
     The backend binds the ops by ``from ... import`` when it is imported
@@ -85,7 +85,12 @@ def install_sglang(prefix: str = "sglang.srt.layers.attention.unlimited_dash_ops
     backend module, which holds its own copies.  A module imported later picks
     up the ops modules' (already rebound) attributes.  The torch-only planning
     helpers (kbar_tail_plan, kbar_all_plan, prefill_row2req) stay the
-    reference's.  Returns the qualified names rebound."""
+    reference's.  overlap_router: the backend's own dash_sparse_attn_decode
+    becomes paged.dash_sparse_attn_decode_after_router, since its _forward
+    issues the attend right after route_decode_triton with only views in
+    between, and writes q and the caches before routing
+    (unlimited_ocr_v2_backend.py:1412-1448); the ops module keeps the plain
+    op for other callers.  Returns the qualified names rebound."""
     done = []
     for mod_name, names in _SGLANG_OPS.items():
         mod = sys.modules.get(f"{prefix}.{mod_name}")
@@ -99,6 +104,9 @@ def install_sglang(prefix: str = "sglang.srt.layers.attention.unlimited_dash_ops
         for names in _SGLANG_OPS.values():
             for name in names:
                 if hasattr(be, name):
-                    setattr(be, name, getattr(paged, name))
+                    op = getattr(paged, name)
+                    if overlap_router and name == "dash_sparse_attn_decode":
+                        op = paged.dash_sparse_attn_decode_after_router
+                    setattr(be, name, op)
                     done.append(f"{be.__name__}.{name}")
     return done

@@ -440,14 +440,19 @@ def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_win
 
 def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_blocks, sm_scale,
                   out=None, block_table=None, seq_lens=None, q_pos=None, rows_per_req=1,
-                  valid=None, lse=False, nsplit=0, kv_layout=None, skip_local=False, lse_out=None):
+                  valid=None, lse=False, nsplit=0, kv_layout=None, skip_local=False, lse_out=None,
+                  overlap=False):
     """Sparse decode attend.  q [N,H,D]; paged k/v caches [P, BS, Hkv, D] (any
     strides with D contiguous) indexed by block_table [R,W].  With
     block_table None, kv_layout = (R, W, s_req, s_pos, s_head, Hkv) describes
     one contiguous cache per request (block blk of request r at r*s_req +
     blk*BS*s_pos).  topk_idx [Hkv or 1 (stride 0 ok), N, K] or [N, K]; bias
     like topk_idx or None.  skip_local: attend the selected remote blocks
-    only (a split-KV shard that does not own the window)."""
+    only (a split-KV shard that does not own the window).  overlap: the
+    attend starts on the window keys while the kernel just before it on the
+    stream (the router that made topk_idx / bias) finishes; q, the caches,
+    block_table, seq_lens and q_pos must have been written before that
+    kernel began (srswa_decode_desc.overlap).  Same results either way."""
     N, H, D = q.shape
     assert k_cache.stride() == v_cache.stride()
     if block_table is not None:
@@ -493,11 +498,16 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
         R, W = bt.shape
     else:
         R, W = kv_layout[0], kv_layout[1]
+    # an input converted here was written by a kernel right before the attend:
+    # then the window may not be read early
+    early = all(x is None or (x.data_ptr() == y.data_ptr() and x.dtype == y.dtype)
+                for x, y in ((bt, block_table), (sl, seq_lens), (qp, q_pos)))
     d = L.DecodeDesc(N, H, Hkv, D, ti.shape[-1], block_size, local_blocks, float(sm_scale),
                      L.dtype_code(q), L.dtype_code(k_cache), L.dtype_code(out), q.stride(0), q.stride(1),
                      s_page, s_pos, s_head, out.stride(0), out.stride(1),
                      R, W, s_req, rows_per_req, 1 if ti.dtype == torch.int64 else 0,
-                     s_ti_h, ti.stride(1), s_b_h, s_b_n, int(nsplit), 1 if skip_local else 0)
+                     s_ti_h, ti.stride(1), s_b_h, s_b_n, int(nsplit), 1 if skip_local else 0,
+                     1 if (overlap and early) else 0)
     if ti.dtype not in (torch.int32, torch.int64):
         raise NotImplementedError("topk_idx must be int32 or int64")
     rc = L.lib().srswa_decode_attend(C.byref(d), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),

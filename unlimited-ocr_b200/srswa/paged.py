@@ -35,17 +35,30 @@ SPARSE_BLOCK_SIZE = 128
 @torch.no_grad()
 def dash_sparse_attn_decode(q, k_cache, v_cache, topk_idx, blk_bias, block_table, seq_lens, num_kv_heads,
                             sm_scale, output, decode_query_len, local_blocks=0,
-                            sparse_block_size=SPARSE_BLOCK_SIZE, chunk_width=None, cg_rows=None):
+                            sparse_block_size=SPARSE_BLOCK_SIZE, chunk_width=None, cg_rows=None,
+                            overlap_router=False):
     """Bias-aware block-sparse decode.  q [R*dql, H, D]; caches [P, BS, Hkv, D];
     topk_idx/blk_bias [Hkv, R*dql, K] (stride 0 over heads allowed); output
     [R*dql, H, D] written in place.  chunk_width / cg_rows are accepted for
-    signature compatibility (no scratch geometry to pre-allocate)."""
+    signature compatibility (no scratch geometry to pre-allocate).
+    overlap_router: called right after route_decode on the same stream (as
+    the SGLang backend's _forward does), with q, the caches, block_table and
+    seq_lens written before it: the window keys are attended while the
+    router finishes (ops.decode_attend's overlap)."""
     total_q = q.shape[0]
     assert total_q == seq_lens.shape[0] * decode_query_len
     assert k_cache.shape[2] == num_kv_heads
     ops.decode_attend(q, k_cache, v_cache, topk_idx, blk_bias, block_size=sparse_block_size,
                       local_blocks=local_blocks, sm_scale=sm_scale, out=output, block_table=block_table,
-                      seq_lens=seq_lens, rows_per_req=decode_query_len)
+                      seq_lens=seq_lens, rows_per_req=decode_query_len, overlap=overlap_router)
+
+
+@torch.no_grad()
+def dash_sparse_attn_decode_after_router(*args, **kwargs):
+    """dash_sparse_attn_decode with overlap_router=True: for a caller that
+    issues it right after route_decode on the same stream."""
+    kwargs.setdefault("overlap_router", True)
+    return dash_sparse_attn_decode(*args, **kwargs)
 
 
 @torch.no_grad()

@@ -113,10 +113,12 @@ class CudaBackend:
             out, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:N * H * D + N * H].view(N, H)
         else:
             out, lse = torch.empty(q.shape, device=q.device, dtype=out_dtype), None
+        # overlap: the attend follows the router's last kernel on the stream and
+        # starts on the window keys (q and the caches predate the router)
         return self.ops.decode_attend(q, layer["k_cache"], layer["v_cache"], topi, bias, block_size=block_size,
                                       local_blocks=local_blocks, sm_scale=sm_scale, out=out,
                                       block_table=layer["block_table"], q_pos=q_pos, rows_per_req=N,
-                                      lse=True, skip_local=skip_local, lse_out=lse)
+                                      lse=True, skip_local=skip_local, lse_out=lse, overlap=True)
 
     def gather_keys(self, keys, world):
         """All-gather of the router keys [N, M] -> [world, N, M]."""
