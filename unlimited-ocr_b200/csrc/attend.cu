@@ -140,17 +140,20 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
 
   // ---- this lane's slice of q (pre-scaled into the log2 domain) ----
   const int g = lane / LPK, u = lane % LPK;
-  float qv[8];
-  load8(a.q, seq * a.s_q_seq + t * a.s_q_t + static_cast<int64_t>(h) * a.s_qh + u * 8, a.q_dtype, qv);
+  float2 qv2[4];  // features (2w, 2w + 1): operands of the paired fp32 FMAs
+  {
+    float qv[8];
+    load8(a.q, seq * a.s_q_seq + t * a.s_q_t + static_cast<int64_t>(h) * a.s_qh + u * 8, a.q_dtype, qv);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) qv[e] *= a.q_scale_log2;
+    for (int w = 0; w < 4; ++w) qv2[w] = make_float2(qv[2 * w] * a.q_scale_log2, qv[2 * w + 1] * a.q_scale_log2);
+  }
 
   const int cpb = static_cast<int>(BS / KPC);  // chunks per block
 
   float m = -INFINITY, lsum = 0.f;
-  float o[8];
+  float2 o2[4];  // this lane's 8 output features, paired
 #pragma unroll
-  for (int e = 0; e < 8; ++e) o[e] = 0.f;
+  for (int w = 0; w < 4; ++w) o2[w] = make_float2(0.f, 0.f);
   // after transpose_reduce8 each key's score sits in LPK/8 lanes; count it once
   const int count_lane = (u & (LPK / 8 - 1)) == 0;
   const int my_idx = 4 * ((u & (LPK / 2)) != 0) + 2 * ((u & (LPK / 4)) != 0) + ((u & (LPK / 8)) != 0);
@@ -190,15 +193,16 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
           vr[i] = make_uint4(0, 0, 0, 0);
         }
       }
+      // q.k over this lane's 8 features: paired FMAs (fma.rn.f32x2) into
+      // even / odd partial sums
       float part[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float f[8];
-        unpack8<KVT>(kr[i], f);
-        float acc = 0.f;
+        const uint32_t kw[4] = {kr[i].x, kr[i].y, kr[i].z, kr[i].w};
+        float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc = fmaf(qv[e], f[e], acc);
-        part[i] = acc;
+        for (int w = 0; w < 4; ++w) acc = __ffma2_rn(qv2[w], unpack2<KVT>(kw[w]), acc);
+        part[i] = acc.x + acc.y;
       }
       const float dot = transpose_reduce8<LPK>(part, u);
       const int64_t my_pos = k0 + my_idx * KPI + g;
@@ -209,15 +213,16 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
       const float alpha = exp2f(m - m_use);
       const float pr = exp2f(s2 - m_use);
       lsum = lsum * alpha + (count_lane ? pr : 0.f);
+      const float2 alpha2 = make_float2(alpha, alpha);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] *= alpha;
+      for (int w = 0; w < 4; ++w) o2[w] = __fmul2_rn(o2[w], alpha2);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float pi = __shfl_sync(0xffffffffu, pr, g * LPK + transpose_owner<LPK>(i));
-        float f[8];
-        unpack8<KVT>(vr[i], f);
+        const float2 p2 = make_float2(pi, pi);
+        const uint32_t vw[4] = {vr[i].x, vr[i].y, vr[i].z, vr[i].w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = fmaf(pi, f[e], o[e]);
+        for (int w = 0; w < 4; ++w) o2[w] = __ffma2_rn(p2, unpack2<KVT>(vw[w]), o2[w]);
       }
       m = m_new;
     }
@@ -282,6 +287,10 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
   }
   __syncthreads();
   stream_slots(nw, n_slots);
+
+  float o[8];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) { o[2 * w] = o2[w].x; o[2 * w + 1] = o2[w].y; }
 
   // ---- warp combine: sum l over lanes, o over key groups ----
   lsum = warp_sum(lsum);

@@ -83,6 +83,13 @@ __device__ __forceinline__ void unpack8(const uint4& r, float* f) {
   }
 }
 
+// Two consecutive 16-bit elements (one 32-bit word) -> fp32 pair.
+template <int KVT>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if (KVT == SRSWA_BF16) return make_float2(bf16_lo(w), bf16_hi(w));
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
 int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st);
 
 }  // namespace srswa
