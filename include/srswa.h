@@ -360,6 +360,18 @@ SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, co
                         const int32_t* seq_lens, const int64_t* q_pos, const void* topk_idx,
                         const float* bias, const uint8_t* valid, void* out, float* lse_out,
                         srswa_stream_t stream);
+/* srswa_decode_attend whose results also travel to the peers: out (fp32,
+ * contiguous [N, H, D]) and lse_out ([N, H]) must lie in this rank's own slot
+ * of the exchange `push` (srswa_peer below); every (row, head) result is
+ * stored at the same offset of every region, and the storing CTAs are the
+ * exchange's producer units (the last releases the flags).  The consumer is
+ * srswa_lse_merge with the same exchange as its wait.  The split-KV decode's
+ * partial all-gather fused into the attend; no reference counterpart. */
+SRSWA_API int srswa_decode_attend_push(const srswa_decode_desc* dd, const void* q, const void* k_cache,
+                        const void* v_cache, const int32_t* block_table,
+                        const int32_t* seq_lens, const int64_t* q_pos, const void* topk_idx,
+                        const float* bias, const uint8_t* valid, float* out, float* lse_out,
+                        const srswa_peer* push, srswa_stream_t stream);
 
 /* Paged varlen prefill attend (the SGLang prefill op): rows n of request r
  * are cu_seqlens_q[r] <= n < cu_seqlens_q[r + 1] (int32 [R + 1], device), row

@@ -54,3 +54,46 @@ def test_peer_wait_expires_with_status(cuda):
     assert float(y.sum().item()) == 16.0
     for p in regs:
         assert lib.srswa_peer_region_free(C.c_void_p(p)) == 0
+
+
+@pytest.mark.parametrize("nsplit", [0, 1, 4])
+def test_attend_push_world1_equals_plain(cuda, nsplit):
+    """srswa_decode_attend_push with a one-rank exchange: the partial o / lse
+    land in the rank's own slot, equal to the plain attend's, and the
+    log-sum-exp merge that waits on the exchange returns the same output;
+    three calls in a row (the exchange's epochs advance)."""
+    import math
+    from srswa import ops
+    g = torch.Generator(device=cuda).manual_seed(3)
+    N, H, Hkv, D, BS, L_, K, nblk = 2, 10, 10, 128, 64, 8, 8, 512
+    kc = torch.randn(nblk, BS, Hkv, D, device=cuda, generator=g).to(torch.bfloat16)
+    vc = torch.randn(nblk, BS, Hkv, D, device=cuda, generator=g).to(torch.bfloat16)
+    table = torch.randperm(nblk, device=cuda, generator=g).to(torch.int32)[None]
+    kbar = torch.randn(nblk, 128, device=cuda, generator=g)
+    q = torch.randn(N, H, D, device=cuda, generator=g).to(torch.bfloat16)
+    iq = torch.randn(N, 128, device=cuda, generator=g).to(torch.bfloat16)
+    S = nblk * BS - 5
+    q_pos = torch.tensor([S - 2, S - 1], device=cuda, dtype=torch.int64)
+    sel = ops.route(iq, kbar, block_table=table, q_pos=q_pos, rows_per_seq=N, want=("topi32", "bias"),
+                    block_size=BS, local_blocks=L_, topk=K, topm=16, idx_scale=128 / math.sqrt(128), floor=1e-4,
+                    sigma=1.0)
+    kw = dict(block_size=BS, local_blocks=L_, sm_scale=1 / math.sqrt(D), block_table=table, q_pos=q_pos,
+              rows_per_req=N, lse=True, nsplit=nsplit)
+    ref_o, ref_l = ops.decode_attend(q, kc, vc, sel["topi32"], sel["bias"], out=torch.empty(N, H, D, device=cuda),
+                                     **kw)
+    n4 = -(-(N * H * D + N * H) // 4) * 4
+    ex = PeerAllGather(n4 * 4)
+    for rep in range(3):
+        buf = ex.own_slot((n4,), torch.float32)
+        buf.zero_()
+        o, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:N * H * D + N * H].view(N, H)
+        ops.decode_attend(q, kc, vc, sel["topi32"], sel["bias"], out=o, lse_out=lse, push=ex.peer, **kw)
+        parts = ex.slots((n4,), torch.float32)
+        merged = ops.lse_merge(parts[:, :N * H * D].view(1, N, H, D), parts[:, N * H * D:N * H * D + N * H].view(1, N, H),
+                               out_dtype=torch.float32, wait=ex.peer)[0]
+        torch.cuda.synchronize()
+        assert torch.equal(o, ref_o) and torch.equal(lse, ref_l)
+        torch.testing.assert_close(merged, ref_o, rtol=1e-6, atol=1e-6)
+    assert int(ex.counter.item()) == 3
+    ex.check()
+    ex.close()

@@ -78,6 +78,34 @@ __device__ __forceinline__ int64_t block_offset(const AttendArgs& a, int64_t seq
 // MINB = CTAs per SM the register allocation must allow: 4 (128 registers)
 // for the bandwidth-bound loads; 5 (96 registers, a few spills) for light
 // loads, where a whole 2-way split then fits in one wave.
+// One output value: to a.out, or with a.push (fp32 out inside this rank's
+// own slot) to the same offset of every region of the exchange.
+__device__ __forceinline__ void put_out(const AttendArgs& a, int64_t i, float v) {
+  if (!a.push.regions) {
+    store_elem(a.out, i, a.out_dtype, v);
+    return;
+  }
+  const int64_t off = reinterpret_cast<const char*>(static_cast<const float*>(a.out) + i) -
+                      static_cast<const char*>(a.push.own_region);
+  for (int d = 0; d < static_cast<int>(a.push.world); ++d)
+    *reinterpret_cast<float*>(static_cast<char*>(a.push.regions[d]) + off) = v;
+}
+__device__ __forceinline__ void put_lse(const AttendArgs& a, int64_t i, float v) {
+  if (!a.push.regions) {
+    a.lse_out[i] = v;
+    return;
+  }
+  const int64_t off = reinterpret_cast<const char*>(a.lse_out + i) - static_cast<const char*>(a.push.own_region);
+  for (int d = 0; d < static_cast<int>(a.push.world); ++d)
+    *reinterpret_cast<float*>(static_cast<char*>(a.push.regions[d]) + off) = v;
+}
+// after a storing CTA's puts: it is one producer unit of the exchange
+__device__ __forceinline__ void push_done(const AttendArgs& a) {
+  if (!a.push.regions) return;
+  __syncthreads();
+  if (threadIdx.x == 0) peer_unit_done(a.push, static_cast<unsigned>(a.N * a.H));
+}
+
 template <int D, int KVT, int MINB>
 __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const AttendArgs a) {
   constexpr int LPK = D / 8;     // lanes per key row
@@ -327,8 +355,9 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
   if (nsplit == 1) {
     __syncthreads();
     const float inv = c_l > 0.f ? 1.f / c_l : 0.f;
-    for (int d = tid; d < D; d += kAttendThreads) store_elem(a.out, obase + d, a.out_dtype, c_o[d] * inv);
-    if (tid == 0 && a.lse_out) a.lse_out[lbase] = c_l > 0.f ? (c_m + log2f(c_l)) * kLn2 : -INFINITY;
+    for (int d = tid; d < D; d += kAttendThreads) put_out(a, obase + d, c_o[d] * inv);
+    if (tid == 0 && a.lse_out) put_lse(a, lbase, c_l > 0.f ? (c_m + log2f(c_l)) * kLn2 : -INFINITY);
+    push_done(a);
     return;
   }
 
@@ -347,9 +376,10 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
       float acc = 0.f;
       for (int s = 0; s < nsplit; ++s)
         acc += cluster.map_shared_rank(c_o, s)[d] * exp2f(*cluster.map_shared_rank(&c_m, s) - Mgu);
-      store_elem(a.out, obase + d, a.out_dtype, acc * inv);
+      put_out(a, obase + d, acc * inv);
     }
-    if (tid == 0 && a.lse_out) a.lse_out[lbase] = Lg > 0.f ? (Mg + log2f(Lg)) * kLn2 : -INFINITY;
+    if (tid == 0 && a.lse_out) put_lse(a, lbase, Lg > 0.f ? (Mg + log2f(Lg)) * kLn2 : -INFINITY);
+    push_done(a);  // CTA-uniform: the cluster's first CTA stores
   }
   cluster.sync();
 }
@@ -475,7 +505,8 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   if (a.K + a.LW / a.BS + 2 > kAttendMaxSlots) return SRSWA_ETOOLARGE;
   if (a.H >= 65536) return SRSWA_ETOOLARGE;
   int nsplit = a.nsplit;
-  a.split_tail = nsplit <= 0 ? 1 : 0;
+  // a push counts its producer units over one launch: no second launch
+  a.split_tail = (nsplit <= 0 && !a.push.regions) ? 1 : 0;
   if (nsplit <= 0) nsplit = auto_nsplit(a, D, kv_dtype);
   if (nsplit < 1 || nsplit > 8) return SRSWA_EUNSUPPORTED;
   if (a.N * 8 >= (1ll << 31)) return SRSWA_ETOOLARGE;
@@ -535,11 +566,47 @@ using namespace srswa;
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+static int decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache, const void* v_cache,
+                         const int32_t* block_table, const int32_t* seq_lens, const int64_t* q_pos,
+                         const void* topk_idx, const float* bias, const uint8_t* valid, void* out, float* lse_out,
+                         const srswa_peer* push, srswa_stream_t stream);
+
 extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache,
                                    const void* v_cache, const int32_t* block_table,
                                    const int32_t* seq_lens, const int64_t* q_pos,
                                    const void* topk_idx, const float* bias, const uint8_t* valid,
                                    void* out, float* lse_out, srswa_stream_t stream) {
+  return decode_attend(dd, q, k_cache, v_cache, block_table, seq_lens, q_pos, topk_idx, bias, valid, out, lse_out,
+                       nullptr, stream);
+}
+
+extern "C" int srswa_decode_attend_push(const srswa_decode_desc* dd, const void* q, const void* k_cache,
+                                        const void* v_cache, const int32_t* block_table,
+                                        const int32_t* seq_lens, const int64_t* q_pos,
+                                        const void* topk_idx, const float* bias, const uint8_t* valid,
+                                        float* out, float* lse_out, const srswa_peer* push,
+                                        srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(push && push->regions && push->own_region && push->counter && push->tickets &&
+                      push->world >= 1 && push->world <= 32 && push->rank >= 0 && push->rank < push->world,
+                  SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(dd && out && lse_out && dd->out_dtype == SRSWA_F32, SRSWA_EINVAL);
+  // o and lse must lie in this rank's own slot, contiguous [N, H, D] and [N, H]
+  const char* slot = static_cast<const char*>(push->own_region) + kPeerHeader + push->rank * push->slot_bytes;
+  const char* o0 = reinterpret_cast<const char*>(out);
+  const char* l0 = reinterpret_cast<const char*>(lse_out);
+  const int64_t ob = dd->N * dd->H * dd->D * 4, lb = dd->N * dd->H * 4;
+  SRSWA_CHECK_ARG(dd->s_on == dd->H * dd->D && dd->s_oh == dd->D, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(o0 >= slot && o0 + ob <= slot + push->slot_bytes && l0 >= slot &&
+                      l0 + lb <= slot + push->slot_bytes,
+                  SRSWA_EINVAL);
+  return decode_attend(dd, q, k_cache, v_cache, block_table, seq_lens, q_pos, topk_idx, bias, valid, out, lse_out,
+                       push, stream);
+}
+
+static int decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache, const void* v_cache,
+                         const int32_t* block_table, const int32_t* seq_lens, const int64_t* q_pos,
+                         const void* topk_idx, const float* bias, const uint8_t* valid, void* out, float* lse_out,
+                         const srswa_peer* push, srswa_stream_t stream) {
   SRSWA_CHECK_ARG(dd && q && k_cache && v_cache && out, SRSWA_EINVAL);
   const srswa_decode_desc& d = *dd;
   SRSWA_CHECK_ARG(d.N >= 0 && d.H > 0 && d.Hkv > 0 && d.H % d.Hkv == 0, SRSWA_EINVAL);
@@ -568,6 +635,7 @@ extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, c
   a.out = out; a.s_o_seq = d.rows_per_req * d.s_on; a.s_o_t = d.s_on; a.s_oh = d.s_oh;
   a.lse_out = lse_out; a.s_l_seq = d.rows_per_req * d.H; a.s_l_t = d.H;
   a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0; a.overlap = d.overlap ? 1 : 0;
+  if (push) a.push = *push;
   return attend_rows_launch(a, d.D, d.kv_dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -65,6 +65,9 @@ struct AttendArgs {
   int split_tail;  // the split was left open: a nearly empty last wave may be split
   int heads_inner; // grid (heads x splits, rows) instead of (rows x splits, heads)
   int overlap;     // window keys before pdl_wait (srswa_decode_desc.overlap)
+  srswa_peer push; // regions != NULL: out / lse_out lie in this rank's own slot
+                   // and every (row, head) result goes to that slot of every
+                   // region; the storing CTAs are the exchange's producer units
 };
 
 template <int KVT>

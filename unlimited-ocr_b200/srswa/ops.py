@@ -441,7 +441,7 @@ def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_win
 def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_blocks, sm_scale,
                   out=None, block_table=None, seq_lens=None, q_pos=None, rows_per_req=1,
                   valid=None, lse=False, nsplit=0, kv_layout=None, skip_local=False, lse_out=None,
-                  overlap=False):
+                  overlap=False, push=None):
     """Sparse decode attend.  q [N,H,D]; paged k/v caches [P, BS, Hkv, D] (any
     strides with D contiguous) indexed by block_table [R,W].  With
     block_table None, kv_layout = (R, W, s_req, s_pos, s_head, Hkv) describes
@@ -452,7 +452,10 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
     attend starts on the window keys while the kernel just before it on the
     stream (the router that made topk_idx / bias) finishes; q, the caches,
     block_table, seq_lens and q_pos must have been written before that
-    kernel began (srswa_decode_desc.overlap).  Same results either way."""
+    kernel began (srswa_decode_desc.overlap).  Same results either way.
+    push (an srswa_peer): out / lse_out are fp32 views of this rank's own
+    slot of that exchange and the results are also stored into every peer's
+    region (srswa_decode_attend_push)."""
     N, H, D = q.shape
     assert k_cache.stride() == v_cache.stride()
     if block_table is not None:
@@ -510,6 +513,12 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
                      1 if (overlap and early) else 0)
     if ti.dtype not in (torch.int32, torch.int64):
         raise NotImplementedError("topk_idx must be int32 or int64")
+    if push is not None:
+        rc = L.lib().srswa_decode_attend_push(C.byref(d), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                              L.ptr(bt), L.ptr(sl), L.ptr(qp), ti.data_ptr(), L.ptr(b), L.ptr(vd),
+                                              out.data_ptr(), L.ptr(lse_t), C.byref(push), L.stream_of(q))
+        L.check(rc, "srswa_decode_attend_push")
+        return (out, lse_t) if lse else out
     rc = L.lib().srswa_decode_attend(C.byref(d), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                                      L.ptr(bt), L.ptr(sl), L.ptr(qp), ti.data_ptr(), L.ptr(b), L.ptr(vd),
                                      out.data_ptr(), L.ptr(lse_t), L.stream_of(q))

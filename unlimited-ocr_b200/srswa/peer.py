@@ -83,6 +83,12 @@ class PeerAllGather:
         nbytes = torch.Size(shape).numel() * torch.empty(0, dtype=dtype).element_size()
         return self._slots[:, :nbytes].view(dtype).view((self.world,) + tuple(shape))
 
+    def own_slot(self, shape, dtype) -> torch.Tensor:
+        """View of this rank's own slot in its own region: a producer kernel
+        that pushes itself (srswa_decode_attend_push) writes its payload here."""
+        nbytes = torch.Size(shape).numel() * torch.empty(0, dtype=dtype).element_size()
+        return self._slots[self.rank, :nbytes].view(dtype).view(tuple(shape))
+
     def push(self, payload: torch.Tensor) -> torch.Tensor:
         """Producer half only (one launch); a consumer kernel given
         ``self.peer`` as its wait reads the returned view."""

@@ -189,8 +189,24 @@ class PeerBackend(CudaBackend):
             return self._shard_select(idx_q, layer, plan, q_pos, rp, self.keys_x.peer)
         return super().select(idx_q, layer, plan, q_pos, rp)
 
+    def attend(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local,
+               out_dtype=torch.float32):
+        if not self.fused or out_dtype != torch.float32:
+            return super().attend(q, layer, topi, bias, q_pos, block_size=block_size, local_blocks=local_blocks,
+                                  sm_scale=sm_scale, skip_local=skip_local, out_dtype=out_dtype)
+        # fused: the attend writes its partial into this rank's own slot and
+        # stores it into every peer's region itself (no push launch)
+        N, H, D = q.shape
+        buf = self.part_x.own_slot((-(-(N * H * D + N * H) // 4) * 4,), torch.float32)
+        out, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:N * H * D + N * H].view(N, H)
+        return self.ops.decode_attend(q, layer["k_cache"], layer["v_cache"], topi, bias, block_size=block_size,
+                                      local_blocks=local_blocks, sm_scale=sm_scale, out=out,
+                                      block_table=layer["block_table"], q_pos=q_pos, rows_per_req=N, lse=True,
+                                      skip_local=skip_local, lse_out=lse, overlap=True, push=self.part_x.peer)
+
     def gather_partials(self, buf, world):
-        return self.part_x.push(buf) if self.fused else self.part_x(buf)
+        # fused: the attend has already stored the partials into every region
+        return self.part_x.slots(buf.shape, buf.dtype) if self.fused else self.part_x(buf)
 
     def lse_merge(self, o_parts, lse_parts, out_dtype):
         return self.ops.lse_merge(o_parts, lse_parts, out_dtype=out_dtype,
