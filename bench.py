@@ -940,13 +940,39 @@ def longctx_measure(args):
             torch.cuda.current_stream().wait_stream(side)
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def waits_expired():
+        """Any rank's bounded peer wait expired (collective: every rank
+        decides the same way)."""
+        if backend is None:
+            return False
+        torch.cuda.synchronize()
+        bad = torch.tensor([int(int(backend.keys_x.status.item()) != 0 or int(backend.part_x.status.item()) != 0)],
+                           device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        return bool(bad.item())
+
+    def failed(why):
+        if backend is not None:
+            backend.close()            # collective: every rank
+        del layers[:], decs[:], outs[:]
+        torch.cuda.empty_cache()
+        return None if rank != 0 else {"error": why, "n_gpus": world}
+
     if world > 1:
         dist.barrier()
+        step()                         # one eager step first: a peer that never arrives shows here
+        if waits_expired():
+            return failed("a bounded peer wait expired in the first step; not timed")
     clocks = Clocks(local)
     clocks.start()
     times, g = timed_graph(step, args.steps, max(args.warmup, 3), flush, not args.no_graph)
     clk = clocks.stop()
     ms = sum(times) / len(times)
+    if waits_expired():
+        if g is not None:
+            del g
+        return failed("a bounded peer wait expired during the timed steps")
     # algorithmic bytes of this rank: k_bar of its remote-candidate blocks,
     # the K/V rows of the keys it attends (its selected blocks + the window
     # on its owner), q and o; the selection is recomputed once, untimed, with
@@ -970,8 +996,7 @@ def longctx_measure(args):
     if g is not None:
         del g
     if backend is not None:
-        backend.check()
-        backend.close()            # collective: every rank
+        backend.close()            # collective: every rank (waits checked above)
     del layers, decs, outs
     torch.cuda.empty_cache()
     if rank != 0:
@@ -1153,15 +1178,23 @@ def main():
     torch.cuda.empty_cache()
     extras = {}
     if not args.no_extras:
-        extras["prefill"] = dense_measure(args, False)
-        extras["train"] = dense_measure(args, True)
-        extras["longctx"] = longctx_measure(args)
+        # a failed extra is reported in its key; the headline line still prints
+        for key, fn in (("prefill", lambda: dense_measure(args, False)), ("train", lambda: dense_measure(args, True)),
+                        ("longctx", lambda: longctx_measure(args))):
+            try:
+                extras[key] = fn()
+            except Exception as e:  # noqa: BLE001
+                extras[key] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+                torch.cuda.empty_cache()
     if rank == 0:
         line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        try:
+            dist.barrier()
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001  (a rank whose extra failed in a collective)
+            pass
     return 0
 
 

@@ -536,6 +536,7 @@ __global__ void lse_merge_kernel(const float* __restrict__ o_parts, const float*
                                  int64_t C, int64_t NH, int64_t D, int64_t s_o, int64_t s_l, void* out,
                                  int out_dtype, float* lse_out, const srswa_peer wait) {
   const int64_t nh = blockIdx.x;
+  pdl_wait();  // launched to overlap the kernel ahead: its writes are visible from here
   if (wait.regions) {  // the parts are the peers' pushes into this rank's region
     if (threadIdx.x == 0) peer_wait_all(wait, gridDim.x);
     __syncthreads();
@@ -688,7 +689,18 @@ extern "C" int srswa_lse_merge(const float* o_parts, const float* lse_parts, int
   SRSWA_CHECK_ARG(s_o_part >= N * H * D && s_l_part >= N * H, SRSWA_EINVAL);
   if (N == 0) return 0;
   SRSWA_CHECK_ARG(N * H < (1ll << 31), SRSWA_ETOOLARGE);
-  lse_merge_kernel<<<static_cast<unsigned>(N * H), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      o_parts, lse_parts, C, N * H, D, s_o_part, s_l_part, out, out_dtype, lse_out, pw);
-  return srswa_last_launch_status();
+  // may launch while the kernel ahead (the attend making the parts) runs:
+  // the kernel waits for it before reading anything
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(N * H), 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, lse_merge_kernel, o_parts, lse_parts, C, N * H, D, s_o_part,
+                                           s_l_part, out, out_dtype, lse_out, pw);
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
