@@ -894,7 +894,7 @@ def longctx_measure(args):
     if world > 1 and args.exchange != "nccl":
         from srswa.split_kv import PeerBackend
         backend = PeerBackend(rows=1, topm=M, heads=H, head_dim=D,   # one for all layers
-                              fused=args.exchange == "p2p")
+                              mode={"p2p": "ll", "p2p-flag": "flag", "p2p-launch": "launch"}[args.exchange])
     pool = torch.randn(64 << 20, generator=gen).to(torch.bfloat16).to(dev)
     hc = torch.zeros(DI, device=dev)
     for _ in range(nl):
@@ -1005,8 +1005,12 @@ def longctx_measure(args):
             "ms_per_step": ms, "us_per_step": ms * 1e3, "scaling": "strong", "dtype": "bf16",
             "config": {"workload": "cfg5 attention share: 12-layer split-KV decode, one 1M-token sequence",
                        "seq_len": S0, "layers": nl, "K": K, "LW": L * BS, "parallelism": f"split-kv{world}",
-                       "exchange": (("peer-memory push + bounded flag wait (CUDA IPC over NVLink), "
-                                     + ("in the router / merge kernels" if backend.fused else "own launches"))
+                       "exchange": ({"ll": "peer memory (CUDA IPC over NVLink), LL words stored and polled by the "
+                                           "router / attend / merge kernels",
+                                     "flag": "peer memory (CUDA IPC over NVLink), payload + released flags in the "
+                                             "router / attend / merge kernels",
+                                     "launch": "peer memory (CUDA IPC over NVLink), push + flag-wait launches"}
+                                    [backend.mode]
                                     if backend is not None else ("NCCL all-gather" if world > 1 else "none")),
                        "l2": "flushed before every timed step", "graph": not args.no_graph},
             "roofline": {"bound": "latency", "achieved": byts / (ms * 1e-3) / 1e9, "peak": hbm * world,

@@ -39,7 +39,9 @@ extern "C" {
 typedef struct CUstream_st* srswa_stream_t; /* == cudaStream_t */
 
 /* element types */
-enum { SRSWA_F32 = 0, SRSWA_BF16 = 1, SRSWA_F16 = 2 };
+enum { SRSWA_F32 = 0, SRSWA_BF16 = 1, SRSWA_F16 = 2, SRSWA_F8E4M3 = 3, SRSWA_F8E5M2 = 4 };
+/* (the fp8 codes are accepted where an entry point says so: the decode /
+ * prefill attend's K/V caches) */
 
 /* negative status codes */
 enum {
@@ -52,7 +54,8 @@ enum {
 };
 
 /* A peer-memory exchange region (see "peer exchange" below); entry points
- * that take one accept NULL = no exchange. */
+ * that take one accept NULL = no exchange.  ll selects the protocol: 0 =
+ * payload + per-source flags, 1 = LL words (see below). */
 typedef struct {
   void* const* regions;
   void* own_region;
@@ -60,6 +63,7 @@ typedef struct {
   uint64_t* counter;
   uint32_t* tickets;
   int32_t* status;
+  int64_t ll;
 } srswa_peer;
 
 /* Library version (major*10000 + minor*100 + patch) and status text. */
@@ -326,7 +330,10 @@ SRSWA_API int srswa_gather_bwd_noalloc_status(int* out, srswa_stream_t stream);
  * local keys: max(0, p-LW+1) <= pos <= p (unbiased), LW = L*BS.
  * out [N,H,D] (out_dtype, strides), lse_out [N,H] fp32 natural log (optional).
  * nsplit: CTAs per (row, head) merged on-chip through a thread-block cluster
- * (0 = choose).  Replaces dash_sparse_attn_decode + K9/K10
+ * (0 = choose).  kv_dtype: SRSWA_BF16, SRSWA_F16, or SRSWA_F8E4M3 /
+ * SRSWA_F8E5M2 caches (converted exactly to fp32 in the kernel; the
+ * reference's use_fp8 path casts them to the query dtype, attend_triton.py:545,
+ * 626).  Replaces dash_sparse_attn_decode + K9/K10
  * (whl:.../unlimited_dash_ops/attend_triton.py:307-518, 600-715; common.py:43-89)
  * and _decode_attend (hf-model-code/modeling_deepseekv2.py:455-481). */
 typedef struct {
@@ -361,11 +368,14 @@ SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, co
                         const float* bias, const uint8_t* valid, void* out, float* lse_out,
                         srswa_stream_t stream);
 /* srswa_decode_attend whose results also travel to the peers: out (fp32,
- * contiguous [N, H, D]) and lse_out ([N, H]) must lie in this rank's own slot
- * of the exchange `push` (srswa_peer below); every (row, head) result is
- * stored at the same offset of every region, and the storing CTAs are the
- * exchange's producer units (the last releases the flags).  The consumer is
- * srswa_lse_merge with the same exchange as its wait.  The split-KV decode's
+ * contiguous [N, H, D]) and lse_out ([N, H]).  Flag protocol: out and lse_out
+ * must lie in this rank's own slot of the exchange `push` (srswa_peer
+ * below); every (row, head) result is stored at the same offset of every
+ * region, and the storing CTAs are the exchange's producer units (the last
+ * releases the flags).  LL protocol: out / lse_out are any buffers (the local
+ * copy); element e of the packed o-then-lse partial goes to LL word e of
+ * every region.  The consumer is srswa_lse_merge with the same exchange as
+ * its wait (LL: o_parts / lse_parts may be NULL, C = world).  The split-KV decode's
  * partial all-gather fused into the attend; no reference counterpart. */
 SRSWA_API int srswa_decode_attend_push(const srswa_decode_desc* dd, const void* q, const void* k_cache,
                         const void* v_cache, const int32_t* block_table,
@@ -478,7 +488,20 @@ SRSWA_API int srswa_gather_kl_bwd(const srswa_kl_desc* g, const void* idx_q, con
  * No NCCL, no TMA, no multicast: peer bytes move only by plain stores.  A
  * rank must not start exchange e+1 on a region before its consumers of e
  * have read it; stream order gives this when two regions alternate (router
- * keys, then attention partials). */
+ * keys, then attention partials).
+ *
+ * LL protocol (ll = 1): every 32-bit payload word travels as one 8-byte
+ * word (payload, epoch = low 32 bits of *counter + 1) in one aligned store,
+ * which is single-copy atomic; a consumer polls each word it reads until its
+ * epoch matches (bounded, status 501 on expiry), so no fence, flag or
+ * producer ticket is needed and the flag header is unused.  The consumer
+ * CTAs still count themselves (tickets[1]) and the last advances *counter.
+ * Slot k of a region is then 8-byte word k of the payload's 32-bit word k.
+ * Taken by srswa_route_shard_select (the router keys: row n, key j as words
+ * 2 (n M + j) and 2 (n M + j) + 1, low half first), srswa_decode_attend_push
+ * (partial element e of the packed [N, H, D] o then [N, H] lse) and
+ * srswa_lse_merge (wait); the other entry points refuse an LL region
+ * (SRSWA_EUNSUPPORTED). */
 SRSWA_API int srswa_peer_region_size(int64_t world, int64_t slot_bytes, size_t* out);
 SRSWA_API int srswa_peer_region_alloc(size_t bytes, void** out);
 SRSWA_API int srswa_peer_region_free(void* region);

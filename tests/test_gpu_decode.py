@@ -207,3 +207,41 @@ def test_decode_overlap_after_router_equals_plain(cuda, R, nsplit):
     ref, _ = O.paged_decode(q[rows], kc, vc, O.dedup_rows(sel_np["topi32"][rows])[None], sel_np["bias"][rows][None],
                             bt[rows], np.asarray(seqs)[rows], 0.088, 1, L, BS)
     np.testing.assert_allclose(outs[1].cpu().numpy()[rows], ref, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("fp8", [torch.float8_e4m3fn, torch.float8_e5m2])
+@pytest.mark.parametrize("D", [128, 64])
+def test_decode_fp8_cache_equals_bf16_of_same_values(cuda, fp8, D):
+    """FP8 K/V caches (the reference's use_fp8 path, attend_triton.py:545,626:
+    the cache is cast to the query dtype before the dots): the attend on fp8
+    caches equals, bit for bit, the attend on the same values held in bf16
+    (fp8 -> bf16 is exact), decode and paged prefill alike; and the oracle on
+    the dequantised values."""
+    rng = np.random.default_rng(D + (3 if fp8 == torch.float8_e4m3fn else 5))
+    R, H, Hkv, BS, L, K = 6, 8, 4, 64, 8, 8
+    seqs = list(rng.integers(700, 3000, R))
+    bt, kc, vc, q, idx, bias = _paged_case(rng, R, H, Hkv, D, BS, L, K, seqs)
+    k8 = T(kc, cuda).to(fp8)
+    v8 = T(vc, cuda).to(fp8)
+    kb, vb = k8.to(torch.bfloat16), v8.to(torch.bfloat16)
+    args = dict(block_size=BS, local_blocks=L, sm_scale=0.1, block_table=T(bt, cuda),
+                seq_lens=T(np.asarray(seqs, np.int32), cuda))
+    qt, it, bt_ = T(q, cuda, torch.bfloat16), T(idx, cuda), T(bias, cuda)
+    o8 = ops.decode_attend(qt, k8, v8, it, bt_, out=torch.empty(R, H, D, device=cuda), **args)
+    ob = ops.decode_attend(qt, kb, vb, it, bt_, out=torch.empty(R, H, D, device=cuda), **args)
+    # paged prefill (K8 op): the last 3 positions of each request as rows
+    cu = torch.arange(0, 3 * R + 1, 3, device=cuda, dtype=torch.int32)
+    pre = T(np.asarray(seqs, np.int32) - 3, cuda)
+    qp = torch.repeat_interleave(qt, 3, dim=0)
+    ip = torch.repeat_interleave(it, 3, dim=0)
+    bp = torch.repeat_interleave(bt_, 3, dim=0)
+    p8 = ops.prefill_attend(qp, k8, v8, ip, bp, block_table=T(bt, cuda), cu_seqlens_q=cu, prefix_lens=pre,
+                            block_size=BS, local_blocks=L, sm_scale=0.1, out=torch.empty(3 * R, H, D, device=cuda))
+    pb = ops.prefill_attend(qp, kb, vb, ip, bp, block_table=T(bt, cuda), cu_seqlens_q=cu, prefix_lens=pre,
+                            block_size=BS, local_blocks=L, sm_scale=0.1, out=torch.empty(3 * R, H, D, device=cuda))
+    torch.cuda.synchronize()
+    assert torch.equal(o8, ob)
+    assert torch.equal(p8, pb)
+    ref, _ = O.paged_decode(q, k8.float().cpu().numpy(), v8.float().cpu().numpy(), O.dedup_rows(idx)[None],
+                            bias[None], bt, np.asarray(seqs), 0.1, 1, L, BS)
+    np.testing.assert_allclose(o8.cpu().numpy(), ref, rtol=1e-4, atol=1e-4)

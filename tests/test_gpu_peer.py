@@ -56,8 +56,9 @@ def test_peer_wait_expires_with_status(cuda):
         assert lib.srswa_peer_region_free(C.c_void_p(p)) == 0
 
 
+@pytest.mark.parametrize("ll", [False, True])
 @pytest.mark.parametrize("nsplit", [0, 1, 4])
-def test_attend_push_world1_equals_plain(cuda, nsplit):
+def test_attend_push_world1_equals_plain(cuda, nsplit, ll):
     """srswa_decode_attend_push with a one-rank exchange: the partial o / lse
     land in the rank's own slot, equal to the plain attend's, and the
     log-sum-exp merge that waits on the exchange returns the same output;
@@ -82,15 +83,20 @@ def test_attend_push_world1_equals_plain(cuda, nsplit):
     ref_o, ref_l = ops.decode_attend(q, kc, vc, sel["topi32"], sel["bias"], out=torch.empty(N, H, D, device=cuda),
                                      **kw)
     n4 = -(-(N * H * D + N * H) // 4) * 4
-    ex = PeerAllGather(n4 * 4)
+    ex = PeerAllGather(n4 * 4 * (2 if ll else 1), ll=ll)
     for rep in range(3):
-        buf = ex.own_slot((n4,), torch.float32)
+        # flag protocol: the local copy is this rank's own slot; LL: any buffer
+        buf = torch.empty(n4, device=cuda) if ll else ex.own_slot((n4,), torch.float32)
         buf.zero_()
         o, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:N * H * D + N * H].view(N, H)
         ops.decode_attend(q, kc, vc, sel["topi32"], sel["bias"], out=o, lse_out=lse, push=ex.peer, **kw)
-        parts = ex.slots((n4,), torch.float32)
-        merged = ops.lse_merge(parts[:, :N * H * D].view(1, N, H, D), parts[:, N * H * D:N * H * D + N * H].view(1, N, H),
-                               out_dtype=torch.float32, wait=ex.peer)[0]
+        if ll:
+            merged = ops.lse_merge_exchange(ex.peer, 1, N, H, D, cuda)[0]
+        else:
+            parts = ex.slots((n4,), torch.float32)
+            merged = ops.lse_merge(parts[:, :N * H * D].view(1, N, H, D),
+                                   parts[:, N * H * D:N * H * D + N * H].view(1, N, H),
+                                   out_dtype=torch.float32, wait=ex.peer)[0]
         torch.cuda.synchronize()
         assert torch.equal(o, ref_o) and torch.equal(lse, ref_l)
         torch.testing.assert_close(merged, ref_o, rtol=1e-6, atol=1e-6)

@@ -63,8 +63,8 @@ def test_sharded_route_equals_whole_row(cuda, nblk, nshard, paged):
         torch.testing.assert_close(merged["bias"], full["bias"], rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("nblk,exchange", [(16384, False), (16384, True), (100, False), (100, True),
-                                            (3000, True)])
+@pytest.mark.parametrize("nblk,exchange", [(16384, None), (16384, "flag"), (16384, "ll"), (100, None),
+                                            (100, "flag"), (100, "ll"), (3000, "flag"), (3000, "ll")])
 def test_shard_select_equals_two_stages(cuda, nblk, exchange):
     """srswa_route_shard_select (one launch: shard keys, optional exchange of
     one rank, merge and epilogue) = shard keys + merge, bit for bit."""
@@ -77,7 +77,7 @@ def test_shard_select_equals_two_stages(cuda, nblk, exchange):
     q_pos = torch.tensor([S - 1, S // 3, 9 * 64 + 1], device=cuda, dtype=torch.int64)
     p = {k: v for k, v in RP.items() if k not in ("block_size", "local_blocks")}
     own = (nblk // 4, nblk // 2)
-    ex = PeerAllGather(N * RP["topm"] * 8, None, cuda) if exchange else None
+    ex = None if exchange is None else PeerAllGather(N * RP["topm"] * 16, None, cuda, ll=exchange == "ll")
     for rep in range(3):   # the exchange's epochs advance from call to call
         keys = ops.route_shard_keys(idx_q, kbar, block_offset=0, nblk_local=nblk, nblk_total=nblk, q_pos=q_pos,
                                     rows_per_seq=N, **RP)

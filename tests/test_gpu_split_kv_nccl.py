@@ -44,9 +44,9 @@ def _worker(rank, world, port, result_q, exchange="nccl"):
         S = NBLK * BS - 5
         q_pos = torch.tensor([S - 2, S - 1], device=dev, dtype=torch.int64)
         backend = None
-        if exchange == "p2p":
+        if exchange != "nccl":   # p2p-<mode>: the peer-memory exchange
             from srswa.split_kv import PeerBackend
-            backend = PeerBackend(rows=2, topm=RP["topm"], heads=H, head_dim=D)
+            backend = PeerBackend(rows=2, topm=RP["topm"], heads=H, head_dim=D, mode=exchange[4:])
         dec = SplitKVDecode(nblk_total=NBLK, nblk_filled=NBLK, sm_scale=1 / math.sqrt(D), rank=rank, world=world,
                             backend=backend, **RP)
         lo, hi = dec.plan.lo, dec.plan.hi
@@ -57,7 +57,7 @@ def _worker(rank, world, port, result_q, exchange="nccl"):
         qd, iqd = q.to(dev), iq.to(dev)
         outs = [dec.step(qd, iqd, q_pos, layer, p_range=(S - 2, S - 1), out_dtype=torch.float32).clone()
                 for _ in range(2)]          # two steps: the exchange epochs advance
-        if exchange == "p2p":
+        if exchange != "nccl":
             # captured once, replayed: the epochs advance on the device
             s_ = torch.cuda.Stream()
             s_.wait_stream(torch.cuda.current_stream())
@@ -83,7 +83,7 @@ def _worker(rank, world, port, result_q, exchange="nccl"):
             torch.cuda.synchronize()
             result_q.put(("ok", max(float((o - ref).abs().max()) for o in outs)))
         torch.cuda.synchronize()
-        if exchange == "p2p":
+        if exchange != "nccl":
             dec.backend.close()
         dist.barrier()
     except Exception as e:
@@ -93,7 +93,7 @@ def _worker(rank, world, port, result_q, exchange="nccl"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+@pytest.mark.parametrize("exchange", ["nccl", "p2p-ll", "p2p-flag", "p2p-launch"])
 def test_split_kv_two_gpus_matches_one_gpu(exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")

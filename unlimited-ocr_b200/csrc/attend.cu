@@ -78,11 +78,17 @@ __device__ __forceinline__ int64_t block_offset(const AttendArgs& a, int64_t seq
 // MINB = CTAs per SM the register allocation must allow: 4 (128 registers)
 // for the bandwidth-bound loads; 5 (96 registers, a few spills) for light
 // loads, where a whole 2-way split then fits in one wave.
-// One output value: to a.out, or with a.push (fp32 out inside this rank's
-// own slot) to the same offset of every region of the exchange.
-__device__ __forceinline__ void put_out(const AttendArgs& a, int64_t i, float v) {
+// One output value: to a.out; with a.push also to every region of the
+// exchange: as LL word i (ll), or at the same offset (fp32 out inside this
+// rank's own slot, flag protocol).
+__device__ __forceinline__ void put_out(const AttendArgs& a, int64_t i, float v, uint32_t ep) {
   if (!a.push.regions) {
     store_elem(a.out, i, a.out_dtype, v);
+    return;
+  }
+  if (a.push.ll) {
+    static_cast<float*>(a.out)[i] = v;
+    ll_put(a.push, i, ep, __float_as_uint(v));
     return;
   }
   const int64_t off = reinterpret_cast<const char*>(static_cast<const float*>(a.out) + i) -
@@ -90,9 +96,15 @@ __device__ __forceinline__ void put_out(const AttendArgs& a, int64_t i, float v)
   for (int d = 0; d < static_cast<int>(a.push.world); ++d)
     *reinterpret_cast<float*>(static_cast<char*>(a.push.regions[d]) + off) = v;
 }
-__device__ __forceinline__ void put_lse(const AttendArgs& a, int64_t i, float v) {
+// o_elems: N * H * D, the LL word of lse element 0
+__device__ __forceinline__ void put_lse(const AttendArgs& a, int64_t i, float v, uint32_t ep, int64_t o_elems) {
   if (!a.push.regions) {
     a.lse_out[i] = v;
+    return;
+  }
+  if (a.push.ll) {
+    a.lse_out[i] = v;
+    ll_put(a.push, o_elems + i, ep, __float_as_uint(v));
     return;
   }
   const int64_t off = reinterpret_cast<const char*>(a.lse_out + i) - static_cast<const char*>(a.push.own_region);
@@ -101,7 +113,7 @@ __device__ __forceinline__ void put_lse(const AttendArgs& a, int64_t i, float v)
 }
 // after a storing CTA's puts: it is one producer unit of the exchange
 __device__ __forceinline__ void push_done(const AttendArgs& a) {
-  if (!a.push.regions) return;
+  if (!a.push.regions || a.push.ll) return;  // LL words need no flag
   __syncthreads();
   if (threadIdx.x == 0) peer_unit_done(a.push, static_cast<unsigned>(a.N * a.H));
 }
@@ -214,8 +226,8 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
         const int64_t pos = k0 + j;
         if (pos >= lo && pos < hi_) {
           const int64_t off = base + j * a.s_pos;
-          kr[i] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(a.k) + off));
-          vr[i] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(a.v) + off));
+          kr[i] = load_kv8<KVT>(a.k, off);
+          vr[i] = load_kv8<KVT>(a.v, off);
         } else {
           kr[i] = make_uint4(0, 0, 0, 0);
           vr[i] = make_uint4(0, 0, 0, 0);
@@ -226,10 +238,11 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
       float part[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const uint32_t kw[4] = {kr[i].x, kr[i].y, kr[i].z, kr[i].w};
         float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int w = 0; w < 4; ++w) acc = __ffma2_rn(qv2[w], unpack2<KVT>(kw[w]), acc);
+        acc = __ffma2_rn(qv2[0], kv_pair<KVT, 0>(kr[i]), acc);
+        acc = __ffma2_rn(qv2[1], kv_pair<KVT, 1>(kr[i]), acc);
+        acc = __ffma2_rn(qv2[2], kv_pair<KVT, 2>(kr[i]), acc);
+        acc = __ffma2_rn(qv2[3], kv_pair<KVT, 3>(kr[i]), acc);
         part[i] = acc.x + acc.y;
       }
       const float dot = transpose_reduce8<LPK>(part, u);
@@ -248,9 +261,10 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
       for (int i = 0; i < 8; ++i) {
         const float pi = __shfl_sync(0xffffffffu, pr, g * LPK + transpose_owner<LPK>(i));
         const float2 p2 = make_float2(pi, pi);
-        const uint32_t vw[4] = {vr[i].x, vr[i].y, vr[i].z, vr[i].w};
-#pragma unroll
-        for (int w = 0; w < 4; ++w) o2[w] = __ffma2_rn(p2, unpack2<KVT>(vw[w]), o2[w]);
+        o2[0] = __ffma2_rn(p2, kv_pair<KVT, 0>(vr[i]), o2[0]);
+        o2[1] = __ffma2_rn(p2, kv_pair<KVT, 1>(vr[i]), o2[1]);
+        o2[2] = __ffma2_rn(p2, kv_pair<KVT, 2>(vr[i]), o2[2]);
+        o2[3] = __ffma2_rn(p2, kv_pair<KVT, 3>(vr[i]), o2[3]);
       }
       m = m_new;
     }
@@ -355,8 +369,10 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
   if (nsplit == 1) {
     __syncthreads();
     const float inv = c_l > 0.f ? 1.f / c_l : 0.f;
-    for (int d = tid; d < D; d += kAttendThreads) put_out(a, obase + d, c_o[d] * inv);
-    if (tid == 0 && a.lse_out) put_lse(a, lbase, c_l > 0.f ? (c_m + log2f(c_l)) * kLn2 : -INFINITY);
+    const uint32_t ep = a.push.regions && a.push.ll ? ll_epoch(a.push) : 0u;
+    for (int d = tid; d < D; d += kAttendThreads) put_out(a, obase + d, c_o[d] * inv, ep);
+    if (tid == 0 && a.lse_out)
+      put_lse(a, lbase, c_l > 0.f ? (c_m + log2f(c_l)) * kLn2 : -INFINITY, ep, a.N * a.H * D);
     push_done(a);
     return;
   }
@@ -365,6 +381,7 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
   if (cluster.block_rank() == 0) {
+    const uint32_t ep = a.push.regions && a.push.ll ? ll_epoch(a.push) : 0u;
     float Mg = -INFINITY;
     for (int s = 0; s < nsplit; ++s) Mg = fmaxf(Mg, *cluster.map_shared_rank(&c_m, s));
     const float Mgu = (Mg == -INFINITY) ? 0.f : Mg;
@@ -376,9 +393,9 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
       float acc = 0.f;
       for (int s = 0; s < nsplit; ++s)
         acc += cluster.map_shared_rank(c_o, s)[d] * exp2f(*cluster.map_shared_rank(&c_m, s) - Mgu);
-      put_out(a, obase + d, acc * inv);
+      put_out(a, obase + d, acc * inv, ep);
     }
-    if (tid == 0 && a.lse_out) put_lse(a, lbase, Lg > 0.f ? (Mg + log2f(Lg)) * kLn2 : -INFINITY);
+    if (tid == 0 && a.lse_out) put_lse(a, lbase, Lg > 0.f ? (Mg + log2f(Lg)) * kLn2 : -INFINITY, ep, a.N * a.H * D);
     push_done(a);  // CTA-uniform: the cluster's first CTA stores
   }
   cluster.sync();
@@ -421,7 +438,7 @@ static int launch_attend(const AttendArgs& a, cudaStream_t st) {
 // device and instantiation).
 template <typename K>
 static double kernel_slots(K kern, int idx) {
-  static int sms[64] = {0}, per_sm[64][8] = {};
+  static int sms[64] = {0}, per_sm[64][12] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   if (sms[dev] == 0) {
@@ -437,11 +454,20 @@ static double kernel_slots(K kern, int idx) {
 }
 
 static double attend_slots(int64_t D, int kv_dtype) {
-  if (D == 128)
-    return kv_dtype == SRSWA_BF16 ? kernel_slots(attend_rows_kernel<128, SRSWA_BF16, 4>, 0)
-                                  : kernel_slots(attend_rows_kernel<128, SRSWA_F16, 4>, 1);
-  return kv_dtype == SRSWA_BF16 ? kernel_slots(attend_rows_kernel<64, SRSWA_BF16, 4>, 2)
-                                : kernel_slots(attend_rows_kernel<64, SRSWA_F16, 4>, 3);
+  if (D == 128) {
+    switch (kv_dtype) {
+      case SRSWA_BF16: return kernel_slots(attend_rows_kernel<128, SRSWA_BF16, 4>, 0);
+      case SRSWA_F16: return kernel_slots(attend_rows_kernel<128, SRSWA_F16, 4>, 1);
+      case SRSWA_F8E4M3: return kernel_slots(attend_rows_kernel<128, SRSWA_F8E4M3, 4>, 5);
+      default: return kernel_slots(attend_rows_kernel<128, SRSWA_F8E5M2, 4>, 6);
+    }
+  }
+  switch (kv_dtype) {
+    case SRSWA_BF16: return kernel_slots(attend_rows_kernel<64, SRSWA_BF16, 4>, 2);
+    case SRSWA_F16: return kernel_slots(attend_rows_kernel<64, SRSWA_F16, 4>, 3);
+    case SRSWA_F8E4M3: return kernel_slots(attend_rows_kernel<64, SRSWA_F8E4M3, 4>, 7);
+    default: return kernel_slots(attend_rows_kernel<64, SRSWA_F8E5M2, 4>, 8);
+  }
 }
 
 // The light-load instantiation (5 CTAs per SM), bf16, head dim 128.
@@ -499,7 +525,7 @@ static int launch_attend_rows(AttendArgs a, cudaStream_t st) {
 int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   if (a.N == 0) return 0;
   if (!(D == 64 || D == 128)) return SRSWA_EUNSUPPORTED;
-  if (!(kv_dtype == SRSWA_BF16 || kv_dtype == SRSWA_F16)) return SRSWA_EUNSUPPORTED;
+  if (!(kv_dtype == SRSWA_BF16 || kv_dtype == SRSWA_F16 || kv_is_fp8(kv_dtype))) return SRSWA_EUNSUPPORTED;
   const int kpc = (32 / (static_cast<int>(D) / 8)) * 8;
   if (a.BS % kpc != 0) return SRSWA_EUNSUPPORTED;
   if (a.K + a.LW / a.BS + 2 > kAttendMaxSlots) return SRSWA_ETOOLARGE;
@@ -526,10 +552,14 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
       }
       return launch_attend_rows<128, SRSWA_BF16>(a, st);
     }
-    return launch_attend_rows<128, SRSWA_F16>(a, st);
+    if (kv_dtype == SRSWA_F16) return launch_attend_rows<128, SRSWA_F16>(a, st);
+    if (kv_dtype == SRSWA_F8E4M3) return launch_attend_rows<128, SRSWA_F8E4M3>(a, st);
+    return launch_attend_rows<128, SRSWA_F8E5M2>(a, st);
   }
   if (kv_dtype == SRSWA_BF16) return launch_attend_rows<64, SRSWA_BF16>(a, st);
-  return launch_attend_rows<64, SRSWA_F16>(a, st);
+  if (kv_dtype == SRSWA_F16) return launch_attend_rows<64, SRSWA_F16>(a, st);
+  if (kv_dtype == SRSWA_F8E4M3) return launch_attend_rows<64, SRSWA_F8E4M3>(a, st);
+  return launch_attend_rows<64, SRSWA_F8E5M2>(a, st);
 }
 
 __global__ void lse_merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ lse_parts,
@@ -537,6 +567,31 @@ __global__ void lse_merge_kernel(const float* __restrict__ o_parts, const float*
                                  int out_dtype, float* lse_out, const srswa_peer wait) {
   const int64_t nh = blockIdx.x;
   pdl_wait();  // launched to overlap the kernel ahead: its writes are visible from here
+  if (wait.regions && wait.ll) {  // the parts are LL words in this rank's region: part c = source rank c
+    __shared__ float lse_s[32];
+    const uint32_t ep = ll_epoch(wait);
+    bool ok = true;
+    if (threadIdx.x < C) lse_s[threadIdx.x] = __uint_as_float(ll_get(wait, threadIdx.x, NH * D + nh, ep, ok));
+    __syncthreads();
+    float M = -INFINITY;
+    for (int64_t c = 0; c < C; ++c) M = fmaxf(M, lse_s[c]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float den = 0.f;
+    for (int64_t c = 0; c < C; ++c) den += (lse_s[c] == -INFINITY) ? 0.f : expf(lse_s[c] - Mu);
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
+      float acc = 0.f;
+      for (int64_t c = 0; c < C; ++c) {
+        const float ov = __uint_as_float(ll_get(wait, static_cast<int>(c), nh * D + d, ep, ok));
+        if (lse_s[c] != -INFINITY) acc += expf(lse_s[c] - Mu) * ov;
+      }
+      store_elem(out, nh * D + d, out_dtype, acc * inv);
+    }
+    if (threadIdx.x == 0 && lse_out) lse_out[nh] = den > 0.f ? Mu + logf(den) : -INFINITY;
+    __syncthreads();
+    if (threadIdx.x == 0) ll_consumer_done(wait, gridDim.x);
+    return;
+  }
   if (wait.regions) {  // the parts are the peers' pushes into this rank's region
     if (threadIdx.x == 0) peer_wait_all(wait, gridDim.x);
     __syncthreads();
@@ -591,15 +646,18 @@ extern "C" int srswa_decode_attend_push(const srswa_decode_desc* dd, const void*
                       push->world >= 1 && push->world <= 32 && push->rank >= 0 && push->rank < push->world,
                   SRSWA_EINVAL);
   SRSWA_CHECK_ARG(dd && out && lse_out && dd->out_dtype == SRSWA_F32, SRSWA_EINVAL);
-  // o and lse must lie in this rank's own slot, contiguous [N, H, D] and [N, H]
-  const char* slot = static_cast<const char*>(push->own_region) + kPeerHeader + push->rank * push->slot_bytes;
-  const char* o0 = reinterpret_cast<const char*>(out);
-  const char* l0 = reinterpret_cast<const char*>(lse_out);
+  SRSWA_CHECK_ARG(dd->s_on == dd->H * dd->D && dd->s_oh == dd->D, SRSWA_EINVAL);  // contiguous [N, H, D]
   const int64_t ob = dd->N * dd->H * dd->D * 4, lb = dd->N * dd->H * 4;
-  SRSWA_CHECK_ARG(dd->s_on == dd->H * dd->D && dd->s_oh == dd->D, SRSWA_EINVAL);
-  SRSWA_CHECK_ARG(o0 >= slot && o0 + ob <= slot + push->slot_bytes && l0 >= slot &&
-                      l0 + lb <= slot + push->slot_bytes,
-                  SRSWA_EINVAL);
+  if (push->ll) {  // LL words of the packed o then lse, 8 bytes per element
+    SRSWA_CHECK_ARG((ob + lb) * 2 <= push->slot_bytes, SRSWA_EINVAL);
+  } else {  // o and lse must lie in this rank's own slot, contiguous [N, H, D] and [N, H]
+    const char* slot = static_cast<const char*>(push->own_region) + kPeerHeader + push->rank * push->slot_bytes;
+    const char* o0 = reinterpret_cast<const char*>(out);
+    const char* l0 = reinterpret_cast<const char*>(lse_out);
+    SRSWA_CHECK_ARG(o0 >= slot && o0 + ob <= slot + push->slot_bytes && l0 >= slot &&
+                        l0 + lb <= slot + push->slot_bytes,
+                    SRSWA_EINVAL);
+  }
   return decode_attend(dd, q, k_cache, v_cache, block_table, seq_lens, q_pos, topk_idx, bias, valid, out, lse_out,
                        push, stream);
 }
@@ -676,12 +734,15 @@ extern "C" int srswa_prefill_attend(const srswa_decode_desc* dd, const void* q, 
 extern "C" int srswa_lse_merge(const float* o_parts, const float* lse_parts, int64_t C, int64_t N,
                                int64_t H, int64_t D, int64_t s_o_part, int64_t s_l_part, void* out,
                                int out_dtype, float* lse_out, const srswa_peer* wait, srswa_stream_t stream) {
-  SRSWA_CHECK_ARG(o_parts && lse_parts && out && C > 0 && N >= 0 && H > 0 && D > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(out && C > 0 && N >= 0 && H > 0 && D > 0, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG((o_parts && lse_parts) || (wait && wait->ll), SRSWA_EINVAL);
   srswa_peer pw = {};
   if (wait) {
     SRSWA_CHECK_ARG(wait->regions && wait->own_region && wait->counter && wait->tickets && wait->world >= 1 &&
                         wait->world <= 32,
                     SRSWA_EINVAL);
+    // LL: the parts are read from the region (o_parts / lse_parts unused), one per rank
+    SRSWA_CHECK_ARG(!wait->ll || (C == wait->world && (N * H * D + N * H) * 8 <= wait->slot_bytes), SRSWA_EINVAL);
     pw = *wait;
   }
   if (s_o_part == 0) s_o_part = N * H * D;

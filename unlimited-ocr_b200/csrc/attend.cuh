@@ -1,6 +1,8 @@
 // Internal interface of the row-streaming sparse attend (attend.cu).
 #pragma once
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace srswa {
@@ -91,6 +93,35 @@ template <int KVT>
 __device__ __forceinline__ float2 unpack2(uint32_t w) {
   if (KVT == SRSWA_BF16) return make_float2(bf16_lo(w), bf16_hi(w));
   return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+constexpr bool kv_is_fp8(int kvt) { return kvt == SRSWA_F8E4M3 || kvt == SRSWA_F8E5M2; }
+
+// 8 consecutive K / V elements at element offset off: one 16-byte load for
+// 16-bit caches, one 8-byte load (in .x / .y) for fp8 caches.
+template <int KVT>
+__device__ __forceinline__ uint4 load_kv8(const void* p, int64_t off) {
+  if constexpr (kv_is_fp8(KVT)) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(p) + off));
+    return make_uint4(v.x, v.y, 0u, 0u);
+  } else {
+    return __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(p) + off));
+  }
+}
+
+// Elements (2w, 2w + 1) of 8 loaded by load_kv8, as fp32 (fp8 -> fp16 by the
+// hardware conversion, exact, then fp32: the reference casts fp8 caches to
+// the query dtype, which is exact too).
+template <int KVT, int W>
+__device__ __forceinline__ float2 kv_pair(const uint4& r) {
+  if constexpr (kv_is_fp8(KVT)) {
+    const uint32_t word = W < 2 ? r.x : r.y;
+    const __nv_fp8x2_storage_t h = static_cast<__nv_fp8x2_storage_t>((W & 1) ? (word >> 16) : (word & 0xffffu));
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(h, KVT == SRSWA_F8E4M3 ? __NV_E4M3 : __NV_E5M2);
+    return __half22float2(__half2(hr));
+  } else {
+    return unpack2<KVT>(W == 0 ? r.x : W == 1 ? r.y : W == 2 ? r.z : r.w);
+  }
 }
 
 int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st);

@@ -51,6 +51,7 @@ using namespace srswa;
 
 static int check_peer(const srswa_peer* p) {
   if (!p || !p->regions || !p->own_region || !p->counter || !p->tickets) return SRSWA_EINVAL;
+  if (p->ll) return SRSWA_EUNSUPPORTED;  // the generic push / wait move flagged payloads
   if (p->world < 1 || p->world > 32 || p->rank < 0 || p->rank >= p->world || p->slot_bytes < 0) return SRSWA_EINVAL;
   if (((reinterpret_cast<uintptr_t>(p->own_region) | static_cast<uintptr_t>(p->slot_bytes)) & 15) != 0)
     return SRSWA_EALIGN;

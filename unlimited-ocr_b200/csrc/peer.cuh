@@ -76,4 +76,53 @@ __device__ __forceinline__ bool peer_wait_all(const srswa_peer& p, unsigned nuni
   return ok;
 }
 
+// ---- LL protocol (srswa_peer.ll = 1) ----
+// A 32-bit payload word travels with the exchange's epoch in one aligned
+// 8-byte store (single-copy atomic), so a consumer that reads the epoch has
+// the payload too: no fence, no flag, no producer ticket.
+__device__ __forceinline__ uint32_t ll_epoch(const srswa_peer& p) {
+  return static_cast<uint32_t>(*p.counter + 1);
+}
+
+// word k of this rank's slot, in every region
+__device__ __forceinline__ void ll_put(const srswa_peer& p, int64_t k, uint32_t epoch, uint32_t v) {
+  const unsigned long long w = (static_cast<unsigned long long>(epoch) << 32) | v;
+  for (int d = 0; d < static_cast<int>(p.world); ++d) {
+    unsigned long long* a = reinterpret_cast<unsigned long long*>(peer_slot(p, d)) + k;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+  }
+}
+
+// word k of source rank r's slot in this rank's region, once it carries
+// `epoch` (bounded wait; on expiry ok = false, status 501, returns 0)
+__device__ __forceinline__ uint32_t ll_get(const srswa_peer& p, int r, int64_t k, uint32_t epoch, bool& ok) {
+  const unsigned long long* a = reinterpret_cast<const unsigned long long*>(
+                                    static_cast<const char*>(p.own_region) + kPeerHeader + r * p.slot_bytes) + k;
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+  if (static_cast<uint32_t>(w >> 32) == epoch) return static_cast<uint32_t>(w);
+  if (!ok) return 0u;  // this thread already gave up on a peer: no second wait
+  const uint64_t t0 = peer_now();
+  for (;;) {
+    __nanosleep(20);
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+    if (static_cast<uint32_t>(w >> 32) == epoch) return static_cast<uint32_t>(w);
+    if (peer_now() - t0 > kPeerWaitNs) {
+      if (ok && p.status) atomicCAS(reinterpret_cast<int*>(p.status), 0, kPeerExpired);
+      ok = false;
+      return 0u;
+    }
+  }
+}
+
+// one consumer unit has read everything it needs: the last of nunits
+// advances the counter (the next exchange's epoch)
+__device__ __forceinline__ void ll_consumer_done(const srswa_peer& p, unsigned nunits) {
+  const unsigned t = atomicAdd(p.tickets + 1, 1u);
+  if (t == nunits - 1) {
+    *p.counter = *p.counter + 1;
+    p.tickets[1] = 0u;
+  }
+}
+
 }  // namespace srswa

@@ -811,6 +811,7 @@ __device__ __forceinline__ unsigned long long warp_merge_heads(unsigned long lon
 // lists.  Two short loops: the merge runs once per row, from a cold
 // instruction cache.  Called by all threads; lane m of warp 0 gets key m.
 constexpr int64_t kSortedListsMax = 8 * 32;
+template <bool kShared = false>  // lists in shared memory instead of global
 __device__ unsigned long long block_merge_lists(const unsigned long long* src, int64_t stride, int64_t nlists,
                                                 int M, unsigned long long (*lists)[kMaxTopM], int warp, int lane) {
   const int64_t per = (nlists + 7) / 8;
@@ -818,7 +819,8 @@ __device__ unsigned long long block_merge_lists(const unsigned long long* src, i
   const bool has = lane < per && l < nlists;
   unsigned long long v[16];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) v[k] = (has && k < M) ? __ldcg(src + l * stride + k) : 0ull;
+  for (int k = 0; k < 16; ++k)
+    v[k] = (has && k < M) ? (kShared ? src[l * stride + k] : __ldcg(src + l * stride + k)) : 0ull;
   const unsigned long long top = warp_merge_heads(v, M, lane);
   if (lane < M) lists[warp][lane] = top;
   __syncthreads();
@@ -1070,6 +1072,31 @@ __global__ void __launch_bounds__(kRouteThreads) route_chunk_keys_kernel(const R
   }
   __syncthreads();
   // rowk: this rank's top-M keys of the row
+  if (push.regions && push.ll) {  // LL exchange (with the finish stage only)
+    // this rank's keys as LL words to every region, then every rank's from
+    // this rank's region, each word polled until it carries the epoch
+    const uint32_t ep = ll_epoch(push);
+    if (tid < M) {
+      const unsigned long long key = rowk[tid];
+      ll_put(push, 2 * (n * M + tid), ep, static_cast<uint32_t>(key));
+      ll_put(push, 2 * (n * M + tid) + 1, ep, static_cast<uint32_t>(key >> 32));
+    }
+    const int world = static_cast<int>(push.world);
+    bool ok = true;
+    for (int i = tid; i < world * M; i += kRouteThreads) {
+      const int r = i / M, j = i - r * M;
+      const uint32_t lo = ll_get(push, r, 2 * (n * M + j), ep, ok);
+      const uint32_t hi = ll_get(push, r, 2 * (n * M + j) + 1, ep, ok);
+      mk[i] = (static_cast<unsigned long long>(hi) << 32) | lo;
+    }
+    __syncthreads();
+    if (tid == 0) ll_consumer_done(push, gridDim.y);
+    const unsigned long long merged =
+        M <= 16 ? block_merge_lists<true>(mk, M, world, M, lists, warp, lane)
+                : block_topm(mk, static_cast<int64_t>(world) * M, M, lists, topm_scratch, warp, lane);
+    if (warp == 0) finish_row(a, fin, n, lane, merged);
+    return;
+  }
   if (push.regions && tid < M) peer_put8(push, (n * M + tid) * 8, rowk[tid]);  // to every peer
   if (!fin.on) {
     if (keys_out && tid < M) keys_out[n * M + tid] = rowk[tid];
@@ -1746,7 +1773,8 @@ static int shard_launch(const void* idx_q, int q_dtype, int64_t s_q, int64_t N, 
   SRSWA_CHECK_ARG(N < 65536, SRSWA_ETOOLARGE);
   const int64_t nch = (nblk_local + kChunkBlocks - 1) / kChunkBlocks;
   unsigned long long* out = reinterpret_cast<unsigned long long*>(keys_out);
-  SRSWA_CHECK_ARG(!push || N * a.M * 8 <= push->slot_bytes, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(!push || N * a.M * (push->ll ? 16 : 8) <= push->slot_bytes, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(!push || !push->ll || fin.on, SRSWA_EUNSUPPORTED);  // LL: keys are merged in the same launch
   // the ranks' lists of a row are merged in the same shared array as its chunk lists
   const int64_t lists = fin.on && push ? (nch > push->world ? nch : push->world) : (nch > 1 ? nch : 0);
   SRSWA_CHECK_ARG(lists * a.M <= kMergeMaxKeys, SRSWA_ETOOLARGE);
@@ -1817,6 +1845,7 @@ extern "C" int srswa_route_merge_keys(const uint64_t* keys, int64_t nlists, int6
     SRSWA_CHECK_ARG(wait->regions && wait->own_region && wait->counter && wait->tickets && wait->world >= 1 &&
                         wait->world <= 32,
                     SRSWA_EINVAL);
+    SRSWA_CHECK_ARG(!wait->ll, SRSWA_EUNSUPPORTED);
     pw = *wait;
   }
   RouteArgs a = {};

@@ -15,8 +15,10 @@ import torch
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("SRSWA_LIB", os.path.join(_HERE, "libsrswa.so"))
 
-F32, BF16, F16 = 0, 1, 2
-_DTYPES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+F32, BF16, F16, F8E4M3, F8E5M2 = 0, 1, 2, 3, 4
+# fp8 only where an entry point accepts it (the attends' K/V caches)
+_DTYPES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16, torch.float8_e4m3fn: F8E4M3,
+           torch.float8_e5m2: F8E5M2}
 
 EINVAL, EUNSUPPORTED, EALIGN, EWORKSPACE, ETOOLARGE = -1, -2, -3, -4, -5
 
@@ -58,7 +60,7 @@ class KlDesc(C.Structure):
 class Peer(C.Structure):
     """srswa_peer: one peer-memory exchange region (device pointers)."""
     _fields_ = [("regions", vp), ("own_region", vp), ("slot_bytes", i64), ("rank", i64), ("world", i64),
-                ("counter", vp), ("tickets", vp), ("status", vp)]
+                ("counter", vp), ("tickets", vp), ("status", vp), ("ll", i64)]
 
 
 _SIGS = {

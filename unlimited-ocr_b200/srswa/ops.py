@@ -568,6 +568,21 @@ def prefill_attend(q, k_cache, v_cache, topk_idx, bias, *, block_table, cu_seqle
     return (out, lse_t) if lse else out
 
 
+def lse_merge_exchange(exchange, world, N, H, D, device, out_dtype=torch.float32, out=None, lse=None):
+    """Log-sum-exp merge of the world ranks' partials that
+    srswa_decode_attend_push stored as LL words into this rank's region of
+    ``exchange`` (an LL srswa_peer): waits for them itself (bounded)."""
+    if out is None:
+        out = torch.empty(N, H, D, device=device, dtype=out_dtype)
+    assert out.is_contiguous()
+    if lse is None:
+        lse = torch.empty(N, H, device=device, dtype=torch.float32)
+    rc = L.lib().srswa_lse_merge(None, None, int(world), N, H, D, 0, 0, out.data_ptr(), L.dtype_code(out),
+                                 lse.data_ptr(), C.byref(exchange), L.stream_of(out))
+    L.check(rc, "srswa_lse_merge")
+    return out, lse
+
+
 def lse_merge(o_parts, lse_parts, out_dtype=torch.float32, out=None, lse=None, wait=None):
     """o_parts [C,N,H,D], lse_parts [C,N,H] fp32 (each part contiguous; the
     parts may be strided, e.g. views into one packed all-gather buffer) ->

@@ -12,7 +12,10 @@ alone, for a consumer kernel that waits itself (the library's key merge and
 log-sum-exp merge take ``self.peer`` for that), and ``self.peer`` also makes
 the router's shard kernel push its keys itself.  A returned view is valid
 until the next exchange on the same object overwrites it, so a decode step
-alternates two objects (router keys, attention partials).
+alternates two objects (router keys, attention partials).  With ll=True the
+object speaks the LL protocol (srswa.h, "peer exchange"): only the fused
+kernels (srswa_route_shard_select, srswa_decode_attend_push, srswa_lse_merge)
+use it, and ``push`` / ``__call__`` are refused.
 """
 
 from __future__ import annotations
@@ -25,7 +28,7 @@ from . import _lib as L
 
 
 class PeerAllGather:
-    def __init__(self, slot_bytes: int, group=None, device=None):
+    def __init__(self, slot_bytes: int, group=None, device=None, ll: bool = False):
         import torch.distributed as dist
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -64,8 +67,12 @@ class PeerAllGather:
         self.tickets = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         # the srswa_peer descriptor the library's producers / consumers take
+        # ll: the LL protocol (payload words carry the epoch; only the
+        # library's fused producers / consumers take it)
+        self.ll = bool(ll)
         self.peer = L.Peer(self.regions.data_ptr(), self.region, self.slot, self.rank, self.world,
-                           self.counter.data_ptr(), self.tickets.data_ptr(), self.status.data_ptr())
+                           self.counter.data_ptr(), self.tickets.data_ptr(), self.status.data_ptr(),
+                           1 if self.ll else 0)
         # this rank's region as bytes: slot r (after the 256-byte flag header) = rank r's payload
         self._slots = _RegionView(self.region, self.size, self.device).tensor[256:].view(self.world, self.slot)
 

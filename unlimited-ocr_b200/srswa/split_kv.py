@@ -149,38 +149,55 @@ class CudaBackend:
 
 class PeerBackend(CudaBackend):
     """CudaBackend whose two exchanges per layer go through peer memory
-    (srswa.peer.PeerAllGather over CUDA IPC): one push and one bounded wait
-    launch each instead of a library all-gather, and no collective after
-    set-up.  One object serves every layer of a step (the two regions
-    alternate, which keeps a rank from overwriting data a peer still reads).
-    rows / topm / heads / head_dim bound the payloads."""
+    (srswa.peer.PeerAllGather over CUDA IPC) instead of a library all-gather,
+    with no collective after set-up.  One object serves every layer of a
+    step (the two regions alternate, which keeps a rank from overwriting
+    data a peer still reads).  rows / topm / heads / head_dim bound the
+    payloads.  mode:
 
-    def __init__(self, group=None, *, rows, topm, heads, head_dim, fused=True):
+    * "ll" (default): the router's one-launch select exchanges the keys and
+      the attend stores its partials as LL words (payload + epoch in one
+      8-byte store, no fence or flag); the log-sum-exp merge polls them;
+    * "flag": the same kernels with the flag protocol (payload stores, a
+      system-scope fence, then a released flag per source);
+    * "launch": each exchange is its own push launch + wait launch."""
+
+    MODES = ("ll", "flag", "launch")
+
+    def __init__(self, group=None, *, rows, topm, heads, head_dim, mode="ll"):
         super().__init__(group)
         from .peer import PeerAllGather
-        self.fused = fused
-        self.keys_x = PeerAllGather(rows * topm * 8, group)
-        self.part_x = PeerAllGather(-(-(rows * heads * head_dim + rows * heads) // 4) * 16, group)
+        if mode not in self.MODES:
+            raise ValueError(f"mode {mode!r} not in {self.MODES}")
+        self.mode = mode
+        self.fused = mode != "launch"
+        ll = mode == "ll"
+        words = 2 if ll else 1       # LL: 8 bytes per 32-bit payload word
+        self.keys_x = PeerAllGather(rows * topm * 8 * words, group, ll=ll)
+        self.part_x = PeerAllGather(-(-(rows * heads * head_dim + rows * heads) // 4) * 16 * words, group, ll=ll)
 
-    # fused: the router's shard kernel pushes its keys into every peer's
-    # region itself, the key merge and the log-sum-exp merge wait themselves;
-    # else each exchange is a push launch + a wait launch
+    # flag: the shard kernel pushes its keys itself and the merges wait
+    # themselves; ll: only the one-launch select exchanges keys, so these
+    # stage-by-stage calls (more than 128 rows, the bench's untimed byte
+    # count) go through the library all-gather; launch: push + wait launches
     def shard_keys(self, idx_q, layer, plan, q_pos, rp):
         return self.ops.route_shard_keys(
             idx_q, layer["kbar"], block_offset=plan.lo, nblk_local=plan.hi - plan.lo,
             nblk_total=plan.nblk_total, q_pos=q_pos, rows_per_seq=idx_q.shape[0],
-            block_table=layer.get("kbar_table"), push=self.keys_x.peer if self.fused else None, **rp)
+            block_table=layer.get("kbar_table"), push=self.keys_x.peer if self.mode == "flag" else None, **rp)
 
     def gather_keys(self, keys, world):
-        if not self.fused:
+        if self.mode == "launch":
             return self.keys_x(keys)
+        if self.mode == "ll":
+            return self.all_gather(keys, world)
         return self.keys_x.slots(keys.shape, keys.dtype)   # filled by the peers' shard kernels
 
     def merge_keys(self, keys, plan, rp):
         p = {k: v for k, v in rp.items() if k not in ("block_size", "local_blocks")}
         return self.ops.route_merge_keys(keys, nblk_total=plan.nblk_total, own=(plan.lo, plan.hi),
-                                         want=("topi32", "bias"), wait=self.keys_x.peer if self.fused else None,
-                                         **p)
+                                         want=("topi32", "bias"),
+                                         wait=self.keys_x.peer if self.mode == "flag" else None, **p)
 
     def select(self, idx_q, layer, plan, q_pos, rp):
         # fused: one launch per layer does the shard keys, the key exchange
@@ -194,21 +211,35 @@ class PeerBackend(CudaBackend):
         if not self.fused or out_dtype != torch.float32:
             return super().attend(q, layer, topi, bias, q_pos, block_size=block_size, local_blocks=local_blocks,
                                   sm_scale=sm_scale, skip_local=skip_local, out_dtype=out_dtype)
-        # fused: the attend writes its partial into this rank's own slot and
-        # stores it into every peer's region itself (no push launch)
+        # fused: the attend stores its partial into every rank's region
+        # itself (no push launch); flag: its local copy must be this rank's
+        # own slot, ll: any buffer
         N, H, D = q.shape
-        buf = self.part_x.own_slot((-(-(N * H * D + N * H) // 4) * 4,), torch.float32)
+        n4 = -(-(N * H * D + N * H) // 4) * 4
+        if self.mode == "flag":
+            buf = self.part_x.own_slot((n4,), torch.float32)
+        else:
+            buf = torch.empty(n4, device=q.device, dtype=torch.float32)
         out, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:N * H * D + N * H].view(N, H)
         return self.ops.decode_attend(q, layer["k_cache"], layer["v_cache"], topi, bias, block_size=block_size,
                                       local_blocks=local_blocks, sm_scale=sm_scale, out=out,
                                       block_table=layer["block_table"], q_pos=q_pos, rows_per_req=N, lse=True,
                                       skip_local=skip_local, lse_out=lse, overlap=True, push=self.part_x.peer)
 
+    def exchange_partials(self, o_part, lse_part, world):
+        if self.mode == "ll":   # the merge reads the LL words from the region itself
+            return o_part, lse_part
+        return super().exchange_partials(o_part, lse_part, world)
+
     def gather_partials(self, buf, world):
-        # fused: the attend has already stored the partials into every region
+        # flag: the attend has already stored the partials into every region
         return self.part_x.slots(buf.shape, buf.dtype) if self.fused else self.part_x(buf)
 
     def lse_merge(self, o_parts, lse_parts, out_dtype):
+        if self.mode == "ll":
+            N, H, D = o_parts.shape
+            return self.ops.lse_merge_exchange(self.part_x.peer, self.part_x.world, N, H, D, o_parts.device,
+                                               out_dtype=out_dtype)[0]
         return self.ops.lse_merge(o_parts, lse_parts, out_dtype=out_dtype,
                                   wait=self.part_x.peer if self.fused else None)[0]
 
