@@ -65,9 +65,10 @@ def parse():
                          "pagegate = PageGate candidate masks of a cfg2-shaped prefill; "
                          "rope = page2d RoPE coordinates + fused rotary of a cfg2-shaped prefill")
     ap.add_argument("--layers", type=int, default=12, help="longctx: decoder layers")
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "p2p-launch", "nccl"],
-                    help="longctx with N > 1: peer-memory exchange fused into the router / merge kernels "
-                         "(default), the same exchange as separate push + wait launches, or NCCL all-gathers")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "p2p-flag", "p2p-launch", "nccl"],
+                    help="longctx with N > 1: peer-memory exchange fused into the router / attend / merge "
+                         "kernels with LL words (default) or with flags, the flag exchange as separate push + "
+                         "wait launches, or NCCL all-gathers")
     ap.add_argument("--batch", type=int, default=0, help="prefill/train batch override (smaller cases)")
     ap.add_argument("--seq", type=int, default=0, help="prefill/train sequence override")
     return ap.parse_args()
