@@ -377,6 +377,21 @@ SRSWA_API int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, co
  * every region.  The consumer is srswa_lse_merge with the same exchange as
  * its wait (LL: o_parts / lse_parts may be NULL, C = world).  The split-KV decode's
  * partial all-gather fused into the attend; no reference counterpart. */
+/* srswa_decode_attend_push with an LL exchange whose log-sum-exp merge is
+ * done by the attend itself: each (row, head)'s storing CTA, after its own
+ * puts, waits (bounded) for every rank's partial of that (row, head) and
+ * writes the merge to final_out ([N, H, D] contiguous, final_dtype F32 /
+ * BF16 / F16) and final_lse ([N, H], optional) -- the same values as
+ * srswa_lse_merge.  The CTAs of one rank wait for the peers' CTAs, so the
+ * whole grid must be resident at once (N * H * split CTAs within the GPU's
+ * resident slots), else SRSWA_ETOOLARGE and the caller takes
+ * srswa_decode_attend_push + srswa_lse_merge.  No reference counterpart: the
+ * split-KV decode's partial all-gather and combine fused into the attend. */
+SRSWA_API int srswa_decode_attend_exchange(const srswa_decode_desc* dd, const void* q, const void* k_cache,
+                        const void* v_cache, const int32_t* block_table, const int32_t* seq_lens,
+                        const int64_t* q_pos, const void* topk_idx, const float* bias, const uint8_t* valid,
+                        float* out, float* lse_out, const srswa_peer* exchange, void* final_out,
+                        int final_dtype, float* final_lse, srswa_stream_t stream);
 SRSWA_API int srswa_decode_attend_push(const srswa_decode_desc* dd, const void* q, const void* k_cache,
                         const void* v_cache, const int32_t* block_table,
                         const int32_t* seq_lens, const int64_t* q_pos, const void* topk_idx,

@@ -92,6 +92,12 @@ def test_attend_push_world1_equals_plain(cuda, nsplit, ll):
         ops.decode_attend(q, kc, vc, sel["topi32"], sel["bias"], out=o, lse_out=lse, push=ex.peer, **kw)
         if ll:
             merged = ops.lse_merge_exchange(ex.peer, 1, N, H, D, cuda)[0]
+            # the attend that also exchanges and merges (one launch)
+            fused = ops.decode_attend(q, kc, vc, sel["topi32"], sel["bias"], out=torch.empty_like(o),
+                                      lse_out=torch.empty_like(lse), push=ex.peer,
+                                      merged_out=torch.empty(N, H, D, device=cuda), **kw)
+            torch.cuda.synchronize()
+            assert torch.equal(fused, ref_o)
         else:
             parts = ex.slots((n4,), torch.float32)
             merged = ops.lse_merge(parts[:, :N * H * D].view(1, N, H, D),
@@ -100,6 +106,6 @@ def test_attend_push_world1_equals_plain(cuda, nsplit, ll):
         torch.cuda.synchronize()
         assert torch.equal(o, ref_o) and torch.equal(lse, ref_l)
         torch.testing.assert_close(merged, ref_o, rtol=1e-6, atol=1e-6)
-    assert int(ex.counter.item()) == 3
+    assert int(ex.counter.item()) == (6 if ll else 3)   # ll: two exchanges per repetition
     ex.check()
     ex.close()

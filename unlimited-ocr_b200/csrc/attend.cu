@@ -118,6 +118,39 @@ __device__ __forceinline__ void push_done(const AttendArgs& a) {
   if (threadIdx.x == 0) peer_unit_done(a.push, static_cast<unsigned>(a.N * a.H));
 }
 
+// LL exchange + merge of one (row, head), by its storing CTA after its own
+// puts: every rank's partial o (LL words e_o .. e_o + D - 1) and lse (word
+// e_l) from this rank's region, merged by log-sum-exp in the same order and
+// arithmetic as lse_merge_kernel into final_out[fo .. fo + D - 1]; then the
+// CTA is one consumer unit of the exchange.
+template <int D>
+__device__ void merge_exchange(const AttendArgs& a, int64_t e_o, int64_t e_l, int64_t fo, int64_t fl,
+                               uint32_t ep) {
+  __shared__ float lse_s[32];
+  const int tid = threadIdx.x;
+  const int C = static_cast<int>(a.push.world);
+  bool ok = true;
+  if (tid < C) lse_s[tid] = __uint_as_float(ll_get(a.push, tid, e_l, ep, ok));
+  __syncthreads();
+  float M = -INFINITY;
+  for (int c = 0; c < C; ++c) M = fmaxf(M, lse_s[c]);
+  const float Mu = (M == -INFINITY) ? 0.f : M;
+  float den = 0.f;
+  for (int c = 0; c < C; ++c) den += (lse_s[c] == -INFINITY) ? 0.f : expf(lse_s[c] - Mu);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  for (int d = tid; d < D; d += kAttendThreads) {
+    float acc = 0.f;
+    for (int c = 0; c < C; ++c) {
+      const float ov = __uint_as_float(ll_get(a.push, c, e_o + d, ep, ok));
+      if (lse_s[c] != -INFINITY) acc += expf(lse_s[c] - Mu) * ov;
+    }
+    store_elem(a.final_out, fo + d, a.final_dtype, acc * inv);
+  }
+  if (tid == 0 && a.final_lse) a.final_lse[fl] = den > 0.f ? Mu + logf(den) : -INFINITY;
+  __syncthreads();
+  if (tid == 0) ll_consumer_done(a.push, static_cast<unsigned>(a.N * a.H));
+}
+
 template <int D, int KVT, int MINB>
 __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const AttendArgs a) {
   constexpr int LPK = D / 8;     // lanes per key row
@@ -374,6 +407,10 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
     if (tid == 0 && a.lse_out)
       put_lse(a, lbase, c_l > 0.f ? (c_m + log2f(c_l)) * kLn2 : -INFINITY, ep, a.N * a.H * D);
     push_done(a);
+    if (a.final_out) {
+      __syncthreads();  // this CTA's puts precede its gets (its own slot included)
+      merge_exchange<D>(a, obase, a.N * a.H * D + lbase, obase, lbase, ep);
+    }
     return;
   }
 
@@ -397,6 +434,10 @@ __global__ void __launch_bounds__(kAttendThreads, MINB) attend_rows_kernel(const
     }
     if (tid == 0 && a.lse_out) put_lse(a, lbase, Lg > 0.f ? (Mg + log2f(Lg)) * kLn2 : -INFINITY, ep, a.N * a.H * D);
     push_done(a);  // CTA-uniform: the cluster's first CTA stores
+    if (a.final_out) {
+      __syncthreads();
+      merge_exchange<D>(a, obase, a.N * a.H * D + lbase, obase, lbase, ep);
+    }
   }
   cluster.sync();
 }
@@ -538,6 +579,9 @@ int attend_rows_launch(AttendArgs a, int64_t D, int kv_dtype, cudaStream_t st) {
   if (a.N * 8 >= (1ll << 31)) return SRSWA_ETOOLARGE;
   a.nsplit = nsplit;
   a.heads_inner = (a.N <= 65535 && a.H * 8 <= 65535) ? 1 : 0;
+  // the merge inside the attend waits for the peers' CTAs of the same (row,
+  // head): the whole grid must be resident at once
+  if (a.final_out && static_cast<double>(a.N) * a.H * nsplit > attend_slots(D, kv_dtype)) return SRSWA_ETOOLARGE;
   if (D == 128) {
     if (kv_dtype == SRSWA_BF16) {
       // A light load that one wave holds unsplit but not 2-way split (e.g.
@@ -625,7 +669,8 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 static int decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache, const void* v_cache,
                          const int32_t* block_table, const int32_t* seq_lens, const int64_t* q_pos,
                          const void* topk_idx, const float* bias, const uint8_t* valid, void* out, float* lse_out,
-                         const srswa_peer* push, srswa_stream_t stream);
+                         const srswa_peer* push, srswa_stream_t stream, void* final_out = nullptr,
+                         int final_dtype = 0, float* final_lse = nullptr);
 
 extern "C" int srswa_decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache,
                                    const void* v_cache, const int32_t* block_table,
@@ -662,10 +707,33 @@ extern "C" int srswa_decode_attend_push(const srswa_decode_desc* dd, const void*
                        push, stream);
 }
 
+extern "C" int srswa_decode_attend_exchange(const srswa_decode_desc* dd, const void* q, const void* k_cache,
+                                            const void* v_cache, const int32_t* block_table,
+                                            const int32_t* seq_lens, const int64_t* q_pos,
+                                            const void* topk_idx, const float* bias, const uint8_t* valid,
+                                            float* out, float* lse_out, const srswa_peer* exchange,
+                                            void* final_out, int final_dtype, float* final_lse,
+                                            srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(exchange && exchange->ll && final_out, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(final_dtype == SRSWA_F32 || final_dtype == SRSWA_BF16 || final_dtype == SRSWA_F16,
+                  SRSWA_EUNSUPPORTED);
+  SRSWA_CHECK_ARG(aligned16(final_out), SRSWA_EALIGN);
+  SRSWA_CHECK_ARG(exchange->regions && exchange->own_region && exchange->counter && exchange->tickets &&
+                      exchange->world >= 1 && exchange->world <= 32 && exchange->rank >= 0 &&
+                      exchange->rank < exchange->world,
+                  SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(dd && out && lse_out && dd->out_dtype == SRSWA_F32, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(dd->s_on == dd->H * dd->D && dd->s_oh == dd->D, SRSWA_EINVAL);
+  SRSWA_CHECK_ARG((dd->N * dd->H * (dd->D + 1)) * 8 <= exchange->slot_bytes, SRSWA_EINVAL);
+  return decode_attend(dd, q, k_cache, v_cache, block_table, seq_lens, q_pos, topk_idx, bias, valid, out, lse_out,
+                       exchange, stream, final_out, final_dtype, final_lse);
+}
+
 static int decode_attend(const srswa_decode_desc* dd, const void* q, const void* k_cache, const void* v_cache,
                          const int32_t* block_table, const int32_t* seq_lens, const int64_t* q_pos,
                          const void* topk_idx, const float* bias, const uint8_t* valid, void* out, float* lse_out,
-                         const srswa_peer* push, srswa_stream_t stream) {
+                         const srswa_peer* push, srswa_stream_t stream, void* final_out, int final_dtype,
+                         float* final_lse) {
   SRSWA_CHECK_ARG(dd && q && k_cache && v_cache && out, SRSWA_EINVAL);
   const srswa_decode_desc& d = *dd;
   SRSWA_CHECK_ARG(d.N >= 0 && d.H > 0 && d.Hkv > 0 && d.H % d.Hkv == 0, SRSWA_EINVAL);
@@ -695,6 +763,7 @@ static int decode_attend(const srswa_decode_desc* dd, const void* q, const void*
   a.lse_out = lse_out; a.s_l_seq = d.rows_per_req * d.H; a.s_l_t = d.H;
   a.nsplit = d.nsplit; a.skip_local = d.skip_local ? 1 : 0; a.overlap = d.overlap ? 1 : 0;
   if (push) a.push = *push;
+  a.final_out = final_out; a.final_dtype = final_dtype; a.final_lse = final_lse;
   return attend_rows_launch(a, d.D, d.kv_dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -70,6 +70,11 @@ struct AttendArgs {
   srswa_peer push; // regions != NULL: out / lse_out lie in this rank's own slot
                    // and every (row, head) result goes to that slot of every
                    // region; the storing CTAs are the exchange's producer units
+  void* final_out; // LL push only: each storing CTA also waits for every rank's
+                   // partial of its (row, head) and writes the log-sum-exp
+                   // merge here ([N, H, D] contiguous, final_dtype)
+  int final_dtype;
+  float* final_lse;  // [N, H] natural log (optional)
 };
 
 template <int KVT>

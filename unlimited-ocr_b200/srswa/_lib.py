@@ -98,6 +98,8 @@ _SIGS = {
                                       vp]),
     "srswa_decode_attend_push": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                            vp, vp]),
+    "srswa_decode_attend_exchange": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                               vp, vp, vp, C.c_int, vp, vp]),
     "srswa_prefill_attend": (C.c_int, [C.POINTER(DecodeDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "srswa_workspace_status": (C.c_int, [vp, C.POINTER(C.c_int), vp]),
     "srswa_gather_bwd_noalloc_status": (C.c_int, [C.POINTER(C.c_int), vp]),

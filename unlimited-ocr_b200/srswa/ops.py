@@ -441,7 +441,7 @@ def gather_bwd(q, k, v, o, lse, do, sel, bias, seg, block_size, scale, local_win
 def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_blocks, sm_scale,
                   out=None, block_table=None, seq_lens=None, q_pos=None, rows_per_req=1,
                   valid=None, lse=False, nsplit=0, kv_layout=None, skip_local=False, lse_out=None,
-                  overlap=False, push=None):
+                  overlap=False, push=None, merged_out=None, merged_lse=None):
     """Sparse decode attend.  q [N,H,D]; paged k/v caches [P, BS, Hkv, D] (any
     strides with D contiguous) indexed by block_table [R,W].  With
     block_table None, kv_layout = (R, W, s_req, s_pos, s_head, Hkv) describes
@@ -455,7 +455,11 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
     kernel began (srswa_decode_desc.overlap).  Same results either way.
     push (an srswa_peer): out / lse_out are fp32 views of this rank's own
     slot of that exchange and the results are also stored into every peer's
-    region (srswa_decode_attend_push)."""
+    region (srswa_decode_attend_push).  merged_out (with an LL push): the
+    attend also waits for every rank's partial and writes their log-sum-exp
+    merge there (and to merged_lse), srswa_decode_attend_exchange; raises
+    NotImplementedError (ETOOLARGE, nothing launched) when the grid would not
+    be resident at once."""
     N, H, D = q.shape
     assert k_cache.stride() == v_cache.stride()
     if block_table is not None:
@@ -513,6 +517,15 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
                      1 if (overlap and early) else 0)
     if ti.dtype not in (torch.int32, torch.int64):
         raise NotImplementedError("topk_idx must be int32 or int64")
+    if merged_out is not None:
+        assert merged_out.is_contiguous() and merged_out.shape == (N, H, D)
+        rc = L.lib().srswa_decode_attend_exchange(C.byref(d), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                                  L.ptr(bt), L.ptr(sl), L.ptr(qp), ti.data_ptr(), L.ptr(b),
+                                                  L.ptr(vd), out.data_ptr(), L.ptr(lse_t), C.byref(push),
+                                                  merged_out.data_ptr(), L.dtype_code(merged_out),
+                                                  L.ptr(merged_lse), L.stream_of(q))
+        L.check(rc, "srswa_decode_attend_exchange")
+        return merged_out
     if push is not None:
         rc = L.lib().srswa_decode_attend_push(C.byref(d), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                                               L.ptr(bt), L.ptr(sl), L.ptr(qp), ti.data_ptr(), L.ptr(b), L.ptr(vd),

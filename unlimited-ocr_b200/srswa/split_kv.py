@@ -226,6 +226,27 @@ class PeerBackend(CudaBackend):
                                       block_table=layer["block_table"], q_pos=q_pos, rows_per_req=N, lse=True,
                                       skip_local=skip_local, lse_out=lse, overlap=True, push=self.part_x.peer)
 
+    def attend_merge(self, q, layer, topi, bias, q_pos, *, block_size, local_blocks, sm_scale, skip_local,
+                     out_dtype):
+        """ll: the attend also exchanges and merges the partials (one launch
+        instead of attend + merge); None when its grid would not be resident
+        at once (the caller then attends and merges separately)."""
+        if self.mode != "ll":
+            return None
+        N, H, D = q.shape
+        n4 = -(-(N * H * D + N * H) // 4) * 4
+        buf = torch.empty(n4, device=q.device, dtype=torch.float32)
+        out, lse = buf[:N * H * D].view(N, H, D), buf[N * H * D:N * H * D + N * H].view(N, H)
+        final = torch.empty(N, H, D, device=q.device, dtype=out_dtype)
+        try:
+            return self.ops.decode_attend(q, layer["k_cache"], layer["v_cache"], topi, bias, block_size=block_size,
+                                          local_blocks=local_blocks, sm_scale=sm_scale, out=out,
+                                          block_table=layer["block_table"], q_pos=q_pos, rows_per_req=N, lse=True,
+                                          skip_local=skip_local, lse_out=lse, overlap=True, push=self.part_x.peer,
+                                          merged_out=final)
+        except NotImplementedError:
+            return None
+
     def exchange_partials(self, o_part, lse_part, world):
         if self.mode == "ll":   # the merge reads the LL words from the region itself
             return o_part, lse_part
@@ -304,6 +325,13 @@ class SplitKVDecode:
         else:
             keys = be.shard_keys(idx_q, layer, plan, q_pos, self.rp)        # [N, M]
             sel = be.merge_keys(be.gather_keys(keys, world), plan, self.rp)  # [world, N, M] -> selection
+        kw = dict(block_size=self.block_size, local_blocks=self.local_blocks, sm_scale=self.sm_scale,
+                  skip_local=(plan.rank != owner))
+        attend_merge = getattr(be, "attend_merge", None)      # steps 4-5 in one launch
+        if world > 1 and attend_merge is not None:
+            out = attend_merge(q, layer, sel["topi32_own"], sel["bias"], q_pos, out_dtype=out_dtype, **kw)
+            if out is not None:
+                return out
         # one rank: its output is final, written in out_dtype; else fp32 partials
         o_part, lse_part = be.attend(q, layer, sel["topi32_own"], sel["bias"], q_pos,
                                      block_size=self.block_size, local_blocks=self.local_blocks,
