@@ -58,7 +58,7 @@ def parse():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode: skip the cfg2 / cfg4 / cfg5 results that ride along in the line")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx", "pagegate", "rope"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx", "pagegate", "rope", "kl"],
                     help="decode = cfg3 (default, the headline); prefill = cfg2; train = cfg4 fwd+bwd; "
                          "route = the cfg3 router alone (k_bar cache + block table, no KV; for profiling); "
                          "longctx = cfg5 attention share (12 layers, one 1M-token sequence, split-KV); "
@@ -743,6 +743,74 @@ def page_doc(B, T, seed, per_page=273, img=128815, mark=128827):
     return out
 
 
+def main_kl(args):
+    """DSA gather-KL distillation (srswa.dsa.gather_kl, the select_and_kl_loss
+    KL of the reference's sparse stage) forward + backward at the cfg4 per-
+    element shape: T = 32768 rows, index d = 128, main H = Hkv = 10 x 128,
+    16 selected 64-token blocks per row below a 1024-token window.  The
+    selection is seeded random blocks of each row's remote range (the
+    router's output stands in).  The kernels gather the selected keys' index
+    and main rows from L2 (idx_k + k_main = 92 MB here): the figure is the
+    gathered bytes per second, bound by L2, not HBM.  One GPU (each rank its
+    own copy under torchrun)."""
+    from srswa import dsa
+    world, rank, local = rank_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_dist(dev, world)
+    T_ = args.seq or 32768
+    H_, Dm, d_, BS_, LW_, S_ = 10, 128, 128, 64, 1024, 16
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    iq = (torch.randn(1, T_, d_, device=dev, generator=g) * 0.08).to(torch.bfloat16).requires_grad_(True)
+    ik = torch.randn(1, T_, d_, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+    qm = torch.randn(1, T_, H_, Dm, device=dev, generator=g).to(torch.bfloat16)
+    km = torch.randn(1, T_, H_, Dm, device=dev, generator=g).to(torch.bfloat16)
+    pos = torch.arange(T_, device=dev)[None]
+    nrem = ((pos - LW_ + 1).clamp(min=0) // BS_)                     # remote blocks of each row: [0, nrem)
+    r = torch.rand(1, T_, S_, device=dev, generator=g)
+    sel = (r * nrem[..., None]).long()
+    sel = torch.where(torch.arange(S_, device=dev) < nrem[..., None], sel, torch.full_like(sel, -1)).to(torch.int32)
+    gout = torch.randn(1, T_, device=dev, generator=g)
+    kept = int(((sel >= 0).sum()).item()) * BS_                       # gathered keys (upper bound: repeats)
+
+    def step():
+        iq.grad = None
+        ik.grad = None
+        kl, _ = dsa.gather_kl(iq, ik, qm, km, sel, pos, block_size=BS_, local_window=LW_, scaling=1 / math.sqrt(Dm))
+        kl.backward(gout)
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    clocks = Clocks(local)
+    clocks.start()
+    times, g_ = timed_graph(step, args.steps, max(args.warmup, 3), flush, False)
+    clk = clocks.stop()
+    ms = sum(times) / len(times)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    # gathered bytes: forward reads each kept key's index row and its main
+    # rows of every head; the backward reads them again and writes a logit
+    # gradient per key slot
+    byts = kept * (d_ + H_ * Dm) * 2 * 2 + kept * 4
+    if rank == 0:
+        print(json.dumps({"metric": "DSA gather-KL forward + backward (cfg4 shape)", "value": T_ * world / (ms * 1e-3),
+                          "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+                          "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "bf16", "data": "synthetic seeded N(0,1), seeded random remote selections",
+                          "config": {"workload": "gather-KL fwd+bwd", "rows": T_, "heads": H_, "head_dim": Dm,
+                                     "index_dim": d_, "blocks_per_row": S_, "block": BS_, "window": LW_,
+                                     "l2": "flushed before every timed step (the gathered rows then stay in L2)"},
+                          "gathered_gb_s": byts / (ms * 1e-3) / 1e9, "bound": "L2 gather", "clocks": clk}),
+              flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main_pagegate(args):
     """PageGate candidate masks for a prefill of cfg2's shape (B=4, T=16384,
     block 64): page-aware ids -> block descriptors -> per-query candidate
@@ -1029,6 +1097,8 @@ def main():
         return main_pagegate(args)
     if args.workload == "rope":
         return main_rope(args)
+    if args.workload == "kl":
+        return main_kl(args)
     if args.workload != "decode" and args.impl != "reference":
         return main_dense(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))

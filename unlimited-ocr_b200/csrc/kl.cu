@@ -19,7 +19,8 @@
 // (P = sum of p over the row's keys) and dQ = sum_j ds_j idx_k[j].
 // kl_dk_kernel: one CTA per (batch, key block): dK of the block's keys, the
 // sum over the rows that selected the block in row order (no atomics: the
-// gradient is deterministic).
+// gradient is deterministic), walking the block's list of (row, slot) pairs
+// built by the kl_pairs_* kernels.
 // Memory-bound on gathered rows (the keys of a row are read by that row only).
 #include "common.cuh"
 
@@ -54,17 +55,24 @@ __device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(_
 
 // dot of an 8-lane group: this lane's nd features of q (registers) with the
 // same features of the row at p (element offset off), reduced over the group
+// (loops run to the compile-time bound with a predicate so that qv stays in
+// registers: nd <= kKlMaxDim / 8 = 16)
 __device__ __forceinline__ float group_dot(const float* qv, int nd, const void* p, int64_t off, int dtype) {
   float acc = 0.f;
   if (nd % 8 == 0 && dtype != SRSWA_F32) {
-    for (int e = 0; e < nd; e += 8) {
-      float v[8];
-      load8(p, off + e, dtype, v);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc = fmaf(qv[e + u], v[u], acc);
+    for (int e = 0; e < kKlMaxDim / 8; e += 8) {
+      if (e < nd) {
+        float v[8];
+        load8(p, off + e, dtype, v);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc = fmaf(qv[e + u], v[u], acc);
+      }
     }
   } else {
-    for (int e = 0; e < nd; ++e) acc = fmaf(qv[e], load_elem(p, off + e, dtype), acc);
+#pragma unroll
+    for (int e = 0; e < kKlMaxDim / 8; ++e)
+      if (e < nd) acc = fmaf(qv[e], load_elem(p, off + e, dtype), acc);
   }
   acc += __shfl_xor_sync(0xffffffffu, acc, 1);
   acc += __shfl_xor_sync(0xffffffffu, acc, 2);
@@ -127,7 +135,9 @@ __global__ void __launch_bounds__(kKlThreads) kl_row_kernel(const KlArgs a) {
   };
   // ---- student logits ----
   float qv[kKlMaxDim / 8];
-  for (int e = 0; e < nd; ++e) qv[e] = load_elem(a.iq, b * a.s_iq_b + c * a.s_iq_c + u * nd + e, a.iq_dtype);
+#pragma unroll
+  for (int e = 0; e < kKlMaxDim / 8; ++e)
+    qv[e] = e < nd ? load_elem(a.iq, b * a.s_iq_b + c * a.s_iq_c + u * nd + e, a.iq_dtype) : 0.f;
   float mx = -INFINITY;
   for (int k0 = 0; k0 < NK; k0 += kKlThreads / 8) {
     const int k = k0 + grp;
@@ -155,8 +165,9 @@ __global__ void __launch_bounds__(kKlThreads) kl_row_kernel(const KlArgs a) {
   // ---- teacher: per main head softmax over the same keys, averaged ----
   const int64_t grp_h = a.H / a.Hkv;
   for (int64_t h = 0; h < a.H; ++h) {
-    for (int e = 0; e < nD; ++e)
-      qv[e] = load_elem(a.qm, b * a.s_qm_b + c * a.s_qm_c + h * a.s_qm_h + u * nD + e, a.qm_dtype);
+#pragma unroll
+    for (int e = 0; e < kKlMaxDim / 8; ++e)
+      qv[e] = e < nD ? load_elem(a.qm, b * a.s_qm_b + c * a.s_qm_c + h * a.s_qm_h + u * nD + e, a.qm_dtype) : 0.f;
     float mh = -INFINITY;
     for (int k0 = 0; k0 < NK; k0 += kKlThreads / 8) {
       const int k = k0 + grp;
@@ -211,14 +222,19 @@ __global__ void __launch_bounds__(kKlThreads) kl_row_kernel(const KlArgs a) {
   }
   __syncthreads();
   float dacc[kKlMaxDim / 8];
-  for (int e = 0; e < nd; ++e) dacc[e] = 0.f;
+#pragma unroll
+  for (int e = 0; e < kKlMaxDim / 8; ++e) dacc[e] = 0.f;
   for (int k = grp; k < NK; k += kKlThreads / 8) {
     if (!kept(k)) continue;
     const float w = tv[k];
     const int64_t off = b * a.s_ik_b + key_pos(k) * a.s_ik_s + u * nd;
-    for (int e = 0; e < nd; ++e) dacc[e] = fmaf(w, load_elem(a.ik, off + e, a.ik_dtype), dacc[e]);
+#pragma unroll
+    for (int e = 0; e < kKlMaxDim / 8; ++e)
+      if (e < nd) dacc[e] = fmaf(w, load_elem(a.ik, off + e, a.ik_dtype), dacc[e]);
   }
-  for (int e = 0; e < nd; ++e) dq_part[grp][u * nd + e] = dacc[e];
+#pragma unroll
+  for (int e = 0; e < kKlMaxDim / 8; ++e)
+    if (e < nd) dq_part[grp][u * nd + e] = dacc[e];
   __syncthreads();
   for (int e = tid; e < a.d; e += kKlThreads) {
     float v = 0.f;
@@ -229,69 +245,177 @@ __global__ void __launch_bounds__(kKlThreads) kl_row_kernel(const KlArgs a) {
 
 // dK of key block bk of batch b: the sum over the rows that selected the
 // block (ascending row order) of ds[row, slot, i] * idx_q[row].
-__global__ void __launch_bounds__(kKlThreads) kl_dk_kernel(const KlArgs a) {
-  __shared__ int32_t rows[kKlThreads], slots[kKlThreads];
-  __shared__ int n_found;
+// ---- dK through per-block pair lists (row order, deterministic) ----
+// kl_pairs_bitmap_kernel: bit (b, block, row) set when the row selects the
+//   block (atomicOr: the bitmap does not depend on the order of the ORs);
+// kl_pairs_count_kernel: one warp per list, its length;
+// kl_pairs_scan_kernel: one CTA, exclusive offsets of the lists;
+// kl_pairs_fill_kernel: one CTA per list, (row * S + first slot holding the
+//   block) in row order;
+// kl_dk_kernel: one CTA per (batch, key block) over its list, 16 pairs at a
+//   time staged in shared memory; the sum runs in row order, as before.
+constexpr int kKlPairGroup = 16;
+
+__global__ void kl_pairs_bitmap_kernel(const KlArgs a, int64_t nbk, int64_t C32, uint32_t* bitmap) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // b * C + c
+  if (row >= a.B * a.C) return;
+  const int64_t b = row / a.C, c = row % a.C;
+  const int32_t* sr = a.sel + row * a.S;
+  for (int64_t s = 0; s < a.S; ++s) {
+    const int32_t blk = sr[s];
+    if (blk < 0 || blk >= nbk) continue;
+    atomicOr(bitmap + (b * nbk + blk) * C32 + (c >> 5), 1u << (c & 31));
+  }
+}
+
+__global__ void kl_pairs_count_kernel(int64_t nlists, int64_t C32, const uint32_t* bitmap, int32_t* count) {
+  const int lane = threadIdx.x & 31;
+  const int64_t l = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (l >= nlists) return;
+  const uint32_t* w = bitmap + l * C32;
+  int n = 0;
+  for (int64_t i = lane; i < C32; i += 32) n += __popc(w[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+  if (lane == 0) count[l] = n;
+}
+
+// exclusive scan of count[0, n) into offs (one CTA of 1024 threads: each
+// thread a contiguous range, a CTA scan of the range sums)
+__global__ void __launch_bounds__(1024) kl_pairs_scan_kernel(const int32_t* count, int64_t n, int32_t* offs) {
+  __shared__ int32_t part[1024];
+  const int tid = threadIdx.x;
+  const int64_t per = (n + 1023) / 1024;
+  const int64_t lo = tid * per, hi = min(n, lo + per);
+  int32_t sum = 0;
+  for (int64_t i = lo; i < hi; ++i) sum += count[i];
+  part[tid] = sum;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const int32_t v = tid >= o ? part[tid - o] : 0;
+    __syncthreads();
+    part[tid] += v;
+    __syncthreads();
+  }
+  int32_t run = part[tid] - sum;
+  for (int64_t i = lo; i < hi; ++i) {
+    offs[i] = run;
+    run += count[i];
+  }
+}
+
+__global__ void __launch_bounds__(256) kl_pairs_fill_kernel(const KlArgs a, int64_t nbk, int64_t C32,
+                                                            const uint32_t* bitmap, const int32_t* offs,
+                                                            int32_t* pairs) {
+  __shared__ int32_t wcount[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t l = blockIdx.x;  // b * nbk + block
+  const int64_t b = l / nbk, blk = l % nbk;
+  const uint32_t* w = bitmap + l * C32;
+  const int64_t per = (C32 + 7) / 8;
+  const int64_t wlo = warp * per, whi = min(C32, wlo + per);
+  int n = 0;
+  for (int64_t i = wlo + lane; i < whi; i += 32) n += __popc(w[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+  if (lane == 0) wcount[warp] = n;
+  __syncthreads();
+  int64_t pos = offs[l];
+  for (int u = 0; u < warp; ++u) pos += wcount[u];
+  for (int64_t w0 = wlo; w0 < whi; w0 += 32) {
+    uint32_t word = (w0 + lane < whi) ? w[w0 + lane] : 0u;
+    const int nb = __popc(word);
+    int incl = nb;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int64_t p = pos + incl - nb;
+    while (word) {
+      const int bit = __ffs(word) - 1;
+      word &= word - 1;
+      const int64_t c = (w0 + lane) * 32 + bit;
+      const int32_t* sr = a.sel + (b * a.C + c) * a.S;
+      int32_t slot = 0;
+      for (int32_t s = static_cast<int32_t>(a.S) - 1; s >= 0; --s) slot = sr[s] == blk ? s : slot;  // first
+      pairs[p++] = static_cast<int32_t>((c << 6) | slot);  // S <= 64
+    }
+    pos += __shfl_sync(0xffffffffu, incl, 31);
+  }
+}
+
+template <bool kFast>  // kFast: d == 128 and BS == 64
+__global__ void __launch_bounds__(kKlThreads) kl_dk_kernel(const KlArgs a, int64_t nbk, const int32_t* offs,
+                                                          const int32_t* count, const int32_t* pairs) {
+  __shared__ __align__(16) float s_ds[kKlPairGroup][64];
+  __shared__ float s_iq[kKlPairGroup][kKlMaxDim];
   const int64_t bk = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x;
   const int BS = static_cast<int>(a.BS), d = static_cast<int>(a.d);
   const int NK = static_cast<int>(a.S) * BS;
   const int nel = BS * d;
-  const int per = (nel + kKlThreads - 1) / kKlThreads;  // <= 32 (BS <= 64, d <= 128)
+  // element r of this thread: key ki[r], feature fe[r] of the block's
+  // [BS, d] dK; kFast: feature tid % 128 and keys 32 (tid / 128) + r, so one
+  // index-query value per pair and four 16-byte loads of its logit
+  // gradients feed the 32 FMAs.  Registers only (r loops unrolled).
   float acc[32];
-  for (int r = 0; r < 32; ++r) acc[r] = 0.f;
-  for (int64_t c0 = 0; c0 < a.C; c0 += kKlThreads) {
-    if (tid == 0) n_found = 0;
+  int ki[32], fe[32];
+#pragma unroll
+  for (int r = 0; r < 32; ++r) {
+    acc[r] = 0.f;
+    if (kFast) {
+      ki[r] = (tid >> 7) * 32 + r;
+      fe[r] = tid & 127;
+    } else {
+      const int el = tid + r * kKlThreads;
+      ki[r] = el < nel ? el / d : -1;
+      fe[r] = el < nel ? el - (el / d) * d : 0;
+    }
+  }
+  const int64_t l = b * nbk + bk;
+  const int32_t* lp = pairs + offs[l];
+  const int np = count[l];
+  for (int g0 = 0; g0 < np; g0 += kKlPairGroup) {
+    const int ng = min(kKlPairGroup, np - g0);
+    // stage the group's logit-gradient slices and index-query rows
+    for (int e = tid; e < ng * BS; e += kKlThreads) {
+      const int f = e / BS, i = e - f * BS;
+      const int32_t pr = lp[g0 + f];
+      const int64_t c = pr >> 6, slot = pr & 63;
+      s_ds[f][i] = a.ds[(b * a.C + c) * NK + slot * BS + i];
+    }
+    for (int e = tid; e < ng * d; e += kKlThreads) {
+      const int f = e / d, k = e - f * d;
+      const int64_t c = lp[g0 + f] >> 6;
+      s_iq[f][k] = load_elem(a.iq, b * a.s_iq_b + c * a.s_iq_c + k, a.iq_dtype);
+    }
     __syncthreads();
-    const int64_t c = c0 + tid;
-    int hit = -1;
-    if (c < a.C) {
-      const int32_t* sr = a.sel + (b * a.C + c) * a.S;
-      for (int s = 0; s < a.S; ++s)
-        if (sr[s] == bk) {
-          hit = s;  // the first slot: a repeat keeps no keys (ds = 0)
-          break;
+    for (int f = 0; f < ng; ++f) {
+      if (kFast) {
+        const float q = s_iq[f][tid & 127];
+        const float4* dsv = reinterpret_cast<const float4*>(&s_ds[f][(tid >> 7) * 32]);
+#pragma unroll
+        for (int r4 = 0; r4 < 8; ++r4) {
+          const float4 v = dsv[r4];
+          acc[4 * r4] = fmaf(v.x, q, acc[4 * r4]);
+          acc[4 * r4 + 1] = fmaf(v.y, q, acc[4 * r4 + 1]);
+          acc[4 * r4 + 2] = fmaf(v.z, q, acc[4 * r4 + 2]);
+          acc[4 * r4 + 3] = fmaf(v.w, q, acc[4 * r4 + 3]);
         }
-    }
-    // compact the hits in row order (warp ballots, then warps in order)
-    const unsigned m = __ballot_sync(0xffffffffu, hit >= 0);
-    __shared__ int warp_cnt[kKlThreads / 32];
-    if ((tid & 31) == 0) warp_cnt[tid >> 5] = __popc(m);
-    __syncthreads();
-    int base = 0;
-    for (int w = 0; w < (tid >> 5); ++w) base += warp_cnt[w];
-    if (hit >= 0) {
-      const int at = base + __popc(m & ((1u << (tid & 31)) - 1u));
-      rows[at] = static_cast<int32_t>(c);
-      slots[at] = hit;
-    }
-    if (tid == kKlThreads - 1) {
-      int t = 0;
-      for (int w = 0; w < kKlThreads / 32; ++w) t += warp_cnt[w];
-      n_found = t;
-    }
-    __syncthreads();
-    const int nf = n_found;
-    for (int f = 0; f < nf; ++f) {
-      const int64_t rr = b * a.C + rows[f];
-      const float* dsr = a.ds + rr * NK + static_cast<int64_t>(slots[f]) * BS;
-      for (int r = 0; r < per; ++r) {
-        const int el = tid + r * kKlThreads;
-        if (el < nel) {
-          const int i = el / d, e = el - i * d;
-          acc[r] = fmaf(dsr[i], load_elem(a.iq, b * a.s_iq_b + rows[f] * a.s_iq_c + e, a.iq_dtype), acc[r]);
-        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < 32; ++r)
+          if (ki[r] >= 0) acc[r] = fmaf(s_ds[f][ki[r]], s_iq[f][fe[r]], acc[r]);
       }
     }
     __syncthreads();
   }
-  for (int r = 0; r < per; ++r) {
-    const int el = tid + r * kKlThreads;
-    if (el < nel) {
-      const int i = el / d, e = el - i * d;
-      const int64_t j = bk * a.BS + i;
-      if (j < a.Sk) a.dk[(b * a.Sk + j) * a.d + e] = acc[r];
-    }
+#pragma unroll
+  for (int r = 0; r < 32; ++r) {
+    if (ki[r] < 0) continue;
+    const int64_t j = bk * a.BS + ki[r];
+    if (j < a.Sk) a.dk[(b * a.Sk + j) * a.d + fe[r]] = acc[r];
   }
 }
 
@@ -332,9 +456,31 @@ extern "C" int srswa_gather_kl_fwd(const srswa_kl_desc* g, const void* idx_q, co
   return srswa_last_launch_status();
 }
 
+// backward workspace: logit gradients [B, C, S * BS] fp32, then the dK pair
+// lists: bitmap [B, nbk, ceil(C / 32)], count and offsets [B, nbk], pairs
+// [B, C, S] (each part 256-byte aligned)
+struct KlBwdLayout {
+  size_t ds, bitmap, count, offs, pairs, total;
+  int64_t nbk, C32;
+};
+static size_t kl_align(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+static KlBwdLayout kl_bwd_layout(const srswa_kl_desc* g) {
+  KlBwdLayout L = {};
+  L.nbk = g->Sk > 0 ? (g->Sk + g->block_size - 1) / g->block_size : 0;
+  L.C32 = (g->C + 31) / 32;
+  size_t off = 0;
+  L.ds = off; off += kl_align(static_cast<size_t>(g->B * g->C * g->S * g->block_size) * sizeof(float));
+  L.bitmap = off; off += kl_align(static_cast<size_t>(g->B * L.nbk * L.C32) * 4);
+  L.count = off; off += kl_align(static_cast<size_t>(g->B * L.nbk) * 4);
+  L.offs = off; off += kl_align(static_cast<size_t>(g->B * L.nbk) * 4);
+  L.pairs = off; off += kl_align(static_cast<size_t>(g->B * g->C * g->S) * 4);
+  L.total = off;
+  return L;
+}
+
 extern "C" size_t srswa_gather_kl_bwd_workspace_size(const srswa_kl_desc* g) {
-  if (!g || g->B < 0 || g->C < 0 || g->S < 0 || g->block_size <= 0) return 0;
-  return static_cast<size_t>(g->B * g->C * g->S * g->block_size) * sizeof(float);
+  if (!g || g->B < 0 || g->C < 0 || g->S < 0 || g->block_size <= 0 || g->Sk < 0) return 0;
+  return kl_bwd_layout(g).total;
 }
 
 extern "C" int srswa_gather_kl_bwd(const srswa_kl_desc* g, const void* idx_q, const void* idx_k, const void* q_main,
@@ -353,12 +499,29 @@ extern "C" int srswa_gather_kl_bwd(const srswa_kl_desc* g, const void* idx_q, co
   SRSWA_CHECK_ARG(workspace && workspace_bytes >= srswa_gather_kl_bwd_workspace_size(g), SRSWA_EWORKSPACE);
   SRSWA_CHECK_ARG(g->B * g->C < (1ll << 31) && g->B < 65536, SRSWA_ETOOLARGE);
   a.iq = idx_q; a.ik = idx_k; a.qm = q_main; a.km = k_main; a.sel = sel; a.pos = pos; a.seg = seg;
-  a.g = grad; a.ds = static_cast<float*>(workspace); a.dq = d_idx_q; a.dk = d_idx_k;
+  const KlBwdLayout L = kl_bwd_layout(g);
+  char* ws = static_cast<char*>(workspace);
+  a.g = grad; a.ds = reinterpret_cast<float*>(ws + L.ds); a.dq = d_idx_q; a.dk = d_idx_k;
   kl_row_kernel<true><<<static_cast<unsigned>(g->B * g->C), kKlThreads, 0, st>>>(a);
   SRSWA_CUDA_TRY(cudaGetLastError());
   if (g->S > 0 && g->Sk > 0) {
-    const int64_t nbk = (g->Sk + g->block_size - 1) / g->block_size;
-    kl_dk_kernel<<<dim3(static_cast<unsigned>(nbk), static_cast<unsigned>(g->B)), kKlThreads, 0, st>>>(a);
+    const int64_t nlists = g->B * L.nbk;
+    SRSWA_CHECK_ARG(L.nbk < 65536 && g->B * g->C * g->S < (1ll << 31), SRSWA_ETOOLARGE);
+    uint32_t* bitmap = reinterpret_cast<uint32_t*>(ws + L.bitmap);
+    int32_t* count = reinterpret_cast<int32_t*>(ws + L.count);
+    int32_t* offs = reinterpret_cast<int32_t*>(ws + L.offs);
+    int32_t* pairs = reinterpret_cast<int32_t*>(ws + L.pairs);
+    SRSWA_CUDA_TRY(cudaMemsetAsync(bitmap, 0, static_cast<size_t>(nlists * L.C32) * 4, st));
+    kl_pairs_bitmap_kernel<<<static_cast<unsigned>((g->B * g->C + 255) / 256), 256, 0, st>>>(a, L.nbk, L.C32,
+                                                                                            bitmap);
+    kl_pairs_count_kernel<<<static_cast<unsigned>((nlists + 7) / 8), 256, 0, st>>>(nlists, L.C32, bitmap, count);
+    kl_pairs_scan_kernel<<<1, 1024, 0, st>>>(count, nlists, offs);
+    kl_pairs_fill_kernel<<<static_cast<unsigned>(nlists), 256, 0, st>>>(a, L.nbk, L.C32, bitmap, offs, pairs);
+    const dim3 grid(static_cast<unsigned>(L.nbk), static_cast<unsigned>(g->B));
+    if (g->d == 128 && g->block_size == 64)
+      kl_dk_kernel<true><<<grid, kKlThreads, 0, st>>>(a, L.nbk, offs, count, pairs);
+    else
+      kl_dk_kernel<false><<<grid, kKlThreads, 0, st>>>(a, L.nbk, offs, count, pairs);
   }
   return srswa_last_launch_status();
 }
