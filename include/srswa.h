@@ -469,6 +469,22 @@ SRSWA_API int srswa_gather_kl_bwd(const srswa_kl_desc* g, const void* idx_q, con
                         const void* k_main, const int32_t* sel, const int64_t* pos, const int64_t* seg,
                         const float* grad, float* d_idx_q, float* d_idx_k, void* workspace,
                         size_t workspace_bytes, srswa_stream_t stream);
+/* The same pair keeping the teacher: srswa_gather_kl_fwd_save also writes
+ * each row's averaged teacher probabilities over its S * block_size key
+ * slots, teacher [B, C, S * block_size] fp32 (0 on slots that keep no key),
+ * and srswa_gather_kl_bwd_saved reads them instead of recomputing the H
+ * teacher softmaxes (the gather of every head's main keys, most of the
+ * backward's work).  Results equal the recomputing pair bit for bit; the
+ * price is the teacher buffer kept between the two calls.  No reference
+ * counterpart (the reference recomputes inside its chunked autograd
+ * function). */
+SRSWA_API int srswa_gather_kl_fwd_save(const srswa_kl_desc* g, const void* idx_q, const void* idx_k,
+                        const void* q_main, const void* k_main, const int32_t* sel, const int64_t* pos,
+                        const int64_t* seg, float* kl, uint8_t* valid, float* teacher, srswa_stream_t stream);
+SRSWA_API int srswa_gather_kl_bwd_saved(const srswa_kl_desc* g, const void* idx_q, const void* idx_k,
+                        const int32_t* sel, const int64_t* pos, const int64_t* seg, const float* teacher,
+                        const float* grad, float* d_idx_q, float* d_idx_k, void* workspace,
+                        size_t workspace_bytes, srswa_stream_t stream);
 
 /* --------------------------------------------------- peer exchange ------
  * All-gather through peer memory for the split-KV decode across the GPUs of

@@ -79,3 +79,31 @@ def test_gather_kl_baseline_heads_vs_oracle(cuda):
     # deterministic backward
     _, _, dq2, dk2 = _run(cuda, iq, ik, qm, km, sel, pos, None, BS, LW, scaling, gout)
     assert np.array_equal(dq, dq2) and np.array_equal(dk, dk2)
+
+
+def test_gather_kl_saved_teacher_equals_recompute(cuda):
+    """The backward that reads the forward's saved teacher probabilities
+    (srswa_gather_kl_fwd_save / _bwd_saved) gives the recomputing backward's
+    gradients bit for bit."""
+    rng = np.random.default_rng(43)
+    B, Cq, H, Hkv, D, d, BS, LW, S = 1, 1200, 10, 10, 128, 128, 64, 512, 8
+    iq = (rng.standard_normal((B, Cq, d)) * 0.08).astype(np.float32)
+    ik = rng.standard_normal((B, Cq, d)).astype(np.float32)
+    qm = rng.standard_normal((B, Cq, H, D)).astype(np.float32)
+    km = rng.standard_normal((B, Cq, Hkv, D)).astype(np.float32)
+    pos = np.arange(Cq)[None]
+    nrem = np.maximum(pos - LW + 1, 0) // BS
+    sel = np.where(np.arange(S) < nrem[..., None], (rng.random((B, Cq, S)) * nrem[..., None]).astype(np.int64), -1)
+    gout = rng.standard_normal((B, Cq)).astype(np.float32)
+    res = []
+    for save in (True, False):
+        qi = T(iq, cuda, torch.bfloat16).requires_grad_(True)
+        ki = T(ik, cuda, torch.bfloat16).requires_grad_(True)
+        kl, _ = dsa.gather_kl(qi, ki, T(qm, cuda, torch.bfloat16), T(km, cuda, torch.bfloat16), T(sel, cuda),
+                              T(pos, cuda), block_size=BS, local_window=LW, scaling=1 / math.sqrt(D),
+                              save_teacher=save)
+        kl.backward(T(gout, cuda))
+        torch.cuda.synchronize()
+        res.append((kl.detach(), qi.grad, ki.grad))
+    for a, b in zip(*res):
+        assert torch.equal(a, b)

@@ -47,6 +47,8 @@ struct KlArgs {
   uint8_t* valid;
   const float* g;
   float* ds;   // [B, C, S * BS] logit gradients (backward)
+  float* tp_out;       // forward: averaged teacher probabilities [B, C, S * BS] (optional)
+  const float* tp_in;  // backward: those probabilities instead of recomputing the teacher
   float* dq;   // [B, C, d]
   float* dk;   // [B, Sk, d]
 };
@@ -163,8 +165,15 @@ __global__ void __launch_bounds__(kKlThreads) kl_row_kernel(const KlArgs a) {
   const bool any = m_s != -INFINITY;
   const float lse_s = any ? m_s + logf(l_s) : 0.f;
   // ---- teacher: per main head softmax over the same keys, averaged ----
+  // (pa holds the sum over heads; with a saved teacher the backward reads
+  // pa / H directly)
   const int64_t grp_h = a.H / a.Hkv;
-  for (int64_t h = 0; h < a.H; ++h) {
+  const bool saved = BWD && a.tp_in != nullptr;
+  if (saved) {
+    for (int k = tid; k < NK; k += kKlThreads) pa[k] = a.tp_in[row * NK + k];
+    __syncthreads();
+  }
+  for (int64_t h = 0; h < (saved ? 0 : a.H); ++h) {
 #pragma unroll
     for (int e = 0; e < kKlMaxDim / 8; ++e)
       qv[e] = e < nD ? load_elem(a.qm, b * a.s_qm_b + c * a.s_qm_c + h * a.s_qm_h + u * nD + e, a.qm_dtype) : 0.f;
@@ -194,11 +203,18 @@ __global__ void __launch_bounds__(kKlThreads) kl_row_kernel(const KlArgs a) {
     __syncthreads();
   }
   const float invH = 1.f / static_cast<float>(a.H);
+  // averaged teacher probability of slot k: a rounded product (never fused
+  // into a neighbouring add), so the saved and the recomputed value are the
+  // same float and every use rounds alike
+  auto pt = [&](int k) { return saved ? pa[k] : __fmul_rn(pa[k], invH); };
+  if (!BWD && a.tp_out) {
+    for (int k = tid; k < NK; k += kKlThreads) a.tp_out[row * NK + k] = kept(k) ? pt(k) : 0.f;
+  }
   if (!BWD) {
     float acc = 0.f;
     for (int k = tid; k < NK; k += kKlThreads)
       if (kept(k)) {
-        const float p = pa[k] * invH;
+        const float p = pt(k);
         acc += p * (logf(fmaxf(p, 1e-12f)) - (sv[k] - lse_s));
       }
     const float kl = block_reduce(acc, red, false);
@@ -211,12 +227,12 @@ __global__ void __launch_bounds__(kKlThreads) kl_row_kernel(const KlArgs a) {
   // ---- backward: logit gradients of the row, then dQ ----
   float ps = 0.f;
   for (int k = tid; k < NK; k += kKlThreads)
-    if (kept(k)) ps += pa[k] * invH;
+    if (kept(k)) ps += pt(k);
   const float P = block_reduce(ps, red, false);
   const float gr = a.g[row];
   for (int k = tid; k < NK; k += kKlThreads) {
     float dsk = 0.f;
-    if (kept(k)) dsk = gr * (P * expf(sv[k] - lse_s) - pa[k] * invH);
+    if (kept(k)) dsk = gr * (P * expf(sv[k] - lse_s) - pt(k));
     tv[k] = dsk;
     a.ds[row * NK + k] = dsk;
   }
@@ -441,9 +457,21 @@ static int kl_args(const srswa_kl_desc* g, KlArgs& a) {
 
 using namespace srswa;
 
+extern "C" int srswa_gather_kl_fwd_save(const srswa_kl_desc* g, const void* idx_q, const void* idx_k,
+                                        const void* q_main, const void* k_main, const int32_t* sel,
+                                        const int64_t* pos, const int64_t* seg, float* kl, uint8_t* valid,
+                                        float* teacher, srswa_stream_t stream);
+
 extern "C" int srswa_gather_kl_fwd(const srswa_kl_desc* g, const void* idx_q, const void* idx_k, const void* q_main,
                                    const void* k_main, const int32_t* sel, const int64_t* pos, const int64_t* seg,
                                    float* kl, uint8_t* valid, srswa_stream_t stream) {
+  return srswa_gather_kl_fwd_save(g, idx_q, idx_k, q_main, k_main, sel, pos, seg, kl, valid, nullptr, stream);
+}
+
+extern "C" int srswa_gather_kl_fwd_save(const srswa_kl_desc* g, const void* idx_q, const void* idx_k,
+                                        const void* q_main, const void* k_main, const int32_t* sel,
+                                        const int64_t* pos, const int64_t* seg, float* kl, uint8_t* valid,
+                                        float* teacher, srswa_stream_t stream) {
   KlArgs a;
   int rc = kl_args(g, a);
   if (rc) return rc;
@@ -451,7 +479,7 @@ extern "C" int srswa_gather_kl_fwd(const srswa_kl_desc* g, const void* idx_q, co
   SRSWA_CHECK_ARG(idx_q && idx_k && q_main && k_main && pos && kl && valid && (g->S == 0 || sel), SRSWA_EINVAL);
   SRSWA_CHECK_ARG(g->B * g->C < (1ll << 31), SRSWA_ETOOLARGE);
   a.iq = idx_q; a.ik = idx_k; a.qm = q_main; a.km = k_main; a.sel = sel; a.pos = pos; a.seg = seg;
-  a.kl = kl; a.valid = valid;
+  a.kl = kl; a.valid = valid; a.tp_out = teacher;
   kl_row_kernel<false><<<static_cast<unsigned>(g->B * g->C), kKlThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return srswa_last_launch_status();
 }
@@ -483,15 +511,37 @@ extern "C" size_t srswa_gather_kl_bwd_workspace_size(const srswa_kl_desc* g) {
   return kl_bwd_layout(g).total;
 }
 
+static int kl_bwd(const srswa_kl_desc* g, const void* idx_q, const void* idx_k, const void* q_main,
+                  const void* k_main, const int32_t* sel, const int64_t* pos, const int64_t* seg,
+                  const float* teacher, const float* grad, float* d_idx_q, float* d_idx_k, void* workspace,
+                  size_t workspace_bytes, srswa_stream_t stream);
+
 extern "C" int srswa_gather_kl_bwd(const srswa_kl_desc* g, const void* idx_q, const void* idx_k, const void* q_main,
                                    const void* k_main, const int32_t* sel, const int64_t* pos, const int64_t* seg,
                                    const float* grad, float* d_idx_q, float* d_idx_k, void* workspace,
                                    size_t workspace_bytes, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(q_main && k_main, SRSWA_EINVAL);
+  return kl_bwd(g, idx_q, idx_k, q_main, k_main, sel, pos, seg, nullptr, grad, d_idx_q, d_idx_k, workspace,
+                workspace_bytes, stream);
+}
+
+extern "C" int srswa_gather_kl_bwd_saved(const srswa_kl_desc* g, const void* idx_q, const void* idx_k,
+                                         const int32_t* sel, const int64_t* pos, const int64_t* seg,
+                                         const float* teacher, const float* grad, float* d_idx_q, float* d_idx_k,
+                                         void* workspace, size_t workspace_bytes, srswa_stream_t stream) {
+  SRSWA_CHECK_ARG(teacher, SRSWA_EINVAL);
+  return kl_bwd(g, idx_q, idx_k, nullptr, nullptr, sel, pos, seg, teacher, grad, d_idx_q, d_idx_k, workspace,
+                workspace_bytes, stream);
+}
+
+static int kl_bwd(const srswa_kl_desc* g, const void* idx_q, const void* idx_k, const void* q_main,
+                  const void* k_main, const int32_t* sel, const int64_t* pos, const int64_t* seg,
+                  const float* teacher, const float* grad, float* d_idx_q, float* d_idx_k, void* workspace,
+                  size_t workspace_bytes, srswa_stream_t stream) {
   KlArgs a;
   int rc = kl_args(g, a);
   if (rc) return rc;
-  SRSWA_CHECK_ARG(idx_q && idx_k && q_main && k_main && pos && grad && d_idx_q && d_idx_k && (g->S == 0 || sel),
-                  SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(idx_q && idx_k && pos && grad && d_idx_q && d_idx_k && (g->S == 0 || sel), SRSWA_EINVAL);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (g->B * g->Sk > 0 && (g->B * g->C == 0 || g->S == 0))  // no row selects anything: dK is zero
     SRSWA_CUDA_TRY(cudaMemsetAsync(d_idx_k, 0, static_cast<size_t>(g->B * g->Sk * g->d) * 4, st));
@@ -501,7 +551,7 @@ extern "C" int srswa_gather_kl_bwd(const srswa_kl_desc* g, const void* idx_q, co
   a.iq = idx_q; a.ik = idx_k; a.qm = q_main; a.km = k_main; a.sel = sel; a.pos = pos; a.seg = seg;
   const KlBwdLayout L = kl_bwd_layout(g);
   char* ws = static_cast<char*>(workspace);
-  a.g = grad; a.ds = reinterpret_cast<float*>(ws + L.ds); a.dq = d_idx_q; a.dk = d_idx_k;
+  a.g = grad; a.ds = reinterpret_cast<float*>(ws + L.ds); a.dq = d_idx_q; a.dk = d_idx_k; a.tp_in = teacher;
   kl_row_kernel<true><<<static_cast<unsigned>(g->B * g->C), kKlThreads, 0, st>>>(a);
   SRSWA_CUDA_TRY(cudaGetLastError());
   if (g->S > 0 && g->Sk > 0) {

@@ -115,6 +115,9 @@ _SIGS = {
     "srswa_decode_allow": (C.c_int, [vp, i64, i64, i64, vp, vp, i64, i64, vp, vp, i64, vp, vp]),
     "srswa_win_bounds_decode": (C.c_int, [vp, i64, i64, vp, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp]),
     "srswa_gather_kl_fwd": (C.c_int, [C.POINTER(KlDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "srswa_gather_kl_fwd_save": (C.c_int, [C.POINTER(KlDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "srswa_gather_kl_bwd_saved": (C.c_int, [C.POINTER(KlDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                            C.c_size_t, vp]),
     "srswa_gather_kl_bwd_workspace_size": (C.c_size_t, [C.POINTER(KlDesc)]),
     "srswa_gather_kl_bwd": (C.c_int, [C.POINTER(KlDesc), vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t,
                                       vp]),

@@ -45,16 +45,26 @@ def _feat_contig(x):
 
 class _GatherKLFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, iq, ik, qm, km, sel, pos, seg, block_size, local_window, scaling, logits_bf16):
+    def forward(ctx, iq, ik, qm, km, sel, pos, seg, block_size, local_window, scaling, logits_bf16,
+                save_teacher):
         iq, ik, qm, km = (_feat_contig(x) for x in (iq, ik, qm, km))
         B, Cq, _ = iq.shape
-        g = _desc(iq, ik, qm, km, sel.shape[-1], block_size, local_window, scaling, logits_bf16)
+        S = sel.shape[-1]
+        g = _desc(iq, ik, qm, km, S, block_size, local_window, scaling, logits_bf16)
         kl = torch.empty(B, Cq, device=iq.device, dtype=torch.float32)
         valid = torch.empty(B, Cq, device=iq.device, dtype=torch.uint8)
-        rc = L.lib().srswa_gather_kl_fwd(C.byref(g), iq.data_ptr(), ik.data_ptr(), qm.data_ptr(), km.data_ptr(),
-                                         sel.data_ptr(), pos.data_ptr(), L.ptr(seg), kl.data_ptr(), valid.data_ptr(),
-                                         L.stream_of(iq))
+        # save_teacher: keep the averaged teacher probabilities [B, C, S * BS]
+        # (fp32) so that the backward does not gather every head's main keys again
+        teacher = torch.empty(B, Cq, S * int(block_size), device=iq.device, dtype=torch.float32) \
+            if save_teacher else None
+        rc = L.lib().srswa_gather_kl_fwd_save(C.byref(g), iq.data_ptr(), ik.data_ptr(), qm.data_ptr(),
+                                              km.data_ptr(), sel.data_ptr(), pos.data_ptr(), L.ptr(seg),
+                                              kl.data_ptr(), valid.data_ptr(), L.ptr(teacher), L.stream_of(iq))
         L.check(rc, "srswa_gather_kl_fwd")
+        if teacher is not None:   # the main tensors are not needed again
+            qm, km = qm.new_empty(0), km.new_empty(0)
+        ctx.teacher = teacher
+        ctx.main_shapes = (g.H, g.Hkv, g.D)
         ctx.save_for_backward(iq, ik, qm, km, sel, pos, seg if seg is not None else pos.new_empty(0))
         ctx.has_seg = seg is not None
         ctx.cfg = (block_size, local_window, scaling, logits_bf16)
@@ -66,35 +76,55 @@ class _GatherKLFn(torch.autograd.Function):
         iq, ik, qm, km, sel, pos, seg = ctx.saved_tensors
         seg = seg if ctx.has_seg else None
         block_size, local_window, scaling, logits_bf16 = ctx.cfg
-        g = _desc(iq, ik, qm, km, sel.shape[-1], block_size, local_window, scaling, logits_bf16)
+        teacher = ctx.teacher
+        if teacher is not None:   # descriptor of the main tensors without them (only their shapes count)
+            H, Hkv, D = ctx.main_shapes
+            B, Cq, _ = iq.shape
+            g = L.KlDesc(B, Cq, ik.shape[1], H, Hkv, D, iq.shape[2], sel.shape[-1], int(block_size),
+                         int(local_window), float(scaling), 1 if logits_bf16 else 0, L.dtype_code(iq),
+                         L.dtype_code(ik), L.dtype_code(iq), L.dtype_code(ik), iq.stride(0), iq.stride(1),
+                         ik.stride(0), ik.stride(1), 0, 0, 0, 0, 0, 0)
+        else:
+            g = _desc(iq, ik, qm, km, sel.shape[-1], block_size, local_window, scaling, logits_bf16)
         lib = L.lib()
         gr = gkl.float().contiguous()
         diq = torch.empty(iq.shape, device=iq.device, dtype=torch.float32)
         dik = torch.empty(ik.shape, device=ik.device, dtype=torch.float32)
         ws_n = lib.srswa_gather_kl_bwd_workspace_size(C.byref(g))
         ws = torch.empty(max(ws_n, 1), device=iq.device, dtype=torch.uint8)
-        rc = lib.srswa_gather_kl_bwd(C.byref(g), iq.data_ptr(), ik.data_ptr(), qm.data_ptr(), km.data_ptr(),
-                                     sel.data_ptr(), pos.data_ptr(), L.ptr(seg), gr.data_ptr(), diq.data_ptr(),
-                                     dik.data_ptr(), ws.data_ptr(), ws_n, L.stream_of(iq))
+        if teacher is not None:
+            rc = lib.srswa_gather_kl_bwd_saved(C.byref(g), iq.data_ptr(), ik.data_ptr(), sel.data_ptr(),
+                                               pos.data_ptr(), L.ptr(seg), teacher.data_ptr(), gr.data_ptr(),
+                                               diq.data_ptr(), dik.data_ptr(), ws.data_ptr(), ws_n,
+                                               L.stream_of(iq))
+            ctx.teacher = None
+        else:
+            rc = lib.srswa_gather_kl_bwd(C.byref(g), iq.data_ptr(), ik.data_ptr(), qm.data_ptr(), km.data_ptr(),
+                                         sel.data_ptr(), pos.data_ptr(), L.ptr(seg), gr.data_ptr(), diq.data_ptr(),
+                                         dik.data_ptr(), ws.data_ptr(), ws_n, L.stream_of(iq))
         L.check(rc, "srswa_gather_kl_bwd")
-        return diq.to(iq.dtype), dik.to(ik.dtype), None, None, None, None, None, None, None, None, None
+        return diq.to(iq.dtype), dik.to(ik.dtype), None, None, None, None, None, None, None, None, None, None
 
 
 def gather_kl(idx_q, idx_k, q_main, k_main, sel, pos, seg=None, *, block_size, local_window, scaling,
-              logits_bf16=None):
+              logits_bf16=None, save_teacher=True):
     """Per-row KL (and row validity) of the DSA distillation.
     idx_q [B,C,d], idx_k [B,Sk,d] (differentiable), q_main [B,C,H,D], k_main
     [B,Sk,Hkv,D] (detached teacher; [B,H,C,D] tensors go in as
     .transpose(1, 2) views), sel [B,C,S] block ids (-1 pad), pos / seg [B,C]
     (global positions, segment starts).  logits_bf16 defaults to the index
-    tensors being bf16 (the reference rounds its matmul outputs to them)."""
+    tensors being bf16 (the reference rounds its matmul outputs to them).
+    save_teacher: keep the rows' averaged teacher probabilities ([B, C, S *
+    block_size] fp32) from the forward for the backward, which then skips
+    the teacher's gather of every head's main keys (same gradients, bit for
+    bit); False recomputes them."""
     if logits_bf16 is None:
         logits_bf16 = idx_q.dtype == torch.bfloat16
     sel32 = sel.to(torch.int32).contiguous()
     pos64 = pos.to(device=idx_q.device, dtype=torch.int64).contiguous()
     seg64 = None if seg is None else seg.to(device=idx_q.device, dtype=torch.int64).contiguous()
     return _GatherKLFn.apply(idx_q, idx_k, q_main.detach(), k_main.detach(), sel32, pos64, seg64, int(block_size),
-                             int(local_window), float(scaling), bool(logits_bf16))
+                             int(local_window), float(scaling), bool(logits_bf16), bool(save_teacher))
 
 
 _ORIGINAL = {}   # indexer class -> the reference's select_and_kl_loss
