@@ -60,6 +60,7 @@ def _inputs(rng, B, T_, H, Hkv, K, scale=0.5):
     (1, 1536, 10, 10, 8, 512, False, True),    # BASELINE head layout
     (1, 2560, 10, 10, 16, 1024, False, True),  # cfg4 selection geometry: K = 16, LW = 1024
     (2, 1100, 4, 4, 16, 1024, True, True),     # K = 16, LW = 1024 with packing and T % 128 != 0
+    (1, 1800, 4, 2, 20, 256, False, True),     # K = 20 slots, GQA, LW = 256
 ])
 def test_tc_forward_vs_oracle(cuda, B, T_, H, Hkv, K, LW, packed, use_bias):
     rng = np.random.default_rng(T_ + K)
