@@ -200,6 +200,47 @@ def test_route_decode_long_vs_oracle(cuda, S_list):
         assert np.array_equal(t32 >= 0, gv) and (t32[gv] <= qb - L).all()
 
 
+def test_route_decode_short_rows_both_paths_vs_oracle(cuda):
+    """Decode rows with fewer than 512 blocks take route_kernel when there are
+    enough of them to give every SM a CTA (600 rows here) and the chunked
+    score + select kernels when there are few (the first 40 rows alone).
+    Both against the oracle on sampled rows, and against each other."""
+    rng = np.random.default_rng(7)
+    BS, L, K, M, d = 64, 8, 8, 16, 128
+    idx_scale, floor, sigma = 11.3, 1e-4, 1.0
+    R, few = 600, 40
+    S_list = rng.integers(1500, 16000, R).tolist()
+    W = max((s + BS - 1) // BS for s in S_list)
+    P = R * W
+    perm = rng.permutation(P).astype(np.int32).reshape(R, W)
+    kbar = rng.standard_normal((P, d)).astype(np.float32) * 0.1
+    idx_q = O.bf16_round(rng.standard_normal((R, d)).astype(np.float32))
+    sl = np.asarray(S_list, np.int32)
+    want = ("topi64", "bias", "valid", "scores")
+    kw = dict(block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=idx_scale, floor=floor, sigma=sigma)
+    r_all = ops.route(T(idx_q, cuda), T(kbar, cuda), seq_lens=T(sl, cuda), block_table=T(perm, cuda),
+                      want=want, **kw)
+    r_few = ops.route(T(idx_q[:few], cuda), T(kbar, cuda), seq_lens=T(sl[:few], cuda),
+                      block_table=T(perm[:few], cuda), want=want, **kw)
+    res = [{k: v.cpu().numpy() for k, v in r.items()} for r in (r_all, r_few)]
+    rows = list(range(0, few, 3)) + list(range(few, R, 37))
+    for i in rows:
+        cv = np.arange(W) < (S_list[i] + BS - 1) // BS
+        ref_sc = O.block_scores_headcls(idx_q[i][None, None], kbar[perm[i]][None], cv[None],
+                                        np.array([[S_list[i] - 1]]), BS, L)[0, 0]
+        topi, bias, valid = O.infer_route_select(ref_sc[None], None, idx_scale, floor, sigma, K, M)
+        for r in res:
+            if i >= len(r["valid"]):
+                continue
+            np.testing.assert_allclose(r["scores"][i], ref_sc, rtol=2e-5, atol=2e-5)
+            assert np.array_equal(r["valid"][i], valid[0])
+            assert ties_only(r["topi64"][i][None], topi, valid, ref_sc[None]) == 0
+            np.testing.assert_allclose(r["bias"][i], bias[0], rtol=1e-5, atol=5e-4)
+    a, b = res
+    assert np.array_equal(a["valid"][:few], b["valid"])
+    assert ties_only(a["topi64"][:few], b["topi64"], b["valid"], a["scores"][:few]) == 0
+
+
 def test_route_decode_cand_mask_vs_oracle(cuda):
     """Chunked decode router with a page-aware candidate mask; rows 1 and 3
     have an empty mask and fall back to every remote block."""

@@ -1519,7 +1519,25 @@ static size_t chunk_workspace(int64_t N, int64_t nblk) {
   return (static_cast<size_t>(N * nblk) * 4 + 255) & ~static_cast<size_t>(255);
 }
 
-static bool use_chunked(const RouteArgs& a) { return !a.from_scores && a.d == 128 && use_wide(a); }
+// Rows per CTA of route_kernel (several short rows share a CTA).
+static int route_rows_per_cta(int64_t nblk) {
+  int rpc = 1;
+  while (rpc < 8 && nblk * rpc * 2 <= 2048) rpc *= 2;
+  return rpc;
+}
+
+// Decode-shaped rows go to the chunked score pass + one-CTA-per-row select
+// when they have many blocks, or when they are too few for route_kernel to
+// give every SM a CTA (e.g. 32 decode rows of 256 blocks would be 8 CTAs of 4
+// rows: 146 us against 25 us for the two chunked kernels).  A function of
+// (N, nblk, d) only, so that srswa_route_workspace_size agrees with it.
+constexpr int64_t kFewRowCtas = 148;
+static bool use_chunked(const RouteArgs& a) {
+  if (a.from_scores || a.d != 128 || a.nblk > kWideMaxBlocks) return false;
+  if (use_wide(a)) return true;
+  const int rpc = route_rows_per_cta(a.nblk);
+  return (a.N + rpc - 1) / rpc < kFewRowCtas;
+}
 
 static int select_wide_launch(RouteArgs a, const float* z, int64_t s_z, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(a.nblk) * 8;
@@ -1567,8 +1585,7 @@ static int route_launch(RouteArgs a, cudaStream_t st, void* ws = nullptr, size_t
   // decode-shaped rows with many candidate blocks -> chunked score + merge
   if (use_chunked(a)) return route_chunk_launch(a, ws, ws_bytes, st);
   if (a.from_scores && use_wide(a)) return select_wide_launch(a, a.scores_in, a.s_sc, st);
-  int rpc = 1;
-  while (rpc < 8 && a.nblk * rpc * 2 <= 2048) rpc *= 2;
+  const int rpc = route_rows_per_cta(a.nblk);
   a.rows_per_cta = rpc;
   const size_t smem = static_cast<size_t>(rpc) * a.nblk * (sizeof(float) + 1);
   if (smem > 227 * 1024) return SRSWA_ETOOLARGE;
