@@ -532,11 +532,12 @@ constexpr int kChunkBlocks = 128;
 // slice are loaded once for all of them (two dependent round trips), then
 // the k_bar loads of one chunk after the other.
 constexpr int kScoreReps = 2;
-__global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const RouteArgs a, float* zout) {
+__global__ void __launch_bounds__(kRouteThreads, 3) route_score_kernel(const RouteArgs a, float* zout,
+                                                                       int64_t row0) {
   pdl_launch_dependents();  // lets the selection kernel launch early
   constexpr int kSpan = kChunkBlocks * kScoreReps;
   __shared__ int32_t bts[kSpan];
-  const int64_t n = blockIdx.y;
+  const int64_t n = row0 + blockIdx.y;  // rows go in launches of at most 65535 (grid.y)
   const int64_t lo = static_cast<int64_t>(blockIdx.x) * kSpan;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t seq = route_row_seq(a, n);
@@ -1570,10 +1571,16 @@ static int route_chunk_launch(RouteArgs a, void* ws, size_t ws_bytes, cudaStream
     z = static_cast<float*>(ws);
   }
   const int64_t nch = (a.nblk + kChunkBlocks * kScoreReps - 1) / (kChunkBlocks * kScoreReps);
-  if (a.N >= 65536) return SRSWA_ETOOLARGE;
-  route_score_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(a.N)), kRouteThreads, 0, st>>>(a, z);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return static_cast<int>(e);
+  // grid.y holds at most 65535 rows: longer row sets (prefill of >= 64k
+  // tokens) take several launches, each complete before the next starts
+  constexpr int64_t kMaxGridY = 65535;
+  for (int64_t r0 = 0; r0 < a.N; r0 += kMaxGridY) {
+    const int64_t nr = a.N - r0 < kMaxGridY ? a.N - r0 : kMaxGridY;
+    route_score_kernel<<<dim3(static_cast<unsigned>(nch), static_cast<unsigned>(nr)), kRouteThreads, 0, st>>>(
+        a, z, r0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
   a.scores_out = nullptr;  // already written
   return select_wide_launch(a, z, a.nblk, st);
 }
