@@ -24,8 +24,19 @@ def _stage0(router):
     return str(getattr(router, "stage0", "head_cls")).lower()
 
 
+_seq_lens_cache = {}
+
+
 def _seq_lens(B, S, dev):
-    return torch.full((B,), S, device=dev, dtype=torch.int32)
+    """[B] int32 tensor of S, read-only: kept per (B, S, device), so that
+    every layer of a forward does not allocate and fill its own."""
+    key = (B, S, dev)
+    t = _seq_lens_cache.get(key)
+    if t is None:
+        if len(_seq_lens_cache) > 64:
+            _seq_lens_cache.clear()
+        t = _seq_lens_cache[key] = torch.full((B,), S, device=dev, dtype=torch.int32)
+    return t
 
 
 @torch.no_grad()
@@ -64,7 +75,7 @@ def route(router, idx_q, idx_k, q_pos, nblk, block_cand, p):
     bs = int(router.block_size)
     if _stage0(router) != "head_cls":
         return _infer_route_select(_block_scores_infer(router, idx_q, idx_k, q_pos, nblk), block_cand, p)
-    kb, _ = ops.kbar_contig(idx_k, router.head_cls.detach(), bs)
+    kb, _ = ops.kbar_contig(idx_k, router.head_cls.detach(), bs, chunk_valid=False)
     if kb.shape[1] < nblk:
         kb = torch.cat([kb, kb.new_zeros(B, nblk - kb.shape[1], d)], 1)
     r = ops.route(idx_q.reshape(B * Lq, d), kb[:, :nblk].contiguous(), block_size=bs,
