@@ -241,6 +241,33 @@ def test_route_decode_short_rows_both_paths_vs_oracle(cuda):
     assert ties_only(a["topi64"][:few], b["topi64"], b["valid"], a["scores"][:few]) == 0
 
 
+def test_route_prefill_tiled_1024_blocks_vs_oracle(cuda):
+    """Prefill rows of one 40000-token sequence (625 blocks): the tiled
+    router's wide instantiation (32 keys per lane, up to 1024 blocks);
+    sampled rows, early and late, against the oracle."""
+    rng = np.random.default_rng(11)
+    BS, L, K, M, d = 64, 8, 8, 16, 128
+    idx_scale, floor, sigma = 11.3, 1e-4, 1.0
+    T_ = 40000
+    nblk = (T_ + BS - 1) // BS
+    kbar = rng.standard_normal((1, nblk, d)).astype(np.float32) * 0.1
+    idx_q = O.bf16_round(rng.standard_normal((T_, d)).astype(np.float32))
+    r = ops.route(T(idx_q, cuda), T(kbar, cuda), block_size=BS, local_blocks=L, topk=K, topm=M,
+                  idx_scale=idx_scale, floor=floor, sigma=sigma, seq_lens=T(np.array([T_], np.int32), cuda),
+                  rows_per_seq=T_, want=("topi64", "bias", "valid", "scores"))
+    rows = [0, 530, 577, 4000, 16383, 31000, 38911, T_ - 1]
+    idx = torch.tensor(rows, device=cuda)
+    got = {k: v[idx].cpu().numpy() for k, v in r.items()}
+    cv = np.ones(nblk, bool)
+    for j, i in enumerate(rows):
+        ref_sc = O.block_scores_headcls(idx_q[i][None, None], kbar[0][None], cv[None], np.array([[i]]), BS, L)[0, 0]
+        np.testing.assert_allclose(got["scores"][j], ref_sc, rtol=2e-5, atol=2e-5)
+        topi, bias, valid = O.infer_route_select(ref_sc[None], None, idx_scale, floor, sigma, K, M)
+        assert np.array_equal(got["valid"][j], valid[0])
+        assert ties_only(got["topi64"][j][None], topi, valid, ref_sc[None]) == 0
+        np.testing.assert_allclose(got["bias"][j], bias[0], rtol=1e-5, atol=5e-4)
+
+
 def test_route_prefill_beyond_65535_rows_vs_oracle(cuda):
     """One 66000-token sequence (1032 blocks, above the tiled prefill
     router's 512): the score pass takes its rows in launches of at most

@@ -1310,7 +1310,7 @@ __global__ void pack_selection_kernel(const void* sel, int is64, int64_t rows, i
 }
 
 // ============================================================================
-// a2 + a4 for prefill rows (many rows of one sequence, up to 512 blocks):
+// a2 + a4 for prefill rows (many rows of one sequence, up to 1024 blocks):
 // route_tile_kernel, one CTA per 32 consecutive rows of one sequence.
 //   scores  k_bar is staged in 64-block chunks in shared memory (rows padded
 //           to 132 floats: the float4 reads of 8 consecutive lanes hit
@@ -1325,7 +1325,7 @@ __global__ void pack_selection_kernel(const void* sel, int is64, int64_t rows, i
 constexpr int kRtRows = 32;
 constexpr int kRtChunk = 64;
 constexpr int kRtLd = 132;
-constexpr int64_t kRtMaxBlocks = 512;
+constexpr int64_t kRtMaxBlocks = 1024;  // [32][1024] fp32 scores + staging: 192 KB of shared memory
 
 static size_t route_tile_smem(int64_t nblk) {
   const size_t ab = static_cast<size_t>(kRtRows + kRtChunk) * kRtLd * 4;   // q tile + k_bar chunk
@@ -1376,6 +1376,10 @@ __device__ __forceinline__ void route_tile_select(const RouteArgs& a, const floa
   }
 }
 
+// NPLMAX: keys per lane of the widest selection compiled in (16: up to 512
+// blocks; 32: up to 1024, a separate instantiation since its registers would
+// halve the CTAs per SM of the narrower cases).
+template <int NPLMAX>
 __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteArgs a) {
   pdl_launch_dependents();
   extern __shared__ __align__(16) float rt_smem[];
@@ -1493,7 +1497,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
   // ---- selection: warp w, rows 4w .. 4w+3; lane holds blocks lane + 32 i ----
   if (nblk <= 128) route_tile_select<4>(a, zs, n0, r0, lane, topm_scratch[warp]);
   else if (nblk <= 256) route_tile_select<8>(a, zs, n0, r0, lane, topm_scratch[warp]);
-  else route_tile_select<kRtMaxBlocks / 32>(a, zs, n0, r0, lane, topm_scratch[warp]);
+  else if (NPLMAX == 16 || nblk <= 512) route_tile_select<16>(a, zs, n0, r0, lane, topm_scratch[warp]);
+  else route_tile_select<NPLMAX>(a, zs, n0, r0, lane, topm_scratch[warp]);
 }
 
 static bool use_tile(const RouteArgs& a) {
@@ -1501,17 +1506,22 @@ static bool use_tile(const RouteArgs& a) {
          a.nblk <= kRtMaxBlocks && a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0;
 }
 
-static int route_tile_launch(const RouteArgs& a, cudaStream_t st) {
+template <int NPLMAX>
+static int route_tile_launch_npl(const RouteArgs& a, cudaStream_t st) {
   const size_t smem = route_tile_smem(a.nblk);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(route_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(route_tile_kernel<NPLMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   const int64_t grid = a.N / kRtRows;
   if (grid >= (1ll << 31)) return SRSWA_ETOOLARGE;
-  route_tile_kernel<<<static_cast<unsigned>(grid), kRouteThreads, smem, st>>>(a);
+  route_tile_kernel<NPLMAX><<<static_cast<unsigned>(grid), kRouteThreads, smem, st>>>(a);
   return srswa_last_launch_status();
+}
+
+static int route_tile_launch(const RouteArgs& a, cudaStream_t st) {
+  return a.nblk <= 512 ? route_tile_launch_npl<16>(a, st) : route_tile_launch_npl<kRtMaxBlocks / 32>(a, st);
 }
 
 static bool use_wide(const RouteArgs& a) { return a.nblk >= 512 && a.nblk <= kWideMaxBlocks; }
