@@ -58,12 +58,14 @@ def parse():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode: skip the cfg2 / cfg4 / cfg5 results that ride along in the line")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx", "pagegate", "rope", "kl"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "train", "route", "longctx", "pagegate", "rope", "kl",
+                                                     "paged-prefill"],
                     help="decode = cfg3 (default, the headline); prefill = cfg2; train = cfg4 fwd+bwd; "
                          "route = the cfg3 router alone (k_bar cache + block table, no KV; for profiling); "
                          "longctx = cfg5 attention share (12 layers, one 1M-token sequence, split-KV); "
                          "pagegate = PageGate candidate masks of a cfg2-shaped prefill; "
-                         "rope = page2d RoPE coordinates + fused rotary of a cfg2-shaped prefill")
+                         "rope = page2d RoPE coordinates + fused rotary of a cfg2-shaped prefill; "
+                         "paged-prefill = SGLang extend: route_prefill_triton + dash_sparse_attn (K8)")
     ap.add_argument("--layers", type=int, default=12, help="longctx: decoder layers")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "p2p-flag", "p2p-launch", "nccl"],
                     help="longctx with N > 1: peer-memory exchange fused into the router / attend / merge "
@@ -1087,6 +1089,70 @@ def longctx_measure(args):
             "clocks": clk}
 
 
+def main_paged_prefill(args):
+    """SGLang serving prefill (extend) through the paged drop-ins:
+    route_prefill_triton (the varlen router over the k_bar page cache) +
+    dash_sparse_attn (K8, the paged prefill attend) for 4 requests that each
+    extend 4096 tokens after cached prefixes of 0, 4096, 16384 and 60000
+    tokens, on a shuffled page pool (BASELINE head layout, K = 8, LW = 512).
+    TFLOP/s counts 4 * D * H flops per attended (row, key) at window +
+    selected keys per row.  One GPU (each rank its own copy under torchrun)."""
+    from srswa import paged
+    world, rank, local = rank_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_dist(dev, world)
+    g = torch.Generator(device=dev).manual_seed(41 + rank)
+    ctx_l, qlen_l = [0, 4096, 16384, 60000], [4096] * 4
+    ctx = torch.tensor(ctx_l, dtype=torch.int32, device=dev)
+    qlen = torch.tensor(qlen_l, dtype=torch.int32, device=dev)
+    seq = ctx + qlen
+    R = len(ctx_l)
+    W = (max(c + q for c, q in zip(ctx_l, qlen_l)) + BS - 1) // BS + 1
+    P = R * W
+    bt = torch.randperm(P, device=dev, generator=g).to(torch.int32).view(R, W)
+    cu = torch.zeros(R + 1, dtype=torch.int32, device=dev)
+    cu[1:] = torch.cumsum(qlen, 0)
+    N = sum(qlen_l)
+    kc = torch.randn(P, BS, HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    vc = torch.randn(P, BS, HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    kbar = torch.randn(P, DI, device=dev, generator=g) * 0.1
+    q = torch.randn(N, H, D, device=dev, generator=g).to(torch.bfloat16)
+    iq = (torch.randn(N, DI, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    row2req = (torch.searchsorted(cu, torch.arange(N, device=dev, dtype=torch.int32), right=True) - 1).to(torch.int32)
+    out_idx = torch.empty(N, K, device=dev, dtype=torch.int32)
+    out_bias = torch.empty(N, K, device=dev)
+    out = torch.empty(N, H, D, device=dev, dtype=torch.bfloat16)
+
+    def step():
+        paged.route_prefill_triton(idx_q=iq, k_bar=kbar, block_table=bt, seq_lens=seq, cu_seqlens_q=cu,
+                                   context_lens=ctx, row2req=row2req, image_allow=None, out_idx=out_idx,
+                                   out_bias=out_bias, max_block=W, block_size=BS, local_blocks=L,
+                                   idx_scale=IDX_SCALE, prior_floor=FLOOR, sigma=SIGMA, topm=M, budget=K)
+        paged.dash_sparse_attn(q, kc, vc, out_idx.unsqueeze(0).expand(HKV, -1, -1),
+                               out_bias.unsqueeze(0).expand(HKV, -1, -1), bt, cu, seq, ctx, max(qlen_l), HKV,
+                               SM_SCALE, out, local_blocks=L, sparse_block_size=BS)
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    clocks = Clocks(local)
+    clocks.start()
+    times, _ = timed_graph(step, args.steps, max(args.warmup, 3), flush, False)
+    clk = clocks.stop()
+    ms = sum(times) / len(times)
+    fl = 4.0 * D * H * N * (L * BS + K * BS)
+    if rank == 0:
+        print(json.dumps({"metric": "SGLang paged prefill (route_prefill_triton + dash_sparse_attn)",
+                          "value": fl * world / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                          "data": "synthetic seeded N(0,1), shuffled page pool",
+                          "config": {"workload": "paged prefill: 4 requests x 4096 new tokens, prefixes "
+                                                 "0 / 4096 / 16384 / 60000", "rows": N, "K": K, "LW": L * BS,
+                                     "l2": "flushed before every timed step"},
+                          "clocks": clk}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.workload == "route":
@@ -1099,6 +1165,8 @@ def main():
         return main_rope(args)
     if args.workload == "kl":
         return main_kl(args)
+    if args.workload == "paged-prefill":
+        return main_paged_prefill(args)
     if args.workload != "decode" and args.impl != "reference":
         return main_dense(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
