@@ -279,6 +279,29 @@ SRSWA_API int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const 
                      int o_dtype, int64_t sob, int64_t sot, int64_t soh, float* lse,
                      void* workspace, size_t workspace_bytes, srswa_stream_t stream);
 
+/* Forward of one sequence (B = 1) over paged K / V, on the tensor cores: the
+ * long requests of the paged prefill attend K8 (whl:sglang/srt/layers/
+ * attention/unlimited_dash_ops/attend_triton.py:88-292, 523-597), same
+ * semantics as srswa_prefill_attend for one request.  k_cache / v_cache
+ * [num_pages, 64, Hkv, 128] bf16, strides in the descriptor's k / v fields
+ * (skb = svb: page, skt = svt: slot, skh = svh: head); key block j is page
+ * pages[j] (pages covers ceil((qoff + T) / 64) blocks); query row t sits at
+ * position qoff + t (a cached prefix of qoff tokens).  q / o [T, HQ, 128]
+ * with the descriptor's sqt / sqh and o's sot / soh (sqb, sob unused).
+ * sel [HI, T, S] int32 packed (srswa_pack_selection), bias [T, S] fp32 or
+ * NULL, lse [T, HQ] (natural log) or NULL.  Slots of the last page past the
+ * sequence's last token are never read.  D = 128, bf16, 64-token pages and
+ * 8-element-aligned strides only: SRSWA_EUNSUPPORTED otherwise (nothing
+ * launched; the row kernel of srswa_prefill_attend takes any shape).
+ * workspace: srswa_gather_fwd_paged_workspace_size(g, qoff) bytes (0: not
+ * a supported shape). */
+SRSWA_API size_t srswa_gather_fwd_paged_workspace_size(const srswa_gather_desc* g, int64_t qoff);
+SRSWA_API int srswa_gather_fwd_paged(const srswa_gather_desc* g, const void* q, const void* k_cache,
+                     const void* v_cache, int64_t num_pages, const int32_t* pages, int64_t qoff,
+                     const int32_t* sel, const float* bias, void* o, int64_t sob, int64_t sot,
+                     int64_t soh, float* lse, void* workspace, size_t workspace_bytes,
+                     srswa_stream_t stream);
+
 /* Backward.  do [B,T,HQ,D] (strides as o), o and lse from the forward.
  * Outputs dq/dk/dv (dtype of q, same strides as q/k/v), d_bias [B,T,S] fp32
  * (required iff bias != NULL; 0 on -1/deduped slots).  Deterministic, no

@@ -148,3 +148,55 @@ def test_paged_prefill_long_prefix_vs_oracle(cuda):
             assert abs(ref[b] - mine[b]) < 1e-4, (n, b)
     ref_o, _ = O.paged_prefill(q, kc, vc, oi[None], ob[None], bt, cu, ctx, 1 / math.sqrt(D), L, BS, rows=rows)
     np.testing.assert_allclose(out.float().cpu().numpy()[rows], ref_o[rows], rtol=1e-2, atol=2e-2)
+
+
+def test_paged_prefill_tensor_core_equals_row_kernel(cuda):
+    """dash_sparse_attn sends requests of at least paged.TC_MIN_ROWS rows
+    through the tensor-core forward over the paged caches (prefixes not a
+    multiple of 64, partial last pages) and shorter ones through the row
+    kernel.  Against the row kernel on every row, within the bf16 bar.  The
+    unused slots of each request's last page hold NaN: neither path may read
+    them."""
+    from srswa import ops
+    rng = np.random.default_rng(5)
+    H = Hkv = 10
+    D, BS, L, K = 128, 64, 8, 8
+    LW = L * BS
+    ctx = [0, 1000, 4133, 0, 50]
+    qlen = [700, 1300, 257, 130, 20]
+    R = len(ctx)
+    seq = [c + n for c, n in zip(ctx, qlen)]
+    W = max((s + BS - 1) // BS for s in seq) + 1
+    P = R * W + 3
+    bt = rng.permutation(P)[:R * W].reshape(R, W).astype(np.int32)
+    cu = np.concatenate([[0], np.cumsum(qlen)]).astype(np.int32)
+    N = int(cu[-1])
+    kc = torch.randn(P, BS, Hkv, D, device=cuda).to(torch.bfloat16)
+    vc = torch.randn(P, BS, Hkv, D, device=cuda).to(torch.bfloat16)
+    for r in range(R):
+        last, used = (seq[r] - 1) // BS, seq[r] % BS
+        if used:
+            kc[int(bt[r, last]), used:] = float("nan")
+            vc[int(bt[r, last]), used:] = float("nan")
+    q = torch.randn(N, H, D, device=cuda).to(torch.bfloat16)
+    sel = np.full((N, K), -1, np.int32)
+    for r in range(R):
+        for i in range(qlen[r]):
+            p = ctx[r] + i
+            nrem = max(p - LW + 1, 0) // BS + 1   # blocks holding remote keys (the last one partly)
+            pick = rng.choice(nrem + 2, size=min(K, nrem + 2), replace=False) - 1   # -1 and one past: unused
+            sel[cu[r] + i, :len(pick)] = pick
+    sel[::7, 1] = sel[::7, 0]                                  # repeats count once
+    bias = (rng.standard_normal((N, K)) * 0.5).astype(np.float32)
+    ti = T(sel, cuda).unsqueeze(0).expand(Hkv, -1, -1)
+    tb = T(bias, cuda).unsqueeze(0).expand(Hkv, -1, -1)
+    out_tc = torch.empty(N, H, D, device=cuda, dtype=torch.bfloat16)
+    paged.dash_sparse_attn(q, kc, vc, ti, tb, T(bt, cuda), T(cu, cuda), T(np.asarray(seq, np.int32), cuda),
+                           T(np.asarray(ctx, np.int32), cuda), max(qlen), Hkv, 1 / math.sqrt(D), out_tc,
+                           local_blocks=L, sparse_block_size=BS)
+    out_row = ops.prefill_attend(q, kc, vc, ti, tb, block_table=T(bt, cuda), cu_seqlens_q=T(cu, cuda),
+                                 prefix_lens=T(np.asarray(ctx, np.int32), cuda), block_size=BS, local_blocks=L,
+                                 sm_scale=1 / math.sqrt(D))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out_tc).all() and torch.isfinite(out_row).all()
+    np.testing.assert_allclose(out_tc.float().cpu().numpy(), out_row.float().cpu().numpy(), rtol=1e-2, atol=2e-2)

@@ -32,6 +32,17 @@ struct TcLayout {
   int64_t max_tiles;  // tiles of partial rows (128 each) per query head of an index head
 };
 
+// Paged K / V for the tensor-core forward (one sequence, B = 1): the caches
+// are [num_pages, 64, Hkv, D] (strides in the gather descriptor's k / v
+// fields), key block j is page pages[j], and query row t sits at position
+// qoff + t.
+struct TcPagedKV {
+  int64_t num_pages;
+  const int32_t* pages;
+  int64_t s_pages;
+  int64_t qoff;
+};
+
 struct AttendArgs {
   const void* q;
   const void* k;

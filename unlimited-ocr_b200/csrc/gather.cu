@@ -376,11 +376,13 @@ static int check_gather_desc(const srswa_gather_desc* g) {
 using namespace srswa;
 
 namespace srswa {
-TcLayout tc_layout(const srswa_gather_desc* g);
+TcLayout tc_layout(const srswa_gather_desc* g, int64_t qoff);
 bool tc_eligible(const srswa_gather_desc* g);
+bool tc_paged_eligible(const srswa_gather_desc* g, int64_t qoff);
 int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const int32_t* sel,
                   const float* bias, const int32_t* seg, void* o, int64_t sob, int64_t sot, int64_t soh, float* lse,
-                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t st);
+                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t st,
+                  const TcPagedKV* pk = nullptr);
 size_t tc_bwd_workspace(const srswa_gather_desc* g, bool with_bias);
 int tc_gather_bwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const void* o,
                   int64_t sob, int64_t sot, int64_t soh, const void* dout, const float* lse, const int32_t* sel,
@@ -426,7 +428,35 @@ static size_t bwd_need(const srswa_gather_desc* g, int64_t sob, int64_t sot, int
 
 extern "C" size_t srswa_gather_fwd_workspace_size(const srswa_gather_desc* g) {
   if (check_gather_desc(g)) return 0;
-  return kStatusBytes + (tc_eligible(g) ? tc_layout(g).total : 0);
+  return kStatusBytes + (tc_eligible(g) ? tc_layout(g, 0).total : 0);
+}
+
+extern "C" size_t srswa_gather_fwd_paged_workspace_size(const srswa_gather_desc* g, int64_t qoff) {
+  if (check_gather_desc(g) || !tc_paged_eligible(g, qoff)) return 0;
+  return kStatusBytes + tc_layout(g, qoff).total;
+}
+
+extern "C" int srswa_gather_fwd_paged(const srswa_gather_desc* g, const void* q, const void* k_cache,
+                                      const void* v_cache, int64_t num_pages, const int32_t* pages, int64_t qoff,
+                                      const int32_t* sel, const float* bias, void* o, int64_t sob, int64_t sot,
+                                      int64_t soh, float* lse, void* workspace, size_t workspace_bytes,
+                                      srswa_stream_t stream) {
+  int rc = check_gather_desc(g);
+  if (rc) return rc;
+  SRSWA_CHECK_ARG(q && k_cache && v_cache && pages && o && num_pages > 0 && (g->S == 0 || sel), SRSWA_EINVAL);
+  SRSWA_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) |
+                    reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(o)) & 15) == 0, SRSWA_EALIGN);
+  // tensor cores only: bf16, D = 128, 64-token pages, one sequence
+  SRSWA_CHECK_ARG(tc_paged_eligible(g, qoff) && ((sob | sot | soh) & 7) == 0, SRSWA_EUNSUPPORTED);
+  if (g->T == 0) return 0;
+  SRSWA_CHECK_ARG(workspace && workspace_bytes >= kStatusBytes + tc_layout(g, qoff).total, SRSWA_EWORKSPACE);
+  int* status = nullptr;
+  rc = take_status(&workspace, &workspace_bytes, &status, reinterpret_cast<cudaStream_t>(stream));
+  if (rc) return rc;
+  TcPagedKV pk = {num_pages, pages, 0, qoff};
+  rc = tc_gather_fwd(g, q, k_cache, v_cache, sel, bias, nullptr, o, sob, sot, soh, lse, workspace, workspace_bytes,
+                     status, reinterpret_cast<cudaStream_t>(stream), &pk);
+  return rc == kTcNoTensorMap ? SRSWA_EUNSUPPORTED : rc;
 }
 
 extern "C" int srswa_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v,

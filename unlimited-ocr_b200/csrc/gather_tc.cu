@@ -85,13 +85,35 @@ struct TcArgs {
   const int32_t* offs;        // first pair of each (b*HI + hi, block)
   int64_t B, T, HQ, Hkv, HI, S, LW, nblk;
   float scale_log2;
+  // paged K / V (forward only): key block j of batch element b is the whole
+  // page kv_pages[b * s_pages + j] of the caches (the tensor maps then span
+  // [pages, 64 slots, Hkv, D]); query row t sits at position t + qoff (a
+  // cached prefix of qoff tokens precedes the rows).  Null / 0: contiguous
+  // [B, T, H, D] keys at the rows' own positions.
+  const int32_t* kv_pages;
+  int64_t s_pages, qoff;
+  int64_t tail_blk, tail_slots;  // paged (B = 1): the last block and its used slots (0: full)
 };
+
+// position of query row t
+__device__ __forceinline__ int64_t qpos(const TcArgs& a, int64_t t) { return t + a.qoff; }
+
+// TMA coordinates (row, batch) of key block blk of batch element b
+__device__ __forceinline__ void kv_coord(const TcArgs& a, int64_t b, int64_t blk, int& row0, int& bb) {
+  if (a.kv_pages) {
+    row0 = 0;
+    bb = a.kv_pages[b * a.s_pages + blk];
+  } else {
+    row0 = static_cast<int>(blk * kBlk);
+    bb = static_cast<int>(b);
+  }
+}
 
 __device__ __forceinline__ int64_t seg_start(const TcArgs& a, int64_t b, int64_t t) {
   return a.seg ? static_cast<int64_t>(a.seg[b * a.T + t]) : 0;
 }
 __device__ __forceinline__ int64_t win_start(const TcArgs& a, int64_t b, int64_t t) {
-  int64_t ls = t - a.LW + 1;
+  int64_t ls = qpos(a, t) - a.LW + 1;
   const int64_t sg = seg_start(a, b, t);
   if (ls < sg) ls = sg;
   return ls < 0 ? 0 : ls;
@@ -102,7 +124,7 @@ __device__ __forceinline__ void remote_range(const TcArgs& a, int64_t b, int64_t
   const int64_t sg = seg_start(a, b, t);
   const int64_t ls = win_start(a, b, t);
   lo = blk * kBlk > sg ? blk * kBlk : sg;
-  hi = min(min((blk + 1) * kBlk, ls), t + 1);
+  hi = min(min((blk + 1) * kBlk, ls), qpos(a, t) + 1);
 }
 
 
@@ -436,10 +458,10 @@ __device__ __forceinline__ WsItem ws_item(const TcArgs& a, int64_t item) {
   w.h = bh % a.HQ;
   w.t0 = tile * kTileM;
   const int64_t tlast = min(a.T, w.t0 + kTileM) - 1;
-  int64_t key_lo = w.t0 - a.LW + 1;
+  int64_t key_lo = qpos(a, w.t0) - a.LW + 1;
   if (key_lo < 0) key_lo = 0;
   w.blo = key_lo / kBlk;
-  w.bhi = tlast / kBlk;
+  w.bhi = qpos(a, tlast) / kBlk;
   w.hk = w.h / (a.HQ / a.Hkv);
   return w;
 }
@@ -615,7 +637,8 @@ __global__ void __launch_bounds__(kMgHeads * 16) merge_partials_kernel(const TcA
 
 __global__ void __launch_bounds__(kWsThreads, 1)
     fwd_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                  const __grid_constant__ CUtensorMap tmv) {
+                  const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmk_tail,
+                  const __grid_constant__ CUtensorMap tmv_tail) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ uint64_t q_full[2], q_empty[2], kv_full[2][2], kv_empty[2][2], s_full[2], p_full[2], o_full[2];
   __shared__ uint64_t drain_bar;
@@ -685,13 +708,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           break;
         }
         if (lane == 0) {  // K and V of the block: four 64 x 64 boxes (rows past T read as zeros)
-          const int row0 = static_cast<int>(cs.j * kBlk), hh = static_cast<int>(w.hk), bb = static_cast<int>(w.b);
+          const int hh = static_cast<int>(w.hk);
+          int row0, bb;
+          kv_coord(a, w.b, cs.j, row0, bb);
+          // paged: the sequence's partial last page goes through maps whose
+          // slot extent ends at the last token, so its unused slots read as
+          // zeros like rows past T of a contiguous tensor
+          const bool tail = a.kv_pages && a.tail_slots > 0 && cs.j == a.tail_blk;
+          const CUtensorMap* mk = tail ? &tmk_tail : &tmk;
+          const CUtensorMap* mv = tail ? &tmv_tail : &tmv;
           const uint32_t dst = kv_s(s, st);
           mbar_arrive_expect_tx(&kv_full[s][st], kWsStage);
-          tma_load_4d(dst, &tmk, 0, row0, hh, bb, &kv_full[s][st]);
-          tma_load_4d(dst + kKVHalf, &tmk, 64, row0, hh, bb, &kv_full[s][st]);
-          tma_load_4d(dst + kKVBytes, &tmv, 0, row0, hh, bb, &kv_full[s][st]);
-          tma_load_4d(dst + kKVBytes + kKVHalf, &tmv, 64, row0, hh, bb, &kv_full[s][st]);
+          tma_load_4d(dst, mk, 0, row0, hh, bb, &kv_full[s][st]);
+          tma_load_4d(dst + kKVHalf, mk, 64, row0, hh, bb, &kv_full[s][st]);
+          tma_load_4d(dst + kKVBytes, mv, 0, row0, hh, bb, &kv_full[s][st]);
+          tma_load_4d(dst + kKVBytes + kKVHalf, mv, 64, row0, hh, bb, &kv_full[s][st]);
         }
         __syncwarp();
         cs.advance(a);
@@ -779,7 +810,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       int klo = 0, khi = 0;  // this row's valid keys of the block, relative
       if (row_ok) {
         klo = clamp_key(ls - k0);
-        khi = clamp_key(t + 1 - k0);
+        khi = clamp_key(qpos(a, t) + 1 - k0);
       }
       const bool full = __all_sync(0xffffffffu, klo == 0 && khi == kBlk);
       const float mraw = block_row_max(sv, klo, khi, full);
@@ -1046,13 +1077,14 @@ __global__ void __launch_bounds__(kRwThreads, 1)
             break;
           }
           if (lane == 0) {  // K and V of the block: four 64 x 64 boxes
-            const int row0 = cs.blk * kBlk;
+            int row0, bb;
+            kv_coord(a, cs.b, cs.blk, row0, bb);
             const uint32_t dst = kv_buf(st);
             mbar_arrive_expect_tx(&kv_full[st], kWsStage);
-            tma_load_4d(dst, &tmk, 0, row0, cs.hk, cs.b, &kv_full[st]);
-            tma_load_4d(dst + kKVHalf, &tmk, 64, row0, cs.hk, cs.b, &kv_full[st]);
-            tma_load_4d(dst + kKVBytes, &tmv, 0, row0, cs.hk, cs.b, &kv_full[st]);
-            tma_load_4d(dst + kKVBytes + kKVHalf, &tmv, 64, row0, cs.hk, cs.b, &kv_full[st]);
+            tma_load_4d(dst, &tmk, 0, row0, cs.hk, bb, &kv_full[st]);
+            tma_load_4d(dst + kKVHalf, &tmk, 64, row0, cs.hk, bb, &kv_full[st]);
+            tma_load_4d(dst + kKVBytes, &tmv, 0, row0, cs.hk, bb, &kv_full[st]);
+            tma_load_4d(dst + kKVBytes + kKVHalf, &tmv, 64, row0, cs.hk, bb, &kv_full[st]);
           }
           __syncwarp();
         }
@@ -2490,9 +2522,9 @@ __global__ void tc_dbias_reduce_kernel(const TcBwdArgs a) {
 
 static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-TcLayout tc_layout(const srswa_gather_desc* g) {
+TcLayout tc_layout(const srswa_gather_desc* g, int64_t qoff) {
   TcLayout L;
-  const int64_t nblk = (g->T + kBlk - 1) / kBlk;
+  const int64_t nblk = (g->T + qoff + kBlk - 1) / kBlk;
   const int64_t nbh = g->B * g->HI * nblk;
   const int64_t nsel = g->B * g->HI * g->T * g->S;
   const int64_t hpi = g->HI > 0 ? g->HQ / g->HI : 1;
@@ -2588,6 +2620,12 @@ bool tc_eligible(const srswa_gather_desc* g) {
          ((g->sqb | g->sqt | g->sqh | g->skb | g->skt | g->skh | g->svb | g->svt | g->svh) & 7) == 0;
 }
 
+// The paged forward: one sequence whose rows follow a prefix of qoff tokens.
+bool tc_paged_eligible(const srswa_gather_desc* g, int64_t qoff) {
+  return tc_eligible(g) && g->B == 1 && qoff >= 0 && (g->T + qoff + kBlk - 1) / kBlk <= kMaxListBlocks &&
+         g->T + qoff < (1ll << 31);
+}
+
 // Launch properties per device: the SM count, and whether the kernels'
 // shared-memory limits have been raised there (a per-context setting).  The
 // only process-wide state of the tensor-core path; filled under a mutex on
@@ -2632,8 +2670,9 @@ static int tc_device_props(bool bwd, int* num_sms) {
 
 int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, const void* v, const int32_t* sel,
                   const float* bias, const int32_t* seg, void* o, int64_t sob, int64_t sot, int64_t soh, float* lse,
-                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t st) {
-  const TcLayout L = tc_layout(g);
+                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t st, const TcPagedKV* pk) {
+  const int64_t qoff = pk ? pk->qoff : 0;
+  const TcLayout L = tc_layout(g, qoff);
   if (!workspace || workspace_bytes < L.total) return SRSWA_EWORKSPACE;
   char* ws = static_cast<char*>(workspace);
   TcArgs a = {};
@@ -2658,8 +2697,15 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   a.prow_cap = L.max_tiles * kTileM;
   a.B = g->B; a.T = g->T; a.HQ = g->HQ; a.Hkv = g->Hkv; a.HI = g->HI; a.S = g->S;
   a.LW = g->local_window > 0 ? g->local_window : kBlk;
-  a.nblk = (g->T + kBlk - 1) / kBlk;
+  a.nblk = (g->T + qoff + kBlk - 1) / kBlk;
   a.scale_log2 = g->scale * kLog2e;
+  if (pk) {
+    a.kv_pages = pk->pages;
+    a.s_pages = pk->s_pages;
+    a.qoff = qoff;
+    a.tail_blk = (qoff + g->T - 1) / kBlk;
+    a.tail_slots = (qoff + g->T) % kBlk;
+  }
   int32_t* count = reinterpret_cast<int32_t*>(ws + L.count);
   int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
   // partial rows and selections are indexed with 32-bit integers
@@ -2670,11 +2716,20 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   if (const int prc = tc_device_props(false, &num_sms)) return prc;
   // the tensor maps of q, k, v and the partial rows; when the driver refuses
   // one, the caller runs the CUDA-core kernels instead (nothing launched yet)
-  alignas(64) CUtensorMap tmq, tmk, tmv, tmp;
+  alignas(64) CUtensorMap tmq, tmk, tmv, tmp, tmk_tail, tmv_tail;
+  // paged caches: [pages, 64 slots, Hkv, D]; the tail maps end the slot
+  // extent at the sequence's last token (its partial last page)
+  const int64_t kv_b = pk ? pk->num_pages : g->B, kv_t = pk ? kBlk : g->T;
   if (!(make_tmap(&tmq, q, g->B, g->T, g->HQ, g->sqb, g->sqt, g->sqh, kTileM) &&
-        make_tmap(&tmk, k, g->B, g->T, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
-        make_tmap(&tmv, v, g->B, g->T, g->Hkv, g->svb, g->svt, g->svh, kBlk) &&
+        make_tmap(&tmk, k, kv_b, kv_t, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
+        make_tmap(&tmv, v, kv_b, kv_t, g->Hkv, g->svb, g->svt, g->svh, kBlk) &&
         make_tmap_rows(&tmp, a.part_o, a.prow_cap, hpi)))
+    return kTcNoTensorMap;
+  tmk_tail = tmk;
+  tmv_tail = tmv;
+  if (pk && a.tail_slots > 0 &&
+      !(make_tmap(&tmk_tail, k, kv_b, a.tail_slots, g->Hkv, g->skb, g->skt, g->skh, kBlk) &&
+        make_tmap(&tmv_tail, v, kv_b, a.tail_slots, g->Hkv, g->svb, g->svt, g->svh, kBlk)))
     return kTcNoTensorMap;
   if (g->S > 0) {
     const int64_t nbh = a.B * a.HI * a.nblk;
@@ -2700,7 +2755,7 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
   }
   const int64_t band_items = g->B * g->HQ * ((g->T + kTileM - 1) / kTileM);
   const unsigned band_grid = static_cast<unsigned>(band_items < num_sms ? band_items : num_sms);
-  fwd_ws_kernel<<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv);
+  fwd_ws_kernel<<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv, tmk_tail, tmv_tail);
   if (a.part_o) {
     SRSWA_CUDA_TRY(cudaGetLastError());
     const int64_t hpc = g->HQ < kMgHeads ? g->HQ : kMgHeads;

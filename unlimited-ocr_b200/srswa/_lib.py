@@ -88,6 +88,9 @@ _SIGS = {
     "srswa_gather_fwd_workspace_size": (C.c_size_t, [C.POINTER(GatherDesc)]),
     "srswa_gather_fwd": (C.c_int, [C.POINTER(GatherDesc), vp, vp, vp, vp, vp, vp, vp, C.c_int, i64, i64,
                                    i64, vp, vp, C.c_size_t, vp]),
+    "srswa_gather_fwd_paged_workspace_size": (C.c_size_t, [C.POINTER(GatherDesc), i64]),
+    "srswa_gather_fwd_paged": (C.c_int, [C.POINTER(GatherDesc), vp, vp, vp, i64, vp, i64, vp, vp, vp, i64, i64,
+                                         i64, vp, vp, C.c_size_t, vp]),
     "srswa_gather_bwd_workspace_size": (C.c_size_t, [C.POINTER(GatherDesc)]),
     "srswa_gather_bwd": (C.c_int, [C.POINTER(GatherDesc), vp, vp, vp, vp, i64, i64, i64, vp, vp, vp, vp,
                                    vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),

@@ -539,6 +539,36 @@ def decode_attend(q, k_cache, v_cache, topk_idx, bias, *, block_size, local_bloc
     return (out, lse_t) if lse else out
 
 
+def gather_fwd_paged(q, k_cache, v_cache, sel, bias, pages, qoff, block_size, scale, local_window, out,
+                     workspace=None):
+    """Tensor-core forward of one sequence over paged K / V: q [T, HQ, D]
+    (its rows at positions qoff .. qoff + T - 1), caches [P, 64, Hkv, D],
+    pages [>= ceil((qoff + T) / 64)] int32 (key block j is page pages[j]),
+    sel [HI, T, S] int32 packed (pack_selection), bias [T, S] fp32 or None,
+    out [T, HQ, D] written in place.  Raises NotImplementedError where the
+    tensor-core path does not apply (shape, dtype, alignment)."""
+    T_, HQ, D = q.shape
+    P, BS, Hkv, _ = k_cache.shape
+    if k_cache.stride() != v_cache.stride():
+        raise NotImplementedError("k and v caches must share strides")
+    HI, S = sel.shape[0], sel.shape[-1]
+    lw = block_size if local_window is None else max(1, int(local_window))
+    g = L.GatherDesc(1, T_, HQ, Hkv, HI, D, S, int(block_size), lw, float(scale), L.dtype_code(q),
+                     0, q.stride(0), q.stride(1), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+                     v_cache.stride(0), v_cache.stride(1), v_cache.stride(2))
+    lib = L.lib()
+    ws_n = lib.srswa_gather_fwd_paged_workspace_size(C.byref(g), int(qoff))
+    if ws_n == 0:
+        raise NotImplementedError("gather_fwd_paged: not a tensor-core shape")
+    ws = _workspace(ws_n, q.device, workspace)
+    rc = lib.srswa_gather_fwd_paged(C.byref(g), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), P,
+                                    pages.data_ptr(), int(qoff), sel.data_ptr(), L.ptr(bias), out.data_ptr(),
+                                    0, out.stride(0), out.stride(1), None, ws.data_ptr(), ws_n, L.stream_of(q))
+    L.check(rc, "srswa_gather_fwd_paged")
+    _after_gather(ws, "srswa_gather_fwd_paged")
+    return out
+
+
 def prefill_attend(q, k_cache, v_cache, topk_idx, bias, *, block_table, cu_seqlens_q, prefix_lens, block_size,
                    local_blocks, sm_scale, out=None, lse=False):
     """Paged varlen prefill attend: q [total_q, H, D]; caches [P, BS, Hkv, D];

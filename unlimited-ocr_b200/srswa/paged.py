@@ -75,9 +75,76 @@ def dash_sparse_attn(q, k_cache, v_cache, topk_idx, blk_bias, block_table, cu_se
     assert k_cache.shape[2] == num_kv_heads
     if blk_bias is not None:
         assert blk_bias.shape == topk_idx.shape and blk_bias.dtype == torch.float32
-    ops.prefill_attend(q, k_cache, v_cache, topk_idx, blk_bias, block_table=block_table,
-                       cu_seqlens_q=cu_seqlens_q, prefix_lens=prefix_lens, block_size=sparse_block_size,
-                       local_blocks=local_blocks, sm_scale=sm_scale, out=output)
+    rest = _tc_prefill(q, k_cache, v_cache, topk_idx, blk_bias, block_table, cu_seqlens_q, prefix_lens, sm_scale,
+                       output, local_blocks, sparse_block_size)
+    if rest is None:  # the tensor-core path does not apply: every row on the row kernel
+        ops.prefill_attend(q, k_cache, v_cache, topk_idx, blk_bias, block_table=block_table,
+                           cu_seqlens_q=cu_seqlens_q, prefix_lens=prefix_lens, block_size=sparse_block_size,
+                           local_blocks=local_blocks, sm_scale=sm_scale, out=output)
+        return
+    for r, a, b, ctx in rest:  # short requests: one row-kernel launch each
+        dev = q.device
+        ops.prefill_attend(q[a:b], k_cache, v_cache, topk_idx[:, a:b], None if blk_bias is None else blk_bias[:, a:b],
+                           block_table=block_table[r:r + 1],
+                           cu_seqlens_q=torch.tensor([0, b - a], dtype=torch.int32, device=dev),
+                           prefix_lens=torch.tensor([ctx], dtype=torch.int32, device=dev),
+                           block_size=sparse_block_size, local_blocks=local_blocks, sm_scale=sm_scale,
+                           out=output[a:b])
+
+
+# Requests with at least this many rows take the tensor-core forward.
+TC_MIN_ROWS = 128
+
+
+def _tc_prefill(q, k_cache, v_cache, topk_idx, blk_bias, block_table, cu_seqlens_q, prefix_lens, sm_scale, output,
+                local_blocks, block_size):
+    """Runs every request of at least TC_MIN_ROWS rows through the
+    tensor-core gather forward over the paged caches (srswa_gather_fwd_paged:
+    one launch sequence per request, its rows after a prefix of
+    prefix_lens[r] tokens) and returns the other requests as (r, first row,
+    end row, prefix); None when the path does not apply to this call (dtype,
+    head dim, 64-token pages, a selection or bias that differs per head, no
+    local window).  Reads cu_seqlens_q and prefix_lens on the host."""
+    if (q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or output.dtype != torch.bfloat16
+            or q.shape[-1] != 128 or block_size != 64 or k_cache.shape[1] != 64 or local_blocks <= 0
+            or k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1 or q.stride(-1) != 1
+            or output.stride(-1) != 1):
+        return None
+    ti = topk_idx.unsqueeze(0) if topk_idx.dim() == 2 else topk_idx
+    if ti.shape[0] > 1 and ti.stride(0) != 0:
+        return None
+    bb = None
+    if blk_bias is not None:
+        bb = blk_bias.unsqueeze(0) if blk_bias.dim() == 2 else blk_bias
+        if bb.shape[0] > 1 and bb.stride(0) != 0:
+            return None
+        bb = bb[0]
+    ti = ti[0]
+    cu = cu_seqlens_q.tolist()
+    ctxs = prefix_lens.tolist()
+    if not any(cu[r + 1] - cu[r] >= TC_MIN_ROWS for r in range(len(ctxs))):
+        return None
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    rest = []
+    for r, ctx in enumerate(ctxs):
+        a, b = cu[r], cu[r + 1]
+        if b - a < TC_MIN_ROWS:
+            if b > a:
+                rest.append((r, a, b, ctx))
+            continue
+        nblk = (ctx + b - a + block_size - 1) // block_size
+        if nblk > bt.shape[1]:  # the block table must cover every key block
+            rest.append((r, a, b, ctx))
+            continue
+        sel = ops.pack_selection(ti[a:b].unsqueeze(0), nblk)
+        bias = None if bb is None else bb[a:b].contiguous()
+        pages = bt[r].contiguous()
+        try:
+            ops.gather_fwd_paged(q[a:b], k_cache, v_cache, sel, bias, pages, ctx, block_size, sm_scale,
+                                 local_blocks * block_size, output[a:b])
+        except NotImplementedError:
+            rest.append((r, a, b, ctx))
+    return rest
 
 
 class KBarCache:
