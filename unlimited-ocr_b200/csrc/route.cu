@@ -1437,7 +1437,10 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
     for (int k8 = 0; k8 < kRtChunk * 32 / kRouteThreads; ++k8) {
       const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
       const int64_t c = cb + j;
-      pf[k8] = c < cmax ? __ldg(reinterpret_cast<const float4*>(a.kbar + seq * a.s_kbar_b + c * a.s_kbar_c + 4 * u))
+      // k_bar row of block c: contiguous per sequence, or a page of the cache
+      const int64_t kb_off = a.block_table ? static_cast<int64_t>(a.block_table[seq * a.s_bt + c]) * a.s_kbar_c
+                                           : seq * a.s_kbar_b + c * a.s_kbar_c;
+      pf[k8] = c < cmax ? __ldg(reinterpret_cast<const float4*>(a.kbar + kb_off + 4 * u))
                         : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
@@ -1501,9 +1504,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
   else route_tile_select<NPLMAX>(a, zs, n0, r0, lane, topm_scratch[warp]);
 }
 
+// Rows of one sequence (at least 32), or of several whose row counts are
+// multiples of 32 (a tile never spans two sequences); k_bar contiguous or
+// paged.
 static bool use_tile(const RouteArgs& a) {
-  return !a.from_scores && a.block_table == nullptr && a.row_seq == nullptr && a.d == 128 &&
-         a.nblk <= kRtMaxBlocks && a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0;
+  return !a.from_scores && a.row_seq == nullptr && a.d == 128 && a.nblk <= kRtMaxBlocks &&
+         ((a.rows_per_seq == a.N && a.N >= kRtRows) || (a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0));
 }
 
 template <int NPLMAX>
@@ -1514,7 +1520,7 @@ static int route_tile_launch_npl(const RouteArgs& a, cudaStream_t st) {
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  const int64_t grid = a.N / kRtRows;
+  const int64_t grid = (a.N + kRtRows - 1) / kRtRows;
   if (grid >= (1ll << 31)) return SRSWA_ETOOLARGE;
   route_tile_kernel<NPLMAX><<<static_cast<unsigned>(grid), kRouteThreads, smem, st>>>(a);
   return srswa_last_launch_status();

@@ -255,6 +255,42 @@ def route_decode_triton(*, idx_q, k_bar, block_table, seq_lens, image_allow, out
                         out_slots=out_slots)
 
 
+# A request with at least this many rows is routed on its own by the tiled
+# router (32 rows share each k_bar chunk), up to this many blocks.
+ROUTE_TILE_MIN_ROWS = 64
+ROUTE_TILE_MAX_BLOCKS = 1024
+
+
+def _route_by_request(idx_q, k_bar, bt, seq_lens, cu_seqlens_q, row2req, q_pos, cand, out_idx, out_bias, kw):
+    """Routes each request of at least ROUTE_TILE_MIN_ROWS rows with its own
+    call (the tiled router; the varlen per-row score pass would read the
+    request's k_bar once per row) and the remaining rows with one varlen
+    call on their gathered rows.  Same results as one varlen call.  Returns
+    False (nothing done) when no request is long enough.  Reads
+    cu_seqlens_q on the host."""
+    cu = cu_seqlens_q.tolist()
+    R = len(cu) - 1
+    long_r = [r for r in range(R) if cu[r + 1] - cu[r] >= ROUTE_TILE_MIN_ROWS]
+    if not long_r:
+        return False
+    dev = idx_q.device
+    sl = seq_lens.to(device=dev, dtype=torch.int32)
+    for r in long_r:
+        a, b = cu[r], cu[r + 1]
+        ops.route(idx_q[a:b], k_bar, seq_lens=sl[r:r + 1], q_pos=q_pos[a:b], rows_per_seq=b - a,
+                  block_table=bt[r:r + 1], cand=None if cand is None else cand[a:b],
+                  out={"topi32": out_idx[a:b], "bias": out_bias[a:b]}, **kw)
+    short = [torch.arange(cu[r], cu[r + 1]) for r in range(R)
+             if 0 < cu[r + 1] - cu[r] < ROUTE_TILE_MIN_ROWS]
+    if short:
+        idx = torch.cat(short).to(dev)
+        res = ops.route(idx_q[idx], k_bar, seq_lens=sl, q_pos=q_pos[idx], row_seq=row2req[idx], block_table=bt,
+                        cand=None if cand is None else cand[idx], **kw)
+        out_idx.index_copy_(0, idx, res["topi32"])
+        out_bias.index_copy_(0, idx, res["bias"])
+    return True
+
+
 @torch.no_grad()
 def route_prefill_triton(*, idx_q, k_bar, block_table, seq_lens, cu_seqlens_q, context_lens, row2req, image_allow,
                          out_idx, out_bias, max_block: int, block_size: int, local_blocks: int, idx_scale: float,
@@ -263,8 +299,10 @@ def route_prefill_triton(*, idx_q, k_bar, block_table, seq_lens, cu_seqlens_q, c
     """Route varlen prefill rows idx_q [total_q, d]: row i of request
     r = row2req[i] sits at position context_lens[r] + i - cu_seqlens_q[r].
     Writes out_idx / out_bias like route_decode; returns (slot width, None,
-    0): all rows are routed in one launch (no q_chunk loop, so no last score
-    chunk to hand back)."""
+    0): no q_chunk loop, so no last score chunk to hand back.  Requests of
+    at least ROUTE_TILE_MIN_ROWS rows are routed one by one by the tiled
+    router (up to ROUTE_TILE_MAX_BLOCKS blocks), the other rows in one
+    varlen launch."""
     del q_chunk, score_buf
     dev = idx_q.device
     N = int(idx_q.shape[0])
@@ -280,6 +318,12 @@ def route_prefill_triton(*, idx_q, k_bar, block_table, seq_lens, cu_seqlens_q, c
              - cu_seqlens_q.to(device=dev, dtype=torch.int64)[r])
     direct = (out_idx.dtype == torch.int32 and out_bias.dtype == torch.float32 and out_idx.is_contiguous()
               and out_bias.is_contiguous() and tuple(out_idx.shape) == (N, Ke) and tuple(out_bias.shape) == (N, Ke))
+    kw = dict(block_size=block_size, local_blocks=local_blocks, topk=K, topm=topm, idx_scale=idx_scale,
+              floor=prior_floor, sigma=sigma, want=("topi32", "bias"), nblk=W)
+    if direct and W <= ROUTE_TILE_MAX_BLOCKS and _route_by_request(idx_q, k_bar, block_table[:, :W], seq_lens,
+                                                                   cu_seqlens_q, row2req, q_pos, image_allow,
+                                                                   out_idx, out_bias, kw):
+        return width, None, 0
     res = ops.route(idx_q, k_bar, block_size=block_size, local_blocks=local_blocks, topk=K, topm=topm,
                     idx_scale=idx_scale, floor=prior_floor, sigma=sigma, seq_lens=seq_lens, q_pos=q_pos,
                     row_seq=row2req, block_table=block_table[:, :W], cand=image_allow, want=("topi32", "bias"),
