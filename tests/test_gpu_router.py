@@ -268,6 +268,42 @@ def test_route_prefill_tiled_1024_blocks_vs_oracle(cuda):
         np.testing.assert_allclose(got["bias"][j], bias[0], rtol=1e-5, atol=5e-4)
 
 
+def test_route_prefill_long_rows_tiled_vs_oracle(cuda):
+    """One 90000-token sequence (1407 blocks, past the one-pass tiled
+    router's 1024): the long-row tiled router (512-block spans merged into a
+    running top-M), contiguous k_bar, sampled rows against the oracle; then
+    the same rows over a shuffled paged k_bar, which must give the same
+    outputs bit for bit."""
+    rng = np.random.default_rng(13)
+    BS, L, K, M, d = 64, 8, 8, 16, 128
+    idx_scale, floor, sigma = 11.3, 1e-4, 1.0
+    T_ = 90000
+    nblk = (T_ + BS - 1) // BS
+    kbar = rng.standard_normal((1, nblk, d)).astype(np.float32) * 0.1
+    idx_q = O.bf16_round(rng.standard_normal((T_, d)).astype(np.float32))
+    kw = dict(block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=idx_scale, floor=floor, sigma=sigma,
+              want=("topi64", "bias", "valid"))
+    sl = T(np.array([T_], np.int32), cuda)
+    r = ops.route(T(idx_q, cuda), T(kbar, cuda), seq_lens=sl, rows_per_seq=T_, **kw)
+    rows = [0, 520, 535, 600, 33000, 32767, 65600, 77777, T_ - 1]
+    idx = torch.tensor(rows, device=cuda)
+    got = {k: v[idx].cpu().numpy() for k, v in r.items()}
+    cv = np.ones(nblk, bool)
+    for j, i in enumerate(rows):
+        ref_sc = O.block_scores_headcls(idx_q[i][None, None], kbar[0][None], cv[None], np.array([[i]]), BS, L)[0, 0]
+        topi, bias, valid = O.infer_route_select(ref_sc[None], None, idx_scale, floor, sigma, K, M)
+        assert np.array_equal(got["valid"][j], valid[0])
+        assert ties_only(got["topi64"][j][None], topi, valid, ref_sc[None]) == 0
+        np.testing.assert_allclose(got["bias"][j], bias[0], rtol=1e-5, atol=5e-4)
+    perm = rng.permutation(nblk + 5)[:nblk].astype(np.int32)
+    pool = np.zeros((nblk + 5, d), np.float32)
+    pool[perm] = kbar[0]
+    rp = ops.route(T(idx_q, cuda), T(pool, cuda), seq_lens=sl, rows_per_seq=T_, block_table=T(perm[None], cuda),
+                   **kw)
+    for k in r:
+        assert torch.equal(r[k], rp[k]), k
+
+
 def test_route_prefill_beyond_65535_rows_vs_oracle(cuda):
     """One 66000-token sequence (1032 blocks, above the tiled prefill
     router's 512): the score pass takes its rows in launches of at most

@@ -1438,10 +1438,14 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
       const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
       const int64_t c = cb + j;
       // k_bar row of block c: contiguous per sequence, or a page of the cache
-      const int64_t kb_off = a.block_table ? static_cast<int64_t>(a.block_table[seq * a.s_bt + c]) * a.s_kbar_c
-                                           : seq * a.s_kbar_b + c * a.s_kbar_c;
-      pf[k8] = c < cmax ? __ldg(reinterpret_cast<const float4*>(a.kbar + kb_off + 4 * u))
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      // (the block table is read for remote blocks only: c < cmax <= nblk)
+      pf[k8] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < cmax) {
+        const int64_t kb_off = a.block_table
+                                   ? static_cast<int64_t>(a.block_table[seq * a.s_bt + c]) * a.s_kbar_c
+                                   : seq * a.s_kbar_b + c * a.s_kbar_c;
+        pf[k8] = __ldg(reinterpret_cast<const float4*>(a.kbar + kb_off + 4 * u));
+      }
     }
   };
   if (cmax > 0) load_chunk(0);
@@ -1512,6 +1516,197 @@ static bool use_tile(const RouteArgs& a) {
          ((a.rows_per_seq == a.N && a.N >= kRtRows) || (a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0));
 }
 
+// ----------------------------------------------------------------------------
+// route_tile_long_kernel: prefill rows of one sequence with more than 1024
+// blocks (long contexts).  As route_tile_kernel, 32 rows per CTA share each
+// staged 64-block k_bar chunk; the blocks go in 512-block spans: each span's
+// scores sit in shared memory, each row's top-M of the span (warp top-M) is
+// merged into the row's running top-M (a 64-key bitonic sort of the two
+// sorted lists) and the entmax / top-K / bias epilogue runs once at the end.
+// The top-M of a union is the top-M of the spans' top-Ms, so the selection
+// equals the one-pass kernels'.  Spans past every row's remote range are
+// skipped: their blocks rank below the first span's (sentinel x, larger
+// index).  No candidate mask and no scores output in this form.
+// ----------------------------------------------------------------------------
+constexpr int kRlSpan = 512;
+
+static size_t route_tile_long_smem() {
+  return static_cast<size_t>(kRtRows + kRtChunk) * kRtLd * 4 + static_cast<size_t>(kRtRows) * kRlSpan * 4;
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const RouteArgs a) {
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) float rt_smem[];
+  const int64_t nblk = a.nblk;
+  float* qs = rt_smem;                     // [32][132]
+  float* kb = qs + kRtRows * kRtLd;        // [64][132]
+  float* zs = kb + kRtChunk * kRtLd;       // [32][512]: one span's scores
+  __shared__ int64_t chi[kRtRows];
+  __shared__ int64_t cmax_s;
+  __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
+  __shared__ unsigned long long best[kRtRows][kMaxTopM];  // running top-M per row, descending
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int M = static_cast<int>(a.M);
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kRtRows;
+  const int64_t seq = n0 / a.rows_per_seq;  // all 32 rows share it
+  if (tid < kRtRows) {
+    const int64_t n = n0 + tid;
+    int64_t c_hi = 0;
+    if (n < a.N) {
+      const int64_t p = a.q_pos ? a.q_pos[n]
+                                : static_cast<int64_t>(a.seq_lens[seq]) - a.rows_per_seq + n % a.rows_per_seq;
+      c_hi = p >= 0 ? p / a.BS - a.L + 1 : 0;
+      if (c_hi < 0) c_hi = 0;
+      if (c_hi > nblk) c_hi = nblk;
+      if (a.seq_lens) {
+        const int64_t nb = (static_cast<int64_t>(a.seq_lens[seq]) + a.BS - 1) / a.BS;
+        if (c_hi > nb) c_hi = nb;
+      }
+    }
+    chi[tid] = c_hi;
+    int64_t m = c_hi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int64_t y = __shfl_xor_sync(0xffffffffu, m, o);
+      m = y > m ? y : m;
+    }
+    if (tid == 0) cmax_s = m;
+  }
+  for (int i = tid; i < kRtRows * kMaxTopM; i += kRouteThreads) best[i / kMaxTopM][i % kMaxTopM] = 0ull;
+  for (int i = tid; i < kRtRows * 32; i += kRouteThreads) {
+    const int r = i >> 5, u = i & 31;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (n0 + r < a.N) load4(a.q, (n0 + r) * a.s_q + 4 * u, a.q_dtype, v);
+    *reinterpret_cast<float4*>(qs + r * kRtLd + 4 * u) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+  __syncthreads();
+  const int64_t cmax = cmax_s;
+  const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
+  const int r0 = warp * 4;
+  float4 pf[kRtChunk * 32 / kRouteThreads];
+  auto load_chunk = [&](int64_t cb) {
+#pragma unroll
+    for (int k8 = 0; k8 < kRtChunk * 32 / kRouteThreads; ++k8) {
+      const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
+      const int64_t c = cb + j;
+      pf[k8] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < cmax) {  // the block table is read for remote blocks only
+        const int64_t kb_off = a.block_table
+                                   ? static_cast<int64_t>(a.block_table[seq * a.s_bt + c]) * a.s_kbar_c
+                                   : seq * a.s_kbar_b + c * a.s_kbar_c;
+        pf[k8] = __ldg(reinterpret_cast<const float4*>(a.kbar + kb_off + 4 * u));
+      }
+    }
+  };
+  // spans [s0, s0 + 512): at least the first (fillers of rows with fewer
+  // than M remote blocks), then those holding remote blocks of some row
+  const int64_t s_end = cmax > kRlSpan ? cmax : kRlSpan;
+  if (cmax > 0) load_chunk(0);
+  for (int64_t s0 = 0; s0 < s_end && s0 < nblk; s0 += kRlSpan) {
+    const int64_t s1 = min(s0 + kRlSpan, nblk);
+    for (int64_t c0 = s0; c0 < s1; c0 += kRtChunk) {
+      if (c0 >= cmax) {  // no row has remote blocks here: sentinel scores only
+        for (int i = tid; i < kRtRows * kRtChunk; i += kRouteThreads) {
+          const int r = i / kRtChunk;
+          const int64_t c = c0 + i % kRtChunk;
+          if (c < s1) zs[r * kRlSpan + (c - s0)] = kScoreNeg;
+        }
+        continue;
+      }
+#pragma unroll
+      for (int k8 = 0; k8 < kRtChunk * 32 / kRouteThreads; ++k8) {
+        const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
+        *reinterpret_cast<float4*>(kb + j * kRtLd + 4 * u) = pf[k8];
+      }
+      __syncthreads();
+      if (c0 + kRtChunk < cmax) load_chunk(c0 + kRtChunk);
+      float acc[4][2];
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) acc[rr][0] = acc[rr][1] = 0.f;
+#pragma unroll 4
+      for (int d4 = 0; d4 < 32; ++d4) {
+        const float4 k0v = *reinterpret_cast<const float4*>(kb + lane * kRtLd + 4 * d4);
+        const float4 k1v = *reinterpret_cast<const float4*>(kb + (lane + 32) * kRtLd + 4 * d4);
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          const float4 qv = *reinterpret_cast<const float4*>(qs + (r0 + rr) * kRtLd + 4 * d4);
+          acc[rr][0] = fmaf(qv.x, k0v.x, acc[rr][0]);
+          acc[rr][0] = fmaf(qv.y, k0v.y, acc[rr][0]);
+          acc[rr][0] = fmaf(qv.z, k0v.z, acc[rr][0]);
+          acc[rr][0] = fmaf(qv.w, k0v.w, acc[rr][0]);
+          acc[rr][1] = fmaf(qv.x, k1v.x, acc[rr][1]);
+          acc[rr][1] = fmaf(qv.y, k1v.y, acc[rr][1]);
+          acc[rr][1] = fmaf(qv.z, k1v.z, acc[rr][1]);
+          acc[rr][1] = fmaf(qv.w, k1v.w, acc[rr][1]);
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+        const int r = r0 + rr;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int64_t c = c0 + lane + 32 * h;
+          if (c >= s1) continue;
+          const float sdot = acc[rr][h];
+          float z = fminf(fmaxf(sdot * inv_sqrt_d, -kActClamp), kActClamp);
+          if (sdot != sdot) z = sdot;
+          zs[r * kRlSpan + (c - s0)] = c < chi[r] ? z : kScoreNeg;
+        }
+      }
+      __syncthreads();  // k_bar chunk reuse
+    }
+    __syncthreads();
+    // this span's top-M of each of the warp's rows, merged into the running list
+    for (int rr = 0; rr < 4; ++rr) {
+      const int r = r0 + rr;
+      if (n0 + r >= a.N) break;  // warp-uniform
+      unsigned long long v[kRlSpan / 32];
+#pragma unroll
+      for (int k = 0; k < kRlSpan / 32; ++k) {
+        const int64_t c = s0 + lane + 32 * k;
+        v[k] = 0ull;
+        if (c < s1) {
+          const float zc = zs[r * kRlSpan + (c - s0)];
+          const bool cm = zc > kScoreNeg * 0.5f;  // NaN -> not remote
+          float x = cm ? zc * a.idx_scale : kEntmaxNeg;
+          if (!isfinite(x)) x = kEntmaxNeg;
+          v[k] = pack_key(x, c, cm);
+        }
+      }
+      const unsigned long long top = warp_topm_filtered<kRlSpan / 32>(v, M, lane, topm_scratch[warp]);
+      unsigned long long e0 = lane < M ? best[r][lane] : 0ull;
+      unsigned long long e1 = lane < M ? top : 0ull;
+      bitonic64_desc(e0, e1, lane);
+      __syncwarp();
+      if (lane < M) best[r][lane] = e0;
+      __syncwarp();
+    }
+    __syncthreads();  // zs reuse
+  }
+  for (int rr = 0; rr < 4; ++rr) {
+    const int r = r0 + rr;
+    const int64_t n = n0 + r;
+    if (n >= a.N) break;  // warp-uniform
+    float sel_v = 0.f;
+    int sel_i = -1;
+    bool sel_c = false;
+    if (lane < M) unpack_key(best[r][lane], sel_v, sel_i, sel_c);
+    route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
+    __syncwarp();
+  }
+}
+
+static int route_tile_long_launch(const RouteArgs& a, cudaStream_t st) {
+  const size_t smem = route_tile_long_smem();
+  cudaError_t e = cudaFuncSetAttribute(route_tile_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const int64_t grid = (a.N + kRtRows - 1) / kRtRows;
+  if (grid >= (1ll << 31)) return SRSWA_ETOOLARGE;
+  route_tile_long_kernel<<<static_cast<unsigned>(grid), kRouteThreads, smem, st>>>(a);
+  return srswa_last_launch_status();
+}
+
 template <int NPLMAX>
 static int route_tile_launch_npl(const RouteArgs& a, cudaStream_t st) {
   const size_t smem = route_tile_smem(a.nblk);
@@ -1524,6 +1719,13 @@ static int route_tile_launch_npl(const RouteArgs& a, cudaStream_t st) {
   if (grid >= (1ll << 31)) return SRSWA_ETOOLARGE;
   route_tile_kernel<NPLMAX><<<static_cast<unsigned>(grid), kRouteThreads, smem, st>>>(a);
   return srswa_last_launch_status();
+}
+
+// Long rows of one sequence (> 1024 blocks), no candidate mask, no scores out.
+static bool use_tile_long(const RouteArgs& a) {
+  return !a.from_scores && a.row_seq == nullptr && a.d == 128 && a.nblk > kRtMaxBlocks && a.cand == nullptr &&
+         a.scores_out == nullptr &&
+         ((a.rows_per_seq == a.N && a.N >= kRtRows) || (a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0));
 }
 
 static int route_tile_launch(const RouteArgs& a, cudaStream_t st) {
@@ -1605,6 +1807,7 @@ static int route_launch(RouteArgs a, cudaStream_t st, void* ws = nullptr, size_t
   if (a.N == 0) return 0;
   // prefill rows: many rows of one sequence sharing a contiguous k_bar
   if (use_tile(a)) return route_tile_launch(a, st);
+  if (use_tile_long(a)) return route_tile_long_launch(a, st);
   // decode-shaped rows with many candidate blocks -> chunked score + merge
   if (use_chunked(a)) return route_chunk_launch(a, ws, ws_bytes, st);
   if (a.from_scores && use_wide(a)) return select_wide_launch(a, a.scores_in, a.s_sc, st);
