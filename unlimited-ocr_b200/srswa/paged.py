@@ -104,7 +104,10 @@ def _tc_prefill(q, k_cache, v_cache, topk_idx, blk_bias, block_table, cu_seqlens
     prefix_lens[r] tokens) and returns the other requests as (r, first row,
     end row, prefix); None when the path does not apply to this call (dtype,
     head dim, 64-token pages, a selection or bias that differs per head, no
-    local window).  Reads cu_seqlens_q and prefix_lens on the host."""
+    local window, or inside a CUDA graph capture).  Reads cu_seqlens_q and
+    prefix_lens on the host."""
+    if torch.cuda.is_current_stream_capturing():  # no host reads inside a CUDA graph capture
+        return None
     if (q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or output.dtype != torch.bfloat16
             or q.shape[-1] != 128 or block_size != 64 or k_cache.shape[1] != 64 or local_blocks <= 0
             or k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1 or q.stride(-1) != 1
@@ -267,8 +270,10 @@ def _route_by_request(idx_q, k_bar, bt, seq_lens, cu_seqlens_q, row2req, q_pos, 
     call (the tiled router; the varlen per-row score pass would read the
     request's k_bar once per row) and the remaining rows with one varlen
     call on their gathered rows.  Same results as one varlen call.  Returns
-    False (nothing done) when no request is long enough.  Reads
-    cu_seqlens_q on the host."""
+    False (nothing done) when no request is long enough or a CUDA graph is
+    being captured.  Reads cu_seqlens_q on the host."""
+    if torch.cuda.is_current_stream_capturing():  # no host reads inside a CUDA graph capture
+        return False
     cu = cu_seqlens_q.tolist()
     R = len(cu) - 1
     long_r = [r for r in range(R) if cu[r + 1] - cu[r] >= ROUTE_TILE_MIN_ROWS]
