@@ -98,9 +98,11 @@ struct TcArgs {
 // position of query row t
 __device__ __forceinline__ int64_t qpos(const TcArgs& a, int64_t t) { return t + a.qoff; }
 
-// TMA coordinates (row, batch) of key block blk of batch element b
+// TMA coordinates (row, batch) of key block blk of batch element b; kPaged:
+// the forward kernels' paged instantiation (a.kv_pages set)
+template <bool kPaged>
 __device__ __forceinline__ void kv_coord(const TcArgs& a, int64_t b, int64_t blk, int& row0, int& bb) {
-  if (a.kv_pages) {
+  if constexpr (kPaged) {
     row0 = 0;
     bb = a.kv_pages[b * a.s_pages + blk];
   } else {
@@ -635,6 +637,7 @@ __global__ void __launch_bounds__(kMgHeads * 16) merge_partials_kernel(const TcA
   if (f8 == 0) *lse_p = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
 }
 
+template <bool kPaged>
 __global__ void __launch_bounds__(kWsThreads, 1)
     fwd_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmk_tail,
@@ -710,13 +713,19 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (lane == 0) {  // K and V of the block: four 64 x 64 boxes (rows past T read as zeros)
           const int hh = static_cast<int>(w.hk);
           int row0, bb;
-          kv_coord(a, w.b, cs.j, row0, bb);
+          kv_coord<kPaged>(a, w.b, cs.j, row0, bb);
           // paged: the sequence's partial last page goes through maps whose
           // slot extent ends at the last token, so its unused slots read as
           // zeros like rows past T of a contiguous tensor
-          const bool tail = a.kv_pages && a.tail_slots > 0 && cs.j == a.tail_blk;
-          const CUtensorMap* mk = tail ? &tmk_tail : &tmk;
-          const CUtensorMap* mv = tail ? &tmv_tail : &tmv;
+          const bool tail = kPaged && a.tail_slots > 0 && cs.j == a.tail_blk;
+          const CUtensorMap* mk = &tmk;
+          const CUtensorMap* mv = &tmv;
+          if constexpr (kPaged) {
+            if (tail) {
+              mk = &tmk_tail;
+              mv = &tmv_tail;
+            }
+          }
           const uint32_t dst = kv_s(s, st);
           mbar_arrive_expect_tx(&kv_full[s][st], kWsStage);
           tma_load_4d(dst, mk, 0, row0, hh, bb, &kv_full[s][st]);
@@ -974,6 +983,7 @@ __device__ __forceinline__ void store_o_chunk(uint32_t addr, const float* v, flo
                : "memory");
 }
 
+template <bool kPaged>
 __global__ void __launch_bounds__(kRwThreads, 1)
     remote_ws_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                      const __grid_constant__ CUtensorMap tmp) {
@@ -1078,7 +1088,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
           }
           if (lane == 0) {  // K and V of the block: four 64 x 64 boxes
             int row0, bb;
-            kv_coord(a, cs.b, cs.blk, row0, bb);
+            kv_coord<kPaged>(a, cs.b, cs.blk, row0, bb);
             const uint32_t dst = kv_buf(st);
             mbar_arrive_expect_tx(&kv_full[st], kWsStage);
             tma_load_4d(dst, &tmk, 0, row0, cs.hk, bb, &kv_full[st]);
@@ -2650,8 +2660,13 @@ static int tc_device_props(bool bwd, int* num_sms) {
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   if (!bwd && !p.fwd_ready) {
-    e = cudaFuncSetAttribute(remote_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmem);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
+    e = cudaFuncSetAttribute(remote_ws_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(remote_ws_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fwd_ws_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fwd_ws_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     p.fwd_ready = true;
   }
@@ -2748,14 +2763,20 @@ int tc_gather_fwd(const srswa_gather_desc* g, const void* q, const void* k, cons
     SRSWA_CUDA_TRY(cudaGetLastError());
     pairs_fill_kernel<<<lgrid, kListRows, static_cast<size_t>(a.nblk) * 8, st>>>(a, cursor);
     SRSWA_CUDA_TRY(cudaGetLastError());
-    remote_ws_kernel<<<num_sms, kRwThreads, kRwSmem, st>>>(a, tmk, tmv, tmp);
+    if (pk)
+      remote_ws_kernel<true><<<num_sms, kRwThreads, kRwSmem, st>>>(a, tmk, tmv, tmp);
+    else
+      remote_ws_kernel<false><<<num_sms, kRwThreads, kRwSmem, st>>>(a, tmk, tmv, tmp);
     SRSWA_CUDA_TRY(cudaGetLastError());
   } else {
     a.part_o = nullptr;
   }
   const int64_t band_items = g->B * g->HQ * ((g->T + kTileM - 1) / kTileM);
   const unsigned band_grid = static_cast<unsigned>(band_items < num_sms ? band_items : num_sms);
-  fwd_ws_kernel<<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv, tmk_tail, tmv_tail);
+  if (pk)
+    fwd_ws_kernel<true><<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv, tmk_tail, tmv_tail);
+  else
+    fwd_ws_kernel<false><<<band_grid, kWsThreads, kWsSmem, st>>>(a, tmq, tmk, tmv, tmk_tail, tmv_tail);
   if (a.part_o) {
     SRSWA_CUDA_TRY(cudaGetLastError());
     const int64_t hpc = g->HQ < kMgHeads ? g->HQ : kMgHeads;
