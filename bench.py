@@ -1094,7 +1094,8 @@ def main_paged_prefill(args):
     route_prefill_triton (the varlen router over the k_bar page cache) +
     dash_sparse_attn (K8, the paged prefill attend) for 4 requests that each
     extend 4096 tokens after cached prefixes of 0, 4096, 16384 and 60000
-    tokens, on a shuffled page pool (BASELINE head layout, K = 8, LW = 512).
+    tokens, on a shuffled page pool (BASELINE head layout, K = 8, LW = 512);
+    with --seq S one request extends 8192 rows after an S-token prefix.
     TFLOP/s counts 4 * D * H flops per attended (row, key) at window +
     selected keys per row.  One GPU (each rank its own copy under torchrun)."""
     from srswa import paged
@@ -1103,7 +1104,8 @@ def main_paged_prefill(args):
     torch.cuda.set_device(dev)
     init_dist(dev, world)
     g = torch.Generator(device=dev).manual_seed(41 + rank)
-    ctx_l, qlen_l = [0, 4096, 16384, 60000], [4096] * 4
+    # --seq S: one request extending 8192 rows after an S-token prefix instead
+    ctx_l, qlen_l = ([args.seq], [8192]) if args.seq else ([0, 4096, 16384, 60000], [4096] * 4)
     ctx = torch.tensor(ctx_l, dtype=torch.int32, device=dev)
     qlen = torch.tensor(qlen_l, dtype=torch.int32, device=dev)
     seq = ctx + qlen
@@ -1146,8 +1148,10 @@ def main_paged_prefill(args):
                           "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
                           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                           "data": "synthetic seeded N(0,1), shuffled page pool",
-                          "config": {"workload": "paged prefill: 4 requests x 4096 new tokens, prefixes "
-                                                 "0 / 4096 / 16384 / 60000", "rows": N, "K": K, "LW": L * BS,
+                          "config": {"workload": (f"paged prefill: 1 request x 8192 new tokens after {args.seq}"
+                                                  if args.seq else "paged prefill: 4 requests x 4096 new tokens, "
+                                                  "prefixes 0 / 4096 / 16384 / 60000"),
+                                     "rows": N, "K": K, "LW": L * BS,
                                      "l2": "flushed before every timed step"},
                           "clocks": clk}), flush=True)
     return 0
