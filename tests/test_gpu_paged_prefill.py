@@ -162,8 +162,8 @@ def test_paged_prefill_tensor_core_equals_row_kernel(cuda):
     H = Hkv = 10
     D, BS, L, K = 128, 64, 8, 8
     LW = L * BS
-    ctx = [0, 1000, 4133, 0, 50]
-    qlen = [700, 1300, 257, 130, 20]
+    ctx = [0, 1000, 4133, 0, 50, 640]
+    qlen = [700, 1300, 257, 130, 20, 384]   # the last ends on a page boundary (no partial page)
     R = len(ctx)
     seq = [c + n for c, n in zip(ctx, qlen)]
     W = max((s + BS - 1) // BS for s in seq) + 1
