@@ -1327,10 +1327,11 @@ constexpr int kRtChunk = 64;
 constexpr int kRtLd = 132;
 constexpr int64_t kRtMaxBlocks = 1024;  // [32][1024] fp32 scores + staging: 192 KB of shared memory
 
-static size_t route_tile_smem(int64_t nblk) {
+static size_t route_tile_smem(int64_t nblk, bool paged) {
   const size_t ab = static_cast<size_t>(kRtRows + kRtChunk) * kRtLd * 4;   // q tile + k_bar chunk
   const size_t keys = static_cast<size_t>(8) * nblk * 8;                   // per-warp keys (aliases ab)
-  return (ab > keys ? ab : keys) + static_cast<size_t>(kRtRows) * nblk * 4;  // + scores
+  return (ab > keys ? ab : keys) + static_cast<size_t>(kRtRows) * nblk * 4 +  // + scores
+         (paged ? static_cast<size_t>(nblk) * 4 : 0);                        // + block table
 }
 
 // Selection of route_tile_kernel for the 4 rows of one warp (NPL keys per
@@ -1389,6 +1390,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
   const size_t ab = static_cast<size_t>(kRtRows + kRtChunk) * kRtLd;
   const size_t kw = static_cast<size_t>(8) * nblk * 2;
   float* zs = rt_smem + (ab > kw ? ab : kw);  // [32][nblk]
+  int32_t* bts = reinterpret_cast<int32_t*>(zs + kRtRows * nblk);  // [nblk] block table (paged k_bar)
   __shared__ int64_t chi[kRtRows];
   __shared__ int64_t cmax_s;
   __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
@@ -1427,6 +1429,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
   }
   __syncthreads();
   const int64_t cmax = cmax_s;
+  // paged k_bar: the sequence's block-table entries of the remote range,
+  // staged once (the chunk loads then take one dependent round trip, not two)
+  if (a.block_table) {
+    for (int64_t c = tid; c < cmax; c += kRouteThreads) bts[c] = a.block_table[seq * a.s_bt + c];
+    __syncthreads();
+  }
   const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
   const int r0 = warp * 4;
   // k_bar chunks: this thread's 8 float4 of the next chunk are loaded into
@@ -1441,9 +1449,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_kernel(const RouteAr
       // (the block table is read for remote blocks only: c < cmax <= nblk)
       pf[k8] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (c < cmax) {
-        const int64_t kb_off = a.block_table
-                                   ? static_cast<int64_t>(a.block_table[seq * a.s_bt + c]) * a.s_kbar_c
-                                   : seq * a.s_kbar_b + c * a.s_kbar_c;
+        const int64_t kb_off = a.block_table ? static_cast<int64_t>(bts[c]) * a.s_kbar_c
+                                             : seq * a.s_kbar_b + c * a.s_kbar_c;
         pf[k8] = __ldg(reinterpret_cast<const float4*>(a.kbar + kb_off + 4 * u));
       }
     }
@@ -1530,9 +1537,12 @@ static bool use_tile(const RouteArgs& a) {
 // ----------------------------------------------------------------------------
 constexpr int kRlSpan = 512;
 
-static size_t route_tile_long_smem() {
-  return static_cast<size_t>(kRtRows + kRtChunk) * kRtLd * 4 + static_cast<size_t>(kRtRows) * kRlSpan * 4;
+static size_t route_tile_long_smem(int64_t nblk, bool paged) {
+  return static_cast<size_t>(kRtRows + kRtChunk) * kRtLd * 4 + static_cast<size_t>(kRtRows) * kRlSpan * 4 +
+         (paged ? static_cast<size_t>(nblk) * 4 : 0);
 }
+// paged long rows: the staged block table bounds the block count (64 KB)
+constexpr int64_t kRlMaxPagedBlocks = 16384;
 
 __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const RouteArgs a) {
   pdl_launch_dependents();
@@ -1541,6 +1551,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
   float* qs = rt_smem;                     // [32][132]
   float* kb = qs + kRtRows * kRtLd;        // [64][132]
   float* zs = kb + kRtChunk * kRtLd;       // [32][512]: one span's scores
+  int32_t* bts = reinterpret_cast<int32_t*>(zs + kRtRows * kRlSpan);  // [nblk] block table (paged k_bar)
   __shared__ int64_t chi[kRtRows];
   __shared__ int64_t cmax_s;
   __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
@@ -1581,6 +1592,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
   }
   __syncthreads();
   const int64_t cmax = cmax_s;
+  // paged k_bar: the sequence's block-table entries of the remote range,
+  // staged once (the chunk loads then take one dependent round trip, not two)
+  if (a.block_table) {
+    for (int64_t c = tid; c < cmax; c += kRouteThreads) bts[c] = a.block_table[seq * a.s_bt + c];
+    __syncthreads();
+  }
   const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
   const int r0 = warp * 4;
   float4 pf[kRtChunk * 32 / kRouteThreads];
@@ -1590,10 +1607,9 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
       const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
       const int64_t c = cb + j;
       pf[k8] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c < cmax) {  // the block table is read for remote blocks only
-        const int64_t kb_off = a.block_table
-                                   ? static_cast<int64_t>(a.block_table[seq * a.s_bt + c]) * a.s_kbar_c
-                                   : seq * a.s_kbar_b + c * a.s_kbar_c;
+      if (c < cmax) {
+        const int64_t kb_off = a.block_table ? static_cast<int64_t>(bts[c]) * a.s_kbar_c
+                                             : seq * a.s_kbar_b + c * a.s_kbar_c;
         pf[k8] = __ldg(reinterpret_cast<const float4*>(a.kbar + kb_off + 4 * u));
       }
     }
@@ -1697,7 +1713,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
 }
 
 static int route_tile_long_launch(const RouteArgs& a, cudaStream_t st) {
-  const size_t smem = route_tile_long_smem();
+  const size_t smem = route_tile_long_smem(a.nblk, a.block_table != nullptr);
   cudaError_t e = cudaFuncSetAttribute(route_tile_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -1709,7 +1725,7 @@ static int route_tile_long_launch(const RouteArgs& a, cudaStream_t st) {
 
 template <int NPLMAX>
 static int route_tile_launch_npl(const RouteArgs& a, cudaStream_t st) {
-  const size_t smem = route_tile_smem(a.nblk);
+  const size_t smem = route_tile_smem(a.nblk, a.block_table != nullptr);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(route_tile_kernel<NPLMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
@@ -1724,7 +1740,7 @@ static int route_tile_launch_npl(const RouteArgs& a, cudaStream_t st) {
 // Long rows of one sequence (> 1024 blocks), no candidate mask, no scores out.
 static bool use_tile_long(const RouteArgs& a) {
   return !a.from_scores && a.row_seq == nullptr && a.d == 128 && a.nblk > kRtMaxBlocks && a.cand == nullptr &&
-         a.scores_out == nullptr &&
+         a.scores_out == nullptr && (a.block_table == nullptr || a.nblk <= kRlMaxPagedBlocks) &&
          ((a.rows_per_seq == a.N && a.N >= kRtRows) || (a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0));
 }
 
