@@ -1536,21 +1536,22 @@ static bool use_tile(const RouteArgs& a) {
 // index).  No candidate mask and no scores output in this form.
 // ----------------------------------------------------------------------------
 constexpr int kRlSpan = 512;
+constexpr int kRlChunk = 128;  // k_bar blocks staged at a time
 
 static size_t route_tile_long_smem(int64_t nblk, bool paged) {
-  return static_cast<size_t>(kRtRows + kRtChunk) * kRtLd * 4 + static_cast<size_t>(kRtRows) * kRlSpan * 4 +
+  return static_cast<size_t>(kRtRows + kRlChunk) * kRtLd * 4 + static_cast<size_t>(kRtRows) * kRlSpan * 4 +
          (paged ? static_cast<size_t>(nblk) * 4 : 0);
 }
-// paged long rows: the staged block table bounds the block count (64 KB)
-constexpr int64_t kRlMaxPagedBlocks = 16384;
+// paged long rows: the staged block table bounds the block count (48 KB)
+constexpr int64_t kRlMaxPagedBlocks = 12288;
 
 __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const RouteArgs a) {
   pdl_launch_dependents();
   extern __shared__ __align__(16) float rt_smem[];
   const int64_t nblk = a.nblk;
   float* qs = rt_smem;                     // [32][132]
-  float* kb = qs + kRtRows * kRtLd;        // [64][132]
-  float* zs = kb + kRtChunk * kRtLd;       // [32][512]: one span's scores
+  float* kb = qs + kRtRows * kRtLd;        // [128][132]
+  float* zs = kb + kRlChunk * kRtLd;       // [32][512]: one span's scores
   int32_t* bts = reinterpret_cast<int32_t*>(zs + kRtRows * kRlSpan);  // [nblk] block table (paged k_bar)
   __shared__ int64_t chi[kRtRows];
   __shared__ int64_t cmax_s;
@@ -1599,11 +1600,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
     __syncthreads();
   }
   const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(a.d));
-  const int r0 = warp * 4;
-  float4 pf[kRtChunk * 32 / kRouteThreads];
+  const int r0 = warp * 4;                 // selection: rows 4w .. 4w + 3
+  const int rg = (warp & 3) * 8, bh = (warp >> 2) * 64;  // scores: rows rg .. rg + 7, blocks bh + lane (+32)
+  float4 pf[kRlChunk * 32 / kRouteThreads];
   auto load_chunk = [&](int64_t cb) {
 #pragma unroll
-    for (int k8 = 0; k8 < kRtChunk * 32 / kRouteThreads; ++k8) {
+    for (int k8 = 0; k8 < kRlChunk * 32 / kRouteThreads; ++k8) {
       const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
       const int64_t c = cb + j;
       pf[k8] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1620,32 +1622,33 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
   if (cmax > 0) load_chunk(0);
   for (int64_t s0 = 0; s0 < s_end && s0 < nblk; s0 += kRlSpan) {
     const int64_t s1 = min(s0 + kRlSpan, nblk);
-    for (int64_t c0 = s0; c0 < s1; c0 += kRtChunk) {
+    for (int64_t c0 = s0; c0 < s1; c0 += kRlChunk) {
       if (c0 >= cmax) {  // no row has remote blocks here: sentinel scores only
-        for (int i = tid; i < kRtRows * kRtChunk; i += kRouteThreads) {
-          const int r = i / kRtChunk;
-          const int64_t c = c0 + i % kRtChunk;
+        for (int i = tid; i < kRtRows * kRlChunk; i += kRouteThreads) {
+          const int r = i / kRlChunk;
+          const int64_t c = c0 + i % kRlChunk;
           if (c < s1) zs[r * kRlSpan + (c - s0)] = kScoreNeg;
         }
         continue;
       }
 #pragma unroll
-      for (int k8 = 0; k8 < kRtChunk * 32 / kRouteThreads; ++k8) {
+      for (int k8 = 0; k8 < kRlChunk * 32 / kRouteThreads; ++k8) {
         const int i = tid + k8 * kRouteThreads, j = i >> 5, u = i & 31;
         *reinterpret_cast<float4*>(kb + j * kRtLd + 4 * u) = pf[k8];
       }
       __syncthreads();
-      if (c0 + kRtChunk < cmax) load_chunk(c0 + kRtChunk);
-      float acc[4][2];
+      if (c0 + kRlChunk < cmax) load_chunk(c0 + kRlChunk);
+      // thread: 8 rows x 2 blocks (two k_bar reads per 8 broadcast q reads)
+      float acc[8][2];
 #pragma unroll
-      for (int rr = 0; rr < 4; ++rr) acc[rr][0] = acc[rr][1] = 0.f;
-#pragma unroll 4
+      for (int rr = 0; rr < 8; ++rr) acc[rr][0] = acc[rr][1] = 0.f;
+#pragma unroll 2
       for (int d4 = 0; d4 < 32; ++d4) {
-        const float4 k0v = *reinterpret_cast<const float4*>(kb + lane * kRtLd + 4 * d4);
-        const float4 k1v = *reinterpret_cast<const float4*>(kb + (lane + 32) * kRtLd + 4 * d4);
+        const float4 k0v = *reinterpret_cast<const float4*>(kb + (bh + lane) * kRtLd + 4 * d4);
+        const float4 k1v = *reinterpret_cast<const float4*>(kb + (bh + lane + 32) * kRtLd + 4 * d4);
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-          const float4 qv = *reinterpret_cast<const float4*>(qs + (r0 + rr) * kRtLd + 4 * d4);
+        for (int rr = 0; rr < 8; ++rr) {
+          const float4 qv = *reinterpret_cast<const float4*>(qs + (rg + rr) * kRtLd + 4 * d4);
           acc[rr][0] = fmaf(qv.x, k0v.x, acc[rr][0]);
           acc[rr][0] = fmaf(qv.y, k0v.y, acc[rr][0]);
           acc[rr][0] = fmaf(qv.z, k0v.z, acc[rr][0]);
@@ -1657,11 +1660,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
         }
       }
 #pragma unroll
-      for (int rr = 0; rr < 4; ++rr) {
-        const int r = r0 + rr;
+      for (int rr = 0; rr < 8; ++rr) {
+        const int r = rg + rr;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int64_t c = c0 + lane + 32 * h;
+          const int64_t c = c0 + bh + lane + 32 * h;
           if (c >= s1) continue;
           const float sdot = acc[rr][h];
           float z = fminf(fmaxf(sdot * inv_sqrt_d, -kActClamp), kActClamp);
