@@ -302,6 +302,20 @@ def test_route_prefill_long_rows_tiled_vs_oracle(cuda):
                    **kw)
     for k in r:
         assert torch.equal(r[k], rp[k]), k
+    # a candidate mask (PageGate): ~20 % of the blocks; rows 520 and 65600
+    # have none among their remote blocks and fall back to all of them
+    cand = torch.rand(T_, nblk, device=cuda) < 0.2
+    cand[520] = False
+    cand[65600] = False
+    rc = ops.route(T(idx_q, cuda), T(kbar, cuda), seq_lens=sl, rows_per_seq=T_, cand=cand, **kw)
+    got = {k: v[idx].cpu().numpy() for k, v in rc.items()}
+    cm = cand[idx].cpu().numpy()
+    for j, i in enumerate(rows):
+        ref_sc = O.block_scores_headcls(idx_q[i][None, None], kbar[0][None], cv[None], np.array([[i]]), BS, L)[0, 0]
+        topi, bias, valid = O.infer_route_select(ref_sc[None], cm[j][None], idx_scale, floor, sigma, K, M)
+        assert np.array_equal(got["valid"][j], valid[0]), i
+        assert ties_only(got["topi64"][j][None], topi, valid, ref_sc[None]) == 0, i
+        np.testing.assert_allclose(got["bias"][j], bias[0], rtol=1e-5, atol=5e-4)
 
 
 def test_route_prefill_beyond_65535_rows_vs_oracle(cuda):

@@ -1533,7 +1533,9 @@ static bool use_tile(const RouteArgs& a) {
 // The top-M of a union is the top-M of the spans' top-Ms, so the selection
 // equals the one-pass kernels'.  Spans past every row's remote range are
 // skipped: their blocks rank below the first span's (sentinel x, larger
-// index).  No candidate mask and no scores output in this form.
+// index).  A candidate mask keeps a second running list over every remote
+// block, taken for a row none of whose remote blocks is a candidate (the
+// reference's fallback).  No scores output in this form.
 // ----------------------------------------------------------------------------
 constexpr int kRlSpan = 512;
 constexpr int kRlChunk = 128;  // k_bar blocks staged at a time
@@ -1557,6 +1559,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
   __shared__ int64_t cmax_s;
   __shared__ unsigned long long topm_scratch[kRouteThreads / 32][64];
   __shared__ unsigned long long best[kRtRows][kMaxTopM];  // running top-M per row, descending
+  __shared__ unsigned long long best_all[kRtRows][kMaxTopM];  // the same over every remote block (masks)
+  __shared__ int found_s[kRtRows];                            // a candidate among the row's remote blocks
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int M = static_cast<int>(a.M);
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kRtRows;
@@ -1584,7 +1588,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
     }
     if (tid == 0) cmax_s = m;
   }
-  for (int i = tid; i < kRtRows * kMaxTopM; i += kRouteThreads) best[i / kMaxTopM][i % kMaxTopM] = 0ull;
+  for (int i = tid; i < kRtRows * kMaxTopM; i += kRouteThreads) {
+    best[i / kMaxTopM][i % kMaxTopM] = 0ull;
+    best_all[i / kMaxTopM][i % kMaxTopM] = 0ull;
+  }
+  if (tid < kRtRows) found_s[tid] = 0;
   for (int i = tid; i < kRtRows * 32; i += kRouteThreads) {
     const int r = i >> 5, u = i & 31;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1675,30 +1683,41 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
       __syncthreads();  // k_bar chunk reuse
     }
     __syncthreads();
-    // this span's top-M of each of the warp's rows, merged into the running list
+    // this span's top-M of each of the warp's rows, merged into the running
+    // list; with a candidate mask also the list of every remote block (the
+    // fallback of a row whose candidate set turns out empty)
     for (int rr = 0; rr < 4; ++rr) {
       const int r = r0 + rr;
-      if (n0 + r >= a.N) break;  // warp-uniform
-      unsigned long long v[kRlSpan / 32];
+      const int64_t n = n0 + r;
+      if (n >= a.N) break;  // warp-uniform
+      for (int pass = 0; pass < (a.cand ? 2 : 1); ++pass) {
+        const bool masked = a.cand && pass == 0;
+        unsigned long long v[kRlSpan / 32];
+        int f = 0;
 #pragma unroll
-      for (int k = 0; k < kRlSpan / 32; ++k) {
-        const int64_t c = s0 + lane + 32 * k;
-        v[k] = 0ull;
-        if (c < s1) {
-          const float zc = zs[r * kRlSpan + (c - s0)];
-          const bool cm = zc > kScoreNeg * 0.5f;  // NaN -> not remote
-          float x = cm ? zc * a.idx_scale : kEntmaxNeg;
-          if (!isfinite(x)) x = kEntmaxNeg;
-          v[k] = pack_key(x, c, cm);
+        for (int k = 0; k < kRlSpan / 32; ++k) {
+          const int64_t c = s0 + lane + 32 * k;
+          v[k] = 0ull;
+          if (c < s1) {
+            const float zc = zs[r * kRlSpan + (c - s0)];
+            const bool remote = zc > kScoreNeg * 0.5f;  // NaN -> not remote
+            const bool cm = remote && (!masked || a.cand[n * a.s_cand + c] != 0);
+            f |= masked && cm;
+            float x = cm ? zc * a.idx_scale : kEntmaxNeg;
+            if (!isfinite(x)) x = kEntmaxNeg;
+            v[k] = pack_key(x, c, cm);
+          }
         }
+        if (masked && __any_sync(0xffffffffu, f) && lane == 0) found_s[r] = 1;
+        unsigned long long (*lst)[kMaxTopM] = pass == 0 ? best : best_all;
+        const unsigned long long top = warp_topm_filtered<kRlSpan / 32>(v, M, lane, topm_scratch[warp]);
+        unsigned long long e0 = lane < M ? lst[r][lane] : 0ull;
+        unsigned long long e1 = lane < M ? top : 0ull;
+        bitonic64_desc(e0, e1, lane);
+        __syncwarp();
+        if (lane < M) lst[r][lane] = e0;
+        __syncwarp();
       }
-      const unsigned long long top = warp_topm_filtered<kRlSpan / 32>(v, M, lane, topm_scratch[warp]);
-      unsigned long long e0 = lane < M ? best[r][lane] : 0ull;
-      unsigned long long e1 = lane < M ? top : 0ull;
-      bitonic64_desc(e0, e1, lane);
-      __syncwarp();
-      if (lane < M) best[r][lane] = e0;
-      __syncwarp();
     }
     __syncthreads();  // zs reuse
   }
@@ -1709,7 +1728,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_tile_long_kernel(const Ro
     float sel_v = 0.f;
     int sel_i = -1;
     bool sel_c = false;
-    if (lane < M) unpack_key(best[r][lane], sel_v, sel_i, sel_c);
+    const bool fallback = a.cand && !found_s[r];  // no candidate among the remote blocks
+    if (lane < M) unpack_key(fallback ? best_all[r][lane] : best[r][lane], sel_v, sel_i, sel_c);
     route_epilogue(a, n, lane, sel_v, sel_i, sel_c);
     __syncwarp();
   }
@@ -1740,10 +1760,9 @@ static int route_tile_launch_npl(const RouteArgs& a, cudaStream_t st) {
   return srswa_last_launch_status();
 }
 
-// Long rows of one sequence (> 1024 blocks), no candidate mask, no scores out.
+// Long rows of one sequence (> 1024 blocks), no scores output.
 static bool use_tile_long(const RouteArgs& a) {
-  return !a.from_scores && a.row_seq == nullptr && a.d == 128 && a.nblk > kRtMaxBlocks && a.cand == nullptr &&
-         a.scores_out == nullptr && (a.block_table == nullptr || a.nblk <= kRlMaxPagedBlocks) &&
+  return !a.from_scores && a.row_seq == nullptr && a.d == 128 && a.nblk > kRtMaxBlocks && a.scores_out == nullptr && (a.block_table == nullptr || a.nblk <= kRlMaxPagedBlocks) &&
          ((a.rows_per_seq == a.N && a.N >= kRtRows) || (a.rows_per_seq % kRtRows == 0 && a.N % kRtRows == 0));
 }
 

@@ -259,10 +259,9 @@ def route_decode_triton(*, idx_q, k_bar, block_table, seq_lens, image_allow, out
 
 
 # A request with at least this many rows is routed on its own by the tiled
-# router (32 rows share each k_bar chunk): up to this many blocks with a
-# candidate mask, any number without one (the long-row tiled router).
+# routers (32 rows share each k_bar chunk; past 12288 blocks of a paged
+# k_bar the library takes its per-row pass for such a call).
 ROUTE_TILE_MIN_ROWS = 64
-ROUTE_TILE_MAX_BLOCKS = 1024
 
 
 def _route_by_request(idx_q, k_bar, bt, seq_lens, cu_seqlens_q, row2req, q_pos, cand, out_idx, out_bias, kw):
@@ -307,8 +306,7 @@ def route_prefill_triton(*, idx_q, k_bar, block_table, seq_lens, cu_seqlens_q, c
     Writes out_idx / out_bias like route_decode; returns (slot width, None,
     0): no q_chunk loop, so no last score chunk to hand back.  Requests of
     at least ROUTE_TILE_MIN_ROWS rows are routed one by one by the tiled
-    routers (up to ROUTE_TILE_MAX_BLOCKS blocks with image_allow, any count
-    without), the other rows in one varlen launch."""
+    routers, the other rows in one varlen launch."""
     del q_chunk, score_buf
     dev = idx_q.device
     N = int(idx_q.shape[0])
@@ -326,7 +324,7 @@ def route_prefill_triton(*, idx_q, k_bar, block_table, seq_lens, cu_seqlens_q, c
               and out_bias.is_contiguous() and tuple(out_idx.shape) == (N, Ke) and tuple(out_bias.shape) == (N, Ke))
     kw = dict(block_size=block_size, local_blocks=local_blocks, topk=K, topm=topm, idx_scale=idx_scale,
               floor=prior_floor, sigma=sigma, want=("topi32", "bias"), nblk=W)
-    if direct and (W <= ROUTE_TILE_MAX_BLOCKS or image_allow is None) and _route_by_request(idx_q, k_bar, block_table[:, :W], seq_lens,
+    if direct and _route_by_request(idx_q, k_bar, block_table[:, :W], seq_lens,
                                                                    cu_seqlens_q, row2req, q_pos, image_allow,
                                                                    out_idx, out_bias, kw):
         return width, None, 0
