@@ -318,6 +318,36 @@ def test_route_prefill_long_rows_tiled_vs_oracle(cuda):
         np.testing.assert_allclose(got["bias"][j], bias[0], rtol=1e-5, atol=5e-4)
 
 
+def test_route_prefill_ragged_batch_per_sequence(cuda):
+    """Three sequences of 3000 rows (not a multiple of the 32-row tile): the
+    tiled router runs once per sequence; against the same rows routed one
+    sequence per call, bit for bit, and sampled rows against the oracle."""
+    rng = np.random.default_rng(17)
+    BS, L, K, M, d = 64, 8, 8, 16, 128
+    idx_scale, floor, sigma = 11.3, 1e-4, 1.0
+    B, T_ = 3, 3000
+    nblk = (T_ + BS - 1) // BS
+    kbar = rng.standard_normal((B, nblk, d)).astype(np.float32) * 0.1
+    idx_q = O.bf16_round(rng.standard_normal((B * T_, d)).astype(np.float32))
+    kw = dict(block_size=BS, local_blocks=L, topk=K, topm=M, idx_scale=idx_scale, floor=floor, sigma=sigma,
+              want=("topi64", "bias", "valid", "scores"))
+    sl = T(np.full(B, T_, np.int32), cuda)
+    r = ops.route(T(idx_q, cuda), T(kbar, cuda), seq_lens=sl, rows_per_seq=T_, **kw)
+    for b in range(B):
+        rb = ops.route(T(idx_q[b * T_:(b + 1) * T_], cuda), T(kbar[b:b + 1], cuda), seq_lens=sl[b:b + 1],
+                       rows_per_seq=T_, **kw)
+        for k in rb:
+            assert torch.equal(r[k][b * T_:(b + 1) * T_], rb[k]), (b, k)
+    cv = np.ones(nblk, bool)
+    for i in [0, 700, 2999, 3000, 4500, 8999]:
+        b, t = divmod(i, T_)
+        ref_sc = O.block_scores_headcls(idx_q[i][None, None], kbar[b][None], cv[None], np.array([[t]]), BS, L)[0, 0]
+        np.testing.assert_allclose(r["scores"][i].cpu().numpy(), ref_sc, rtol=2e-5, atol=2e-5)
+        topi, bias, valid = O.infer_route_select(ref_sc[None], None, idx_scale, floor, sigma, K, M)
+        assert np.array_equal(r["valid"][i].cpu().numpy(), valid[0])
+        assert ties_only(r["topi64"][i].cpu().numpy()[None], topi, valid, ref_sc[None]) == 0
+
+
 def test_route_prefill_beyond_65535_rows_vs_oracle(cuda):
     """One 66000-token sequence (1032 blocks, above the tiled prefill
     router's 512): the score pass takes its rows in launches of at most

@@ -1841,11 +1841,48 @@ static int route_chunk_launch(RouteArgs a, void* ws, size_t ws_bytes, cudaStream
   return select_wide_launch(a, z, a.nblk, st);
 }
 
+// The rows of sequence b as a call of their own (one sequence, its rows
+// first): pointers advanced past the earlier sequences' rows.
+static RouteArgs route_seq_args(const RouteArgs& a, int64_t b) {
+  RouteArgs s = a;
+  const int64_t r0 = b * a.rows_per_seq;
+  s.N = a.rows_per_seq;  // callers: N a multiple of rows_per_seq
+  s.rows_per_seq = s.N;
+  const int64_t esz = a.q_dtype == SRSWA_F32 ? 4 : 2;
+  s.q = static_cast<const char*>(a.q) + r0 * a.s_q * esz;
+  if (a.q_pos) s.q_pos = a.q_pos + r0;
+  if (a.seq_lens) s.seq_lens = a.seq_lens + b;
+  if (a.block_table) s.block_table = a.block_table + b * a.s_bt;
+  else s.kbar = a.kbar + b * a.s_kbar_b;
+  if (a.cand) s.cand = a.cand + r0 * a.s_cand;
+  if (a.topi64) s.topi64 = a.topi64 + r0 * a.K;
+  if (a.topi32) s.topi32 = a.topi32 + r0 * a.K;
+  if (a.bias) s.bias = a.bias + r0 * a.K;
+  if (a.valid) s.valid = a.valid + r0 * a.K;
+  if (a.scores_out) s.scores_out = a.scores_out + r0 * a.nblk;
+  return s;
+}
+
 static int route_launch(RouteArgs a, cudaStream_t st, void* ws = nullptr, size_t ws_bytes = 0) {
   if (a.N == 0) return 0;
   // prefill rows: many rows of one sequence sharing a contiguous k_bar
   if (use_tile(a)) return route_tile_launch(a, st);
   if (use_tile_long(a)) return route_tile_long_launch(a, st);
+  // several sequences whose row count is not a multiple of the 32-row tile
+  // (a tile would span two of them): the tiled routers once per sequence
+  constexpr int64_t kMaxSeqLaunches = 64;
+  if (!a.from_scores && a.row_seq == nullptr && a.rows_per_seq < a.N && a.rows_per_seq >= 4 * kRtRows &&
+      a.N % a.rows_per_seq == 0 && a.N / a.rows_per_seq <= kMaxSeqLaunches) {
+    const RouteArgs s0 = route_seq_args(a, 0);
+    if (use_tile(s0) || use_tile_long(s0)) {
+      for (int64_t b = 0; b < a.N / a.rows_per_seq; ++b) {
+        const RouteArgs sb = route_seq_args(a, b);
+        const int rc = use_tile(sb) ? route_tile_launch(sb, st) : route_tile_long_launch(sb, st);
+        if (rc) return rc;
+      }
+      return 0;
+    }
+  }
   // decode-shaped rows with many candidate blocks -> chunked score + merge
   if (use_chunked(a)) return route_chunk_launch(a, ws, ws_bytes, st);
   if (a.from_scores && use_wide(a)) return select_wide_launch(a, a.scores_in, a.s_sc, st);
