@@ -137,7 +137,11 @@ typedef struct {
  * topi32 (-1 on invalid slots: the serving layout), bias (0 on invalid),
  * valid (uint8); scores [N, nblk] fp32 (the _block_scores_infer output).
  * workspace: caller scratch of srswa_route_workspace_size(N, nblk, params,
- * cand != NULL) bytes (0 for small rows; ~N*nblk/8 bytes for decode rows).
+ * cand != NULL) bytes: N*nblk*4 (one fp32 score per row and block) where the
+ * rows may take the chunked score pass (>= 512 blocks, or too few rows to
+ * give the row-packed kernel a CTA per SM), else 0.  Rows of one sequence
+ * (prefill) take the tiled routers whenever they apply and then leave the
+ * workspace unused.
  * Replaces _block_scores_infer + _infer_route_select (modeling_deepseekv2.py:339-430)
  * and route_decode_triton / route_prefill_triton
  * (whl:.../unlimited_dash_ops/route_triton.py:624-680, 729-847). */
