@@ -166,12 +166,21 @@ def route(idx_q, kbar, *, block_size, local_blocks, topk, topm, idx_scale, floor
     p = _route_params(block_size, local_blocks, topk, topm, idx_scale, floor, sigma)
     lib = L.lib()
     ws_n = lib.srswa_route_workspace_size(N, nblk, d, p, 1 if cnd is not None else 0)
-    ws = torch.empty(ws_n, device=dev, dtype=torch.uint8) if ws_n else None
-    rc = lib.srswa_route(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
-                         kbar.data_ptr(), s_b, s_c, nblk, L.ptr(bt), 0 if bt is None else bt.stride(0),
-                         L.ptr(sl), int(rows_per_seq), L.ptr(row_seq), L.ptr(qp), L.ptr(cnd), s_cand, p,
-                         L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
-                         L.ptr(out["valid"]), L.ptr(out["scores"]), L.ptr(ws), ws_n, L.stream_of(idx_q))
+
+    def call(ws, n):
+        return lib.srswa_route(idx_q.data_ptr(), L.dtype_code(idx_q), idx_q.stride(0), N, d,
+                               kbar.data_ptr(), s_b, s_c, nblk, L.ptr(bt), 0 if bt is None else bt.stride(0),
+                               L.ptr(sl), int(rows_per_seq), L.ptr(row_seq), L.ptr(qp), L.ptr(cnd), s_cand, p,
+                               L.ptr(out["topi64"]), L.ptr(out["topi32"]), L.ptr(out["bias"]),
+                               L.ptr(out["valid"]), L.ptr(out["scores"]), L.ptr(ws), n, L.stream_of(idx_q))
+
+    rc = L.EWORKSPACE
+    if ws_n and row_seq is None and int(rows_per_seq) >= 32:
+        # prefill-shaped rows usually take the tiled routers, which need no
+        # workspace: try without (nothing is launched when the call needs one)
+        rc = call(None, 0)
+    if rc == L.EWORKSPACE:
+        rc = call(torch.empty(ws_n, device=dev, dtype=torch.uint8) if ws_n else None, ws_n)
     L.check(rc, "srswa_route")
     if out["valid"] is not None:
         out["valid"] = out["valid"].view(torch.bool)  # 0 / 1 bytes: no copy
