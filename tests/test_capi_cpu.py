@@ -74,6 +74,27 @@ def test_invalid_arguments_rejected_without_launch():
     assert lib.srswa_gather_bwd_workspace_size(C.byref(g)) > 0
 
 
+def test_paged_gather_forward_checks_without_launch():
+    """srswa_gather_fwd_paged (the tensor-core forward of one request over
+    paged K / V): unsupported shapes and bad arguments are refused before
+    any CUDA call, and the workspace query reports 0 for them."""
+    lib = L.lib()
+    # one 1000-row request after a 5000-token prefix, 64-token pages [P, 64, 10, 128]
+    g = L.GatherDesc(1, 1000, 10, 10, 1, 128, 8, 64, 512, 0.088, L.BF16, 0, 1280, 128,
+                     64 * 1280, 1280, 128, 64 * 1280, 1280, 128)
+    assert lib.srswa_gather_fwd_paged_workspace_size(C.byref(g), 5000) > 0
+    assert lib.srswa_gather_fwd_paged_workspace_size(C.byref(g), -1) == 0   # negative prefix
+    fake = C.c_void_p(1 << 20)  # never dereferenced: every call below is refused first
+    args = (fake, fake, fake, 100, None, 5000, fake, None, fake, 0, 1280, 128, None, fake, 1 << 30, None)
+    assert lib.srswa_gather_fwd_paged(C.byref(g), *args) == L.EINVAL          # no page table
+    g.B = 2
+    assert lib.srswa_gather_fwd_paged_workspace_size(C.byref(g), 5000) == 0
+    args = (fake, fake, fake, 100, fake, 5000, fake, None, fake, 0, 1280, 128, None, fake, 1 << 30, None)
+    assert lib.srswa_gather_fwd_paged(C.byref(g), *args) == L.EUNSUPPORTED   # one sequence per call
+    g.B, g.dtype = 1, L.F16
+    assert lib.srswa_gather_fwd_paged(C.byref(g), *args) == L.EUNSUPPORTED   # bf16 only
+
+
 def test_route_topm_limit():
     lib = L.lib()
     p = L.RouteParams(64, 8, 8, 64, 11.3, 1e-4, 1.0)  # M = 64 > 32 unsupported
