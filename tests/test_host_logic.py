@@ -119,3 +119,86 @@ def test_install_sglang_reaches_the_backend(monkeypatch):
     assert len(done) == 12
     dropin.install_sglang(overlap_router=False)
     assert be.dash_sparse_attn_decode is paged.dash_sparse_attn_decode
+
+
+def _no_capture(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: False)
+
+
+def test_paged_prefill_dispatch_per_request(monkeypatch):
+    """dash_sparse_attn: requests of >= TC_MIN_ROWS rows go to the
+    tensor-core forward over the paged caches (one call each, their prefix
+    as the query offset), shorter ones to the row kernel one by one; a
+    request whose block table is too narrow, or a selection that differs per
+    head, keeps the row kernel."""
+    from srswa import paged
+    _no_capture(monkeypatch)
+    calls = []
+    monkeypatch.setattr(ops, "pack_selection", lambda sel, nblk: sel.to(torch.int32))
+    monkeypatch.setattr(ops, "gather_fwd_paged",
+                        lambda q, kc, vc, sel, bias, pages, qoff, bs, sc, lw, out:
+                        calls.append(("tc", q.shape[0], qoff, pages.shape[0], lw, out.shape[0])))
+    monkeypatch.setattr(ops, "prefill_attend",
+                        lambda q, kc, vc, ti, b, **kw:
+                        calls.append(("row", q.shape[0], kw["prefix_lens"].tolist(), kw["block_table"].shape[0])))
+    H, D, K = 2, 128, 4
+    qlen, ctx = [200, 50, 130], [0, 100, 5000]
+    N = sum(qlen)
+    cu = torch.tensor([0, 200, 250, 380], dtype=torch.int32)
+    pre = torch.tensor(ctx, dtype=torch.int32)
+    q = torch.zeros(N, H, D, dtype=torch.bfloat16)
+    kc = torch.zeros(4, 64, H, D, dtype=torch.bfloat16)
+    ti = torch.zeros(N, K, dtype=torch.int32).unsqueeze(0).expand(H, -1, -1)
+    tb = torch.zeros(N, K).unsqueeze(0).expand(H, -1, -1)
+    out = torch.zeros(N, H, D, dtype=torch.bfloat16)
+
+    def run(bt, ti_, tb_):
+        calls.clear()
+        paged.dash_sparse_attn(q, kc, kc.clone(), ti_, tb_, bt, cu, cu, pre, 200, H, 0.1, out,
+                               local_blocks=8, sparse_block_size=64)
+        return sorted(calls)
+
+    bt = torch.zeros(3, 90, dtype=torch.int32)           # covers ceil((5000 + 130) / 64) = 81 blocks
+    assert run(bt, ti, tb) == sorted([("tc", 200, 0, 90, 512, 200), ("tc", 130, 5000, 90, 512, 130),
+                                      ("row", 50, [100], 1)])
+    bt = torch.zeros(3, 60, dtype=torch.int32)           # too narrow for the 5130-token request
+    assert run(bt, ti, tb) == sorted([("tc", 200, 0, 60, 512, 200), ("row", 130, [5000], 1),
+                                      ("row", 50, [100], 1)])
+    per_head = torch.zeros(H, N, K, dtype=torch.int32)   # a selection per KV head: all on the row kernel
+    assert run(bt, per_head, tb) == [("row", N, ctx, 3)]
+
+
+def test_route_prefill_dispatch_per_request(monkeypatch):
+    """route_prefill_triton: each request of >= ROUTE_TILE_MIN_ROWS rows is
+    routed by a call of its own (one sequence, the tiled routers), the other
+    rows by one varlen call on their gathered rows, whose results land in the
+    caller's rows."""
+    from srswa import paged
+    _no_capture(monkeypatch)
+    calls = []
+
+    def fake_route(idx_q, kbar, **kw):
+        n = idx_q.shape[0]
+        calls.append((n, kw.get("rows_per_seq"), kw.get("row_seq") is not None))
+        if kw.get("out") is not None:
+            kw["out"]["topi32"].fill_(7)
+            kw["out"]["bias"].fill_(0.5)
+            return kw["out"]
+        return {"topi32": torch.full((n, 4), 3, dtype=torch.int32), "bias": torch.full((n, 4), 0.25)}
+
+    monkeypatch.setattr(ops, "route", fake_route)
+    qlen = [100, 30, 100]
+    N = sum(qlen)
+    cu = torch.tensor([0, 100, 130, 230], dtype=torch.int32)
+    row2req = torch.repeat_interleave(torch.arange(3, dtype=torch.int32), torch.tensor(qlen))
+    out_idx = torch.zeros(N, 4, dtype=torch.int32)
+    out_bias = torch.zeros(N, 4)
+    paged.route_prefill_triton(idx_q=torch.zeros(N, 128), k_bar=torch.zeros(200, 128),
+                               block_table=torch.zeros(3, 50, dtype=torch.int32),
+                               seq_lens=torch.tensor([100, 130, 300], dtype=torch.int32), cu_seqlens_q=cu,
+                               context_lens=torch.tensor([0, 100, 200], dtype=torch.int32), row2req=row2req,
+                               image_allow=None, out_idx=out_idx, out_bias=out_bias, max_block=50, block_size=64,
+                               local_blocks=8, idx_scale=11.3, prior_floor=1e-4, sigma=1.0, topm=16, budget=4)
+    assert sorted(calls, key=str) == sorted([(100, 100, False), (100, 100, False), (30, None, True)], key=str)
+    assert (out_idx[:100] == 7).all() and (out_idx[130:] == 7).all() and (out_idx[100:130] == 3).all()
+    assert (out_bias[100:130] == 0.25).all() and (out_bias[:100] == 0.5).all()
