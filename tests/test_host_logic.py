@@ -177,9 +177,13 @@ def test_route_prefill_dispatch_per_request(monkeypatch):
     _no_capture(monkeypatch)
     calls = []
 
+    masks = []
+
     def fake_route(idx_q, kbar, **kw):
         n = idx_q.shape[0]
         calls.append((n, kw.get("rows_per_seq"), kw.get("row_seq") is not None))
+        if kw.get("cand") is not None:
+            masks.append(tuple(kw["cand"].shape))
         if kw.get("out") is not None:
             kw["out"]["topi32"].fill_(7)
             kw["out"]["bias"].fill_(0.5)
@@ -202,3 +206,15 @@ def test_route_prefill_dispatch_per_request(monkeypatch):
     assert sorted(calls, key=str) == sorted([(100, 100, False), (100, 100, False), (30, None, True)], key=str)
     assert (out_idx[:100] == 7).all() and (out_idx[130:] == 7).all() and (out_idx[100:130] == 3).all()
     assert (out_bias[100:130] == 0.25).all() and (out_bias[:100] == 0.5).all()
+    # image_allow: a per-row mask follows its rows, a shared row is passed as is
+    for allow, want in ((torch.ones(N, 60, dtype=torch.bool), [(100, 60), (100, 60), (30, 60)]),
+                        (torch.ones(60, dtype=torch.bool), [(60,)] * 3)):
+        masks.clear()
+        paged.route_prefill_triton(idx_q=torch.zeros(N, 128), k_bar=torch.zeros(200, 128),
+                                   block_table=torch.zeros(3, 50, dtype=torch.int32),
+                                   seq_lens=torch.tensor([100, 130, 300], dtype=torch.int32), cu_seqlens_q=cu,
+                                   context_lens=torch.tensor([0, 100, 200], dtype=torch.int32), row2req=row2req,
+                                   image_allow=allow, out_idx=out_idx, out_bias=out_bias, max_block=50,
+                                   block_size=64, local_blocks=8, idx_scale=11.3, prior_floor=1e-4, sigma=1.0,
+                                   topm=16, budget=4)
+        assert sorted(masks) == sorted(want)

@@ -280,17 +280,22 @@ def _route_by_request(idx_q, k_bar, bt, seq_lens, cu_seqlens_q, row2req, q_pos, 
         return False
     dev = idx_q.device
     sl = seq_lens.to(device=dev, dtype=torch.int32)
+    per_row = cand is not None and cand.dim() == 2 and cand.shape[0] == idx_q.shape[0] and cand.shape[0] > 1
+
+    def rows_of(m, sel):  # a per-row mask follows its rows; a shared row stays as it is
+        return None if m is None else (m[sel] if per_row else m)
+
     for r in long_r:
         a, b = cu[r], cu[r + 1]
         ops.route(idx_q[a:b], k_bar, seq_lens=sl[r:r + 1], q_pos=q_pos[a:b], rows_per_seq=b - a,
-                  block_table=bt[r:r + 1], cand=None if cand is None else cand[a:b],
+                  block_table=bt[r:r + 1], cand=rows_of(cand, slice(a, b)),
                   out={"topi32": out_idx[a:b], "bias": out_bias[a:b]}, **kw)
     short = [torch.arange(cu[r], cu[r + 1]) for r in range(R)
              if 0 < cu[r + 1] - cu[r] < ROUTE_TILE_MIN_ROWS]
     if short:
         idx = torch.cat(short).to(dev)
         res = ops.route(idx_q[idx], k_bar, seq_lens=sl, q_pos=q_pos[idx], row_seq=row2req[idx], block_table=bt,
-                        cand=None if cand is None else cand[idx], **kw)
+                        cand=rows_of(cand, idx), **kw)
         out_idx.index_copy_(0, idx, res["topi32"])
         out_bias.index_copy_(0, idx, res["bias"])
     return True
